@@ -1,0 +1,709 @@
+// hb_engine.cu -- host side of libhawkb200.so (C ABI in include/hawkb200.h).
+//
+// Owns the device buffers of one engine (weights blob, per-slot KV cache,
+// step activations, control block), launches the persistent decoder kernel
+// cooperatively (all CTAs co-resident, one per SM, so the grid barriers always
+// complete), reads back one small result block per call and turns device-side
+// wait timeouts into HB_ERR_DEVICE_TIMEOUT.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "hawkb200.h"
+#include "hb_decoder.cuh"
+#include "hb_gemv.cuh"
+
+using hb::DecParams;
+using hb::kMaxBatch;
+
+namespace {
+
+constexpr uint64_t kDefaultLimitNs = 2000000000ull;  // 2 s per device wait
+constexpr int kMaxSlotsRing = 16;
+constexpr int kMinSlotsRing = 4;
+constexpr int kProfileCap = 1 << 16;
+
+thread_local std::string g_lib_error;
+
+struct Variant {
+  const void *fn = nullptr;
+  size_t smem = 0;
+  int nslots = 0;
+  int mb = 0;
+};
+
+}  // namespace
+
+struct hb_engine {
+  int device = 0;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  hb_model_desc desc{};
+  int G = 0;
+  int red_rows = 0;
+  int xs_elems = 0;
+  Variant var1, var8;
+  bool loaded = false;
+
+  uint8_t *d_blob = nullptr;
+  hb::LayerPtrs *d_layers = nullptr;
+  float *d_rope_cos = nullptr, *d_rope_sin = nullptr;
+  __nv_bfloat16 *d_kv = nullptr;
+  size_t kv_slot_elems = 0;
+  __nv_bfloat16 *d_hbuf = nullptr, *d_qkv = nullptr, *d_act = nullptr;
+  float *d_opart = nullptr, *d_logits = nullptr, *d_part_val = nullptr;
+  int *d_part_idx = nullptr;
+  hb::Result *d_result = nullptr;
+  hb::StepState *d_st = nullptr;
+  int *d_prompt = nullptr, *d_gen = nullptr;
+  unsigned long long *d_trace = nullptr;
+
+  hb::StepState *h_st = nullptr;
+  hb::Result *h_result = nullptr;
+  int *h_prompt = nullptr, *h_gen = nullptr;
+
+  std::vector<hb::LayerPtrs> layer_ptrs;
+  std::string last_error;
+  uint64_t limit_ns = kDefaultLimitNs;
+  uint64_t stall_next_ns = 0;
+  bool trace_enabled = false;
+
+  bool profiling = false;
+  std::vector<cudaEvent_t> ev_a, ev_b;
+  int prof_count = 0;
+};
+
+namespace {
+
+int fail(hb_engine *e, int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  if (e) e->last_error = buf;
+  g_lib_error = buf;
+  return code;
+}
+
+#define HB_CUDA(e, call)                                                              \
+  do {                                                                                \
+    cudaError_t err_ = (call);                                                        \
+    if (err_ != cudaSuccess)                                                          \
+      return fail((e), HB_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(err_));       \
+  } while (0)
+
+template <class T>
+int dev_alloc(hb_engine *e, T **p, size_t count) {
+  HB_CUDA(e, cudaMalloc(reinterpret_cast<void **>(p), sizeof(T) * (count ? count : 1)));
+  HB_CUDA(e, cudaMemset(*p, 0, sizeof(T) * (count ? count : 1)));
+  return HB_OK;
+}
+
+int validate_desc(const hb_model_desc *d) {
+  if (!d) return fail(nullptr, HB_ERR_INVALID_ARG, "desc is NULL");
+  if (d->abi_version != HB_ABI_VERSION)
+    return fail(nullptr, HB_ERR_INVALID_ARG, "abi_version %d != %d", d->abi_version, HB_ABI_VERSION);
+  if (d->head_dim != hb::kHeadDim) return fail(nullptr, HB_ERR_UNSUPPORTED, "head_dim must be 64");
+  if (d->hidden <= 0 || d->intermediate <= 0 || d->q_heads <= 0 || d->kv_heads <= 0 ||
+      d->layers <= 0 || d->vocab <= 0 || d->context <= 0 || d->context > 1024)
+    return fail(nullptr, HB_ERR_INVALID_ARG, "invalid model dimensions");
+  if (d->q_heads % d->kv_heads) return fail(nullptr, HB_ERR_INVALID_ARG, "q_heads %% kv_heads != 0");
+  if (d->hidden != d->q_heads * d->head_dim)
+    return fail(nullptr, HB_ERR_UNSUPPORTED, "hidden must equal q_heads * head_dim");
+  if (d->weight_format != HB_WEIGHTS_BF16 && d->weight_format != HB_WEIGHTS_W8)
+    return fail(nullptr, HB_ERR_INVALID_ARG, "unknown weight_format");
+  const int qkv = (d->q_heads + 2 * d->kv_heads) * d->head_dim;
+  if (d->hidden % 16 || d->intermediate % 16 || qkv % 8 || d->vocab % 8)
+    return fail(nullptr, HB_ERR_UNSUPPORTED, "dimensions must be multiples of 16 (rows of 8)");
+  const int esize = d->weight_format == HB_WEIGHTS_W8 ? 1 : 2;
+  if (d->hidden * esize > 2048)
+    return fail(nullptr, HB_ERR_UNSUPPORTED, "hidden too large for one LM-head chunk");
+  if (d->max_slots <= 0 || d->max_batch <= 0 || d->max_batch > kMaxBatch)
+    return fail(nullptr, HB_ERR_INVALID_ARG, "max_slots > 0 and 1 <= max_batch <= 8 required");
+  if (!d->layer_offsets || !d->rope_cos || !d->rope_sin)
+    return fail(nullptr, HB_ERR_INVALID_ARG, "layer_offsets / rope tables missing");
+  // every tensor inside the blob and 16-byte aligned (bulk copies need it)
+  const uint64_t B = d->blob_bytes;
+  auto in_blob = [&](uint64_t off, uint64_t bytes) { return off % 16 == 0 && off + bytes <= B; };
+  const uint64_t h = d->hidden, I = d->intermediate;
+  for (int l = 0; l < d->layers; ++l) {
+    const hb_layer_offsets &o = d->layer_offsets[l];
+    bool ok = in_blob(o.gamma_in, 4 * h) && in_blob(o.gamma_post, 4 * h) && in_blob(o.qkv_bias, 4 * qkv) &&
+              in_blob(o.w_qkv, qkv * h * esize) && in_blob(o.w_o, h * h * esize) &&
+              in_blob(o.w_gate_up, 2 * I * h * esize) && in_blob(o.w_down, h * I * esize);
+    if (esize == 1)
+      ok = ok && in_blob(o.s_qkv, 4 * qkv) && in_blob(o.s_o, 4 * h) && in_blob(o.s_gate_up, 8 * I) &&
+           in_blob(o.s_down, 4 * h);
+    if (!ok) return fail(nullptr, HB_ERR_INVALID_ARG, "layer %d offsets outside the blob or unaligned", l);
+  }
+  bool ok = in_blob(d->gamma_final, 4 * h) && in_blob(d->w_lm, uint64_t(d->vocab) * h * esize) &&
+            in_blob(d->embedding, uint64_t(d->vocab) * h * 2);
+  if (esize == 1) ok = ok && in_blob(d->s_lm, 4ull * d->vocab);
+  if (!ok) return fail(nullptr, HB_ERR_INVALID_ARG, "global offsets outside the blob or unaligned");
+  return HB_OK;
+}
+
+int setup_variant(hb_engine *e, Variant &v, int mb, const void *fn, int smem_optin) {
+  const hb_model_desc &d = e->desc;
+  const hb::SmemPlan base = hb::smem_plan(0, mb, e->xs_elems, d.hidden, e->red_rows, d.context);
+  int nslots = static_cast<int>((static_cast<size_t>(smem_optin) - base.total - 16 * kMaxSlotsRing) /
+                                hb::kSlotBytes);
+  if (nslots > kMaxSlotsRing) nslots = kMaxSlotsRing;
+  if (nslots < kMinSlotsRing)
+    return fail(e, HB_ERR_UNSUPPORTED, "model too large for the shared-memory plan (batch %d)", mb);
+  const hb::SmemPlan sp = hb::smem_plan(nslots, mb, e->xs_elems, d.hidden, e->red_rows, d.context);
+  HB_CUDA(e, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sp.total)));
+  int blocks = 0;
+  HB_CUDA(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, hb::kThreads, sp.total));
+  if (blocks < 1) return fail(e, HB_ERR_UNSUPPORTED, "decoder kernel does not fit on an SM");
+  v.fn = fn;
+  v.smem = sp.total;
+  v.nslots = nslots;
+  v.mb = mb;
+  return HB_OK;
+}
+
+DecParams base_params(hb_engine *e, const Variant &v) {
+  const hb_model_desc &d = e->desc;
+  const int esize = d.weight_format == HB_WEIGHTS_W8 ? 1 : 2;
+  DecParams P{};
+  P.H = d.hidden;
+  P.I = d.intermediate;
+  P.QH = d.q_heads;
+  P.KVH = d.kv_heads;
+  P.L = d.layers;
+  P.V = d.vocab;
+  P.CTX = d.context;
+  P.QKV = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
+  P.group = d.q_heads / d.kv_heads;
+  P.has_bias = d.has_qkv_bias;
+  P.eps = d.rms_eps;
+  P.kc_h = d.hidden * esize / 16;
+  P.kc_i = d.intermediate * esize / 16;
+  P.kc_d = d.head_dim * esize / 16;
+  P.slab_bytes = d.hidden * d.head_dim * esize;
+  P.layers = e->d_layers;
+  P.gamma_final = reinterpret_cast<const float *>(e->d_blob + d.gamma_final);
+  P.w_lm = e->d_blob + d.w_lm;
+  P.s_lm = esize == 1 ? reinterpret_cast<const float *>(e->d_blob + d.s_lm) : nullptr;
+  P.embed = reinterpret_cast<const __nv_bfloat16 *>(e->d_blob + d.embedding);
+  P.rope_cos = e->d_rope_cos;
+  P.rope_sin = e->d_rope_sin;
+  P.kv = e->d_kv;
+  P.hbuf = e->d_hbuf;
+  P.qkv = e->d_qkv;
+  P.opart = e->d_opart;
+  P.act = e->d_act;
+  P.logits = e->d_logits;
+  P.part_val = e->d_part_val;
+  P.part_idx = e->d_part_idx;
+  P.result = e->d_result;
+  P.st = e->d_st;
+  P.prompt = e->d_prompt;
+  P.gen_out = e->d_gen;
+  P.red_rows = e->red_rows;
+  P.nslots = v.nslots;
+  P.xs_elems = e->xs_elems;
+  P.limit_ns = e->limit_ns;
+  P.trace = e->trace_enabled ? e->d_trace : nullptr;
+  return P;
+}
+
+const void *decoder_fn(int mb, bool w8) {
+  if (mb == 1) return w8 ? reinterpret_cast<const void *>(&hb::decoder_kernel<1, true>)
+                         : reinterpret_cast<const void *>(&hb::decoder_kernel<1, false>);
+  return w8 ? reinterpret_cast<const void *>(&hb::decoder_kernel<8, true>)
+            : reinterpret_cast<const void *>(&hb::decoder_kernel<8, false>);
+}
+
+// Launch phases [pb, pe) for the rows in d_st.
+int launch(hb_engine *e, int rows, int pb, int pe, int write_logits) {
+  const Variant &v = rows > 1 ? e->var8 : e->var1;
+  DecParams P = base_params(e, v);
+  P.phase_begin = pb;
+  P.phase_end = pe;
+  P.write_logits = write_logits;
+  P.stall_ns = e->stall_next_ns;
+  e->stall_next_ns = 0;
+  void *args[] = {&P};
+  const bool prof = e->profiling && e->prof_count < kProfileCap;
+  if (prof) {
+    while (static_cast<int>(e->ev_a.size()) <= e->prof_count) {
+      cudaEvent_t a, b;
+      HB_CUDA(e, cudaEventCreate(&a));
+      HB_CUDA(e, cudaEventCreate(&b));
+      e->ev_a.push_back(a);
+      e->ev_b.push_back(b);
+    }
+    HB_CUDA(e, cudaEventRecord(e->ev_a[e->prof_count], e->stream));
+  }
+  HB_CUDA(e, cudaLaunchCooperativeKernel(v.fn, dim3(e->G), dim3(hb::kThreads), args, v.smem, e->stream));
+  if (prof) {
+    HB_CUDA(e, cudaEventRecord(e->ev_b[e->prof_count], e->stream));
+    ++e->prof_count;
+  }
+  return HB_OK;
+}
+
+// Copies the result block back, waits, and maps a device error to a code.
+int finish(hb_engine *e) {
+  HB_CUDA(e, cudaMemcpyAsync(e->h_result, e->d_result, sizeof(hb::Result), cudaMemcpyDeviceToHost, e->stream));
+  HB_CUDA(e, cudaStreamSynchronize(e->stream));
+  if (e->h_result->ctrl.err != 0) {
+    const int where = e->h_result->ctrl.err_where;
+    HB_CUDA(e, cudaMemsetAsync(e->d_result, 0, sizeof(hb::Result), e->stream));
+    HB_CUDA(e, cudaStreamSynchronize(e->stream));
+    static const char *names[] = {"?", "weight chunk", "ring slot", "grid barrier", "test stall flag", "drain"};
+    return fail(e, HB_ERR_DEVICE_TIMEOUT, "device wait on %s timed out; engine state reset",
+                names[(where >= 0 && where <= 5) ? where : 0]);
+  }
+  return HB_OK;
+}
+
+int check_engine(hb_engine *e) {
+  if (!e) return fail(nullptr, HB_ERR_INVALID_ARG, "engine is NULL");
+  if (!e->loaded) return fail(e, HB_ERR_STATE, "weights not loaded");
+  HB_CUDA(e, cudaSetDevice(e->device));
+  return HB_OK;
+}
+
+int check_row(hb_engine *e, int slot, int token, int position) {
+  const hb_model_desc &d = e->desc;
+  if (slot < 0 || slot >= d.max_slots) return fail(e, HB_ERR_INVALID_ARG, "slot %d outside [0, %d)", slot, d.max_slots);
+  if (token < 0 || token >= d.vocab) return fail(e, HB_ERR_INVALID_ARG, "token id %d outside the vocabulary", token);
+  if (position < 0 || position >= d.context)
+    return fail(e, HB_ERR_INVALID_ARG, "position outside the %d-token context", d.context);
+  return HB_OK;
+}
+
+// Device-resident chained run: positions start..n_prompt-1 of ids (prefill;
+// the LM head only at the last), then n_new-1 further greedy steps.
+int run_chained(hb_engine *e, int slot, const int32_t *ids, int n_prompt, int start, int n_new,
+                int32_t *out_tokens, float *last_logits) {
+  const hb_model_desc &d = e->desc;
+  if (!ids || n_prompt <= 0 || start < 0 || start >= n_prompt || n_new < 1)
+    return fail(e, HB_ERR_INVALID_ARG, "invalid prompt range");
+  if (n_prompt + n_new - 1 > d.context)
+    return fail(e, HB_ERR_INVALID_ARG, "prompt + generated tokens exceed the %d-token context", d.context);
+  for (int p = start; p < n_prompt; ++p) {
+    int rc = check_row(e, slot, ids[p], p);
+    if (rc) return rc;
+  }
+  for (int p = 0; p < d.context; ++p) e->h_prompt[p] = (p >= start && p < n_prompt) ? ids[p] : 0;
+  hb::StepState &st = *e->h_st;
+  std::memset(&st, 0, sizeof(st));
+  st.token[0] = ids[start];
+  st.pos[0] = start;
+  st.slot[0] = slot;
+  st.rows = 1;
+  st.chained = 1;
+  st.n_prompt = n_prompt;
+  st.n_out = 0;
+  HB_CUDA(e, cudaMemcpyAsync(e->d_prompt, e->h_prompt, sizeof(int) * d.context, cudaMemcpyHostToDevice, e->stream));
+  HB_CUDA(e, cudaMemcpyAsync(e->d_st, e->h_st, sizeof(hb::StepState), cudaMemcpyHostToDevice, e->stream));
+  const int full = 4 * d.layers + 1;
+  const int body = 4 * d.layers;
+  for (int p = start; p < n_prompt - 1; ++p) {
+    int rc = launch(e, 1, 0, body, 0);
+    if (rc) return rc;
+  }
+  for (int t = 0; t < n_new; ++t) {
+    const bool want_logits = last_logits != nullptr && t == n_new - 1;
+    int rc = launch(e, 1, 0, full, want_logits ? 1 : 0);
+    if (rc) return rc;
+  }
+  HB_CUDA(e, cudaMemcpyAsync(e->h_gen, e->d_gen, sizeof(int) * n_new, cudaMemcpyDeviceToHost, e->stream));
+  if (last_logits)
+    HB_CUDA(e, cudaMemcpyAsync(last_logits, e->d_logits, sizeof(float) * d.vocab, cudaMemcpyDeviceToHost, e->stream));
+  int rc = finish(e);
+  if (rc) return rc;
+  if (out_tokens) std::memcpy(out_tokens, e->h_gen, sizeof(int) * n_new);
+  return HB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int hb_device_sm_count(int device) {
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+const char *hb_library_error(void) { return g_lib_error.c_str(); }
+
+const char *hb_last_error(const hb_engine *engine) {
+  return engine ? engine->last_error.c_str() : g_lib_error.c_str();
+}
+
+int hb_create(const hb_model_desc *desc, int device, hb_engine **out) {
+  if (!out) return fail(nullptr, HB_ERR_INVALID_ARG, "out is NULL");
+  *out = nullptr;
+  int rc = validate_desc(desc);
+  if (rc) return rc;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+    cudaGetLastError();
+    return fail(nullptr, HB_ERR_INVALID_ARG, "CUDA device %d not available", device);
+  }
+  hb_engine *e = new hb_engine();
+  e->device = device;
+  e->desc = *desc;
+  e->desc.layer_offsets = nullptr;
+  e->desc.rope_cos = e->desc.rope_sin = nullptr;
+  auto bail = [&](int code) {
+    hb_destroy(e);
+    return code;
+  };
+  if (cudaSetDevice(device) != cudaSuccess) return bail(fail(nullptr, HB_ERR_CUDA, "cudaSetDevice failed"));
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess)
+    return bail(fail(nullptr, HB_ERR_CUDA, "cudaGetDeviceProperties failed"));
+  if (prop.major < 10) return bail(fail(nullptr, HB_ERR_UNSUPPORTED, "this build targets sm_100a (B200)"));
+  if (!prop.cooperativeLaunch) return bail(fail(nullptr, HB_ERR_UNSUPPORTED, "cooperative launch unsupported"));
+  const hb_model_desc &d = e->desc;
+  e->G = prop.multiProcessorCount;
+  if (e->G < d.q_heads) return bail(fail(nullptr, HB_ERR_UNSUPPORTED, "fewer SMs than attention heads"));
+  const int qkv = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
+  auto ceil_div = [](int a, int b) { return (a + b - 1) / b; };
+  e->red_rows = std::max(std::max(ceil_div(qkv / 8, e->G) * 8, ceil_div(d.intermediate / 8, e->G) * 16),
+                         ceil_div(d.hidden / 8, e->G) * 8);
+  e->xs_elems = std::max(std::max(d.hidden, d.intermediate), hb::kHeadDim);
+  e->xs_elems = (e->xs_elems + 15) / 16 * 16;
+  const bool w8 = d.weight_format == HB_WEIGHTS_W8;
+  if ((rc = setup_variant(e, e->var1, 1, decoder_fn(1, w8), prop.sharedMemPerBlockOptin))) return bail(rc);
+  if (d.max_batch > 1 && (rc = setup_variant(e, e->var8, 8, decoder_fn(8, w8), prop.sharedMemPerBlockOptin)))
+    return bail(rc);
+  if (cudaStreamCreateWithFlags(&e->own_stream, cudaStreamNonBlocking) != cudaSuccess)
+    return bail(fail(nullptr, HB_ERR_CUDA, "stream creation failed"));
+  e->stream = e->own_stream;
+
+  const int mb = d.max_batch > 1 ? kMaxBatch : 1;
+  e->kv_slot_elems = static_cast<size_t>(d.layers) * d.kv_heads * 2 * d.context * hb::kHeadDim;
+  const size_t half = static_cast<size_t>(d.head_dim / 2) * d.context;
+  if ((rc = dev_alloc(e, &e->d_blob, d.blob_bytes)) || (rc = dev_alloc(e, &e->d_layers, d.layers)) ||
+      (rc = dev_alloc(e, &e->d_rope_cos, half)) || (rc = dev_alloc(e, &e->d_rope_sin, half)) ||
+      (rc = dev_alloc(e, &e->d_kv, e->kv_slot_elems * d.max_slots)) ||
+      (rc = dev_alloc(e, &e->d_hbuf, static_cast<size_t>(kMaxBatch) * d.hidden)) ||
+      (rc = dev_alloc(e, &e->d_qkv, static_cast<size_t>(kMaxBatch) * qkv)) ||
+      (rc = dev_alloc(e, &e->d_act, static_cast<size_t>(kMaxBatch) * d.intermediate)) ||
+      (rc = dev_alloc(e, &e->d_opart, static_cast<size_t>(kMaxBatch) * d.q_heads * d.hidden)) ||
+      (rc = dev_alloc(e, &e->d_logits, static_cast<size_t>(kMaxBatch) * d.vocab)) ||
+      (rc = dev_alloc(e, &e->d_part_val, static_cast<size_t>(e->G) * kMaxBatch)) ||
+      (rc = dev_alloc(e, &e->d_part_idx, static_cast<size_t>(e->G) * kMaxBatch)) ||
+      (rc = dev_alloc(e, &e->d_result, 1)) || (rc = dev_alloc(e, &e->d_st, 1)) ||
+      (rc = dev_alloc(e, &e->d_prompt, d.context)) || (rc = dev_alloc(e, &e->d_gen, d.context + 1)) ||
+      (rc = dev_alloc(e, &e->d_trace, static_cast<size_t>(e->G) * (4 * d.layers + 2))))
+    return bail(rc);
+  (void)mb;
+  if (cudaHostAlloc(reinterpret_cast<void **>(&e->h_st), sizeof(hb::StepState), cudaHostAllocDefault) != cudaSuccess ||
+      cudaHostAlloc(reinterpret_cast<void **>(&e->h_result), sizeof(hb::Result), cudaHostAllocDefault) != cudaSuccess ||
+      cudaHostAlloc(reinterpret_cast<void **>(&e->h_prompt), sizeof(int) * d.context, cudaHostAllocDefault) != cudaSuccess ||
+      cudaHostAlloc(reinterpret_cast<void **>(&e->h_gen), sizeof(int) * (d.context + 1), cudaHostAllocDefault) != cudaSuccess)
+    return bail(fail(nullptr, HB_ERR_CUDA, "pinned host allocation failed"));
+
+  // device pointers of every layer's tensors
+  const bool has_scales = w8;
+  e->layer_ptrs.resize(d.layers);
+  for (int l = 0; l < d.layers; ++l) {
+    const hb_layer_offsets &o = desc->layer_offsets[l];
+    hb::LayerPtrs &p = e->layer_ptrs[l];
+    auto f = [&](uint64_t off) { return reinterpret_cast<const float *>(e->d_blob + off); };
+    p.gamma_in = f(o.gamma_in);
+    p.gamma_post = f(o.gamma_post);
+    p.bias = f(o.qkv_bias);
+    p.w_qkv = e->d_blob + o.w_qkv;
+    p.w_o = e->d_blob + o.w_o;
+    p.w_gu = e->d_blob + o.w_gate_up;
+    p.w_down = e->d_blob + o.w_down;
+    p.s_qkv = has_scales ? f(o.s_qkv) : nullptr;
+    p.s_o = has_scales ? f(o.s_o) : nullptr;
+    p.s_gu = has_scales ? f(o.s_gate_up) : nullptr;
+    p.s_down = has_scales ? f(o.s_down) : nullptr;
+  }
+  if (cudaMemcpy(e->d_layers, e->layer_ptrs.data(), sizeof(hb::LayerPtrs) * d.layers, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(e->d_rope_cos, desc->rope_cos, sizeof(float) * half, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(e->d_rope_sin, desc->rope_sin, sizeof(float) * half, cudaMemcpyHostToDevice) != cudaSuccess)
+    return bail(fail(nullptr, HB_ERR_CUDA, "descriptor upload failed"));
+  *out = e;
+  return HB_OK;
+}
+
+int hb_load_weights(hb_engine *e, const void *host_blob, size_t bytes, int layout_version) {
+  if (!e) return fail(nullptr, HB_ERR_INVALID_ARG, "engine is NULL");
+  if (!host_blob || bytes != e->desc.blob_bytes)
+    return fail(e, HB_ERR_INVALID_ARG, "blob size %zu != %llu", bytes,
+                static_cast<unsigned long long>(e->desc.blob_bytes));
+  if (layout_version != 1) return fail(e, HB_ERR_UNSUPPORTED, "layout version %d unsupported", layout_version);
+  HB_CUDA(e, cudaSetDevice(e->device));
+  HB_CUDA(e, cudaMemcpy(e->d_blob, host_blob, bytes, cudaMemcpyHostToDevice));
+  e->loaded = true;
+  return HB_OK;
+}
+
+int hb_destroy(hb_engine *e) {
+  if (!e) return HB_OK;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  for (auto ev : e->ev_a) cudaEventDestroy(ev);
+  for (auto ev : e->ev_b) cudaEventDestroy(ev);
+  void *dev[] = {e->d_blob, e->d_layers, e->d_rope_cos, e->d_rope_sin, e->d_kv, e->d_hbuf, e->d_qkv,
+                 e->d_act, e->d_opart, e->d_logits, e->d_part_val, e->d_part_idx, e->d_result,
+                 e->d_st, e->d_prompt, e->d_gen, e->d_trace};
+  for (void *p : dev)
+    if (p) cudaFree(p);
+  void *host[] = {e->h_st, e->h_result, e->h_prompt, e->h_gen};
+  for (void *p : host)
+    if (p) cudaFreeHost(p);
+  if (e->own_stream) cudaStreamDestroy(e->own_stream);
+  delete e;
+  return HB_OK;
+}
+
+int hb_step(hb_engine *e, int slot, int token_id, int position, int flags, float *logits_out,
+            int32_t *argmax_out) {
+  int rc = check_engine(e);
+  if (rc) return rc;
+  if ((rc = check_row(e, slot, token_id, position))) return rc;
+  if (logits_out) flags |= HB_STEP_LOGITS;
+  if (flags & HB_STEP_LOGITS) flags |= HB_STEP_ARGMAX;
+  hb::StepState &st = *e->h_st;
+  std::memset(&st, 0, sizeof(st));
+  st.token[0] = token_id;
+  st.pos[0] = position;
+  st.slot[0] = slot;
+  st.rows = 1;
+  HB_CUDA(e, cudaMemcpyAsync(e->d_st, e->h_st, sizeof(hb::StepState), cudaMemcpyHostToDevice, e->stream));
+  const int pe = (flags & HB_STEP_ARGMAX) ? 4 * e->desc.layers + 1 : 4 * e->desc.layers;
+  if ((rc = launch(e, 1, 0, pe, logits_out ? 1 : 0))) return rc;
+  if (logits_out)
+    HB_CUDA(e, cudaMemcpyAsync(logits_out, e->d_logits, sizeof(float) * e->desc.vocab, cudaMemcpyDeviceToHost, e->stream));
+  if ((rc = finish(e))) return rc;
+  if (argmax_out) *argmax_out = (flags & HB_STEP_ARGMAX) ? e->h_result->out_token[0] : -1;
+  return HB_OK;
+}
+
+int hb_prefill(hb_engine *e, int slot, const int32_t *ids, int n, int start_pos, float *last_logits,
+               int32_t *argmax_out) {
+  int rc = check_engine(e);
+  if (rc) return rc;
+  if (!ids || n <= 0) return fail(e, HB_ERR_INVALID_ARG, "empty prefill");
+  if (start_pos < 0 || start_pos + n > e->desc.context)
+    return fail(e, HB_ERR_INVALID_ARG, "position outside the %d-token context", e->desc.context);
+  std::vector<int32_t> by_pos(start_pos + n, 0);
+  for (int i = 0; i < n; ++i) by_pos[start_pos + i] = ids[i];
+  int32_t tok = -1;
+  rc = run_chained(e, slot, by_pos.data(), start_pos + n, start_pos, 1, &tok, last_logits);
+  if (rc) return rc;
+  if (argmax_out) *argmax_out = tok;
+  return HB_OK;
+}
+
+int hb_generate(hb_engine *e, int slot, const int32_t *ids, int n_prompt, int start_pos, int n_new,
+                int32_t *out_tokens) {
+  int rc = check_engine(e);
+  if (rc) return rc;
+  return run_chained(e, slot, ids, n_prompt, start_pos, n_new, out_tokens, nullptr);
+}
+
+int hb_step_batch(hb_engine *e, int n, const int32_t *slots, const int32_t *token_ids,
+                  const int32_t *positions, int flags, float *logits_out, int32_t *argmax_out) {
+  int rc = check_engine(e);
+  if (rc) return rc;
+  if (n < 1 || n > e->desc.max_batch || !slots || !token_ids || !positions)
+    return fail(e, HB_ERR_INVALID_ARG, "batch of %d rows outside [1, %d]", n, e->desc.max_batch);
+  for (int i = 0; i < n; ++i) {
+    if ((rc = check_row(e, slots[i], token_ids[i], positions[i]))) return rc;
+    for (int j = 0; j < i; ++j)
+      if (slots[j] == slots[i]) return fail(e, HB_ERR_INVALID_ARG, "slot %d appears twice in one batch", slots[i]);
+  }
+  if (logits_out) flags |= HB_STEP_LOGITS;
+  if (flags & HB_STEP_LOGITS) flags |= HB_STEP_ARGMAX;
+  hb::StepState &st = *e->h_st;
+  std::memset(&st, 0, sizeof(st));
+  for (int i = 0; i < n; ++i) {
+    st.token[i] = token_ids[i];
+    st.pos[i] = positions[i];
+    st.slot[i] = slots[i];
+  }
+  st.rows = n;
+  HB_CUDA(e, cudaMemcpyAsync(e->d_st, e->h_st, sizeof(hb::StepState), cudaMemcpyHostToDevice, e->stream));
+  const int pe = (flags & HB_STEP_ARGMAX) ? 4 * e->desc.layers + 1 : 4 * e->desc.layers;
+  if ((rc = launch(e, n, 0, pe, logits_out ? 1 : 0))) return rc;
+  if (logits_out)
+    HB_CUDA(e, cudaMemcpyAsync(logits_out, e->d_logits, sizeof(float) * e->desc.vocab * n, cudaMemcpyDeviceToHost, e->stream));
+  if ((rc = finish(e))) return rc;
+  if (argmax_out)
+    for (int i = 0; i < n; ++i) argmax_out[i] = (flags & HB_STEP_ARGMAX) ? e->h_result->out_token[i] : -1;
+  return HB_OK;
+}
+
+int hb_reset(hb_engine *e, int slot) {
+  if (!e) return fail(nullptr, HB_ERR_INVALID_ARG, "engine is NULL");
+  if (slot < 0 || slot >= e->desc.max_slots) return fail(e, HB_ERR_INVALID_ARG, "slot %d out of range", slot);
+  HB_CUDA(e, cudaSetDevice(e->device));
+  HB_CUDA(e, cudaMemsetAsync(e->d_kv + e->kv_slot_elems * slot, 0, e->kv_slot_elems * 2, e->stream));
+  HB_CUDA(e, cudaStreamSynchronize(e->stream));
+  return HB_OK;
+}
+
+int hb_copy_prefix(hb_engine *e, int src, int dst, int n_positions) {
+  if (!e) return fail(nullptr, HB_ERR_INVALID_ARG, "engine is NULL");
+  const hb_model_desc &d = e->desc;
+  if (src < 0 || src >= d.max_slots || dst < 0 || dst >= d.max_slots)
+    return fail(e, HB_ERR_INVALID_ARG, "slot out of range");
+  if (n_positions < 0 || n_positions > d.context) return fail(e, HB_ERR_INVALID_ARG, "n_positions out of range");
+  if (src == dst || n_positions == 0) return HB_OK;
+  HB_CUDA(e, cudaSetDevice(e->device));
+  const size_t pitch = static_cast<size_t>(d.context) * hb::kHeadDim * 2;
+  const size_t height = static_cast<size_t>(d.layers) * d.kv_heads * 2;
+  HB_CUDA(e, cudaMemcpy2DAsync(e->d_kv + e->kv_slot_elems * dst, pitch, e->d_kv + e->kv_slot_elems * src, pitch,
+                               static_cast<size_t>(n_positions) * hb::kHeadDim * 2, height,
+                               cudaMemcpyDeviceToDevice, e->stream));
+  HB_CUDA(e, cudaStreamSynchronize(e->stream));
+  return HB_OK;
+}
+
+int hb_debug_dump(hb_engine *e, int what, void *out, size_t bytes) {
+  if (!e || !out) return fail(e, HB_ERR_INVALID_ARG, "engine or out is NULL");
+  HB_CUDA(e, cudaSetDevice(e->device));
+  const hb_model_desc &d = e->desc;
+  if (what == HB_DUMP_HIDDEN) {
+    const size_t need = static_cast<size_t>(kMaxBatch) * d.hidden * 2;
+    if (bytes < need) return fail(e, HB_ERR_INVALID_ARG, "need %zu bytes", need);
+    HB_CUDA(e, cudaMemcpyAsync(out, e->d_hbuf, need, cudaMemcpyDeviceToHost, e->stream));
+  } else if (what == HB_DUMP_KV) {
+    const int slot = *reinterpret_cast<int *>(out);
+    if (slot < 0 || slot >= d.max_slots) return fail(e, HB_ERR_INVALID_ARG, "slot out of range");
+    const size_t need = e->kv_slot_elems * 2;
+    if (bytes < need) return fail(e, HB_ERR_INVALID_ARG, "need %zu bytes", need);
+    HB_CUDA(e, cudaMemcpyAsync(out, e->d_kv + e->kv_slot_elems * slot, need, cudaMemcpyDeviceToHost, e->stream));
+  } else if (what == 2) {
+    // phase trace: [G][4L+2] globaltimer stamps of the last traced launch
+    const size_t need = static_cast<size_t>(e->G) * (4 * d.layers + 2) * 8;
+    if (bytes < need) return fail(e, HB_ERR_INVALID_ARG, "need %zu bytes", need);
+    HB_CUDA(e, cudaMemcpyAsync(out, e->d_trace, need, cudaMemcpyDeviceToHost, e->stream));
+  } else {
+    return fail(e, HB_ERR_INVALID_ARG, "unknown dump kind %d", what);
+  }
+  HB_CUDA(e, cudaStreamSynchronize(e->stream));
+  return HB_OK;
+}
+
+int hb_profile(hb_engine *e, int enable) {
+  if (!e) return fail(nullptr, HB_ERR_INVALID_ARG, "engine is NULL");
+  e->profiling = enable & 1;
+  e->trace_enabled = (enable & 2) != 0;
+  e->prof_count = 0;
+  return HB_OK;
+}
+
+int hb_profile_read(hb_engine *e, float *ms, int max, int *count) {
+  if (!e || !count) return fail(e, HB_ERR_INVALID_ARG, "engine or count is NULL");
+  HB_CUDA(e, cudaSetDevice(e->device));
+  HB_CUDA(e, cudaStreamSynchronize(e->stream));
+  const int n = std::min(max, e->prof_count);
+  for (int i = 0; i < n; ++i) HB_CUDA(e, cudaEventElapsedTime(&ms[i], e->ev_a[i], e->ev_b[i]));
+  *count = n;
+  e->prof_count = 0;
+  return HB_OK;
+}
+
+int hb_set_stream(hb_engine *e, void *stream) {
+  if (!e) return fail(nullptr, HB_ERR_INVALID_ARG, "engine is NULL");
+  e->stream = stream ? static_cast<cudaStream_t>(stream) : e->own_stream;
+  return HB_OK;
+}
+
+int hb_test_stall_next(hb_engine *e, uint64_t limit_ns) {
+  if (!e) return fail(nullptr, HB_ERR_INVALID_ARG, "engine is NULL");
+  if (limit_ns == 0 || limit_ns > 10000000000ull) return fail(e, HB_ERR_INVALID_ARG, "limit must be in (0, 10 s]");
+  e->stall_next_ns = limit_ns;
+  return HB_OK;
+}
+
+// ------------------------------------------------------------------ GEMV --
+size_t hb_gemv_scratch_bytes(int rows, int batch) {
+  (void)rows;
+  (void)batch;
+  return sizeof(hb::Ctrl) + 2 * sizeof(float) * 1024 * hb::kMaxBatchGemv;
+}
+
+int hb_gemv(const void *w_dev, const float *scales_dev, int weight_format, int rows, int k, const void *x_dev,
+            int batch, void *y_dev, int flags, int32_t *argmax_dev, void *scratch_dev, size_t scratch_bytes,
+            void *stream) {
+  const int out_mode = flags & 3;
+  const bool want_argmax = (flags & HB_GEMV_ARGMAX) != 0;
+  if (!w_dev || !x_dev || rows <= 0 || k <= 0 || rows % 8 || k % 16 || batch < 1 || batch > hb::kMaxBatchGemv)
+    return fail(nullptr, HB_ERR_INVALID_ARG, "hb_gemv: bad shape (rows %% 8, k %% 16, batch 1..8)");
+  if (weight_format != HB_WEIGHTS_BF16 && weight_format != HB_WEIGHTS_W8)
+    return fail(nullptr, HB_ERR_INVALID_ARG, "hb_gemv: unknown weight format");
+  if (weight_format == HB_WEIGHTS_W8 && !scales_dev) return fail(nullptr, HB_ERR_INVALID_ARG, "hb_gemv: W8 needs scales");
+  if (out_mode > 2 || (out_mode != 2 && !y_dev)) return fail(nullptr, HB_ERR_INVALID_ARG, "hb_gemv: bad output");
+  if (want_argmax && !argmax_dev) return fail(nullptr, HB_ERR_INVALID_ARG, "hb_gemv: argmax output missing");
+  if (!scratch_dev || scratch_bytes < hb_gemv_scratch_bytes(rows, batch))
+    return fail(nullptr, HB_ERR_INVALID_ARG, "hb_gemv: scratch too small");
+  const auto check = [](uintptr_t p) { return p % 16 == 0; };
+  if (!check(reinterpret_cast<uintptr_t>(w_dev)) || !check(reinterpret_cast<uintptr_t>(x_dev)))
+    return fail(nullptr, HB_ERR_INVALID_ARG, "hb_gemv: W and x must be 16-byte aligned");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(nullptr, HB_ERR_CUDA, "no CUDA device");
+  int sms = 0, optin = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  const bool w8 = weight_format == HB_WEIGHTS_W8;
+  const int esize = w8 ? 1 : 2;
+  const int kc = k * esize / 16;
+  const int n_rg = rows / 8;
+  const int G = std::min(sms, n_rg);
+  if (G > 1024) return fail(nullptr, HB_ERR_UNSUPPORTED, "hb_gemv: too many SMs");
+  const int rg_per_cta = (n_rg + G - 1) / G;
+  const bool whole = kc * 128 <= static_cast<int>(hb::kSlotBytes);
+  const int per_warp = (whole && rg_per_cta >= 16) ? 1 : 0;
+  const int red_rows = per_warp ? 1 : rg_per_cta * 8;
+  const int mb = batch > 1 ? 8 : 1;
+  const size_t fixed = hb::gemv_smem_bytes(0, mb, k, red_rows);
+  int nslots = static_cast<int>((static_cast<size_t>(optin) - fixed - 16 * kMaxSlotsRing) / hb::kSlotBytes);
+  nslots = std::min(nslots, kMaxSlotsRing);
+  if (nslots < kMinSlotsRing) return fail(nullptr, HB_ERR_UNSUPPORTED, "hb_gemv: shape too large for shared memory");
+  const size_t smem = hb::gemv_smem_bytes(nslots, mb, k, red_rows);
+  const void *fn;
+  if (mb == 1) fn = w8 ? reinterpret_cast<const void *>(&hb::gemv_kernel<1, true>) : reinterpret_cast<const void *>(&hb::gemv_kernel<1, false>);
+  else fn = w8 ? reinterpret_cast<const void *>(&hb::gemv_kernel<8, true>) : reinterpret_cast<const void *>(&hb::gemv_kernel<8, false>);
+  cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (err != cudaSuccess) return fail(nullptr, HB_ERR_CUDA, "hb_gemv: %s", cudaGetErrorString(err));
+  hb::GemvParams P{};
+  P.w = static_cast<const uint8_t *>(w_dev);
+  P.scales = scales_dev;
+  P.rows = rows;
+  P.kc = kc;
+  P.K = k;
+  P.x = static_cast<const __nv_bfloat16 *>(x_dev);
+  P.batch = batch;
+  P.y = y_dev;
+  P.out_mode = out_mode;
+  P.argmax = want_argmax ? 1 : 0;
+  P.argmax_out = argmax_dev;
+  P.ctrl = static_cast<hb::Ctrl *>(scratch_dev);
+  P.part_val = reinterpret_cast<float *>(static_cast<uint8_t *>(scratch_dev) + sizeof(hb::Ctrl));
+  P.part_idx = reinterpret_cast<int *>(P.part_val + 1024 * hb::kMaxBatchGemv);
+  P.nslots = nslots;
+  P.red_rows = red_rows;
+  P.per_warp = per_warp;
+  P.limit_ns = kDefaultLimitNs;
+  void *args[] = {&P};
+  err = cudaLaunchKernel(fn, dim3(G), dim3(hb::kThreads), args, smem, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return fail(nullptr, HB_ERR_CUDA, "hb_gemv launch: %s", cudaGetErrorString(err));
+  return HB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,230 @@
+"""Host object of the B200 decoder engine: the counterpart of the reference's
+``QwenDecoderEngine`` / ``DecoderEngine`` (npu_llm/runtime/qwen_engine.py:37-102,
+npu_llm/runtime/engine.py:29-91).
+
+Differences from the reference object, all on the device side of the
+boundary: the embedding gather, the RoPE tables and the K/V append happen on
+the GPU, so ``step`` takes the token id instead of an embedding row; the LM
+head and the argmax run on the GPU for both model families; the KV cache has
+``max_slots`` independent slots (streams).
+"""
+
+import ctypes
+
+import numpy as np
+
+from runtime import hb_lib, layout
+from runtime.synthetic import shape_from_metadata
+
+
+def rope_tables(theta, head_dim, context):
+    """cos/sin of ``float32(position) * inv_freq`` with
+    ``inv_freq = 1 / theta ** (arange(d/2) / (d/2))``, all float32 and
+    evaluated by NumPy exactly as the reference host does
+    (npu_llm/runtime/qwen_engine.py:44-51, 68-71) -- the device reads the table."""
+    half = head_dim // 2
+    inv = 1.0 / (np.float32(theta) ** (np.arange(half, dtype=np.float32) / np.float32(half)))
+    inv = inv.astype(np.float32)
+    cos = np.empty((context, half), np.float32)
+    sin = np.empty((context, half), np.float32)
+    for position in range(context):
+        angle = np.float32(position) * inv
+        cos[position] = np.cos(angle)
+        sin[position] = np.sin(angle)
+    return cos, sin
+
+
+class B200DecoderEngine:
+    """All decoder layers + final norm + LM head + argmax of one position per
+    call, on one GPU."""
+
+    def __init__(self, model, weights="bf16", device=0, max_slots=1, max_batch=1, blob=None):
+        self._lib = hb_lib.load()
+        self._handle = None
+        meta = model.metadata
+        self.shape = shape_from_metadata(meta)
+        layout.check_dims(self.shape, weights)
+        if self.shape.context != 64:
+            raise ValueError("the engine keeps the reference's 64-token context")
+        self.weights = weights
+        self.layers = self.shape.layers
+        self.vocab = self.shape.vocab
+        self.context = self.shape.context
+        self.max_slots = int(max_slots)
+        self.max_batch = int(max_batch)
+        if blob is None:
+            blob, lay = layout.pack(model, weights)
+        else:
+            blob, lay = blob
+        self._layout = lay
+        self._layer_table = lay.layer_table()
+        cos, sin = rope_tables(self.shape.rope_theta, self.shape.head_dim, self.context)
+        self._cos = np.ascontiguousarray(cos)
+        self._sin = np.ascontiguousarray(sin)
+        desc = hb_lib.HbModelDesc()
+        desc.abi_version = hb_lib.ABI_VERSION
+        desc.family = 1 if self.shape.family == "qwen2" else 0
+        desc.hidden = self.shape.hidden
+        desc.intermediate = self.shape.intermediate
+        desc.q_heads = self.shape.q_heads
+        desc.kv_heads = self.shape.kv_heads
+        desc.head_dim = self.shape.head_dim
+        desc.layers = self.shape.layers
+        desc.vocab = self.shape.vocab
+        desc.context = self.context
+        desc.has_qkv_bias = 1 if any(k.endswith("qkv_bias") for k in model.tensors) else 0
+        desc.weight_format = layout.FORMATS[weights]
+        desc.max_slots = self.max_slots
+        desc.max_batch = self.max_batch
+        desc.rms_eps = float(np.float32(self.shape.rms_eps))
+        desc.blob_bytes = lay.total
+        desc.gamma_final = lay.gamma_final
+        desc.w_lm = lay.w_lm
+        desc.s_lm = lay.s_lm
+        desc.embedding = lay.embedding
+        desc.layer_offsets = self._layer_table
+        desc.rope_cos = self._cos.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        desc.rope_sin = self._sin.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        handle = ctypes.c_void_p()
+        hb_lib.check(self._lib.hb_create(ctypes.byref(desc), int(device), ctypes.byref(handle)))
+        self._handle = handle
+        try:
+            blob = np.ascontiguousarray(blob)
+            hb_lib.check(
+                self._lib.hb_load_weights(handle, blob.ctypes.data, blob.nbytes, layout.LAYOUT_VERSION),
+                handle,
+            )
+        except Exception:
+            self.close()
+            raise
+        self._logits = np.empty(self.vocab, np.float32)
+        self._argmax = ctypes.c_int32(-1)
+
+    # -- helpers ---------------------------------------------------------------
+    def _check(self, rc):
+        hb_lib.check(rc, self._handle)
+
+    def _live(self):
+        if self._handle is None:
+            raise RuntimeError("engine is closed")
+        return self._handle
+
+    # -- reference engine surface -------------------------------------------------
+    def step(self, token_id, position, logits=True, slot=0):
+        """One position through every layer.  Returns the FP32 logits (a fresh
+        array) or, with ``logits=False``, None after the layers only."""
+        h = self._live()
+        if logits:
+            out = np.empty(self.vocab, np.float32)
+            self._check(self._lib.hb_step(
+                h, slot, int(token_id), int(position), hb_lib.HB_STEP_LOGITS,
+                out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), ctypes.byref(self._argmax)))
+            return out
+        self._check(self._lib.hb_step(h, slot, int(token_id), int(position), 0, None, None))
+        return None
+
+    def step_argmax(self, token_id, position, slot=0):
+        """One position with the LM head; returns only the argmax token."""
+        h = self._live()
+        self._check(self._lib.hb_step(
+            h, slot, int(token_id), int(position), hb_lib.HB_STEP_ARGMAX, None,
+            ctypes.byref(self._argmax)))
+        return int(self._argmax.value)
+
+    def prefill(self, ids, start=0, slot=0, logits=False):
+        """Sequential prefill of ``ids`` at positions start..; returns
+        (argmax of the last position, its logits or None)."""
+        h = self._live()
+        ids = np.ascontiguousarray(ids, np.int32)
+        out = np.empty(self.vocab, np.float32) if logits else None
+        self._check(self._lib.hb_prefill(
+            h, slot, ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), ids.size, int(start),
+            out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)) if logits else None,
+            ctypes.byref(self._argmax)))
+        return int(self._argmax.value), out
+
+    def generate(self, prompt_ids, new_tokens, start=0, slot=0):
+        """Device-resident greedy generation; returns the ``new_tokens`` ids."""
+        h = self._live()
+        ids = np.ascontiguousarray(prompt_ids, np.int32)
+        out = np.empty(int(new_tokens), np.int32)
+        self._check(self._lib.hb_generate(
+            h, slot, ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), ids.size, int(start),
+            int(new_tokens), out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))))
+        return [int(t) for t in out]
+
+    def step_batch(self, slots, tokens, positions, logits=False):
+        h = self._live()
+        n = len(slots)
+        s = np.ascontiguousarray(slots, np.int32)
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        out = np.empty((n, self.vocab), np.float32) if logits else None
+        am = np.empty(n, np.int32)
+        ip = ctypes.POINTER(ctypes.c_int32)
+        self._check(self._lib.hb_step_batch(
+            h, n, s.ctypes.data_as(ip), t.ctypes.data_as(ip), p.ctypes.data_as(ip),
+            hb_lib.HB_STEP_ARGMAX,
+            out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)) if logits else None,
+            am.ctypes.data_as(ip)))
+        return am, out
+
+    def reset(self, slot=None):
+        """Forget every cached position (of one slot, or of all)."""
+        h = self._live()
+        slots = range(self.max_slots) if slot is None else [slot]
+        for s in slots:
+            self._check(self._lib.hb_reset(h, int(s)))
+
+    def copy_prefix(self, src, dst, n_positions):
+        self._check(self._lib.hb_copy_prefix(self._live(), int(src), int(dst), int(n_positions)))
+
+    def hidden(self):
+        """BF16 residual stream rows after the last step (as uint16 bits)."""
+        out = np.empty((8, self.shape.hidden), np.uint16)
+        self._check(self._lib.hb_debug_dump(self._live(), hb_lib.HB_DUMP_HIDDEN, out.ctypes.data, out.nbytes))
+        return out
+
+    def kv_cache(self, slot=0):
+        """BF16 bits of one slot's cache: [layers, kv_heads, 2, context, 64]."""
+        s = self.shape
+        out = np.zeros((s.layers, s.kv_heads, 2, self.context, s.head_dim), np.uint16)
+        out.view(np.int32).reshape(-1)[0] = slot
+        self._check(self._lib.hb_debug_dump(self._live(), hb_lib.HB_DUMP_KV, out.ctypes.data, out.nbytes))
+        return out
+
+    def phase_trace(self):
+        """globaltimer stamps [G, 4L+2] of the last launch traced with profile(trace=True)."""
+        g = self._lib.hb_device_sm_count(0)
+        out = np.zeros((g, 4 * self.layers + 2), np.uint64)
+        self._check(self._lib.hb_debug_dump(self._live(), hb_lib.HB_DUMP_TRACE, out.ctypes.data, out.nbytes))
+        return out
+
+    def profile(self, enable=True, trace=False):
+        self._check(self._lib.hb_profile(self._live(), (1 if enable else 0) | (2 if trace else 0)))
+
+    def profile_read(self, max_launches=65536):
+        buf = np.zeros(max_launches, np.float32)
+        count = ctypes.c_int(0)
+        self._check(self._lib.hb_profile_read(
+            self._live(), buf.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), max_launches,
+            ctypes.byref(count)))
+        return buf[: count.value].copy()
+
+    def set_stream(self, stream_handle):
+        self._check(self._lib.hb_set_stream(self._live(), ctypes.c_void_p(stream_handle or None)))
+
+    def test_stall_next(self, limit_ns):
+        self._check(self._lib.hb_test_stall_next(self._live(), int(limit_ns)))
+
+    def close(self):
+        """Release every device buffer (idempotent)."""
+        if self._handle is not None:
+            self._lib.hb_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

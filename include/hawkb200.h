@@ -1,0 +1,189 @@
+/*
+ * hawkb200.h -- C ABI of libhawkb200.so, the B200 (sm_100a) decoder engine.
+ *
+ * Drop-in replacement for the device side of the reference's single-dispatch
+ * decoder engine (c8dhjp4tyv-bit/hawkpoint-npu-llm): the IRON designs
+ * npu_llm/designs/{engine,qwen_engine}.py, their AIE2 kernels
+ * npu_llm/kernels/{engine_bf16,qwen_engine_bf16,qwen_engine_hub_bf16}.cc, and the
+ * host engines npu_llm/runtime/{engine,qwen_engine}.py.  Python binds it with
+ * ctypes (hawkpoint-npu-llm_b200/runtime/hb_lib.py); INTEGRATION.md shows the
+ * binding a reference maintainer would add.
+ *
+ * Rules: every function returns 0 (HB_OK) or a negative HB_ERR_* code; the
+ * message of the last failure is in hb_last_error().  An engine is not
+ * thread-safe (one engine per GPU per process, calls serialised by the caller,
+ * as npu_llm/api_server.py:646-678 serialises NPU calls).  The engine owns its
+ * device memory; the caller owns host buffers.  Pointers named *_dev are device
+ * pointers; all others are host pointers.  Device-side waits are bounded in
+ * time; a wait that runs out makes the call return HB_ERR_DEVICE_TIMEOUT and
+ * leaves the engine usable.
+ */
+#ifndef HAWKB200_H
+#define HAWKB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HB_ABI_VERSION 1
+
+enum {
+  HB_OK = 0,
+  HB_ERR_INVALID_ARG = -1,     /* bad argument: ValueError on the Python side */
+  HB_ERR_CUDA = -2,            /* CUDA runtime error */
+  HB_ERR_DEVICE_TIMEOUT = -3,  /* a bounded device wait gave up */
+  HB_ERR_UNSUPPORTED = -4,     /* shape / layout this build does not run */
+  HB_ERR_STATE = -5            /* e.g. weights not loaded */
+};
+
+enum { HB_FAMILY_LLAMA = 0, HB_FAMILY_QWEN2 = 1 };
+enum { HB_WEIGHTS_BF16 = 0, HB_WEIGHTS_W8 = 1 };
+
+/* hb_step / hb_prefill / hb_step_batch flags */
+enum {
+  HB_STEP_ARGMAX = 1,   /* run final norm + LM head + argmax */
+  HB_STEP_LOGITS = 2    /* also copy the FP32 logits out (implies ARGMAX) */
+};
+
+/* Byte offsets (from the start of the weight blob) of one layer's tensors.
+ * The blob layout is defined by runtime/layout.py; the engine only validates
+ * it.  Projections are stored "row-group major": 8 consecutive output rows
+ * form a group, and a group stores its K dimension as 16-byte column chunks,
+ * each chunk holding those 8 rows (chunk j of row r at group_base + j*128 +
+ * r*16).  o_proj is split by attention head into [hidden x head_dim] slabs;
+ * gate_up alternates 8 gate rows and the 8 matching up rows.  W8 projections
+ * store int8 in the same arrangement plus one FP32 scale per (packed) row. */
+typedef struct hb_layer_offsets {
+  uint64_t gamma_in, gamma_post, qkv_bias;      /* FP32 [hidden], [hidden], [qkv] */
+  uint64_t w_qkv, s_qkv;                        /* s_*: W8 row scales, else 0 */
+  uint64_t w_o, s_o;
+  uint64_t w_gate_up, s_gate_up;
+  uint64_t w_down, s_down;
+} hb_layer_offsets;
+
+typedef struct hb_model_desc {
+  int32_t abi_version;      /* HB_ABI_VERSION */
+  int32_t family;           /* HB_FAMILY_* */
+  int32_t hidden, intermediate, q_heads, kv_heads, head_dim, layers, vocab, context;
+  int32_t has_qkv_bias;
+  int32_t weight_format;    /* HB_WEIGHTS_* */
+  int32_t max_slots;        /* independent KV-cache slots (streams) */
+  int32_t max_batch;        /* rows per batched step (1 or 8) */
+  float rms_eps;
+  int32_t reserved0;
+  uint64_t blob_bytes;
+  uint64_t gamma_final, w_lm, s_lm, embedding;  /* embedding: BF16 row-major [vocab x hidden] */
+  const hb_layer_offsets *layer_offsets;        /* [layers], host memory, copied */
+  const float *rope_cos;    /* [context x head_dim/2], host memory, copied */
+  const float *rope_sin;
+} hb_model_desc;
+
+typedef struct hb_engine hb_engine;
+
+/* Engine lifecycle.  Replaces QwenDecoderEngine.__init__ / DecoderEngine.__init__
+ * (npu_llm/runtime/qwen_engine.py:41-63, npu_llm/runtime/engine.py:32-49):
+ * allocates the device weights, the KV cache of every slot and the step
+ * buffers on `device`. */
+int hb_create(const hb_model_desc *desc, int device, hb_engine **out);
+
+/* Copies the packed weight blob (runtime/layout.py) to the device.  Replaces
+ * the iron.tensor(pack_weights(...)) upload (npu_llm/runtime/qwen_engine.py:52-54). */
+int hb_load_weights(hb_engine *engine, const void *host_blob, size_t bytes,
+                    int layout_version);
+
+/* Releases every device buffer.  Replaces QwenDecoderEngine.close
+ * (npu_llm/runtime/qwen_engine.py:96-102).  Accepts NULL. */
+int hb_destroy(hb_engine *engine);
+
+/* One position of one stream through every layer, then (flags) the final
+ * norm, the LM head and the argmax.  Replaces QwenDecoderEngine.step /
+ * DecoderEngine.step (npu_llm/runtime/qwen_engine.py:77-94,
+ * npu_llm/runtime/engine.py:65-82) plus the host argmax of
+ * NPUDecoder._decode_result (npu_llm/runtime/generate.py:709-714).  The
+ * embedding gather, RoPE and the K/V append all run on the device.
+ * logits_out (host, [vocab] FP32) may be NULL; argmax_out may be NULL. */
+int hb_step(hb_engine *engine, int slot, int token_id, int position, int flags,
+            float *logits_out, int32_t *argmax_out);
+
+/* Sequential prefill of n prompt positions start_pos..start_pos+n-1, one
+ * engine step each, only the last with the LM head -- the loop of
+ * npu_llm/runtime/generate.py:1110-1126.  last_logits may be NULL. */
+int hb_prefill(hb_engine *engine, int slot, const int32_t *ids, int n,
+               int start_pos, float *last_logits, int32_t *argmax_out);
+
+/* Device-resident greedy generation (no host round trip per token): prefill
+ * ids[start_pos..n_prompt-1], then n_new-1 further greedy steps feeding each
+ * argmax back on the device.  out_tokens receives n_new ids.  Same result as
+ * the host loop of npu_llm/runtime/generate.py:1110-1158 with greedy
+ * selection and no stop strings. */
+int hb_generate(hb_engine *engine, int slot, const int32_t *ids, int n_prompt,
+                int start_pos, int n_new, int32_t *out_tokens);
+
+/* Several streams, one position each, in one pass over the weights
+ * (n <= max_batch).  New in this build (the reference serialises requests). */
+int hb_step_batch(hb_engine *engine, int n, const int32_t *slots,
+                  const int32_t *token_ids, const int32_t *positions, int flags,
+                  float *logits_out, int32_t *argmax_out);
+
+/* KV-cache management.  hb_reset replaces QwenDecoderEngine.reset
+ * (npu_llm/runtime/qwen_engine.py:65-66); hb_copy_prefix copies positions
+ * [0, n_positions) of every layer from one slot to another (prefix sharing). */
+int hb_reset(hb_engine *engine, int slot);
+int hb_copy_prefix(hb_engine *engine, int src_slot, int dst_slot, int n_positions);
+
+/* Diagnostics.  hb_debug_dump copies engine state for parity tests:
+ * HB_DUMP_HIDDEN = BF16 residual stream [max_batch x hidden] after the last
+ * step; HB_DUMP_KV = BF16 cache of one slot [layers][kv_heads][2][context][head_dim]
+ * (slot taken from *(int*)out on entry). */
+enum { HB_DUMP_HIDDEN = 0, HB_DUMP_KV = 1 };
+const char *hb_last_error(const hb_engine *engine);
+int hb_debug_dump(hb_engine *engine, int what, void *out, size_t bytes);
+
+/* Profiling: when enabled, each decode-kernel launch is bracketed by CUDA
+ * events on the engine's stream; hb_profile_read returns the durations (ms)
+ * of up to max launches since the last read and clears the record. */
+int hb_profile(hb_engine *engine, int enable);
+int hb_profile_read(hb_engine *engine, float *ms, int max, int *count);
+
+/* Runs the engine's work on the caller's stream (cudaStream_t as void*);
+ * NULL restores the engine's own stream. */
+int hb_set_stream(hb_engine *engine, void *stream);
+
+/* Fault-path test hook: the next launch makes every CTA wait on a device flag
+ * that nothing sets, with the given limit (ns), so the bounded wait runs out
+ * and the call returns HB_ERR_DEVICE_TIMEOUT.  No GPU fault is involved. */
+int hb_test_stall_next(hb_engine *engine, uint64_t limit_ns);
+
+/* Standalone weight-streaming GEMV (the microbenchmark of the reference's
+ * q_gemv4 / q_gemv_slice, npu_llm/kernels/qwen_engine_common.h:89-110, and
+ * the BF16 projection of npu_llm/runtime/cpu_backend.py:64-69):
+ *   y[b][r] = bf16(sum_k W[r][k] * x[b][k])        (HB_GEMV_OUT_BF16)
+ *   y[b][r] = sum_k W[r][k] * x[b][k]   (FP32)     (HB_GEMV_OUT_F32)
+ * with W8 weights the sum is multiplied by scales[r] before rounding.
+ * HB_GEMV_ARGMAX also writes argmax_dev[b] (first index of the maximum, as
+ * np.argmax).  W is packed row-group major (runtime/layout.py); rows % 8 == 0,
+ * k % 16 == 0; batch is 1..8.  All pointers are device pointers; scratch_dev
+ * must hold hb_gemv_scratch_bytes(rows, batch) bytes.  Runs on `stream`. */
+enum { HB_GEMV_OUT_BF16 = 0, HB_GEMV_OUT_F32 = 1, HB_GEMV_OUT_NONE = 2 };
+enum { HB_GEMV_ARGMAX = 4 };
+size_t hb_gemv_scratch_bytes(int rows, int batch);
+int hb_gemv(const void *w_dev, const float *scales_dev, int weight_format,
+            int rows, int k, const void *x_dev, int batch, void *y_dev,
+            int flags, int32_t *argmax_dev, void *scratch_dev,
+            size_t scratch_bytes, void *stream);
+
+/* Library-level error text (for calls that have no engine, e.g. hb_gemv). */
+const char *hb_library_error(void);
+
+/* Number of multiprocessors the persistent kernels are sized for on `device`
+ * (0 when no device is present). */
+int hb_device_sm_count(int device);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HAWKB200_H */
