@@ -1,20 +1,30 @@
 // hb_decoder.cuh -- the persistent decode kernel.
 //
-// One cooperative launch runs a range of "phases" of one decode step for up
-// to MB batch rows.  For each layer l there are four phases, separated by a
-// bounded grid barrier:
-//   A (4l+0)  x = rmsnorm(h) ; qkv = bf16(bf16(Wqkv x) + bias)      (cpu_backend.py:131-143)
-//   B (4l+1)  rotate q,k (RoPE) ; append k,v to the KV cache ; GQA attention
-//             of one head per CTA ; that head's slice of o_proj -> FP32 partials
-//                                                                    (cpu_backend.py:78-129)
-//   C (4l+2)  h1 = bf16(bf16(sum of o partials) + h) ; x2 = rmsnorm(h1) ;
-//             act = bf16(silu(bf16 gate) * bf16 up)                  (cpu_backend.py:145-165)
-//   D (4l+3)  h = bf16(bf16(Wdown act) + h1)                          (cpu_backend.py:166-171)
+// One cooperative launch (one CTA per SM, all co-resident) runs a range of
+// phases of one decode step for up to MB batch rows.  Per layer l:
+//   1 (4l+0)  x = rmsnorm(h) ; qkv = bf16(bf16(Wqkv x) + bias)       (cpu_backend.py:131-143)
+//   2 (4l+1)  RoPE on q,k ; append k,v to the KV cache ; GQA attention over
+//             every head ; h1 = bf16(bf16(Wo a) + h)                   (cpu_backend.py:78-151)
+//   3 (4l+2)  x2 = rmsnorm(h1) ; act = bf16(silu(bf16 gate) * bf16 up) (cpu_backend.py:152-165)
+//   4 (4l+3)  h' = bf16(bf16(Wdown act) + h1)                           (cpu_backend.py:166-171)
 // and after the last layer
-//   E (4L)    logits = W_lm rmsnorm(h) (FP32) ; argmax (first maximum)
-//                                                     (cpu_backend.py:173-181, generate.py:709-714)
-// A producer warp streams every weight chunk of the launch through the
-// shared-memory ring (hb_stream.cuh) without waiting on the barriers.
+//   E (4L)    logits = W_lm rmsnorm(h) (FP32) ; argmax, first maximum
+//                                                    (cpu_backend.py:173-181, generate.py:709-714)
+// Each phase's CTAs own a contiguous share of the projection rows.  Results
+// move between CTAs through "LL" words in global memory: one 64-bit store of
+// {32-bit payload, 32-bit epoch}, read with 64-bit loads until the epoch
+// matches this launch's.  A reader therefore needs no barrier and no fence:
+// a word is valid exactly when its epoch is current.  Every (layer, phase)
+// has its own buffer, so no word is rewritten within a launch.
+//
+// A producer warp streams every weight chunk -- and, for phase 2, each row's
+// K/V history -- through the shared-memory ring (hb_stream.cuh) without
+// waiting on activations, so HBM keeps streaming while consumers wait for
+// the previous phase's words.
+//
+// KV cache layout per (slot, layer, kv head): K transposed [64 dims][CTX]
+// (positions contiguous, so lane-per-position score loops read consecutive
+// shared-memory addresses), then V [CTX][64].
 #pragma once
 
 #include "hb_stream.cuh"
@@ -23,6 +33,7 @@ namespace hb {
 
 constexpr int kMaxBatch = 8;
 constexpr int kHeadDim = 64;
+constexpr int kMaxHPerThread = 4;  // hidden <= 1024
 
 struct LayerPtrs {
   const float *gamma_in, *gamma_post, *bias;
@@ -36,9 +47,9 @@ struct LayerPtrs {
   const float *s_down;
 };
 
-// Inputs of a step, in device memory.  In chained mode (device-resident greedy
-// generation) the last CTA to finish advances row 0: next position, next token
-// (the prompt's, or this step's argmax).
+// Inputs of a step, in device memory.  In chained mode (device-resident
+// greedy generation) the last CTA also advances row 0: next position, next
+// token (the prompt's, or this step's argmax).
 struct StepState {
   int token[kMaxBatch];
   int pos[kMaxBatch];
@@ -58,24 +69,21 @@ struct Result {
 struct DecParams {
   int H, I, QH, KVH, L, V, CTX, QKV, group, has_bias;
   float eps;
-  int kc_h, kc_i, kc_d;   // 16-byte chunk columns of K = hidden, intermediate, head_dim
-  int slab_bytes;         // bytes of one head's o_proj slab
+  int kc_h, kc_i;   // 16-byte chunk columns of K = hidden, intermediate
   const LayerPtrs *layers;
   const float *gamma_final;
   const uint8_t *w_lm;
   const float *s_lm;
   const __nv_bfloat16 *embed;
   const float *rope_cos, *rope_sin;  // [CTX][32]
-  __nv_bfloat16 *kv;                 // [slots][L][KVH][2][CTX][64]
-  __nv_bfloat16 *hbuf;               // [MB][H]
-  __nv_bfloat16 *qkv;                // [MB][QKV]
-  float *opart;                      // [MB][QH][H]
-  __nv_bfloat16 *act;                // [MB][I]
+  __nv_bfloat16 *kv;                 // [slots][L][KVH][K^T 64xCTX | V CTXx64]
+  uint64_t *ll;                      // LL words, see ll_* below
   float *logits;                     // [MB][V]
-  float *part_val;                   // [G][MB]
-  int *part_idx;                     // [G][MB]
+  float *part_val;                   // [G][kMaxBatch]
+  int *part_idx;
   Result *result;
   StepState *st;
+  unsigned int *epoch;               // tags this launch's LL words; the last CTA increments it
   const int *prompt;                 // chained: token of each prompt position
   int *gen_out;                      // chained: generated tokens
   int phase_begin, phase_end;
@@ -85,18 +93,22 @@ struct DecParams {
   int xs_elems;                      // BF16 elements per batch row of xs
   uint64_t limit_ns;
   uint64_t stall_ns;
-  unsigned long long *trace;         // optional [G][4L+2] phase timestamps
+  unsigned long long *trace;         // optional [G][4L+2][4] phase timestamps
 };
 
-// Shared-memory carve-up (offsets from the dynamic smem base).
+// LL buffer layout: per layer a block of kMaxBatch rows of each kind.
+__host__ __device__ inline size_t ll_layer_words(int H, int I, int QKV) {
+  return static_cast<size_t>(kMaxBatch) * (QKV + 2 * H + I) / 2;
+}
+
 struct SmemPlan {
-  size_t ring, full, empty, xs, hx, red, att, misc, total;
+  size_t ring, full, empty, xs, hx, red, qkv, att, misc, total;
 };
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-__host__ __device__ inline SmemPlan smem_plan(int nslots, int mb, int xs_elems, int H, int red_rows,
-                                              int ctx) {
+__host__ __device__ inline SmemPlan smem_plan(int nslots, int mb, int xs_elems, int H, int QKV,
+                                              int QH, int KVH, int red_rows, int ctx) {
   SmemPlan s;
   size_t o = 0;
   s.ring = o;
@@ -112,12 +124,73 @@ __host__ __device__ inline SmemPlan smem_plan(int nslots, int mb, int xs_elems, 
   o += align_up(static_cast<size_t>(mb) * H * 4, 128);
   s.red = o;
   o += align_up(static_cast<size_t>(kWarps) * mb * red_rows * 4, 128);
+  s.qkv = o;
+  o += align_up(static_cast<size_t>(mb) * QKV * 2, 128);
   s.att = o;
-  o += align_up((3 * kHeadDim + ctx + kWarps * kHeadDim) * 4, 128);
+  o += align_up(static_cast<size_t>(QH * kHeadDim + 2 * KVH * kHeadDim + QH * ctx) * 4, 128);
   s.misc = o;
   o += 1024;
   s.total = o;
   return s;
+}
+
+// ---- LL words ---------------------------------------------------------------
+__device__ __forceinline__ void ll_store(uint64_t *p, uint32_t data, uint32_t epoch) {
+  const uint64_t v = (static_cast<uint64_t>(epoch) << 32) | data;
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ll_load(const uint64_t *p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const uint32_t a = __bfloat16_as_ushort(f2bf(lo));
+  const uint32_t b = __bfloat16_as_ushort(f2bf(hi));
+  return a | (b << 16);
+}
+
+// All consumer threads: wait until words [0, n) of src carry `epoch`, and
+// pass each payload to sink(i, payload).  Up to 8 loads in flight per thread.
+template <class Sink>
+__device__ __forceinline__ bool ll_gather(const uint64_t *src, int n, uint32_t epoch, Ctrl *ctrl,
+                                          uint64_t limit_ns, Sink &&sink) {
+  const int tid = threadIdx.x;
+  constexpr int U = 8;
+  for (int base = tid; base < n; base += kConsumerThreads * U) {
+    uint32_t pend = 0;
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (base + u * kConsumerThreads < n) pend |= 1u << u;
+    uint64_t start = 0;
+    uint32_t spins = 0;
+    while (pend) {
+      uint64_t v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (pend & (1u << u)) v[u] = ll_load(src + base + u * kConsumerThreads);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if ((pend & (1u << u)) && static_cast<uint32_t>(v[u] >> 32) == epoch) {
+          sink(base + u * kConsumerThreads, static_cast<uint32_t>(v[u]));
+          pend &= ~(1u << u);
+        }
+      }
+      if (pend) {
+        if (start == 0) start = globaltimer_ns();
+        if ((++spins & 31u) == 0) {
+          if (ld_volatile_int(&ctrl->abort)) return false;
+          if (globaltimer_ns() - start > limit_ns) {
+            raise_error(ctrl, kErrTimeout, kWhereGrid);
+            return false;
+          }
+        }
+      }
+    }
+  }
+  return true;
 }
 
 template <int MB, bool W8>
@@ -126,95 +199,130 @@ struct DecoderCta {
   Ring ring;
   __nv_bfloat16 *xs;
   float *hx, *red, *att;
-  int *s_tok, *s_pos, *s_slot, *s_flag, *s_last;
-  float *s_norm;      // [kWarps * MB] partial sums, then [MB] inverse rms
-  float *s_bestv;     // [kWarps * MB]
+  uint32_t *qkv_s;
+  int *s_tok, *s_pos, *s_slot, *s_misc;
+  float *s_norm;      // [kWarps * kMaxBatch] partial sums, then [kMaxBatch] inverse rms
+  float *s_bestv;     // [kWarps * kMaxBatch]
   int *s_besti;
   int cta, G, mrows, tid;
+  uint32_t epoch;
+  size_t lw;          // LL words per layer block
 
   __device__ DecoderCta(const DecParams &p, uint8_t *smem) : P(p) {
-    const SmemPlan sp = smem_plan(P.nslots, MB, P.xs_elems, P.H, P.red_rows, P.CTX);
+    const SmemPlan sp = smem_plan(P.nslots, MB, P.xs_elems, P.H, P.QKV, P.QH, P.KVH, P.red_rows, P.CTX);
     ring.slots = smem + sp.ring;
     ring.full = reinterpret_cast<uint64_t *>(smem + sp.full);
     ring.empty = reinterpret_cast<uint64_t *>(smem + sp.empty);
     ring.nslots = P.nslots;
-    ring.counter = 0;
+    ring.slot = 0;
+    ring.parity = 0;
+    ring.timing = P.trace != nullptr;
+    ring.wait_ns = 0;
     xs = reinterpret_cast<__nv_bfloat16 *>(smem + sp.xs);
     hx = reinterpret_cast<float *>(smem + sp.hx);
     red = reinterpret_cast<float *>(smem + sp.red);
+    qkv_s = reinterpret_cast<uint32_t *>(smem + sp.qkv);
     att = reinterpret_cast<float *>(smem + sp.att);
     int *mi = reinterpret_cast<int *>(smem + sp.misc);
     s_tok = mi;
     s_pos = mi + kMaxBatch;
     s_slot = mi + 2 * kMaxBatch;
-    s_flag = mi + 3 * kMaxBatch;
-    s_last = mi + 3 * kMaxBatch + 1;
-    s_norm = reinterpret_cast<float *>(mi + 4 * kMaxBatch);          // kWarps*MB + MB floats
+    s_misc = mi + 3 * kMaxBatch;  // [0] rows, [1] last-CTA flag, [2] epoch
+    s_norm = reinterpret_cast<float *>(mi + 4 * kMaxBatch);
     s_bestv = s_norm + kWarps * kMaxBatch + kMaxBatch;
     s_besti = reinterpret_cast<int *>(s_bestv + kWarps * kMaxBatch);
     cta = blockIdx.x;
     G = gridDim.x;
     tid = threadIdx.x;
     mrows = 0;
+    epoch = 0;
+    lw = ll_layer_words(P.H, P.I, P.QKV);
   }
 
-  // ---- work split ------------------------------------------------------------
-  __device__ int head_of(int c) const { return (c * P.QH) / G; }
-  __device__ int first_cta_of_head(int h) const { return (h * G + P.QH - 1) / P.QH; }
+  // ---- LL buffers of layer l, batch row m ----------------------------------
+  __device__ uint64_t *ll_qkv(int l, int m) const { return P.ll + l * lw + static_cast<size_t>(m) * P.QKV / 2; }
+  __device__ uint64_t *ll_h1(int l, int m) const {
+    return P.ll + l * lw + static_cast<size_t>(kMaxBatch) * P.QKV / 2 + static_cast<size_t>(m) * P.H / 2;
+  }
+  __device__ uint64_t *ll_act(int l, int m) const {
+    return P.ll + l * lw + static_cast<size_t>(kMaxBatch) * (P.QKV + P.H) / 2 + static_cast<size_t>(m) * P.I / 2;
+  }
+  __device__ uint64_t *ll_hout(int l, int m) const {
+    return P.ll + l * lw + static_cast<size_t>(kMaxBatch) * (P.QKV + P.H + P.I) / 2 +
+           static_cast<size_t>(m) * P.H / 2;
+  }
 
+  // ---- work split -------------------------------------------------------------
   __device__ MatRange phase_range(int k) const {
-    MatRange r{nullptr, 0, 0, 0};
     if (k >= 4 * P.L) {
       const int n = P.V / 8;
-      r = MatRange{P.w_lm, split_lo(n, G, cta), split_lo(n, G, cta + 1), P.kc_h};
-      return r;
+      return MatRange{P.w_lm, split_lo(n, G, cta), split_lo(n, G, cta + 1), P.kc_h};
     }
     const LayerPtrs &lp = P.layers[k >> 2];
     switch (k & 3) {
       case 0: {
         const int n = P.QKV / 8;
-        r = MatRange{lp.w_qkv, split_lo(n, G, cta), split_lo(n, G, cta + 1), P.kc_h};
-        break;
+        return MatRange{lp.w_qkv, split_lo(n, G, cta), split_lo(n, G, cta + 1), P.kc_h};
       }
       case 1: {
-        const int h = head_of(cta);
-        const int c0 = first_cta_of_head(h), c1 = first_cta_of_head(h + 1);
         const int n = P.H / 8;
-        r = MatRange{lp.w_o + static_cast<size_t>(h) * P.slab_bytes, split_lo(n, c1 - c0, cta - c0),
-                     split_lo(n, c1 - c0, cta - c0 + 1), P.kc_d};
-        break;
+        return MatRange{lp.w_o, split_lo(n, G, cta), split_lo(n, G, cta + 1), P.kc_h};
       }
       case 2: {
         const int n = P.I / 8;  // gate/up pair blocks
-        r = MatRange{lp.w_gu, 2 * split_lo(n, G, cta), 2 * split_lo(n, G, cta + 1), P.kc_h};
-        break;
+        return MatRange{lp.w_gu, 2 * split_lo(n, G, cta), 2 * split_lo(n, G, cta + 1), P.kc_h};
       }
       default: {
         const int n = P.H / 8;
-        r = MatRange{lp.w_down, split_lo(n, G, cta), split_lo(n, G, cta + 1), P.kc_i};
-        break;
+        return MatRange{lp.w_down, split_lo(n, G, cta), split_lo(n, G, cta + 1), P.kc_i};
       }
+    }
+  }
+
+  // K^T (kind 0) or V (kind 1) block of one kv head of one slot/layer.
+  __device__ __nv_bfloat16 *kv_block(int slot, int layer, int kvh, int kind) const {
+    return P.kv + (((static_cast<size_t>(slot) * P.L + layer) * P.KVH + kvh) * 2 + kind) *
+                      static_cast<size_t>(P.CTX) * kHeadDim;
+  }
+
+  // trace point (0 start, 1 inputs ready, 2 weights consumed, 3 outputs stored)
+  __device__ __forceinline__ void mark(int k, int point) const {
+    if (P.trace && tid == 0) {
+      unsigned long long *t = P.trace + (static_cast<size_t>(cta) * (4 * P.L + 2) + k) * 8;
+      t[point] = globaltimer_ns();
+      if (point == 1) t[6] = clock64();
+      if (point == 2) t[7] = clock64();
+    }
+  }
+
+  // ---- helpers -------------------------------------------------------------------
+  // Per-thread registers of a norm weight vector (elements tid + 256 j),
+  // loaded before the thread waits for its inputs.
+  struct Gamma {
+    float v[kMaxHPerThread];
+  };
+  __device__ Gamma load_gamma(const float *g) const {
+    Gamma r;
+#pragma unroll
+    for (int j = 0; j < kMaxHPerThread; ++j) {
+      const int i = tid + j * kConsumerThreads;
+      r.v[j] = i < P.H ? g[i] : 0.f;
+    }
+    return r;
+  }
+  // Two consecutive per-row constants (bias / W8 scales) of this thread's
+  // first epilogue pair, loaded early; 0 when absent.
+  __device__ float2 load_pair(const float *base, int row0, int npairs) const {
+    float2 r = make_float2(0.f, 0.f);
+    if (base != nullptr && tid < npairs) {
+      r.x = base[row0 + 2 * tid];
+      r.y = base[row0 + 2 * tid + 1];
     }
     return r;
   }
 
-  // ---- helpers ----------------------------------------------------------------
-  __device__ __forceinline__ float h_in(int layer, int m, int i) const {
-    if (layer == 0) return bf2f(P.embed[static_cast<size_t>(s_tok[m]) * P.H + i]);
-    return bf2f(__ldcg(P.hbuf + static_cast<size_t>(m) * P.H + i));
-  }
-
-  // h1 = bf16(bf16(sum_h o_partial_h [* s_o]) + h_in): identical wherever used.
-  __device__ __forceinline__ float h1_value(const LayerPtrs &lp, int layer, int m, int i) const {
-    float o = 0.f;
-    const float *op = P.opart + static_cast<size_t>(m) * P.QH * P.H + i;
-    for (int h = 0; h < P.QH; ++h) o += __ldcg(op + static_cast<size_t>(h) * P.H);
-    if (W8) o *= lp.s_o[i];
-    return rbf(__fadd_rn(rbf(o), h_in(layer, m, i)));
-  }
-
   // xs[m][i] = bf16((v * inv_rms) * gamma) for v = hx[m][:]  (cpu_backend.py:71-76)
-  __device__ void norm_rows(const float *gamma) {
+  __device__ void norm_rows(const Gamma &gamma) {
     const int warp = tid >> 5, lane = tid & 31;
     for (int m = 0; m < mrows; ++m) {
       float s = 0.f;
@@ -233,10 +341,14 @@ struct DecoderCta {
       s_norm[kWarps * kMaxBatch + tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, P.eps)));
     }
     consumer_sync(kConsumerThreads);
-    for (int idx = tid; idx < mrows * P.H; idx += kConsumerThreads) {
-      const int m = idx / P.H, i = idx - m * P.H;
-      const float inv = s_norm[kWarps * kMaxBatch + m];
-      xs[m * P.xs_elems + i] = f2bf(__fmul_rn(__fmul_rn(hx[idx], inv), gamma[i]));
+#pragma unroll
+    for (int j = 0; j < kMaxHPerThread; ++j) {
+      const int i = tid + j * kConsumerThreads;
+      if (i < P.H)
+        for (int m = 0; m < mrows; ++m) {
+          const float inv = s_norm[kWarps * kMaxBatch + m];
+          xs[m * P.xs_elems + i] = f2bf(__fmul_rn(__fmul_rn(hx[m * P.H + i], inv), gamma.v[j]));
+        }
     }
     consumer_sync(kConsumerThreads);
   }
@@ -248,206 +360,316 @@ struct DecoderCta {
     return v;
   }
 
-  // ---- phases -----------------------------------------------------------------
-  __device__ bool phase_a(int layer) {
-    const LayerPtrs &lp = P.layers[layer];
-    for (int idx = tid; idx < mrows * P.H; idx += kConsumerThreads) {
-      const int m = idx / P.H, i = idx - m * P.H;
-      hx[idx] = h_in(layer, m, i);
-    }
-    consumer_sync(kConsumerThreads);
-    norm_rows(lp.gamma_in);
-    const MatRange r = phase_range(4 * layer);
-    if (!consume_splitk<MB, W8>(ring, r, xs, P.xs_elems, mrows, red, P.red_rows, &P.result->ctrl,
-                                P.limit_ns))
-      return false;
-    consumer_sync(kConsumerThreads);
-    const int nrows = (r.g1 - r.g0) * 8;
-    for (int idx = tid; idx < mrows * nrows; idx += kConsumerThreads) {
-      const int m = idx / nrows, lr = idx - m * nrows;
-      const int row = r.g0 * 8 + lr;
-      float v = red_sum(m, lr);
-      if (W8) v *= lp.s_qkv[row];
-      float y = rbf(v);
-      if (P.has_bias) y = rbf(__fadd_rn(y, lp.bias[row]));
-      P.qkv[static_cast<size_t>(m) * P.QKV + row] = f2bf(y);
+  // hx[m][:] = f32 of the BF16 vector in LL buffer(m)
+  template <class BufFn>
+  __device__ bool gather_to_hx(BufFn &&buf, int nvals) {
+    const int words = nvals / 2;
+    float *h = hx;
+    for (int m = 0; m < mrows; ++m) {
+      float *dst = h + m * P.H;
+      if (!ll_gather(buf(m), words, epoch, &P.result->ctrl, P.limit_ns, [&](int i, uint32_t d) {
+            dst[2 * i] = bf_lo(d);
+            dst[2 * i + 1] = bf_hi(d);
+          }))
+        return false;
     }
     return true;
   }
 
-  __device__ bool phase_b(int layer) {
+  // ---- phases -------------------------------------------------------------------
+  __device__ bool phase_qkv(int layer) {
     const LayerPtrs &lp = P.layers[layer];
-    const int warp = tid >> 5, lane = tid & 31;
-    const int head = head_of(cta);
-    const int kvh = head / P.group;
-    const bool writer = (cta == first_cta_of_head(kvh * P.group));
-    float *aq = att, *ak = att + kHeadDim, *av = att + 2 * kHeadDim;
-    float *sc = att + 3 * kHeadDim;
-    float *pv = sc + P.CTX;
-    for (int m = 0; m < mrows; ++m) {
-      const int p = s_pos[m];
-      __nv_bfloat16 *kcache = P.kv + ((static_cast<size_t>(s_slot[m]) * P.L + layer) * P.KVH + kvh) *
-                                         2 * P.CTX * kHeadDim;
-      __nv_bfloat16 *vcache = kcache + static_cast<size_t>(P.CTX) * kHeadDim;
-      const __nv_bfloat16 *row = P.qkv + static_cast<size_t>(m) * P.QKV;
-      if (tid < 32) {
-        const int d = tid;
-        const float c = P.rope_cos[p * 32 + d], s = P.rope_sin[p * 32 + d];
-        // rotate-half (cpu_backend.py:78-93), multiplies and adds unfused
-        const float q0 = bf2f(__ldcg(row + head * kHeadDim + d));
-        const float q1 = bf2f(__ldcg(row + head * kHeadDim + d + 32));
-        aq[d] = rbf(__fsub_rn(__fmul_rn(q0, c), __fmul_rn(q1, s)));
-        aq[d + 32] = rbf(__fadd_rn(__fmul_rn(q1, c), __fmul_rn(q0, s)));
-        const int kb = P.QH * kHeadDim + kvh * kHeadDim;
-        const float k0 = bf2f(__ldcg(row + kb + d)), k1 = bf2f(__ldcg(row + kb + d + 32));
-        const float ka = rbf(__fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, s)));
-        const float kz = rbf(__fadd_rn(__fmul_rn(k1, c), __fmul_rn(k0, s)));
-        ak[d] = ka;
-        ak[d + 32] = kz;
-        const int vb = (P.QH + P.KVH) * kHeadDim + kvh * kHeadDim;
-        const __nv_bfloat16 v0 = __ldcg(row + vb + d), v1 = __ldcg(row + vb + d + 32);
-        av[d] = bf2f(v0);
-        av[d + 32] = bf2f(v1);
-        if (writer) {
-          kcache[p * kHeadDim + d] = f2bf(ka);
-          kcache[p * kHeadDim + d + 32] = f2bf(kz);
-          vcache[p * kHeadDim + d] = v0;
-          vcache[p * kHeadDim + d + 32] = v1;
-        }
+    const MatRange r = phase_range(4 * layer);
+    const int npairs = (r.g1 - r.g0) * 4;
+    const Gamma gamma = load_gamma(lp.gamma_in);
+    const float2 bias0 = load_pair(P.has_bias ? lp.bias : nullptr, r.g0 * 8, npairs);
+    const float2 scale0 = load_pair(W8 ? lp.s_qkv : nullptr, r.g0 * 8, npairs);
+    if (layer == 0) {
+      for (int idx = tid; idx < mrows * P.H; idx += kConsumerThreads) {
+        const int m = idx / P.H, i = idx - m * P.H;
+        hx[idx] = bf2f(P.embed[static_cast<size_t>(s_tok[m]) * P.H + i]);
       }
-      consumer_sync(kConsumerThreads);
-      // scores: warp per position, lane per pair of dims
-      for (int s = warp; s <= p; s += kWarps) {
-        float k0, k1;
-        if (s == p) {
-          k0 = ak[2 * lane];
-          k1 = ak[2 * lane + 1];
-        } else {
-          const uint32_t kk = __ldcg(reinterpret_cast<const unsigned int *>(kcache + s * kHeadDim) + lane);
-          k0 = bf_lo(kk);
-          k1 = bf_hi(kk);
-        }
-        float part = aq[2 * lane] * k0;
-        part = fmaf(aq[2 * lane + 1], k1, part);
-        part = warp_sum(part);
-        if (lane == 0) sc[s] = part * 0.125f;
-      }
-      consumer_sync(kConsumerThreads);
-      if (warp == 0) {
-        float mx = -INFINITY;
-        for (int s = lane; s <= p; s += 32) mx = fmaxf(mx, sc[s]);
-        mx = warp_max(mx);
-        float sum = 0.f;
-        for (int s = lane; s <= p; s += 32) {
-          const float e = expf(__fsub_rn(sc[s], mx));
-          sc[s] = e;
-          sum += e;
-        }
-        sum = warp_sum(sum);
-        for (int s = lane; s <= p; s += 32) sc[s] = __fdiv_rn(sc[s], sum);
-      }
-      consumer_sync(kConsumerThreads);
-      float a0 = 0.f, a1 = 0.f;
-      for (int s = warp; s <= p; s += kWarps) {
-        const float pr = sc[s];
-        float v0, v1;
-        if (s == p) {
-          v0 = av[2 * lane];
-          v1 = av[2 * lane + 1];
-        } else {
-          const uint32_t vv = __ldcg(reinterpret_cast<const unsigned int *>(vcache + s * kHeadDim) + lane);
-          v0 = bf_lo(vv);
-          v1 = bf_hi(vv);
-        }
-        a0 = fmaf(pr, v0, a0);
-        a1 = fmaf(pr, v1, a1);
-      }
-      pv[warp * kHeadDim + 2 * lane] = a0;
-      pv[warp * kHeadDim + 2 * lane + 1] = a1;
-      consumer_sync(kConsumerThreads);
-      if (tid < kHeadDim) {
-        float o = 0.f;
-        for (int w = 0; w < kWarps; ++w) o += pv[w * kHeadDim + tid];
-        xs[m * P.xs_elems + tid] = f2bf(o);
-      }
-      consumer_sync(kConsumerThreads);
-    }
-    const MatRange r = phase_range(4 * layer + 1);
-    float *opart = P.opart;
-    const int QH = P.QH, H = P.H;
-    return consume_rg_per_warp<MB, W8>(
-        ring, r, xs, P.xs_elems, mrows, &P.result->ctrl, P.limit_ns,
-        [&](int m, int row, float v) { opart[(static_cast<size_t>(m) * QH + head) * H + row] = v; });
-  }
-
-  __device__ bool phase_c(int layer) {
-    const LayerPtrs &lp = P.layers[layer];
-    for (int idx = tid; idx < mrows * P.H; idx += kConsumerThreads) {
-      const int m = idx / P.H, i = idx - m * P.H;
-      hx[idx] = h1_value(lp, layer, m, i);
+    } else if (!gather_to_hx([&](int m) { return ll_hout(layer - 1, m); }, P.H)) {
+      return false;
     }
     consumer_sync(kConsumerThreads);
-    norm_rows(lp.gamma_post);
+    mark(4 * layer, 1);
+    norm_rows(gamma);
+    if (!consume_splitk<MB, W8>(ring, r, xs, P.xs_elems, mrows, red, P.red_rows, &P.result->ctrl,
+                                P.limit_ns))
+      return false;
+    consumer_sync(kConsumerThreads);
+    mark(4 * layer, 2);
+    for (int idx = tid; idx < mrows * npairs; idx += kConsumerThreads) {
+      const int m = idx / npairs, lp2 = idx - m * npairs;
+      const int row = r.g0 * 8 + 2 * lp2;
+      const bool mine = lp2 == tid;
+      float y[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float v = red_sum(m, 2 * lp2 + e);
+        if (W8) v *= mine ? (e ? scale0.y : scale0.x) : lp.s_qkv[row + e];
+        y[e] = rbf(v);
+        if (P.has_bias) y[e] = __fadd_rn(y[e], mine ? (e ? bias0.y : bias0.x) : lp.bias[row + e]);
+      }
+      ll_store(ll_qkv(layer, m) + row / 2, pack_bf16x2(y[0], y[1]), epoch);
+    }
+    return true;
+  }
+
+  // Attention of every head for batch row m, reading the K/V history from
+  // ring chunks; writes the BF16 output to xs[m][0..QH*64).
+  __device__ bool attention_row(int layer, int m, float2 rope0) {
+    const int warp = tid >> 5, lane = tid & 31;
+    const int p = s_pos[m];
+    const int QH = P.QH, KVH = P.KVH, CTX = P.CTX;
+    float *aq = att;                       // [QH][64] rotated q
+    float *ak = aq + QH * kHeadDim;        // [KVH][64] rotated k
+    float *av = ak + KVH * kHeadDim;       // [KVH][64] v
+    float *prob = av + KVH * kHeadDim;     // [QH][CTX]
+    const uint32_t *row = qkv_s + static_cast<size_t>(m) * P.QKV / 2;
+    // RoPE on q and k (rotate-half, cpu_backend.py:78-93), unfused mul/add
+    const int npairs = (QH + KVH) * 32;
+    for (int idx = tid; idx < npairs + KVH * 32; idx += kConsumerThreads) {
+      if (idx < npairs) {
+        const int hh = idx >> 5, d = idx & 31;
+        const int base = hh * kHeadDim;  // q heads then k heads are contiguous in qkv
+        const __nv_bfloat16 *rb = reinterpret_cast<const __nv_bfloat16 *>(row);
+        const float x0 = bf2f(rb[base + d]), x1 = bf2f(rb[base + d + 32]);
+        const float c = m == 0 ? rope0.x : P.rope_cos[p * 32 + d];
+        const float s = m == 0 ? rope0.y : P.rope_sin[p * 32 + d];
+        const float lo = rbf(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s)));
+        const float hi = rbf(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s)));
+        float *dst = hh < QH ? aq + hh * kHeadDim : ak + (hh - QH) * kHeadDim;
+        dst[d] = lo;
+        dst[d + 32] = hi;
+      } else {
+        const int j = (idx - npairs) >> 5, d = (idx - npairs) & 31;
+        const __nv_bfloat16 *rb = reinterpret_cast<const __nv_bfloat16 *>(row);
+        const int base = (QH + KVH + j) * kHeadDim;
+        av[j * kHeadDim + d] = bf2f(rb[base + d]);
+        av[j * kHeadDim + d + 32] = bf2f(rb[base + d + 32]);
+      }
+    }
+    consumer_sync(kConsumerThreads);
+    // CTA j appends kv head j of this position to the cache (K transposed).
+    if (cta < KVH && tid < kHeadDim) {
+      const int j = cta;
+      __nv_bfloat16 *kt = kv_block(s_slot[m], layer, j, 0);
+      __nv_bfloat16 *vv = kv_block(s_slot[m], layer, j, 1);
+      kt[tid * CTX + p] = f2bf(ak[j * kHeadDim + tid]);
+      vv[p * kHeadDim + tid] = f2bf(av[j * kHeadDim + tid]);
+    }
+    // history chunks: K^T of every kv head, then V of every kv head, in
+    // consecutive ring positions
+    const RingPos first{ring.slot, ring.parity};
+    RingPos pos = first;
+    for (int c = 0; c < 2 * KVH; ++c) {
+      if (!ring_wait(ring, pos, &P.result->ctrl, P.limit_ns)) return false;
+      ring_advance(pos, 1, ring.nslots);
+    }
+    ring.slot = pos.slot;
+    ring.parity = pos.parity;
+    auto chunk_ptr = [&](int c) {
+      RingPos q = first;
+      ring_advance(q, c, ring.nslots);
+      return slot_ptr(ring, q.slot);
+    };
+    // scores + softmax: warp per head, lane per position
+    for (int h = warp; h < QH; h += kWarps) {
+      const int j = h / P.group;
+      const __nv_bfloat16 *kt = reinterpret_cast<const __nv_bfloat16 *>(chunk_ptr(j));
+      const float *q = aq + h * kHeadDim;
+      float sc[4];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int s = lane + 32 * t;
+        sc[t] = -INFINITY;
+        if (s <= p && s < CTX) {
+          float a4[4] = {0.f, 0.f, 0.f, 0.f};
+          if (s == p) {
+            const float *kk = ak + j * kHeadDim;
+#pragma unroll
+            for (int d = 0; d < kHeadDim; ++d) a4[d & 3] = fmaf(q[d], kk[d], a4[d & 3]);
+          } else {
+#pragma unroll
+            for (int d = 0; d < kHeadDim; ++d) a4[d & 3] = fmaf(q[d], bf2f(kt[d * CTX + s]), a4[d & 3]);
+          }
+          sc[t] = ((a4[0] + a4[1]) + (a4[2] + a4[3])) * 0.125f;
+          mx = fmaxf(mx, sc[t]);
+        }
+      }
+      mx = warp_max(mx);
+      float sum = 0.f;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int s = lane + 32 * t;
+        if (s <= p && s < CTX) {
+          sc[t] = expf(__fsub_rn(sc[t], mx));
+          sum += sc[t];
+        }
+      }
+      sum = warp_sum(sum);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int s = lane + 32 * t;
+        if (s <= p && s < CTX) prob[h * CTX + s] = __fdiv_rn(sc[t], sum);
+      }
+    }
+    consumer_sync(kConsumerThreads);
+    // P.V: warp per head, lane per pair of dims
+    for (int h = warp; h < QH; h += kWarps) {
+      const int j = h / P.group;
+      const uint32_t *vv = reinterpret_cast<const uint32_t *>(chunk_ptr(KVH + j));
+      const float *pr = prob + h * CTX;
+      float e0[4] = {0.f, 0.f, 0.f, 0.f}, e1[4] = {0.f, 0.f, 0.f, 0.f};
+      int s = 0;
+      for (; s + 4 <= p; s += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t w = vv[(s + u) * (kHeadDim / 2) + lane];
+          e0[u] = fmaf(pr[s + u], bf_lo(w), e0[u]);
+          e1[u] = fmaf(pr[s + u], bf_hi(w), e1[u]);
+        }
+      }
+      for (; s < p; ++s) {
+        const uint32_t w = vv[s * (kHeadDim / 2) + lane];
+        e0[0] = fmaf(pr[s], bf_lo(w), e0[0]);
+        e1[0] = fmaf(pr[s], bf_hi(w), e1[0]);
+      }
+      e0[1] = fmaf(pr[p], av[j * kHeadDim + 2 * lane], e0[1]);
+      e1[1] = fmaf(pr[p], av[j * kHeadDim + 2 * lane + 1], e1[1]);
+      const float a0 = (e0[0] + e0[1]) + (e0[2] + e0[3]);
+      const float a1 = (e1[0] + e1[1]) + (e1[2] + e1[3]);
+      reinterpret_cast<uint32_t *>(xs + static_cast<size_t>(m) * P.xs_elems)[h * 32 + lane] = pack_bf16x2(a0, a1);
+    }
+    __syncwarp();
+    consumer_sync(kConsumerThreads);
+    if (tid == 0) {
+      RingPos q = first;
+      for (int c = 0; c < 2 * KVH; ++c) {
+        mbar_arrive_count(&ring.empty[q.slot], kWarps);
+        ring_advance(q, 1, ring.nslots);
+      }
+    }
+    return true;
+  }
+
+  __device__ bool phase_attn(int layer) {
+    const LayerPtrs &lp = P.layers[layer];
+    const MatRange r = phase_range(4 * layer + 1);
+    const int npairs = (r.g1 - r.g0) * 4;
+    const float2 scale0 = load_pair(W8 ? lp.s_o : nullptr, r.g0 * 8, npairs);
+    const float2 rope0 = make_float2(P.rope_cos[s_pos[0] * 32 + (tid & 31)], P.rope_sin[s_pos[0] * 32 + (tid & 31)]);
+    for (int m = 0; m < mrows; ++m) {
+      uint32_t *dst = qkv_s + static_cast<size_t>(m) * P.QKV / 2;
+      if (!ll_gather(ll_qkv(layer, m), P.QKV / 2, epoch, &P.result->ctrl, P.limit_ns,
+                     [&](int i, uint32_t d) { dst[i] = d; }))
+        return false;
+    }
+    consumer_sync(kConsumerThreads);
+    mark(4 * layer + 1, 1);
+    for (int m = 0; m < mrows; ++m)
+      if (!attention_row(layer, m, rope0)) return false;
+    if (!consume_splitk<MB, W8>(ring, r, xs, P.xs_elems, mrows, red, P.red_rows, &P.result->ctrl,
+                                P.limit_ns))
+      return false;
+    consumer_sync(kConsumerThreads);
+    mark(4 * layer + 1, 2);
+    for (int idx = tid; idx < mrows * npairs; idx += kConsumerThreads) {
+      const int m = idx / npairs, lp2 = idx - m * npairs;
+      const int row = r.g0 * 8 + 2 * lp2;
+      const bool mine = lp2 == tid;
+      float y[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float v = red_sum(m, 2 * lp2 + e);
+        if (W8) v *= mine ? (e ? scale0.y : scale0.x) : lp.s_o[row + e];
+        y[e] = __fadd_rn(rbf(v), hx[m * P.H + row + e]);
+      }
+      ll_store(ll_h1(layer, m) + row / 2, pack_bf16x2(y[0], y[1]), epoch);
+    }
+    return true;
+  }
+
+  __device__ bool phase_mlp_in(int layer) {
+    const LayerPtrs &lp = P.layers[layer];
+    const Gamma gamma = load_gamma(lp.gamma_post);
+    if (!gather_to_hx([&](int m) { return ll_h1(layer, m); }, P.H)) return false;
+    consumer_sync(kConsumerThreads);
+    mark(4 * layer + 2, 1);
+    norm_rows(gamma);
     const MatRange r = phase_range(4 * layer + 2);
     if (!consume_splitk<MB, W8>(ring, r, xs, P.xs_elems, mrows, red, P.red_rows, &P.result->ctrl,
                                 P.limit_ns))
       return false;
     consumer_sync(kConsumerThreads);
-    const int b0 = r.g0 / 2, npairs = (r.g1 - r.g0) / 2;
-    for (int idx = tid; idx < mrows * npairs * 8; idx += kConsumerThreads) {
-      const int m = idx / (npairs * 8);
-      const int rem = idx - m * npairs * 8;
-      const int pr = rem >> 3, rr = rem & 7;
-      float g = red_sum(m, pr * 16 + rr);
-      float u = red_sum(m, pr * 16 + 8 + rr);
-      if (W8) {
-        g *= lp.s_gu[(2 * (b0 + pr)) * 8 + rr];
-        u *= lp.s_gu[(2 * (b0 + pr) + 1) * 8 + rr];
+    mark(4 * layer + 2, 2);
+    const int b0 = r.g0 / 2, nblk = (r.g1 - r.g0) / 2;
+    const int per_row = nblk * 4;  // LL words (pairs of intermediate indices)
+    for (int idx = tid; idx < mrows * per_row; idx += kConsumerThreads) {
+      const int m = idx / per_row;
+      const int rem = idx - m * per_row;
+      const int blk = rem >> 2, rr = (rem & 3) * 2;
+      float a[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float g = red_sum(m, blk * 16 + rr + e);
+        float u = red_sum(m, blk * 16 + 8 + rr + e);
+        if (W8) {
+          g *= lp.s_gu[(2 * (b0 + blk)) * 8 + rr + e];
+          u *= lp.s_gu[(2 * (b0 + blk) + 1) * 8 + rr + e];
+        }
+        g = rbf(g);
+        u = rbf(u);
+        // SwiGLU (cpu_backend.py:154-165): g / (1 + exp(-clip(g, -80, 80))) * u
+        const float ex = expf(-fminf(fmaxf(g, -80.f), 80.f));
+        a[e] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, ex)), u);
       }
-      g = rbf(g);
-      u = rbf(u);
-      // SwiGLU (cpu_backend.py:154-165): g / (1 + exp(-clip(g, -80, 80))) * u
-      const float e = expf(-fminf(fmaxf(g, -80.f), 80.f));
-      const float a = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, e)), u);
-      P.act[static_cast<size_t>(m) * P.I + (b0 + pr) * 8 + rr] = f2bf(a);
+      ll_store(ll_act(layer, m) + ((b0 + blk) * 8 + rr) / 2, pack_bf16x2(a[0], a[1]), epoch);
     }
     return true;
   }
 
-  __device__ bool phase_d(int layer) {
+  __device__ bool phase_mlp_out(int layer) {
     const LayerPtrs &lp = P.layers[layer];
-    const int n8 = P.I / 8;
-    for (int idx = tid; idx < mrows * n8; idx += kConsumerThreads) {
-      const int m = idx / n8, c = idx - m * n8;
-      const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(P.act + static_cast<size_t>(m) * P.I) + c);
-      *reinterpret_cast<uint4 *>(xs + m * P.xs_elems + c * 8) = v;
+    for (int m = 0; m < mrows; ++m) {
+      uint32_t *dst = reinterpret_cast<uint32_t *>(xs + static_cast<size_t>(m) * P.xs_elems);
+      if (!ll_gather(ll_act(layer, m), P.I / 2, epoch, &P.result->ctrl, P.limit_ns,
+                     [&](int i, uint32_t d) { dst[i] = d; }))
+        return false;
     }
     consumer_sync(kConsumerThreads);
+    mark(4 * layer + 3, 1);
     const MatRange r = phase_range(4 * layer + 3);
     if (!consume_splitk<MB, W8>(ring, r, xs, P.xs_elems, mrows, red, P.red_rows, &P.result->ctrl,
                                 P.limit_ns))
       return false;
     consumer_sync(kConsumerThreads);
-    const int nrows = (r.g1 - r.g0) * 8;
-    for (int idx = tid; idx < mrows * nrows; idx += kConsumerThreads) {
-      const int m = idx / nrows, lr = idx - m * nrows;
-      const int row = r.g0 * 8 + lr;
-      float v = red_sum(m, lr);
-      if (W8) v *= lp.s_down[row];
-      const float d = rbf(v);
-      const float h1 = h1_value(lp, layer, m, row);
-      P.hbuf[static_cast<size_t>(m) * P.H + row] = f2bf(__fadd_rn(d, h1));
+    mark(4 * layer + 3, 2);
+    const int npairs = (r.g1 - r.g0) * 4;
+    for (int idx = tid; idx < mrows * npairs; idx += kConsumerThreads) {
+      const int m = idx / npairs, lp2 = idx - m * npairs;
+      const int row = r.g0 * 8 + 2 * lp2;
+      float y[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float v = red_sum(m, 2 * lp2 + e);
+        if (W8) v *= lp.s_down[row + e];
+        y[e] = __fadd_rn(rbf(v), hx[m * P.H + row + e]);
+      }
+      ll_store(ll_hout(layer, m) + row / 2, pack_bf16x2(y[0], y[1]), epoch);
     }
     return true;
   }
 
-  __device__ bool phase_e() {
+  __device__ bool phase_head() {
     const int warp = tid >> 5, lane = tid & 31;
-    for (int idx = tid; idx < mrows * P.H; idx += kConsumerThreads) {
-      hx[idx] = bf2f(__ldcg(P.hbuf + idx));
-    }
+    const Gamma gamma = load_gamma(P.gamma_final);
+    if (!gather_to_hx([&](int m) { return ll_hout(P.L - 1, m); }, P.H)) return false;
     consumer_sync(kConsumerThreads);
-    norm_rows(P.gamma_final);
+    norm_rows(gamma);
     float bv[MB];
     int bi[MB];
 #pragma unroll
@@ -505,48 +727,53 @@ struct DecoderCta {
       s_pos[tid] = __ldcg(&st->pos[tid]);
       s_slot[tid] = __ldcg(&st->slot[tid]);
     }
-    if (tid == 0) *s_flag = __ldcg(&P.st->rows);
+    if (tid == 0) {
+      s_misc[0] = __ldcg(&P.st->rows);
+      s_misc[2] = static_cast<int>(__ldcg(P.epoch));
+    }
     consumer_sync(kConsumerThreads);
-    mrows = min(*s_flag, MB);
+    mrows = min(s_misc[0], MB);
+    epoch = static_cast<uint32_t>(s_misc[2]);
     if (P.stall_ns != 0 && tid == 0) stall_on_unset_flag(ctrl, P.stall_ns);
     consumer_sync(kConsumerThreads);
     bool ok = ld_volatile_int(&ctrl->abort) == 0;
     const int nph = 4 * P.L + 2;
-    unsigned int barriers = 0;
-    bool ran_e = false;
+    (void)nph;
+    bool ran_head = false;
     for (int k = P.phase_begin; k < P.phase_end && ok; ++k) {
-      if (P.trace && tid == 0) P.trace[static_cast<size_t>(cta) * nph + k] = globaltimer_ns();
+      mark(k, 0);
       if (k >= 4 * P.L) {
-        ok = phase_e();
-        ran_e = true;
+        ok = phase_head();
+        ran_head = true;
       } else {
         const int layer = k >> 2;
         switch (k & 3) {
-          case 0: ok = phase_a(layer); break;
-          case 1: ok = phase_b(layer); break;
-          case 2: ok = phase_c(layer); break;
-          default: ok = phase_d(layer); break;
+          case 0: ok = phase_qkv(layer); break;
+          case 1: ok = phase_attn(layer); break;
+          case 2: ok = phase_mlp_in(layer); break;
+          default: ok = phase_mlp_out(layer); break;
         }
       }
-      if (ok && k + 1 < P.phase_end) {
-        ++barriers;
-        ok = grid_barrier(ctrl, barriers * static_cast<unsigned int>(G), kConsumerThreads, P.limit_ns,
-                          s_flag);
+      consumer_sync(kConsumerThreads);
+      mark(k, 3);
+      if (P.trace && tid == 0) {
+        P.trace[(static_cast<size_t>(cta) * (4 * P.L + 2) + k) * 8 + 4] = ring.wait_ns;
+        ring.wait_ns = 0;
       }
     }
-    if (P.trace && tid == 0) P.trace[static_cast<size_t>(cta) * nph + nph - 1] = globaltimer_ns();
-    // exit protocol: the last CTA finishes the argmax and resets the counters
+    mark(nph - 1, 0);
+    // exit protocol: the last CTA finishes the argmax and advances the state
     consumer_sync(kConsumerThreads);
     if (tid == 0) {
       __threadfence();
       const unsigned int prev = atomicAdd(&ctrl->done, 1u);
-      *s_last = (prev == static_cast<unsigned int>(G) - 1u) ? 1 : 0;
+      s_misc[1] = (prev == static_cast<unsigned int>(G) - 1u) ? 1 : 0;
     }
     consumer_sync(kConsumerThreads);
-    if (*s_last) {
+    if (s_misc[1]) {
       __threadfence();
       const int warp = tid >> 5, lane = tid & 31;
-      if (ran_e && warp == 0 && ld_volatile_int(&ctrl->abort) == 0) {
+      if (ran_head && warp == 0 && ld_volatile_int(&ctrl->abort) == 0) {
         for (int m = 0; m < mrows; ++m) {
           float v = -INFINITY;
           int i = 0x7fffffff;
@@ -567,7 +794,7 @@ struct DecoderCta {
         if (st->chained && ld_volatile_int(&ctrl->abort) == 0) {
           const int p = st->pos[0];
           int next = (p + 1 < st->n_prompt) ? P.prompt[p + 1] : -1;
-          if (ran_e) {
+          if (ran_head) {
             const int tok = P.result->out_token[0];
             P.gen_out[st->n_out] = tok;
             st->n_out = st->n_out + 1;
@@ -576,7 +803,9 @@ struct DecoderCta {
           st->token[0] = next < 0 ? 0 : next;
           st->pos[0] = p + 1;
         }
-        atomicExch(&ctrl->bar, 0u);
+        unsigned int ne = *P.epoch + 1u;
+        if (ne == 0u) ne = 1u;
+        *P.epoch = ne;
         atomicExch(&ctrl->done, 0u);
         __threadfence();
       }
@@ -584,15 +813,28 @@ struct DecoderCta {
   }
 
   // ---- producer main ----------------------------------------------------------
+  // The chunk sequence of a launch: per phase, the K/V history of every row
+  // (attention phases), then the phase's weight row groups.
   __device__ void run_producer() {
-    Ctrl *ctrl = &P.result->ctrl;
-    const uint64_t policy = policy_evict_first();
-    uint32_t issued = 0;
-    for (int k = P.phase_begin; k < P.phase_end; ++k) {
-      const MatRange r = phase_range(k);
-      if (!produce_range(ring, r, issued, ctrl, P.limit_ns, policy)) break;
+    Producer prod{&ring, RingPos{0, 0}, 0, &P.result->ctrl, P.limit_ns, policy_evict_first()};
+    const StepState *st = P.st;
+    const int rows = min(__ldcg(&st->rows), MB);
+    const uint32_t kv_bytes = static_cast<uint32_t>(P.CTX) * kHeadDim * 2;
+    bool ok = true;
+    for (int k = P.phase_begin; k < P.phase_end && ok; ++k) {
+      if (P.trace) P.trace[(static_cast<size_t>(cta) * (4 * P.L + 2) + k) * 8 + 5] = globaltimer_ns();
+      if (k < 4 * P.L && (k & 3) == 1) {
+        for (int m = 0; m < rows && ok; ++m) {
+          const int slot = __ldcg(&st->slot[m]);
+          for (int c = 0; c < 2 * P.KVH && ok; ++c) {
+            const int kind = c < P.KVH ? 0 : 1, j = c < P.KVH ? c : c - P.KVH;
+            ok = prod.issue(reinterpret_cast<const uint8_t *>(kv_block(slot, k >> 2, j, kind)), kv_bytes);
+          }
+        }
+      }
+      if (ok) ok = prod.issue_range(phase_range(k));
     }
-    drain_ring(ring, issued, ctrl);
+    prod.drain();
   }
 };
 

@@ -97,21 +97,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread until the phase
+// completes or `hint_ns` passes, instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with `parity` to complete.  Returns false on
 // timeout or when another CTA raised the abort flag.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, Ctrl *ctrl,
                                           uint64_t limit_ns, int where) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = globaltimer_ns();
-  uint32_t spins = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 63u) == 0) {
-      if (ld_volatile_int(&ctrl->abort)) return false;
-      if (globaltimer_ns() - start > limit_ns) {
-        raise_error(ctrl, kErrTimeout, where);
-        return false;
-      }
+    if (mbar_try_wait_suspend(bar, parity, 20000u)) return true;
+    if (ld_volatile_int(&ctrl->abort)) return false;
+    if (globaltimer_ns() - start > limit_ns) {
+      raise_error(ctrl, kErrTimeout, where);
+      return false;
     }
   }
 }
@@ -135,6 +146,11 @@ __device__ __forceinline__ void bulk_g2s_evict_first(void *smem_dst, const void 
       " [%0], [%1], %2, [%3], %4;"
       ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
+}
+
+// Bulk prefetch of [src, src+bytes) into L2 (no completion tracking).
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ uint64_t policy_evict_first() {
@@ -212,17 +228,18 @@ __device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16
 // Round to BF16 and back: the oracle's rounding points.
 __device__ __forceinline__ float rbf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
-// 8 BF16 weights x 8 BF16 activations, FP32 accumulate.
+// 8 BF16 weights x 8 BF16 activations, FP32 accumulate (two independent
+// chains, summed at the end).
 __device__ __forceinline__ float dot8_bf16(const uint4 w, const uint4 x, float acc) {
-  acc = fmaf(bf_lo(w.x), bf_lo(x.x), acc);
-  acc = fmaf(bf_hi(w.x), bf_hi(x.x), acc);
-  acc = fmaf(bf_lo(w.y), bf_lo(x.y), acc);
-  acc = fmaf(bf_hi(w.y), bf_hi(x.y), acc);
-  acc = fmaf(bf_lo(w.z), bf_lo(x.z), acc);
-  acc = fmaf(bf_hi(w.z), bf_hi(x.z), acc);
-  acc = fmaf(bf_lo(w.w), bf_lo(x.w), acc);
-  acc = fmaf(bf_hi(w.w), bf_hi(x.w), acc);
-  return acc;
+  float a = fmaf(bf_lo(w.x), bf_lo(x.x), acc);
+  float b = bf_hi(w.x) * bf_hi(x.x);
+  a = fmaf(bf_lo(w.y), bf_lo(x.y), a);
+  b = fmaf(bf_hi(w.y), bf_hi(x.y), b);
+  a = fmaf(bf_lo(w.z), bf_lo(x.z), a);
+  b = fmaf(bf_hi(w.z), bf_hi(x.z), b);
+  a = fmaf(bf_lo(w.w), bf_lo(x.w), a);
+  b = fmaf(bf_hi(w.w), bf_hi(x.w), b);
+  return a + b;
 }
 
 // Exact int8 -> FP32 for byte k of a word: build the float 2^23 + (b + 128)
@@ -234,21 +251,19 @@ __device__ __forceinline__ float i8f(uint32_t biased_word, uint32_t selector) {
 // 4 int8 weights (one word) x 4 BF16 activations (two words).
 __device__ __forceinline__ float dot4_i8(uint32_t w, uint32_t x01, uint32_t x23, float acc) {
   const uint32_t b = w ^ 0x80808080u;
-  acc = fmaf(i8f(b, 0x7540u), bf_lo(x01), acc);
-  acc = fmaf(i8f(b, 0x7541u), bf_hi(x01), acc);
-  acc = fmaf(i8f(b, 0x7542u), bf_lo(x23), acc);
-  acc = fmaf(i8f(b, 0x7543u), bf_hi(x23), acc);
-  return acc;
+  float a0 = fmaf(i8f(b, 0x7540u), bf_lo(x01), acc);
+  float a1 = i8f(b, 0x7541u) * bf_hi(x01);
+  a0 = fmaf(i8f(b, 0x7542u), bf_lo(x23), a0);
+  a1 = fmaf(i8f(b, 0x7543u), bf_hi(x23), a1);
+  return a0 + a1;
 }
 
 // 16 int8 weights x 16 BF16 activations (x0: elements 0-7, x1: 8-15).
 __device__ __forceinline__ float dot16_i8(const uint4 w, const uint4 x0, const uint4 x1,
                                           float acc) {
-  acc = dot4_i8(w.x, x0.x, x0.y, acc);
-  acc = dot4_i8(w.y, x0.z, x0.w, acc);
-  acc = dot4_i8(w.z, x1.x, x1.y, acc);
-  acc = dot4_i8(w.w, x1.z, x1.w, acc);
-  return acc;
+  const float a = dot4_i8(w.x, x0.x, x0.y, acc) + dot4_i8(w.y, x0.z, x0.w, 0.f);
+  const float b = dot4_i8(w.z, x1.x, x1.y, 0.f) + dot4_i8(w.w, x1.z, x1.w, 0.f);
+  return a + b;
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

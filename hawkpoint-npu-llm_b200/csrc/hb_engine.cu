@@ -54,8 +54,10 @@ struct hb_engine {
   float *d_rope_cos = nullptr, *d_rope_sin = nullptr;
   __nv_bfloat16 *d_kv = nullptr;
   size_t kv_slot_elems = 0;
-  __nv_bfloat16 *d_hbuf = nullptr, *d_qkv = nullptr, *d_act = nullptr;
-  float *d_opart = nullptr, *d_logits = nullptr, *d_part_val = nullptr;
+  uint64_t *d_ll = nullptr;
+  size_t ll_words = 0;
+  unsigned int *d_epoch = nullptr;
+  float *d_logits = nullptr, *d_part_val = nullptr;
   int *d_part_idx = nullptr;
   hb::Result *d_result = nullptr;
   hb::StepState *d_st = nullptr;
@@ -123,6 +125,8 @@ int validate_desc(const hb_model_desc *d) {
   const int esize = d->weight_format == HB_WEIGHTS_W8 ? 1 : 2;
   if (d->hidden * esize > 2048)
     return fail(nullptr, HB_ERR_UNSUPPORTED, "hidden too large for one LM-head chunk");
+  if (d->kv_heads > 8 || d->context > 128)
+    return fail(nullptr, HB_ERR_UNSUPPORTED, "kv_heads <= 8 and context <= 128 required");
   if (d->max_slots <= 0 || d->max_batch <= 0 || d->max_batch > kMaxBatch)
     return fail(nullptr, HB_ERR_INVALID_ARG, "max_slots > 0 and 1 <= max_batch <= 8 required");
   if (!d->layer_offsets || !d->rope_cos || !d->rope_sin)
@@ -150,13 +154,16 @@ int validate_desc(const hb_model_desc *d) {
 
 int setup_variant(hb_engine *e, Variant &v, int mb, const void *fn, int smem_optin) {
   const hb_model_desc &d = e->desc;
-  const hb::SmemPlan base = hb::smem_plan(0, mb, e->xs_elems, d.hidden, e->red_rows, d.context);
+  const int qkv = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
+  const hb::SmemPlan base =
+      hb::smem_plan(0, mb, e->xs_elems, d.hidden, qkv, d.q_heads, d.kv_heads, e->red_rows, d.context);
   int nslots = static_cast<int>((static_cast<size_t>(smem_optin) - base.total - 16 * kMaxSlotsRing) /
                                 hb::kSlotBytes);
   if (nslots > kMaxSlotsRing) nslots = kMaxSlotsRing;
-  if (nslots < kMinSlotsRing)
+  if (nslots < kMinSlotsRing || nslots < 2 * d.kv_heads)
     return fail(e, HB_ERR_UNSUPPORTED, "model too large for the shared-memory plan (batch %d)", mb);
-  const hb::SmemPlan sp = hb::smem_plan(nslots, mb, e->xs_elems, d.hidden, e->red_rows, d.context);
+  const hb::SmemPlan sp =
+      hb::smem_plan(nslots, mb, e->xs_elems, d.hidden, qkv, d.q_heads, d.kv_heads, e->red_rows, d.context);
   HB_CUDA(e, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sp.total)));
   int blocks = 0;
   HB_CUDA(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, hb::kThreads, sp.total));
@@ -185,8 +192,6 @@ DecParams base_params(hb_engine *e, const Variant &v) {
   P.eps = d.rms_eps;
   P.kc_h = d.hidden * esize / 16;
   P.kc_i = d.intermediate * esize / 16;
-  P.kc_d = d.head_dim * esize / 16;
-  P.slab_bytes = d.hidden * d.head_dim * esize;
   P.layers = e->d_layers;
   P.gamma_final = reinterpret_cast<const float *>(e->d_blob + d.gamma_final);
   P.w_lm = e->d_blob + d.w_lm;
@@ -195,10 +200,8 @@ DecParams base_params(hb_engine *e, const Variant &v) {
   P.rope_cos = e->d_rope_cos;
   P.rope_sin = e->d_rope_sin;
   P.kv = e->d_kv;
-  P.hbuf = e->d_hbuf;
-  P.qkv = e->d_qkv;
-  P.opart = e->d_opart;
-  P.act = e->d_act;
+  P.ll = e->d_ll;
+  P.epoch = e->d_epoch;
   P.logits = e->d_logits;
   P.part_val = e->d_part_val;
   P.part_idx = e->d_part_idx;
@@ -256,6 +259,8 @@ int finish(hb_engine *e) {
   HB_CUDA(e, cudaStreamSynchronize(e->stream));
   if (e->h_result->ctrl.err != 0) {
     const int where = e->h_result->ctrl.err_where;
+    // words of the aborted launch may carry the current epoch: clear them all
+    HB_CUDA(e, cudaMemsetAsync(e->d_ll, 0, e->ll_words * 8, e->stream));
     HB_CUDA(e, cudaMemsetAsync(e->d_result, 0, sizeof(hb::Result), e->stream));
     HB_CUDA(e, cudaStreamSynchronize(e->stream));
     static const char *names[] = {"?", "weight chunk", "ring slot", "grid barrier", "test stall flag", "drain"};
@@ -326,6 +331,19 @@ int run_chained(hb_engine *e, int slot, const int32_t *ids, int n_prompt, int st
   return HB_OK;
 }
 
+// Copies positions [0, n) of every (layer, kv head) block of one slot's cache
+// into another slot: K^T rows (first n of each of the 64 dims) and V rows.
+__global__ void kv_copy_prefix_kernel(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int ctx, int n) {
+  const size_t block = static_cast<size_t>(blockIdx.x) * 2 * ctx * hb::kHeadDim;
+  const __nv_bfloat16 *ks = src + block, *vs = ks + static_cast<size_t>(ctx) * hb::kHeadDim;
+  __nv_bfloat16 *kd = dst + block, *vd = kd + static_cast<size_t>(ctx) * hb::kHeadDim;
+  for (int i = threadIdx.x; i < hb::kHeadDim * n; i += blockDim.x) {
+    const int d = i / n, s = i - d * n;
+    kd[d * ctx + s] = ks[d * ctx + s];
+    vd[s * hb::kHeadDim + d] = vs[s * hb::kHeadDim + d];
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -389,20 +407,18 @@ int hb_create(const hb_model_desc *desc, int device, hb_engine **out) {
 
   const int mb = d.max_batch > 1 ? kMaxBatch : 1;
   e->kv_slot_elems = static_cast<size_t>(d.layers) * d.kv_heads * 2 * d.context * hb::kHeadDim;
+  e->ll_words = hb::ll_layer_words(d.hidden, d.intermediate, qkv) * d.layers;
   const size_t half = static_cast<size_t>(d.head_dim / 2) * d.context;
   if ((rc = dev_alloc(e, &e->d_blob, d.blob_bytes)) || (rc = dev_alloc(e, &e->d_layers, d.layers)) ||
       (rc = dev_alloc(e, &e->d_rope_cos, half)) || (rc = dev_alloc(e, &e->d_rope_sin, half)) ||
       (rc = dev_alloc(e, &e->d_kv, e->kv_slot_elems * d.max_slots)) ||
-      (rc = dev_alloc(e, &e->d_hbuf, static_cast<size_t>(kMaxBatch) * d.hidden)) ||
-      (rc = dev_alloc(e, &e->d_qkv, static_cast<size_t>(kMaxBatch) * qkv)) ||
-      (rc = dev_alloc(e, &e->d_act, static_cast<size_t>(kMaxBatch) * d.intermediate)) ||
-      (rc = dev_alloc(e, &e->d_opart, static_cast<size_t>(kMaxBatch) * d.q_heads * d.hidden)) ||
+      (rc = dev_alloc(e, &e->d_ll, e->ll_words)) || (rc = dev_alloc(e, &e->d_epoch, 1)) ||
       (rc = dev_alloc(e, &e->d_logits, static_cast<size_t>(kMaxBatch) * d.vocab)) ||
       (rc = dev_alloc(e, &e->d_part_val, static_cast<size_t>(e->G) * kMaxBatch)) ||
       (rc = dev_alloc(e, &e->d_part_idx, static_cast<size_t>(e->G) * kMaxBatch)) ||
       (rc = dev_alloc(e, &e->d_result, 1)) || (rc = dev_alloc(e, &e->d_st, 1)) ||
       (rc = dev_alloc(e, &e->d_prompt, d.context)) || (rc = dev_alloc(e, &e->d_gen, d.context + 1)) ||
-      (rc = dev_alloc(e, &e->d_trace, static_cast<size_t>(e->G) * (4 * d.layers + 2))))
+      (rc = dev_alloc(e, &e->d_trace, static_cast<size_t>(e->G) * (4 * d.layers + 2) * 8)))
     return bail(rc);
   (void)mb;
   if (cudaHostAlloc(reinterpret_cast<void **>(&e->h_st), sizeof(hb::StepState), cudaHostAllocDefault) != cudaSuccess ||
@@ -434,6 +450,9 @@ int hb_create(const hb_model_desc *desc, int device, hb_engine **out) {
       cudaMemcpy(e->d_rope_cos, desc->rope_cos, sizeof(float) * half, cudaMemcpyHostToDevice) != cudaSuccess ||
       cudaMemcpy(e->d_rope_sin, desc->rope_sin, sizeof(float) * half, cudaMemcpyHostToDevice) != cudaSuccess)
     return bail(fail(nullptr, HB_ERR_CUDA, "descriptor upload failed"));
+  const unsigned int first_epoch = 1;
+  if (cudaMemcpy(e->d_epoch, &first_epoch, sizeof(first_epoch), cudaMemcpyHostToDevice) != cudaSuccess)
+    return bail(fail(nullptr, HB_ERR_CUDA, "epoch upload failed"));
   *out = e;
   return HB_OK;
 }
@@ -456,9 +475,9 @@ int hb_destroy(hb_engine *e) {
   if (e->stream) cudaStreamSynchronize(e->stream);
   for (auto ev : e->ev_a) cudaEventDestroy(ev);
   for (auto ev : e->ev_b) cudaEventDestroy(ev);
-  void *dev[] = {e->d_blob, e->d_layers, e->d_rope_cos, e->d_rope_sin, e->d_kv, e->d_hbuf, e->d_qkv,
-                 e->d_act, e->d_opart, e->d_logits, e->d_part_val, e->d_part_idx, e->d_result,
-                 e->d_st, e->d_prompt, e->d_gen, e->d_trace};
+  void *dev[] = {e->d_blob, e->d_layers, e->d_rope_cos, e->d_rope_sin, e->d_kv, e->d_ll, e->d_epoch,
+                 e->d_logits, e->d_part_val, e->d_part_idx, e->d_result, e->d_st, e->d_prompt,
+                 e->d_gen, e->d_trace};
   for (void *p : dev)
     if (p) cudaFree(p);
   void *host[] = {e->h_st, e->h_result, e->h_prompt, e->h_gen};
@@ -564,11 +583,11 @@ int hb_copy_prefix(hb_engine *e, int src, int dst, int n_positions) {
   if (n_positions < 0 || n_positions > d.context) return fail(e, HB_ERR_INVALID_ARG, "n_positions out of range");
   if (src == dst || n_positions == 0) return HB_OK;
   HB_CUDA(e, cudaSetDevice(e->device));
-  const size_t pitch = static_cast<size_t>(d.context) * hb::kHeadDim * 2;
-  const size_t height = static_cast<size_t>(d.layers) * d.kv_heads * 2;
-  HB_CUDA(e, cudaMemcpy2DAsync(e->d_kv + e->kv_slot_elems * dst, pitch, e->d_kv + e->kv_slot_elems * src, pitch,
-                               static_cast<size_t>(n_positions) * hb::kHeadDim * 2, height,
-                               cudaMemcpyDeviceToDevice, e->stream));
+  const int blocks = d.layers * d.kv_heads;
+  kv_copy_prefix_kernel<<<blocks, 256, 0, e->stream>>>(e->d_kv + e->kv_slot_elems * src,
+                                                        e->d_kv + e->kv_slot_elems * dst, d.context,
+                                                        n_positions);
+  HB_CUDA(e, cudaGetLastError());
   HB_CUDA(e, cudaStreamSynchronize(e->stream));
   return HB_OK;
 }
@@ -578,9 +597,17 @@ int hb_debug_dump(hb_engine *e, int what, void *out, size_t bytes) {
   HB_CUDA(e, cudaSetDevice(e->device));
   const hb_model_desc &d = e->desc;
   if (what == HB_DUMP_HIDDEN) {
+    // payloads of the last layer's output words: BF16 [kMaxBatch][hidden]
     const size_t need = static_cast<size_t>(kMaxBatch) * d.hidden * 2;
     if (bytes < need) return fail(e, HB_ERR_INVALID_ARG, "need %zu bytes", need);
-    HB_CUDA(e, cudaMemcpyAsync(out, e->d_hbuf, need, cudaMemcpyDeviceToHost, e->stream));
+    const int qkv = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
+    const size_t lw = hb::ll_layer_words(d.hidden, d.intermediate, qkv);
+    const size_t off = lw * (d.layers - 1) + static_cast<size_t>(kMaxBatch) * (qkv + d.hidden + d.intermediate) / 2;
+    std::vector<uint64_t> words(static_cast<size_t>(kMaxBatch) * d.hidden / 2);
+    HB_CUDA(e, cudaMemcpyAsync(words.data(), e->d_ll + off, words.size() * 8, cudaMemcpyDeviceToHost, e->stream));
+    HB_CUDA(e, cudaStreamSynchronize(e->stream));
+    uint32_t *o = static_cast<uint32_t *>(out);
+    for (size_t i = 0; i < words.size(); ++i) o[i] = static_cast<uint32_t>(words[i]);
   } else if (what == HB_DUMP_KV) {
     const int slot = *reinterpret_cast<int *>(out);
     if (slot < 0 || slot >= d.max_slots) return fail(e, HB_ERR_INVALID_ARG, "slot out of range");
@@ -589,7 +616,7 @@ int hb_debug_dump(hb_engine *e, int what, void *out, size_t bytes) {
     HB_CUDA(e, cudaMemcpyAsync(out, e->d_kv + e->kv_slot_elems * slot, need, cudaMemcpyDeviceToHost, e->stream));
   } else if (what == 2) {
     // phase trace: [G][4L+2] globaltimer stamps of the last traced launch
-    const size_t need = static_cast<size_t>(e->G) * (4 * d.layers + 2) * 8;
+    const size_t need = static_cast<size_t>(e->G) * (4 * d.layers + 2) * 8 * 8;
     if (bytes < need) return fail(e, HB_ERR_INVALID_ARG, "need %zu bytes", need);
     HB_CUDA(e, cudaMemcpyAsync(out, e->d_trace, need, cudaMemcpyDeviceToHost, e->stream));
   } else {

@@ -64,7 +64,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   int *s_bi = reinterpret_cast<int *>(s_bv + kWarps * kMaxBatchGemv);
   int *s_last = s_bi + kWarps * kMaxBatchGemv;
   ring.nslots = P.nslots;
-  ring.counter = 0;
+  ring.slot = 0;
+  ring.parity = 0;
+  ring.timing = false;
+  ring.wait_ns = 0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < P.nslots; ++i) {
@@ -81,9 +84,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
 
   if (tid >= kConsumerThreads) {
     if (tid == kConsumerThreads) {
-      uint32_t issued = 0;
-      produce_range(ring, r, issued, ctrl, P.limit_ns, policy_evict_first());
-      drain_ring(ring, issued, ctrl);
+      Producer prod{&ring, RingPos{0, 0}, 0, ctrl, P.limit_ns, policy_evict_first()};
+      prod.issue_range(r);
+      prod.drain();
     }
     return;
   }

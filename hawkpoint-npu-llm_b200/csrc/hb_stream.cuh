@@ -5,13 +5,17 @@
 // shared-memory slots with cp.async.bulk (completion on a per-slot "full"
 // mbarrier); the consumer warps compute on a slot and release it on its
 // "empty" mbarrier.  The producer never waits on activations, so it keeps
-// streaming weights for the next phases while the consumers wait at a grid
-// barrier: the barrier latency hides under the HBM stream.
+// streaming weights for the next phases while the consumers wait for their
+// inputs: that latency hides under the HBM stream.
 //
 // Packed projection layout (runtime/layout.py): row group g (8 rows) at
 // g * kc * 128 bytes, then chunk column j (16 bytes of each of the 8 rows) at
 // j * 128 + r * 16.  A chunk is either several whole row groups or, when one
 // row group is larger than a slot, a K-slice of kPartCols chunk columns.
+//
+// BF16 dot products run on the tensor cores (mma.m16n8k16, FP32 accumulate):
+// the weights of a row group are the B operand as stored, so nothing is
+// converted; W8 weights use FP32 CUDA-core FMAs.
 #pragma once
 
 #include "hb_device.cuh"
@@ -31,272 +35,352 @@ struct MatRange {
   int kc;               // 16-byte chunk columns per row
 };
 
-__device__ __forceinline__ int rg_per_chunk(int kc) {
-  const int rgb = kc * 128;
-  return rgb <= static_cast<int>(kSlotBytes) ? static_cast<int>(kSlotBytes) / rgb : 0;
-}
-
-__device__ __forceinline__ int parts_per_rg(int kc) { return (kc + kPartCols - 1) / kPartCols; }
-
-__device__ __forceinline__ int num_chunks(const MatRange &r) {
-  const int n = r.g1 - r.g0;
-  if (n <= 0 || r.base == nullptr) return 0;
-  const int rpc = rg_per_chunk(r.kc);
-  if (rpc > 0) return (n + rpc - 1) / rpc;
-  return n * parts_per_rg(r.kc);
-}
-
-struct ChunkInfo {
-  const uint8_t *src;
-  uint32_t bytes;
-  int rg;         // first row group
-  int nrg;        // row groups in the chunk
-  int col0;       // first chunk column
-  int ncols;      // chunk columns per row group in the chunk
-  bool last_part; // the chunk ends its row group(s)
-};
-
-__device__ __forceinline__ ChunkInfo chunk_info(const MatRange &r, int t) {
-  ChunkInfo c;
-  const int rpc = rg_per_chunk(r.kc);
-  const size_t rgb = static_cast<size_t>(r.kc) * 128;
-  if (rpc > 0) {
-    c.rg = r.g0 + t * rpc;
-    c.nrg = min(rpc, r.g1 - c.rg);
-    c.col0 = 0;
-    c.ncols = r.kc;
-    c.last_part = true;
-    c.src = r.base + static_cast<size_t>(c.rg) * rgb;
-    c.bytes = static_cast<uint32_t>(c.nrg * rgb);
-  } else {
-    const int ppr = parts_per_rg(r.kc);
-    const int q = t / ppr, p = t - q * ppr;
-    c.rg = r.g0 + q;
-    c.nrg = 1;
-    c.col0 = p * kPartCols;
-    c.ncols = min(kPartCols, r.kc - c.col0);
-    c.last_part = (p == ppr - 1);
-    c.src = r.base + static_cast<size_t>(c.rg) * rgb + static_cast<size_t>(c.col0) * 128;
-    c.bytes = static_cast<uint32_t>(c.ncols * 128);
-  }
-  return c;
-}
-
 // Balanced contiguous split of n units over parts.
 __device__ __forceinline__ int split_lo(int n, int parts, int idx) {
   return static_cast<int>((static_cast<long long>(n) * idx) / parts);
 }
 
-// Shared-memory ring state of one CTA.
+// The chunks of a range, in stream order: whole row groups packed into a
+// slot, or -- when one row group exceeds a slot -- K-slices of kPartCols
+// chunk columns.  f(rg, nrg, col0, ncols, last_part) returns false to stop.
+// Producer and consumers walk the same sequence.
+template <class F>
+__device__ __forceinline__ bool for_each_chunk(const MatRange &r, F &&f) {
+  if (r.base == nullptr || r.g1 <= r.g0) return true;
+  const int rgb = r.kc * 128;
+  if (rgb <= static_cast<int>(kSlotBytes)) {
+    const int rpc = static_cast<int>(kSlotBytes) / rgb;
+    for (int g = r.g0; g < r.g1; g += rpc)
+      if (!f(g, min(rpc, r.g1 - g), 0, r.kc, true)) return false;
+  } else {
+    for (int g = r.g0; g < r.g1; ++g)
+      for (int c0 = 0; c0 < r.kc; c0 += kPartCols)
+        if (!f(g, 1, c0, min(kPartCols, r.kc - c0), c0 + kPartCols >= r.kc)) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ int num_chunks(const MatRange &r) {
+  int n = 0;
+  for_each_chunk(r, [&](int, int, int, int, bool) {
+    ++n;
+    return true;
+  });
+  return n;
+}
+
+// Shared-memory ring of one CTA.  Slot index and phase parity advance
+// incrementally (no divisions on the per-chunk path).
 struct Ring {
   uint8_t *slots;
   uint64_t *full;
   uint64_t *empty;
   int nslots;
-  uint32_t counter;  // chunks consumed so far in this launch (per thread copy)
+  int slot;          // consumer cursor (identical in every consumer thread)
+  uint32_t parity;
+  bool timing;       // accumulate wait_ns (diagnostic traces only)
+  uint64_t wait_ns;
 };
 
-// Producer: issue every chunk of `r` in order.  Returns false on abort.
-__device__ __forceinline__ bool produce_range(Ring &ring, const MatRange &r, uint32_t &issued,
-                                              Ctrl *ctrl, uint64_t limit_ns, uint64_t policy) {
-  const int n = num_chunks(r);
-  for (int t = 0; t < n; ++t) {
-    const int slot = static_cast<int>(issued % ring.nslots);
-    const uint32_t use = issued / ring.nslots;
-    if (use > 0 && !mbar_wait(&ring.empty[slot], (use - 1) & 1u, ctrl, limit_ns, kWhereEmpty))
-      return false;
-    const ChunkInfo c = chunk_info(r, t);
-    mbar_arrive_expect_tx(&ring.full[slot], c.bytes);
-    bulk_g2s_evict_first(ring.slots + static_cast<size_t>(slot) * kSlotBytes, c.src, c.bytes,
-                         &ring.full[slot], policy);
-    ++issued;
+struct RingPos {
+  int slot;
+  uint32_t parity;
+};
+
+__device__ __forceinline__ void ring_advance(RingPos &p, int by, int nslots) {
+  p.slot += by;
+  while (p.slot >= nslots) {
+    p.slot -= nslots;
+    p.parity ^= 1u;
   }
-  return true;
 }
 
-// Producer exit: wait until every issued copy has landed, so no bulk copy
-// still targets this CTA's shared memory when it exits.
-__device__ __forceinline__ void drain_ring(Ring &ring, uint32_t issued, Ctrl *ctrl) {
-  const uint32_t first = issued > static_cast<uint32_t>(ring.nslots) ? issued - ring.nslots : 0;
-  for (uint32_t i = first; i < issued; ++i) {
-    const int slot = static_cast<int>(i % ring.nslots);
-    const uint32_t parity = (i / ring.nslots) & 1u;
-    const uint64_t start = globaltimer_ns();
-    while (!mbar_try_wait(&ring.full[slot], parity)) {
-      if (globaltimer_ns() - start > 2000000000ull) {
-        raise_error(ctrl, kErrTimeout, kWhereDrain);
-        break;
+// Producer side: issue one chunk into the next slot.
+struct Producer {
+  Ring *ring;
+  RingPos pos;
+  uint32_t issued;
+  Ctrl *ctrl;
+  uint64_t limit_ns;
+  uint64_t policy;
+
+  __device__ __forceinline__ bool issue(const uint8_t *src, uint32_t bytes) {
+    // reuse of a slot waits for the consumers to release its previous use
+    if (issued >= static_cast<uint32_t>(ring->nslots) &&
+        !mbar_wait(&ring->empty[pos.slot], pos.parity ^ 1u, ctrl, limit_ns, kWhereEmpty))
+      return false;
+    mbar_arrive_expect_tx(&ring->full[pos.slot], bytes);
+    bulk_g2s_evict_first(ring->slots + static_cast<size_t>(pos.slot) * kSlotBytes, src, bytes,
+                         &ring->full[pos.slot], policy);
+    ++issued;
+    ring_advance(pos, 1, ring->nslots);
+    return true;
+  }
+
+  __device__ __forceinline__ bool issue_range(const MatRange &r) {
+    const size_t rgb = static_cast<size_t>(r.kc) * 128;
+    return for_each_chunk(r, [&](int g, int nrg, int c0, int ncols, bool) {
+      const uint8_t *src = r.base + static_cast<size_t>(g) * rgb + static_cast<size_t>(c0) * 128;
+      return issue(src, static_cast<uint32_t>(nrg) * ncols * 128);
+    });
+  }
+
+  // Wait until every issued copy has landed, so no bulk copy still targets
+  // this CTA's shared memory when it exits.
+  __device__ __forceinline__ void drain() {
+    const int n = issued < static_cast<uint32_t>(ring->nslots) ? static_cast<int>(issued) : ring->nslots;
+    RingPos p = pos;
+    for (int i = 0; i < n; ++i) {
+      // step back one slot
+      if (p.slot == 0) {
+        p.slot = ring->nslots - 1;
+        p.parity ^= 1u;
+      } else {
+        --p.slot;
+      }
+      const uint64_t start = globaltimer_ns();
+      while (!mbar_try_wait(&ring->full[p.slot], p.parity)) {
+        if (globaltimer_ns() - start > 2000000000ull) {
+          raise_error(ctrl, kErrTimeout, kWhereDrain);
+          return;
+        }
       }
     }
   }
-}
-
-// Consumer: wait for the next chunk.
-__device__ __forceinline__ bool ring_acquire(Ring &ring, uint32_t g, Ctrl *ctrl, uint64_t limit_ns,
-                                             const uint8_t *&slot_ptr, int &slot) {
-  slot = static_cast<int>(g % ring.nslots);
-  slot_ptr = ring.slots + static_cast<size_t>(slot) * kSlotBytes;
-  return mbar_wait(&ring.full[slot], (g / ring.nslots) & 1u, ctrl, limit_ns, kWhereFull);
-}
-
-// Activation vector element loads from shared memory (BF16 [K] per batch row).
-template <bool W8>
-struct XLoad;
-
-template <>
-struct XLoad<false> {
-  // chunk column = 8 BF16 activations
-  __device__ __forceinline__ static float dot(const uint4 w, const __nv_bfloat16 *x, int col,
-                                              float acc) {
-    const uint4 xv = *reinterpret_cast<const uint4 *>(x + col * 8);
-    return dot8_bf16(w, xv, acc);
-  }
 };
 
-template <>
-struct XLoad<true> {
-  // chunk column = 16 int8 weights = 16 activations
-  __device__ __forceinline__ static float dot(const uint4 w, const __nv_bfloat16 *x, int col,
-                                              float acc) {
-    const uint4 x0 = *reinterpret_cast<const uint4 *>(x + col * 16);
-    const uint4 x1 = *reinterpret_cast<const uint4 *>(x + col * 16 + 8);
-    return dot16_i8(w, x0, x1, acc);
-  }
-};
+// Consumer: wait for the chunk at ring position p.
+__device__ __forceinline__ bool ring_wait(Ring &ring, const RingPos &p, Ctrl *ctrl, uint64_t limit_ns) {
+  if (!ring.timing) return mbar_wait(&ring.full[p.slot], p.parity, ctrl, limit_ns, kWhereFull);
+  const uint64_t t0 = globaltimer_ns();
+  const bool ok = mbar_wait(&ring.full[p.slot], p.parity, ctrl, limit_ns, kWhereFull);
+  ring.wait_ns += globaltimer_ns() - t0;
+  return ok;
+}
 
-// Split-K consumption of a row-group range by all consumer warps.  Every
-// warp sees every chunk; column group cg = warp*4 + lane/8 takes chunk columns
-// cg, cg+32, ... (chunk-column offsets of K-slices are multiples of 32, so a
-// lane keeps the same columns across the slices of one row group).  The
+__device__ __forceinline__ const uint8_t *slot_ptr(const Ring &ring, int slot) {
+  return ring.slots + static_cast<size_t>(slot) * kSlotBytes;
+}
+
+// ---- tensor-core dot products (BF16) -------------------------------------------
+// One row group (8 weight rows) is the B operand of mma.m16n8k16 (n = the 8
+// rows, k = 16 columns); the activations are the A operand with batch row m
+// in row m (rows >= MB are zero).  D[m][n] accumulates in FP32.  The packed
+// weight layout is exactly ldmatrix's 8x8 tiles: chunk column j of the group
+// holds 8 rows x 16 bytes at j * 128.
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+// Accumulate the dot products of one row group over chunk columns
+// [jc_begin, jc_end) stepping by `stride` (multiples of 4): 4 chunk columns
+// = 2 k16 steps per iteration.  `sg` = the group's bytes in shared memory,
+// `xrow` = this lane's activation row (lane/4) or nullptr for zero rows,
+// `col0` = chunk-column offset of sg within the full K.
+__device__ __forceinline__ void mma_group(float (&d)[4], const uint8_t *sg, const __nv_bfloat16 *xrow,
+                                          int col0, int jc_begin, int jc_end, int stride) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t base = smem_u32(sg) + ((lane >> 3) * 128) + ((lane & 7) * 16);
+  const int t2 = (lane & 3) * 2;
+  for (int jc = jc_begin; jc < jc_end; jc += stride) {
+    uint32_t b[4];
+    ldsm_x4(b, base + jc * 128);
+    uint32_t a0 = 0, a2 = 0, c0 = 0, c2 = 0;
+    if (xrow != nullptr) {
+      const __nv_bfloat16 *x = xrow + (col0 + jc) * 8 + t2;
+      a0 = *reinterpret_cast<const uint32_t *>(x);
+      a2 = *reinterpret_cast<const uint32_t *>(x + 8);
+      c0 = *reinterpret_cast<const uint32_t *>(x + 16);
+      c2 = *reinterpret_cast<const uint32_t *>(x + 24);
+    }
+    mma_16816(d, a0, a2, b[0], b[1]);
+    mma_16816(d, c0, c2, b[2], b[3]);
+  }
+}
+
+// CUDA-core dot products for W8 (int8 weights, chunk column = 16 weights).
+__device__ __forceinline__ float dot_w8_cols(const uint8_t *sg, const __nv_bfloat16 *x, int col0, int j0,
+                                             int jend, int stride) {
+  const int rr = threadIdx.x & 7;
+  float acc = 0.f;
+  for (int j = j0; j < jend; j += stride) {
+    const uint4 w = *reinterpret_cast<const uint4 *>(sg + j * 128 + rr * 16);
+    const uint4 x0 = *reinterpret_cast<const uint4 *>(x + (col0 + j) * 16);
+    const uint4 x1 = *reinterpret_cast<const uint4 *>(x + (col0 + j) * 16 + 8);
+    acc = dot16_i8(w, x0, x1, acc);
+  }
+  return acc;
+}
+
+// Split-K consumption of a row-group range by all consumer warps (latency
+// mode): every warp sees every chunk and takes 1/8 of its columns.  The
 // per-warp partial of (batch row m, local row) goes to
 // red[(warp * MB + m) * red_rows + local_row]; the caller sums the warps
 // after a consumer_sync.  xs: BF16 activations [MB][K] in shared memory.
 template <int MB, bool W8>
-__device__ __forceinline__ bool consume_splitk(Ring &ring, const MatRange &r,
-                                               const __nv_bfloat16 *xs, int K, int mrows,
-                                               float *red, int red_rows, Ctrl *ctrl,
+__device__ __forceinline__ bool consume_splitk(Ring &ring, const MatRange &r, const __nv_bfloat16 *xs, int K,
+                                               int mrows, float *red, int red_rows, Ctrl *ctrl,
                                                uint64_t limit_ns) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rr = lane & 7;
-  const int cg = warp * 4 + (lane >> 3);
-  const int n = num_chunks(r);
-  float acc[MB];
+  float d[4] = {0.f, 0.f, 0.f, 0.f};   // BF16 path: D fragment of the current group
+  float acc[MB];                        // W8 path
 #pragma unroll
   for (int m = 0; m < MB; ++m) acc[m] = 0.f;
-  for (int t = 0; t < n; ++t) {
-    const uint8_t *s;
-    int slot;
-    if (!ring_acquire(ring, ring.counter++, ctrl, limit_ns, s, slot)) return false;
-    const ChunkInfo c = chunk_info(r, t);
-    for (int q = 0; q < c.nrg; ++q) {
-      const uint8_t *sg = s + static_cast<size_t>(q) * c.ncols * 128 + rr * 16;
-      for (int j = cg; j < c.ncols; j += kColGroups) {
-        const uint4 w = *reinterpret_cast<const uint4 *>(sg + j * 128);
-        const int col = c.col0 + j;
+  RingPos pos{ring.slot, ring.parity};
+  const bool ok = for_each_chunk(r, [&](int g, int nrg, int col0, int ncols, bool last) {
+    if (!ring_wait(ring, pos, ctrl, limit_ns)) return false;
+    const uint8_t *s = slot_ptr(ring, pos.slot);
+    for (int q = 0; q < nrg; ++q) {
+      const uint8_t *sg = s + static_cast<size_t>(q) * ncols * 128;
+      if (!W8) {
+        const int m = lane >> 2;
+        const __nv_bfloat16 *xrow = m < mrows ? xs + static_cast<size_t>(m) * K : nullptr;
+        mma_group(d, sg, xrow, col0, warp * 4, ncols, kWarps * 4);
+      } else {
+        const int cg = warp * 4 + (lane >> 3);
 #pragma unroll
         for (int m = 0; m < MB; ++m)
-          if (m < mrows) acc[m] = XLoad<W8>::dot(w, xs + static_cast<size_t>(m) * K, col, acc[m]);
+          if (m < mrows) acc[m] += dot_w8_cols(sg, xs + static_cast<size_t>(m) * K, col0, cg, ncols, kColGroups);
       }
-      if (c.last_part) {
-        const int local = (c.rg + q - r.g0) * 8 + rr;
+      if (last) {
+        const int local = (g + q - r.g0) * 8;
+        if (!W8) {
+          const int m = lane >> 2, n = (lane & 3) * 2;
+          if (m < mrows) {
+            red[(warp * MB + m) * red_rows + local + n] = d[0];
+            red[(warp * MB + m) * red_rows + local + n + 1] = d[1];
+          }
+          d[0] = d[1] = d[2] = d[3] = 0.f;
+        } else {
 #pragma unroll
-        for (int m = 0; m < MB; ++m) {
-          float v = acc[m];
-          v += __shfl_xor_sync(0xffffffffu, v, 8);
-          v += __shfl_xor_sync(0xffffffffu, v, 16);
-          if (lane < 8 && m < mrows) red[(warp * MB + m) * red_rows + local] = v;
-          acc[m] = 0.f;
+          for (int m = 0; m < MB; ++m) {
+            float v = acc[m];
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            if (lane < 8 && m < mrows) red[(warp * MB + m) * red_rows + local + lane] = v;
+            acc[m] = 0.f;
+          }
         }
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive_count(&ring.empty[slot], 1);
-  }
-  return true;
+    if (lane == 0) mbar_arrive_count(&ring.empty[pos.slot], 1);
+    ring_advance(pos, 1, ring.nslots);
+    return true;
+  });
+  ring.slot = pos.slot;
+  ring.parity = pos.parity;
+  return ok;
 }
 
-// Row-group-per-warp consumption (small K): every warp waits for every chunk,
-// warp w takes row groups w, w+8, ... of it; lane/8 strides the columns.
-// on_row(m, row, value) runs on lanes 0..7 with the full dot product.
+// Row-group-per-warp consumption (small K, several groups per chunk).
+// on_row(m, row, value) receives every dot product.
 template <int MB, bool W8, class F>
-__device__ __forceinline__ bool consume_rg_per_warp(Ring &ring, const MatRange &r,
-                                                    const __nv_bfloat16 *xs, int K, int mrows,
-                                                    Ctrl *ctrl, uint64_t limit_ns, F &&on_row) {
+__device__ __forceinline__ bool consume_rg_per_warp(Ring &ring, const MatRange &r, const __nv_bfloat16 *xs,
+                                                    int K, int mrows, Ctrl *ctrl, uint64_t limit_ns,
+                                                    F &&on_row) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rr = lane & 7, cq = lane >> 3;
-  const int n = num_chunks(r);
-  for (int t = 0; t < n; ++t) {
-    const uint8_t *s;
-    int slot;
-    if (!ring_acquire(ring, ring.counter++, ctrl, limit_ns, s, slot)) return false;
-    const ChunkInfo c = chunk_info(r, t);
-    for (int q = warp; q < c.nrg; q += kWarps) {
-      const uint8_t *sg = s + static_cast<size_t>(q) * c.ncols * 128 + rr * 16;
-      float acc[MB];
+  RingPos pos{ring.slot, ring.parity};
+  const bool ok = for_each_chunk(r, [&](int g, int nrg, int col0, int ncols, bool) {
+    if (!ring_wait(ring, pos, ctrl, limit_ns)) return false;
+    const uint8_t *s = slot_ptr(ring, pos.slot);
+    for (int q = warp; q < nrg; q += kWarps) {
+      const uint8_t *sg = s + static_cast<size_t>(q) * ncols * 128;
+      if (!W8) {
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        const int m = lane >> 2;
+        mma_group(d, sg, m < mrows ? xs + static_cast<size_t>(m) * K : nullptr, col0, 0, ncols, 4);
 #pragma unroll
-      for (int m = 0; m < MB; ++m) acc[m] = 0.f;
-      for (int j = cq; j < c.ncols; j += 4) {
-        const uint4 w = *reinterpret_cast<const uint4 *>(sg + j * 128);
+        for (int mm = 0; mm < MB; ++mm) {
+          if (mm == m && m < mrows) {  // compile-time batch index for the callback
+            on_row(mm, (g + q) * 8 + (lane & 3) * 2, d[0]);
+            on_row(mm, (g + q) * 8 + (lane & 3) * 2 + 1, d[1]);
+          }
+        }
+      } else {
 #pragma unroll
-        for (int m = 0; m < MB; ++m)
-          if (m < mrows) acc[m] = XLoad<W8>::dot(w, xs + static_cast<size_t>(m) * K, c.col0 + j, acc[m]);
-      }
-      const int row = (c.rg + q) * 8 + rr;
-#pragma unroll
-      for (int m = 0; m < MB; ++m) {
-        float v = acc[m];
-        v += __shfl_xor_sync(0xffffffffu, v, 8);
-        v += __shfl_xor_sync(0xffffffffu, v, 16);
-        if (lane < 8 && m < mrows) on_row(m, row, v);
+        for (int m = 0; m < MB; ++m) {
+          if (m < mrows) {
+            float v = dot_w8_cols(sg, xs + static_cast<size_t>(m) * K, col0, lane >> 3, ncols, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            if (lane < 8) on_row(m, (g + q) * 8 + lane, v);
+          }
+        }
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive_count(&ring.empty[slot], 1);
-  }
-  return true;
+    if (lane == 0) mbar_arrive_count(&ring.empty[pos.slot], 1);
+    ring_advance(pos, 1, ring.nslots);
+    return true;
+  });
+  ring.slot = pos.slot;
+  ring.parity = pos.parity;
+  return ok;
 }
 
 // Chunk-per-warp consumption (throughput mode, whole row groups per chunk):
-// chunk t goes to warp t % 8, which releases it alone (arrival count 8).
+// chunk t is computed by warp t % 8.  Every warp still waits for and
+// releases every chunk in order (empty-barrier count 8), so no warp ever
+// waits more than one phase ahead on a slot.
 template <int MB, bool W8, class F>
-__device__ __forceinline__ bool consume_chunk_per_warp(Ring &ring, const MatRange &r,
-                                                       const __nv_bfloat16 *xs, int K, int mrows,
-                                                       Ctrl *ctrl, uint64_t limit_ns, F &&on_row) {
+__device__ __forceinline__ bool consume_chunk_per_warp(Ring &ring, const MatRange &r, const __nv_bfloat16 *xs,
+                                                       int K, int mrows, Ctrl *ctrl, uint64_t limit_ns,
+                                                       F &&on_row) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rr = lane & 7, cq = lane >> 3;
-  const int n = num_chunks(r);
-  const uint32_t base = ring.counter;
-  ring.counter += n;
-  for (int t = warp; t < n; t += kWarps) {
-    const uint8_t *s;
-    int slot;
-    if (!ring_acquire(ring, base + t, ctrl, limit_ns, s, slot)) return false;
-    const ChunkInfo c = chunk_info(r, t);
-    for (int q = 0; q < c.nrg; ++q) {
-      const uint8_t *sg = s + static_cast<size_t>(q) * c.ncols * 128 + rr * 16;
-      float acc[MB];
+  RingPos pos{ring.slot, ring.parity};
+  int owner = 0;
+  const bool ok = for_each_chunk(r, [&](int g, int nrg, int col0, int ncols, bool) {
+    if (!ring_wait(ring, pos, ctrl, limit_ns)) return false;
+    if (owner == warp) {
+      const uint8_t *s = slot_ptr(ring, pos.slot);
+      for (int q = 0; q < nrg; ++q) {
+        const uint8_t *sg = s + static_cast<size_t>(q) * ncols * 128;
+        if (!W8) {
+          float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+          const int m = lane >> 2;
+          const __nv_bfloat16 *xrow = m < mrows ? xs + static_cast<size_t>(m) * K : nullptr;
+          mma_group(d0, sg, xrow, col0, 0, ncols, 8);
+          mma_group(d1, sg, xrow, col0, 4, ncols, 8);
 #pragma unroll
-      for (int m = 0; m < MB; ++m) acc[m] = 0.f;
-#pragma unroll 4
-      for (int j = cq; j < c.ncols; j += 4) {
-        const uint4 w = *reinterpret_cast<const uint4 *>(sg + j * 128);
+          for (int mm = 0; mm < MB; ++mm) {
+            if (mm == m && m < mrows) {  // compile-time batch index for the callback
+              on_row(mm, (g + q) * 8 + (lane & 3) * 2, d0[0] + d1[0]);
+              on_row(mm, (g + q) * 8 + (lane & 3) * 2 + 1, d0[1] + d1[1]);
+            }
+          }
+        } else {
 #pragma unroll
-        for (int m = 0; m < MB; ++m)
-          if (m < mrows) acc[m] = XLoad<W8>::dot(w, xs + static_cast<size_t>(m) * K, c.col0 + j, acc[m]);
-      }
-      const int row = (c.rg + q) * 8 + rr;
-#pragma unroll
-      for (int m = 0; m < MB; ++m) {
-        float v = acc[m];
-        v += __shfl_xor_sync(0xffffffffu, v, 8);
-        v += __shfl_xor_sync(0xffffffffu, v, 16);
-        if (lane < 8 && m < mrows) on_row(m, row, v);
+          for (int m = 0; m < MB; ++m) {
+            if (m < mrows) {
+              float v = dot_w8_cols(sg, xs + static_cast<size_t>(m) * K, col0, lane >> 3, ncols, 4);
+              v += __shfl_xor_sync(0xffffffffu, v, 8);
+              v += __shfl_xor_sync(0xffffffffu, v, 16);
+              if (lane < 8) on_row(m, (g + q) * 8 + lane, v);
+            }
+          }
+        }
       }
     }
+    owner = owner + 1 == kWarps ? 0 : owner + 1;
     __syncwarp();
-    if (lane == 0) mbar_arrive_count(&ring.empty[slot], kWarps);
-  }
-  return true;
+    if (lane == 0) mbar_arrive_count(&ring.empty[pos.slot], 1);
+    ring_advance(pos, 1, ring.nslots);
+    return true;
+  });
+  ring.slot = pos.slot;
+  ring.parity = pos.parity;
+  return ok;
 }
 
 }  // namespace hb

@@ -186,17 +186,25 @@ class B200DecoderEngine:
         return out
 
     def kv_cache(self, slot=0):
-        """BF16 bits of one slot's cache: [layers, kv_heads, 2, context, 64]."""
+        """BF16 bits of one slot's cache as [layers, kv_heads, 2 (K, V), context, 64].
+
+        The device keeps K transposed ([64, context] per head); this view
+        undoes that so it compares directly with the reference's caches."""
         s = self.shape
-        out = np.zeros((s.layers, s.kv_heads, 2, self.context, s.head_dim), np.uint16)
-        out.view(np.int32).reshape(-1)[0] = slot
-        self._check(self._lib.hb_debug_dump(self._live(), hb_lib.HB_DUMP_KV, out.ctypes.data, out.nbytes))
-        return out
+        raw = np.zeros((s.layers, s.kv_heads, 2, self.context * s.head_dim), np.uint16)
+        raw.view(np.int32).reshape(-1)[0] = slot
+        self._check(self._lib.hb_debug_dump(self._live(), hb_lib.HB_DUMP_KV, raw.ctypes.data, raw.nbytes))
+        keys = raw[:, :, 0].reshape(s.layers, s.kv_heads, s.head_dim, self.context).transpose(0, 1, 3, 2)
+        values = raw[:, :, 1].reshape(s.layers, s.kv_heads, self.context, s.head_dim)
+        return np.ascontiguousarray(np.stack([keys, values], axis=2))
 
     def phase_trace(self):
-        """globaltimer stamps [G, 4L+2] of the last launch traced with profile(trace=True)."""
+        """globaltimer stamps [G, 4L+2, 8] of the last launch traced with
+        profile(trace=True): per phase its start, inputs ready, weights
+        consumed, outputs stored, ring wait total (ns), producer's first
+        issue of the phase."""
         g = self._lib.hb_device_sm_count(0)
-        out = np.zeros((g, 4 * self.layers + 2), np.uint64)
+        out = np.zeros((g, 4 * self.layers + 2, 8), np.uint64)
         self._check(self._lib.hb_debug_dump(self._live(), hb_lib.HB_DUMP_TRACE, out.ctypes.data, out.nbytes))
         return out
 

@@ -14,9 +14,6 @@ their share of each projection through a shared-memory ring with bulk copies:
   contiguous too, and a warp reading one chunk column touches 128 contiguous
   bytes (bank-conflict free).  The same bytes are the no-swizzle K-major
   8x16-byte "core matrix" arrangement the tensor-core descriptors use.
-* **o_proj split by head.**  ``o_proj`` [hidden, q_heads*head_dim] is stored as
-  q_heads slabs of [hidden, head_dim], so the CTAs that compute one head's
-  attention also apply that head's slice of o_proj.
 * **gate_up paired.**  Packed row group 2b holds gate rows 8b..8b+7 and packed
   group 2b+1 the matching up rows, so a CTA always owns both halves of the
   SwiGLU it computes.
@@ -162,15 +159,15 @@ def check_dims(shape, fmt="bf16"):
         problems.append("q_heads must be a multiple of kv_heads")
     for name, rows, k in (
         ("qkv", shape.qkv_rows, shape.hidden),
-        ("o_proj", shape.hidden, shape.head_dim),
+        ("o_proj", shape.hidden, shape.q_heads * shape.head_dim),
         ("gate_up", 2 * shape.intermediate, shape.hidden),
         ("down_proj", shape.hidden, shape.intermediate),
         ("lm_head", shape.vocab, shape.hidden),
     ):
         if rows % ROW_GROUP:
             problems.append(f"{name} rows must be a multiple of 8")
-        if (k * e) % CHUNK or k % 16:
-            problems.append(f"{name} K must be a multiple of 16")
+        if (k * e) % CHUNK or k % 32:
+            problems.append(f"{name} K must be a multiple of 32")
     if shape.intermediate % ROW_GROUP:
         problems.append("intermediate must be a multiple of 8")
     if problems:
@@ -213,8 +210,7 @@ def pack(model, fmt="bf16"):
         if s is not None:
             put(off["s_qkv"], s)
         w, s = _weights_of(model, f"{p}.o_proj", fmt)
-        slabs = [pack_matrix_bytes(w[:, hd * d: (hd + 1) * d]) for hd in range(shape.q_heads)]
-        put(off["w_o"], np.concatenate(slabs))
+        put(off["w_o"], pack_matrix_bytes(w))
         if s is not None:
             put(off["s_o"], s)
         w, s = _weights_of(model, f"{p}.gate_up", fmt)
@@ -262,9 +258,7 @@ def unpack(blob, lay):
         out[f"{p}.post_attn_norm"] = raw(off["gamma_post"], 4 * h).view(np.float32).copy()
         out[f"{p}.qkv_bias"] = raw(off["qkv_bias"], 4 * shape.qkv_rows).view(np.float32).copy()
         out[f"{p}.qkv"] = matrix(off["w_qkv"], shape.qkv_rows, h)
-        slab_bytes = h * d * e
-        slabs = [matrix(off["w_o"] + hd * slab_bytes, h, d) for hd in range(shape.q_heads)]
-        out[f"{p}.o_proj"] = np.concatenate(slabs, axis=1)
+        out[f"{p}.o_proj"] = matrix(off["w_o"], h, shape.q_heads * d)
         packed = matrix(off["w_gate_up"], 2 * i, h)
         order = gate_up_order(i)
         restored = np.empty_like(packed)

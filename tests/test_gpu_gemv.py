@@ -3,9 +3,11 @@ reference of the same op: ``bf16(W_f32 @ x_f32)`` (the BF16 projection of
 npu_llm/runtime/cpu_backend.py:64-69) and the W8 form
 ``bf16((q_f32 @ x_f32) * scale)`` (npu_llm/kernels/decoder_layer_bf16.cc:64-80).
 
-Tolerance: the FP32 sum is order-dependent, so the BF16 output may differ
-from the reference's rounding by one BF16 unit in the last place; FP32 outputs
-must agree to 1e-5 of sum(|w x|).  The fused argmax must equal the first
+Tolerance: the FP32 sum is order-dependent (the BF16 kernels accumulate on
+the tensor cores), so the BF16 output may differ from the reference's
+rounding by one BF16 unit in the last place (plus 1e-5 of sum(|w x|) where
+the sum cancels to nearly zero); FP32 outputs must agree to 1e-5 of
+sum(|w x|).  The fused argmax must equal the first
 maximum of the kernel's own FP32 outputs, and the reference argmax whenever
 the reference top-2 margin exceeds 1e-3.
 """
@@ -99,8 +101,15 @@ def test_gemv_matches_torch_fp32(rows, k, batch, fmt):
 
     out_bf16, _ = run_gemv(packed, scales, fmt, rows, k, x, hb_lib.HB_GEMV_OUT_BF16)
     ref_bf16 = ref.astype(bfloat16).astype(np.float32)
+    # one BF16 unit of the larger of the two (the FP32 sums may straddle a
+    # rounding midpoint or a power of two in different summation orders),
+    # plus the FP32 accumulation error bound for results that cancel to ~0
     diff = np.abs(out_bf16 - ref_bf16)
-    assert np.all(diff <= bf16_ulp(ref) * 1.01 + 1e-30), f"max bf16 diff {diff.max()}"
+    ulp = bf16_ulp(np.maximum(np.abs(out_bf16), np.abs(ref_bf16)))
+    bad = diff > ulp * 1.01 + 1e-5 * mag + 1e-30
+    assert not bad.any(), (
+        f"{bad.sum()} BF16 outputs off by more than one unit; first at "
+        f"{np.argwhere(bad)[0]}: got {out_bf16[bad][0]}, ref {ref[bad][0]}")
     assert np.mean(diff > 0) < 0.01
 
     out_f32, am = run_gemv(packed, scales, fmt, rows, k, x,
