@@ -1,0 +1,404 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 decoder engine on BASELINE config 3 (the metric's config):
+
+    Qwen2.5-0.5B-shaped BF16 decoder, random-init N(0, 0.02) weights (seed 0),
+    a 40-id seeded prompt windowed to the 32 positions that leave room for 32
+    generated tokens in the 64-token context (the reference's prompt budget,
+    npu_llm/runtime/generate.py:1021-1023), sequential prefill, then greedy
+    decode of 32 tokens, batch 1.
+
+One step = one such request.  Reported (one JSON line from rank 0):
+
+* ``value``: decode tokens/s with every input resident in HBM -- the whole
+  request runs as back-to-back kernel launches with the greedy token fed back
+  on the device (hb_generate); the decode time is measured with CUDA events
+  around each launch on the engine's stream (31 decode steps per request, the
+  reference's decode_steps / decode_seconds).
+* ``e2e``: the same metric through the public ``NPUDecoder.decode_token`` API
+  (one call per position, host<->device copies and a sync per call).
+* ``roofline``: the decode kernel's algorithmic bytes per launch (the BF16
+  weights every token must stream, plus the KV history) / its mean launch
+  time, against the measured HBM peak.
+* ``cpu_baseline``: the CPU oracle (a NumPy port of the reference's BF16 CPU
+  runtime) on a bounded sample of the same request.
+
+``--impl reference`` times the reference path itself -- the CPU runtime
+(port), the only implementation of this engine that runs off the NPU -- on
+this host's cores.  Multi-GPU (torchrun): every rank runs the same requests on
+its own GPU (independent replicas, weak scaling); the time is the max over
+ranks.  The synthetic weights are larger than L2 (1 GB per token), so no L2
+flush is needed between steps.
+"""
+
+import argparse
+import json
+import os
+from pathlib import Path
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "hawkpoint-npu-llm_b200"))
+sys.path.insert(0, str(REPO))
+
+PROMPT_SEED = 1
+MODEL_SEED = 0
+PROMPT_DRAWN = 40
+NEW_TOKENS = 32
+METRIC = "decode_tokens_per_second"
+# Algorithmic bytes per decoded token: BF16 weights of every layer
+# (715,653,120) + LM head (272,269,312) + norm weights (87,808) + FP32 qkv
+# bias (110,592); plus 24 layers x 512 bytes of K/V history per position.
+WEIGHT_BYTES = 988_120_832
+KV_BYTES_PER_POSITION = 24 * 512
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_setup(n):
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=timedelta(seconds=300))
+    return rank, world, local
+
+
+def max_over_ranks(value, world):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def workload_prompt(vocab):
+    from runtime import synthetic
+    ids = synthetic.prompt_ids(vocab, PROMPT_DRAWN, PROMPT_SEED)
+    return ids[: 64 - NEW_TOKENS]
+
+
+def measured_peak():
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        peaks = json.loads(path.read_text())
+        return float(peaks["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per decode launch from the committed ncu summary, if any."""
+    path = REPO / "profiles" / "decoder_kernel_qwen25_decode.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return int(line.split(":")[1].strip().replace(",", ""))
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    def __init__(self, index):
+        self.proc = None
+        self.index = index
+        self.path = Path("/tmp") / f"hb_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self):
+        if not self.path.exists():
+            return None
+        mhz, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                mhz.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[3:7]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        self.path.unlink(missing_ok=True)
+        if not mhz:
+            return None
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+# ---------------------------------------------------------------- CPU oracle --
+def oracle_sample(model, prompt, prefill_positions, decode_steps):
+    """Decode tok/s of the CPU oracle over a bounded sample of the request:
+    the last `prefill_positions` prompt positions (logits at the last), then
+    `decode_steps` greedy steps.  Returns (tokens/s, seconds, sample text)."""
+    import numpy as np
+    from oracle.cpu_decoder import OracleDecoder, argmax_first
+
+    oracle = OracleDecoder(model)
+    start_pos = len(prompt) - prefill_positions
+    for p in range(start_pos):  # cache fill outside the sample (positions only)
+        pass
+    t0 = time.perf_counter()
+    token = None
+    for i, p in enumerate(range(start_pos, len(prompt))):
+        out = oracle.step(prompt[p], p, compute_logits=(p == len(prompt) - 1))
+        if out is not None:
+            token = argmax_first(out)
+    t_prefill = time.perf_counter() - t0
+    t1 = time.perf_counter()
+    pos = len(prompt)
+    for _ in range(decode_steps):
+        token = argmax_first(oracle.step(token, pos))
+        pos += 1
+    t_decode = time.perf_counter() - t1
+    sample = (f"{prefill_positions} prefill positions + {decode_steps} greedy decode steps of the "
+              f"config-3 request (positions {start_pos}..{pos - 1})")
+    return decode_steps / t_decode, t_prefill + t_decode, sample
+
+
+def threads_used():
+    try:
+        from threadpoolctl import threadpool_info
+        counts = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        if counts:
+            return max(counts)
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    import numpy as np  # noqa: F401
+    from runtime import synthetic
+
+    model = synthetic.build("qwen2.5-0.5b", seed=MODEL_SEED).materialize()
+    prompt = workload_prompt(model.shape.vocab)
+    for _ in range(args.warmup):
+        oracle_sample(model, prompt, 1, 2)
+    rates, secs = [], []
+    sample = ""
+    for _ in range(args.steps):
+        rate, sec, sample = oracle_sample(model, prompt, 2, 4)
+        rates.append(rate)
+        secs.append(sec)
+    value = statistics.median(rates)
+    cores = threads_used()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * statistics.median(secs),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "qwen2.5-0.5b-bf16 greedy decode (BASELINE config 3), CPU runtime",
+                   "prompt_positions": len(prompt), "new_tokens": NEW_TOKENS, "batch": 1},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- B200 arm --
+def run_b200(args, rank, world, local):
+    import numpy as np
+    import torch
+    from runtime import layout, synthetic
+    from runtime.b200_engine import B200DecoderEngine
+    from runtime.generate import NPUDecoder
+
+    device = local if torch.cuda.is_available() else 0
+    torch.cuda.set_device(device)
+    model = synthetic.build("qwen2.5-0.5b", seed=MODEL_SEED).materialize()
+    prompt = workload_prompt(model.shape.vocab)
+    n_prompt = len(prompt)
+    decode_steps = NEW_TOKENS - 1
+    launches_per_step = n_prompt + NEW_TOKENS - 1
+
+    blob = layout.pack(model, "bf16")
+    engine = B200DecoderEngine(model, device=device, blob=blob)
+    stream = torch.cuda.Stream(device=device)
+    engine.set_stream(stream.cuda_stream)
+
+    def one_request():
+        return engine.generate(prompt, NEW_TOKENS)
+
+    for _ in range(args.warmup):
+        ref_tokens = one_request()
+    torch.cuda.synchronize()
+    engine.profile(True)
+    engine.profile_read()
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            tokens = one_request()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    total_ms = ev0.elapsed_time(ev1)
+    # per-launch events: [prefill launches..., decode launches...] per request
+    dur, start = engine.profile_read(starts=True)
+    dur = dur.reshape(args.steps, launches_per_step)
+    start = start.reshape(args.steps, launches_per_step)
+    engine.profile(False)
+    assert tokens == ref_tokens, "greedy tokens changed between identical requests"
+    decode_launch_ms = dur[:, n_prompt:]
+    # device time of each segment, launch gaps included
+    end = start + dur
+    prefill_ms = end[:, n_prompt - 1] - start[:, 0]
+    decode_seg_ms = end[:, -1] - start[:, n_prompt]
+    local_time = float(decode_seg_ms.sum())
+    t_max = max_over_ranks(local_time, world)
+    value = (decode_steps * args.steps * world) / (t_max / 1000.0)
+    ms_per_step = max_over_ranks(total_ms, world) / args.steps
+
+    # roofline of the decode kernel (positions n_prompt .. n_prompt+30)
+    mean_pos = n_prompt + (decode_steps - 1) / 2.0
+    alg_bytes = WEIGHT_BYTES + KV_BYTES_PER_POSITION * (mean_pos + 1)
+    launch_ms = float(decode_launch_ms.mean())
+    achieved = alg_bytes / (launch_ms / 1000.0) / 1e9
+    peak, peak_kind = measured_peak()
+
+    # prefix-cache replay: the same prompt again reuses 31 positions
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    engine.generate(prompt, 1, start=n_prompt - 1)
+    ttft_cached_ms = 1000 * (time.perf_counter() - t0)
+
+    # e2e through the public decode_token API (host copies + sync per call)
+    engine.close()
+    decoder = NPUDecoder(model)
+    for _ in range(max(1, args.warmup - 1)):
+        run_decode_token_request(decoder, prompt)
+    barrier(world)
+    e2e_decode = 0.0
+    e2e_ttft = []
+    for _ in range(args.steps):
+        generated, ttft, dec = run_decode_token_request(decoder, prompt)
+        e2e_decode += dec
+        e2e_ttft.append(ttft)
+    assert generated == ref_tokens, "decode_token path disagrees with the device-resident path"
+    e2e_t = max_over_ranks(e2e_decode, world)
+    e2e_value = decode_steps * args.steps * world / e2e_t
+    decoder.close()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, _, sample = oracle_sample(model, prompt, 2, 8)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": threads_used(), "kind": "port", "sample": sample}
+
+    if rank == 0:
+        step_state_bytes = 32 * 4 - 16  # StepState: 3x8 ints + 4 ints
+        result_bytes = 64               # Result: control block + 8 token ids
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "qwen2.5-0.5b-bf16 greedy decode (BASELINE config 3)",
+                       "prompt_positions": n_prompt, "new_tokens": NEW_TOKENS, "decode_steps": decode_steps,
+                       "batch": 1, "parallelism": f"replicas x{world}",
+                       "l2": "weights 1 GB per token > 126 MB L2, no flush needed"},
+            "ttft_ms": float(np.median(prefill_ms)),
+            "ttft_cached_ms": ttft_cached_ms,
+            "e2e_ttft_ms": 1000 * statistics.median(e2e_ttft),
+            "decode_launch_ms": launch_ms,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": profiled_traffic(),
+                         "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg_bytes},
+            "e2e": {"value": e2e_value, "unit": "tokens/s",
+                    "h2d_bytes_per_step": launches_per_step * step_state_bytes,
+                    "d2h_bytes_per_step": launches_per_step * result_bytes},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+
+def run_decode_token_request(decoder, prompt):
+    """The reference's greedy loop over decode_token: sequential prefill
+    (logits only at the last position), then decode steps; returns
+    (generated ids, ttft seconds, decode seconds)."""
+    decoder.reset_prefix_cache()
+    ttft = 0.0
+    token = None
+    last = len(prompt) - 1
+    for p, t in enumerate(prompt):
+        token, elapsed = decoder.decode_token(t, p, compute_logits=(p == last))
+        ttft += elapsed
+    generated = [token]
+    decode = 0.0
+    pos = len(prompt)
+    while len(generated) < NEW_TOKENS:
+        token, elapsed = decoder.decode_token(generated[-1], pos)
+        generated.append(token)
+        decode += elapsed
+        pos += 1
+    return generated, ttft, decode
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_b200(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

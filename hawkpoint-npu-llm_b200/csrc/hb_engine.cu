@@ -634,12 +634,15 @@ int hb_profile(hb_engine *e, int enable) {
   return HB_OK;
 }
 
-int hb_profile_read(hb_engine *e, float *ms, int max, int *count) {
-  if (!e || !count) return fail(e, HB_ERR_INVALID_ARG, "engine or count is NULL");
+int hb_profile_read(hb_engine *e, float *ms, float *start_ms, int max, int *count) {
+  if (!e || !count || !ms) return fail(e, HB_ERR_INVALID_ARG, "engine, ms or count is NULL");
   HB_CUDA(e, cudaSetDevice(e->device));
   HB_CUDA(e, cudaStreamSynchronize(e->stream));
   const int n = std::min(max, e->prof_count);
-  for (int i = 0; i < n; ++i) HB_CUDA(e, cudaEventElapsedTime(&ms[i], e->ev_a[i], e->ev_b[i]));
+  for (int i = 0; i < n; ++i) {
+    HB_CUDA(e, cudaEventElapsedTime(&ms[i], e->ev_a[i], e->ev_b[i]));
+    if (start_ms) HB_CUDA(e, cudaEventElapsedTime(&start_ms[i], e->ev_a[0], e->ev_a[i]));
+  }
   *count = n;
   e->prof_count = 0;
   return HB_OK;

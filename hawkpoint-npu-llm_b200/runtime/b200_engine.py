@@ -211,13 +211,17 @@ class B200DecoderEngine:
     def profile(self, enable=True, trace=False):
         self._check(self._lib.hb_profile(self._live(), (1 if enable else 0) | (2 if trace else 0)))
 
-    def profile_read(self, max_launches=65536):
+    def profile_read(self, max_launches=65536, starts=False):
+        """Kernel durations (ms) of the launches since the last read; with
+        starts=True also each launch's start (ms) relative to the first."""
         buf = np.zeros(max_launches, np.float32)
+        st = np.zeros(max_launches, np.float32)
         count = ctypes.c_int(0)
+        fp = ctypes.POINTER(ctypes.c_float)
         self._check(self._lib.hb_profile_read(
-            self._live(), buf.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), max_launches,
-            ctypes.byref(count)))
-        return buf[: count.value].copy()
+            self._live(), buf.ctypes.data_as(fp), st.ctypes.data_as(fp), max_launches, ctypes.byref(count)))
+        n = count.value
+        return (buf[:n].copy(), st[:n].copy()) if starts else buf[:n].copy()
 
     def set_stream(self, stream_handle):
         self._check(self._lib.hb_set_stream(self._live(), ctypes.c_void_p(stream_handle or None)))

@@ -1,0 +1,401 @@
+"""Drop-in ``NPUDecoder`` running the decoder engine on a B200.
+
+Same import path and surface as the reference orchestrator
+(``from runtime.generate import NPUDecoder``; npu_llm/runtime/generate.py:41-1316),
+so ``api_server.py``, ``chat.py`` and the benchmark scripts run on it
+unchanged:
+
+* ``NPUDecoder(model_dir, context_length=64, npu_layers=None)``;
+* ``decode_token(token_id, position, *, diagnostics=False, select=None,
+  compute_logits=True)`` -> ``(next_token, elapsed[, diagnostics])``;
+* ``generate_messages`` / ``generate_text`` / ``generate`` generators,
+  ``warmup``, ``reset_prefix_cache``, ``close``;
+* attributes ``tokenizer``, ``context_length``, ``model.metadata``,
+  ``_engine``, ``_cached_prefix``, ``_prefix_cache_enabled``, ``npu_layers``,
+  ``layers``; the same generation statistics keys.
+
+Every layer, the final norm, the LM head and the greedy argmax run on the GPU
+in one kernel launch per position (libhawkb200.so); logits are copied to the
+host only when a ``select`` callback or diagnostics need them.  There is no
+CPU path: ``npu_layers`` other than all layers is rejected.
+
+Host-side helpers outside the engine path (sampling, stop strings, the chat
+tokenizer) come from the reference's own ``runtime.sampling``,
+``runtime.stopping`` and ``runtime.tokenizer`` when this package is overlaid
+on the reference; a standalone install falls back to ``runtime.host_shims``
+(greedy decoding only).
+
+Environment: ``HAWKPOINT_PREFIX_CACHE`` (default 1) and ``HAWKPOINT_PROFILE``
+as in the reference; ``HAWKPOINT_W8=1`` selects int8 weights;
+``HAWKPOINT_DEVICE`` picks the CUDA device (default 0).
+"""
+
+from collections import OrderedDict
+import gc
+import os
+import resource
+import time
+
+import numpy as np
+
+from runtime.model import open_model
+
+try:  # the reference's host modules, when overlaid
+    from runtime.sampling import GREEDY, Sampler, SamplingParams
+    from runtime.stopping import StopMatcher, log_softmax, normalize_logprobs, normalize_stop
+except ImportError:  # standalone install
+    from runtime.host_shims import (  # noqa: F401
+        GREEDY, Sampler, SamplingParams, StopMatcher, log_softmax, normalize_logprobs, normalize_stop,
+    )
+try:
+    from runtime.tokenizer import SmolLMTokenizer, StreamDetokenizer
+except ImportError:
+    SmolLMTokenizer = None
+    from runtime.host_shims import StreamDetokenizer
+
+CONTEXT = 64
+
+
+def _load_tokenizer(model_dir, family):
+    if SmolLMTokenizer is None or not isinstance(model_dir, (str, os.PathLike)):
+        return None
+    if not os.path.exists(os.path.join(model_dir, "tokenizer.json")):
+        return None
+    system = (
+        "You are Qwen, created by Alibaba Cloud. You are a helpful assistant."
+        if family == "qwen2"
+        else "You are a helpful AI assistant named SmolLM."
+    )
+    return SmolLMTokenizer(model_dir, default_system=system)
+
+
+class NPUDecoder:
+    """Greedy / sampled generation over the B200 decoder engine."""
+
+    def __init__(self, model_dir, context_length=64, npu_layers=None):
+        if context_length != CONTEXT:
+            raise ValueError("the decoder engine keeps a fixed 64-token cache")
+        self._closed = False
+        self._engine = None
+        self.model = open_model(model_dir)
+        meta = self.model.metadata
+        self.model_family = meta.get("model_family", "llama")
+        self.tokenizer = _load_tokenizer(model_dir, self.model_family)
+        self.context_length = context_length
+        self.hidden_size = int(meta["hidden_size"])
+        self.intermediate_size = int(meta["intermediate_size"])
+        self.q_heads = int(meta["attention_heads"])
+        self.kv_heads = int(meta["kv_heads"])
+        self.head_dim = int(meta["head_dim"])
+        self.rms_norm_eps = float(meta.get("rms_norm_eps", 1e-5))
+        self.layers = int(meta["layers"])
+        self.npu_layers = self.layers if npu_layers is None else int(npu_layers)
+        if self.npu_layers != self.layers:
+            raise ValueError(
+                f"npu_layers must be {self.layers}: every layer runs on the GPU "
+                "(there is no CPU decoder path)"
+            )
+        self._profile_enabled = os.environ.get("HAWKPOINT_PROFILE") == "1"
+        self._phase_totals = {}
+        # Token ids whose keys and values are valid at cache positions 0..n-1
+        # (the prefix-cache contract of npu_llm/runtime/generate.py:76-79).
+        self._cached_prefix = []
+        self._prefix_cache_enabled = os.environ.get("HAWKPOINT_PREFIX_CACHE", "1") != "0"
+        weights = "w8" if os.environ.get("HAWKPOINT_W8") == "1" else "bf16"
+        device = int(os.environ.get("HAWKPOINT_DEVICE", "0"))
+        from runtime.b200_engine import B200DecoderEngine
+
+        self._engine = B200DecoderEngine(self.model, weights=weights, device=device)
+        self.weights = weights
+        self._qwen_embedding_cache = OrderedDict()  # kept for attribute compatibility
+
+    # -- helpers ---------------------------------------------------------------
+    def _record_phase(self, name, started):
+        if self._profile_enabled:
+            self._phase_totals[name] = self._phase_totals.get(name, 0.0) + (time.perf_counter() - started)
+
+    def _eos_id(self):
+        if self.tokenizer is not None:
+            return self.tokenizer.eos_id
+        return None
+
+    @staticmethod
+    def _decode_result(logits, start, diagnostics, select=None):
+        """Token selection and optional top-5 diagnostics
+        (npu_llm/runtime/generate.py:709-730)."""
+        values = np.asarray(logits, dtype=np.float32)
+        token = int(np.argmax(values)) if select is None else int(select(values))
+        elapsed = time.perf_counter() - start
+        if not diagnostics:
+            return token, elapsed
+        top = np.argpartition(values, -5)[-5:]
+        top = top[np.argsort(values[top])[::-1]]
+        return token, elapsed, {
+            "top_token_ids": [int(i) for i in top],
+            "top_logits": [float(values[i]) for i in top],
+            "top_logit_margin": float(values[top[0]] - values[top[1]]),
+        }
+
+    # -- engine step ---------------------------------------------------------------
+    def decode_token(self, token_id, position, *, diagnostics=False, select=None, compute_logits=True):
+        """One position through the whole model; ``(next_token, elapsed)``.
+
+        ``select`` picks the token from the FP32 logits (default: argmax, taken
+        on the GPU without copying the logits back).  ``compute_logits=False``
+        (non-final prefill positions) advances the KV cache and returns
+        ``(None, elapsed)``.
+        """
+        if not 0 <= position < self.context_length:
+            raise ValueError("position outside the 64-token context")
+        # This step overwrites the cache at `position`: later positions were
+        # computed from another history and are no longer reusable.
+        del self._cached_prefix[position:]
+        if self._engine is None:
+            raise RuntimeError("decoder is closed")
+        start = time.perf_counter()
+        if not compute_logits:
+            self._engine.step(token_id, position, logits=False)
+            self._record_phase("npu_engine", start)
+            return None, time.perf_counter() - start
+        if select is None and not diagnostics:
+            token = self._engine.step_argmax(token_id, position)
+            self._record_phase("npu_engine", start)
+            return token, time.perf_counter() - start
+        logits = self._engine.step(token_id, position, logits=True)
+        self._record_phase("npu_engine", start)
+        return self._decode_result(logits, start, diagnostics, select)
+
+    def warmup(self):
+        """Run one step, then forget it (npu_llm/runtime/generate.py:895-946)."""
+        eos = self._eos_id()
+        self.decode_token(eos if eos is not None else 0, 0)
+        self._engine.reset()
+        self._cached_prefix.clear()
+
+    def reset_prefix_cache(self):
+        """Forget the reusable prompt prefix so the next prompt is fully prefilled."""
+        self._cached_prefix.clear()
+
+    def _reusable_prefix(self, prompt_ids):
+        """Leading prompt positions still valid in the cache; the last prompt
+        position is always recomputed for its logits."""
+        if not self._prefix_cache_enabled:
+            return 0
+        shared = 0
+        for cached, token in zip(self._cached_prefix, prompt_ids):
+            if cached != token:
+                break
+            shared += 1
+        return min(shared, len(prompt_ids) - 1)
+
+    def _decode_step(self, token_id, position, **kwargs):
+        del self._cached_prefix[position:]
+        result = self.decode_token(token_id, position, **kwargs)
+        if len(self._cached_prefix) == position:
+            self._cached_prefix.append(int(token_id))
+        return result
+
+    def _logprob_entry(self, logits, token_id, top_logprobs):
+        """OpenAI ``logprobs`` entry from the raw distribution."""
+        values = log_softmax(logits)
+
+        def describe(index):
+            return {
+                "token": self.tokenizer.decode([int(index)]),
+                "logprob": float(values[index]),
+                "bytes": list(self.tokenizer.token_bytes(int(index))),
+            }
+
+        entry = describe(token_id)
+        top = []
+        if top_logprobs:
+            count = min(top_logprobs, values.shape[0])
+            best = np.argpartition(values, -count)[-count:]
+            best = best[np.argsort(values[best])[::-1]]
+            top = [describe(i) for i in best]
+        entry["top_logprobs"] = top
+        return entry
+
+    # -- generation ------------------------------------------------------------------
+    def _prepare(self, max_new_tokens, sampling, stop, logprobs):
+        if not 0 < max_new_tokens < self.context_length:
+            raise ValueError(f"max_new_tokens must be between 1 and {self.context_length - 1}")
+        if sampling is None:
+            params = GREEDY
+        elif isinstance(sampling, SamplingParams):
+            params = sampling
+        else:
+            params = SamplingParams.from_dict(sampling)
+        stop_matcher = StopMatcher(normalize_stop(stop))
+        top_logprobs = normalize_logprobs(logprobs)
+        sampler = Sampler(params, vocab_size=self.model.metadata["vocab_size"])
+        if getattr(self, "_profile_enabled", False):
+            self._phase_totals = {}
+        if self.tokenizer is None:
+            raise RuntimeError("the model package has no tokenizer; use decode_token with token ids")
+        return sampler, stop_matcher, top_logprobs
+
+    def generate_messages(self, messages, max_new_tokens=16, sampling=None, *, stop=None, logprobs=None):
+        """Chat completion over an OpenAI-style message list, windowed to the
+        64-token context at turn boundaries; yields ``(text, None[, entries])``
+        chunks then ``("", stats[, []])``."""
+        sampler, stop_matcher, top_logprobs = self._prepare(max_new_tokens, sampling, stop, logprobs)
+        prompt_ids, truncation = self.tokenizer.encode_chat_window(
+            messages, self.context_length - max_new_tokens
+        )
+        yield from self._generate_tokens_core(
+            prompt_ids, truncation, max_new_tokens, sampler, stop_matcher, top_logprobs
+        )
+
+    def generate_text(self, prompt, max_new_tokens=16, sampling=None, *, stop=None, logprobs=None):
+        """Completion of a raw prompt without chat scaffolding."""
+        sampler, stop_matcher, top_logprobs = self._prepare(max_new_tokens, sampling, stop, logprobs)
+        prompt_ids, truncated = self.tokenizer.encode_prompt_window(
+            prompt, self.context_length - max_new_tokens
+        )
+        yield from self._generate_tokens_core(
+            prompt_ids, {"truncated_prompt": truncated}, max_new_tokens, sampler, stop_matcher, top_logprobs
+        )
+
+    def generate(self, prompt, max_new_tokens=32, sampling=None, *, stop=None, logprobs=None):
+        """Single-prompt chat generation."""
+        yield from self.generate_messages(
+            [{"role": "user", "content": prompt}],
+            max_new_tokens=max_new_tokens, sampling=sampling, stop=stop, logprobs=logprobs,
+        )
+
+    def _generate_tokens_core(self, prompt_ids, truncation, max_new_tokens, sampler, stop_matcher, top_logprobs):
+        """Prefill (one step per prompt position, logits only at the last),
+        then decode until the token budget, EOS or a stop string -- the loop of
+        npu_llm/runtime/generate.py:1050-1200."""
+        history = list(prompt_ids)         # penalties see the prompt too
+        pending = []                       # (byte offset of the token's text, logprob entry)
+        state = {"entry": None}
+        produced = 0
+        emitted = 0
+
+        def choose(logits):
+            token = int(np.argmax(logits)) if sampler.greedy else sampler.select(logits, history)
+            if top_logprobs is not None:
+                state["entry"] = self._logprob_entry(logits, token, top_logprobs)
+            return token
+
+        # greedy without logprobs keeps the on-device argmax path
+        select = None if sampler.greedy and top_logprobs is None else choose
+
+        def release(text, final=False):
+            nonlocal emitted
+            emitted += len(text.encode("utf-8"))
+            if final and stop_matcher.matched is None:
+                ready = len(pending)
+            else:
+                ready = 0
+                while ready < len(pending) and pending[ready][0] < emitted:
+                    ready += 1
+            out = [entry for _, entry in pending[:ready]]
+            del pending[:ready]
+            return out
+
+        def chunk(text, entries):
+            return (text, None) if top_logprobs is None else (text, None, entries)
+
+        reused = self._reusable_prefix(prompt_ids)
+        timings = []
+        token = None
+        last = len(prompt_ids) - 1
+        for index in range(reused, len(prompt_ids)):
+            token, elapsed = self._decode_step(
+                prompt_ids[index], index,
+                select=select if index == last else None,
+                compute_logits=index == last,
+            )
+            timings.append(elapsed)
+        prefill_steps = len(timings)
+        position = len(prompt_ids)
+        detokenizer = StreamDetokenizer(self.tokenizer)
+        generated = []
+        finish_reason = "length"
+        text = ""
+        while len(generated) < max_new_tokens:
+            entry, state["entry"] = state["entry"], None
+            if token == self.tokenizer.eos_id:
+                finish_reason = "stop"
+                break
+            generated.append(token)
+            history.append(token)
+            if entry is not None:
+                pending.append((produced, entry))
+                produced += len(self.tokenizer.token_bytes(token))
+            text = stop_matcher.feed(detokenizer.push(token))
+            if stop_matcher.matched is not None:
+                finish_reason = "stop"
+                break
+            if text:
+                yield chunk(text, release(text))
+            if len(generated) >= max_new_tokens:
+                break  # never compute a discarded successor token
+            token, elapsed = self._decode_step(token, position, select=select)
+            timings.append(elapsed)
+            position += 1
+        if stop_matcher.matched is None:
+            text = stop_matcher.feed(detokenizer.flush())
+            if stop_matcher.matched is not None:
+                finish_reason = "stop"
+            text += stop_matcher.flush()
+        entries = release(text, final=True) if top_logprobs is not None else []
+        if text or entries:
+            yield chunk(text, entries)
+        prefill_seconds = sum(timings[:prefill_steps])
+        decode_seconds = sum(timings[prefill_steps:])
+        decode_steps = len(timings) - prefill_steps
+        stats = {
+            "prompt_tokens": len(prompt_ids),
+            "cached_prompt_tokens": reused,
+            "prompt_truncation": truncation,
+            "generated_tokens": len(generated),
+            "generated_token_ids": generated,
+            "npu_layers": self.npu_layers,
+            "cpu_layers": self.layers - self.npu_layers,
+            "finish_reason": finish_reason,
+            "stop_sequence": stop_matcher.matched,
+            "ttft_seconds": prefill_seconds,
+            "prefill_tokens_per_second": prefill_steps / max(1e-9, prefill_seconds),
+            "decode_steps": decode_steps,
+            "decode_seconds": decode_seconds,
+            "decode_tokens_per_second": decode_steps / max(1e-9, decode_seconds),
+            "peak_ram_mib": resource.getrusage(resource.RUSAGE_SELF).ru_maxrss / 1024,
+            "sampling": sampler.stats(),
+        }
+        if getattr(self, "_profile_enabled", False):
+            stats["phase_ms"] = {name: round(s * 1000.0, 3) for name, s in self._phase_totals.items()}
+        if top_logprobs is None:
+            yield "", stats
+        else:
+            yield "", stats, []
+
+    def generate_ids(self, prompt_ids, max_new_tokens):
+        """Greedy generation from token ids with the whole loop on the device
+        (prefix reuse as in ``generate_messages``); returns (ids, stats)."""
+        if not 0 < max_new_tokens < self.context_length:
+            raise ValueError(f"max_new_tokens must be between 1 and {self.context_length - 1}")
+        prompt_ids = [int(t) for t in prompt_ids]
+        if not prompt_ids or len(prompt_ids) + max_new_tokens > self.context_length:
+            raise ValueError("prompt + generated tokens must fit the 64-token context")
+        reused = self._reusable_prefix(prompt_ids)
+        start = time.perf_counter()
+        ids = self._engine.generate(prompt_ids, max_new_tokens, start=reused)
+        elapsed = time.perf_counter() - start
+        self._cached_prefix[reused:] = prompt_ids[reused:] + ids[:-1]
+        return ids, {"cached_prompt_tokens": reused, "seconds": elapsed}
+
+    def close(self):
+        """Release the GPU engine (idempotent)."""
+        if getattr(self, "_closed", False):
+            return
+        self._closed = True
+        engine = getattr(self, "_engine", None)
+        if engine is not None:
+            engine.close()
+        self._engine = None
+        self._cached_prefix = []
+        gc.collect()

@@ -91,7 +91,7 @@ SIGNATURES = {
     "hb_last_error": (ctypes.c_char_p, [_P]),
     "hb_debug_dump": (_I, [_P, _I, _P, ctypes.c_size_t]),
     "hb_profile": (_I, [_P, _I]),
-    "hb_profile_read": (_I, [_P, _FP, _I, ctypes.POINTER(_I)]),
+    "hb_profile_read": (_I, [_P, _FP, _FP, _I, ctypes.POINTER(_I)]),
     "hb_set_stream": (_I, [_P, _P]),
     "hb_test_stall_next": (_I, [_P, ctypes.c_uint64]),
     "hb_gemv_scratch_bytes": (ctypes.c_size_t, [_I, _I]),

@@ -53,9 +53,9 @@ enum {
  * it.  Projections are stored "row-group major": 8 consecutive output rows
  * form a group, and a group stores its K dimension as 16-byte column chunks,
  * each chunk holding those 8 rows (chunk j of row r at group_base + j*128 +
- * r*16).  o_proj is split by attention head into [hidden x head_dim] slabs;
- * gate_up alternates 8 gate rows and the 8 matching up rows.  W8 projections
- * store int8 in the same arrangement plus one FP32 scale per (packed) row. */
+ * r*16).  gate_up alternates 8 gate rows and the 8 matching up rows.  W8
+ * projections store int8 in the same arrangement plus one FP32 scale per
+ * (packed) row. */
 typedef struct hb_layer_offsets {
   uint64_t gamma_in, gamma_post, qkv_bias;      /* FP32 [hidden], [hidden], [qkv] */
   uint64_t w_qkv, s_qkv;                        /* s_*: W8 row scales, else 0 */
@@ -135,18 +135,23 @@ int hb_reset(hb_engine *engine, int slot);
 int hb_copy_prefix(hb_engine *engine, int src_slot, int dst_slot, int n_positions);
 
 /* Diagnostics.  hb_debug_dump copies engine state for parity tests:
- * HB_DUMP_HIDDEN = BF16 residual stream [max_batch x hidden] after the last
- * step; HB_DUMP_KV = BF16 cache of one slot [layers][kv_heads][2][context][head_dim]
- * (slot taken from *(int*)out on entry). */
-enum { HB_DUMP_HIDDEN = 0, HB_DUMP_KV = 1 };
+ * HB_DUMP_HIDDEN = BF16 residual stream [8 x hidden] after the last step;
+ * HB_DUMP_KV = BF16 cache of one slot, per (layer, kv head) K transposed
+ * [head_dim][context] then V [context][head_dim] (slot taken from *(int*)out
+ * on entry); HB_DUMP_TRACE = uint64 [SMs][4*layers+2][8] device timestamps of
+ * the last launch traced with hb_profile(engine, 2). */
+enum { HB_DUMP_HIDDEN = 0, HB_DUMP_KV = 1, HB_DUMP_TRACE = 2 };
 const char *hb_last_error(const hb_engine *engine);
 int hb_debug_dump(hb_engine *engine, int what, void *out, size_t bytes);
 
-/* Profiling: when enabled, each decode-kernel launch is bracketed by CUDA
- * events on the engine's stream; hb_profile_read returns the durations (ms)
- * of up to max launches since the last read and clears the record. */
+/* Profiling: when enabled (bit 0), each decode-kernel launch is bracketed by
+ * CUDA events on the engine's stream; bit 1 also records per-phase device
+ * timestamps of every CTA (hb_debug_dump kind 2).  hb_profile_read returns
+ * the durations (ms) of up to max launches since the last read, and when
+ * start_ms is not NULL each launch's start relative to the first one, then
+ * clears the record. */
 int hb_profile(hb_engine *engine, int enable);
-int hb_profile_read(hb_engine *engine, float *ms, int max, int *count);
+int hb_profile_read(hb_engine *engine, float *ms, float *start_ms, int max, int *count);
 
 /* Runs the engine's work on the caller's stream (cudaStream_t as void*);
  * NULL restores the engine's own stream. */

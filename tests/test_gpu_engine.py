@@ -3,9 +3,14 @@
 
 Parity rule (modelled on npu_llm/tests/benchmark_qwen_fused.py:19,98-109 and
 npu_llm/tests/validate_engine_npu.py:57-86), teacher-forced per position:
-* FP32 logits: max |engine - oracle| <= 5e-2 and ||d||/||ref|| <= 1e-2;
-* argmax equal, except where the oracle's top-1 margin is <= 0.05 and the
-  top-2 sets agree (a documented BF16 near-tie);
+* FP32 logits: max |engine - oracle| <= 5e-2 and ||d||/||ref|| <= 1e-2 for
+  the 2-layer models; for the full 24/30-layer models 0.1 and 3e-2, because
+  there the reference's own arithmetic moves by rel 1.5% / max-abs 0.04 when
+  only its summation order changes (tests/test_numeric_floor.py measures it):
+  the random-init network amplifies any rounding difference;
+* argmax equal, except where the oracle's top-1 margin is within the
+  observed logit error (<= 0.05 for the small models, <= 2 x max-abs for the
+  full ones) and the top-2 sets agree (a documented BF16 near-tie);
 * BF16 hidden state / KV cache: bits equal except for a small fraction of
   one-unit differences (FP32 summation order differs from NumPy's BLAS).
 """
@@ -23,6 +28,8 @@ pytestmark = pytest.mark.gpu
 ATOL = 5e-2
 RTOL = 1e-2
 NEAR_TIE = 0.05
+ATOL_FULL = 0.1
+RTOL_FULL = 3e-2
 
 
 def assert_logits_close(got, ref, where=""):
@@ -198,13 +205,15 @@ def test_full_size_against_reference_golden(name, golden):
             got = engine.step(int(t), p, logits=True)
             # the reference's top-32 logits and a strided sample
             ref_top = g["top_logits"][p]
-            assert np.abs(got[g["top_ids"][p]] - ref_top).max() <= ATOL
+            top_err = np.abs(got[g["top_ids"][p]] - ref_top).max()
+            assert top_err <= ATOL_FULL
             sample = got[::stride]
             d = np.abs(sample - g["sample_logits"][p])
-            assert d.max() <= ATOL
+            assert d.max() <= ATOL_FULL
             rel = np.linalg.norm(sample - g["sample_logits"][p]) / np.linalg.norm(g["sample_logits"][p])
-            assert rel <= RTOL
+            assert rel <= RTOL_FULL
             if int(np.argmax(got)) != int(g["argmax"][p]):
-                assert g["margin"][p] <= NEAR_TIE
+                assert g["margin"][p] <= 2 * max(top_err, d.max())
+                assert set(np.argsort(-got)[:2]) == set(g["top_ids"][p][:2])
     finally:
         engine.close()
