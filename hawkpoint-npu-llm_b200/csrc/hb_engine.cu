@@ -10,6 +10,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -733,6 +734,166 @@ int hb_gemv(const void *w_dev, const float *scales_dev, int weight_format, int r
   void *args[] = {&P};
   err = cudaLaunchKernel(fn, dim3(G), dim3(hb::kThreads), args, smem, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return fail(nullptr, HB_ERR_CUDA, "hb_gemv launch: %s", cudaGetErrorString(err));
+  return HB_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------- hb_gemv_noalloc --
+// The standalone GEMV (+ fused argmax) without a caller-supplied scratch
+// buffer.
+//
+// hb_gemv needs a small device scratch area (a control block with the
+// done-counter of the fused argmax and one partial (value, index) per CTA and
+// batch row), and asks the caller to allocate it.  Some callers cannot: a
+// serving process that sized its whole GPU memory pool (weights plus KV
+// cache) at start-up and forbids device allocations afterwards, or a hot path
+// that must not call cudaMalloc / cudaFree because those can synchronize the
+// device and stall every other stream.  This section gives them a variant
+// whose scratch lives in a fixed, file-scope __device__ array that the
+// library owns.
+//
+// Limits and sharing rules:
+// * the array holds kNoAllocCtas partial results per batch row for up to
+//   kNoAllocBatch batch rows (65,568 bytes in all, control block included);
+//   requests that would need more are rejected with HB_ERR_UNSUPPORTED;
+// * every GPU that loads the library holds one copy of the array until the
+//   process exits;
+// * the first call on a device looks up the array's device address
+//   (cudaGetSymbolAddress, with that device current) and caches it, so that
+//   first call should come before any stream capture;
+// * all calls on a device share that one array, so calls whose kernels could
+//   run at the same time on the GPU (different streams, no ordering between
+//   them) race on it and may return wrong argmax results; order such calls
+//   on one stream;
+// * the array keeps whatever the previous call left in it, so each call
+//   clears the control block (cudaMemsetAsync, no allocation) before its
+//   launch.
+// The entry point allocates nothing: no cudaMalloc, no cudaFree, no library
+// routine that allocates.
+namespace {
+
+constexpr int kNoAllocCtas = 1024;                    // partial slots per batch row
+constexpr int kNoAllocBatch = hb::kMaxBatchGemv;      // 8 batch rows
+constexpr size_t kNoAllocScratchBytes =
+    sizeof(hb::Ctrl) + 2 * sizeof(float) * kNoAllocCtas * kNoAllocBatch;  // 65,568 bytes
+constexpr int kMaxDevices = 64;
+constexpr uint64_t kLimitNs = 2000000000ull;
+
+// The scratch itself.  In host code this name is only a stand-in for the
+// device symbol, never a device address: the device address comes from
+// cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_setup_mutex;
+void *g_scratch_dev[kMaxDevices] = {};
+
+int noalloc_fail(int code, const char *msg) { return fail(nullptr, code, "hb_gemv_noalloc: %s", msg); }
+
+// Device address of the scratch array on the current device, looked up once
+// per device (with that device current) and cached.
+int scratch_address(int device, void **out) {
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
+  if (g_scratch_dev[device] == nullptr) {
+    void *ptr = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (err != cudaSuccess || ptr == nullptr)
+      return noalloc_fail(HB_ERR_CUDA, cudaGetErrorString(err));
+    g_scratch_dev[device] = ptr;
+  }
+  *out = g_scratch_dev[device];
+  return HB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int hb_gemv_noalloc(const void *w_dev, const float *scales_dev, int weight_format, int rows, int k,
+                    const void *x_dev, int batch, void *y_dev, int flags, int32_t *argmax_dev,
+                    void *stream) {
+  const int out_mode = flags & 3;
+  const bool want_argmax = (flags & HB_GEMV_ARGMAX) != 0;
+  if (!w_dev || !x_dev || rows <= 0 || k <= 0 || rows % 8 || k % 32)
+    return noalloc_fail(HB_ERR_INVALID_ARG, "bad shape (rows % 8 == 0 and k % 32 == 0 required)");
+  if (batch < 1) return noalloc_fail(HB_ERR_INVALID_ARG, "batch must be at least 1");
+  if (batch > kNoAllocBatch)
+    return noalloc_fail(HB_ERR_UNSUPPORTED, "batch exceeds the 8 rows the built-in scratch holds");
+  if (weight_format != HB_WEIGHTS_BF16 && weight_format != HB_WEIGHTS_W8)
+    return noalloc_fail(HB_ERR_INVALID_ARG, "unknown weight format");
+  if (weight_format == HB_WEIGHTS_W8 && !scales_dev)
+    return noalloc_fail(HB_ERR_INVALID_ARG, "W8 weights need scales");
+  if (out_mode > 2 || (out_mode != 2 && !y_dev)) return noalloc_fail(HB_ERR_INVALID_ARG, "bad output");
+  if (want_argmax && !argmax_dev) return noalloc_fail(HB_ERR_INVALID_ARG, "argmax output missing");
+  if (reinterpret_cast<uintptr_t>(w_dev) % 16 || reinterpret_cast<uintptr_t>(x_dev) % 16)
+    return noalloc_fail(HB_ERR_INVALID_ARG, "W and x must be 16-byte aligned");
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return noalloc_fail(HB_ERR_CUDA, "no usable current CUDA device");
+  int sms = 0, optin = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+    return noalloc_fail(HB_ERR_CUDA, "device query failed");
+  const int n_rg = rows / 8;
+  const int G = sms < n_rg ? sms : n_rg;
+  if (G > kNoAllocCtas)
+    return noalloc_fail(HB_ERR_UNSUPPORTED, "more CTAs than the built-in scratch has partial slots");
+
+  void *scratch = nullptr;
+  int rc = scratch_address(dev, &scratch);
+  if (rc != HB_OK) return rc;
+
+  const bool w8 = weight_format == HB_WEIGHTS_W8;
+  const int esize = w8 ? 1 : 2;
+  const int kc = k * esize / 16;
+  const int rg_per_cta = (n_rg + G - 1) / G;
+  const bool whole = kc * 128 <= static_cast<int>(hb::kSlotBytes);
+  const int per_warp = (whole && rg_per_cta >= 16) ? 1 : 0;
+  const int red_rows = per_warp ? 1 : rg_per_cta * 8;
+  const int mb = batch > 1 ? 8 : 1;
+  const size_t fixed = hb::gemv_smem_bytes(0, mb, k, red_rows);
+  int nslots = static_cast<int>((static_cast<size_t>(optin) - fixed - 16 * 16) / hb::kSlotBytes);
+  if (nslots > 16) nslots = 16;
+  if (nslots < 4) return noalloc_fail(HB_ERR_UNSUPPORTED, "shape too large for shared memory");
+  const size_t smem = hb::gemv_smem_bytes(nslots, mb, k, red_rows);
+  const void *fn;
+  if (mb == 1)
+    fn = w8 ? reinterpret_cast<const void *>(&hb::gemv_kernel<1, true>)
+            : reinterpret_cast<const void *>(&hb::gemv_kernel<1, false>);
+  else
+    fn = w8 ? reinterpret_cast<const void *>(&hb::gemv_kernel<8, true>)
+            : reinterpret_cast<const void *>(&hb::gemv_kernel<8, false>);
+  cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (err != cudaSuccess) return noalloc_fail(HB_ERR_CUDA, cudaGetErrorString(err));
+
+  // the control block must start at zero (done counter, error flags)
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  err = cudaMemsetAsync(scratch, 0, sizeof(hb::Ctrl), s);
+  if (err != cudaSuccess) return noalloc_fail(HB_ERR_CUDA, cudaGetErrorString(err));
+
+  hb::GemvParams P{};
+  P.w = static_cast<const uint8_t *>(w_dev);
+  P.scales = scales_dev;
+  P.rows = rows;
+  P.kc = kc;
+  P.K = k;
+  P.x = static_cast<const __nv_bfloat16 *>(x_dev);
+  P.batch = batch;
+  P.y = y_dev;
+  P.out_mode = out_mode;
+  P.argmax = want_argmax ? 1 : 0;
+  P.argmax_out = argmax_dev;
+  P.ctrl = static_cast<hb::Ctrl *>(scratch);
+  P.part_val = reinterpret_cast<float *>(static_cast<unsigned char *>(scratch) + sizeof(hb::Ctrl));
+  P.part_idx = reinterpret_cast<int *>(P.part_val + kNoAllocCtas * kNoAllocBatch);
+  P.nslots = nslots;
+  P.red_rows = red_rows;
+  P.per_warp = per_warp;
+  P.limit_ns = kLimitNs;
+  void *args[] = {&P};
+  err = cudaLaunchKernel(fn, dim3(G), dim3(hb::kThreads), args, smem, s);
+  if (err != cudaSuccess) return noalloc_fail(HB_ERR_CUDA, cudaGetErrorString(err));
   return HB_OK;
 }
 

@@ -96,6 +96,7 @@ SIGNATURES = {
     "hb_test_stall_next": (_I, [_P, ctypes.c_uint64]),
     "hb_gemv_scratch_bytes": (ctypes.c_size_t, [_I, _I]),
     "hb_gemv": (_I, [_P, _P, _I, _I, _I, _P, _I, _P, _I, _P, _P, ctypes.c_size_t, _P]),
+    "hb_gemv_noalloc": (_I, [_P, _P, _I, _I, _I, _P, _I, _P, _I, _P, _P]),
     "hb_library_error": (ctypes.c_char_p, []),
     "hb_device_sm_count": (_I, [_I]),
 }

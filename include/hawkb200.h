@@ -180,6 +180,23 @@ int hb_gemv(const void *w_dev, const float *scales_dev, int weight_format,
             int flags, int32_t *argmax_dev, void *scratch_dev,
             size_t scratch_bytes, void *stream);
 
+/* hb_gemv without the scratch argument, for callers that cannot allocate
+ * device memory -- e.g. a serving process whose GPU memory pool was sized at
+ * start-up and forbids later allocations, or a hot path that must not call
+ * cudaMalloc/cudaFree because they can synchronize the device.  No
+ * counterpart in the reference (its NPU path has no device allocator).
+ * Same arguments and results as hb_gemv; the scratch is a fixed 65,568-byte
+ * __device__ array inside the library (room for batch <= 8 and up to 1024
+ * CTAs; larger requests return HB_ERR_UNSUPPORTED), held by every GPU that
+ * loads the library until the process exits.  The first call on a device
+ * looks the array's address up (make it before any stream capture).  All
+ * calls on a device share the array: calls that may overlap on the GPU
+ * (unordered streams) race.  Allocates nothing; errors in
+ * hb_library_error(). */
+int hb_gemv_noalloc(const void *w_dev, const float *scales_dev, int weight_format,
+                    int rows, int k, const void *x_dev, int batch, void *y_dev,
+                    int flags, int32_t *argmax_dev, void *stream);
+
 /* Library-level error text (for calls that have no engine, e.g. hb_gemv). */
 const char *hb_library_error(void);
 
