@@ -674,8 +674,8 @@ int hb_gemv(const void *w_dev, const float *scales_dev, int weight_format, int r
             void *stream) {
   const int out_mode = flags & 3;
   const bool want_argmax = (flags & HB_GEMV_ARGMAX) != 0;
-  if (!w_dev || !x_dev || rows <= 0 || k <= 0 || rows % 8 || k % 16 || batch < 1 || batch > hb::kMaxBatchGemv)
-    return fail(nullptr, HB_ERR_INVALID_ARG, "hb_gemv: bad shape (rows %% 8, k %% 16, batch 1..8)");
+  if (!w_dev || !x_dev || rows <= 0 || k <= 0 || rows % 8 || k % 32 || batch < 1 || batch > hb::kMaxBatchGemv)
+    return fail(nullptr, HB_ERR_INVALID_ARG, "hb_gemv: bad shape (rows %% 8, k %% 32, batch 1..8)");
   if (weight_format != HB_WEIGHTS_BF16 && weight_format != HB_WEIGHTS_W8)
     return fail(nullptr, HB_ERR_INVALID_ARG, "hb_gemv: unknown weight format");
   if (weight_format == HB_WEIGHTS_W8 && !scales_dev) return fail(nullptr, HB_ERR_INVALID_ARG, "hb_gemv: W8 needs scales");

@@ -170,7 +170,7 @@ int hb_test_stall_next(hb_engine *engine, uint64_t limit_ns);
  * with W8 weights the sum is multiplied by scales[r] before rounding.
  * HB_GEMV_ARGMAX also writes argmax_dev[b] (first index of the maximum, as
  * np.argmax).  W is packed row-group major (runtime/layout.py); rows % 8 == 0,
- * k % 16 == 0; batch is 1..8.  All pointers are device pointers; scratch_dev
+ * k % 32 == 0; batch is 1..8.  All pointers are device pointers; scratch_dev
  * must hold hb_gemv_scratch_bytes(rows, batch) bytes.  Runs on `stream`. */
 enum { HB_GEMV_OUT_BF16 = 0, HB_GEMV_OUT_F32 = 1, HB_GEMV_OUT_NONE = 2 };
 enum { HB_GEMV_ARGMAX = 4 };

@@ -73,6 +73,9 @@ def test_layout_offsets_outside_the_blob_are_rejected(lib):
 def test_gemv_rejects_bad_shapes_on_the_host(lib):
     from runtime import hb_lib
     assert lib.hb_gemv(None, None, 0, 12, 16, None, 1, None, 0, None, None, 0, None) == hb_lib.HB_ERR_INVALID_ARG
+    # K must be a multiple of 32 (the tensor-core step covers 32 columns)
+    fake = ctypes.c_void_p(256)
+    assert lib.hb_gemv(fake, None, 0, 16, 48, fake, 1, fake, 0, None, fake, 1 << 20, None) == hb_lib.HB_ERR_INVALID_ARG
     assert lib.hb_gemv_scratch_bytes(896, 1) >= 32
 
 
