@@ -22,9 +22,11 @@
 // waiting on activations, so HBM keeps streaming while consumers wait for
 // the previous phase's words.
 //
-// KV cache layout per (slot, layer, kv head): K transposed [64 dims][CTX]
-// (positions contiguous, so lane-per-position score loops read consecutive
-// shared-memory addresses), then V [CTX][64].
+// KV cache layout per (slot, layer, kv head): K [CTX][64] then V [CTX][64],
+// each row of 128 bytes with its eight 16-byte blocks XOR-swizzled by the
+// position (block cb of row s at s*128 + (cb ^ (s & 7))*16), so tensor-core
+// fragment loads (ldmatrix) of 8 consecutive positions are bank-conflict
+// free.
 #pragma once
 
 #include "hb_stream.cuh"
@@ -76,7 +78,7 @@ struct DecParams {
   const float *s_lm;
   const __nv_bfloat16 *embed;
   const float *rope_cos, *rope_sin;  // [CTX][32]
-  __nv_bfloat16 *kv;                 // [slots][L][KVH][K^T 64xCTX | V CTXx64]
+  __nv_bfloat16 *kv;                 // [slots][L][KVH][K CTXx64 | V CTXx64], swizzled rows
   uint64_t *ll;                      // LL words, see ll_* below
   float *logits;                     // [MB][V]
   float *part_val;                   // [G][kMaxBatch]
@@ -279,7 +281,7 @@ struct DecoderCta {
     }
   }
 
-  // K^T (kind 0) or V (kind 1) block of one kv head of one slot/layer.
+  // K (kind 0) or V (kind 1) block of one kv head of one slot/layer.
   __device__ __nv_bfloat16 *kv_block(int slot, int layer, int kvh, int kind) const {
     return P.kv + (((static_cast<size_t>(slot) * P.L + layer) * P.KVH + kvh) * 2 + kind) *
                       static_cast<size_t>(P.CTX) * kHeadDim;
@@ -360,17 +362,28 @@ struct DecoderCta {
     return v;
   }
 
-  // hx[m][:] = f32 of the BF16 vector in LL buffer(m)
-  template <class BufFn>
-  __device__ bool gather_to_hx(BufFn &&buf, int nvals) {
-    const int words = nvals / 2;
-    float *h = hx;
+  // hx[m][:] = f32 of the BF16 vector in the LL words at src (row m at
+  // src + m * row_words).
+  __device__ bool gather_to_hx(const uint64_t *src, size_t row_words, int nvals) {
     for (int m = 0; m < mrows; ++m) {
-      float *dst = h + m * P.H;
-      if (!ll_gather(buf(m), words, epoch, &P.result->ctrl, P.limit_ns, [&](int i, uint32_t d) {
-            dst[2 * i] = bf_lo(d);
-            dst[2 * i + 1] = bf_hi(d);
-          }))
+      float *dst = hx + m * P.H;
+      if (!ll_gather(src + m * row_words, nvals / 2, epoch, &P.result->ctrl, P.limit_ns,
+                     [&](int i, uint32_t d) {
+                       dst[2 * i] = bf_lo(d);
+                       dst[2 * i + 1] = bf_hi(d);
+                     }))
+        return false;
+    }
+    return true;
+  }
+
+  // Raw payloads of the LL words (BF16 pairs) into dst[m * dst_words + i].
+  __device__ bool gather_raw(const uint64_t *src, size_t row_words, int words, uint32_t *dst,
+                                          size_t dst_words) {
+    for (int m = 0; m < mrows; ++m) {
+      uint32_t *out = dst + m * dst_words;
+      if (!ll_gather(src + m * row_words, words, epoch, &P.result->ctrl, P.limit_ns,
+                     [&](int i, uint32_t d) { out[i] = d; }))
         return false;
     }
     return true;
@@ -389,7 +402,7 @@ struct DecoderCta {
         const int m = idx / P.H, i = idx - m * P.H;
         hx[idx] = bf2f(P.embed[static_cast<size_t>(s_tok[m]) * P.H + i]);
       }
-    } else if (!gather_to_hx([&](int m) { return ll_hout(layer - 1, m); }, P.H)) {
+    } else if (!gather_to_hx(ll_hout(layer - 1, 0), P.H / 2, P.H)) {
       return false;
     }
     consumer_sync(kConsumerThreads);
@@ -417,50 +430,26 @@ struct DecoderCta {
     return true;
   }
 
-  // Attention of every head for batch row m, reading the K/V history from
-  // ring chunks; writes the BF16 output to xs[m][0..QH*64).
+  // Byte offset of 16-byte block cb (dims 8cb..8cb+7) of position s in a K or
+  // V block: rows of 128 bytes, blocks XOR-swizzled by the row so the 8 rows
+  // an ldmatrix reads fall in distinct banks.
+  __device__ __forceinline__ static int kv_off(int s, int cb) { return s * 128 + ((cb ^ (s & 7)) << 4); }
+
+  // Attention of every head for batch row m on the tensor cores, reading the
+  // K/V history from ring chunks; writes the BF16 output to xs[m][0..QH*64).
+  //   S = Q K^T (per kv head: the group's q heads are the A rows, positions
+  //   the N columns), softmax in registers (FP32), O = P V with P split
+  //   exactly into three BF16 terms so the products keep FP32 precision.
   __device__ bool attention_row(int layer, int m, float2 rope0) {
     const int warp = tid >> 5, lane = tid & 31;
     const int p = s_pos[m];
-    const int QH = P.QH, KVH = P.KVH, CTX = P.CTX;
-    float *aq = att;                       // [QH][64] rotated q
-    float *ak = aq + QH * kHeadDim;        // [KVH][64] rotated k
-    float *av = ak + KVH * kHeadDim;       // [KVH][64] v
-    float *prob = av + KVH * kHeadDim;     // [QH][CTX]
-    const uint32_t *row = qkv_s + static_cast<size_t>(m) * P.QKV / 2;
-    // RoPE on q and k (rotate-half, cpu_backend.py:78-93), unfused mul/add
-    const int npairs = (QH + KVH) * 32;
-    for (int idx = tid; idx < npairs + KVH * 32; idx += kConsumerThreads) {
-      if (idx < npairs) {
-        const int hh = idx >> 5, d = idx & 31;
-        const int base = hh * kHeadDim;  // q heads then k heads are contiguous in qkv
-        const __nv_bfloat16 *rb = reinterpret_cast<const __nv_bfloat16 *>(row);
-        const float x0 = bf2f(rb[base + d]), x1 = bf2f(rb[base + d + 32]);
-        const float c = m == 0 ? rope0.x : P.rope_cos[p * 32 + d];
-        const float s = m == 0 ? rope0.y : P.rope_sin[p * 32 + d];
-        const float lo = rbf(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s)));
-        const float hi = rbf(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s)));
-        float *dst = hh < QH ? aq + hh * kHeadDim : ak + (hh - QH) * kHeadDim;
-        dst[d] = lo;
-        dst[d + 32] = hi;
-      } else {
-        const int j = (idx - npairs) >> 5, d = (idx - npairs) & 31;
-        const __nv_bfloat16 *rb = reinterpret_cast<const __nv_bfloat16 *>(row);
-        const int base = (QH + KVH + j) * kHeadDim;
-        av[j * kHeadDim + d] = bf2f(rb[base + d]);
-        av[j * kHeadDim + d + 32] = bf2f(rb[base + d + 32]);
-      }
-    }
-    consumer_sync(kConsumerThreads);
-    // CTA j appends kv head j of this position to the cache (K transposed).
-    if (cta < KVH && tid < kHeadDim) {
-      const int j = cta;
-      __nv_bfloat16 *kt = kv_block(s_slot[m], layer, j, 0);
-      __nv_bfloat16 *vv = kv_block(s_slot[m], layer, j, 1);
-      kt[tid * CTX + p] = f2bf(ak[j * kHeadDim + tid]);
-      vv[p * kHeadDim + tid] = f2bf(av[j * kHeadDim + tid]);
-    }
-    // history chunks: K^T of every kv head, then V of every kv head, in
+    const int QH = P.QH, KVH = P.KVH, grp = P.group;
+    const int qstride = kHeadDim + 8;                    // padded rows: conflict-free fragment loads
+    const int pstride = P.CTX + 4;
+    __nv_bfloat16 *qb = reinterpret_cast<__nv_bfloat16 *>(att);       // [QH][72] rotated q
+    float *prob = att + (QH * qstride + 1) / 2;                        // [QH][CTX+4]
+    const __nv_bfloat16 *rb = reinterpret_cast<const __nv_bfloat16 *>(qkv_s + static_cast<size_t>(m) * P.QKV / 2);
+    // history chunks: K of every kv head, then V of every kv head, in
     // consecutive ring positions
     const RingPos first{ring.slot, ring.parity};
     RingPos pos = first;
@@ -473,76 +462,156 @@ struct DecoderCta {
     auto chunk_ptr = [&](int c) {
       RingPos q = first;
       ring_advance(q, c, ring.nslots);
-      return slot_ptr(ring, q.slot);
+      return const_cast<uint8_t *>(slot_ptr(ring, q.slot));
     };
-    // scores + softmax: warp per head, lane per position
-    for (int h = warp; h < QH; h += kWarps) {
-      const int j = h / P.group;
-      const __nv_bfloat16 *kt = reinterpret_cast<const __nv_bfloat16 *>(chunk_ptr(j));
-      const float *q = aq + h * kHeadDim;
-      float sc[4];
-      float mx = -INFINITY;
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int s = lane + 32 * t;
-        sc[t] = -INFINITY;
-        if (s <= p && s < CTX) {
-          float a4[4] = {0.f, 0.f, 0.f, 0.f};
-          if (s == p) {
-            const float *kk = ak + j * kHeadDim;
-#pragma unroll
-            for (int d = 0; d < kHeadDim; ++d) a4[d & 3] = fmaf(q[d], kk[d], a4[d & 3]);
-          } else {
-#pragma unroll
-            for (int d = 0; d < kHeadDim; ++d) a4[d & 3] = fmaf(q[d], bf2f(kt[d * CTX + s]), a4[d & 3]);
-          }
-          sc[t] = ((a4[0] + a4[1]) + (a4[2] + a4[3])) * 0.125f;
-          mx = fmaxf(mx, sc[t]);
+    // RoPE (rotate-half, cpu_backend.py:78-93, unfused mul/add) on q -> qb,
+    // on k -> row p of the K chunk; v -> row p of the V chunk.
+    const int nrot = (QH + KVH) * 32;
+    for (int idx = tid; idx < nrot + KVH * 32; idx += kConsumerThreads) {
+      const int hh = idx >> 5, d = idx & 31;
+      if (idx < nrot) {
+        const float x0 = bf2f(rb[hh * kHeadDim + d]), x1 = bf2f(rb[hh * kHeadDim + d + 32]);
+        const float c = m == 0 ? rope0.x : P.rope_cos[p * 32 + d];
+        const float sn = m == 0 ? rope0.y : P.rope_sin[p * 32 + d];
+        const __nv_bfloat16 lo = f2bf(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+        const __nv_bfloat16 hi = f2bf(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
+        if (hh < QH) {
+          qb[hh * qstride + d] = lo;
+          qb[hh * qstride + d + 32] = hi;
+        } else {
+          uint8_t *kc = chunk_ptr(hh - QH);
+          *reinterpret_cast<__nv_bfloat16 *>(kc + kv_off(p, d >> 3) + (d & 7) * 2) = lo;
+          *reinterpret_cast<__nv_bfloat16 *>(kc + kv_off(p, 4 + (d >> 3)) + (d & 7) * 2) = hi;
         }
-      }
-      mx = warp_max(mx);
-      float sum = 0.f;
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int s = lane + 32 * t;
-        if (s <= p && s < CTX) {
-          sc[t] = expf(__fsub_rn(sc[t], mx));
-          sum += sc[t];
-        }
-      }
-      sum = warp_sum(sum);
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int s = lane + 32 * t;
-        if (s <= p && s < CTX) prob[h * CTX + s] = __fdiv_rn(sc[t], sum);
+      } else {
+        const int j = hh - QH - KVH;
+        uint8_t *vc = chunk_ptr(KVH + j);
+        const int base = (QH + KVH + j) * kHeadDim;
+        *reinterpret_cast<__nv_bfloat16 *>(vc + kv_off(p, d >> 3) + (d & 7) * 2) = rb[base + d];
+        *reinterpret_cast<__nv_bfloat16 *>(vc + kv_off(p, 4 + (d >> 3)) + (d & 7) * 2) = rb[base + d + 32];
       }
     }
     consumer_sync(kConsumerThreads);
-    // P.V: warp per head, lane per pair of dims
-    for (int h = warp; h < QH; h += kWarps) {
-      const int j = h / P.group;
-      const uint32_t *vv = reinterpret_cast<const uint32_t *>(chunk_ptr(KVH + j));
-      const float *pr = prob + h * CTX;
-      float e0[4] = {0.f, 0.f, 0.f, 0.f}, e1[4] = {0.f, 0.f, 0.f, 0.f};
-      int s = 0;
-      for (; s + 4 <= p; s += 4) {
+    // CTA j appends kv head j of this position to the cache.
+    if (cta < KVH && tid < 16) {
+      const int j = cta, kind = tid >> 3, cb = tid & 7;
+      const uint8_t *src = chunk_ptr(kind * KVH + j) + kv_off(p, cb);
+      uint8_t *dst = reinterpret_cast<uint8_t *>(kv_block(s_slot[m], layer, j, kind)) + kv_off(p, cb);
+      *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
+    }
+    const int g = lane >> 2, t2 = (lane & 3) * 2;
+    const int nks = (p >> 4) + 1;  // 16-position k-steps of P V
+    // S = Q K^T and softmax: one warp per kv head
+    if (warp < KVH) {
+      const int j = warp;
+      const uint32_t kbase = smem_u32(chunk_ptr(j));
+      uint32_t a0[4], a2[4], a1[4], a3[4];
+      const __nv_bfloat16 *q0 = qb + (j * grp + g) * qstride;
+      const __nv_bfloat16 *q1 = qb + (j * grp + g + 8) * qstride;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint32_t w = vv[(s + u) * (kHeadDim / 2) + lane];
-          e0[u] = fmaf(pr[s + u], bf_lo(w), e0[u]);
-          e1[u] = fmaf(pr[s + u], bf_hi(w), e1[u]);
+      for (int ks = 0; ks < 4; ++ks) {
+        a0[ks] = g < grp ? *reinterpret_cast<const uint32_t *>(q0 + 16 * ks + t2) : 0u;
+        a2[ks] = g < grp ? *reinterpret_cast<const uint32_t *>(q0 + 16 * ks + 8 + t2) : 0u;
+        a1[ks] = g + 8 < grp ? *reinterpret_cast<const uint32_t *>(q1 + 16 * ks + t2) : 0u;
+        a3[ks] = g + 8 < grp ? *reinterpret_cast<const uint32_t *>(q1 + 16 * ks + 8 + t2) : 0u;
+      }
+      float sc[8][4];
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = -INFINITY;
+        if (nt <= (p >> 3)) {
+          float d[4] = {0.f, 0.f, 0.f, 0.f};
+          const int row = 8 * nt + (lane & 7);
+#pragma unroll
+          for (int k2 = 0; k2 < 2; ++k2) {
+            uint32_t b[4];
+            ldsm_x4(b, kbase + kv_off(row, 4 * k2 + (lane >> 3)));
+            mma_16816_full(d, a0[2 * k2], a1[2 * k2], a2[2 * k2], a3[2 * k2], b[0], b[1]);
+            mma_16816_full(d, a0[2 * k2 + 1], a1[2 * k2 + 1], a2[2 * k2 + 1], a3[2 * k2 + 1], b[2], b[3]);
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int s = 8 * nt + t2 + (e & 1);
+            sc[nt][e] = s <= p ? d[e] * 0.125f : -INFINITY;
+          }
+          mx0 = fmaxf(mx0, fmaxf(sc[nt][0], sc[nt][1]));
+          mx1 = fmaxf(mx1, fmaxf(sc[nt][2], sc[nt][3]));
         }
       }
-      for (; s < p; ++s) {
-        const uint32_t w = vv[s * (kHeadDim / 2) + lane];
-        e0[0] = fmaf(pr[s], bf_lo(w), e0[0]);
-        e1[0] = fmaf(pr[s], bf_hi(w), e1[0]);
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float mx = e < 2 ? mx0 : mx1;
+          const float v = sc[nt][e] == -INFINITY ? 0.f : expf(__fsub_rn(sc[nt][e], mx));
+          sc[nt][e] = v;
+          if (e < 2) sum0 += v; else sum1 += v;
+        }
       }
-      e0[1] = fmaf(pr[p], av[j * kHeadDim + 2 * lane], e0[1]);
-      e1[1] = fmaf(pr[p], av[j * kHeadDim + 2 * lane + 1], e1[1]);
-      const float a0 = (e0[0] + e0[1]) + (e0[2] + e0[3]);
-      const float a1 = (e1[0] + e1[1]) + (e1[2] + e1[3]);
-      reinterpret_cast<uint32_t *>(xs + static_cast<size_t>(m) * P.xs_elems)[h * 32 + lane] = pack_bf16x2(a0, a1);
+      sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
+      sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
+      sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
+      sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
+      // probabilities of every position the P V k-steps cover (0 past p)
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        if (nt < 2 * nks) {
+          if (g < grp) {
+            float *pr = prob + (j * grp + g) * pstride + 8 * nt + t2;
+            pr[0] = __fdiv_rn(sc[nt][0], sum0);
+            pr[1] = __fdiv_rn(sc[nt][1], sum0);
+          }
+          if (g + 8 < grp) {
+            float *pr = prob + (j * grp + g + 8) * pstride + 8 * nt + t2;
+            pr[0] = __fdiv_rn(sc[nt][2], sum1);
+            pr[1] = __fdiv_rn(sc[nt][3], sum1);
+          }
+        }
+      }
+    }
+    consumer_sync(kConsumerThreads);
+    // O = P V: work items (kv head j, 8-dim block dn) over all warps
+    for (int item = warp; item < KVH * 8; item += kWarps) {
+      const int j = item >> 3, dn = item & 7;
+      const uint32_t vbase = smem_u32(chunk_ptr(KVH + j));
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      const float *pr0 = prob + (j * grp + g) * pstride + t2;
+      const float *pr1 = prob + (j * grp + g + 8) * pstride + t2;
+      for (int ks = 0; ks < nks; ++ks) {
+        uint32_t b[2];
+        ldsm_x2_trans(b, vbase + kv_off(16 * ks + (lane & 15), dn));
+        float v0[4] = {0.f, 0.f, 0.f, 0.f}, v1[4] = {0.f, 0.f, 0.f, 0.f};
+        if (g < grp) {
+          const float2 x = *reinterpret_cast<const float2 *>(pr0 + 16 * ks);
+          const float2 y = *reinterpret_cast<const float2 *>(pr0 + 16 * ks + 8);
+          v0[0] = x.x; v0[1] = x.y; v0[2] = y.x; v0[3] = y.y;
+        }
+        if (g + 8 < grp) {
+          const float2 x = *reinterpret_cast<const float2 *>(pr1 + 16 * ks);
+          const float2 y = *reinterpret_cast<const float2 *>(pr1 + 16 * ks + 8);
+          v1[0] = x.x; v1[1] = x.y; v1[2] = y.x; v1[3] = y.y;
+        }
+        // three BF16 terms per probability: hi + mid + lo == the FP32 value
+        uint32_t ah[4], am[4], al[4];
+        split3_pack(v0[0], v0[1], ah[0], am[0], al[0]);
+        split3_pack(v1[0], v1[1], ah[1], am[1], al[1]);
+        split3_pack(v0[2], v0[3], ah[2], am[2], al[2]);
+        split3_pack(v1[2], v1[3], ah[3], am[3], al[3]);
+        mma_16816_full(d, ah[0], ah[1], ah[2], ah[3], b[0], b[1]);
+        mma_16816_full(d, am[0], am[1], am[2], am[3], b[0], b[1]);
+        mma_16816_full(d, al[0], al[1], al[2], al[3], b[0], b[1]);
+      }
+      __nv_bfloat16 *out = xs + static_cast<size_t>(m) * P.xs_elems;
+      if (g < grp)
+        *reinterpret_cast<uint32_t *>(out + (j * grp + g) * kHeadDim + 8 * dn + t2) = pack_bf16x2(d[0], d[1]);
+      if (g + 8 < grp)
+        *reinterpret_cast<uint32_t *>(out + (j * grp + g + 8) * kHeadDim + 8 * dn + t2) = pack_bf16x2(d[2], d[3]);
     }
     __syncwarp();
     consumer_sync(kConsumerThreads);
@@ -562,12 +631,7 @@ struct DecoderCta {
     const int npairs = (r.g1 - r.g0) * 4;
     const float2 scale0 = load_pair(W8 ? lp.s_o : nullptr, r.g0 * 8, npairs);
     const float2 rope0 = make_float2(P.rope_cos[s_pos[0] * 32 + (tid & 31)], P.rope_sin[s_pos[0] * 32 + (tid & 31)]);
-    for (int m = 0; m < mrows; ++m) {
-      uint32_t *dst = qkv_s + static_cast<size_t>(m) * P.QKV / 2;
-      if (!ll_gather(ll_qkv(layer, m), P.QKV / 2, epoch, &P.result->ctrl, P.limit_ns,
-                     [&](int i, uint32_t d) { dst[i] = d; }))
-        return false;
-    }
+    if (!gather_raw(ll_qkv(layer, 0), P.QKV / 2, P.QKV / 2, qkv_s, P.QKV / 2)) return false;
     consumer_sync(kConsumerThreads);
     mark(4 * layer + 1, 1);
     for (int m = 0; m < mrows; ++m)
@@ -596,7 +660,7 @@ struct DecoderCta {
   __device__ bool phase_mlp_in(int layer) {
     const LayerPtrs &lp = P.layers[layer];
     const Gamma gamma = load_gamma(lp.gamma_post);
-    if (!gather_to_hx([&](int m) { return ll_h1(layer, m); }, P.H)) return false;
+    if (!gather_to_hx(ll_h1(layer, 0), P.H / 2, P.H)) return false;
     consumer_sync(kConsumerThreads);
     mark(4 * layer + 2, 1);
     norm_rows(gamma);
@@ -634,12 +698,8 @@ struct DecoderCta {
 
   __device__ bool phase_mlp_out(int layer) {
     const LayerPtrs &lp = P.layers[layer];
-    for (int m = 0; m < mrows; ++m) {
-      uint32_t *dst = reinterpret_cast<uint32_t *>(xs + static_cast<size_t>(m) * P.xs_elems);
-      if (!ll_gather(ll_act(layer, m), P.I / 2, epoch, &P.result->ctrl, P.limit_ns,
-                     [&](int i, uint32_t d) { dst[i] = d; }))
-        return false;
-    }
+    if (!gather_raw(ll_act(layer, 0), P.I / 2, P.I / 2, reinterpret_cast<uint32_t *>(xs), P.xs_elems / 2))
+      return false;
     consumer_sync(kConsumerThreads);
     mark(4 * layer + 3, 1);
     const MatRange r = phase_range(4 * layer + 3);
@@ -667,7 +727,7 @@ struct DecoderCta {
   __device__ bool phase_head() {
     const int warp = tid >> 5, lane = tid & 31;
     const Gamma gamma = load_gamma(P.gamma_final);
-    if (!gather_to_hx([&](int m) { return ll_hout(P.L - 1, m); }, P.H)) return false;
+    if (!gather_to_hx(ll_hout(P.L - 1, 0), P.H / 2, P.H)) return false;
     consumer_sync(kConsumerThreads);
     norm_rows(gamma);
     float bv[MB];

@@ -332,19 +332,6 @@ int run_chained(hb_engine *e, int slot, const int32_t *ids, int n_prompt, int st
   return HB_OK;
 }
 
-// Copies positions [0, n) of every (layer, kv head) block of one slot's cache
-// into another slot: K^T rows (first n of each of the 64 dims) and V rows.
-__global__ void kv_copy_prefix_kernel(const __nv_bfloat16 *src, __nv_bfloat16 *dst, int ctx, int n) {
-  const size_t block = static_cast<size_t>(blockIdx.x) * 2 * ctx * hb::kHeadDim;
-  const __nv_bfloat16 *ks = src + block, *vs = ks + static_cast<size_t>(ctx) * hb::kHeadDim;
-  __nv_bfloat16 *kd = dst + block, *vd = kd + static_cast<size_t>(ctx) * hb::kHeadDim;
-  for (int i = threadIdx.x; i < hb::kHeadDim * n; i += blockDim.x) {
-    const int d = i / n, s = i - d * n;
-    kd[d * ctx + s] = ks[d * ctx + s];
-    vd[s * hb::kHeadDim + d] = vs[s * hb::kHeadDim + d];
-  }
-}
-
 }  // namespace
 
 extern "C" {
@@ -584,11 +571,13 @@ int hb_copy_prefix(hb_engine *e, int src, int dst, int n_positions) {
   if (n_positions < 0 || n_positions > d.context) return fail(e, HB_ERR_INVALID_ARG, "n_positions out of range");
   if (src == dst || n_positions == 0) return HB_OK;
   HB_CUDA(e, cudaSetDevice(e->device));
-  const int blocks = d.layers * d.kv_heads;
-  kv_copy_prefix_kernel<<<blocks, 256, 0, e->stream>>>(e->d_kv + e->kv_slot_elems * src,
-                                                        e->d_kv + e->kv_slot_elems * dst, d.context,
-                                                        n_positions);
-  HB_CUDA(e, cudaGetLastError());
+  // every K and V block is [context][64] with 128-byte position rows: copy
+  // the first n rows of each block
+  const size_t pitch = static_cast<size_t>(d.context) * hb::kHeadDim * 2;
+  const size_t height = static_cast<size_t>(d.layers) * d.kv_heads * 2;
+  HB_CUDA(e, cudaMemcpy2DAsync(e->d_kv + e->kv_slot_elems * dst, pitch, e->d_kv + e->kv_slot_elems * src, pitch,
+                               static_cast<size_t>(n_positions) * hb::kHeadDim * 2, height,
+                               cudaMemcpyDeviceToDevice, e->stream));
   HB_CUDA(e, cudaStreamSynchronize(e->stream));
   return HB_OK;
 }

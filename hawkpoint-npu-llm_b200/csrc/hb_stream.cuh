@@ -182,6 +182,34 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void ldsm_x2_trans(uint32_t (&r)[2], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_16816_full(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Two FP32 values as three packed BF16 pairs whose per-element sums
+// hi + mid + lo carry every mantissa bit of the inputs.
+__device__ __forceinline__ void split3_pack(float x, float y, uint32_t &hi, uint32_t &mid, uint32_t &lo) {
+  const __nv_bfloat16 xh = __float2bfloat16_rn(x), yh = __float2bfloat16_rn(y);
+  const float xr = x - __bfloat162float(xh), yr = y - __bfloat162float(yh);
+  const __nv_bfloat16 xm = __float2bfloat16_rn(xr), ym = __float2bfloat16_rn(yr);
+  const __nv_bfloat16 xl = __float2bfloat16_rn(xr - __bfloat162float(xm));
+  const __nv_bfloat16 yl = __float2bfloat16_rn(yr - __bfloat162float(ym));
+  hi = static_cast<uint32_t>(__bfloat16_as_ushort(xh)) | (static_cast<uint32_t>(__bfloat16_as_ushort(yh)) << 16);
+  mid = static_cast<uint32_t>(__bfloat16_as_ushort(xm)) | (static_cast<uint32_t>(__bfloat16_as_ushort(ym)) << 16);
+  lo = static_cast<uint32_t>(__bfloat16_as_ushort(xl)) | (static_cast<uint32_t>(__bfloat16_as_ushort(yl)) << 16);
+}
+
 // Accumulate the dot products of one row group over chunk columns
 // [jc_begin, jc_end) stepping by `stride` (multiples of 4): 4 chunk columns
 // = 2 k16 steps per iteration.  `sg` = the group's bytes in shared memory,
@@ -206,6 +234,47 @@ __device__ __forceinline__ void mma_group(float (&d)[4], const uint8_t *sg, cons
     mma_16816(d, a0, a2, b[0], b[1]);
     mma_16816(d, c0, c2, b[2], b[3]);
   }
+}
+
+// Split-K form of mma_group for one warp: at most kPartCols / 32 = 4
+// iterations (chunk columns warp*4 + 32 i); every fragment is loaded before
+// the first MMA and the MMAs alternate two accumulators.
+__device__ __forceinline__ void mma_group_splitk(float (&d)[4], const uint8_t *sg, const __nv_bfloat16 *xrow,
+                                                 int col0, int ncols) {
+  constexpr int U = kPartCols / kColGroups;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t base = smem_u32(sg) + ((lane >> 3) * 128) + ((lane & 7) * 16);
+  const int t2 = (lane & 3) * 2;
+  uint32_t b[U][4], a[U][4];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int jc = warp * 4 + u * kColGroups;
+    if (jc < ncols) {
+      ldsm_x4(b[u], base + jc * 128);
+      if (xrow != nullptr) {
+        const __nv_bfloat16 *x = xrow + (col0 + jc) * 8 + t2;
+        a[u][0] = *reinterpret_cast<const uint32_t *>(x);
+        a[u][1] = *reinterpret_cast<const uint32_t *>(x + 8);
+        a[u][2] = *reinterpret_cast<const uint32_t *>(x + 16);
+        a[u][3] = *reinterpret_cast<const uint32_t *>(x + 24);
+      } else {
+        a[u][0] = a[u][1] = a[u][2] = a[u][3] = 0u;
+      }
+    }
+  }
+  float e[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int jc = warp * 4 + u * kColGroups;
+    if (jc < ncols) {
+      mma_16816(d, a[u][0], a[u][1], b[u][0], b[u][1]);
+      mma_16816(e, a[u][2], a[u][3], b[u][2], b[u][3]);
+    }
+  }
+  d[0] += e[0];
+  d[1] += e[1];
+  d[2] += e[2];
+  d[3] += e[3];
 }
 
 // CUDA-core dot products for W8 (int8 weights, chunk column = 16 weights).

@@ -188,15 +188,17 @@ class B200DecoderEngine:
     def kv_cache(self, slot=0):
         """BF16 bits of one slot's cache as [layers, kv_heads, 2 (K, V), context, 64].
 
-        The device keeps K transposed ([64, context] per head); this view
-        undoes that so it compares directly with the reference's caches."""
+        The device stores each position's 64 values as eight 16-byte blocks
+        XOR-swizzled by the position (block b at (b ^ (pos & 7)) * 16); this
+        view undoes that so it compares directly with the reference's caches."""
         s = self.shape
-        raw = np.zeros((s.layers, s.kv_heads, 2, self.context * s.head_dim), np.uint16)
+        raw = np.zeros((s.layers, s.kv_heads, 2, self.context, 8, 8), np.uint16)
         raw.view(np.int32).reshape(-1)[0] = slot
         self._check(self._lib.hb_debug_dump(self._live(), hb_lib.HB_DUMP_KV, raw.ctypes.data, raw.nbytes))
-        keys = raw[:, :, 0].reshape(s.layers, s.kv_heads, s.head_dim, self.context).transpose(0, 1, 3, 2)
-        values = raw[:, :, 1].reshape(s.layers, s.kv_heads, self.context, s.head_dim)
-        return np.ascontiguousarray(np.stack([keys, values], axis=2))
+        pos = np.arange(self.context)[:, None]
+        block = np.arange(8)[None, :] ^ (pos & 7)          # physical block of logical block b
+        out = np.take_along_axis(raw, block[None, None, None, :, :, None], axis=4)
+        return np.ascontiguousarray(out.reshape(s.layers, s.kv_heads, 2, self.context, s.head_dim))
 
     def phase_trace(self):
         """globaltimer stamps [G, 4L+2, 8] of the last launch traced with

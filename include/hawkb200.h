@@ -136,9 +136,9 @@ int hb_copy_prefix(hb_engine *engine, int src_slot, int dst_slot, int n_position
 
 /* Diagnostics.  hb_debug_dump copies engine state for parity tests:
  * HB_DUMP_HIDDEN = BF16 residual stream [8 x hidden] after the last step;
- * HB_DUMP_KV = BF16 cache of one slot, per (layer, kv head) K transposed
- * [head_dim][context] then V [context][head_dim] (slot taken from *(int*)out
- * on entry); HB_DUMP_TRACE = uint64 [SMs][4*layers+2][8] device timestamps of
+ * HB_DUMP_KV = BF16 cache of one slot, per (layer, kv head) K then V, each
+ * [context][head_dim] with the eight 16-byte blocks of a position stored at
+ * block ^ (position & 7) (slot taken from *(int*)out on entry); HB_DUMP_TRACE = uint64 [SMs][4*layers+2][8] device timestamps of
  * the last launch traced with hb_profile(engine, 2). */
 enum { HB_DUMP_HIDDEN = 0, HB_DUMP_KV = 1, HB_DUMP_TRACE = 2 };
 const char *hb_last_error(const hb_engine *engine);
