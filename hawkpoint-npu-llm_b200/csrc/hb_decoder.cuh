@@ -287,13 +287,13 @@ struct DecoderCta {
                       static_cast<size_t>(P.CTX) * kHeadDim;
   }
 
-  // trace point (0 start, 1 inputs ready, 2 weights consumed, 3 outputs stored)
+  // trace point (0 start, 1 inputs ready, 6 prologue (norm / attention)
+  // done, 2 weights consumed, 3 outputs stored; slots 4 and 5 hold the ring
+  // wait and the producer's first issue of the phase)
   __device__ __forceinline__ void mark(int k, int point) const {
     if (P.trace && tid == 0) {
       unsigned long long *t = P.trace + (static_cast<size_t>(cta) * (4 * P.L + 2) + k) * 8;
       t[point] = globaltimer_ns();
-      if (point == 1) t[6] = clock64();
-      if (point == 2) t[7] = clock64();
     }
   }
 
@@ -390,46 +390,6 @@ struct DecoderCta {
   }
 
   // ---- phases -------------------------------------------------------------------
-  __device__ bool phase_qkv(int layer) {
-    const LayerPtrs &lp = P.layers[layer];
-    const MatRange r = phase_range(4 * layer);
-    const int npairs = (r.g1 - r.g0) * 4;
-    const Gamma gamma = load_gamma(lp.gamma_in);
-    const float2 bias0 = load_pair(P.has_bias ? lp.bias : nullptr, r.g0 * 8, npairs);
-    const float2 scale0 = load_pair(W8 ? lp.s_qkv : nullptr, r.g0 * 8, npairs);
-    if (layer == 0) {
-      for (int idx = tid; idx < mrows * P.H; idx += kConsumerThreads) {
-        const int m = idx / P.H, i = idx - m * P.H;
-        hx[idx] = bf2f(P.embed[static_cast<size_t>(s_tok[m]) * P.H + i]);
-      }
-    } else if (!gather_to_hx(ll_hout(layer - 1, 0), P.H / 2, P.H)) {
-      return false;
-    }
-    consumer_sync(kConsumerThreads);
-    mark(4 * layer, 1);
-    norm_rows(gamma);
-    if (!consume_splitk<MB, W8>(ring, r, xs, P.xs_elems, mrows, red, P.red_rows, &P.result->ctrl,
-                                P.limit_ns))
-      return false;
-    consumer_sync(kConsumerThreads);
-    mark(4 * layer, 2);
-    for (int idx = tid; idx < mrows * npairs; idx += kConsumerThreads) {
-      const int m = idx / npairs, lp2 = idx - m * npairs;
-      const int row = r.g0 * 8 + 2 * lp2;
-      const bool mine = lp2 == tid;
-      float y[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        float v = red_sum(m, 2 * lp2 + e);
-        if (W8) v *= mine ? (e ? scale0.y : scale0.x) : lp.s_qkv[row + e];
-        y[e] = rbf(v);
-        if (P.has_bias) y[e] = __fadd_rn(y[e], mine ? (e ? bias0.y : bias0.x) : lp.bias[row + e]);
-      }
-      ll_store(ll_qkv(layer, m) + row / 2, pack_bf16x2(y[0], y[1]), epoch);
-    }
-    return true;
-  }
-
   // Byte offset of 16-byte block cb (dims 8cb..8cb+7) of position s in a K or
   // V block: rows of 128 bytes, blocks XOR-swizzled by the row so the 8 rows
   // an ldmatrix reads fall in distinct banks.
@@ -625,22 +585,84 @@ struct DecoderCta {
     return true;
   }
 
-  __device__ bool phase_attn(int layer) {
+  // One phase of a layer (kind = k & 3: 0 qkv, 1 attention + o_proj,
+  // 2 gate_up + SwiGLU, 3 down).  A prologue leaves the GEMV's BF16 input in
+  // xs, then the GEMV over this CTA's rows -- a single call site for every
+  // kind, so the hot loop's code stays resident in the instruction cache --
+  // then a short epilogue publishes the results as LL words.
+  __device__ bool layer_phase(int k) {
+    const int layer = k >> 2, kind = k & 3;
     const LayerPtrs &lp = P.layers[layer];
-    const MatRange r = phase_range(4 * layer + 1);
+    const MatRange r = phase_range(k);
     const int npairs = (r.g1 - r.g0) * 4;
-    const float2 scale0 = load_pair(W8 ? lp.s_o : nullptr, r.g0 * 8, npairs);
-    const float2 rope0 = make_float2(P.rope_cos[s_pos[0] * 32 + (tid & 31)], P.rope_sin[s_pos[0] * 32 + (tid & 31)]);
-    if (!gather_raw(ll_qkv(layer, 0), P.QKV / 2, P.QKV / 2, qkv_s, P.QKV / 2)) return false;
+    // constants of this thread's first epilogue word, fetched before the wait
+    const float *bias_p = (kind == 0 && P.has_bias) ? lp.bias : nullptr;
+    const float *scale_p = !W8 ? nullptr : kind == 0 ? lp.s_qkv : kind == 1 ? lp.s_o : kind == 3 ? lp.s_down : nullptr;
+    const float2 bias0 = load_pair(bias_p, r.g0 * 8, npairs);
+    const float2 scale0 = load_pair(scale_p, r.g0 * 8, npairs);
+    Gamma gamma;
+    if (kind == 0 || kind == 2) gamma = load_gamma(kind == 0 ? lp.gamma_in : lp.gamma_post);
+    float2 rope0 = make_float2(0.f, 0.f);
+    if (kind == 1) rope0 = make_float2(P.rope_cos[s_pos[0] * 32 + (tid & 31)], P.rope_sin[s_pos[0] * 32 + (tid & 31)]);
+    // inputs: the previous phase's LL words (the embedding row for layer 0)
+    bool ok = true;
+    if (kind == 0) {
+      if (layer == 0) {
+        for (int idx = tid; idx < mrows * P.H; idx += kConsumerThreads) {
+          const int m = idx / P.H, i = idx - m * P.H;
+          hx[idx] = bf2f(P.embed[static_cast<size_t>(s_tok[m]) * P.H + i]);
+        }
+      } else {
+        ok = gather_to_hx(ll_hout(layer - 1, 0), P.H / 2, P.H);
+      }
+    } else if (kind == 1) {
+      ok = gather_raw(ll_qkv(layer, 0), P.QKV / 2, P.QKV / 2, qkv_s, P.QKV / 2);
+    } else if (kind == 2) {
+      ok = gather_to_hx(ll_h1(layer, 0), P.H / 2, P.H);
+    } else {
+      ok = gather_raw(ll_act(layer, 0), P.I / 2, P.I / 2, reinterpret_cast<uint32_t *>(xs), P.xs_elems / 2);
+    }
+    if (!ok) return false;
     consumer_sync(kConsumerThreads);
-    mark(4 * layer + 1, 1);
-    for (int m = 0; m < mrows; ++m)
-      if (!attention_row(layer, m, rope0)) return false;
-    if (!consume_splitk<MB, W8>(ring, r, xs, P.xs_elems, mrows, red, P.red_rows, &P.result->ctrl,
-                                P.limit_ns))
+    mark(k, 1);
+    if (kind == 0 || kind == 2) {
+      norm_rows(gamma);
+    } else if (kind == 1) {
+      for (int m = 0; m < mrows; ++m)
+        if (!attention_row(layer, m, rope0)) return false;
+    }
+    mark(k, 6);
+    if (!consume_splitk<MB, W8>(ring, r, xs, P.xs_elems, mrows, red, P.red_rows, &P.result->ctrl, P.limit_ns))
       return false;
     consumer_sync(kConsumerThreads);
-    mark(4 * layer + 1, 2);
+    mark(k, 2);
+    if (kind == 2) {
+      // SwiGLU (cpu_backend.py:154-165): g / (1 + exp(-clip(g, -80, 80))) * u
+      const int b0 = r.g0 / 2, nblk = (r.g1 - r.g0) / 2;
+      const int per_row = nblk * 4;  // LL words (pairs of intermediate indices)
+      for (int idx = tid; idx < mrows * per_row; idx += kConsumerThreads) {
+        const int m = idx / per_row;
+        const int rem = idx - m * per_row;
+        const int blk = rem >> 2, rr = (rem & 3) * 2;
+        float a[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float g = red_sum(m, blk * 16 + rr + e);
+          float u = red_sum(m, blk * 16 + 8 + rr + e);
+          if (W8) {
+            g *= lp.s_gu[(2 * (b0 + blk)) * 8 + rr + e];
+            u *= lp.s_gu[(2 * (b0 + blk) + 1) * 8 + rr + e];
+          }
+          g = rbf(g);
+          u = rbf(u);
+          const float ex = expf(-fminf(fmaxf(g, -80.f), 80.f));
+          a[e] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, ex)), u);
+        }
+        ll_store(ll_act(layer, m) + ((b0 + blk) * 8 + rr) / 2, pack_bf16x2(a[0], a[1]), epoch);
+      }
+      return true;
+    }
+    // qkv: bf16(bf16(Wx) + bias); o_proj / down: bf16(bf16(Wx) + residual)
     for (int idx = tid; idx < mrows * npairs; idx += kConsumerThreads) {
       const int m = idx / npairs, lp2 = idx - m * npairs;
       const int row = r.g0 * 8 + 2 * lp2;
@@ -649,77 +671,16 @@ struct DecoderCta {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         float v = red_sum(m, 2 * lp2 + e);
-        if (W8) v *= mine ? (e ? scale0.y : scale0.x) : lp.s_o[row + e];
-        y[e] = __fadd_rn(rbf(v), hx[m * P.H + row + e]);
-      }
-      ll_store(ll_h1(layer, m) + row / 2, pack_bf16x2(y[0], y[1]), epoch);
-    }
-    return true;
-  }
-
-  __device__ bool phase_mlp_in(int layer) {
-    const LayerPtrs &lp = P.layers[layer];
-    const Gamma gamma = load_gamma(lp.gamma_post);
-    if (!gather_to_hx(ll_h1(layer, 0), P.H / 2, P.H)) return false;
-    consumer_sync(kConsumerThreads);
-    mark(4 * layer + 2, 1);
-    norm_rows(gamma);
-    const MatRange r = phase_range(4 * layer + 2);
-    if (!consume_splitk<MB, W8>(ring, r, xs, P.xs_elems, mrows, red, P.red_rows, &P.result->ctrl,
-                                P.limit_ns))
-      return false;
-    consumer_sync(kConsumerThreads);
-    mark(4 * layer + 2, 2);
-    const int b0 = r.g0 / 2, nblk = (r.g1 - r.g0) / 2;
-    const int per_row = nblk * 4;  // LL words (pairs of intermediate indices)
-    for (int idx = tid; idx < mrows * per_row; idx += kConsumerThreads) {
-      const int m = idx / per_row;
-      const int rem = idx - m * per_row;
-      const int blk = rem >> 2, rr = (rem & 3) * 2;
-      float a[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        float g = red_sum(m, blk * 16 + rr + e);
-        float u = red_sum(m, blk * 16 + 8 + rr + e);
-        if (W8) {
-          g *= lp.s_gu[(2 * (b0 + blk)) * 8 + rr + e];
-          u *= lp.s_gu[(2 * (b0 + blk) + 1) * 8 + rr + e];
+        if (W8) v *= mine ? (e ? scale0.y : scale0.x) : scale_p[row + e];
+        y[e] = rbf(v);
+        if (kind == 0) {
+          if (bias_p != nullptr) y[e] = __fadd_rn(y[e], mine ? (e ? bias0.y : bias0.x) : bias_p[row + e]);
+        } else {
+          y[e] = __fadd_rn(y[e], hx[m * P.H + row + e]);
         }
-        g = rbf(g);
-        u = rbf(u);
-        // SwiGLU (cpu_backend.py:154-165): g / (1 + exp(-clip(g, -80, 80))) * u
-        const float ex = expf(-fminf(fmaxf(g, -80.f), 80.f));
-        a[e] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, ex)), u);
       }
-      ll_store(ll_act(layer, m) + ((b0 + blk) * 8 + rr) / 2, pack_bf16x2(a[0], a[1]), epoch);
-    }
-    return true;
-  }
-
-  __device__ bool phase_mlp_out(int layer) {
-    const LayerPtrs &lp = P.layers[layer];
-    if (!gather_raw(ll_act(layer, 0), P.I / 2, P.I / 2, reinterpret_cast<uint32_t *>(xs), P.xs_elems / 2))
-      return false;
-    consumer_sync(kConsumerThreads);
-    mark(4 * layer + 3, 1);
-    const MatRange r = phase_range(4 * layer + 3);
-    if (!consume_splitk<MB, W8>(ring, r, xs, P.xs_elems, mrows, red, P.red_rows, &P.result->ctrl,
-                                P.limit_ns))
-      return false;
-    consumer_sync(kConsumerThreads);
-    mark(4 * layer + 3, 2);
-    const int npairs = (r.g1 - r.g0) * 4;
-    for (int idx = tid; idx < mrows * npairs; idx += kConsumerThreads) {
-      const int m = idx / npairs, lp2 = idx - m * npairs;
-      const int row = r.g0 * 8 + 2 * lp2;
-      float y[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        float v = red_sum(m, 2 * lp2 + e);
-        if (W8) v *= lp.s_down[row + e];
-        y[e] = __fadd_rn(rbf(v), hx[m * P.H + row + e]);
-      }
-      ll_store(ll_hout(layer, m) + row / 2, pack_bf16x2(y[0], y[1]), epoch);
+      uint64_t *dst = kind == 0 ? ll_qkv(layer, m) : kind == 1 ? ll_h1(layer, m) : ll_hout(layer, m);
+      ll_store(dst + row / 2, pack_bf16x2(y[0], y[1]), epoch);
     }
     return true;
   }
@@ -806,13 +767,7 @@ struct DecoderCta {
         ok = phase_head();
         ran_head = true;
       } else {
-        const int layer = k >> 2;
-        switch (k & 3) {
-          case 0: ok = phase_qkv(layer); break;
-          case 1: ok = phase_attn(layer); break;
-          case 2: ok = phase_mlp_in(layer); break;
-          default: ok = phase_mlp_out(layer); break;
-        }
+        ok = layer_phase(k);
       }
       consumer_sync(kConsumerThreads);
       mark(k, 3);
