@@ -48,7 +48,7 @@ MODEL_SEED = 0
 PROMPT_DRAWN = 40
 NEW_TOKENS = 32
 METRIC = "decode_tokens_per_second"
-# Algorithmic bytes per decoded token (SURVEY 8d): BF16 weights of every layer
+# Algorithmic bytes per decoded token: BF16 weights of every layer
 # (715,653,120) + LM head (272,269,312) + norm weights (87,808) + FP32 qkv
 # bias (110,592); plus 24 layers x 512 bytes of K/V history per position.
 WEIGHT_BYTES = 988_120_832

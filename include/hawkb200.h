@@ -6,8 +6,7 @@
  * npu_llm/designs/{engine,qwen_engine}.py, their AIE2 kernels
  * npu_llm/kernels/{engine_bf16,qwen_engine_bf16,qwen_engine_hub_bf16}.cc, and the
  * host engines npu_llm/runtime/{engine,qwen_engine}.py.  Python binds it with
- * ctypes (hawkpoint-npu-llm_b200/runtime/hb_lib.py); INTEGRATION.md shows the
- * binding a reference maintainer would add.
+ * ctypes (hawkpoint-npu-llm_b200/runtime/hb_lib.py).
  *
  * Rules: every function returns 0 (HB_OK) or a negative HB_ERR_* code; the
  * message of the last failure is in hb_last_error().  An engine is not
