@@ -17,10 +17,11 @@
 // a word is valid exactly when its epoch is current.  Every (layer, phase)
 // has its own buffer, so no word is rewritten within a launch.
 //
-// A producer warp streams every weight chunk -- and, for phase 2, each row's
-// K/V history -- through the shared-memory ring (hb_stream.cuh) without
-// waiting on activations, so HBM keeps streaming while consumers wait for
-// the previous phase's words.
+// A producer warp streams every weight chunk through the shared-memory ring
+// (hb_stream.cuh) without waiting on activations, so HBM keeps streaming
+// while consumers wait for the previous phase's words.  Phase 2 copies each
+// row's K/V history from the cache (L2) with cp.async while it waits for
+// q/k/v.
 //
 // KV cache layout per (slot, layer, kv head): K [CTX][64] then V [CTX][64],
 // each row of 128 bytes with its eight 16-byte blocks XOR-swizzled by the
@@ -104,10 +105,19 @@ __host__ __device__ inline size_t ll_layer_words(int H, int I, int QKV) {
 }
 
 struct SmemPlan {
-  size_t ring, full, empty, xs, hx, red, qkv, att, misc, total;
+  size_t ring, full, empty, xs, hx, red, qkv, att, kv, misc, total;
 };
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Attention scratch: rotated q (BF16 [QH][72]), the probabilities as three
+// exact BF16 terms ([3][QH][ctx+8]), and per-warp row maxima / sums
+// ([2][kWarps][16] FP32).
+__host__ __device__ inline size_t att_q_bytes(int QH) { return static_cast<size_t>(QH) * (kHeadDim + 8) * 2; }
+__host__ __device__ inline size_t att_p_bytes(int QH, int ctx) { return static_cast<size_t>(3) * QH * (ctx + 8) * 2; }
+__host__ __device__ inline size_t att_bytes(int QH, int ctx) {
+  return att_q_bytes(QH) + att_p_bytes(QH, ctx) + static_cast<size_t>(2) * kWarps * 16 * 4;
+}
 
 __host__ __device__ inline SmemPlan smem_plan(int nslots, int mb, int xs_elems, int H, int QKV,
                                               int QH, int KVH, int red_rows, int ctx) {
@@ -129,7 +139,9 @@ __host__ __device__ inline SmemPlan smem_plan(int nslots, int mb, int xs_elems, 
   s.qkv = o;
   o += align_up(static_cast<size_t>(mb) * QKV * 2, 128);
   s.att = o;
-  o += align_up(static_cast<size_t>(QH * kHeadDim + 2 * KVH * kHeadDim + QH * ctx) * 4, 128);
+  o += align_up(att_bytes(QH, ctx), 128);
+  s.kv = o;  // K/V history of one batch row: [K of kv heads | V of kv heads][ctx][128 B]
+  o += align_up(static_cast<size_t>(2) * KVH * ctx * 128, 128);
   s.misc = o;
   o += 1024;
   s.total = o;
@@ -202,6 +214,7 @@ struct DecoderCta {
   __nv_bfloat16 *xs;
   float *hx, *red, *att;
   uint32_t *qkv_s;
+  uint8_t *kvs;       // K/V history of the current batch row (attention phase)
   int *s_tok, *s_pos, *s_slot, *s_misc;
   float *s_norm;      // [kWarps * kMaxBatch] partial sums, then [kMaxBatch] inverse rms
   float *s_bestv;     // [kWarps * kMaxBatch]
@@ -218,13 +231,12 @@ struct DecoderCta {
     ring.nslots = P.nslots;
     ring.slot = 0;
     ring.parity = 0;
-    ring.timing = P.trace != nullptr;
-    ring.wait_ns = 0;
     xs = reinterpret_cast<__nv_bfloat16 *>(smem + sp.xs);
     hx = reinterpret_cast<float *>(smem + sp.hx);
     red = reinterpret_cast<float *>(smem + sp.red);
     qkv_s = reinterpret_cast<uint32_t *>(smem + sp.qkv);
     att = reinterpret_cast<float *>(smem + sp.att);
+    kvs = smem + sp.kv;
     int *mi = reinterpret_cast<int *>(smem + sp.misc);
     s_tok = mi;
     s_pos = mi + kMaxBatch;
@@ -288,8 +300,8 @@ struct DecoderCta {
   }
 
   // trace point (0 start, 1 inputs ready, 6 prologue (norm / attention)
-  // done, 2 weights consumed, 3 outputs stored; slots 4 and 5 hold the ring
-  // wait and the producer's first issue of the phase)
+  // done, 2 weights consumed, 3 outputs stored; slot 5 holds the producer's
+  // first issue of the phase, slots 4 and 7 are unused)
   __device__ __forceinline__ void mark(int k, int point) const {
     if (P.trace && tid == 0) {
       unsigned long long *t = P.trace + (static_cast<size_t>(cta) * (4 * P.L + 2) + k) * 8;
@@ -298,17 +310,21 @@ struct DecoderCta {
   }
 
   // ---- helpers -------------------------------------------------------------------
-  // Per-thread registers of a norm weight vector (elements tid + 256 j),
-  // loaded before the thread waits for its inputs.
+  // Per-thread registers of a norm weight vector: the thread owns the
+  // hidden-vector words (element pairs) tid + kConsumerThreads * j, the same
+  // words ll_gather hands it, so gather and norm need no barrier between them.
+  static constexpr int kNormWords = kMaxHPerThread / 2;
   struct Gamma {
     float v[kMaxHPerThread];
   };
   __device__ Gamma load_gamma(const float *g) const {
     Gamma r;
 #pragma unroll
-    for (int j = 0; j < kMaxHPerThread; ++j) {
-      const int i = tid + j * kConsumerThreads;
-      r.v[j] = i < P.H ? g[i] : 0.f;
+    for (int j = 0; j < kNormWords; ++j) {
+      const int w = tid + j * kConsumerThreads;
+      const bool in = 2 * w < P.H;
+      r.v[2 * j] = in ? g[2 * w] : 0.f;
+      r.v[2 * j + 1] = in ? g[2 * w + 1] : 0.f;
     }
     return r;
   }
@@ -323,34 +339,42 @@ struct DecoderCta {
     return r;
   }
 
-  // xs[m][i] = bf16((v * inv_rms) * gamma) for v = hx[m][:]  (cpu_backend.py:71-76)
+  // xs[m][i] = bf16((v * inv_rms) * gamma) for v = hx[m][:]  (cpu_backend.py:71-76).
+  // Each thread reads and writes only its own words of hx / xs; the per-warp
+  // sums of squares meet in shared memory and every thread finishes the
+  // mean itself.  Ends with a barrier (xs is read across threads next).
   __device__ void norm_rows(const Gamma &gamma) {
     const int warp = tid >> 5, lane = tid & 31;
     for (int m = 0; m < mrows; ++m) {
-      float s = 0.f;
-      for (int i = tid; i < P.H; i += kConsumerThreads) {
-        const float v = hx[m * P.H + i];
-        s = fmaf(v, v, s);
-      }
-      s = warp_sum(s);
-      if (lane == 0) s_norm[warp * kMaxBatch + m] = s;
-    }
-    consumer_sync(kConsumerThreads);
-    if (tid < mrows) {
-      float total = 0.f;
-      for (int w = 0; w < kWarps; ++w) total += s_norm[w * kMaxBatch + tid];
-      const float mean = __fdiv_rn(total, static_cast<float>(P.H));
-      s_norm[kWarps * kMaxBatch + tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, P.eps)));
-    }
-    consumer_sync(kConsumerThreads);
+      float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < kMaxHPerThread; ++j) {
-      const int i = tid + j * kConsumerThreads;
-      if (i < P.H)
-        for (int m = 0; m < mrows; ++m) {
-          const float inv = s_norm[kWarps * kMaxBatch + m];
-          xs[m * P.xs_elems + i] = f2bf(__fmul_rn(__fmul_rn(hx[m * P.H + i], inv), gamma.v[j]));
+      for (int j = 0; j < kNormWords; ++j) {
+        const int w = tid + j * kConsumerThreads;
+        if (2 * w < P.H) {
+          const float a = hx[m * P.H + 2 * w], b = hx[m * P.H + 2 * w + 1];
+          ss = fmaf(a, a, ss);
+          ss = fmaf(b, b, ss);
         }
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) s_norm[warp * kMaxBatch + m] = ss;
+    }
+    consumer_sync(kConsumerThreads);
+    for (int m = 0; m < mrows; ++m) {
+      float total = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) total += s_norm[w * kMaxBatch + m];
+      const float mean = __fdiv_rn(total, static_cast<float>(P.H));
+      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, P.eps)));
+#pragma unroll
+      for (int j = 0; j < kNormWords; ++j) {
+        const int w = tid + j * kConsumerThreads;
+        if (2 * w < P.H) {
+          const float a = __fmul_rn(__fmul_rn(hx[m * P.H + 2 * w], inv), gamma.v[2 * j]);
+          const float b = __fmul_rn(__fmul_rn(hx[m * P.H + 2 * w + 1], inv), gamma.v[2 * j + 1]);
+          *reinterpret_cast<uint32_t *>(xs + m * P.xs_elems + 2 * w) = pack_bf16x2(a, b);
+        }
+      }
     }
     consumer_sync(kConsumerThreads);
   }
@@ -398,32 +422,25 @@ struct DecoderCta {
   // Attention of every head for batch row m on the tensor cores, reading the
   // K/V history from ring chunks; writes the BF16 output to xs[m][0..QH*64).
   //   S = Q K^T (per kv head: the group's q heads are the A rows, positions
-  //   the N columns), softmax in registers (FP32), O = P V with P split
-  //   exactly into three BF16 terms so the products keep FP32 precision.
+  //   the N columns; the head's warps split the positions), softmax in FP32
+  //   registers with the row maxima and sums exchanged through shared
+  //   memory, O = P V with P split exactly into three BF16 terms so the
+  //   products keep FP32 precision.
   __device__ bool attention_row(int layer, int m, float2 rope0) {
     const int warp = tid >> 5, lane = tid & 31;
     const int p = s_pos[m];
     const int QH = P.QH, KVH = P.KVH, grp = P.group;
     const int qstride = kHeadDim + 8;                    // padded rows: conflict-free fragment loads
-    const int pstride = P.CTX + 4;
     __nv_bfloat16 *qb = reinterpret_cast<__nv_bfloat16 *>(att);       // [QH][72] rotated q
-    float *prob = att + (QH * qstride + 1) / 2;                        // [QH][CTX+4]
     const __nv_bfloat16 *rb = reinterpret_cast<const __nv_bfloat16 *>(qkv_s + static_cast<size_t>(m) * P.QKV / 2);
     // history chunks: K of every kv head, then V of every kv head, in
     // consecutive ring positions
-    const RingPos first{ring.slot, ring.parity};
-    RingPos pos = first;
-    for (int c = 0; c < 2 * KVH; ++c) {
-      if (!ring_wait(ring, pos, &P.result->ctrl, P.limit_ns)) return false;
-      ring_advance(pos, 1, ring.nslots);
-    }
-    ring.slot = pos.slot;
-    ring.parity = pos.parity;
-    auto chunk_ptr = [&](int c) {
-      RingPos q = first;
-      ring_advance(q, c, ring.nslots);
-      return const_cast<uint8_t *>(slot_ptr(ring, q.slot));
-    };
+    // history blocks (K of every kv head, then V) in kvs, copied by
+    // kv_prefetch; this thread's copies land here, everyone's after the
+    // barrier below
+    if (m > 0) kv_prefetch(layer, m);
+    cp_async_wait_all();
+    auto chunk_ptr = [&](int c) { return kvs + static_cast<size_t>(c) * P.CTX * 128; };
     // RoPE (rotate-half, cpu_backend.py:78-93, unfused mul/add) on q -> qb,
     // on k -> row p of the K chunk; v -> row p of the V chunk.
     const int nrot = (QH + KVH) * 32;
@@ -460,27 +477,33 @@ struct DecoderCta {
       *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
     }
     const int g = lane >> 2, t2 = (lane & 3) * 2;
-    const int nks = (p >> 4) + 1;  // 16-position k-steps of P V
-    // S = Q K^T and softmax: one warp per kv head
-    if (warp < KVH) {
-      const int j = warp;
+    const int nks = (p >> 4) + 1;   // 16-position k-steps of P V
+    const int ntiles = 2 * nks;     // 8-position S tiles the k-steps cover
+    const int last_tile = p >> 3;   // tiles past it are all masked
+    // S = Q K^T: kv head j = warp % KVH; its nsub warps split the position
+    // tiles (tile sub + nsub * k).  Scores stay in registers.
+    const int j = warp % KVH, sub = warp / KVH;
+    const int nsub = (kWarps - j + KVH - 1) / KVH;
+    float sc[4][4];  // <= 4 tiles per warp: 8 tiles, >= 2 warps per kv head
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+    {
       const uint32_t kbase = smem_u32(chunk_ptr(j));
       uint32_t a0[4], a2[4], a1[4], a3[4];
       const __nv_bfloat16 *q0 = qb + (j * grp + g) * qstride;
       const __nv_bfloat16 *q1 = qb + (j * grp + g + 8) * qstride;
+      const bool has_s = sub <= last_tile;
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
-        a0[ks] = g < grp ? *reinterpret_cast<const uint32_t *>(q0 + 16 * ks + t2) : 0u;
-        a2[ks] = g < grp ? *reinterpret_cast<const uint32_t *>(q0 + 16 * ks + 8 + t2) : 0u;
-        a1[ks] = g + 8 < grp ? *reinterpret_cast<const uint32_t *>(q1 + 16 * ks + t2) : 0u;
-        a3[ks] = g + 8 < grp ? *reinterpret_cast<const uint32_t *>(q1 + 16 * ks + 8 + t2) : 0u;
+        a0[ks] = has_s && g < grp ? *reinterpret_cast<const uint32_t *>(q0 + 16 * ks + t2) : 0u;
+        a2[ks] = has_s && g < grp ? *reinterpret_cast<const uint32_t *>(q0 + 16 * ks + 8 + t2) : 0u;
+        a1[ks] = has_s && g + 8 < grp ? *reinterpret_cast<const uint32_t *>(q1 + 16 * ks + t2) : 0u;
+        a3[ks] = has_s && g + 8 < grp ? *reinterpret_cast<const uint32_t *>(q1 + 16 * ks + 8 + t2) : 0u;
       }
-      float sc[8][4];
-      float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = -INFINITY;
-        if (nt <= (p >> 3)) {
+      for (int k = 0; k < 4; ++k) {
+        sc[k][0] = sc[k][1] = sc[k][2] = sc[k][3] = -INFINITY;
+        const int nt = sub + nsub * k;
+        if (nt <= last_tile) {
           float d[4] = {0.f, 0.f, 0.f, 0.f};
           const int row = 8 * nt + (lane & 7);
 #pragma unroll
@@ -492,97 +515,142 @@ struct DecoderCta {
           }
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int s = 8 * nt + t2 + (e & 1);
-            sc[nt][e] = s <= p ? d[e] * 0.125f : -INFINITY;
+            const int sp = 8 * nt + t2 + (e & 1);
+            sc[k][e] = sp <= p ? d[e] * 0.125f : -INFINITY;
           }
-          mx0 = fmaxf(mx0, fmaxf(sc[nt][0], sc[nt][1]));
-          mx1 = fmaxf(mx1, fmaxf(sc[nt][2], sc[nt][3]));
+          mx0 = fmaxf(mx0, fmaxf(sc[k][0], sc[k][1]));
+          mx1 = fmaxf(mx1, fmaxf(sc[k][2], sc[k][3]));
         }
       }
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-      float sum0 = 0.f, sum1 = 0.f;
+    }
+    // softmax (cpu_backend.py:95-129: max-subtract, exp, divide by the sum),
+    // maxima and sums exchanged between the nsub warps of a kv head
+    float *pmax = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(att) + att_q_bytes(QH) + att_p_bytes(QH, P.CTX));
+    float *psum = pmax + kWarps * 16;
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    if ((lane & 3) == 0) {
+      pmax[warp * 16 + g] = mx0;
+      pmax[warp * 16 + g + 8] = mx1;
+    }
+    consumer_sync(kConsumerThreads);
+    for (int w2 = j; w2 < kWarps; w2 += KVH) {
+      mx0 = fmaxf(mx0, pmax[w2 * 16 + g]);
+      mx1 = fmaxf(mx1, pmax[w2 * 16 + g + 8]);
+    }
+    float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+    for (int k = 0; k < 4; ++k) {
+      if (sub + nsub * k <= last_tile) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float mx = e < 2 ? mx0 : mx1;
-          const float v = sc[nt][e] == -INFINITY ? 0.f : expf(__fsub_rn(sc[nt][e], mx));
-          sc[nt][e] = v;
+          const float v = sc[k][e] == -INFINITY ? 0.f : expf(__fsub_rn(sc[k][e], e < 2 ? mx0 : mx1));
+          sc[k][e] = v;
           if (e < 2) sum0 += v; else sum1 += v;
         }
       }
-      sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
-      sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
-      sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
-      sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
-      // probabilities of every position the P V k-steps cover (0 past p)
+    }
+    sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
+    sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
+    sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
+    sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
+    if ((lane & 3) == 0) {
+      psum[warp * 16 + g] = sum0;
+      psum[warp * 16 + g + 8] = sum1;
+    }
+    consumer_sync(kConsumerThreads);
+    sum0 = 0.f;
+    sum1 = 0.f;
+    for (int w2 = j; w2 < kWarps; w2 += KVH) {
+      sum0 += psum[w2 * 16 + g];
+      sum1 += psum[w2 * 16 + g + 8];
+    }
+    // probabilities of every position the P V k-steps cover (0 past p), as
+    // hi + mid + lo BF16 terms
+    __nv_bfloat16 *pt = reinterpret_cast<__nv_bfloat16 *>(reinterpret_cast<uint8_t *>(att) + att_q_bytes(QH));
+    const int pst = P.CTX + 8;
+    const size_t pterm = static_cast<size_t>(QH) * pst;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        if (nt < 2 * nks) {
-          if (g < grp) {
-            float *pr = prob + (j * grp + g) * pstride + 8 * nt + t2;
-            pr[0] = __fdiv_rn(sc[nt][0], sum0);
-            pr[1] = __fdiv_rn(sc[nt][1], sum0);
-          }
-          if (g + 8 < grp) {
-            float *pr = prob + (j * grp + g + 8) * pstride + 8 * nt + t2;
-            pr[0] = __fdiv_rn(sc[nt][2], sum1);
-            pr[1] = __fdiv_rn(sc[nt][3], sum1);
+    for (int k = 0; k < 4; ++k) {
+      const int nt = sub + nsub * k;
+      if (nt < ntiles) {
+        const bool live = nt <= last_tile;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = g + 8 * h;
+          if (row < grp) {
+            const float ssum = h ? sum1 : sum0;
+            const float v0 = live ? __fdiv_rn(sc[k][2 * h], ssum) : 0.f;
+            const float v1 = live ? __fdiv_rn(sc[k][2 * h + 1], ssum) : 0.f;
+            uint32_t hi, mid, lo;
+            split3_pack(v0, v1, hi, mid, lo);
+            const size_t o = static_cast<size_t>(j * grp + row) * pst + 8 * nt + t2;
+            *reinterpret_cast<uint32_t *>(pt + o) = hi;
+            *reinterpret_cast<uint32_t *>(pt + pterm + o) = mid;
+            *reinterpret_cast<uint32_t *>(pt + 2 * pterm + o) = lo;
           }
         }
       }
     }
     consumer_sync(kConsumerThreads);
-    // O = P V: work items (kv head j, 8-dim block dn) over all warps
+    // O = P V: work items (kv head jj, 8-dim block dn) over all warps; the
+    // three probability terms accumulate independently
     for (int item = warp; item < KVH * 8; item += kWarps) {
-      const int j = item >> 3, dn = item & 7;
-      const uint32_t vbase = smem_u32(chunk_ptr(KVH + j));
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      const float *pr0 = prob + (j * grp + g) * pstride + t2;
-      const float *pr1 = prob + (j * grp + g + 8) * pstride + t2;
+      const int jj = item >> 3, dn = item & 7;
+      const uint32_t vbase = smem_u32(chunk_ptr(KVH + jj));
+      float dh[4] = {0.f, 0.f, 0.f, 0.f}, dm[4] = {0.f, 0.f, 0.f, 0.f}, dl[4] = {0.f, 0.f, 0.f, 0.f};
+      const bool r0 = g < grp, r1 = g + 8 < grp;
+      const __nv_bfloat16 *pr0 = pt + static_cast<size_t>(jj * grp + g) * pst + t2;
+      const __nv_bfloat16 *pr1 = pt + static_cast<size_t>(jj * grp + g + 8) * pst + t2;
       for (int ks = 0; ks < nks; ++ks) {
         uint32_t b[2];
         ldsm_x2_trans(b, vbase + kv_off(16 * ks + (lane & 15), dn));
-        float v0[4] = {0.f, 0.f, 0.f, 0.f}, v1[4] = {0.f, 0.f, 0.f, 0.f};
-        if (g < grp) {
-          const float2 x = *reinterpret_cast<const float2 *>(pr0 + 16 * ks);
-          const float2 y = *reinterpret_cast<const float2 *>(pr0 + 16 * ks + 8);
-          v0[0] = x.x; v0[1] = x.y; v0[2] = y.x; v0[3] = y.y;
+        uint32_t a[3][4];
+#pragma unroll
+        for (int t = 0; t < 3; ++t) {
+          const size_t to = t * pterm + 16 * ks;
+          a[t][0] = r0 ? *reinterpret_cast<const uint32_t *>(pr0 + to) : 0u;
+          a[t][1] = r1 ? *reinterpret_cast<const uint32_t *>(pr1 + to) : 0u;
+          a[t][2] = r0 ? *reinterpret_cast<const uint32_t *>(pr0 + to + 8) : 0u;
+          a[t][3] = r1 ? *reinterpret_cast<const uint32_t *>(pr1 + to + 8) : 0u;
         }
-        if (g + 8 < grp) {
-          const float2 x = *reinterpret_cast<const float2 *>(pr1 + 16 * ks);
-          const float2 y = *reinterpret_cast<const float2 *>(pr1 + 16 * ks + 8);
-          v1[0] = x.x; v1[1] = x.y; v1[2] = y.x; v1[3] = y.y;
-        }
-        // three BF16 terms per probability: hi + mid + lo == the FP32 value
-        uint32_t ah[4], am[4], al[4];
-        split3_pack(v0[0], v0[1], ah[0], am[0], al[0]);
-        split3_pack(v1[0], v1[1], ah[1], am[1], al[1]);
-        split3_pack(v0[2], v0[3], ah[2], am[2], al[2]);
-        split3_pack(v1[2], v1[3], ah[3], am[3], al[3]);
-        mma_16816_full(d, ah[0], ah[1], ah[2], ah[3], b[0], b[1]);
-        mma_16816_full(d, am[0], am[1], am[2], am[3], b[0], b[1]);
-        mma_16816_full(d, al[0], al[1], al[2], al[3], b[0], b[1]);
+        mma_16816_full(dh, a[0][0], a[0][1], a[0][2], a[0][3], b[0], b[1]);
+        mma_16816_full(dm, a[1][0], a[1][1], a[1][2], a[1][3], b[0], b[1]);
+        mma_16816_full(dl, a[2][0], a[2][1], a[2][2], a[2][3], b[0], b[1]);
       }
+      float d[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) d[e] = dh[e] + (dm[e] + dl[e]);
       __nv_bfloat16 *out = xs + static_cast<size_t>(m) * P.xs_elems;
-      if (g < grp)
-        *reinterpret_cast<uint32_t *>(out + (j * grp + g) * kHeadDim + 8 * dn + t2) = pack_bf16x2(d[0], d[1]);
-      if (g + 8 < grp)
-        *reinterpret_cast<uint32_t *>(out + (j * grp + g + 8) * kHeadDim + 8 * dn + t2) = pack_bf16x2(d[2], d[3]);
+      if (r0)
+        *reinterpret_cast<uint32_t *>(out + (jj * grp + g) * kHeadDim + 8 * dn + t2) = pack_bf16x2(d[0], d[1]);
+      if (r1)
+        *reinterpret_cast<uint32_t *>(out + (jj * grp + g + 8) * kHeadDim + 8 * dn + t2) = pack_bf16x2(d[2], d[3]);
     }
     __syncwarp();
     consumer_sync(kConsumerThreads);
-    if (tid == 0) {
-      RingPos q = first;
-      for (int c = 0; c < 2 * KVH; ++c) {
-        mbar_arrive_count(&ring.empty[q.slot], kWarps);
-        ring_advance(q, 1, ring.nslots);
-      }
-    }
     return true;
+  }
+
+  // Start copying the K/V history of batch row m, layer `layer` (rows of the
+  // k-steps attention covers, all but the current position, which the
+  // attention writes itself) from the cache into kvs.
+  __device__ void kv_prefetch(int layer, int m) {
+    const int p = s_pos[m], slot = s_slot[m];
+    const int per_block = ((p >> 4) + 1) * 16 * 8;  // 16-byte pieces
+    const int total = 2 * P.KVH * per_block;
+    for (int i = tid; i < total; i += kConsumerThreads) {
+      const int c = i / per_block, rem = i - c * per_block;
+      const int row = rem >> 3;
+      if (row == p) continue;
+      const int kind = c < P.KVH ? 0 : 1, j = c < P.KVH ? c : c - P.KVH;
+      const size_t off = static_cast<size_t>(row) * 128 + (rem & 7) * 16;
+      cp_async16(kvs + static_cast<size_t>(c) * P.CTX * 128 + off,
+                 reinterpret_cast<const uint8_t *>(kv_block(slot, layer, j, kind)) + off);
+    }
+    cp_async_commit();
   }
 
   // One phase of a layer (kind = k & 3: 0 qkv, 1 attention + o_proj,
@@ -608,22 +676,29 @@ struct DecoderCta {
     bool ok = true;
     if (kind == 0) {
       if (layer == 0) {
-        for (int idx = tid; idx < mrows * P.H; idx += kConsumerThreads) {
-          const int m = idx / P.H, i = idx - m * P.H;
-          hx[idx] = bf2f(P.embed[static_cast<size_t>(s_tok[m]) * P.H + i]);
+        // the embedding row (generate.py:758-768), same word ownership as the gather
+        for (int m = 0; m < mrows; ++m) {
+          const uint32_t *e = reinterpret_cast<const uint32_t *>(P.embed + static_cast<size_t>(s_tok[m]) * P.H);
+          for (int w = tid; w < P.H / 2; w += kConsumerThreads) {
+            const uint32_t v = __ldg(e + w);
+            hx[m * P.H + 2 * w] = bf_lo(v);
+            hx[m * P.H + 2 * w + 1] = bf_hi(v);
+          }
         }
       } else {
         ok = gather_to_hx(ll_hout(layer - 1, 0), P.H / 2, P.H);
       }
     } else if (kind == 1) {
+      kv_prefetch(layer, 0);  // overlaps the wait for q/k/v
       ok = gather_raw(ll_qkv(layer, 0), P.QKV / 2, P.QKV / 2, qkv_s, P.QKV / 2);
+      if (!ok) cp_async_wait_all();
     } else if (kind == 2) {
       ok = gather_to_hx(ll_h1(layer, 0), P.H / 2, P.H);
     } else {
       ok = gather_raw(ll_act(layer, 0), P.I / 2, P.I / 2, reinterpret_cast<uint32_t *>(xs), P.xs_elems / 2);
     }
     if (!ok) return false;
-    consumer_sync(kConsumerThreads);
+    if (kind == 1 || kind == 3) consumer_sync(kConsumerThreads);  // read across threads next
     mark(k, 1);
     if (kind == 0 || kind == 2) {
       norm_rows(gamma);
@@ -689,7 +764,6 @@ struct DecoderCta {
     const int warp = tid >> 5, lane = tid & 31;
     const Gamma gamma = load_gamma(P.gamma_final);
     if (!gather_to_hx(ll_hout(P.L - 1, 0), P.H / 2, P.H)) return false;
-    consumer_sync(kConsumerThreads);
     norm_rows(gamma);
     float bv[MB];
     int bi[MB];
@@ -771,10 +845,6 @@ struct DecoderCta {
       }
       consumer_sync(kConsumerThreads);
       mark(k, 3);
-      if (P.trace && tid == 0) {
-        P.trace[(static_cast<size_t>(cta) * (4 * P.L + 2) + k) * 8 + 4] = ring.wait_ns;
-        ring.wait_ns = 0;
-      }
     }
     mark(nph - 1, 0);
     // exit protocol: the last CTA finishes the argmax and advances the state
@@ -832,21 +902,9 @@ struct DecoderCta {
   // (attention phases), then the phase's weight row groups.
   __device__ void run_producer() {
     Producer prod{&ring, RingPos{0, 0}, 0, &P.result->ctrl, P.limit_ns, policy_evict_first()};
-    const StepState *st = P.st;
-    const int rows = min(__ldcg(&st->rows), MB);
-    const uint32_t kv_bytes = static_cast<uint32_t>(P.CTX) * kHeadDim * 2;
     bool ok = true;
     for (int k = P.phase_begin; k < P.phase_end && ok; ++k) {
       if (P.trace) P.trace[(static_cast<size_t>(cta) * (4 * P.L + 2) + k) * 8 + 5] = globaltimer_ns();
-      if (k < 4 * P.L && (k & 3) == 1) {
-        for (int m = 0; m < rows && ok; ++m) {
-          const int slot = __ldcg(&st->slot[m]);
-          for (int c = 0; c < 2 * P.KVH && ok; ++c) {
-            const int kind = c < P.KVH ? 0 : 1, j = c < P.KVH ? c : c - P.KVH;
-            ok = prod.issue(reinterpret_cast<const uint8_t *>(kv_block(slot, k >> 2, j, kind)), kv_bytes);
-          }
-        }
-      }
       if (ok) ok = prod.issue_range(phase_range(k));
     }
     prod.drain();

@@ -127,6 +127,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, Ctrl *
   }
 }
 
+// 16-byte asynchronous copy global -> shared (L2 only, no L1 allocation),
+// grouped with cp_async_commit and completed by cp_async_wait_all.
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // Untiled bulk copy global -> shared, completion signalled on `bar`
 // (16-byte aligned addresses, size a multiple of 16).  No multicast.
 __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes,

@@ -126,8 +126,12 @@ int validate_desc(const hb_model_desc *d) {
   const int esize = d->weight_format == HB_WEIGHTS_W8 ? 1 : 2;
   if (d->hidden * esize > 2048)
     return fail(nullptr, HB_ERR_UNSUPPORTED, "hidden too large for one LM-head chunk");
-  if (d->kv_heads > 8 || d->context > 128)
-    return fail(nullptr, HB_ERR_UNSUPPORTED, "kv_heads <= 8 and context <= 128 required");
+  if (d->hidden > hb::kMaxHPerThread * hb::kConsumerThreads)
+    return fail(nullptr, HB_ERR_UNSUPPORTED, "hidden > %d", hb::kMaxHPerThread * hb::kConsumerThreads);
+  // attention: 8-position tiles of a 64-position context, split over at
+  // least two warps per kv head
+  if (d->kv_heads > 4 || d->context > 64)
+    return fail(nullptr, HB_ERR_UNSUPPORTED, "kv_heads <= 4 and context <= 64 required");
   if (d->max_slots <= 0 || d->max_batch <= 0 || d->max_batch > kMaxBatch)
     return fail(nullptr, HB_ERR_INVALID_ARG, "max_slots > 0 and 1 <= max_batch <= 8 required");
   if (!d->layer_offsets || !d->rope_cos || !d->rope_sin)
@@ -161,7 +165,7 @@ int setup_variant(hb_engine *e, Variant &v, int mb, const void *fn, int smem_opt
   int nslots = static_cast<int>((static_cast<size_t>(smem_optin) - base.total - 16 * kMaxSlotsRing) /
                                 hb::kSlotBytes);
   if (nslots > kMaxSlotsRing) nslots = kMaxSlotsRing;
-  if (nslots < kMinSlotsRing || nslots < 2 * d.kv_heads)
+  if (nslots < kMinSlotsRing)
     return fail(e, HB_ERR_UNSUPPORTED, "model too large for the shared-memory plan (batch %d)", mb);
   const hb::SmemPlan sp =
       hb::smem_plan(nslots, mb, e->xs_elems, d.hidden, qkv, d.q_heads, d.kv_heads, e->red_rows, d.context);

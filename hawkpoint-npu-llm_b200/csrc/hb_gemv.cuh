@@ -66,8 +66,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   ring.nslots = P.nslots;
   ring.slot = 0;
   ring.parity = 0;
-  ring.timing = false;
-  ring.wait_ns = 0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < P.nslots; ++i) {

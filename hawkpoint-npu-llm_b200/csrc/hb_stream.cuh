@@ -78,8 +78,6 @@ struct Ring {
   int nslots;
   int slot;          // consumer cursor (identical in every consumer thread)
   uint32_t parity;
-  bool timing;       // accumulate wait_ns (diagnostic traces only)
-  uint64_t wait_ns;
 };
 
 struct RingPos {
@@ -151,11 +149,7 @@ struct Producer {
 
 // Consumer: wait for the chunk at ring position p.
 __device__ __forceinline__ bool ring_wait(Ring &ring, const RingPos &p, Ctrl *ctrl, uint64_t limit_ns) {
-  if (!ring.timing) return mbar_wait(&ring.full[p.slot], p.parity, ctrl, limit_ns, kWhereFull);
-  const uint64_t t0 = globaltimer_ns();
-  const bool ok = mbar_wait(&ring.full[p.slot], p.parity, ctrl, limit_ns, kWhereFull);
-  ring.wait_ns += globaltimer_ns() - t0;
-  return ok;
+  return mbar_wait(&ring.full[p.slot], p.parity, ctrl, limit_ns, kWhereFull);
 }
 
 __device__ __forceinline__ const uint8_t *slot_ptr(const Ring &ring, int slot) {
@@ -236,47 +230,6 @@ __device__ __forceinline__ void mma_group(float (&d)[4], const uint8_t *sg, cons
   }
 }
 
-// Split-K form of mma_group for one warp: at most kPartCols / 32 = 4
-// iterations (chunk columns warp*4 + 32 i); every fragment is loaded before
-// the first MMA and the MMAs alternate two accumulators.
-__device__ __forceinline__ void mma_group_splitk(float (&d)[4], const uint8_t *sg, const __nv_bfloat16 *xrow,
-                                                 int col0, int ncols) {
-  constexpr int U = kPartCols / kColGroups;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t base = smem_u32(sg) + ((lane >> 3) * 128) + ((lane & 7) * 16);
-  const int t2 = (lane & 3) * 2;
-  uint32_t b[U][4], a[U][4];
-#pragma unroll
-  for (int u = 0; u < U; ++u) {
-    const int jc = warp * 4 + u * kColGroups;
-    if (jc < ncols) {
-      ldsm_x4(b[u], base + jc * 128);
-      if (xrow != nullptr) {
-        const __nv_bfloat16 *x = xrow + (col0 + jc) * 8 + t2;
-        a[u][0] = *reinterpret_cast<const uint32_t *>(x);
-        a[u][1] = *reinterpret_cast<const uint32_t *>(x + 8);
-        a[u][2] = *reinterpret_cast<const uint32_t *>(x + 16);
-        a[u][3] = *reinterpret_cast<const uint32_t *>(x + 24);
-      } else {
-        a[u][0] = a[u][1] = a[u][2] = a[u][3] = 0u;
-      }
-    }
-  }
-  float e[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int u = 0; u < U; ++u) {
-    const int jc = warp * 4 + u * kColGroups;
-    if (jc < ncols) {
-      mma_16816(d, a[u][0], a[u][1], b[u][0], b[u][1]);
-      mma_16816(e, a[u][2], a[u][3], b[u][2], b[u][3]);
-    }
-  }
-  d[0] += e[0];
-  d[1] += e[1];
-  d[2] += e[2];
-  d[3] += e[3];
-}
-
 // CUDA-core dot products for W8 (int8 weights, chunk column = 16 weights).
 __device__ __forceinline__ float dot_w8_cols(const uint8_t *sg, const __nv_bfloat16 *x, int col0, int j0,
                                              int jend, int stride) {
@@ -291,8 +244,49 @@ __device__ __forceinline__ float dot_w8_cols(const uint8_t *sg, const __nv_bfloa
   return acc;
 }
 
+// One split-K step of a warp over up to kStepRows row groups that share
+// their columns (whole row groups of several chunks, or the same K-slice of
+// several row groups).  unit[i] = shared address of row group i's first
+// chunk column of the slice + this lane's ldmatrix offset; the warp takes
+// chunk columns warp*4 + kColGroups*u.  The row groups accumulate in
+// independent chains d[i], so one activation fragment feeds nb MMAs and the
+// MMA latency is hidden behind the other chains.
+constexpr int kStepRows = 4;
+
+template <int NR>
+__device__ __forceinline__ void mma_step_rows(float (&d)[kStepRows][4], const uint32_t (&unit)[kStepRows],
+                                              const __nv_bfloat16 *xrow, int col0, int ncols) {
+  for (int jc = (threadIdx.x >> 5) * 4; jc < ncols; jc += kColGroups) {
+    uint32_t b[NR][4];
+#pragma unroll
+    for (int i = 0; i < NR; ++i) ldsm_x4(b[i], unit[i] + jc * 128);
+    uint32_t a0 = 0u, a2 = 0u, c0 = 0u, c2 = 0u;
+    if (xrow != nullptr) {
+      const __nv_bfloat16 *x = xrow + (col0 + jc) * 8;
+      a0 = *reinterpret_cast<const uint32_t *>(x);
+      a2 = *reinterpret_cast<const uint32_t *>(x + 8);
+      c0 = *reinterpret_cast<const uint32_t *>(x + 16);
+      c2 = *reinterpret_cast<const uint32_t *>(x + 24);
+    }
+#pragma unroll
+    for (int i = 0; i < NR; ++i) mma_16816(d[i], a0, a2, b[i][0], b[i][1]);
+#pragma unroll
+    for (int i = 0; i < NR; ++i) mma_16816(d[i], c0, c2, b[i][2], b[i][3]);
+  }
+}
+
+__device__ __forceinline__ void mma_step(float (&d)[kStepRows][4], const uint32_t (&unit)[kStepRows], int nb,
+                                         const __nv_bfloat16 *xrow, int col0, int ncols) {
+  switch (nb) {
+    case 4: mma_step_rows<4>(d, unit, xrow, col0, ncols); break;
+    case 3: mma_step_rows<3>(d, unit, xrow, col0, ncols); break;
+    case 2: mma_step_rows<2>(d, unit, xrow, col0, ncols); break;
+    default: mma_step_rows<1>(d, unit, xrow, col0, ncols); break;
+  }
+}
+
 // Split-K consumption of a row-group range by all consumer warps (latency
-// mode): every warp sees every chunk and takes 1/8 of its columns.  The
+// mode): every warp sees every chunk and takes 1/kWarps of its columns.  The
 // per-warp partial of (batch row m, local row) goes to
 // red[(warp * MB + m) * red_rows + local_row]; the caller sums the warps
 // after a consumer_sync.  xs: BF16 activations [MB][K] in shared memory.
@@ -301,36 +295,114 @@ __device__ __forceinline__ bool consume_splitk(Ring &ring, const MatRange &r, co
                                                int mrows, float *red, int red_rows, Ctrl *ctrl,
                                                uint64_t limit_ns) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float d[4] = {0.f, 0.f, 0.f, 0.f};   // BF16 path: D fragment of the current group
-  float acc[MB];                        // W8 path
+  if (r.base == nullptr || r.g1 <= r.g0) return true;
+  if constexpr (!W8) {
+    const int am = lane >> 2, n = (lane & 3) * 2;
+    const __nv_bfloat16 *xrow = am < mrows ? xs + static_cast<size_t>(am) * K + n : nullptr;
+    const uint32_t lane_off = ((lane >> 3) * 128) + ((lane & 7) * 16);
+    const int rgb = r.kc * 128;
+    float d[kStepRows][4];
+    uint32_t unit[kStepRows];
+    RingPos pos{ring.slot, ring.parity};
 #pragma unroll
-  for (int m = 0; m < MB; ++m) acc[m] = 0.f;
-  RingPos pos{ring.slot, ring.parity};
-  const bool ok = for_each_chunk(r, [&](int g, int nrg, int col0, int ncols, bool last) {
-    if (!ring_wait(ring, pos, ctrl, limit_ns)) return false;
-    const uint8_t *s = slot_ptr(ring, pos.slot);
-    for (int q = 0; q < nrg; ++q) {
-      const uint8_t *sg = s + static_cast<size_t>(q) * ncols * 128;
-      if (!W8) {
-        const int m = lane >> 2;
-        const __nv_bfloat16 *xrow = m < mrows ? xs + static_cast<size_t>(m) * K : nullptr;
-        mma_group(d, sg, xrow, col0, warp * 4, ncols, kWarps * 4);
-      } else {
+    for (int i = 0; i < kStepRows; ++i) d[i][0] = d[i][1] = d[i][2] = d[i][3] = 0.f;
+    // wait for the n (<= kStepRows) chunks from the cursor on
+    auto wait_chunks = [&](int n) {
+      RingPos p = pos;
+      bool ok = true;
+#pragma unroll
+      for (int c = 0; c < kStepRows; ++c) {
+        if (c < n) {
+          ok = ok && ring_wait(ring, p, ctrl, limit_ns);
+          unit[c] = smem_u32(slot_ptr(ring, p.slot)) + lane_off;
+          ring_advance(p, 1, ring.nslots);
+        }
+      }
+      return ok;
+    };
+    // hand the n chunks at the cursor back to the producer, one lane each
+    auto release_chunks = [&](int n) {
+      __syncwarp();
+      if (lane < n) {
+        int sl = pos.slot + lane;
+        if (sl >= ring.nslots) sl -= ring.nslots;
+        mbar_arrive_count(&ring.empty[sl], 1);
+      }
+      ring_advance(pos, n, ring.nslots);
+    };
+    // row groups g..g+nb-1 are complete
+    auto flush = [&](int g, int nb) {
+#pragma unroll
+      for (int i = 0; i < kStepRows; ++i) {
+        if (i < nb && am < mrows) {
+          float *o = red + (warp * MB + am) * red_rows + (g + i - r.g0) * 8 + n;
+          o[0] = d[i][0];
+          o[1] = d[i][1];
+        }
+        d[i][0] = d[i][1] = d[i][2] = d[i][3] = 0.f;
+      }
+    };
+    if (rgb > static_cast<int>(kSlotBytes) || r.g1 - r.g0 == 1) {
+      // one row group (or K-slices of row groups): chunk by chunk, one
+      // accumulator chain per warp
+      const __nv_bfloat16 *xr = am < mrows ? xs + static_cast<size_t>(am) * K : nullptr;
+      const bool ok = for_each_chunk(r, [&](int g, int nrg, int col0, int ncols, bool last) {
+        if (!ring_wait(ring, pos, ctrl, limit_ns)) return false;
+        const uint8_t *sc = slot_ptr(ring, pos.slot);
+        for (int q = 0; q < nrg; ++q) {
+          mma_group(d[0], sc + static_cast<size_t>(q) * ncols * 128, xr, col0, warp * 4, ncols, kColGroups);
+          if (last) flush(g + q, 1);
+        }
+        release_chunks(1);
+        return true;
+      });
+      if (!ok) return false;
+    } else if (2 * rgb > static_cast<int>(kSlotBytes)) {
+      // one row group per chunk: up to kStepRows chunks per step
+      for (int g = r.g0; g < r.g1; g += kStepRows) {
+        const int nb = min(kStepRows, r.g1 - g);
+        if (!wait_chunks(nb)) return false;
+        mma_step(d, unit, nb, xrow, 0, r.kc);
+        flush(g, nb);
+        release_chunks(nb);
+      }
+    } else {
+      // several row groups per chunk, kStepRows at a time
+      const int rpc = static_cast<int>(kSlotBytes) / rgb;
+      for (int g = r.g0; g < r.g1;) {
+        if (!wait_chunks(1)) return false;
+        const uint32_t cbase = unit[0];
+        const int take = min(rpc, r.g1 - g);
+        for (int t0 = 0; t0 < take; t0 += kStepRows) {
+#pragma unroll
+          for (int i = 0; i < kStepRows; ++i) unit[i] = cbase + (t0 + i) * rgb;
+          const int nb = min(kStepRows, take - t0);
+          mma_step(d, unit, nb, xrow, 0, r.kc);
+          flush(g + t0, nb);
+        }
+        release_chunks(1);
+        g += take;
+      }
+    }
+    ring.slot = pos.slot;
+    ring.parity = pos.parity;
+    return true;
+  } else {
+    float acc[MB];
+#pragma unroll
+    for (int m = 0; m < MB; ++m) acc[m] = 0.f;
+    RingPos pos{ring.slot, ring.parity};
+    const bool ok = for_each_chunk(r, [&](int g, int nrg, int col0, int ncols, bool last) {
+      if (!ring_wait(ring, pos, ctrl, limit_ns)) return false;
+      const uint8_t *s = slot_ptr(ring, pos.slot);
+      for (int q = 0; q < nrg; ++q) {
+        const uint8_t *sg = s + static_cast<size_t>(q) * ncols * 128;
         const int cg = warp * 4 + (lane >> 3);
 #pragma unroll
         for (int m = 0; m < MB; ++m)
           if (m < mrows) acc[m] += dot_w8_cols(sg, xs + static_cast<size_t>(m) * K, col0, cg, ncols, kColGroups);
-      }
-      if (last) {
-        const int local = (g + q - r.g0) * 8;
-        if (!W8) {
-          const int m = lane >> 2, n = (lane & 3) * 2;
-          if (m < mrows) {
-            red[(warp * MB + m) * red_rows + local + n] = d[0];
-            red[(warp * MB + m) * red_rows + local + n + 1] = d[1];
-          }
-          d[0] = d[1] = d[2] = d[3] = 0.f;
-        } else {
+        if (last) {
+          const int local = (g + q - r.g0) * 8;
 #pragma unroll
           for (int m = 0; m < MB; ++m) {
             float v = acc[m];
@@ -341,61 +413,15 @@ __device__ __forceinline__ bool consume_splitk(Ring &ring, const MatRange &r, co
           }
         }
       }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive_count(&ring.empty[pos.slot], 1);
-    ring_advance(pos, 1, ring.nslots);
-    return true;
-  });
-  ring.slot = pos.slot;
-  ring.parity = pos.parity;
-  return ok;
-}
-
-// Row-group-per-warp consumption (small K, several groups per chunk).
-// on_row(m, row, value) receives every dot product.
-template <int MB, bool W8, class F>
-__device__ __forceinline__ bool consume_rg_per_warp(Ring &ring, const MatRange &r, const __nv_bfloat16 *xs,
-                                                    int K, int mrows, Ctrl *ctrl, uint64_t limit_ns,
-                                                    F &&on_row) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  RingPos pos{ring.slot, ring.parity};
-  const bool ok = for_each_chunk(r, [&](int g, int nrg, int col0, int ncols, bool) {
-    if (!ring_wait(ring, pos, ctrl, limit_ns)) return false;
-    const uint8_t *s = slot_ptr(ring, pos.slot);
-    for (int q = warp; q < nrg; q += kWarps) {
-      const uint8_t *sg = s + static_cast<size_t>(q) * ncols * 128;
-      if (!W8) {
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
-        const int m = lane >> 2;
-        mma_group(d, sg, m < mrows ? xs + static_cast<size_t>(m) * K : nullptr, col0, 0, ncols, 4);
-#pragma unroll
-        for (int mm = 0; mm < MB; ++mm) {
-          if (mm == m && m < mrows) {  // compile-time batch index for the callback
-            on_row(mm, (g + q) * 8 + (lane & 3) * 2, d[0]);
-            on_row(mm, (g + q) * 8 + (lane & 3) * 2 + 1, d[1]);
-          }
-        }
-      } else {
-#pragma unroll
-        for (int m = 0; m < MB; ++m) {
-          if (m < mrows) {
-            float v = dot_w8_cols(sg, xs + static_cast<size_t>(m) * K, col0, lane >> 3, ncols, 4);
-            v += __shfl_xor_sync(0xffffffffu, v, 8);
-            v += __shfl_xor_sync(0xffffffffu, v, 16);
-            if (lane < 8) on_row(m, (g + q) * 8 + lane, v);
-          }
-        }
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive_count(&ring.empty[pos.slot], 1);
-    ring_advance(pos, 1, ring.nslots);
-    return true;
-  });
-  ring.slot = pos.slot;
-  ring.parity = pos.parity;
-  return ok;
+      __syncwarp();
+      if (lane == 0) mbar_arrive_count(&ring.empty[pos.slot], 1);
+      ring_advance(pos, 1, ring.nslots);
+      return true;
+    });
+    ring.slot = pos.slot;
+    ring.parity = pos.parity;
+    return ok;
+  }
 }
 
 // Chunk-per-warp consumption (throughput mode, whole row groups per chunk):

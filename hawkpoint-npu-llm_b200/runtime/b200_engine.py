@@ -203,8 +203,8 @@ class B200DecoderEngine:
     def phase_trace(self):
         """globaltimer stamps [G, 4L+2, 8] of the last launch traced with
         profile(trace=True): per phase its start, inputs ready, weights
-        consumed, outputs stored, ring wait total (ns), producer's first
-        issue of the phase, prologue (norm / attention) done."""
+        consumed, outputs stored, (unused), producer's first issue of the
+        phase, prologue (norm / attention) done, (unused)."""
         g = self._lib.hb_device_sm_count(0)
         out = np.zeros((g, 4 * self.layers + 2, 8), np.uint64)
         self._check(self._lib.hb_debug_dump(self._live(), hb_lib.HB_DUMP_TRACE, out.ctypes.data, out.nbytes))
