@@ -92,6 +92,79 @@ def max_over_ranks(value, world):
     return float(t.item())
 
 
+def sum_over_ranks(value, world):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def config5_requests(vocab, n=512, new_tokens=16, seed=MODEL_SEED + 5):
+    """8 x 64 independent requests, prompt lengths U[8, 48],
+    every fourth request opening with one shared 16-token prefix, 16 greedy
+    tokens each (seeded ids stand in for real prompts)."""
+    import numpy as np
+    from runtime.serving import Request
+
+    rng = np.random.default_rng(seed)
+    shared = rng.integers(0, vocab, 16).tolist()
+    reqs = []
+    for i in range(n):
+        length = int(rng.integers(8, 49))
+        ids = rng.integers(0, vocab, length).tolist()
+        if i % 4 == 0:
+            ids = shared + ids[: max(1, length - 16)]
+        reqs.append(Request(prompt=ids, new_tokens=new_tokens, rid=i))
+    return reqs
+
+
+def run_multistream(model, blob, device, rank, world):
+    """Config 5 on this rank's shard: continuous batching of 8 streams per
+    launch, shared prefixes reused from the KV prefix pool."""
+    import numpy as np
+    import torch
+    from runtime import dispatch
+    from runtime.b200_engine import B200DecoderEngine
+    from runtime.serving import MultiStreamServer, Request
+
+    everything = config5_requests(model.shape.vocab)
+    mine = dispatch.shard([r.prompt for r in everything], rank, world, 16)
+    engine = B200DecoderEngine(model, device=device, blob=blob, max_slots=12, max_batch=8)
+    try:
+        warm = [Request(prompt=everything[i].prompt, new_tokens=4) for i in mine[:8]]
+        MultiStreamServer(engine).run(warm)
+        reqs = [Request(prompt=everything[i].prompt, new_tokens=everything[i].new_tokens, rid=i) for i in mine]
+        server = MultiStreamServer(engine)
+        torch.cuda.synchronize()
+        barrier(world)
+        engine.profile(True)
+        engine.profile_read()
+        t0 = time.perf_counter()
+        server.run(reqs)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        device_s = float(engine.profile_read().sum()) / 1000.0
+        engine.profile(False)
+    finally:
+        engine.close()
+    tokens = sum(len(r.tokens) for r in reqs)
+    all_tokens = sum_over_ranks(float(tokens), world)
+    t_max = max_over_ranks(wall, world)
+    d_max = max_over_ranks(device_s, world)
+    return {
+        "workload": "config 5: 512 requests, prompts U[8,48], 25% share a 16-token prefix, 16 greedy tokens",
+        "requests": len(everything), "requests_this_rank": len(reqs), "batch": 8,
+        "value": all_tokens / t_max, "unit": "tokens/s", "device_value": all_tokens / d_max,
+        "p50_ttft_ms": 1000 * float(np.median([r.ttft for r in reqs])),
+        "launches_rank0": server.launches, "rows_rank0": server.rows,
+        "prefix_reuses_rank0": sum(1 for r in reqs if r.reused_prefix),
+    }
+
+
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
@@ -330,6 +403,8 @@ def run_b200(args, rank, world, local):
     e2e_value = decode_steps * args.steps * world / e2e_t
     decoder.close()
 
+    multistream = run_multistream(model, blob, device, rank, world)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, _, sample = oracle_sample(model, prompt, 2, 8)
@@ -357,6 +432,7 @@ def run_b200(args, rank, world, local):
                     "h2d_bytes_per_step": launches_per_step * step_state_bytes,
                     "d2h_bytes_per_step": launches_per_step * result_bytes},
             "gpu_launches": launches_per_step * args.steps,
+            "multistream": multistream,
             "clocks": clocks.summary(),
         }
         if cpu is not None:

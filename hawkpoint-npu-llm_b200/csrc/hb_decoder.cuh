@@ -3,8 +3,8 @@
 // One cooperative launch (one CTA per SM, all co-resident) runs a range of
 // phases of one decode step for up to MB batch rows.  Per layer l:
 //   1 (4l+0)  x = rmsnorm(h) ; qkv = bf16(bf16(Wqkv x) + bias)       (cpu_backend.py:131-143)
-//   2 (4l+1)  RoPE on q,k ; append k,v to the KV cache ; GQA attention over
-//             every head ; h1 = bf16(bf16(Wo a) + h)                   (cpu_backend.py:78-151)
+//   2 (4l+1)  RoPE on q,k ; append k,v to the KV cache ; GQA attention, one
+//             (row, head) per CTA ; h1 = bf16(bf16(Wo a) + h)            (cpu_backend.py:78-151)
 //   3 (4l+2)  x2 = rmsnorm(h1) ; act = bf16(silu(bf16 gate) * bf16 up) (cpu_backend.py:152-165)
 //   4 (4l+3)  h' = bf16(bf16(Wdown act) + h1)                           (cpu_backend.py:166-171)
 // and after the last layer
@@ -19,9 +19,11 @@
 //
 // A producer warp streams every weight chunk through the shared-memory ring
 // (hb_stream.cuh) without waiting on activations, so HBM keeps streaming
-// while consumers wait for the previous phase's words.  Phase 2 copies each
-// row's K/V history from the cache (L2) with cp.async while it waits for
-// q/k/v.
+// while consumers wait for the previous phase's words.  Phase 2 splits the
+// attention into (batch row, q head) units, one per CTA: the unit copies its
+// K/V history from the cache (L2) with cp.async while it waits for q/k/v,
+// publishes its 64 outputs as LL words, and every CTA gathers all heads for
+// the o-projection.
 //
 // KV cache layout per (slot, layer, kv head): K [CTX][64] then V [CTX][64],
 // each row of 128 bytes with its eight 16-byte blocks XOR-swizzled by the
@@ -99,25 +101,21 @@ struct DecParams {
   unsigned long long *trace;         // optional [G][4L+2][4] phase timestamps
 };
 
-// LL buffer layout: per layer a block of kMaxBatch rows of each kind.
+// LL buffer layout: per layer a block of kMaxBatch rows of each kind
+// (q/k/v, h1, act, h_out, attention output).
 __host__ __device__ inline size_t ll_layer_words(int H, int I, int QKV) {
-  return static_cast<size_t>(kMaxBatch) * (QKV + 2 * H + I) / 2;
+  return static_cast<size_t>(kMaxBatch) * (QKV + 3 * H + I) / 2;
 }
 
 struct SmemPlan {
-  size_t ring, full, empty, xs, hx, red, qkv, att, kv, misc, total;
+  size_t ring, full, empty, xs, hx, red, att, kv, misc, total;
 };
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Attention scratch: rotated q (BF16 [QH][72]), the probabilities as three
-// exact BF16 terms ([3][QH][ctx+8]), and per-warp row maxima / sums
-// ([2][kWarps][16] FP32).
-__host__ __device__ inline size_t att_q_bytes(int QH) { return static_cast<size_t>(QH) * (kHeadDim + 8) * 2; }
-__host__ __device__ inline size_t att_p_bytes(int QH, int ctx) { return static_cast<size_t>(3) * QH * (ctx + 8) * 2; }
-__host__ __device__ inline size_t att_bytes(int QH, int ctx) {
-  return att_q_bytes(QH) + att_p_bytes(QH, ctx) + static_cast<size_t>(2) * kWarps * 16 * 4;
-}
+// Attention scratch of one (row, head) unit: its q/k/v words [96], rotated
+// q [64], scores / probabilities [64], P.V partial sums [4][64] (FP32).
+__host__ __device__ inline size_t att_bytes(int /*QH*/, int /*ctx*/) { return 2048; }
 
 __host__ __device__ inline SmemPlan smem_plan(int nslots, int mb, int xs_elems, int H, int QKV,
                                               int QH, int KVH, int red_rows, int ctx) {
@@ -130,18 +128,21 @@ __host__ __device__ inline SmemPlan smem_plan(int nslots, int mb, int xs_elems, 
   s.empty = o;
   o += 8 * nslots;
   o = align_up(o, 128);
-  s.xs = o;
+  s.xs = o;  // xs[m] = BF16 GEMV input of row m
   o += align_up(static_cast<size_t>(mb) * xs_elems * 2, 128);
+  // hx[m] = BF16 residual row (the phase's norm input / residual)
   s.hx = o;
-  o += align_up(static_cast<size_t>(mb) * H * 4, 128);
+  o += align_up(static_cast<size_t>(mb) * H * 2, 128);
+  // attention scratch and the split-K partials share one region: attention
+  // ends (barrier) before the phase's GEMV writes partials, and the next
+  // attention starts after the previous phase's epilogue read them
+  const size_t red_bytes = align_up(static_cast<size_t>(kWarps) * mb * red_rows * 4, 128);
+  const size_t att_b = align_up(att_bytes(QH, ctx), 128);
+  const size_t kv_b = align_up(static_cast<size_t>(2) * ctx * 128, 128);
   s.red = o;
-  o += align_up(static_cast<size_t>(kWarps) * mb * red_rows * 4, 128);
-  s.qkv = o;
-  o += align_up(static_cast<size_t>(mb) * QKV * 2, 128);
   s.att = o;
-  o += align_up(att_bytes(QH, ctx), 128);
-  s.kv = o;  // K/V history of one batch row: [K of kv heads | V of kv heads][ctx][128 B]
-  o += align_up(static_cast<size_t>(2) * KVH * ctx * 128, 128);
+  s.kv = o + att_b;  // K then V history of one (row, kv head): [2][ctx][128 B]
+  o += red_bytes > att_b + kv_b ? red_bytes : att_b + kv_b;
   s.misc = o;
   o += 1024;
   s.total = o;
@@ -169,26 +170,39 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // All consumer threads: wait until words [0, n) of src carry `epoch`, and
 // pass each payload to sink(i, payload).  Up to 8 loads in flight per thread.
 template <class Sink>
-__device__ __forceinline__ bool ll_gather(const uint64_t *src, int n, uint32_t epoch, Ctrl *ctrl,
-                                          uint64_t limit_ns, Sink &&sink) {
+__device__ __forceinline__ bool ll_gather(const uint64_t *src, size_t row_words, int words, int rows,
+                                          uint32_t epoch, Ctrl *ctrl, uint64_t limit_ns, Sink &&sink) {
+  // Word i of row m (at src + m * row_words + i) goes to thread i % 256 for
+  // every row, so a thread owns the same columns of each row; all rows are
+  // polled together, up to U words per thread in flight.
   const int tid = threadIdx.x;
   constexpr int U = 8;
-  for (int base = tid; base < n; base += kConsumerThreads * U) {
+  const int per_row = (words + kConsumerThreads - 1) / kConsumerThreads;  // words per thread and row
+  const int total = rows * per_row;
+  for (int base = 0; base < total; base += U) {
     uint32_t pend = 0;
+    const uint64_t *addr[U];
+    int col[U], row[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u)
-      if (base + u * kConsumerThreads < n) pend |= 1u << u;
+    for (int u = 0; u < U; ++u) {
+      const int e = base + u;
+      const int m = e / per_row, k = e - m * per_row;
+      row[u] = m;
+      col[u] = tid + k * kConsumerThreads;
+      addr[u] = src + m * row_words + col[u];
+      if (e < total && col[u] < words) pend |= 1u << u;
+    }
     uint64_t start = 0;
     uint32_t spins = 0;
     while (pend) {
       uint64_t v[U];
 #pragma unroll
       for (int u = 0; u < U; ++u)
-        if (pend & (1u << u)) v[u] = ll_load(src + base + u * kConsumerThreads);
+        if (pend & (1u << u)) v[u] = ll_load(addr[u]);
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         if ((pend & (1u << u)) && static_cast<uint32_t>(v[u] >> 32) == epoch) {
-          sink(base + u * kConsumerThreads, static_cast<uint32_t>(v[u]));
+          sink(row[u], col[u], static_cast<uint32_t>(v[u]));
           pend &= ~(1u << u);
         }
       }
@@ -212,8 +226,8 @@ struct DecoderCta {
   const DecParams &P;
   Ring ring;
   __nv_bfloat16 *xs;
-  float *hx, *red, *att;
-  uint32_t *qkv_s;
+  __nv_bfloat16 *hx;  // BF16 residual rows [MB][H]
+  float *red, *att;
   uint8_t *kvs;       // K/V history of the current batch row (attention phase)
   int *s_tok, *s_pos, *s_slot, *s_misc;
   float *s_norm;      // [kWarps * kMaxBatch] partial sums, then [kMaxBatch] inverse rms
@@ -232,9 +246,8 @@ struct DecoderCta {
     ring.slot = 0;
     ring.parity = 0;
     xs = reinterpret_cast<__nv_bfloat16 *>(smem + sp.xs);
-    hx = reinterpret_cast<float *>(smem + sp.hx);
+    hx = reinterpret_cast<__nv_bfloat16 *>(smem + sp.hx);
     red = reinterpret_cast<float *>(smem + sp.red);
-    qkv_s = reinterpret_cast<uint32_t *>(smem + sp.qkv);
     att = reinterpret_cast<float *>(smem + sp.att);
     kvs = smem + sp.kv;
     int *mi = reinterpret_cast<int *>(smem + sp.misc);
@@ -263,6 +276,10 @@ struct DecoderCta {
   }
   __device__ uint64_t *ll_hout(int l, int m) const {
     return P.ll + l * lw + static_cast<size_t>(kMaxBatch) * (P.QKV + P.H + P.I) / 2 +
+           static_cast<size_t>(m) * P.H / 2;
+  }
+  __device__ uint64_t *ll_att(int l, int m) const {
+    return P.ll + l * lw + static_cast<size_t>(kMaxBatch) * (P.QKV + 2 * P.H + P.I) / 2 +
            static_cast<size_t>(m) * P.H / 2;
   }
 
@@ -351,7 +368,8 @@ struct DecoderCta {
       for (int j = 0; j < kNormWords; ++j) {
         const int w = tid + j * kConsumerThreads;
         if (2 * w < P.H) {
-          const float a = hx[m * P.H + 2 * w], b = hx[m * P.H + 2 * w + 1];
+          const uint32_t hw = reinterpret_cast<const uint32_t *>(hx + m * P.H)[w];
+          const float a = bf_lo(hw), b = bf_hi(hw);
           ss = fmaf(a, a, ss);
           ss = fmaf(b, b, ss);
         }
@@ -370,8 +388,9 @@ struct DecoderCta {
       for (int j = 0; j < kNormWords; ++j) {
         const int w = tid + j * kConsumerThreads;
         if (2 * w < P.H) {
-          const float a = __fmul_rn(__fmul_rn(hx[m * P.H + 2 * w], inv), gamma.v[2 * j]);
-          const float b = __fmul_rn(__fmul_rn(hx[m * P.H + 2 * w + 1], inv), gamma.v[2 * j + 1]);
+          const uint32_t hw = reinterpret_cast<const uint32_t *>(hx + m * P.H)[w];
+          const float a = __fmul_rn(__fmul_rn(bf_lo(hw), inv), gamma.v[2 * j]);
+          const float b = __fmul_rn(__fmul_rn(bf_hi(hw), inv), gamma.v[2 * j + 1]);
           *reinterpret_cast<uint32_t *>(xs + m * P.xs_elems + 2 * w) = pack_bf16x2(a, b);
         }
       }
@@ -386,31 +405,17 @@ struct DecoderCta {
     return v;
   }
 
-  // hx[m][:] = f32 of the BF16 vector in the LL words at src (row m at
+  // hx[m][:] = the BF16 vector in the LL words at src (row m at
   // src + m * row_words).
   __device__ bool gather_to_hx(const uint64_t *src, size_t row_words, int nvals) {
-    for (int m = 0; m < mrows; ++m) {
-      float *dst = hx + m * P.H;
-      if (!ll_gather(src + m * row_words, nvals / 2, epoch, &P.result->ctrl, P.limit_ns,
-                     [&](int i, uint32_t d) {
-                       dst[2 * i] = bf_lo(d);
-                       dst[2 * i + 1] = bf_hi(d);
-                     }))
-        return false;
-    }
-    return true;
+    return gather_raw(src, row_words, nvals / 2, reinterpret_cast<uint32_t *>(hx), P.H / 2);
   }
 
   // Raw payloads of the LL words (BF16 pairs) into dst[m * dst_words + i].
   __device__ bool gather_raw(const uint64_t *src, size_t row_words, int words, uint32_t *dst,
                                           size_t dst_words) {
-    for (int m = 0; m < mrows; ++m) {
-      uint32_t *out = dst + m * dst_words;
-      if (!ll_gather(src + m * row_words, words, epoch, &P.result->ctrl, P.limit_ns,
-                     [&](int i, uint32_t d) { out[i] = d; }))
-        return false;
-    }
-    return true;
+    return ll_gather(src, row_words, words, mrows, epoch, &P.result->ctrl, P.limit_ns,
+                     [&](int m, int i, uint32_t d) { dst[m * dst_words + i] = d; });
   }
 
   // ---- phases -------------------------------------------------------------------
@@ -419,238 +424,150 @@ struct DecoderCta {
   // an ldmatrix reads fall in distinct banks.
   __device__ __forceinline__ static int kv_off(int s, int cb) { return s * 128 + ((cb ^ (s & 7)) << 4); }
 
-  // Attention of every head for batch row m on the tensor cores, reading the
-  // K/V history from ring chunks; writes the BF16 output to xs[m][0..QH*64).
-  //   S = Q K^T (per kv head: the group's q heads are the A rows, positions
-  //   the N columns; the head's warps split the positions), softmax in FP32
-  //   registers with the row maxima and sums exchanged through shared
-  //   memory, O = P V with P split exactly into three BF16 terms so the
-  //   products keep FP32 precision.
-  __device__ bool attention_row(int layer, int m, float2 rope0) {
-    const int warp = tid >> 5, lane = tid & 31;
-    const int p = s_pos[m];
-    const int QH = P.QH, KVH = P.KVH, grp = P.group;
-    const int qstride = kHeadDim + 8;                    // padded rows: conflict-free fragment loads
-    __nv_bfloat16 *qb = reinterpret_cast<__nv_bfloat16 *>(att);       // [QH][72] rotated q
-    const __nv_bfloat16 *rb = reinterpret_cast<const __nv_bfloat16 *>(qkv_s + static_cast<size_t>(m) * P.QKV / 2);
-    // history chunks: K of every kv head, then V of every kv head, in
-    // consecutive ring positions
-    // history blocks (K of every kv head, then V) in kvs, copied by
-    // kv_prefetch; this thread's copies land here, everyone's after the
-    // barrier below
-    if (m > 0) kv_prefetch(layer, m);
-    cp_async_wait_all();
-    auto chunk_ptr = [&](int c) { return kvs + static_cast<size_t>(c) * P.CTX * 128; };
-    // RoPE (rotate-half, cpu_backend.py:78-93, unfused mul/add) on q -> qb,
-    // on k -> row p of the K chunk; v -> row p of the V chunk.
-    const int nrot = (QH + KVH) * 32;
-    for (int idx = tid; idx < nrot + KVH * 32; idx += kConsumerThreads) {
-      const int hh = idx >> 5, d = idx & 31;
-      if (idx < nrot) {
-        const float x0 = bf2f(rb[hh * kHeadDim + d]), x1 = bf2f(rb[hh * kHeadDim + d + 32]);
-        const float c = m == 0 ? rope0.x : P.rope_cos[p * 32 + d];
-        const float sn = m == 0 ? rope0.y : P.rope_sin[p * 32 + d];
-        const __nv_bfloat16 lo = f2bf(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
-        const __nv_bfloat16 hi = f2bf(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
-        if (hh < QH) {
-          qb[hh * qstride + d] = lo;
-          qb[hh * qstride + d + 32] = hi;
-        } else {
-          uint8_t *kc = chunk_ptr(hh - QH);
-          *reinterpret_cast<__nv_bfloat16 *>(kc + kv_off(p, d >> 3) + (d & 7) * 2) = lo;
-          *reinterpret_cast<__nv_bfloat16 *>(kc + kv_off(p, 4 + (d >> 3)) + (d & 7) * 2) = hi;
-        }
-      } else {
-        const int j = hh - QH - KVH;
-        uint8_t *vc = chunk_ptr(KVH + j);
-        const int base = (QH + KVH + j) * kHeadDim;
-        *reinterpret_cast<__nv_bfloat16 *>(vc + kv_off(p, d >> 3) + (d & 7) * 2) = rb[base + d];
-        *reinterpret_cast<__nv_bfloat16 *>(vc + kv_off(p, 4 + (d >> 3)) + (d & 7) * 2) = rb[base + d + 32];
-      }
-    }
-    consumer_sync(kConsumerThreads);
-    // CTA j appends kv head j of this position to the cache.
-    if (cta < KVH && tid < 16) {
-      const int j = cta, kind = tid >> 3, cb = tid & 7;
-      const uint8_t *src = chunk_ptr(kind * KVH + j) + kv_off(p, cb);
-      uint8_t *dst = reinterpret_cast<uint8_t *>(kv_block(s_slot[m], layer, j, kind)) + kv_off(p, cb);
-      *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
-    }
-    const int g = lane >> 2, t2 = (lane & 3) * 2;
-    const int nks = (p >> 4) + 1;   // 16-position k-steps of P V
-    const int ntiles = 2 * nks;     // 8-position S tiles the k-steps cover
-    const int last_tile = p >> 3;   // tiles past it are all masked
-    // S = Q K^T: kv head j = warp % KVH; its nsub warps split the position
-    // tiles (tile sub + nsub * k).  Scores stay in registers.
-    const int j = warp % KVH, sub = warp / KVH;
-    const int nsub = (kWarps - j + KVH - 1) / KVH;
-    float sc[4][4];  // <= 4 tiles per warp: 8 tiles, >= 2 warps per kv head
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-    {
-      const uint32_t kbase = smem_u32(chunk_ptr(j));
-      uint32_t a0[4], a2[4], a1[4], a3[4];
-      const __nv_bfloat16 *q0 = qb + (j * grp + g) * qstride;
-      const __nv_bfloat16 *q1 = qb + (j * grp + g + 8) * qstride;
-      const bool has_s = sub <= last_tile;
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        a0[ks] = has_s && g < grp ? *reinterpret_cast<const uint32_t *>(q0 + 16 * ks + t2) : 0u;
-        a2[ks] = has_s && g < grp ? *reinterpret_cast<const uint32_t *>(q0 + 16 * ks + 8 + t2) : 0u;
-        a1[ks] = has_s && g + 8 < grp ? *reinterpret_cast<const uint32_t *>(q1 + 16 * ks + t2) : 0u;
-        a3[ks] = has_s && g + 8 < grp ? *reinterpret_cast<const uint32_t *>(q1 + 16 * ks + 8 + t2) : 0u;
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        sc[k][0] = sc[k][1] = sc[k][2] = sc[k][3] = -INFINITY;
-        const int nt = sub + nsub * k;
-        if (nt <= last_tile) {
-          float d[4] = {0.f, 0.f, 0.f, 0.f};
-          const int row = 8 * nt + (lane & 7);
-#pragma unroll
-          for (int k2 = 0; k2 < 2; ++k2) {
-            uint32_t b[4];
-            ldsm_x4(b, kbase + kv_off(row, 4 * k2 + (lane >> 3)));
-            mma_16816_full(d, a0[2 * k2], a1[2 * k2], a2[2 * k2], a3[2 * k2], b[0], b[1]);
-            mma_16816_full(d, a0[2 * k2 + 1], a1[2 * k2 + 1], a2[2 * k2 + 1], a3[2 * k2 + 1], b[2], b[3]);
-          }
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int sp = 8 * nt + t2 + (e & 1);
-            sc[k][e] = sp <= p ? d[e] * 0.125f : -INFINITY;
-          }
-          mx0 = fmaxf(mx0, fmaxf(sc[k][0], sc[k][1]));
-          mx1 = fmaxf(mx1, fmaxf(sc[k][2], sc[k][3]));
-        }
-      }
-    }
-    // softmax (cpu_backend.py:95-129: max-subtract, exp, divide by the sum),
-    // maxima and sums exchanged between the nsub warps of a kv head
-    float *pmax = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(att) + att_q_bytes(QH) + att_p_bytes(QH, P.CTX));
-    float *psum = pmax + kWarps * 16;
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    if ((lane & 3) == 0) {
-      pmax[warp * 16 + g] = mx0;
-      pmax[warp * 16 + g + 8] = mx1;
-    }
-    consumer_sync(kConsumerThreads);
-    for (int w2 = j; w2 < kWarps; w2 += KVH) {
-      mx0 = fmaxf(mx0, pmax[w2 * 16 + g]);
-      mx1 = fmaxf(mx1, pmax[w2 * 16 + g + 8]);
-    }
-    float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      if (sub + nsub * k <= last_tile) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float v = sc[k][e] == -INFINITY ? 0.f : expf(__fsub_rn(sc[k][e], e < 2 ? mx0 : mx1));
-          sc[k][e] = v;
-          if (e < 2) sum0 += v; else sum1 += v;
-        }
-      }
-    }
-    sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
-    sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
-    sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
-    sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
-    if ((lane & 3) == 0) {
-      psum[warp * 16 + g] = sum0;
-      psum[warp * 16 + g + 8] = sum1;
-    }
-    consumer_sync(kConsumerThreads);
-    sum0 = 0.f;
-    sum1 = 0.f;
-    for (int w2 = j; w2 < kWarps; w2 += KVH) {
-      sum0 += psum[w2 * 16 + g];
-      sum1 += psum[w2 * 16 + g + 8];
-    }
-    // probabilities of every position the P V k-steps cover (0 past p), as
-    // hi + mid + lo BF16 terms
-    __nv_bfloat16 *pt = reinterpret_cast<__nv_bfloat16 *>(reinterpret_cast<uint8_t *>(att) + att_q_bytes(QH));
-    const int pst = P.CTX + 8;
-    const size_t pterm = static_cast<size_t>(QH) * pst;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int nt = sub + nsub * k;
-      if (nt < ntiles) {
-        const bool live = nt <= last_tile;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int row = g + 8 * h;
-          if (row < grp) {
-            const float ssum = h ? sum1 : sum0;
-            const float v0 = live ? __fdiv_rn(sc[k][2 * h], ssum) : 0.f;
-            const float v1 = live ? __fdiv_rn(sc[k][2 * h + 1], ssum) : 0.f;
-            uint32_t hi, mid, lo;
-            split3_pack(v0, v1, hi, mid, lo);
-            const size_t o = static_cast<size_t>(j * grp + row) * pst + 8 * nt + t2;
-            *reinterpret_cast<uint32_t *>(pt + o) = hi;
-            *reinterpret_cast<uint32_t *>(pt + pterm + o) = mid;
-            *reinterpret_cast<uint32_t *>(pt + 2 * pterm + o) = lo;
-          }
-        }
-      }
-    }
-    consumer_sync(kConsumerThreads);
-    // O = P V: work items (kv head jj, 8-dim block dn) over all warps; the
-    // three probability terms accumulate independently
-    for (int item = warp; item < KVH * 8; item += kWarps) {
-      const int jj = item >> 3, dn = item & 7;
-      const uint32_t vbase = smem_u32(chunk_ptr(KVH + jj));
-      float dh[4] = {0.f, 0.f, 0.f, 0.f}, dm[4] = {0.f, 0.f, 0.f, 0.f}, dl[4] = {0.f, 0.f, 0.f, 0.f};
-      const bool r0 = g < grp, r1 = g + 8 < grp;
-      const __nv_bfloat16 *pr0 = pt + static_cast<size_t>(jj * grp + g) * pst + t2;
-      const __nv_bfloat16 *pr1 = pt + static_cast<size_t>(jj * grp + g + 8) * pst + t2;
-      for (int ks = 0; ks < nks; ++ks) {
-        uint32_t b[2];
-        ldsm_x2_trans(b, vbase + kv_off(16 * ks + (lane & 15), dn));
-        uint32_t a[3][4];
-#pragma unroll
-        for (int t = 0; t < 3; ++t) {
-          const size_t to = t * pterm + 16 * ks;
-          a[t][0] = r0 ? *reinterpret_cast<const uint32_t *>(pr0 + to) : 0u;
-          a[t][1] = r1 ? *reinterpret_cast<const uint32_t *>(pr1 + to) : 0u;
-          a[t][2] = r0 ? *reinterpret_cast<const uint32_t *>(pr0 + to + 8) : 0u;
-          a[t][3] = r1 ? *reinterpret_cast<const uint32_t *>(pr1 + to + 8) : 0u;
-        }
-        mma_16816_full(dh, a[0][0], a[0][1], a[0][2], a[0][3], b[0], b[1]);
-        mma_16816_full(dm, a[1][0], a[1][1], a[1][2], a[1][3], b[0], b[1]);
-        mma_16816_full(dl, a[2][0], a[2][1], a[2][2], a[2][3], b[0], b[1]);
-      }
-      float d[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) d[e] = dh[e] + (dm[e] + dl[e]);
-      __nv_bfloat16 *out = xs + static_cast<size_t>(m) * P.xs_elems;
-      if (r0)
-        *reinterpret_cast<uint32_t *>(out + (jj * grp + g) * kHeadDim + 8 * dn + t2) = pack_bf16x2(d[0], d[1]);
-      if (r1)
-        *reinterpret_cast<uint32_t *>(out + (jj * grp + g + 8) * kHeadDim + 8 * dn + t2) = pack_bf16x2(d[2], d[3]);
-    }
-    __syncwarp();
-    consumer_sync(kConsumerThreads);
-    return true;
-  }
+  // ---- attention (cpu_backend.py:78-129) ---------------------------------------
+  // The attention phase splits its work into (batch row m, q head h) units,
+  // one per CTA (unit = cta); each unit publishes its 64 outputs as LL words
+  // and every CTA then gathers all heads of all rows for the o-projection.
+  __device__ bool has_unit() const { return cta < mrows * P.QH; }
 
-  // Start copying the K/V history of batch row m, layer `layer` (rows of the
-  // k-steps attention covers, all but the current position, which the
-  // attention writes itself) from the cache into kvs.
-  __device__ void kv_prefetch(int layer, int m) {
+  // Start copying the K and V history (positions < p) of row m, kv head j
+  // from the cache into kvs with cp.async.
+  __device__ void kv_prefetch_unit(int layer, int m, int j) {
     const int p = s_pos[m], slot = s_slot[m];
-    const int per_block = ((p >> 4) + 1) * 16 * 8;  // 16-byte pieces
-    const int total = 2 * P.KVH * per_block;
-    for (int i = tid; i < total; i += kConsumerThreads) {
-      const int c = i / per_block, rem = i - c * per_block;
-      const int row = rem >> 3;
-      if (row == p) continue;
-      const int kind = c < P.KVH ? 0 : 1, j = c < P.KVH ? c : c - P.KVH;
-      const size_t off = static_cast<size_t>(row) * 128 + (rem & 7) * 16;
-      cp_async16(kvs + static_cast<size_t>(c) * P.CTX * 128 + off,
+    const int pieces = p * 8;  // 16-byte pieces per block
+    for (int i = tid; i < 2 * pieces; i += kConsumerThreads) {
+      const int kind = i >= pieces ? 1 : 0, rem = i - kind * pieces;
+      const size_t off = static_cast<size_t>(rem >> 3) * 128 + (rem & 7) * 16;
+      cp_async16(kvs + static_cast<size_t>(kind) * P.CTX * 128 + off,
                  reinterpret_cast<const uint8_t *>(kv_block(slot, layer, j, kind)) + off);
     }
     cp_async_commit();
+  }
+
+  // The unit's q (head h), k and v (kv head j) words of row m into u96.
+  __device__ bool gather_unit(int layer, int m, int h, int j, uint32_t *u96) {
+    if (tid >= 96) return true;
+    const int seg = tid >> 5, i = tid & 31;
+    const int head = seg == 0 ? h : seg == 1 ? P.QH + j : P.QH + P.KVH + j;
+    const uint64_t *src = ll_qkv(layer, m) + head * 32 + i;
+    uint64_t start = 0;
+    for (uint32_t spins = 0;; ++spins) {
+      const uint64_t v = ll_load(src);
+      if (static_cast<uint32_t>(v >> 32) == epoch) {
+        u96[tid] = static_cast<uint32_t>(v);
+        return true;
+      }
+      if (start == 0) start = globaltimer_ns();
+      if ((spins & 31u) == 31u) {
+        if (ld_volatile_int(&P.result->ctrl.abort)) return false;
+        if (globaltimer_ns() - start > P.limit_ns) {
+          raise_error(&P.result->ctrl, kErrTimeout, kWhereGrid);
+          return false;
+        }
+      }
+    }
+  }
+
+  // One unit: RoPE (rotate-half, unfused mul/add, BF16), K/V append, scores
+  // q.k * 0.125 over positions <= p, softmax (max-subtract, exp, divide),
+  // P.V in FP32; publishes bf16 outputs to ll_att(layer, m) + h * 32.
+  __device__ void attention_unit(int layer, int m, int h, int j, uint32_t *u96) {
+    const int p = s_pos[m];
+    float *qf = reinterpret_cast<float *>(u96 + 96);
+    float *sc = qf + kHeadDim;
+    float *part = sc + kHeadDim;
+    uint8_t *kb = kvs, *vb = kvs + static_cast<size_t>(P.CTX) * 128;
+    auto elem = [&](int seg, int e) {  // element e of q / k / v
+      const uint32_t w = u96[seg * 32 + (e >> 1)];
+      return (e & 1) ? bf_hi(w) : bf_lo(w);
+    };
+    if (tid < 64) {
+      const int d = tid & 31, seg = tid >> 5;  // 0: q, 1: k
+      const float c = P.rope_cos[p * 32 + d], sn = P.rope_sin[p * 32 + d];
+      const float x0 = elem(seg, d), x1 = elem(seg, d + 32);
+      const __nv_bfloat16 lo = f2bf(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+      const __nv_bfloat16 hi = f2bf(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
+      if (seg == 0) {
+        qf[d] = bf2f(lo);
+        qf[d + 32] = bf2f(hi);
+      } else {
+        *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(p, d >> 3) + (d & 7) * 2) = lo;
+        *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(p, 4 + (d >> 3)) + (d & 7) * 2) = hi;
+      }
+    } else if (tid < 96) {
+      const int w = tid - 64;  // v dims 2w, 2w+1 (raw)
+      *reinterpret_cast<uint32_t *>(vb + kv_off(p, (2 * w) >> 3) + ((2 * w) & 7) * 2) = u96[64 + w];
+    }
+    cp_async_wait_all();
+    consumer_sync(kConsumerThreads);
+    // the first q head of kv group j appends row p of K and V to the cache
+    if (h % P.group == 0 && tid < 16) {
+      const int kind = tid >> 3, cb = tid & 7;
+      const uint8_t *srow = (kind ? vb : kb) + kv_off(p, cb);
+      uint8_t *dst = reinterpret_cast<uint8_t *>(kv_block(s_slot[m], layer, j, kind)) + kv_off(p, cb);
+      *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(srow);
+    }
+    // scores: warp w takes positions 8w..8w+7, four lanes per position
+    {
+      const int warp = tid >> 5, lane = tid & 31;
+      const int sp = 8 * warp + (lane >> 2), qd = lane & 3;
+      float acc = 0.f;
+      if (sp <= p) {
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          const uint4 kw = *reinterpret_cast<const uint4 *>(kb + kv_off(sp, 2 * qd + b));
+          const float *q = qf + 16 * qd + 8 * b;
+          acc = fmaf(bf_lo(kw.x), q[0], acc);
+          acc = fmaf(bf_hi(kw.x), q[1], acc);
+          acc = fmaf(bf_lo(kw.y), q[2], acc);
+          acc = fmaf(bf_hi(kw.y), q[3], acc);
+          acc = fmaf(bf_lo(kw.z), q[4], acc);
+          acc = fmaf(bf_hi(kw.z), q[5], acc);
+          acc = fmaf(bf_lo(kw.w), q[6], acc);
+          acc = fmaf(bf_hi(kw.w), q[7], acc);
+        }
+      }
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      if (qd == 0 && sp < kHeadDim) sc[sp] = acc * 0.125f;
+    }
+    consumer_sync(kConsumerThreads);
+    if (tid < 32) {
+      const int lane = tid;
+      const bool in0 = lane <= p, in1 = lane + 32 <= p;
+      const float s0 = in0 ? sc[lane] : -INFINITY, s1 = in1 ? sc[lane + 32] : -INFINITY;
+      float mx = fmaxf(s0, s1);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float e0 = in0 ? expf(__fsub_rn(s0, mx)) : 0.f;
+      const float e1 = in1 ? expf(__fsub_rn(s1, mx)) : 0.f;
+      float sum = e0 + e1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      sc[lane] = __fdiv_rn(e0, sum);
+      sc[lane + 32] = __fdiv_rn(e1, sum);
+    }
+    consumer_sync(kConsumerThreads);
+    // P.V: thread (dim d, position quarter pg)
+    {
+      const int d = tid & 63, pg = tid >> 6;
+      const int s0 = pg * 16, s1 = min(s0 + 15, p);
+      float acc = 0.f;
+      for (int sp = s0; sp <= s1; ++sp)
+        acc = fmaf(sc[sp], bf2f(*reinterpret_cast<const __nv_bfloat16 *>(vb + kv_off(sp, d >> 3) + (d & 7) * 2)),
+                   acc);
+      part[pg * 64 + d] = acc;
+    }
+    consumer_sync(kConsumerThreads);
+    if (tid < 32) {
+      float o[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int d = 2 * tid + e;
+        o[e] = (part[d] + part[64 + d]) + (part[128 + d] + part[192 + d]);
+      }
+      ll_store(ll_att(layer, m) + h * 32 + tid, pack_bf16x2(o[0], o[1]), epoch);
+    }
   }
 
   // One phase of a layer (kind = k & 3: 0 qkv, 1 attention + o_proj,
@@ -670,8 +587,8 @@ struct DecoderCta {
     const float2 scale0 = load_pair(scale_p, r.g0 * 8, npairs);
     Gamma gamma;
     if (kind == 0 || kind == 2) gamma = load_gamma(kind == 0 ? lp.gamma_in : lp.gamma_post);
-    float2 rope0 = make_float2(0.f, 0.f);
-    if (kind == 1) rope0 = make_float2(P.rope_cos[s_pos[0] * 32 + (tid & 31)], P.rope_sin[s_pos[0] * 32 + (tid & 31)]);
+    const int um = cta / P.QH, uh = cta - um * P.QH, uj = uh / P.group;  // attention unit
+    uint32_t *u96 = reinterpret_cast<uint32_t *>(att);
     // inputs: the previous phase's LL words (the embedding row for layer 0)
     bool ok = true;
     if (kind == 0) {
@@ -680,18 +597,18 @@ struct DecoderCta {
         for (int m = 0; m < mrows; ++m) {
           const uint32_t *e = reinterpret_cast<const uint32_t *>(P.embed + static_cast<size_t>(s_tok[m]) * P.H);
           for (int w = tid; w < P.H / 2; w += kConsumerThreads) {
-            const uint32_t v = __ldg(e + w);
-            hx[m * P.H + 2 * w] = bf_lo(v);
-            hx[m * P.H + 2 * w + 1] = bf_hi(v);
+            reinterpret_cast<uint32_t *>(hx + m * P.H)[w] = __ldg(e + w);
           }
         }
       } else {
         ok = gather_to_hx(ll_hout(layer - 1, 0), P.H / 2, P.H);
       }
     } else if (kind == 1) {
-      kv_prefetch(layer, 0);  // overlaps the wait for q/k/v
-      ok = gather_raw(ll_qkv(layer, 0), P.QKV / 2, P.QKV / 2, qkv_s, P.QKV / 2);
-      if (!ok) cp_async_wait_all();
+      if (has_unit()) {
+        kv_prefetch_unit(layer, um, uj);  // overlaps the wait for q/k/v
+        ok = gather_unit(layer, um, uh, uj, u96);
+        if (!ok) cp_async_wait_all();
+      }
     } else if (kind == 2) {
       ok = gather_to_hx(ll_h1(layer, 0), P.H / 2, P.H);
     } else {
@@ -703,8 +620,10 @@ struct DecoderCta {
     if (kind == 0 || kind == 2) {
       norm_rows(gamma);
     } else if (kind == 1) {
-      for (int m = 0; m < mrows; ++m)
-        if (!attention_row(layer, m, rope0)) return false;
+      if (has_unit()) attention_unit(layer, um, uh, uj, u96);
+      if (!gather_raw(ll_att(layer, 0), P.H / 2, P.H / 2, reinterpret_cast<uint32_t *>(xs), P.xs_elems / 2))
+        return false;
+      consumer_sync(kConsumerThreads);
     }
     mark(k, 6);
     if (!consume_splitk<MB, W8>(ring, r, xs, P.xs_elems, mrows, red, P.red_rows, &P.result->ctrl, P.limit_ns))
@@ -751,7 +670,7 @@ struct DecoderCta {
         if (kind == 0) {
           if (bias_p != nullptr) y[e] = __fadd_rn(y[e], mine ? (e ? bias0.y : bias0.x) : bias_p[row + e]);
         } else {
-          y[e] = __fadd_rn(y[e], hx[m * P.H + row + e]);
+          y[e] = __fadd_rn(y[e], bf2f(hx[m * P.H + row + e]));
         }
       }
       uint64_t *dst = kind == 0 ? ll_qkv(layer, m) : kind == 1 ? ll_h1(layer, m) : ll_hout(layer, m);

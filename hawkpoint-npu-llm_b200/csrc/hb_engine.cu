@@ -25,7 +25,7 @@ namespace {
 
 constexpr uint64_t kDefaultLimitNs = 2000000000ull;  // 2 s per device wait
 constexpr int kMaxSlotsRing = 16;
-constexpr int kMinSlotsRing = 4;
+constexpr int kMinSlotsRing = 2;
 constexpr int kProfileCap = 1 << 16;
 
 thread_local std::string g_lib_error;
@@ -382,12 +382,15 @@ int hb_create(const hb_model_desc *desc, int device, hb_engine **out) {
   if (!prop.cooperativeLaunch) return bail(fail(nullptr, HB_ERR_UNSUPPORTED, "cooperative launch unsupported"));
   const hb_model_desc &d = e->desc;
   e->G = prop.multiProcessorCount;
-  if (e->G < d.q_heads) return bail(fail(nullptr, HB_ERR_UNSUPPORTED, "fewer SMs than attention heads"));
+  // the attention phase gives each (batch row, q head) unit its own CTA
+  if (e->G < d.q_heads * d.max_batch)
+    return bail(fail(nullptr, HB_ERR_UNSUPPORTED, "q_heads * max_batch (%d) exceeds the SM count (%d)",
+                     d.q_heads * d.max_batch, e->G));
   const int qkv = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
   auto ceil_div = [](int a, int b) { return (a + b - 1) / b; };
   e->red_rows = std::max(std::max(ceil_div(qkv / 8, e->G) * 8, ceil_div(d.intermediate / 8, e->G) * 16),
                          ceil_div(d.hidden / 8, e->G) * 8);
-  e->xs_elems = std::max(std::max(d.hidden, d.intermediate), hb::kHeadDim);
+  e->xs_elems = std::max(d.hidden, d.intermediate);  // GEMV inputs
   e->xs_elems = (e->xs_elems + 15) / 16 * 16;
   const bool w8 = d.weight_format == HB_WEIGHTS_W8;
   if ((rc = setup_variant(e, e->var1, 1, decoder_fn(1, w8), prop.sharedMemPerBlockOptin))) return bail(rc);

@@ -359,8 +359,11 @@ __device__ __forceinline__ bool consume_splitk(Ring &ring, const MatRange &r, co
       if (!ok) return false;
     } else if (2 * rgb > static_cast<int>(kSlotBytes)) {
       // one row group per chunk: up to kStepRows chunks per step
-      for (int g = r.g0; g < r.g1; g += kStepRows) {
-        const int nb = min(kStepRows, r.g1 - g);
+      // a step waits for at most nslots chunks: the producer must be able
+      // to have them all in flight at once
+      const int maxn = min(kStepRows, ring.nslots);
+      for (int g = r.g0; g < r.g1; g += maxn) {
+        const int nb = min(maxn, r.g1 - g);
         if (!wait_chunks(nb)) return false;
         mma_step(d, unit, nb, xrow, 0, r.kc);
         flush(g, nb);

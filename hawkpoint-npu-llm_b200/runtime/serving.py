@@ -1,0 +1,137 @@
+"""Multi-stream greedy serving on one GPU: continuous batching over the
+engine's batched decode step (``hb_step_batch``).
+
+The reference serves one request at a time behind a lock
+(npu_llm/api_server.py:646-678); its engine has no batched mode.  Here up to
+``max_batch`` independent streams share every kernel launch: each row of a
+launch is one stream at its own position -- a prompt token during sequential
+prefill (npu_llm/runtime/generate.py:1110-1126, logits unused), or its last
+generated token during decode.  A weight-streaming decode step costs about
+the same for 8 rows as for 1, so the aggregate rate scales with the batch.
+
+KV slots: ``max_batch`` slots for the running streams plus a small LRU pool
+that keeps shared prompt prefixes.  A request whose first ``prefix_tokens``
+ids match a kept prefix starts after it (the cached positions are copied into
+its slot with ``hb_copy_prefix``), the same reuse rule as the reference's
+prefix cache (``min(shared, len - 1)`` positions, generate.py:952-973).
+"""
+
+from collections import OrderedDict
+from dataclasses import dataclass, field
+import time
+
+
+@dataclass
+class Request:
+    prompt: list
+    new_tokens: int
+    rid: int = 0
+    tokens: list = field(default_factory=list)
+    admitted: float = 0.0
+    first_token: float = 0.0
+    finished: float = 0.0
+    reused_prefix: int = 0
+
+    @property
+    def ttft(self):
+        return self.first_token - self.admitted
+
+
+class _Stream:
+    __slots__ = ("req", "slot", "pos", "token", "key")
+
+    def __init__(self, req, slot, pos, token, key):
+        self.req, self.slot, self.pos, self.token, self.key = req, slot, pos, token, key
+
+
+class MultiStreamServer:
+    """Runs a list of greedy requests to completion on one engine.
+
+    ``engine`` needs ``step_batch(slots, tokens, positions) -> (argmax, _)``,
+    ``copy_prefix(src, dst, n)``, ``max_slots`` and ``context``; it must have
+    at least ``max_batch + prefix_slots`` KV slots."""
+
+    def __init__(self, engine, max_batch=8, prefix_tokens=16, prefix_slots=4, clock=time.perf_counter):
+        if max_batch < 1:
+            raise ValueError("max_batch must be >= 1")
+        if engine.max_slots < max_batch + prefix_slots:
+            raise ValueError(f"engine has {engine.max_slots} KV slots, needs {max_batch + prefix_slots}")
+        self.engine = engine
+        self.max_batch = max_batch
+        self.prefix_tokens = prefix_tokens
+        self.clock = clock
+        self.stream_slots = list(range(max_batch))
+        self.prefix_pool = list(range(max_batch, max_batch + prefix_slots))
+        self.prefixes = OrderedDict()   # prefix ids -> slot holding their positions
+        self.launches = 0
+        self.rows = 0
+
+    def _key(self, prompt):
+        if self.prefix_tokens > 0 and len(prompt) > self.prefix_tokens:
+            return tuple(int(t) for t in prompt[: self.prefix_tokens])
+        return None
+
+    def _admit(self, req, free):
+        slot = free.pop()
+        key = self._key(req.prompt)
+        start = 0
+        if key is not None and key in self.prefixes:
+            self.prefixes.move_to_end(key)
+            self.engine.copy_prefix(self.prefixes[key], slot, self.prefix_tokens)
+            start = self.prefix_tokens
+        req.reused_prefix = start
+        req.admitted = self.clock()
+        return _Stream(req, slot, start, int(req.prompt[start]), key)
+
+    def _keep_prefix(self, st):
+        """Positions [0, prefix_tokens) of st are computed: keep them."""
+        if st.key is None or st.key in self.prefixes:
+            return
+        if self.prefix_pool:
+            pslot = self.prefix_pool.pop()
+        else:
+            _, pslot = self.prefixes.popitem(last=False)
+        self.engine.copy_prefix(st.slot, pslot, self.prefix_tokens)
+        self.prefixes[st.key] = pslot
+
+    def run(self, requests):
+        context = self.engine.context
+        for req in requests:
+            if not 1 <= len(req.prompt) < context:
+                raise ValueError(f"prompt of {len(req.prompt)} ids does not fit a {context}-token context")
+            if req.new_tokens < 1:
+                raise ValueError("new_tokens must be >= 1")
+        queue = list(reversed(requests))
+        free = list(reversed(self.stream_slots))
+        active = []
+        while queue or active:
+            while queue and free and len(active) < self.max_batch:
+                active.append(self._admit(queue.pop(), free))
+            slots = [st.slot for st in active]
+            tokens = [st.token for st in active]
+            positions = [st.pos for st in active]
+            argmax, _ = self.engine.step_batch(slots, tokens, positions)
+            self.launches += 1
+            self.rows += len(active)
+            now = self.clock()
+            still = []
+            for st, nxt in zip(active, argmax):
+                req = st.req
+                last_prompt = len(req.prompt) - 1
+                if st.pos < last_prompt:
+                    st.token = int(req.prompt[st.pos + 1])        # sequential prefill
+                else:
+                    req.tokens.append(int(nxt))
+                    if len(req.tokens) == 1:
+                        req.first_token = now
+                    st.token = int(nxt)
+                st.pos += 1
+                if st.pos == self.prefix_tokens:
+                    self._keep_prefix(st)
+                if len(req.tokens) >= req.new_tokens or st.pos >= context:
+                    req.finished = now
+                    free.append(st.slot)
+                else:
+                    still.append(st)
+            active = still
+        return requests

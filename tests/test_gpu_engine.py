@@ -217,3 +217,49 @@ def test_full_size_against_reference_golden(name, golden):
                 assert set(np.argsort(-got)[:2]) == set(g["top_ids"][p][:2])
     finally:
         engine.close()
+
+
+def test_full_size_w8_against_w8_oracle():
+    """every projection and the LM head in int8 with FP32
+    row scales, teacher-forced against the W8 oracle at full Qwen size."""
+    model = synthetic.build("qwen2.5-0.5b", seed=0).materialize()
+    engine = B200DecoderEngine(model, weights="w8")
+    try:
+        oracle = OracleDecoder(model, weights="w8")
+        ids = synthetic.prompt_ids(model.shape.vocab, 40, seed=1)[:6]
+        for p, t in enumerate(ids):
+            got = engine.step(int(t), p, logits=True)
+            ref = oracle.step(int(t), p)
+            d = np.abs(got - ref)
+            rel = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
+            assert d.max() <= ATOL_FULL, f"position {p}: max-abs {d.max():.3e}"
+            assert rel <= RTOL_FULL, f"position {p}: rel {rel:.3e}"
+            if int(np.argmax(got)) != int(np.argmax(ref)):
+                top = np.argsort(-ref)[:2]
+                assert ref[top[0]] - ref[top[1]] <= 2 * d.max()
+                assert set(np.argsort(-got)[:2]) == set(top)
+    finally:
+        engine.close()
+
+
+def test_full_size_batch_rows_match_single_rows():
+    """The batch-8 kernel variant at full Qwen size (its ring is only a few
+    slots deep) gives every row the single-row result."""
+    model = synthetic.build("qwen2.5-0.5b", seed=0).materialize()
+    engine = B200DecoderEngine(model, max_slots=4, max_batch=8)
+    try:
+        ids = synthetic.prompt_ids(model.shape.vocab, 12, seed=3)
+        # slot s holds a prefix of 2 + 3s positions
+        depth = [2, 5, 8]
+        for s, n in enumerate(depth):
+            for p in range(n):
+                engine.step(ids[p], p, logits=False, slot=s)
+        am, logits = engine.step_batch([0, 1, 2], [ids[n] for n in depth], depth, logits=True)
+        for s, n in enumerate(depth):
+            # recomputing position n of slot s with the same token rewrites
+            # the same K/V, so the single-row launch sees the same history
+            single = engine.step(ids[n], n, logits=True, slot=s)
+            assert np.abs(single - logits[s]).max() <= ATOL_FULL
+            assert int(am[s]) == int(np.argmax(logits[s]))
+    finally:
+        engine.close()

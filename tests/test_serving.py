@@ -1,0 +1,112 @@
+"""Multi-stream continuous batching (BASELINE config 5 on one GPU): the
+scheduler on CPU against a fake causal engine, and on the GPU against
+single-stream generation through the same kernels."""
+
+import numpy as np
+import pytest
+
+from runtime.serving import MultiStreamServer, Request
+
+
+class FakeEngine:
+    """Causal toy model: the next token is a hash of every token cached in
+    the slot up to the position, so a wrong prefix copy, a skipped position
+    or a shared slot changes the output."""
+
+    def __init__(self, max_slots, context=64, vocab=1000):
+        self.max_slots, self.context, self.vocab = max_slots, context, vocab
+        self.cache = [[None] * context for _ in range(max_slots)]
+        self.batches = []
+        self.copies = []
+
+    def step_batch(self, slots, tokens, positions):
+        assert len(set(slots)) == len(slots), "two rows share a KV slot"
+        self.batches.append(len(slots))
+        out = []
+        for s, t, p in zip(slots, tokens, positions):
+            self.cache[s][p] = t
+            hist = self.cache[s][: p + 1]
+            assert None not in hist, f"slot {s} position {p} reads an unwritten position"
+            out.append(hash(tuple(hist)) % self.vocab)
+        return np.array(out), None
+
+    def copy_prefix(self, src, dst, n):
+        self.copies.append((src, dst, n))
+        self.cache[dst][:n] = self.cache[src][:n]
+
+
+def reference_tokens(prompt, new_tokens, vocab=1000, context=64):
+    hist = list(prompt)
+    out = []
+    while len(out) < new_tokens and len(hist) <= context:
+        nxt = hash(tuple(hist)) % vocab
+        out.append(nxt)
+        if len(hist) == context:
+            break
+        hist.append(nxt)
+    return out
+
+
+def config5_requests(n=64, seed=0, vocab=1000, new_tokens=16):
+    rng = np.random.default_rng(seed)
+    shared = rng.integers(0, vocab, 16).tolist()
+    reqs = []
+    for i in range(n):
+        length = int(rng.integers(8, 49))
+        ids = rng.integers(0, vocab, length).tolist()
+        if i % 4 == 0:
+            ids = shared + ids[: max(1, length - 16)]
+        reqs.append(Request(prompt=ids, new_tokens=new_tokens, rid=i))
+    return reqs
+
+
+def test_continuous_batching_matches_single_streams():
+    eng = FakeEngine(max_slots=12)
+    reqs = config5_requests()
+    MultiStreamServer(eng, max_batch=8, prefix_slots=4).run(reqs)
+    for r in reqs:
+        assert r.tokens == reference_tokens(r.prompt, r.new_tokens), r.rid
+    assert max(eng.batches) == 8
+    # the shared 16-token prefix is computed once and reused afterwards
+    reused = [r for r in reqs if r.reused_prefix]
+    assert len(reused) >= 10 and all(r.reused_prefix == 16 for r in reused)
+    assert eng.copies[0][2] == 16
+
+
+def test_context_limit_and_validation():
+    eng = FakeEngine(max_slots=2, context=20)
+    req = Request(prompt=list(range(18)), new_tokens=10)
+    MultiStreamServer(eng, max_batch=1, prefix_slots=1).run([req])
+    assert req.tokens == reference_tokens(req.prompt, 10, context=20)[: len(req.tokens)]
+    assert len(req.tokens) == 3  # positions 17, 18, 19 produce tokens; then the context is full
+    with pytest.raises(ValueError):
+        MultiStreamServer(eng, max_batch=1, prefix_slots=1).run([Request(prompt=list(range(20)), new_tokens=1)])
+    with pytest.raises(ValueError):
+        MultiStreamServer(FakeEngine(max_slots=4), max_batch=8, prefix_slots=0)
+
+
+@pytest.mark.gpu
+def test_gpu_multistream_matches_generate():
+    from runtime import synthetic
+    from runtime.b200_engine import B200DecoderEngine
+
+    model = synthetic.build("tiny-qwen", seed=31)
+    engine = B200DecoderEngine(model, max_slots=12, max_batch=8)
+    try:
+        rng = np.random.default_rng(4)
+        shared = rng.integers(0, model.shape.vocab, 16).tolist()
+        reqs = []
+        for i in range(20):
+            ids = rng.integers(0, model.shape.vocab, int(rng.integers(8, 40))).tolist()
+            if i % 4 == 0:
+                ids = shared + ids[:8]
+            reqs.append(Request(prompt=ids, new_tokens=6, rid=i))
+        server = MultiStreamServer(engine, max_batch=8, prefix_slots=4)
+        server.run(reqs)
+        assert server.rows > server.launches  # rows really shared launches
+        for r in reqs:
+            single = engine.generate(r.prompt, r.new_tokens, slot=11)
+            assert r.tokens == single, f"request {r.rid}"
+        assert any(r.reused_prefix for r in reqs)
+    finally:
+        engine.close()
