@@ -65,6 +65,9 @@ def parse():
     return p.parse_args()
 
 
+LOCAL_DEVICE = [0]  # this rank's GPU (collectives name it explicitly)
+
+
 def dist_setup(n):
     import torch
     import torch.distributed as dist
@@ -72,12 +75,18 @@ def dist_setup(n):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    LOCAL_DEVICE[0] = local
+    # the drop-in NPUDecoder (e2e leg) opens its engine on HAWKPOINT_DEVICE
+    os.environ["HAWKPOINT_DEVICE"] = str(local)
     if world > 1:
         from datetime import timedelta
         backend = "nccl" if torch.cuda.is_available() else "gloo"
+        kwargs = {}
         if backend == "nccl":
             torch.cuda.set_device(local)
-        dist.init_process_group(backend, timeout=timedelta(seconds=300))
+            kwargs["device_id"] = torch.device("cuda", local)  # one communicator, bound to this GPU
+        # short timeout: a rank that stops answering ends the others' next collective
+        dist.init_process_group(backend, timeout=timedelta(seconds=60), **kwargs)
     return rank, world, local
 
 
@@ -86,7 +95,7 @@ def max_over_ranks(value, world):
         return value
     import torch
     import torch.distributed as dist
-    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    dev = torch.device("cuda", LOCAL_DEVICE[0]) if dist.get_backend() == "nccl" else "cpu"
     t = torch.tensor([value], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
@@ -97,7 +106,7 @@ def sum_over_ranks(value, world):
         return value
     import torch
     import torch.distributed as dist
-    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    dev = torch.device("cuda", LOCAL_DEVICE[0]) if dist.get_backend() == "nccl" else "cpu"
     t = torch.tensor([value], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.SUM)
     return float(t.item())
@@ -168,7 +177,10 @@ def run_multistream(model, blob, device, rank, world):
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
-        dist.barrier()
+        if dist.get_backend() == "nccl":
+            dist.barrier(device_ids=[LOCAL_DEVICE[0]])
+        else:
+            dist.barrier()
 
 
 def workload_prompt(vocab):
