@@ -100,6 +100,24 @@ int fail(hb_engine *e, int code, const char *fmt, ...) {
       return fail((e), HB_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(err_));       \
   } while (0)
 
+// Makes the engine's device current for one call and restores the caller's
+// current device on return, so the library never changes it behind the
+// caller's back.
+struct DeviceScope {
+  int prev = -1;
+  bool ok = false;
+  explicit DeviceScope(int device) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    ok = cudaSetDevice(device) == cudaSuccess;
+  }
+  ~DeviceScope() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+#define HB_ON_DEVICE(e)                                                               \
+  DeviceScope device_scope_((e)->device);                                            \
+  if (!device_scope_.ok) return fail((e), HB_ERR_CUDA, "cudaSetDevice(%d) failed", (e)->device)
+
 template <class T>
 int dev_alloc(hb_engine *e, T **p, size_t count) {
   HB_CUDA(e, cudaMalloc(reinterpret_cast<void **>(p), sizeof(T) * (count ? count : 1)));
@@ -278,7 +296,7 @@ int finish(hb_engine *e) {
 int check_engine(hb_engine *e) {
   if (!e) return fail(nullptr, HB_ERR_INVALID_ARG, "engine is NULL");
   if (!e->loaded) return fail(e, HB_ERR_STATE, "weights not loaded");
-  HB_CUDA(e, cudaSetDevice(e->device));
+  HB_ON_DEVICE(e);
   return HB_OK;
 }
 
@@ -374,7 +392,8 @@ int hb_create(const hb_model_desc *desc, int device, hb_engine **out) {
     hb_destroy(e);
     return code;
   };
-  if (cudaSetDevice(device) != cudaSuccess) return bail(fail(nullptr, HB_ERR_CUDA, "cudaSetDevice failed"));
+  DeviceScope device_scope_(device);
+  if (!device_scope_.ok) return bail(fail(nullptr, HB_ERR_CUDA, "cudaSetDevice(%d) failed", device));
   cudaDeviceProp prop{};
   if (cudaGetDeviceProperties(&prop, device) != cudaSuccess)
     return bail(fail(nullptr, HB_ERR_CUDA, "cudaGetDeviceProperties failed"));
@@ -458,7 +477,7 @@ int hb_load_weights(hb_engine *e, const void *host_blob, size_t bytes, int layou
     return fail(e, HB_ERR_INVALID_ARG, "blob size %zu != %llu", bytes,
                 static_cast<unsigned long long>(e->desc.blob_bytes));
   if (layout_version != 1) return fail(e, HB_ERR_UNSUPPORTED, "layout version %d unsupported", layout_version);
-  HB_CUDA(e, cudaSetDevice(e->device));
+  HB_ON_DEVICE(e);
   HB_CUDA(e, cudaMemcpy(e->d_blob, host_blob, bytes, cudaMemcpyHostToDevice));
   e->loaded = true;
   return HB_OK;
@@ -466,7 +485,7 @@ int hb_load_weights(hb_engine *e, const void *host_blob, size_t bytes, int layou
 
 int hb_destroy(hb_engine *e) {
   if (!e) return HB_OK;
-  cudaSetDevice(e->device);
+  DeviceScope device_scope_(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
   for (auto ev : e->ev_a) cudaEventDestroy(ev);
   for (auto ev : e->ev_b) cudaEventDestroy(ev);
@@ -564,7 +583,7 @@ int hb_step_batch(hb_engine *e, int n, const int32_t *slots, const int32_t *toke
 int hb_reset(hb_engine *e, int slot) {
   if (!e) return fail(nullptr, HB_ERR_INVALID_ARG, "engine is NULL");
   if (slot < 0 || slot >= e->desc.max_slots) return fail(e, HB_ERR_INVALID_ARG, "slot %d out of range", slot);
-  HB_CUDA(e, cudaSetDevice(e->device));
+  HB_ON_DEVICE(e);
   HB_CUDA(e, cudaMemsetAsync(e->d_kv + e->kv_slot_elems * slot, 0, e->kv_slot_elems * 2, e->stream));
   HB_CUDA(e, cudaStreamSynchronize(e->stream));
   return HB_OK;
@@ -577,7 +596,7 @@ int hb_copy_prefix(hb_engine *e, int src, int dst, int n_positions) {
     return fail(e, HB_ERR_INVALID_ARG, "slot out of range");
   if (n_positions < 0 || n_positions > d.context) return fail(e, HB_ERR_INVALID_ARG, "n_positions out of range");
   if (src == dst || n_positions == 0) return HB_OK;
-  HB_CUDA(e, cudaSetDevice(e->device));
+  HB_ON_DEVICE(e);
   // every K and V block is [context][64] with 128-byte position rows: copy
   // the first n rows of each block
   const size_t pitch = static_cast<size_t>(d.context) * hb::kHeadDim * 2;
@@ -591,7 +610,7 @@ int hb_copy_prefix(hb_engine *e, int src, int dst, int n_positions) {
 
 int hb_debug_dump(hb_engine *e, int what, void *out, size_t bytes) {
   if (!e || !out) return fail(e, HB_ERR_INVALID_ARG, "engine or out is NULL");
-  HB_CUDA(e, cudaSetDevice(e->device));
+  HB_ON_DEVICE(e);
   const hb_model_desc &d = e->desc;
   if (what == HB_DUMP_HIDDEN) {
     // payloads of the last layer's output words: BF16 [kMaxBatch][hidden]
@@ -633,7 +652,7 @@ int hb_profile(hb_engine *e, int enable) {
 
 int hb_profile_read(hb_engine *e, float *ms, float *start_ms, int max, int *count) {
   if (!e || !count || !ms) return fail(e, HB_ERR_INVALID_ARG, "engine, ms or count is NULL");
-  HB_CUDA(e, cudaSetDevice(e->device));
+  HB_ON_DEVICE(e);
   HB_CUDA(e, cudaStreamSynchronize(e->stream));
   const int n = std::min(max, e->prof_count);
   for (int i = 0; i < n; ++i) {
