@@ -62,6 +62,8 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-extras", action="store_true",
+                   help="skip the config 1/2/4/5 measurements (profiling runs of config 3 only)")
     return p.parse_args()
 
 
@@ -172,6 +174,83 @@ def run_multistream(model, blob, device, rank, world):
         "launches_rank0": server.launches, "rows_rank0": server.rows,
         "prefix_reuses_rank0": sum(1 for r in reqs if r.reused_prefix),
     }
+
+
+def run_other_configs(device, peak):
+    """BASELINE configs 1, 2 and 4 on this GPU (single-GPU runs only): decode
+    of the SmolLM2-135M shape (BF16) and of the Qwen shape in W8, and the
+    standalone GEMV shapes with HBM GB/s against the roofline."""
+    import ctypes
+    import numpy as np
+    import torch
+    from ml_dtypes import bfloat16
+    from runtime import hb_lib, layout, synthetic
+    from runtime.b200_engine import B200DecoderEngine
+
+    out = {}
+    for key, name, weights, n_prompt, n_new in (("config1_smollm2_135m_bf16", "smollm2-135m", "bf16", 35, 16),
+                                                 ("config4_qwen_w8", "qwen2.5-0.5b", "w8", 32, 32)):
+        model = synthetic.build(name, seed=MODEL_SEED).materialize()
+        eng = B200DecoderEngine(model, weights=weights, device=device)
+        try:
+            ids = synthetic.prompt_ids(model.shape.vocab, 40, seed=MODEL_SEED + 1)[:n_prompt]
+            first = eng.generate(ids, n_new)
+            eng.profile(True)
+            eng.profile_read()
+            for _ in range(3):
+                assert eng.generate(ids, n_new) == first
+            ms = eng.profile_read().reshape(3, n_prompt + n_new - 1)
+            eng.profile(False)
+        finally:
+            eng.close()
+        lay = layout.plan(model.shape, weights)
+        streamed = lay.total - model.shape.vocab * model.shape.hidden * 2  # the embedding is read one row at a time
+        dec = float(np.median(ms[:, n_prompt:]))
+        out[key] = {"decode_tokens_per_second": 1000.0 / dec, "decode_launch_ms": dec,
+                    "ttft_ms": float(ms[:, :n_prompt].sum(axis=1).mean()),
+                    "weight_bytes_per_token": int(streamed),
+                    "hbm_frac": streamed / (dec / 1000.0) / 1e9 / peak}
+    # config 2: y = W x (BF16 out) and the LM head with a fused argmax;
+    # rotating weight copies keep every launch's weights out of L2
+    lib = hb_lib.load()
+    dev = torch.device("cuda", device)
+    stream = torch.cuda.Stream(device=dev)
+    rng = np.random.default_rng(MODEL_SEED + 2)
+    gemv = []
+    for rows, k in ((896, 896), (4864, 896), (896, 4864), (576, 1536), (151936, 896)):
+        w = rng.standard_normal((rows, k), dtype=np.float32).astype(bfloat16)
+        packed = torch.from_numpy(layout.pack_matrix_bytes(w)).to(dev)
+        copies = [packed] + [packed.clone() for _ in range(max(0, -(-256 * 2**20 // packed.numel()) - 1))]
+        head = rows == 151936
+        for batch in (1, 8):
+            x = torch.from_numpy(rng.standard_normal((batch, k), dtype=np.float32).astype(bfloat16).view(np.int16)).to(dev)
+            y = torch.empty((batch, rows), dtype=torch.int16, device=dev)
+            am = torch.empty(batch, dtype=torch.int32, device=dev)
+            nscr = lib.hb_gemv_scratch_bytes(rows, batch)
+            scr = torch.zeros(nscr, dtype=torch.uint8, device=dev)
+            flags = (hb_lib.HB_GEMV_OUT_NONE | hb_lib.HB_GEMV_ARGMAX) if head else hb_lib.HB_GEMV_OUT_BF16
+
+            def launch(i):
+                hb_lib.check(lib.hb_gemv(copies[i % len(copies)].data_ptr(), None, 0, rows, k, x.data_ptr(), batch,
+                                         y.data_ptr(), flags, am.data_ptr(), scr.data_ptr(), nscr,
+                                         ctypes.c_void_p(stream.cuda_stream)))
+            with torch.cuda.stream(stream):
+                for i in range(5):
+                    launch(i)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                n = 40
+                e0.record(stream)
+                for i in range(n):
+                    launch(i)
+                e1.record(stream)
+            torch.cuda.synchronize(dev)
+            us = e0.elapsed_time(e1) * 1000.0 / n
+            nbytes = rows * k * 2 + batch * k * 2 + (0 if head else batch * rows * 2)
+            gemv.append({"rows": rows, "k": k, "batch": batch, "argmax": head, "us": us,
+                         "gbs": nbytes / (us * 1e-6) / 1e9, "hbm_frac": nbytes / (us * 1e-6) / 1e9 / peak})
+        del copies, packed
+    out["config2_gemv"] = gemv
+    return out
 
 
 def barrier(world):
@@ -415,7 +494,8 @@ def run_b200(args, rank, world, local):
     e2e_value = decode_steps * args.steps * world / e2e_t
     decoder.close()
 
-    multistream = run_multistream(model, blob, device, rank, world)
+    multistream = None if args.no_extras else run_multistream(model, blob, device, rank, world)
+    others = run_other_configs(device, measured_peak()[0]) if world == 1 and not args.no_extras else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -445,6 +525,7 @@ def run_b200(args, rank, world, local):
                     "d2h_bytes_per_step": launches_per_step * result_bytes},
             "gpu_launches": launches_per_step * args.steps,
             "multistream": multistream,
+            "other_configs": others,
             "clocks": clocks.summary(),
         }
         if cpu is not None:
