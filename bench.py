@@ -176,6 +176,13 @@ def run_multistream(model, blob, device, rank, world):
     }
 
 
+def prefill_launches(n_prompt, batch=8):
+    """Launches before the one that yields the first token: the engine
+    prefills positions 0 .. n_prompt-2 in launches of up to `batch`
+    consecutive positions (batch 1: one per position)."""
+    return -(-(n_prompt - 1) // batch)
+
+
 def run_other_configs(device, peak):
     """BASELINE configs 1, 2 and 4 on this GPU (single-GPU runs only): decode
     of the SmolLM2-135M shape (BF16) and of the Qwen shape in W8, and the
@@ -191,7 +198,7 @@ def run_other_configs(device, peak):
     for key, name, weights, n_prompt, n_new in (("config1_smollm2_135m_bf16", "smollm2-135m", "bf16", 35, 16),
                                                  ("config4_qwen_w8", "qwen2.5-0.5b", "w8", 32, 32)):
         model = synthetic.build(name, seed=MODEL_SEED).materialize()
-        eng = B200DecoderEngine(model, weights=weights, device=device)
+        eng = B200DecoderEngine(model, weights=weights, device=device, max_batch=8)  # batched prefill
         try:
             ids = synthetic.prompt_ids(model.shape.vocab, 40, seed=MODEL_SEED + 1)[:n_prompt]
             first = eng.generate(ids, n_new)
@@ -199,15 +206,16 @@ def run_other_configs(device, peak):
             eng.profile_read()
             for _ in range(3):
                 assert eng.generate(ids, n_new) == first
-            ms = eng.profile_read().reshape(3, n_prompt + n_new - 1)
+            n_pre = prefill_launches(n_prompt)
+            ms = eng.profile_read().reshape(3, n_pre + n_new)
             eng.profile(False)
         finally:
             eng.close()
         lay = layout.plan(model.shape, weights)
         streamed = lay.total - model.shape.vocab * model.shape.hidden * 2  # the embedding is read one row at a time
-        dec = float(np.median(ms[:, n_prompt:]))
+        dec = float(np.median(ms[:, n_pre + 1:]))
         out[key] = {"decode_tokens_per_second": 1000.0 / dec, "decode_launch_ms": dec,
-                    "ttft_ms": float(ms[:, :n_prompt].sum(axis=1).mean()),
+                    "ttft_ms": float(ms[:, :n_pre + 1].sum(axis=1).mean()),
                     "weight_bytes_per_token": int(streamed),
                     "hbm_frac": streamed / (dec / 1000.0) / 1e9 / peak}
     # config 2: y = W x (BF16 out) and the LM head with a fused argmax;
@@ -422,10 +430,11 @@ def run_b200(args, rank, world, local):
     prompt = workload_prompt(model.shape.vocab)
     n_prompt = len(prompt)
     decode_steps = NEW_TOKENS - 1
-    launches_per_step = n_prompt + NEW_TOKENS - 1
+    n_pre = prefill_launches(n_prompt)             # batched prefill launches
+    launches_per_step = n_pre + NEW_TOKENS
 
     blob = layout.pack(model, "bf16")
-    engine = B200DecoderEngine(model, device=device, blob=blob)
+    engine = B200DecoderEngine(model, device=device, blob=blob, max_batch=8)  # batched prefill
     stream = torch.cuda.Stream(device=device)
     engine.set_stream(stream.cuda_stream)
 
@@ -454,11 +463,11 @@ def run_b200(args, rank, world, local):
     start = start.reshape(args.steps, launches_per_step)
     engine.profile(False)
     assert tokens == ref_tokens, "greedy tokens changed between identical requests"
-    decode_launch_ms = dur[:, n_prompt:]
+    decode_launch_ms = dur[:, n_pre + 1:]
     # device time of each segment, launch gaps included
     end = start + dur
-    prefill_ms = end[:, n_prompt - 1] - start[:, 0]
-    decode_seg_ms = end[:, -1] - start[:, n_prompt]
+    prefill_ms = end[:, n_pre] - start[:, 0]          # through the first generated token
+    decode_seg_ms = end[:, -1] - start[:, n_pre + 1]
     local_time = float(decode_seg_ms.sum())
     t_max = max_over_ranks(local_time, world)
     value = (decode_steps * args.steps * world) / (t_max / 1000.0)
@@ -521,8 +530,9 @@ def run_b200(args, rank, world, local):
                          "frac": achieved / peak, "traffic": profiled_traffic(),
                          "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg_bytes},
             "e2e": {"value": e2e_value, "unit": "tokens/s",
-                    "h2d_bytes_per_step": launches_per_step * step_state_bytes,
-                    "d2h_bytes_per_step": launches_per_step * result_bytes},
+                    # decode_token runs one launch per position
+                    "h2d_bytes_per_step": (n_prompt + NEW_TOKENS - 1) * step_state_bytes,
+                    "d2h_bytes_per_step": (n_prompt + NEW_TOKENS - 1) * result_bytes},
             "gpu_launches": launches_per_step * args.steps,
             "multistream": multistream,
             "other_configs": others,

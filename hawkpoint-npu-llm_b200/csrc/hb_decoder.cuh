@@ -114,8 +114,13 @@ struct SmemPlan {
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Attention scratch of one (row, head) unit: its q/k/v words [96], rotated
-// q [64], scores / probabilities [64], P.V partial sums [4][64] (FP32).
-__host__ __device__ inline size_t att_bytes(int /*QH*/, int /*ctx*/) { return 2048; }
+// q [64], scores / probabilities [64], P.V partial sums [4][64] (FP32), and
+// the k/v words of up to kMaxBatch - 1 earlier positions of the same slot in
+// this launch [7][64].
+constexpr int kUnitWords = 96 + 64 + 64 + 256;
+__host__ __device__ inline size_t att_bytes(int /*QH*/, int /*ctx*/) {
+  return (static_cast<size_t>(kUnitWords) + (kMaxBatch - 1) * 64) * 4;
+}
 
 __host__ __device__ inline SmemPlan smem_plan(int nslots, int mb, int xs_elems, int H, int QKV,
                                               int QH, int KVH, int red_rows, int ctx) {
@@ -430,10 +435,20 @@ struct DecoderCta {
   // and every CTA then gathers all heads of all rows for the o-projection.
   __device__ bool has_unit() const { return cta < mrows * P.QH; }
 
-  // Start copying the K and V history (positions < p) of row m, kv head j
-  // from the cache into kvs with cp.async.
+  // First row of the run of rows that continue row m's sequence in this
+  // launch (same slot, consecutive positions): batched prefill puts up to
+  // kMaxBatch consecutive positions of one slot in one launch.
+  __device__ int run_start(int m) const {
+    int f = m;
+    while (f > 0 && s_slot[f - 1] == s_slot[m] && s_pos[f - 1] == s_pos[f] - 1) --f;
+    return f;
+  }
+
+  // Start copying the K and V history of row m, kv head j from the cache
+  // into kvs with cp.async: positions before the row's run (later ones are
+  // computed in this launch and come from the run's q/k/v words).
   __device__ void kv_prefetch_unit(int layer, int m, int j) {
-    const int p = s_pos[m], slot = s_slot[m];
+    const int p = s_pos[run_start(m)], slot = s_slot[m];
     const int pieces = p * 8;  // 16-byte pieces per block
     for (int i = tid; i < 2 * pieces; i += kConsumerThreads) {
       const int kind = i >= pieces ? 1 : 0, rem = i - kind * pieces;
@@ -444,8 +459,9 @@ struct DecoderCta {
     cp_async_commit();
   }
 
-  // The unit's q (head h), k and v (kv head j) words of row m into u96.
-  __device__ bool gather_unit(int layer, int m, int h, int j, uint32_t *u96) {
+  // Decode (no earlier rows in the run): the 96 q/k/v words of row m, one
+  // per thread.
+  __device__ bool gather_unit_row(int layer, int m, int h, int j, uint32_t *u96) {
     if (tid >= 96) return true;
     const int seg = tid >> 5, i = tid & 31;
     const int head = seg == 0 ? h : seg == 1 ? P.QH + j : P.QH + P.KVH + j;
@@ -468,6 +484,64 @@ struct DecoderCta {
     }
   }
 
+  // The unit's words into u96: q (head h), k and v (kv head j) of row m at
+  // [0, 96), then k and v of each earlier row of its run at 96 + 64 * r.
+  __device__ bool gather_unit(int layer, int m, int h, int j, uint32_t *u96) {
+    const int f = run_start(m);
+    if (f == m) return gather_unit_row(layer, m, h, j, u96);
+    const int n = 96 + 64 * (m - f);
+    constexpr int U = 4;
+    const uint64_t *src[U];
+    int dst[U];
+    uint32_t pend = 0;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = tid + u * kConsumerThreads;
+      dst[u] = i < 96 ? i : kUnitWords + (i - 96);
+      src[u] = nullptr;
+      if (i < n) {
+        int row = m, head, w;
+        if (i < 96) {
+          const int seg = i >> 5;
+          head = seg == 0 ? h : seg == 1 ? P.QH + j : P.QH + P.KVH + j;
+          w = i & 31;
+        } else {
+          const int e = i - 96;
+          row = f + (e >> 6);
+          head = (e & 63) < 32 ? P.QH + j : P.QH + P.KVH + j;
+          w = e & 31;
+        }
+        src[u] = ll_qkv(layer, row) + head * 32 + w;
+        pend |= 1u << u;
+      }
+    }
+    uint64_t start = 0;
+    for (uint32_t spins = 0; pend; ++spins) {
+      uint64_t v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (pend & (1u << u)) v[u] = ll_load(src[u]);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if ((pend & (1u << u)) && static_cast<uint32_t>(v[u] >> 32) == epoch) {
+          u96[dst[u]] = static_cast<uint32_t>(v[u]);
+          pend &= ~(1u << u);
+        }
+      }
+      if (pend) {
+        if (start == 0) start = globaltimer_ns();
+        if ((spins & 31u) == 31u) {
+          if (ld_volatile_int(&P.result->ctrl.abort)) return false;
+          if (globaltimer_ns() - start > P.limit_ns) {
+            raise_error(&P.result->ctrl, kErrTimeout, kWhereGrid);
+            return false;
+          }
+        }
+      }
+    }
+    return true;
+  }
+
   // One unit: RoPE (rotate-half, unfused mul/add, BF16), K/V append, scores
   // q.k * 0.125 over positions <= p, softmax (max-subtract, exp, divide),
   // P.V in FP32; publishes bf16 outputs to ll_att(layer, m) + h * 32.
@@ -477,14 +551,15 @@ struct DecoderCta {
     float *sc = qf + kHeadDim;
     float *part = sc + kHeadDim;
     uint8_t *kb = kvs, *vb = kvs + static_cast<size_t>(P.CTX) * 128;
-    auto elem = [&](int seg, int e) {  // element e of q / k / v
-      const uint32_t w = u96[seg * 32 + (e >> 1)];
-      return (e & 1) ? bf_hi(w) : bf_lo(w);
-    };
+    // RoPE'd q and k, raw v of row m into qf and the K / V rows at p
     if (tid < 64) {
       const int d = tid & 31, seg = tid >> 5;  // 0: q, 1: k
+      auto el = [&](int e) {
+        const uint32_t w = u96[seg * 32 + (e >> 1)];
+        return (e & 1) ? bf_hi(w) : bf_lo(w);
+      };
       const float c = P.rope_cos[p * 32 + d], sn = P.rope_sin[p * 32 + d];
-      const float x0 = elem(seg, d), x1 = elem(seg, d + 32);
+      const float x0 = el(d), x1 = el(d + 32);
       const __nv_bfloat16 lo = f2bf(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
       const __nv_bfloat16 hi = f2bf(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
       if (seg == 0) {
@@ -497,6 +572,29 @@ struct DecoderCta {
     } else if (tid < 96) {
       const int w = tid - 64;  // v dims 2w, 2w+1 (raw)
       *reinterpret_cast<uint32_t *>(vb + kv_off(p, (2 * w) >> 3) + ((2 * w) & 7) * 2) = u96[64 + w];
+    }
+    // batched prefill: RoPE'd k and raw v of the earlier rows of the run
+    const int f = run_start(m);
+    for (int t = tid; t < 64 * (m - f); t += kConsumerThreads) {
+      const int r = t >> 6, i = t & 63;
+      const int pr = s_pos[f + r];
+      const uint32_t *words = u96 + kUnitWords + 64 * r;  // k words [0, 32), v words [32, 64)
+      if (i < 32) {
+        const int d = i;
+        auto el = [&](int e) {
+          const uint32_t w = words[e >> 1];
+          return (e & 1) ? bf_hi(w) : bf_lo(w);
+        };
+        const float c = P.rope_cos[pr * 32 + d], sn = P.rope_sin[pr * 32 + d];
+        const float x0 = el(d), x1 = el(d + 32);
+        *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(pr, d >> 3) + (d & 7) * 2) =
+            f2bf(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+        *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(pr, 4 + (d >> 3)) + (d & 7) * 2) =
+            f2bf(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
+      } else {
+        const int w = i - 32;
+        *reinterpret_cast<uint32_t *>(vb + kv_off(pr, (2 * w) >> 3) + ((2 * w) & 7) * 2) = words[32 + w];
+      }
     }
     cp_async_wait_all();
     consumer_sync(kConsumerThreads);

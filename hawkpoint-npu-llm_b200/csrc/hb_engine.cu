@@ -26,6 +26,9 @@ namespace {
 constexpr uint64_t kDefaultLimitNs = 2000000000ull;  // 2 s per device wait
 constexpr int kMaxSlotsRing = 16;
 constexpr int kMinSlotsRing = 2;
+// Pinned StepState staging buffers: one per upload within one call (a call
+// may queue several launches before it synchronizes).
+constexpr int kStateRing = 16;
 constexpr int kProfileCap = 1 << 16;
 
 thread_local std::string g_lib_error;
@@ -323,20 +326,41 @@ int run_chained(hb_engine *e, int slot, const int32_t *ids, int n_prompt, int st
     if (rc) return rc;
   }
   for (int p = 0; p < d.context; ++p) e->h_prompt[p] = (p >= start && p < n_prompt) ? ids[p] : 0;
-  hb::StepState &st = *e->h_st;
+  const int body = 4 * d.layers;
+  const int full = 4 * d.layers + 1;
+  int upload = 0;
+  int first = start;  // first position the chained (device-advanced) steps run
+  if (d.max_batch > 1) {
+    // batched prefill: up to kMaxBatch consecutive positions per launch, all
+    // but the last prompt position (which the chained steps run with the head)
+    for (int p0 = start; p0 < n_prompt - 1; p0 += kMaxBatch) {
+      const int k = std::min(kMaxBatch, n_prompt - 1 - p0);
+      hb::StepState &sb = e->h_st[upload++];
+      std::memset(&sb, 0, sizeof(sb));
+      for (int i = 0; i < k; ++i) {
+        sb.token[i] = ids[p0 + i];
+        sb.pos[i] = p0 + i;
+        sb.slot[i] = slot;
+      }
+      sb.rows = k;
+      HB_CUDA(e, cudaMemcpyAsync(e->d_st, &sb, sizeof(hb::StepState), cudaMemcpyHostToDevice, e->stream));
+      int rc = launch(e, k, 0, body, 0);
+      if (rc) return rc;
+    }
+    first = n_prompt - 1;
+  }
+  hb::StepState &st = e->h_st[upload++];
   std::memset(&st, 0, sizeof(st));
-  st.token[0] = ids[start];
-  st.pos[0] = start;
+  st.token[0] = ids[first];
+  st.pos[0] = first;
   st.slot[0] = slot;
   st.rows = 1;
   st.chained = 1;
   st.n_prompt = n_prompt;
   st.n_out = 0;
   HB_CUDA(e, cudaMemcpyAsync(e->d_prompt, e->h_prompt, sizeof(int) * d.context, cudaMemcpyHostToDevice, e->stream));
-  HB_CUDA(e, cudaMemcpyAsync(e->d_st, e->h_st, sizeof(hb::StepState), cudaMemcpyHostToDevice, e->stream));
-  const int full = 4 * d.layers + 1;
-  const int body = 4 * d.layers;
-  for (int p = start; p < n_prompt - 1; ++p) {
+  HB_CUDA(e, cudaMemcpyAsync(e->d_st, &st, sizeof(hb::StepState), cudaMemcpyHostToDevice, e->stream));
+  for (int p = first; p < n_prompt - 1; ++p) {
     int rc = launch(e, 1, 0, body, 0);
     if (rc) return rc;
   }
@@ -435,7 +459,8 @@ int hb_create(const hb_model_desc *desc, int device, hb_engine **out) {
       (rc = dev_alloc(e, &e->d_trace, static_cast<size_t>(e->G) * (4 * d.layers + 2) * 8)))
     return bail(rc);
   (void)mb;
-  if (cudaHostAlloc(reinterpret_cast<void **>(&e->h_st), sizeof(hb::StepState), cudaHostAllocDefault) != cudaSuccess ||
+  if (cudaHostAlloc(reinterpret_cast<void **>(&e->h_st), sizeof(hb::StepState) * kStateRing,
+                    cudaHostAllocDefault) != cudaSuccess ||
       cudaHostAlloc(reinterpret_cast<void **>(&e->h_result), sizeof(hb::Result), cudaHostAllocDefault) != cudaSuccess ||
       cudaHostAlloc(reinterpret_cast<void **>(&e->h_prompt), sizeof(int) * d.context, cudaHostAllocDefault) != cudaSuccess ||
       cudaHostAlloc(reinterpret_cast<void **>(&e->h_gen), sizeof(int) * (d.context + 1), cudaHostAllocDefault) != cudaSuccess)

@@ -263,3 +263,26 @@ def test_full_size_batch_rows_match_single_rows():
             assert int(am[s]) == int(np.argmax(logits[s]))
     finally:
         engine.close()
+
+
+def test_full_size_batched_prefill_matches_sequential():
+    """Prefill in launches of up to 8 consecutive positions (the attention
+    units take the run's own k/v words) leaves the same KV cache and
+    produces the same greedy tokens as one position per launch."""
+    model = synthetic.build("qwen2.5-0.5b", seed=0).materialize()
+    ids = synthetic.prompt_ids(model.shape.vocab, 40, seed=1)[:21]
+    batched = B200DecoderEngine(model, max_slots=1, max_batch=8)
+    try:
+        got = batched.generate(ids, 6)
+        kv_b = batched.kv_cache(0)
+    finally:
+        batched.close()
+    single = B200DecoderEngine(model, max_slots=1, max_batch=1)
+    try:
+        ref = single.generate(ids, 6)
+        kv_s = single.kv_cache(0)
+    finally:
+        single.close()
+    assert got == ref
+    n = len(ids) + 5
+    assert np.array_equal(kv_b[:, :, :, :n].view(np.uint16), kv_s[:, :, :, :n].view(np.uint16))
