@@ -132,8 +132,9 @@ class B200DecoderEngine:
         return int(self._argmax.value)
 
     def prefill(self, ids, start=0, slot=0, logits=False):
-        """Sequential prefill of ``ids`` at positions start..; returns
-        (argmax of the last position, its logits or None)."""
+        """Prefill of ``ids`` at positions start..; returns (argmax of the
+        last position, its logits or None).  With max_batch > 1 the positions
+        before the last run up to 8 per launch."""
         h = self._live()
         ids = np.ascontiguousarray(ids, np.int32)
         out = np.empty(self.vocab, np.float32) if logits else None

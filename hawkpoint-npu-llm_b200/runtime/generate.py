@@ -105,7 +105,8 @@ class NPUDecoder:
         device = int(os.environ.get("HAWKPOINT_DEVICE", "0"))
         from runtime.b200_engine import B200DecoderEngine
 
-        self._engine = B200DecoderEngine(self.model, weights=weights, device=device)
+        # max_batch 8: prompts are prefilled up to 8 positions per launch
+        self._engine = B200DecoderEngine(self.model, weights=weights, device=device, max_batch=8)
         self.weights = weights
         self._qwen_embedding_cache = OrderedDict()  # kept for attribute compatibility
 
@@ -187,6 +188,18 @@ class NPUDecoder:
                 break
             shared += 1
         return min(shared, len(prompt_ids) - 1)
+
+    def _prefill_positions(self, prompt_ids, start, end):
+        """Run positions [start, end) through the engine's batched prefill;
+        returns one timing per position (the batch time shared evenly).  On
+        failure the cached prefix keeps only positions before `start`."""
+        del self._cached_prefix[start:]
+        began = time.perf_counter()
+        self._engine.prefill([int(t) for t in prompt_ids[start:end]], start=start)
+        elapsed = time.perf_counter() - began
+        self._cached_prefix.extend(int(t) for t in prompt_ids[start:end])
+        self._record_phase("prefill", began)
+        return [elapsed / (end - start)] * (end - start)
 
     def _decode_step(self, token_id, position, **kwargs):
         del self._cached_prefix[position:]
@@ -303,7 +316,13 @@ class NPUDecoder:
         timings = []
         token = None
         last = len(prompt_ids) - 1
-        for index in range(reused, len(prompt_ids)):
+        if last > reused and getattr(self, "_engine", None) is not None:
+            # positions [reused, last) need no logits: batched prefill launches
+            timings.extend(self._prefill_positions(prompt_ids, reused, last))
+            first = last
+        else:
+            first = reused
+        for index in range(first, len(prompt_ids)):
             token, elapsed = self._decode_step(
                 prompt_ids[index], index,
                 select=select if index == last else None,

@@ -7,6 +7,7 @@ prefix cache (:267-311), a failing step (:313-331) and stop strings."""
 import types
 
 import numpy as np
+import pytest
 
 from runtime.generate import NPUDecoder
 
@@ -175,3 +176,31 @@ def test_invalid_arguments():
         run(decoder, max_new_tokens=64)
     with pytest.raises(ValueError):
         NPUDecoder(object(), context_length=32)
+
+
+@pytest.mark.gpu
+def test_drop_in_batched_prompt_prefill_on_gpu():
+    """On the real engine the drop-in prefills the uncached prompt positions
+    through batched launches; the tokens equal single-stream generation and
+    the prefix cache is reused on a repeated prompt."""
+    from runtime import synthetic
+    from runtime.b200_engine import B200DecoderEngine
+
+    model = synthetic.build("tiny-qwen", seed=41)
+    prompt = synthetic.prompt_ids(model.shape.vocab, 19, seed=3)
+    decoder = NPUDecoder(model)
+    try:
+        decoder.tokenizer = FakeTokenizer(prompt)
+        decoder.tokenizer.eos_id = -1
+        _, stats = run(decoder, max_new_tokens=6)
+        _, again = run(decoder, max_new_tokens=6)
+    finally:
+        decoder.close()
+    single = B200DecoderEngine(model, max_batch=1)
+    try:
+        ref = single.generate(prompt, 6)
+    finally:
+        single.close()
+    assert stats["generated_token_ids"] == ref
+    assert again["generated_token_ids"] == ref
+    assert again["cached_prompt_tokens"] == len(prompt) - 1
