@@ -107,9 +107,11 @@ int hb_destroy(hb_engine *engine);
 int hb_step(hb_engine *engine, int slot, int token_id, int position, int flags,
             float *logits_out, int32_t *argmax_out);
 
-/* Sequential prefill of n prompt positions start_pos..start_pos+n-1, one
- * engine step each, only the last with the LM head -- the loop of
- * npu_llm/runtime/generate.py:1110-1126.  last_logits may be NULL. */
+/* Prefill of n prompt positions start_pos..start_pos+n-1, only the last
+ * with the LM head -- the loop of npu_llm/runtime/generate.py:1110-1126.
+ * With max_batch > 1 the positions before the last run up to 8 per launch
+ * (same KV cache and result as one position per launch).  last_logits may
+ * be NULL. */
 int hb_prefill(hb_engine *engine, int slot, const int32_t *ids, int n,
                int start_pos, float *last_logits, int32_t *argmax_out);
 
