@@ -38,7 +38,7 @@ namespace hb {
 
 constexpr int kMaxBatch = 8;
 constexpr int kHeadDim = 64;
-constexpr int kMaxHPerThread = 4;  // hidden <= 1024
+constexpr int kMaxHPerThread = 6;  // hidden <= 6 * 224 = 1344
 
 struct LayerPtrs {
   const float *gamma_in, *gamma_post, *bias;
@@ -177,7 +177,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 template <class Sink>
 __device__ __forceinline__ bool ll_gather(const uint64_t *src, size_t row_words, int words, int rows,
                                           uint32_t epoch, Ctrl *ctrl, uint64_t limit_ns, Sink &&sink) {
-  // Word i of row m (at src + m * row_words + i) goes to thread i % 256 for
+  // Word i of row m (at src + m * row_words + i) goes to thread i % kConsumerThreads for
   // every row, so a thread owns the same columns of each row; all rows are
   // polled together, up to U words per thread in flight.
   const int tid = threadIdx.x;
@@ -605,10 +605,11 @@ struct DecoderCta {
       uint8_t *dst = reinterpret_cast<uint8_t *>(kv_block(s_slot[m], layer, j, kind)) + kv_off(p, cb);
       *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(srow);
     }
-    // scores: warp w takes positions 8w..8w+7, four lanes per position
-    {
-      const int warp = tid >> 5, lane = tid & 31;
-      const int sp = 8 * warp + (lane >> 2), qd = lane & 3;
+    // scores: groups of 8 positions per warp (8w..8w+7, then + 8 * kWarps),
+    // four lanes per position
+    for (int sp0 = 8 * (tid >> 5); sp0 <= p; sp0 += 8 * kWarps) {
+      const int lane = tid & 31;
+      const int sp = sp0 + (lane >> 2), qd = lane & 3;
       float acc = 0.f;
       if (sp <= p) {
 #pragma unroll
@@ -646,9 +647,9 @@ struct DecoderCta {
       sc[lane + 32] = __fdiv_rn(e1, sum);
     }
     consumer_sync(kConsumerThreads);
-    // P.V: thread (dim d, position quarter pg)
-    {
-      const int d = tid & 63, pg = tid >> 6;
+    // P.V: work item (dim d, position quarter pg)
+    for (int item = tid; item < 256; item += kConsumerThreads) {
+      const int d = item & 63, pg = item >> 6;
       const int s0 = pg * 16, s1 = min(s0 + 15, p);
       float acc = 0.f;
       for (int sp = s0; sp <= s1; ++sp)

@@ -22,7 +22,7 @@
 
 namespace hb {
 
-constexpr int kWarps = 8;                  // consumer warps
+constexpr int kWarps = 7;                  // consumer warps
 constexpr int kConsumerThreads = kWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;  // + producer warp
 constexpr uint32_t kSlotBytes = 16384;
