@@ -11,6 +11,9 @@ where a request runs:
   npu_llm/runtime/generate.py:952-973);
 * **balance** -- groups are placed longest-first on the least-loaded rank
   (load = prompt positions + tokens to generate), ties to the lowest rank.
+  A prefix group heavier than one rank's fair share is first cut into
+  pieces no heavier than that share (members dealt round-robin); each piece
+  computes the shared prefix once on its own rank.
 
 The assignment is a pure function of the request list, so every rank computes
 the same partition without communicating.
@@ -46,9 +49,16 @@ def assign_ranks(prompts, world, new_tokens, prefix_tokens=16):
     groups = OrderedDict()
     for i, ids in enumerate(prompts):
         groups.setdefault(prefix_key(ids, prefix_tokens, i), []).append(i)
+    loads_of = [request_load(prompts[i], budgets[i]) for i in range(n)]
+    share = sum(loads_of) / world
+    pieces = []
+    for members in groups.values():
+        load = sum(loads_of[i] for i in members)
+        k = max(1, min(len(members), -(-int(load) // max(1, int(share))))) if load > share else 1
+        pieces.extend(members[j::k] for j in range(k))
     weighted = []
-    for order, members in enumerate(groups.values()):
-        load = sum(request_load(prompts[i], budgets[i]) for i in members)
+    for order, members in enumerate(pieces):
+        load = sum(loads_of[i] for i in members)
         weighted.append((-load, order, members))
     weighted.sort()
     loads = [0] * world

@@ -40,9 +40,15 @@ def test_every_request_lands_on_exactly_one_rank():
 
 def test_shared_prefix_requests_stay_together():
     prompts = workload()
-    ranks = dispatch.assign_ranks(prompts, 4, 16)
+    ranks = dispatch.assign_ranks(prompts, 2, 16)
     shared = [i for i in range(len(prompts)) if i % 4 == 0]
     assert len({ranks[i] for i in shared}) == 1
+    # a group heavier than one rank's share is cut into as few pieces as
+    # fit the share (here: 16 of 64 requests, 8 ranks)
+    ranks8 = dispatch.assign_ranks(prompts, 8, 16)
+    total = sum(dispatch.request_load(p, 16) for p in prompts)
+    group = sum(dispatch.request_load(prompts[i], 16) for i in shared)
+    assert len({ranks8[i] for i in shared}) == -(-group // int(total / 8))
     # a prompt no longer than the prefix has nothing to reuse: its own group
     assert dispatch.prefix_key(prompts[0][:16], 16, 0) == ("single", 0)
 
