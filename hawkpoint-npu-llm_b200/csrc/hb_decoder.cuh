@@ -545,128 +545,109 @@ struct DecoderCta {
   // One unit: RoPE (rotate-half, unfused mul/add, BF16), K/V append, scores
   // q.k * 0.125 over positions <= p, softmax (max-subtract, exp, divide),
   // P.V in FP32; publishes bf16 outputs to ll_att(layer, m) + h * 32.
+  // Called by every consumer thread (one block barrier publishes the
+  // cp.async history); warp 0 does the work -- one head is a few thousand
+  // FMAs, so block barriers would cost more than the math.
   __device__ void attention_unit(int layer, int m, int h, int j, uint32_t *u96) {
     const int p = s_pos[m];
     float *qf = reinterpret_cast<float *>(u96 + 96);
     float *sc = qf + kHeadDim;
-    float *part = sc + kHeadDim;
     uint8_t *kb = kvs, *vb = kvs + static_cast<size_t>(P.CTX) * 128;
-    // RoPE'd q and k, raw v of row m into qf and the K / V rows at p
-    if (tid < 64) {
-      const int d = tid & 31, seg = tid >> 5;  // 0: q, 1: k
-      auto el = [&](int e) {
-        const uint32_t w = u96[seg * 32 + (e >> 1)];
-        return (e & 1) ? bf_hi(w) : bf_lo(w);
-      };
-      const float c = P.rope_cos[p * 32 + d], sn = P.rope_sin[p * 32 + d];
-      const float x0 = el(d), x1 = el(d + 32);
-      const __nv_bfloat16 lo = f2bf(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
-      const __nv_bfloat16 hi = f2bf(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
-      if (seg == 0) {
-        qf[d] = bf2f(lo);
-        qf[d + 32] = bf2f(hi);
-      } else {
-        *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(p, d >> 3) + (d & 7) * 2) = lo;
-        *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(p, 4 + (d >> 3)) + (d & 7) * 2) = hi;
-      }
-    } else if (tid < 96) {
-      const int w = tid - 64;  // v dims 2w, 2w+1 (raw)
-      *reinterpret_cast<uint32_t *>(vb + kv_off(p, (2 * w) >> 3) + ((2 * w) & 7) * 2) = u96[64 + w];
-    }
-    // batched prefill: RoPE'd k and raw v of the earlier rows of the run
-    const int f = run_start(m);
-    for (int t = tid; t < 64 * (m - f); t += kConsumerThreads) {
-      const int r = t >> 6, i = t & 63;
-      const int pr = s_pos[f + r];
-      const uint32_t *words = u96 + kUnitWords + 64 * r;  // k words [0, 32), v words [32, 64)
-      if (i < 32) {
-        const int d = i;
-        auto el = [&](int e) {
-          const uint32_t w = words[e >> 1];
-          return (e & 1) ? bf_hi(w) : bf_lo(w);
-        };
-        const float c = P.rope_cos[pr * 32 + d], sn = P.rope_sin[pr * 32 + d];
-        const float x0 = el(d), x1 = el(d + 32);
-        *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(pr, d >> 3) + (d & 7) * 2) =
-            f2bf(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
-        *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(pr, 4 + (d >> 3)) + (d & 7) * 2) =
-            f2bf(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
-      } else {
-        const int w = i - 32;
-        *reinterpret_cast<uint32_t *>(vb + kv_off(pr, (2 * w) >> 3) + ((2 * w) & 7) * 2) = words[32 + w];
-      }
-    }
     cp_async_wait_all();
-    consumer_sync(kConsumerThreads);
+    consumer_sync(kConsumerThreads);  // every thread's history copies (and u96) are visible
+    if (tid >= 32) return;
+    const int lane = tid;
+    auto rope_pair = [&](const uint32_t *w32, int pr, int d, __nv_bfloat16 &lo, __nv_bfloat16 &hi) {
+      // elements d and d + 32 of the 64 held as BF16 pairs in w32[0..32)
+      const uint32_t a = w32[d >> 1], b = w32[(d + 32) >> 1];
+      const float x0 = (d & 1) ? bf_hi(a) : bf_lo(a), x1 = (d & 1) ? bf_hi(b) : bf_lo(b);
+      const float c = P.rope_cos[pr * 32 + d], sn = P.rope_sin[pr * 32 + d];
+      lo = f2bf(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+      hi = f2bf(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
+    };
+    auto put_kv = [&](int pr, int d, __nv_bfloat16 klo, __nv_bfloat16 khi, uint32_t vword) {
+      *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(pr, d >> 3) + (d & 7) * 2) = klo;
+      *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(pr, 4 + (d >> 3)) + (d & 7) * 2) = khi;
+      *reinterpret_cast<uint32_t *>(vb + kv_off(pr, (2 * d) >> 3) + ((2 * d) & 7) * 2) = vword;
+    };
+    {
+      __nv_bfloat16 lo, hi;
+      rope_pair(u96, p, lane, lo, hi);  // q
+      qf[lane] = bf2f(lo);
+      qf[lane + 32] = bf2f(hi);
+      rope_pair(u96 + 32, p, lane, lo, hi);  // k
+      put_kv(p, lane, lo, hi, u96[64 + lane]);
+      // batched prefill: k and v of the earlier rows of the run
+      const int f = run_start(m);
+      for (int r = f; r < m; ++r) {
+        const uint32_t *w = u96 + kUnitWords + 64 * (r - f);
+        rope_pair(w, s_pos[r], lane, lo, hi);
+        put_kv(s_pos[r], lane, lo, hi, w[32 + lane]);
+      }
+    }
+    __syncwarp();
     // the first q head of kv group j appends row p of K and V to the cache
-    if (h % P.group == 0 && tid < 16) {
-      const int kind = tid >> 3, cb = tid & 7;
+    if (h % P.group == 0 && lane < 16) {
+      const int kind = lane >> 3, cb = lane & 7;
       const uint8_t *srow = (kind ? vb : kb) + kv_off(p, cb);
       uint8_t *dst = reinterpret_cast<uint8_t *>(kv_block(s_slot[m], layer, j, kind)) + kv_off(p, cb);
       *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(srow);
     }
-    // scores: groups of 8 positions per warp (8w..8w+7, then + 8 * kWarps),
-    // four lanes per position
-    for (int sp0 = 8 * (tid >> 5); sp0 <= p; sp0 += 8 * kWarps) {
-      const int lane = tid & 31;
-      const int sp = sp0 + (lane >> 2), qd = lane & 3;
-      float acc = 0.f;
+    // scores: lane takes positions lane and lane + 32
+    float s2[2];  // (indexed by unrolled e only)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int sp = lane + 32 * e;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
       if (sp <= p) {
 #pragma unroll
-        for (int b = 0; b < 2; ++b) {
-          const uint4 kw = *reinterpret_cast<const uint4 *>(kb + kv_off(sp, 2 * qd + b));
-          const float *q = qf + 16 * qd + 8 * b;
-          acc = fmaf(bf_lo(kw.x), q[0], acc);
-          acc = fmaf(bf_hi(kw.x), q[1], acc);
-          acc = fmaf(bf_lo(kw.y), q[2], acc);
-          acc = fmaf(bf_hi(kw.y), q[3], acc);
-          acc = fmaf(bf_lo(kw.z), q[4], acc);
-          acc = fmaf(bf_hi(kw.z), q[5], acc);
-          acc = fmaf(bf_lo(kw.w), q[6], acc);
-          acc = fmaf(bf_hi(kw.w), q[7], acc);
+        for (int cb = 0; cb < 8; ++cb) {
+          const uint4 kw = *reinterpret_cast<const uint4 *>(kb + kv_off(sp, cb));
+          const float *q = qf + 8 * cb;
+          float &a = acc[cb & 3];
+          a = fmaf(bf_lo(kw.x), q[0], a);
+          a = fmaf(bf_hi(kw.x), q[1], a);
+          a = fmaf(bf_lo(kw.y), q[2], a);
+          a = fmaf(bf_hi(kw.y), q[3], a);
+          a = fmaf(bf_lo(kw.z), q[4], a);
+          a = fmaf(bf_hi(kw.z), q[5], a);
+          a = fmaf(bf_lo(kw.w), q[6], a);
+          a = fmaf(bf_hi(kw.w), q[7], a);
         }
       }
-      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-      if (qd == 0 && sp < kHeadDim) sc[sp] = acc * 0.125f;
+      s2[e] = sp <= p ? ((acc[0] + acc[1]) + (acc[2] + acc[3])) * 0.125f : -INFINITY;
     }
-    consumer_sync(kConsumerThreads);
-    if (tid < 32) {
-      const int lane = tid;
-      const bool in0 = lane <= p, in1 = lane + 32 <= p;
-      const float s0 = in0 ? sc[lane] : -INFINITY, s1 = in1 ? sc[lane + 32] : -INFINITY;
-      float mx = fmaxf(s0, s1);
+    float mx = fmaxf(s2[0], s2[1]);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float e0 = in0 ? expf(__fsub_rn(s0, mx)) : 0.f;
-      const float e1 = in1 ? expf(__fsub_rn(s1, mx)) : 0.f;
-      float sum = e0 + e1;
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float e0 = lane <= p ? expf(__fsub_rn(s2[0], mx)) : 0.f;
+    const float e1 = lane + 32 <= p ? expf(__fsub_rn(s2[1], mx)) : 0.f;
+    float sum = e0 + e1;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      sc[lane] = __fdiv_rn(e0, sum);
-      sc[lane + 32] = __fdiv_rn(e1, sum);
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    sc[lane] = __fdiv_rn(e0, sum);
+    sc[lane + 32] = __fdiv_rn(e1, sum);
+    __syncwarp();
+    // P.V: lane takes dims 2*lane, 2*lane+1; two chains over even / odd positions
+    float o00 = 0.f, o01 = 0.f, o10 = 0.f, o11 = 0.f;
+    const int cbv = (2 * lane) >> 3, offv = ((2 * lane) & 7) * 2;
+    int sp = 0;
+    for (; sp + 1 <= p; sp += 2) {
+      const float w0 = sc[sp], w1 = sc[sp + 1];
+      const uint32_t v0 = *reinterpret_cast<const uint32_t *>(vb + kv_off(sp, cbv) + offv);
+      const uint32_t v1 = *reinterpret_cast<const uint32_t *>(vb + kv_off(sp + 1, cbv) + offv);
+      o00 = fmaf(w0, bf_lo(v0), o00);
+      o01 = fmaf(w0, bf_hi(v0), o01);
+      o10 = fmaf(w1, bf_lo(v1), o10);
+      o11 = fmaf(w1, bf_hi(v1), o11);
     }
-    consumer_sync(kConsumerThreads);
-    // P.V: work item (dim d, position quarter pg)
-    for (int item = tid; item < 256; item += kConsumerThreads) {
-      const int d = item & 63, pg = item >> 6;
-      const int s0 = pg * 16, s1 = min(s0 + 15, p);
-      float acc = 0.f;
-      for (int sp = s0; sp <= s1; ++sp)
-        acc = fmaf(sc[sp], bf2f(*reinterpret_cast<const __nv_bfloat16 *>(vb + kv_off(sp, d >> 3) + (d & 7) * 2)),
-                   acc);
-      part[pg * 64 + d] = acc;
+    if (sp <= p) {
+      const float w0 = sc[sp];
+      const uint32_t v0 = *reinterpret_cast<const uint32_t *>(vb + kv_off(sp, cbv) + offv);
+      o00 = fmaf(w0, bf_lo(v0), o00);
+      o01 = fmaf(w0, bf_hi(v0), o01);
     }
-    consumer_sync(kConsumerThreads);
-    if (tid < 32) {
-      float o[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int d = 2 * tid + e;
-        o[e] = (part[d] + part[64 + d]) + (part[128 + d] + part[192 + d]);
-      }
-      ll_store(ll_att(layer, m) + h * 32 + tid, pack_bf16x2(o[0], o[1]), epoch);
-    }
+    ll_store(ll_att(layer, m) + h * 32 + lane, pack_bf16x2(o00 + o10, o01 + o11), epoch);
   }
 
   // One phase of a layer (kind = k & 3: 0 qkv, 1 attention + o_proj,
@@ -714,7 +695,8 @@ struct DecoderCta {
       ok = gather_raw(ll_act(layer, 0), P.I / 2, P.I / 2, reinterpret_cast<uint32_t *>(xs), P.xs_elems / 2);
     }
     if (!ok) return false;
-    if (kind == 1 || kind == 3) consumer_sync(kConsumerThreads);  // read across threads next
+    // act is read across threads next (the attention unit synchronizes itself)
+    if (kind == 3) consumer_sync(kConsumerThreads);
     mark(k, 1);
     if (kind == 0 || kind == 2) {
       norm_rows(gamma);
