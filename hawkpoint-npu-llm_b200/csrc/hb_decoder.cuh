@@ -38,7 +38,7 @@ namespace hb {
 
 constexpr int kMaxBatch = 8;
 constexpr int kHeadDim = 64;
-constexpr int kMaxHPerThread = 6;  // hidden <= 6 * 224 = 1344
+constexpr int kMaxHPerThread = 8;  // hidden <= 8 * 224 = 1792 (two word pairs per thread)
 
 struct LayerPtrs {
   const float *gamma_in, *gamma_post, *bias;
@@ -166,49 +166,62 @@ __device__ __forceinline__ uint64_t ll_load(const uint64_t *p) {
   return v;
 }
 
+// Two adjacent LL words in one 16-byte load (p 16-byte aligned).  Each
+// 8-byte half is read whole, so each word's payload and epoch still agree;
+// the two halves may come from different epochs and are checked apart.
+__device__ __forceinline__ void ll_load2(const uint64_t *p, uint64_t &a, uint64_t &b) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   const uint32_t a = __bfloat16_as_ushort(f2bf(lo));
   const uint32_t b = __bfloat16_as_ushort(f2bf(hi));
   return a | (b << 16);
 }
 
-// All consumer threads: wait until words [0, n) of src carry `epoch`, and
-// pass each payload to sink(i, payload).  Up to 8 loads in flight per thread.
-template <class Sink>
+// All consumer threads: wait until words [0, words) of each of `rows` rows
+// (row m at src + m * row_words) carry `epoch`, and pass each payload to
+// sink(m, word, payload).  Words travel in aligned pairs, one 16-byte load
+// per pair (words even and < 65536, row_words even, src 16-byte aligned): pair p of every
+// row goes to thread p % kConsumerThreads, so a thread owns the same words
+// (2p, 2p + 1) of each row.  All rows are polled together, up to U pairs per
+// thread in flight: 4 for one row (8 words, as many as the decode kernel's
+// register budget affords without slowing its GEMV loops), 8 for 8 rows,
+// where the deeper queue halves the rounds of the 8 x 4864 activation gather.
+template <int U, class Sink>
 __device__ __forceinline__ bool ll_gather(const uint64_t *src, size_t row_words, int words, int rows,
                                           uint32_t epoch, Ctrl *ctrl, uint64_t limit_ns, Sink &&sink) {
-  // Word i of row m (at src + m * row_words + i) goes to thread i % kConsumerThreads for
-  // every row, so a thread owns the same columns of each row; all rows are
-  // polled together, up to U words per thread in flight.
   const int tid = threadIdx.x;
-  constexpr int U = 8;
-  const int per_row = (words + kConsumerThreads - 1) / kConsumerThreads;  // words per thread and row
+  const int pairs = words >> 1;
+  const int per_row = (pairs + kConsumerThreads - 1) / kConsumerThreads;  // pairs per thread and row
   const int total = rows * per_row;
   for (int base = 0; base < total; base += U) {
-    uint32_t pend = 0;
-    const uint64_t *addr[U];
-    int col[U], row[U];
+    uint32_t pend = 0;  // bits 2u and 2u + 1: the two words of slot u
+    int rc[U];          // (row << 16) | first word of the pair
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int e = base + u;
       const int m = e / per_row, k = e - m * per_row;
-      row[u] = m;
-      col[u] = tid + k * kConsumerThreads;
-      addr[u] = src + m * row_words + col[u];
-      if (e < total && col[u] < words) pend |= 1u << u;
+      const int col = 2 * (tid + k * kConsumerThreads);
+      rc[u] = (m << 16) | (col & 0xffff);
+      if (e < total && col < words) pend |= 3u << (2 * u);
     }
     uint64_t start = 0;
     uint32_t spins = 0;
     while (pend) {
-      uint64_t v[U];
+      uint64_t v0[U], v1[U];
 #pragma unroll
       for (int u = 0; u < U; ++u)
-        if (pend & (1u << u)) v[u] = ll_load(addr[u]);
+        if (pend & (3u << (2 * u))) ll_load2(src + (rc[u] >> 16) * row_words + (rc[u] & 0xffff), v0[u], v1[u]);
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        if ((pend & (1u << u)) && static_cast<uint32_t>(v[u] >> 32) == epoch) {
-          sink(row[u], col[u], static_cast<uint32_t>(v[u]));
-          pend &= ~(1u << u);
+        if ((pend & (1u << (2 * u))) && static_cast<uint32_t>(v0[u] >> 32) == epoch) {
+          sink(rc[u] >> 16, rc[u] & 0xffff, static_cast<uint32_t>(v0[u]));
+          pend &= ~(1u << (2 * u));
+        }
+        if ((pend & (2u << (2 * u))) && static_cast<uint32_t>(v1[u] >> 32) == epoch) {
+          sink(rc[u] >> 16, (rc[u] & 0xffff) + 1, static_cast<uint32_t>(v1[u]));
+          pend &= ~(2u << (2 * u));
         }
       }
       if (pend) {
@@ -333,9 +346,12 @@ struct DecoderCta {
 
   // ---- helpers -------------------------------------------------------------------
   // Per-thread registers of a norm weight vector: the thread owns the
-  // hidden-vector words (element pairs) tid + kConsumerThreads * j, the same
-  // words ll_gather hands it, so gather and norm need no barrier between them.
+  // hidden-vector words (element pairs) 2p and 2p + 1 of the word pairs
+  // p = tid + kConsumerThreads * j, the same words ll_gather hands it, so
+  // gather and norm need no barrier between them.  Word n of the thread is
+  // word 2 (tid + kConsumerThreads (n / 2)) + n % 2 of the row.
   static constexpr int kNormWords = kMaxHPerThread / 2;
+  __device__ __forceinline__ int norm_word(int n) const { return 2 * (tid + (n >> 1) * kConsumerThreads) + (n & 1); }
   struct Gamma {
     float v[kMaxHPerThread];
   };
@@ -343,7 +359,7 @@ struct DecoderCta {
     Gamma r;
 #pragma unroll
     for (int j = 0; j < kNormWords; ++j) {
-      const int w = tid + j * kConsumerThreads;
+      const int w = norm_word(j);
       const bool in = 2 * w < P.H;
       r.v[2 * j] = in ? g[2 * w] : 0.f;
       r.v[2 * j + 1] = in ? g[2 * w + 1] : 0.f;
@@ -371,7 +387,7 @@ struct DecoderCta {
       float ss = 0.f;
 #pragma unroll
       for (int j = 0; j < kNormWords; ++j) {
-        const int w = tid + j * kConsumerThreads;
+        const int w = norm_word(j);
         if (2 * w < P.H) {
           const uint32_t hw = reinterpret_cast<const uint32_t *>(hx + m * P.H)[w];
           const float a = bf_lo(hw), b = bf_hi(hw);
@@ -391,7 +407,7 @@ struct DecoderCta {
       const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, P.eps)));
 #pragma unroll
       for (int j = 0; j < kNormWords; ++j) {
-        const int w = tid + j * kConsumerThreads;
+        const int w = norm_word(j);
         if (2 * w < P.H) {
           const uint32_t hw = reinterpret_cast<const uint32_t *>(hx + m * P.H)[w];
           const float a = __fmul_rn(__fmul_rn(bf_lo(hw), inv), gamma.v[2 * j]);
@@ -419,7 +435,7 @@ struct DecoderCta {
   // Raw payloads of the LL words (BF16 pairs) into dst[m * dst_words + i].
   __device__ bool gather_raw(const uint64_t *src, size_t row_words, int words, uint32_t *dst,
                                           size_t dst_words) {
-    return ll_gather(src, row_words, words, mrows, epoch, &P.result->ctrl, P.limit_ns,
+    return ll_gather<(MB > 1 ? 8 : 4)>(src, row_words, words, mrows, epoch, &P.result->ctrl, P.limit_ns,
                      [&](int m, int i, uint32_t d) { dst[m * dst_words + i] = d; });
   }
 
@@ -673,11 +689,12 @@ struct DecoderCta {
     bool ok = true;
     if (kind == 0) {
       if (layer == 0) {
-        // the embedding row (generate.py:758-768), same word ownership as the gather
+        // the embedding row (generate.py:758-768), same word-pair ownership
+        // as the gather (the norm reads these words next without a barrier)
         for (int m = 0; m < mrows; ++m) {
-          const uint32_t *e = reinterpret_cast<const uint32_t *>(P.embed + static_cast<size_t>(s_tok[m]) * P.H);
-          for (int w = tid; w < P.H / 2; w += kConsumerThreads) {
-            reinterpret_cast<uint32_t *>(hx + m * P.H)[w] = __ldg(e + w);
+          const uint2 *e = reinterpret_cast<const uint2 *>(P.embed + static_cast<size_t>(s_tok[m]) * P.H);
+          for (int w = tid; w < P.H / 4; w += kConsumerThreads) {
+            reinterpret_cast<uint2 *>(hx + m * P.H)[w] = __ldg(e + w);
           }
         }
       } else {
@@ -764,7 +781,9 @@ struct DecoderCta {
     const int warp = tid >> 5, lane = tid & 31;
     const Gamma gamma = load_gamma(P.gamma_final);
     if (!gather_to_hx(ll_hout(P.L - 1, 0), P.H / 2, P.H)) return false;
+    mark(4 * P.L, 1);
     norm_rows(gamma);
+    mark(4 * P.L, 6);
     float bv[MB];
     int bi[MB];
 #pragma unroll
@@ -781,11 +800,12 @@ struct DecoderCta {
         ring, r, xs, P.xs_elems, mrows, &P.result->ctrl, P.limit_ns, [&](int m, int row, float v) {
           if (W8) v *= s_lm[row];
           if (write) logits[static_cast<size_t>(m) * V + row] = v;
-          if (v > bv[m] || (v == bv[m] && row < bi[m])) {
+          if (argmax_better(v, row, bv[m], bi[m])) {
             bv[m] = v;
             bi[m] = row;
           }
         });
+    mark(4 * P.L, 2);
 #pragma unroll
     for (int m = 0; m < MB; ++m) {
       float v = bv[m];
@@ -879,14 +899,20 @@ struct DecoderCta {
         if (st->chained && ld_volatile_int(&ctrl->abort) == 0) {
           const int p = st->pos[0];
           int next = (p + 1 < st->n_prompt) ? P.prompt[p + 1] : -1;
-          if (ran_head) {
-            const int tok = P.result->out_token[0];
-            P.gen_out[st->n_out] = tok;
-            st->n_out = st->n_out + 1;
-            if (next < 0) next = tok;
+          const int tok = ran_head ? P.result->out_token[0] : 0;
+          if (tok < 0 || tok >= P.V) {
+            // the next launch would read this row of the embedding: stop the
+            // chain instead (unreachable while the argmax offers every row)
+            raise_error(ctrl, kErrBadToken, kWhereToken);
+          } else {
+            if (ran_head) {
+              P.gen_out[st->n_out] = tok;
+              st->n_out = st->n_out + 1;
+              if (next < 0) next = tok;
+            }
+            st->token[0] = next < 0 ? 0 : next;
+            st->pos[0] = p + 1;
           }
-          st->token[0] = next < 0 ? 0 : next;
-          st->pos[0] = p + 1;
         }
         unsigned int ne = *P.epoch + 1u;
         if (ne == 0u) ne = 1u;

@@ -28,6 +28,7 @@ struct Ctrl {
 enum : int {
   kErrNone = 0,
   kErrTimeout = 1,
+  kErrBadToken = 2,  // a device-chained token id fell outside the vocabulary
 };
 
 enum : int {
@@ -36,6 +37,7 @@ enum : int {
   kWhereGrid = 3,
   kWhereStall = 4,
   kWhereDrain = 5,
+  kWhereToken = 6,
 };
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -286,9 +288,18 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// (value, index) argmax with the first index winning ties (np.argmax).
+// Selection order of np.argmax (generate.py:713): a NaN ranks above every
+// number, and among equal values (or NaNs) the lower index wins.  So the
+// selected index is always one that was offered, whatever the values.
+__device__ __forceinline__ bool argmax_better(float v, int i, float bv, int bi) {
+  const bool vn = isnan(v), bn = isnan(bv);
+  if (vn || bn) return vn && (!bn || i < bi);
+  return v > bv || (v == bv && i < bi);
+}
+
+// (value, index) argmax merge in that order.
 __device__ __forceinline__ void argmax_merge(float &v, int &i, float ov, int oi) {
-  if (ov > v || (ov == v && oi < i)) {
+  if (argmax_better(ov, oi, v, i)) {
     v = ov;
     i = oi;
   }

@@ -284,11 +284,14 @@ int finish(hb_engine *e) {
   HB_CUDA(e, cudaMemcpyAsync(e->h_result, e->d_result, sizeof(hb::Result), cudaMemcpyDeviceToHost, e->stream));
   HB_CUDA(e, cudaStreamSynchronize(e->stream));
   if (e->h_result->ctrl.err != 0) {
+    const int code = e->h_result->ctrl.err;
     const int where = e->h_result->ctrl.err_where;
     // words of the aborted launch may carry the current epoch: clear them all
     HB_CUDA(e, cudaMemsetAsync(e->d_ll, 0, e->ll_words * 8, e->stream));
     HB_CUDA(e, cudaMemsetAsync(e->d_result, 0, sizeof(hb::Result), e->stream));
     HB_CUDA(e, cudaStreamSynchronize(e->stream));
+    if (code == hb::kErrBadToken)
+      return fail(e, HB_ERR_STATE, "device-chained token id outside the vocabulary; engine state reset");
     static const char *names[] = {"?", "weight chunk", "ring slot", "grid barrier", "test stall flag", "drain"};
     return fail(e, HB_ERR_DEVICE_TIMEOUT, "device wait on %s timed out; engine state reset",
                 names[(where >= 0 && where <= 5) ? where : 0]);

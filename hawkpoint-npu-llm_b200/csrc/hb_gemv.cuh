@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
       reinterpret_cast<__nv_bfloat16 *>(P.y)[static_cast<size_t>(m) * P.rows + row] = f2bf(v);
     else if (P.out_mode == 1)
       reinterpret_cast<float *>(P.y)[static_cast<size_t>(m) * P.rows + row] = v;
-    if (v > bv[m] || (v == bv[m] && row < bi[m])) {
+    if (argmax_better(v, row, bv[m], bi[m])) {
       bv[m] = v;
       bi[m] = row;
     }

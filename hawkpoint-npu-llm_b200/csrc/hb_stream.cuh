@@ -176,34 +176,6 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ void ldsm_x2_trans(uint32_t (&r)[2], uint32_t addr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
-               : "=r"(r[0]), "=r"(r[1])
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void mma_16816_full(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                               uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-// Two FP32 values as three packed BF16 pairs whose per-element sums
-// hi + mid + lo carry every mantissa bit of the inputs.
-__device__ __forceinline__ void split3_pack(float x, float y, uint32_t &hi, uint32_t &mid, uint32_t &lo) {
-  const __nv_bfloat16 xh = __float2bfloat16_rn(x), yh = __float2bfloat16_rn(y);
-  const float xr = x - __bfloat162float(xh), yr = y - __bfloat162float(yh);
-  const __nv_bfloat16 xm = __float2bfloat16_rn(xr), ym = __float2bfloat16_rn(yr);
-  const __nv_bfloat16 xl = __float2bfloat16_rn(xr - __bfloat162float(xm));
-  const __nv_bfloat16 yl = __float2bfloat16_rn(yr - __bfloat162float(ym));
-  hi = static_cast<uint32_t>(__bfloat16_as_ushort(xh)) | (static_cast<uint32_t>(__bfloat16_as_ushort(yh)) << 16);
-  mid = static_cast<uint32_t>(__bfloat16_as_ushort(xm)) | (static_cast<uint32_t>(__bfloat16_as_ushort(ym)) << 16);
-  lo = static_cast<uint32_t>(__bfloat16_as_ushort(xl)) | (static_cast<uint32_t>(__bfloat16_as_ushort(yl)) << 16);
-}
-
 // Accumulate the dot products of one row group over chunk columns
 // [jc_begin, jc_end) stepping by `stride` (multiples of 4): 4 chunk columns
 // = 2 k16 steps per iteration.  `sg` = the group's bytes in shared memory,
@@ -450,11 +422,13 @@ __device__ __forceinline__ bool consume_chunk_per_warp(Ring &ring, const MatRang
           const __nv_bfloat16 *xrow = m < mrows ? xs + static_cast<size_t>(m) * K : nullptr;
           mma_group(d0, sg, xrow, col0, 0, ncols, 8);
           mma_group(d1, sg, xrow, col0, 4, ncols, 8);
+          const float v0 = d0[0] + d1[0];
+          const float v1 = d0[1] + d1[1];
 #pragma unroll
           for (int mm = 0; mm < MB; ++mm) {
             if (mm == m && m < mrows) {  // compile-time batch index for the callback
-              on_row(mm, (g + q) * 8 + (lane & 3) * 2, d0[0] + d1[0]);
-              on_row(mm, (g + q) * 8 + (lane & 3) * 2 + 1, d0[1] + d1[1]);
+              on_row(mm, (g + q) * 8 + (lane & 3) * 2, v0);
+              on_row(mm, (g + q) * 8 + (lane & 3) * 2 + 1, v1);
             }
           }
         } else {

@@ -15,7 +15,10 @@
  * device memory; the caller owns host buffers.  Pointers named *_dev are device
  * pointers; all others are host pointers.  Device-side waits are bounded in
  * time; a wait that runs out makes the call return HB_ERR_DEVICE_TIMEOUT and
- * leaves the engine usable.
+ * leaves the engine usable.  Every argmax follows np.argmax's order (a NaN
+ * ranks above every number, the lowest index wins ties), so NaN logits select
+ * the first NaN row as npu_llm/runtime/generate.py:713 does; a device-chained
+ * token outside the vocabulary stops the chain with HB_ERR_STATE.
  */
 #ifndef HAWKB200_H
 #define HAWKB200_H

@@ -182,6 +182,35 @@ def test_device_wait_timeout_is_reported_and_engine_recovers(tiny):
         assert_logits_close(got, oracle.step(t, p), f"after timeout, position {p}")
 
 
+def test_nan_logits_select_the_first_nan_row_like_numpy():
+    """np.argmax order (npu_llm/runtime/generate.py:713) for NaN logits: a NaN
+    ranks above every number and the first NaN wins.  With the whole LM head
+    NaN every logit is NaN, the argmax is row 0, and the device-chained
+    generate loop keeps feeding valid token ids."""
+    for nan_rows, expect in (([40, 7, 900], 7), (slice(None), 0)):
+        model = synthetic.build("tiny-qwen", seed=23)
+        head = np.array(model.bf16("token_embedding"), copy=True)  # the tied LM head
+        head[nan_rows] = np.nan
+        model._cache["lm_head"] = head  # the embedding itself stays finite
+        engine = B200DecoderEngine(model, max_slots=2, max_batch=8)
+        try:
+            oracle = OracleDecoder(model)
+            ids = synthetic.prompt_ids(model.shape.vocab, 6, seed=12)
+            got = engine.step(ids[0], 0, logits=True)
+            ref = oracle.step(ids[0], 0)
+            assert np.array_equal(np.isnan(got), np.isnan(ref))
+            assert argmax_first(ref) == expect
+            assert engine.step_argmax(ids[1], 1) == expect
+            out = engine.generate(ids, 5, slot=1)
+            ref_out, _ = greedy_generate(OracleDecoder(model), ids, 5)
+            assert out[0] == expect
+            assert out == ref_out
+            am = engine.step_batch([0, 1], [ids[2], ids[2]], [2, 10])[0]
+            assert list(am) == [expect, expect]
+        finally:
+            engine.close()
+
+
 def test_w8_engine_matches_w8_oracle():
     model = synthetic.build("tiny-qwen", seed=22)
     engine = B200DecoderEngine(model, weights="w8")

@@ -134,6 +134,24 @@ def test_gemv_argmax_first_index_on_ties():
     assert am[0] == 5
 
 
+@pytest.mark.parametrize("rows,k", [(1024, 64), (896, 4864)])
+def test_gemv_argmax_ranks_nan_first_like_numpy(rows, k):
+    """np.argmax order (npu_llm/runtime/generate.py:713): a NaN output ranks
+    above every number and the first NaN wins, so the fused argmax always
+    names a row of the matrix, even when every output is NaN."""
+    x = np.zeros((1, k), np.float32)
+    x[0, 0] = 2.0
+    for nan_rows, expect in (([500, 77, rows - 3], 77), (list(range(rows)), 0)):
+        w = np.zeros((rows, k), np.float32)
+        w[3, 0] = 100.0
+        w[nan_rows, 0] = np.nan
+        packed = layout.pack_matrix_bytes(w.astype(bfloat16))
+        out, am = run_gemv(packed, None, "bf16", rows, k, x.astype(bfloat16),
+                           hb_lib.HB_GEMV_OUT_F32 | hb_lib.HB_GEMV_ARGMAX)
+        assert np.isnan(out[0, nan_rows]).all()
+        assert am[0] == expect == int(np.argmax(out[0]))
+
+
 def test_gemv_rejects_bad_shapes():
     lib = hb_lib.load()
     rc = lib.hb_gemv(None, None, 0, 12, 16, None, 1, None, 0, None, None, 0, None)
