@@ -187,7 +187,8 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // (2p, 2p + 1) of each row.  All rows are polled together, up to U pairs per
 // thread in flight: 4 for one row (8 words, as many as the decode kernel's
 // register budget affords without slowing its GEMV loops), 8 for 8 rows,
-// where the deeper queue halves the rounds of the 8 x 4864 activation gather.
+// where the deeper queue halves the rounds of the 8 x 4864 activation gather
+// (6 in the int8-weight 8-row kernel, which has fewer registers to spare).
 template <int U, class Sink>
 __device__ __forceinline__ bool ll_gather(const uint64_t *src, size_t row_words, int words, int rows,
                                           uint32_t epoch, Ctrl *ctrl, uint64_t limit_ns, Sink &&sink) {
@@ -383,36 +384,53 @@ struct DecoderCta {
   // mean itself.  Ends with a barrier (xs is read across threads next).
   __device__ void norm_rows(const Gamma &gamma) {
     const int warp = tid >> 5, lane = tid & 31;
-    for (int m = 0; m < mrows; ++m) {
-      float ss = 0.f;
+    // the rows run side by side (independent chains), each with exactly the
+    // arithmetic of a single row, so one row's result does not depend on MB
+    float ss[MB];
 #pragma unroll
-      for (int j = 0; j < kNormWords; ++j) {
-        const int w = norm_word(j);
-        if (2 * w < P.H) {
-          const uint32_t hw = reinterpret_cast<const uint32_t *>(hx + m * P.H)[w];
-          const float a = bf_lo(hw), b = bf_hi(hw);
-          ss = fmaf(a, a, ss);
-          ss = fmaf(b, b, ss);
+    for (int m = 0; m < MB; ++m) {
+      ss[m] = 0.f;
+      if (m < mrows) {
+#pragma unroll
+        for (int j = 0; j < kNormWords; ++j) {
+          const int w = norm_word(j);
+          if (2 * w < P.H) {
+            const uint32_t hw = reinterpret_cast<const uint32_t *>(hx + m * P.H)[w];
+            const float a = bf_lo(hw), b = bf_hi(hw);
+            ss[m] = fmaf(a, a, ss[m]);
+            ss[m] = fmaf(b, b, ss[m]);
+          }
         }
       }
-      ss = warp_sum(ss);
-      if (lane == 0) s_norm[warp * kMaxBatch + m] = ss;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int m = 0; m < MB; ++m) ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], o);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int m = 0; m < MB; ++m)
+        if (m < mrows) s_norm[warp * kMaxBatch + m] = ss[m];
     }
     consumer_sync(kConsumerThreads);
-    for (int m = 0; m < mrows; ++m) {
-      float total = 0.f;
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) total += s_norm[w * kMaxBatch + m];
-      const float mean = __fdiv_rn(total, static_cast<float>(P.H));
-      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, P.eps)));
+    for (int m = 0; m < MB; ++m) {
+      if (m < mrows) {
+        float total = 0.f;
 #pragma unroll
-      for (int j = 0; j < kNormWords; ++j) {
-        const int w = norm_word(j);
-        if (2 * w < P.H) {
-          const uint32_t hw = reinterpret_cast<const uint32_t *>(hx + m * P.H)[w];
-          const float a = __fmul_rn(__fmul_rn(bf_lo(hw), inv), gamma.v[2 * j]);
-          const float b = __fmul_rn(__fmul_rn(bf_hi(hw), inv), gamma.v[2 * j + 1]);
-          *reinterpret_cast<uint32_t *>(xs + m * P.xs_elems + 2 * w) = pack_bf16x2(a, b);
+        for (int w = 0; w < kWarps; ++w) total += s_norm[w * kMaxBatch + m];
+        const float mean = __fdiv_rn(total, static_cast<float>(P.H));
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, P.eps)));
+#pragma unroll
+        for (int j = 0; j < kNormWords; ++j) {
+          const int w = norm_word(j);
+          if (2 * w < P.H) {
+            const uint32_t hw = reinterpret_cast<const uint32_t *>(hx + m * P.H)[w];
+            const float a = __fmul_rn(__fmul_rn(bf_lo(hw), inv), gamma.v[2 * j]);
+            const float b = __fmul_rn(__fmul_rn(bf_hi(hw), inv), gamma.v[2 * j + 1]);
+            *reinterpret_cast<uint32_t *>(xs + m * P.xs_elems + 2 * w) = pack_bf16x2(a, b);
+          }
         }
       }
     }
@@ -435,7 +453,7 @@ struct DecoderCta {
   // Raw payloads of the LL words (BF16 pairs) into dst[m * dst_words + i].
   __device__ bool gather_raw(const uint64_t *src, size_t row_words, int words, uint32_t *dst,
                                           size_t dst_words) {
-    return ll_gather<(MB > 1 ? 8 : 4)>(src, row_words, words, mrows, epoch, &P.result->ctrl, P.limit_ns,
+    return ll_gather<(MB > 1 ? (W8 ? 6 : 8) : 4)>(src, row_words, words, mrows, epoch, &P.result->ctrl, P.limit_ns,
                      [&](int m, int i, uint32_t d) { dst[m * dst_words + i] = d; });
   }
 
