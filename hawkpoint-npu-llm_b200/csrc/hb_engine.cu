@@ -7,6 +7,7 @@
 // wait timeouts into HB_ERR_DEVICE_TIMEOUT.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -17,6 +18,7 @@
 #include "hawkb200.h"
 #include "hb_decoder.cuh"
 #include "hb_gemv.cuh"
+#include "hb_sample.cuh"
 
 using hb::DecParams;
 using hb::kMaxBatch;
@@ -42,8 +44,11 @@ struct Variant {
 
 }  // namespace
 
+struct hb_sampler;
+
 struct hb_engine {
   int device = 0;
+  hb_sampler *sampler = nullptr;  // created by the first hb_sample
   cudaStream_t own_stream = nullptr;
   cudaStream_t stream = nullptr;
   hb_model_desc desc{};
@@ -526,7 +531,9 @@ int hb_destroy(hb_engine *e) {
   for (void *p : host)
     if (p) cudaFreeHost(p);
   if (e->own_stream) cudaStreamDestroy(e->own_stream);
+  hb_sampler *sampler = e->sampler;
   delete e;
+  hb_sampler_destroy(sampler);
   return HB_OK;
 }
 
@@ -536,7 +543,8 @@ int hb_step(hb_engine *e, int slot, int token_id, int position, int flags, float
   if (rc) return rc;
   if ((rc = check_row(e, slot, token_id, position))) return rc;
   if (logits_out) flags |= HB_STEP_LOGITS;
-  if (flags & HB_STEP_LOGITS) flags |= HB_STEP_ARGMAX;
+  if (flags & (HB_STEP_LOGITS | HB_STEP_DEVICE_LOGITS)) flags |= HB_STEP_ARGMAX;
+  const int device_logits = (logits_out || (flags & HB_STEP_DEVICE_LOGITS)) ? 1 : 0;
   hb::StepState &st = *e->h_st;
   std::memset(&st, 0, sizeof(st));
   st.token[0] = token_id;
@@ -545,7 +553,7 @@ int hb_step(hb_engine *e, int slot, int token_id, int position, int flags, float
   st.rows = 1;
   HB_CUDA(e, cudaMemcpyAsync(e->d_st, e->h_st, sizeof(hb::StepState), cudaMemcpyHostToDevice, e->stream));
   const int pe = (flags & HB_STEP_ARGMAX) ? 4 * e->desc.layers + 1 : 4 * e->desc.layers;
-  if ((rc = launch(e, 1, 0, pe, logits_out ? 1 : 0))) return rc;
+  if ((rc = launch(e, 1, 0, pe, device_logits))) return rc;
   if (logits_out)
     HB_CUDA(e, cudaMemcpyAsync(logits_out, e->d_logits, sizeof(float) * e->desc.vocab, cudaMemcpyDeviceToHost, e->stream));
   if ((rc = finish(e))) return rc;
@@ -588,7 +596,8 @@ int hb_step_batch(hb_engine *e, int n, const int32_t *slots, const int32_t *toke
       if (slots[j] == slots[i]) return fail(e, HB_ERR_INVALID_ARG, "slot %d appears twice in one batch", slots[i]);
   }
   if (logits_out) flags |= HB_STEP_LOGITS;
-  if (flags & HB_STEP_LOGITS) flags |= HB_STEP_ARGMAX;
+  if (flags & (HB_STEP_LOGITS | HB_STEP_DEVICE_LOGITS)) flags |= HB_STEP_ARGMAX;
+  const int device_logits = (logits_out || (flags & HB_STEP_DEVICE_LOGITS)) ? 1 : 0;
   hb::StepState &st = *e->h_st;
   std::memset(&st, 0, sizeof(st));
   for (int i = 0; i < n; ++i) {
@@ -599,7 +608,7 @@ int hb_step_batch(hb_engine *e, int n, const int32_t *slots, const int32_t *toke
   st.rows = n;
   HB_CUDA(e, cudaMemcpyAsync(e->d_st, e->h_st, sizeof(hb::StepState), cudaMemcpyHostToDevice, e->stream));
   const int pe = (flags & HB_STEP_ARGMAX) ? 4 * e->desc.layers + 1 : 4 * e->desc.layers;
-  if ((rc = launch(e, n, 0, pe, logits_out ? 1 : 0))) return rc;
+  if ((rc = launch(e, n, 0, pe, device_logits))) return rc;
   if (logits_out)
     HB_CUDA(e, cudaMemcpyAsync(logits_out, e->d_logits, sizeof(float) * e->desc.vocab * n, cudaMemcpyDeviceToHost, e->stream));
   if ((rc = finish(e))) return rc;
@@ -937,6 +946,289 @@ int hb_gemv_noalloc(const void *w_dev, const float *scales_dev, int weight_forma
   void *args[] = {&P};
   err = cudaLaunchKernel(fn, dim3(G), dim3(hb::kThreads), args, smem, s);
   if (err != cudaSuccess) return noalloc_fail(HB_ERR_CUDA, cudaGetErrorString(err));
+  return HB_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------ sampling ------
+struct hb_sampler {
+  int device = 0;
+  int vocab = 0;
+  cudaStream_t own_stream = nullptr;
+  float *d_in = nullptr, *d_s = nullptr, *d_e = nullptr;
+  int2 *d_leaves = nullptr, *d_nodes = nullptr;
+  int *d_levels = nullptr;
+  int n_leaves = 0, n_nodes = 0, n_levels = 0;
+  int *d_ints = nullptr;     // [2 out][kMaxHistory hist_tok][kMaxBias bias_tok]
+  float *d_floats = nullptr; // [kMaxHistory hist_cnt][kMaxBias bias_val]
+  int *h_ints = nullptr;     // pinned staging, same layout
+  float *h_floats = nullptr;
+};
+
+namespace {
+
+constexpr int kMaxHistory = 8192;
+constexpr int kMaxBias = 1024;  // MAX_LOGIT_BIAS_ENTRIES of the reference
+
+// NumPy's pairwise reduction tree of n values (np.add.reduce on a contiguous
+// float array): leaves are runs of at most 128 values, a longer run splits
+// at half its length rounded down to a multiple of 8.  Leaves are numbered
+// left to right; internal nodes are then sorted by height so the device can
+// combine one height per step.
+struct PairwisePlan {
+  std::vector<int2> leaves;
+  std::vector<int2> nodes;
+  std::vector<int> level_end;
+};
+
+void plan_rec(int lo, int n, std::vector<int2> &leaves, std::vector<int3> &internal, int &id, int &height) {
+  if (n <= 128) {
+    id = static_cast<int>(leaves.size());
+    leaves.push_back(make_int2(lo, n));
+    height = 0;
+    return;
+  }
+  int n2 = n / 2;
+  n2 -= n2 % 8;
+  int lid, lh, rid, rh;
+  plan_rec(lo, n2, leaves, internal, lid, lh);
+  plan_rec(lo + n2, n - n2, leaves, internal, rid, rh);
+  height = 1 + (lh > rh ? lh : rh);
+  id = -1 - static_cast<int>(internal.size());  // provisional id of an internal node
+  internal.push_back(make_int3(lid, rid, height));
+}
+
+PairwisePlan pairwise_plan(int n) {
+  PairwisePlan pl;
+  std::vector<int3> internal;
+  int id = 0, h = 0;
+  plan_rec(0, n, pl.leaves, internal, id, h);
+  const int L = static_cast<int>(pl.leaves.size());
+  std::vector<int> order(internal.size());
+  for (size_t i = 0; i < order.size(); ++i) order[i] = static_cast<int>(i);
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return internal[a].z < internal[b].z; });
+  std::vector<int> final_id(internal.size());
+  for (size_t k = 0; k < order.size(); ++k) final_id[order[k]] = L + static_cast<int>(k);
+  auto resolve = [&](int v) { return v >= 0 ? v : final_id[-1 - v]; };
+  int cur = 1;
+  for (size_t k = 0; k < order.size(); ++k) {
+    const int3 nd = internal[order[k]];
+    if (nd.z != cur) {
+      pl.level_end.push_back(static_cast<int>(k));
+      cur = nd.z;
+    }
+    pl.nodes.push_back(make_int2(resolve(nd.x), resolve(nd.y)));
+  }
+  if (!order.empty()) pl.level_end.push_back(static_cast<int>(order.size()));
+  return pl;
+}
+
+int sampler_fail(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_lib_error = buf;
+  return code;
+}
+
+#define HB_SCUDA(call)                                                                 \
+  do {                                                                                 \
+    cudaError_t err_ = (call);                                                         \
+    if (err_ != cudaSuccess) return sampler_fail(HB_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(err_)); \
+  } while (0)
+
+template <class T>
+int sampler_alloc(T **p, size_t count) {
+  HB_SCUDA(cudaMalloc(reinterpret_cast<void **>(p), sizeof(T) * (count ? count : 1)));
+  return HB_OK;
+}
+
+// Select on `stream` from device logits.  The caller has made the sampler's
+// device current.
+int sampler_run(hb_sampler *sp, cudaStream_t stream, const float *logits_dev, const hb_sampling *q,
+                int32_t *token_out) {
+  const int V = sp->vocab;
+  if (!q || !token_out) return sampler_fail(HB_ERR_INVALID_ARG, "params or token_out is NULL");
+  auto finite = [](double v) { return v == v && v - v == 0.0; };
+  if (!finite(q->temperature) || q->temperature < 0.f)
+    return sampler_fail(HB_ERR_INVALID_ARG, "temperature must be finite and >= 0");
+  if (!finite(q->top_p) || !(q->top_p > 0.f) || q->top_p > 1.f)
+    return sampler_fail(HB_ERR_INVALID_ARG, "top_p must be in (0, 1]");
+  if (q->top_k < 0) return sampler_fail(HB_ERR_INVALID_ARG, "top_k cannot be negative");
+  if (!finite(q->repetition_penalty) || !(q->repetition_penalty > 0.f) || !finite(q->presence_penalty) ||
+      !finite(q->frequency_penalty))
+    return sampler_fail(HB_ERR_INVALID_ARG, "penalties must be finite (repetition > 0)");
+  if (q->n_history < 0 || q->n_history > kMaxHistory || (q->n_history && (!q->history_tokens || !q->history_counts)))
+    return sampler_fail(HB_ERR_INVALID_ARG, "history of %d tokens (at most %d)", q->n_history, kMaxHistory);
+  if (q->n_bias < 0 || q->n_bias > kMaxBias || (q->n_bias && (!q->bias_tokens || !q->bias_values)))
+    return sampler_fail(HB_ERR_INVALID_ARG, "logit bias of %d entries (at most %d)", q->n_bias, kMaxBias);
+  for (int i = 0; i < q->n_history; ++i)
+    if (q->history_tokens[i] < 0 || q->history_tokens[i] >= V)
+      return sampler_fail(HB_ERR_INVALID_ARG, "history token %d outside the vocabulary", q->history_tokens[i]);
+  for (int i = 0; i < q->n_bias; ++i)
+    if (q->bias_tokens[i] < 0 || q->bias_tokens[i] >= V || !finite(q->bias_values[i]))
+      return sampler_fail(HB_ERR_INVALID_ARG, "logit bias entry %d invalid", i);
+  const bool neutral = q->repetition_penalty == 1.f && q->presence_penalty == 0.f && q->frequency_penalty == 0.f;
+  // the reference's `greedy`: nothing can reorder the logits -> argmax, no draw
+  const bool greedy = neutral && (q->temperature == 0.f || q->top_k == 1) && q->n_bias == 0;
+  const bool draws = !greedy && q->temperature != 0.f;
+  if (draws && !(q->uniform >= 0.0 && q->uniform < 1.0))
+    return sampler_fail(HB_ERR_INVALID_ARG, "uniform must be in [0, 1)");
+
+  hb::SampleParams P{};
+  P.logits = logits_dev;
+  P.s = sp->d_s;
+  P.e = sp->d_e;
+  P.V = V;
+  P.temperature = greedy ? 0.f : q->temperature;
+  P.top_p = q->top_p;
+  P.top_k = q->top_k;
+  P.rep = q->repetition_penalty;
+  P.pres = q->presence_penalty;
+  P.freq = q->frequency_penalty;
+  P.u = q->uniform;
+  // penalties apply only when one of them is not neutral (sampling.py:341-346)
+  P.n_hist = (greedy || neutral) ? 0 : q->n_history;
+  P.n_bias = greedy ? 0 : q->n_bias;
+  int *h_out = sp->h_ints;
+  int *h_htok = sp->h_ints + 2, *h_btok = sp->h_ints + 2 + kMaxHistory;
+  float *h_hcnt = sp->h_floats, *h_bval = sp->h_floats + kMaxHistory;
+  for (int i = 0; i < P.n_hist; ++i) {
+    h_htok[i] = q->history_tokens[i];
+    h_hcnt[i] = q->history_counts[i];
+  }
+  for (int i = 0; i < P.n_bias; ++i) {
+    h_btok[i] = q->bias_tokens[i];
+    h_bval[i] = q->bias_values[i];
+  }
+  int *d_out = sp->d_ints;
+  P.hist_tok = sp->d_ints + 2;
+  P.bias_tok = sp->d_ints + 2 + kMaxHistory;
+  P.hist_cnt = sp->d_floats;
+  P.bias_val = sp->d_floats + kMaxHistory;
+  P.leaves = sp->d_leaves;
+  P.n_leaves = sp->n_leaves;
+  P.nodes = sp->d_nodes;
+  P.n_nodes = sp->n_nodes;
+  P.level_end = sp->d_levels;
+  P.n_levels = sp->n_levels;
+  P.out = d_out;
+  if (P.n_hist) {
+    HB_SCUDA(cudaMemcpyAsync(const_cast<int *>(P.hist_tok), h_htok, sizeof(int) * P.n_hist, cudaMemcpyHostToDevice, stream));
+    HB_SCUDA(cudaMemcpyAsync(const_cast<float *>(P.hist_cnt), h_hcnt, sizeof(float) * P.n_hist, cudaMemcpyHostToDevice, stream));
+  }
+  if (P.n_bias) {
+    HB_SCUDA(cudaMemcpyAsync(const_cast<int *>(P.bias_tok), h_btok, sizeof(int) * P.n_bias, cudaMemcpyHostToDevice, stream));
+    HB_SCUDA(cudaMemcpyAsync(const_cast<float *>(P.bias_val), h_bval, sizeof(float) * P.n_bias, cudaMemcpyHostToDevice, stream));
+  }
+  hb::sample_kernel<<<1, hb::kSampThreads, sizeof(hb::SampleSmem), stream>>>(P);
+  HB_SCUDA(cudaGetLastError());
+  HB_SCUDA(cudaMemcpyAsync(h_out, d_out, sizeof(int) * 2, cudaMemcpyDeviceToHost, stream));
+  HB_SCUDA(cudaStreamSynchronize(stream));
+  if (h_out[1] != 0) {
+    *token_out = -1;
+    return sampler_fail(HB_ERR_UNSUPPORTED, "top_p keeps more than %d candidates: select on the host", hb::kTopPMax);
+  }
+  *token_out = h_out[0];
+  return HB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int hb_sampler_create(int vocab, int device, hb_sampler **out) {
+  if (!out) return sampler_fail(HB_ERR_INVALID_ARG, "out is NULL");
+  *out = nullptr;
+  if (vocab < 1 || vocab > hb::kSampMaxVocab)
+    return sampler_fail(HB_ERR_UNSUPPORTED, "vocabulary of %d outside [1, %d]", vocab, hb::kSampMaxVocab);
+  DeviceScope device_scope_(device);
+  if (!device_scope_.ok) return sampler_fail(HB_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+  hb_sampler *sp = new hb_sampler;
+  sp->device = device;
+  sp->vocab = vocab;
+  auto bail = [&](int rc) {
+    hb_sampler_destroy(sp);
+    return rc;
+  };
+  const PairwisePlan pl = pairwise_plan(vocab);
+  sp->n_leaves = static_cast<int>(pl.leaves.size());
+  sp->n_nodes = static_cast<int>(pl.nodes.size());
+  sp->n_levels = static_cast<int>(pl.level_end.size());
+  int rc;
+  if ((rc = sampler_alloc(&sp->d_in, vocab)) || (rc = sampler_alloc(&sp->d_s, vocab)) ||
+      (rc = sampler_alloc(&sp->d_e, vocab)) || (rc = sampler_alloc(&sp->d_leaves, sp->n_leaves)) ||
+      (rc = sampler_alloc(&sp->d_nodes, sp->n_nodes)) || (rc = sampler_alloc(&sp->d_levels, sp->n_levels)) ||
+      (rc = sampler_alloc(&sp->d_ints, 2 + kMaxHistory + kMaxBias)) ||
+      (rc = sampler_alloc(&sp->d_floats, kMaxHistory + kMaxBias)))
+    return bail(rc);
+  if (cudaHostAlloc(reinterpret_cast<void **>(&sp->h_ints), sizeof(int) * (2 + kMaxHistory + kMaxBias),
+                    cudaHostAllocDefault) != cudaSuccess ||
+      cudaHostAlloc(reinterpret_cast<void **>(&sp->h_floats), sizeof(float) * (kMaxHistory + kMaxBias),
+                    cudaHostAllocDefault) != cudaSuccess)
+    return bail(sampler_fail(HB_ERR_CUDA, "pinned host allocation failed"));
+  if (cudaMemcpy(sp->d_leaves, pl.leaves.data(), sizeof(int2) * sp->n_leaves, cudaMemcpyHostToDevice) != cudaSuccess ||
+      (sp->n_nodes && cudaMemcpy(sp->d_nodes, pl.nodes.data(), sizeof(int2) * sp->n_nodes, cudaMemcpyHostToDevice) != cudaSuccess) ||
+      (sp->n_levels && cudaMemcpy(sp->d_levels, pl.level_end.data(), sizeof(int) * sp->n_levels, cudaMemcpyHostToDevice) != cudaSuccess))
+    return bail(sampler_fail(HB_ERR_CUDA, "sampler plan upload failed"));
+  if (cudaFuncSetAttribute(reinterpret_cast<const void *>(&hb::sample_kernel),
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sizeof(hb::SampleSmem))) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&sp->own_stream, cudaStreamNonBlocking) != cudaSuccess)
+    return bail(sampler_fail(HB_ERR_CUDA, "sampler set-up failed"));
+  *out = sp;
+  return HB_OK;
+}
+
+int hb_sampler_select(hb_sampler *sp, const float *logits, int logits_on_device, const hb_sampling *params,
+                      int32_t *token_out) {
+  if (!sp || !logits) return sampler_fail(HB_ERR_INVALID_ARG, "sampler or logits is NULL");
+  DeviceScope device_scope_(sp->device);
+  if (!device_scope_.ok) return sampler_fail(HB_ERR_CUDA, "cudaSetDevice(%d) failed", sp->device);
+  const float *dev = logits;
+  if (!logits_on_device) {
+    HB_SCUDA(cudaMemcpyAsync(sp->d_in, logits, sizeof(float) * sp->vocab, cudaMemcpyHostToDevice, sp->own_stream));
+    dev = sp->d_in;
+  }
+  return sampler_run(sp, sp->own_stream, dev, params, token_out);
+}
+
+int hb_sampler_destroy(hb_sampler *sp) {
+  if (!sp) return HB_OK;
+  DeviceScope device_scope_(sp->device);
+  if (sp->own_stream) cudaStreamSynchronize(sp->own_stream);
+  void *dev[] = {sp->d_in, sp->d_s, sp->d_e, sp->d_leaves, sp->d_nodes, sp->d_levels, sp->d_ints, sp->d_floats};
+  for (void *p : dev)
+    if (p) cudaFree(p);
+  if (sp->h_ints) cudaFreeHost(sp->h_ints);
+  if (sp->h_floats) cudaFreeHost(sp->h_floats);
+  if (sp->own_stream) cudaStreamDestroy(sp->own_stream);
+  delete sp;
+  return HB_OK;
+}
+
+int hb_sample(hb_engine *e, int row, const hb_sampling *params, int32_t *token_out) {
+  int rc = check_engine(e);
+  if (rc) return rc;
+  if (row < 0 || row >= kMaxBatch || row >= e->desc.max_batch)
+    return fail(e, HB_ERR_INVALID_ARG, "row %d outside the batch", row);
+  if (!e->sampler && (rc = hb_sampler_create(e->desc.vocab, e->device, &e->sampler)))
+    return fail(e, rc, "%s", g_lib_error.c_str());
+  rc = sampler_run(e->sampler, e->stream, e->d_logits + static_cast<size_t>(row) * e->desc.vocab, params, token_out);
+  if (rc) return fail(e, rc, "%s", g_lib_error.c_str());
+  return HB_OK;
+}
+
+int hb_read_logits(hb_engine *e, int n_rows, float *logits_out) {
+  int rc = check_engine(e);
+  if (rc) return rc;
+  if (!logits_out || n_rows < 1 || n_rows > e->desc.max_batch)
+    return fail(e, HB_ERR_INVALID_ARG, "%d rows outside [1, %d] or NULL output", n_rows, e->desc.max_batch);
+  HB_CUDA(e, cudaMemcpyAsync(logits_out, e->d_logits, sizeof(float) * e->desc.vocab * n_rows, cudaMemcpyDeviceToHost,
+                             e->stream));
+  HB_CUDA(e, cudaStreamSynchronize(e->stream));
   return HB_OK;
 }
 

@@ -1,0 +1,484 @@
+// hb_sample.cuh -- on-device token selection (one CTA of 1024 threads).
+//
+// The selection pipeline of the reference's Sampler.select
+// (npu_llm/runtime/sampling.py:416-445) on FP32 logits already in device
+// memory, so a sampled request costs no logits copy and no host argsort:
+//   1. repetition / presence / frequency penalties over the unique history
+//      tokens (sampling.py:327-363), in FP32 exactly as NumPy rounds them;
+//   2. logit bias (:366-380);  temperature 0 -> argmax (np.argmax order);
+//   3. scores / temperature;  4. top-k: keep scores >= the k-th largest
+//      (np.partition threshold, ties kept, :383-389);
+//   5. top-p (:392-406): the candidates sorted by (score desc, index desc),
+//      the softmax over that order, the FP32 running sum taken left to right
+//      as np.cumsum does, and the prefix whose mass-before is < top_p kept;
+//   6. the guarded softmax in index order (:409-421), its float64
+//      renormalisation and Generator.choice's draw: the first index whose
+//      normalised cumulative sum exceeds u, where u is the request
+//      generator's next random(), drawn on the host so the random stream
+//      stays the request's own.
+// Every sum whose rounding reaches the result follows NumPy's order: the
+// softmax denominators replay np.add.reduce's pairwise tree (leaves of
+// 64-128 elements with eight accumulators, halves split at multiples of 8),
+// precomputed on the host per vocabulary size (SamplePlan) and evaluated
+// level by level here.  What still differs from NumPy is the float32 exp of
+// each score (CUDA's expf against NumPy's) and, with more than
+// kTopPMax top-p candidates, the order of the softmax denominator in step 5:
+// both move probabilities by an ulp, so only a draw or a top-p cut lying
+// within ~1e-6 of a boundary can select differently.  When the top-p
+// nucleus is larger than kTopPMax candidates the kernel reports
+// "unsupported" and the caller selects on the host instead.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "hb_device.cuh"
+
+namespace hb {
+
+constexpr int kSampThreads = 1024;
+constexpr int kSampWarps = kSampThreads / 32;
+constexpr int kTopPMax = 4096;       // top-p candidates sorted on chip
+constexpr int kSampMaxLeaves = 4096;
+constexpr int kSampMaxVocab = kSampMaxLeaves * 64;  // every pairwise leaf holds >= 64 values
+
+struct SampleParams {
+  const float *logits;  // [V], device
+  float *s;             // [V] working scores
+  float *e;             // [V] shifted exponentials
+  int V;
+  float temperature, top_p, rep, pres, freq;
+  int top_k;
+  int n_hist;
+  const int *hist_tok;     // unique in-vocabulary history tokens
+  const float *hist_cnt;   // their counts
+  int n_bias;
+  const int *bias_tok;     // unique in-vocabulary tokens
+  const float *bias_val;
+  double u;
+  // NumPy's pairwise tree for V values: leaves (first, count) left to right;
+  // internal nodes (left id, right id), ids 0..n_leaves-1 are the leaves and
+  // n_leaves + i is node i; nodes grouped by height, level h ending at
+  // level_end[h]; the root is the last node (or leaf 0 when there is one).
+  const int2 *leaves;
+  int n_leaves;
+  const int2 *nodes;
+  int n_nodes;
+  const int *level_end;
+  int n_levels;
+  int *out;  // [0] token, [1] status: 0 selected, 1 top-p nucleus too large
+};
+
+struct SampleSmem {
+  double tree[2 * kSampMaxLeaves];
+  unsigned long long keys[kTopPMax];  // (score key << 32) | index, for the top-p sort
+  float probs[kTopPMax];
+  unsigned int hist[kSampWarps][256];
+  double wscan[kSampWarps];
+  float wf[kSampWarps];
+  int wi[kSampWarps];
+  int misc[8];
+  double dmisc[2];
+};
+
+// Monotone map of a float to an unsigned key (NaN above +inf, like np.sort).
+__device__ __forceinline__ uint32_t samp_key(float f) {
+  if (f != f) return 0xffffffffu;
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float samp_unkey(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+__device__ __forceinline__ float samp_add(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ double samp_add(double a, double b) { return __dadd_rn(a, b); }
+
+// np.add.reduce of one leaf: < 8 values from zero, else eight accumulators.
+template <class T, class F>
+__device__ T leaf_sum(int lo, int n, F &&elem) {
+  if (n < 8) {
+    T r = T(0);
+    for (int i = 0; i < n; ++i) r = samp_add(r, elem(lo + i));
+    return r;
+  }
+  T r[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) r[j] = elem(lo + j);
+  int i = 8;
+  for (; i < n - n % 8; i += 8) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = samp_add(r[j], elem(lo + i + j));
+  }
+  T res = samp_add(samp_add(samp_add(r[0], r[1]), samp_add(r[2], r[3])),
+                   samp_add(samp_add(r[4], r[5]), samp_add(r[6], r[7])));
+  for (; i < n; ++i) res = samp_add(res, elem(lo + i));
+  return res;
+}
+
+// Sum of elem(0..V-1) in NumPy's pairwise order.  All threads call it.
+template <class T, class F>
+__device__ T tree_sum(const SampleParams &p, SampleSmem &sm, F &&elem) {
+  T *vals = reinterpret_cast<T *>(sm.tree);
+  for (int l = threadIdx.x; l < p.n_leaves; l += kSampThreads) {
+    const int2 lf = p.leaves[l];
+    vals[l] = leaf_sum<T>(lf.x, lf.y, elem);
+  }
+  __syncthreads();
+  int start = 0;
+  for (int h = 0; h < p.n_levels; ++h) {
+    const int end = p.level_end[h];
+    for (int i = start + threadIdx.x; i < end; i += kSampThreads) {
+      const int2 nd = p.nodes[i];
+      vals[p.n_leaves + i] = samp_add(vals[nd.x], vals[nd.y]);
+    }
+    __syncthreads();
+    start = end;
+  }
+  const T r = vals[p.n_nodes > 0 ? p.n_leaves + p.n_nodes - 1 : 0];
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ float samp_block_max(SampleSmem &sm, float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) sm.wf[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = sm.wf[0];
+  for (int w = 1; w < kSampWarps; ++w) r = fmaxf(r, sm.wf[w]);
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ int samp_block_sum(SampleSmem &sm, int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) sm.wi[threadIdx.x >> 5] = v;
+  __syncthreads();
+  int r = 0;
+  for (int w = 0; w < kSampWarps; ++w) r += sm.wi[w];
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ int samp_block_min(SampleSmem &sm, int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) sm.wi[threadIdx.x >> 5] = v;
+  __syncthreads();
+  int r = sm.wi[0];
+  for (int w = 1; w < kSampWarps; ++w) r = min(r, sm.wi[w]);
+  __syncthreads();
+  return r;
+}
+
+// Index of the maximum of s[0..V) in np.argmax order.
+__device__ int samp_argmax(const SampleParams &p, SampleSmem &sm) {
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int j = threadIdx.x; j < p.V; j += kSampThreads) argmax_merge(bv, bi, p.s[j], j);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    argmax_merge(bv, bi, ov, oi);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sm.wf[threadIdx.x >> 5] = bv;
+    sm.wi[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  float v = sm.wf[0];
+  int i = sm.wi[0];
+  for (int w = 1; w < kSampWarps; ++w) argmax_merge(v, i, sm.wf[w], sm.wi[w]);
+  __syncthreads();
+  return i;
+}
+
+// Key of the k-th largest score (1 <= k <= V), duplicates counted: four
+// 8-bit radix passes, per-warp histograms with warp-aggregated increments.
+__device__ uint32_t samp_kth_largest(const SampleParams &p, SampleSmem &sm, int k) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t prefix = 0, mask = 0;
+  int kk = k;
+  const int vpad = (p.V + kSampThreads - 1) / kSampThreads * kSampThreads;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < kSampWarps * 256; i += kSampThreads) (&sm.hist[0][0])[i] = 0u;
+    __syncthreads();
+    for (int j = threadIdx.x; j < vpad; j += kSampThreads) {
+      int bin = 256;
+      if (j < p.V) {
+        const uint32_t key = samp_key(p.s[j]);
+        if ((key & mask) == prefix) bin = (key >> shift) & 255;
+      }
+      const unsigned peers = __match_any_sync(0xffffffffu, bin);
+      if (bin < 256 && lane == __ffs(peers) - 1) sm.hist[warp][bin] += __popc(peers);
+    }
+    __syncthreads();
+    if (threadIdx.x < 256) {
+      unsigned c = 0;
+      for (int w = 0; w < kSampWarps; ++w) c += sm.hist[w][threadIdx.x];
+      sm.hist[0][threadIdx.x] = c;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int acc = 0, b = 255;
+      for (; b > 0; --b) {
+        if (acc + static_cast<int>(sm.hist[0][b]) >= kk) break;
+        acc += static_cast<int>(sm.hist[0][b]);
+      }
+      sm.misc[0] = b;
+      sm.misc[1] = kk - acc;
+    }
+    __syncthreads();
+    prefix |= static_cast<uint32_t>(sm.misc[0]) << shift;
+    mask |= 255u << shift;
+    kk = sm.misc[1];
+    __syncthreads();
+  }
+  return prefix;
+}
+
+__global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p) {
+  extern __shared__ __align__(16) uint8_t samp_smem_raw[];
+  SampleSmem &sm = *reinterpret_cast<SampleSmem *>(samp_smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int V = p.V;
+  float *s = p.s;
+
+  // 1-2. working copy, penalties, bias (each token appears once per list)
+  for (int j = tid; j < V; j += kSampThreads) s[j] = p.logits[j];
+  __syncthreads();
+  for (int t = tid; t < p.n_hist; t += kSampThreads) {
+    const int tok = p.hist_tok[t];
+    float v = s[tok];
+    if (p.rep != 1.0f) v = v > 0.f ? __fdiv_rn(v, p.rep) : __fmul_rn(v, p.rep);
+    v = __fsub_rn(v, __fmul_rn(p.freq, p.hist_cnt[t]));
+    v = __fsub_rn(v, p.pres);
+    s[tok] = v;
+  }
+  __syncthreads();
+  for (int t = tid; t < p.n_bias; t += kSampThreads) {
+    const int tok = p.bias_tok[t];
+    s[tok] = __fadd_rn(s[tok], p.bias_val[t]);
+  }
+  __syncthreads();
+  if (p.temperature == 0.0f) {
+    const int best = samp_argmax(p, sm);
+    if (tid == 0) {
+      p.out[0] = best;
+      p.out[1] = 0;
+    }
+    return;
+  }
+
+  // 3. temperature
+  for (int j = tid; j < V; j += kSampThreads) s[j] = __fdiv_rn(s[j], p.temperature);
+  __syncthreads();
+
+  // 4. top-k
+  if (p.top_k > 0 && p.top_k < V) {
+    const float thr = samp_unkey(samp_kth_largest(p, sm, p.top_k));
+    for (int j = tid; j < V; j += kSampThreads)
+      if (s[j] < thr) s[j] = -INFINITY;
+    __syncthreads();
+  }
+
+  // 5. top-p
+  if (p.top_p < 1.0f) {
+    int cand = 0;
+    float peak = -INFINITY;
+    for (int j = tid; j < V; j += kSampThreads) {
+      const float v = s[j];
+      if (isfinite(v)) {
+        ++cand;
+        peak = fmaxf(peak, v);
+      }
+    }
+    const int C = samp_block_sum(sm, cand);
+    peak = samp_block_max(sm, peak);
+    // the candidates: every finite score, or those >= the kTopPMax-th largest
+    uint32_t lo_key = 0u;
+    if (C > kTopPMax) lo_key = samp_kth_largest(p, sm, kTopPMax);
+    if (tid == 0) sm.misc[2] = 0;
+    __syncthreads();
+    const int vpad = (V + kSampThreads - 1) / kSampThreads * kSampThreads;
+    for (int j = tid; j < vpad; j += kSampThreads) {
+      bool take = false;
+      uint32_t key = 0u;
+      if (j < V) {
+        const float v = s[j];
+        key = samp_key(v);
+        take = isfinite(v) && key >= lo_key;
+      }
+      const unsigned ballot = __ballot_sync(0xffffffffu, take);
+      int base = 0;
+      if (lane == 0 && ballot) base = atomicAdd(&sm.misc[2], __popc(ballot));
+      base = __shfl_sync(0xffffffffu, base, 0);
+      if (take) {
+        const int slot = base + __popc(ballot & ((1u << lane) - 1u));
+        if (slot < kTopPMax) sm.keys[slot] = (static_cast<unsigned long long>(key) << 32) | static_cast<uint32_t>(j);
+      }
+    }
+    __syncthreads();
+    const int cnt = sm.misc[2];
+    if (cnt > kTopPMax) {  // ties at the cut overflow the on-chip sort
+      if (tid == 0) {
+        p.out[0] = -1;
+        p.out[1] = 1;
+      }
+      return;
+    }
+    int n2 = 1;
+    while (n2 < cnt) n2 <<= 1;
+    for (int i = cnt + tid; i < n2; i += kSampThreads) sm.keys[i] = 0ull;
+    __syncthreads();
+    // bitonic sort, descending: score desc, then index desc
+    for (int k = 2; k <= n2; k <<= 1) {
+      for (int jj = k >> 1; jj > 0; jj >>= 1) {
+        for (int i = tid; i < n2; i += kSampThreads) {
+          const int ixj = i ^ jj;
+          if (ixj > i) {
+            const unsigned long long a = sm.keys[i], b = sm.keys[ixj];
+            const bool desc = (i & k) == 0;
+            if (desc ? (a < b) : (a > b)) {
+              sm.keys[i] = b;
+              sm.keys[ixj] = a;
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    // softmax over the scores in sorted order: exp(score - peak), the
+    // denominator over all V positions (non-candidates are 0)
+    for (int i = tid; i < cnt; i += kSampThreads)
+      sm.probs[i] = expf(__fsub_rn(samp_unkey(static_cast<uint32_t>(sm.keys[i] >> 32)), peak));
+    __syncthreads();
+    float total;
+    if (C <= kTopPMax) {
+      total = tree_sum<float>(p, sm, [&](int i) { return i < cnt ? sm.probs[i] : 0.f; });
+    } else {
+      // the tail's order is unknown: the denominator in index order instead
+      for (int j = tid; j < V; j += kSampThreads) {
+        const float v = s[j];
+        p.e[j] = isfinite(v) ? expf(__fsub_rn(v, peak)) : 0.f;
+      }
+      __syncthreads();
+      total = tree_sum<float>(p, sm, [&](int j) { return p.e[j]; });
+    }
+    const bool degenerate = !(total > 0.f) || !isfinite(total);
+    for (int i = tid; i < cnt; i += kSampThreads) sm.probs[i] = __fdiv_rn(sm.probs[i], total);
+    __syncthreads();
+    if (tid == 0) {
+      int keep = -1;
+      if (degenerate) {
+        keep = 1;
+      } else {
+        float cum = 0.f;
+        for (int i = 0; i < cnt; ++i) {
+          const float pi = sm.probs[i];
+          cum = __fadd_rn(cum, pi);
+          if (i > 0 && !(__fsub_rn(cum, pi) < p.top_p)) {
+            keep = i;
+            break;
+          }
+        }
+        if (keep < 0 && C <= kTopPMax) keep = cnt;  // every candidate kept
+      }
+      sm.misc[3] = keep;
+    }
+    __syncthreads();
+    const int keep = sm.misc[3];
+    if (keep < 0) {  // the nucleus extends past the sorted candidates
+      if (tid == 0) {
+        p.out[0] = -1;
+        p.out[1] = 1;
+      }
+      return;
+    }
+    const uint32_t cut_key = static_cast<uint32_t>(sm.keys[keep - 1] >> 32);
+    const float cut = samp_unkey(cut_key);
+    for (int j = tid; j < V; j += kSampThreads)
+      if (s[j] < cut) s[j] = -INFINITY;
+    __syncthreads();
+    for (int i = keep + tid; i < cnt; i += kSampThreads)  // ties with the cut beyond it
+      if (static_cast<uint32_t>(sm.keys[i] >> 32) == cut_key) s[static_cast<uint32_t>(sm.keys[i])] = -INFINITY;
+    __syncthreads();
+  }
+
+  // 6. guarded softmax in index order, float64 renormalisation, the draw
+  float peak = -INFINITY;
+  for (int j = tid; j < V; j += kSampThreads)
+    if (isfinite(s[j])) peak = fmaxf(peak, s[j]);
+  peak = samp_block_max(sm, peak);
+  if (!isfinite(peak)) peak = 0.f;
+  for (int j = tid; j < V; j += kSampThreads) {
+    const float v = s[j];
+    p.e[j] = isfinite(v) ? expf(__fsub_rn(v, peak)) : 0.f;
+  }
+  __syncthreads();
+  const float total = tree_sum<float>(p, sm, [&](int j) { return p.e[j]; });
+  if (!(total > 0.f) || !isfinite(total)) {  // every candidate underflowed
+    const int best = samp_argmax(p, sm);
+    if (tid == 0) {
+      p.out[0] = best;
+      p.out[1] = 0;
+    }
+    return;
+  }
+  // the float32 probabilities, in place
+  float *e = p.e;
+  for (int j = tid; j < V; j += kSampThreads) e[j] = __fdiv_rn(e[j], total);
+  __syncthreads();
+  const double s64 = tree_sum<double>(p, sm, [&](int j) { return static_cast<double>(e[j]); });
+  // Cumulative sums over contiguous chunks, then the first crossing of u.
+  // Scaling by 1/s64 and comparing run > u * last instead of dividing moves
+  // the boundaries by an ulp of a double, far below the float32 effects.
+  const double inv = __ddiv_rn(1.0, s64);
+  const int chunk = (V + kSampThreads - 1) / kSampThreads;
+  const int j0 = min(V, tid * chunk), j1 = min(V, j0 + chunk);
+  double local = 0.0;
+  for (int j = j0; j < j1; ++j) local = __dadd_rn(local, __dmul_rn(static_cast<double>(e[j]), inv));
+  // block exclusive scan of the chunk sums
+  double incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl = __dadd_rn(incl, t);
+  }
+  if (lane == 31) sm.wscan[warp] = incl;
+  __syncthreads();
+  if (tid == 0) {
+    double acc = 0.0;
+    for (int w = 0; w < kSampWarps; ++w) {
+      const double t = sm.wscan[w];
+      sm.wscan[w] = acc;
+      acc = __dadd_rn(acc, t);
+    }
+    sm.dmisc[0] = acc;
+  }
+  __syncthreads();
+  const double last = sm.dmisc[0];
+  double excl = __shfl_up_sync(0xffffffffu, incl, 1);
+  if (lane == 0) excl = 0.0;
+  double run = __dadd_rn(sm.wscan[warp], excl);
+  const double target = __dmul_rn(p.u, last);
+  int first = 0x7fffffff;
+  if (__dadd_rn(run, local) > target) {  // the crossing is in this chunk
+    for (int j = j0; j < j1; ++j) {
+      run = __dadd_rn(run, __dmul_rn(static_cast<double>(e[j]), inv));
+      if (run > target) {
+        first = j;
+        break;
+      }
+    }
+  }
+  first = samp_block_min(sm, first);
+  if (tid == 0) {
+    p.out[0] = first < V ? first : V - 1;
+    p.out[1] = 0;
+  }
+}
+
+}  // namespace hb

@@ -123,6 +123,31 @@ class B200DecoderEngine:
         self._check(self._lib.hb_step(h, slot, int(token_id), int(position), 0, None, None))
         return None
 
+    def step_device_logits(self, token_id, position, slot=0):
+        """One position with the LM head, the FP32 logits kept on the device
+        for ``sample``; returns the argmax token."""
+        h = self._live()
+        self._check(self._lib.hb_step(
+            h, slot, int(token_id), int(position), hb_lib.HB_STEP_DEVICE_LOGITS, None,
+            ctypes.byref(self._argmax)))
+        return int(self._argmax.value)
+
+    def sample(self, params, history, uniform, row=0):
+        """Select a token on the device from the logits of the last
+        ``step_device_logits`` (row 0) -- the reference ``Sampler.select``
+        with ``uniform`` as its generator draw.  None when top_p keeps more
+        candidates than the device sorts (select on the host then)."""
+        from runtime.device_sampler import sample_engine_row
+
+        return sample_engine_row(self._lib, self._live(), self.vocab, row, params, history, uniform)
+
+    def device_logits(self, rows=1):
+        """Host copy of the FP32 logits the last step left on the device."""
+        h = self._live()
+        out = np.empty((rows, self.vocab), np.float32)
+        self._check(self._lib.hb_read_logits(h, int(rows), out.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
+        return out[0] if rows == 1 else out
+
     def step_argmax(self, token_id, position, slot=0):
         """One position with the LM head; returns only the argmax token."""
         h = self._live()

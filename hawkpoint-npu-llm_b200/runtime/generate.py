@@ -201,6 +201,36 @@ class NPUDecoder:
         self._record_phase("prefill", began)
         return [elapsed / (end - start)] * (end - start)
 
+    def _sample_step(self, token_id, position, sampler, history):
+        """One position with the next token selected on the GPU: the
+        reference ``Sampler.select`` (npu_llm/runtime/sampling.py:416-445) run
+        on logits that never leave the device, with the sampler's own
+        generator supplying the one ``random()`` its draw consumes.  When the
+        device reports a top-p nucleus too large to sort on chip, the
+        generator is rewound and the host sampler selects from a copy of the
+        same logits, so the random stream is identical either way."""
+        from runtime.device_sampler import draws_uniform
+
+        if not 0 <= position < self.context_length:
+            raise ValueError("position outside the 64-token context")
+        del self._cached_prefix[position:]
+        if self._engine is None:
+            raise RuntimeError("decoder is closed")
+        start = time.perf_counter()
+        engine = self._engine
+        engine.step_device_logits(token_id, position)
+        rng = sampler._rng
+        state = rng.bit_generator.state
+        u = rng.random() if draws_uniform(sampler.params, engine.vocab) else None
+        token = engine.sample(sampler.params, history, u)
+        if token is None:
+            rng.bit_generator.state = state
+            token = int(sampler.select(engine.device_logits(), history))
+        self._record_phase("npu_engine", start)
+        if len(self._cached_prefix) == position:
+            self._cached_prefix.append(int(token_id))
+        return token, time.perf_counter() - start
+
     def _decode_step(self, token_id, position, **kwargs):
         del self._cached_prefix[position:]
         result = self.decode_token(token_id, position, **kwargs)
@@ -295,6 +325,19 @@ class NPUDecoder:
 
         # greedy without logprobs keeps the on-device argmax path
         select = None if sampler.greedy and top_logprobs is None else choose
+        # a sampled request without logprobs selects on the device when the
+        # sampler exposes its generator (the reference Sampler does)
+        device_sampling = (
+            select is not None and top_logprobs is None and getattr(self, "_engine", None) is not None
+            and getattr(sampler, "_rng", None) is not None and hasattr(sampler, "params")
+            and os.environ.get("HAWKPOINT_DEVICE_SAMPLING", "1") != "0"
+        )
+
+        def step(token_id, position, final=True):
+            if final and device_sampling:
+                return self._sample_step(token_id, position, sampler, history)
+            return self._decode_step(token_id, position, select=select if final else None,
+                                     compute_logits=final)
 
         def release(text, final=False):
             nonlocal emitted
@@ -323,11 +366,7 @@ class NPUDecoder:
         else:
             first = reused
         for index in range(first, len(prompt_ids)):
-            token, elapsed = self._decode_step(
-                prompt_ids[index], index,
-                select=select if index == last else None,
-                compute_logits=index == last,
-            )
+            token, elapsed = step(prompt_ids[index], index, final=index == last)
             timings.append(elapsed)
         prefill_steps = len(timings)
         position = len(prompt_ids)
@@ -353,7 +392,7 @@ class NPUDecoder:
                 yield chunk(text, release(text))
             if len(generated) >= max_new_tokens:
                 break  # never compute a discarded successor token
-            token, elapsed = self._decode_step(token, position, select=select)
+            token, elapsed = step(token, position)
             timings.append(elapsed)
             position += 1
         if stop_matcher.matched is None:

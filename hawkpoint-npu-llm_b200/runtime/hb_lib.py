@@ -21,6 +21,7 @@ HB_ERR_STATE = -5
 
 HB_STEP_ARGMAX = 1
 HB_STEP_LOGITS = 2
+HB_STEP_DEVICE_LOGITS = 4
 HB_DUMP_HIDDEN = 0
 HB_DUMP_KV = 1
 HB_DUMP_TRACE = 2
@@ -62,6 +63,26 @@ class HbModelDesc(ctypes.Structure):
     ]
 
 
+class HbSampling(ctypes.Structure):
+    """hb_sampling: one token selection's parameters (include/hawkb200.h)."""
+
+    _fields_ = [
+        ("temperature", ctypes.c_float),
+        ("top_p", ctypes.c_float),
+        ("repetition_penalty", ctypes.c_float),
+        ("presence_penalty", ctypes.c_float),
+        ("frequency_penalty", ctypes.c_float),
+        ("top_k", ctypes.c_int32),
+        ("n_history", ctypes.c_int32),
+        ("history_tokens", ctypes.POINTER(ctypes.c_int32)),
+        ("history_counts", ctypes.POINTER(ctypes.c_float)),
+        ("n_bias", ctypes.c_int32),
+        ("bias_tokens", ctypes.POINTER(ctypes.c_int32)),
+        ("bias_values", ctypes.POINTER(ctypes.c_float)),
+        ("uniform", ctypes.c_double),
+    ]
+
+
 class HbError(RuntimeError):
     def __init__(self, code, message):
         super().__init__(f"libhawkb200 error {code}: {message}")
@@ -97,6 +118,11 @@ SIGNATURES = {
     "hb_gemv_scratch_bytes": (ctypes.c_size_t, [_I, _I]),
     "hb_gemv": (_I, [_P, _P, _I, _I, _I, _P, _I, _P, _I, _P, _P, ctypes.c_size_t, _P]),
     "hb_gemv_noalloc": (_I, [_P, _P, _I, _I, _I, _P, _I, _P, _I, _P, _P]),
+    "hb_sampler_create": (_I, [_I, _I, ctypes.POINTER(_P)]),
+    "hb_sampler_select": (_I, [_P, _P, _I, ctypes.POINTER(HbSampling), _I32P]),
+    "hb_sampler_destroy": (_I, [_P]),
+    "hb_sample": (_I, [_P, _I, ctypes.POINTER(HbSampling), _I32P]),
+    "hb_read_logits": (_I, [_P, _I, _FP]),
     "hb_library_error": (ctypes.c_char_p, []),
     "hb_device_sm_count": (_I, [_I]),
 }

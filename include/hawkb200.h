@@ -46,8 +46,10 @@ enum { HB_WEIGHTS_BF16 = 0, HB_WEIGHTS_W8 = 1 };
 
 /* hb_step / hb_prefill / hb_step_batch flags */
 enum {
-  HB_STEP_ARGMAX = 1,   /* run final norm + LM head + argmax */
-  HB_STEP_LOGITS = 2    /* also copy the FP32 logits out (implies ARGMAX) */
+  HB_STEP_ARGMAX = 1,         /* run final norm + LM head + argmax */
+  HB_STEP_LOGITS = 2,         /* also copy the FP32 logits out (implies ARGMAX) */
+  HB_STEP_DEVICE_LOGITS = 4   /* keep the FP32 logits on the device for hb_sample
+                                 (implies ARGMAX; no copy to the host) */
 };
 
 /* Byte offsets (from the start of the weight blob) of one layer's tensors.
@@ -200,6 +202,53 @@ int hb_gemv(const void *w_dev, const float *scales_dev, int weight_format,
 int hb_gemv_noalloc(const void *w_dev, const float *scales_dev, int weight_format,
                     int rows, int k, const void *x_dev, int batch, void *y_dev,
                     int flags, int32_t *argmax_dev, void *stream);
+
+/* ---- token sampling on the device -------------------------------------
+ * The selection of the reference's Sampler.select
+ * (npu_llm/runtime/sampling.py:416-445, which the host runs on a logits copy
+ * at npu_llm/runtime/generate.py:1070-1080): penalties over the history,
+ * logit bias, temperature (0 = argmax), top-k, top-p and the multinomial
+ * draw, in that order and with NumPy's FP32/FP64 rounding and summation
+ * order.  The one random number the draw consumes, `uniform`, is the
+ * request generator's next Generator.random() on the host (what
+ * Generator.choice would consume), so a seeded request keeps its stream.
+ * history_* are the unique in-vocabulary history tokens and their counts
+ * (np.unique of the history, as sampling.py:346-353 computes them); bias_*
+ * the in-vocabulary logit_bias entries, each token once.  Parameters that
+ * cannot reorder the logits (the reference's `greedy`) select the argmax
+ * and ignore `uniform`.  Returns HB_ERR_UNSUPPORTED (token -1) when top_p
+ * keeps more than 4096 candidates -- the caller then selects on the host;
+ * HB_ERR_INVALID_ARG for out-of-range parameters or ids.  Vocabularies up
+ * to 262,144 entries. */
+typedef struct {
+  float temperature, top_p, repetition_penalty, presence_penalty, frequency_penalty;
+  int32_t top_k;
+  int32_t n_history;
+  const int32_t *history_tokens;
+  const float *history_counts;
+  int32_t n_bias;
+  const int32_t *bias_tokens;
+  const float *bias_values;
+  double uniform;
+} hb_sampling;
+
+typedef struct hb_sampler hb_sampler;
+/* A standalone sampler for `vocab`-wide logits on `device` (owns its device
+ * scratch and its stream). */
+int hb_sampler_create(int vocab, int device, hb_sampler **out);
+/* Select from `logits` (host memory, or device memory when
+ * logits_on_device is nonzero). */
+int hb_sampler_select(hb_sampler *sampler, const float *logits, int logits_on_device,
+                      const hb_sampling *params, int32_t *token_out);
+int hb_sampler_destroy(hb_sampler *sampler);
+/* Select from row `row` of the logits the engine's last hb_step /
+ * hb_step_batch left on the device (HB_STEP_DEVICE_LOGITS), on the
+ * engine's stream. */
+int hb_sample(hb_engine *engine, int row, const hb_sampling *params, int32_t *token_out);
+/* Copy rows [0, n_rows) of the FP32 logits the last step left on the device
+ * to logits_out (host, n_rows x vocab) -- the host-selection fallback after
+ * hb_sample returned HB_ERR_UNSUPPORTED, without recomputing the step. */
+int hb_read_logits(hb_engine *engine, int n_rows, float *logits_out);
 
 /* Library-level error text (for calls that have no engine, e.g. hb_gemv). */
 const char *hb_library_error(void);
