@@ -90,38 +90,74 @@ __device__ __forceinline__ float samp_unkey(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
+// Visit j = threadIdx.x + k * kSampThreads for k = 0, 1, ... with the loads
+// of eight consecutive visits issued before their bodies run, so one CTA
+// keeps enough loads in flight to stream the vector from L2.
+template <class F>
+__device__ __forceinline__ void samp_map(const float *src, int V, F &&body) {
+  for (int base = threadIdx.x; base < V; base += 8 * kSampThreads) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = base + u * kSampThreads;
+      v[u] = j < V ? src[j] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = base + u * kSampThreads;
+      if (j < V) body(j, v[u]);
+    }
+  }
+}
+
 __device__ __forceinline__ float samp_add(float a, float b) { return __fadd_rn(a, b); }
 __device__ __forceinline__ double samp_add(double a, double b) { return __dadd_rn(a, b); }
 
-// np.add.reduce of one leaf: < 8 values from zero, else eight accumulators.
-template <class T, class F>
-__device__ T leaf_sum(int lo, int n, F &&elem) {
-  if (n < 8) {
-    T r = T(0);
-    for (int i = 0; i < n; ++i) r = samp_add(r, elem(lo + i));
-    return r;
-  }
-  T r[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) r[j] = elem(lo + j);
-  int i = 8;
-  for (; i < n - n % 8; i += 8) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) r[j] = samp_add(r[j], elem(lo + i + j));
-  }
-  T res = samp_add(samp_add(samp_add(r[0], r[1]), samp_add(r[2], r[3])),
-                   samp_add(samp_add(r[4], r[5]), samp_add(r[6], r[7])));
-  for (; i < n; ++i) res = samp_add(res, elem(lo + i));
-  return res;
-}
-
 // Sum of elem(0..V-1) in NumPy's pairwise order.  All threads call it.
+// Leaves go to groups of eight lanes: lane j of a group keeps accumulator j
+// (elements j, j + 8, ... of the leaf, read coalesced across the group), the
+// eight are combined as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) with shuffles,
+// and the group's first lane adds the tail left to right.
 template <class T, class F>
 __device__ T tree_sum(const SampleParams &p, SampleSmem &sm, F &&elem) {
   T *vals = reinterpret_cast<T *>(sm.tree);
-  for (int l = threadIdx.x; l < p.n_leaves; l += kSampThreads) {
-    const int2 lf = p.leaves[l];
-    vals[l] = leaf_sum<T>(lf.x, lf.y, elem);
+  const int lane = threadIdx.x & 31, j = lane & 7;
+  const int group = (threadIdx.x >> 3);  // 128 groups of 8 lanes
+  for (int base = 0; base < p.n_leaves; base += kSampThreads / 8) {
+    const int l = base + group;
+    int lo = 0, n = 0;
+    if (l < p.n_leaves) {
+      const int2 lf = p.leaves[l];
+      lo = lf.x;
+      n = lf.y;
+    }
+    T r = T(0);
+    if (n >= 8) {  // a leaf has at most 128 values: up to 16 per lane, loaded first
+      const int whole = n - n % 8;
+      T v[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) v[k] = 8 * k < whole ? elem(lo + 8 * k + j) : T(0);
+      r = v[0];
+#pragma unroll
+      for (int k = 1; k < 16; ++k)
+        if (8 * k < whole) r = samp_add(r, v[k]);
+    }
+    const T s1 = samp_add(r, __shfl_down_sync(0xffffffffu, r, 1));
+    const T s2 = samp_add(s1, __shfl_down_sync(0xffffffffu, s1, 2));
+    const T s4 = samp_add(s2, __shfl_down_sync(0xffffffffu, s2, 4));
+    if (j == 0 && l < p.n_leaves) {
+      T res;
+      int i;
+      if (n < 8) {
+        res = T(0);
+        i = 0;
+      } else {
+        res = s4;
+        i = n - n % 8;
+      }
+      for (; i < n; ++i) res = samp_add(res, elem(lo + i));
+      vals[l] = res;
+    }
   }
   __syncthreads();
   int start = 0;
@@ -176,7 +212,7 @@ __device__ __forceinline__ int samp_block_min(SampleSmem &sm, int v) {
 __device__ int samp_argmax(const SampleParams &p, SampleSmem &sm) {
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int j = threadIdx.x; j < p.V; j += kSampThreads) argmax_merge(bv, bi, p.s[j], j);
+  samp_map(p.s, p.V, [&](int j, float v) { argmax_merge(bv, bi, v, j); });
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -205,14 +241,24 @@ __device__ uint32_t samp_kth_largest(const SampleParams &p, SampleSmem &sm, int 
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int i = threadIdx.x; i < kSampWarps * 256; i += kSampThreads) (&sm.hist[0][0])[i] = 0u;
     __syncthreads();
-    for (int j = threadIdx.x; j < vpad; j += kSampThreads) {
-      int bin = 256;
-      if (j < p.V) {
-        const uint32_t key = samp_key(p.s[j]);
-        if ((key & mask) == prefix) bin = (key >> shift) & 255;
+    for (int b0 = threadIdx.x; b0 < vpad; b0 += 4 * kSampThreads) {
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = b0 + u * kSampThreads;
+        v[u] = j < p.V ? p.s[j] : 0.f;
       }
-      const unsigned peers = __match_any_sync(0xffffffffu, bin);
-      if (bin < 256 && lane == __ffs(peers) - 1) sm.hist[warp][bin] += __popc(peers);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = b0 + u * kSampThreads;
+        int bin = 256;
+        if (j < p.V) {
+          const uint32_t key = samp_key(v[u]);
+          if ((key & mask) == prefix) bin = (key >> shift) & 255;
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, bin);
+        if (bin < 256 && lane == __ffs(peers) - 1) sm.hist[warp][bin] += __popc(peers);
+      }
     }
     __syncthreads();
     if (threadIdx.x < 256) {
@@ -247,7 +293,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p)
   float *s = p.s;
 
   // 1-2. working copy, penalties, bias (each token appears once per list)
-  for (int j = tid; j < V; j += kSampThreads) s[j] = p.logits[j];
+  samp_map(p.logits, V, [&](int j, float v) { s[j] = v; });
   __syncthreads();
   for (int t = tid; t < p.n_hist; t += kSampThreads) {
     const int tok = p.hist_tok[t];
@@ -273,14 +319,15 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p)
   }
 
   // 3. temperature
-  for (int j = tid; j < V; j += kSampThreads) s[j] = __fdiv_rn(s[j], p.temperature);
+  samp_map(s, V, [&](int j, float v) { s[j] = __fdiv_rn(v, p.temperature); });
   __syncthreads();
 
   // 4. top-k
   if (p.top_k > 0 && p.top_k < V) {
     const float thr = samp_unkey(samp_kth_largest(p, sm, p.top_k));
-    for (int j = tid; j < V; j += kSampThreads)
-      if (s[j] < thr) s[j] = -INFINITY;
+    samp_map(s, V, [&](int j, float v) {
+      if (v < thr) s[j] = -INFINITY;
+    });
     __syncthreads();
   }
 
@@ -288,13 +335,12 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p)
   if (p.top_p < 1.0f) {
     int cand = 0;
     float peak = -INFINITY;
-    for (int j = tid; j < V; j += kSampThreads) {
-      const float v = s[j];
+    samp_map(s, V, [&](int, float v) {
       if (isfinite(v)) {
         ++cand;
         peak = fmaxf(peak, v);
       }
-    }
+    });
     const int C = samp_block_sum(sm, cand);
     peak = samp_block_max(sm, peak);
     // the candidates: every finite score, or those >= the kTopPMax-th largest
@@ -360,10 +406,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p)
       total = tree_sum<float>(p, sm, [&](int i) { return i < cnt ? sm.probs[i] : 0.f; });
     } else {
       // the tail's order is unknown: the denominator in index order instead
-      for (int j = tid; j < V; j += kSampThreads) {
-        const float v = s[j];
-        p.e[j] = isfinite(v) ? expf(__fsub_rn(v, peak)) : 0.f;
-      }
+      samp_map(s, V, [&](int j, float v) { p.e[j] = isfinite(v) ? expf(__fsub_rn(v, peak)) : 0.f; });
       __syncthreads();
       total = tree_sum<float>(p, sm, [&](int j) { return p.e[j]; });
     }
@@ -399,8 +442,9 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p)
     }
     const uint32_t cut_key = static_cast<uint32_t>(sm.keys[keep - 1] >> 32);
     const float cut = samp_unkey(cut_key);
-    for (int j = tid; j < V; j += kSampThreads)
-      if (s[j] < cut) s[j] = -INFINITY;
+    samp_map(s, V, [&](int j, float v) {
+      if (v < cut) s[j] = -INFINITY;
+    });
     __syncthreads();
     for (int i = keep + tid; i < cnt; i += kSampThreads)  // ties with the cut beyond it
       if (static_cast<uint32_t>(sm.keys[i] >> 32) == cut_key) s[static_cast<uint32_t>(sm.keys[i])] = -INFINITY;
@@ -409,14 +453,12 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p)
 
   // 6. guarded softmax in index order, float64 renormalisation, the draw
   float peak = -INFINITY;
-  for (int j = tid; j < V; j += kSampThreads)
-    if (isfinite(s[j])) peak = fmaxf(peak, s[j]);
+  samp_map(s, V, [&](int, float v) {
+    if (isfinite(v)) peak = fmaxf(peak, v);
+  });
   peak = samp_block_max(sm, peak);
   if (!isfinite(peak)) peak = 0.f;
-  for (int j = tid; j < V; j += kSampThreads) {
-    const float v = s[j];
-    p.e[j] = isfinite(v) ? expf(__fsub_rn(v, peak)) : 0.f;
-  }
+  samp_map(s, V, [&](int j, float v) { p.e[j] = isfinite(v) ? expf(__fsub_rn(v, peak)) : 0.f; });
   __syncthreads();
   const float total = tree_sum<float>(p, sm, [&](int j) { return p.e[j]; });
   if (!(total > 0.f) || !isfinite(total)) {  // every candidate underflowed
@@ -429,25 +471,23 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p)
   }
   // the float32 probabilities, in place
   float *e = p.e;
-  for (int j = tid; j < V; j += kSampThreads) e[j] = __fdiv_rn(e[j], total);
+  samp_map(e, V, [&](int j, float v) { e[j] = __fdiv_rn(v, total); });
   __syncthreads();
   const double s64 = tree_sum<double>(p, sm, [&](int j) { return static_cast<double>(e[j]); });
-  // Cumulative sums over contiguous chunks, then the first crossing of u.
-  // Scaling by 1/s64 and comparing run > u * last instead of dividing moves
-  // the boundaries by an ulp of a double, far below the float32 effects.
+  // Cumulative sums: warp w owns the contiguous segment w of the vector and
+  // reads it 32 values at a time; warp sums, a scan over the warps, then
+  // each warp walks its segment to the first crossing of u.  Scaling by
+  // 1/s64 and comparing run > u * last instead of dividing moves the
+  // boundaries by an ulp of a double, far below the float32 effects.
   const double inv = __ddiv_rn(1.0, s64);
-  const int chunk = (V + kSampThreads - 1) / kSampThreads;
-  const int j0 = min(V, tid * chunk), j1 = min(V, j0 + chunk);
+  const int seg = (V + kSampWarps - 1) / kSampWarps;
+  const int j0 = min(V, warp * seg), j1 = min(V, j0 + seg);
   double local = 0.0;
-  for (int j = j0; j < j1; ++j) local = __dadd_rn(local, __dmul_rn(static_cast<double>(e[j]), inv));
-  // block exclusive scan of the chunk sums
-  double incl = local;
+#pragma unroll 8
+  for (int j = j0 + lane; j < j1; j += 32) local = __dadd_rn(local, __dmul_rn(static_cast<double>(e[j]), inv));
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const double t = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl = __dadd_rn(incl, t);
-  }
-  if (lane == 31) sm.wscan[warp] = incl;
+  for (int o = 16; o > 0; o >>= 1) local = __dadd_rn(local, __shfl_xor_sync(0xffffffffu, local, o));
+  if (lane == 0) sm.wscan[warp] = local;
   __syncthreads();
   if (tid == 0) {
     double acc = 0.0;
@@ -460,18 +500,25 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p)
   }
   __syncthreads();
   const double last = sm.dmisc[0];
-  double excl = __shfl_up_sync(0xffffffffu, incl, 1);
-  if (lane == 0) excl = 0.0;
-  double run = __dadd_rn(sm.wscan[warp], excl);
   const double target = __dmul_rn(p.u, last);
+  double run = sm.wscan[warp];
   int first = 0x7fffffff;
-  if (__dadd_rn(run, local) > target) {  // the crossing is in this chunk
-    for (int j = j0; j < j1; ++j) {
-      run = __dadd_rn(run, __dmul_rn(static_cast<double>(e[j]), inv));
-      if (run > target) {
-        first = j;
+  if (__dadd_rn(run, local) > target) {  // the crossing is in this segment
+    for (int jb = j0; jb < j1; jb += 32) {
+      const int jj = jb + lane;
+      double v = jj < j1 ? __dmul_rn(static_cast<double>(e[jj]), inv) : 0.0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v = __dadd_rn(v, t);
+      }
+      const double here = __dadd_rn(run, v);
+      const unsigned hit = __ballot_sync(0xffffffffu, jj < j1 && here > target);
+      if (hit) {
+        first = jb + __ffs(hit) - 1;
         break;
       }
+      run = __dadd_rn(run, __shfl_sync(0xffffffffu, v, 31));
     }
   }
   first = samp_block_min(sm, first);
