@@ -964,6 +964,8 @@ struct hb_sampler {
   float *d_floats = nullptr; // [kMaxHistory hist_cnt][kMaxBias bias_val]
   int *h_ints = nullptr;     // pinned staging, same layout
   float *h_floats = nullptr;
+  double *d_lp = nullptr, *h_lp = nullptr;  // [1 + kMaxTopLogprobs] log-probabilities
+  int *d_lp_ids = nullptr, *h_lp_ids = nullptr;  // [kMaxTopLogprobs + 1]
 };
 
 namespace {
@@ -1136,6 +1138,39 @@ int sampler_run(hb_sampler *sp, cudaStream_t stream, const float *logits_dev, co
   return HB_OK;
 }
 
+int sampler_logprobs_run(hb_sampler *sp, cudaStream_t stream, const float *logits_dev, int token, int n_top,
+                         double *token_logprob, int32_t *top_ids, double *top_logprobs) {
+  const int V = sp->vocab;
+  if (!token_logprob || (n_top > 0 && (!top_ids || !top_logprobs)))
+    return sampler_fail(HB_ERR_INVALID_ARG, "output pointer is NULL");
+  if (token < 0 || token >= V) return sampler_fail(HB_ERR_INVALID_ARG, "token %d outside the vocabulary", token);
+  if (n_top < 0 || n_top > hb::kMaxTopLogprobs || n_top > V)
+    return sampler_fail(HB_ERR_INVALID_ARG, "top_logprobs %d outside [0, %d]", n_top, hb::kMaxTopLogprobs);
+  hb::SampleParams P{};
+  P.logits = logits_dev;
+  P.s = sp->d_s;
+  P.e = sp->d_e;
+  P.V = V;
+  P.leaves = sp->d_leaves;
+  P.n_leaves = sp->n_leaves;
+  P.nodes = sp->d_nodes;
+  P.n_nodes = sp->n_nodes;
+  P.level_end = sp->d_levels;
+  P.n_levels = sp->n_levels;
+  hb::logprob_kernel<<<1, hb::kSampThreads, sizeof(hb::SampleSmem), stream>>>(P, token, n_top, sp->d_lp, sp->d_lp_ids);
+  HB_SCUDA(cudaGetLastError());
+  HB_SCUDA(cudaMemcpyAsync(sp->h_lp, sp->d_lp, sizeof(double) * (1 + n_top), cudaMemcpyDeviceToHost, stream));
+  HB_SCUDA(cudaMemcpyAsync(sp->h_lp_ids, sp->d_lp_ids, sizeof(int) * (n_top + 1), cudaMemcpyDeviceToHost, stream));
+  HB_SCUDA(cudaStreamSynchronize(stream));
+  if (sp->h_lp_ids[n_top] != 0) return sampler_fail(HB_ERR_INVALID_ARG, "logits contain no finite value");
+  *token_logprob = sp->h_lp[0];
+  for (int i = 0; i < n_top; ++i) {
+    top_ids[i] = sp->h_lp_ids[i];
+    top_logprobs[i] = sp->h_lp[1 + i];
+  }
+  return HB_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1163,11 +1198,17 @@ int hb_sampler_create(int vocab, int device, hb_sampler **out) {
       (rc = sampler_alloc(&sp->d_e, vocab)) || (rc = sampler_alloc(&sp->d_leaves, sp->n_leaves)) ||
       (rc = sampler_alloc(&sp->d_nodes, sp->n_nodes)) || (rc = sampler_alloc(&sp->d_levels, sp->n_levels)) ||
       (rc = sampler_alloc(&sp->d_ints, 2 + kMaxHistory + kMaxBias)) ||
-      (rc = sampler_alloc(&sp->d_floats, kMaxHistory + kMaxBias)))
+      (rc = sampler_alloc(&sp->d_floats, kMaxHistory + kMaxBias)) ||
+      (rc = sampler_alloc(&sp->d_lp, 1 + hb::kMaxTopLogprobs)) ||
+      (rc = sampler_alloc(&sp->d_lp_ids, hb::kMaxTopLogprobs + 1)))
     return bail(rc);
   if (cudaHostAlloc(reinterpret_cast<void **>(&sp->h_ints), sizeof(int) * (2 + kMaxHistory + kMaxBias),
                     cudaHostAllocDefault) != cudaSuccess ||
       cudaHostAlloc(reinterpret_cast<void **>(&sp->h_floats), sizeof(float) * (kMaxHistory + kMaxBias),
+                    cudaHostAllocDefault) != cudaSuccess ||
+      cudaHostAlloc(reinterpret_cast<void **>(&sp->h_lp), sizeof(double) * (1 + hb::kMaxTopLogprobs),
+                    cudaHostAllocDefault) != cudaSuccess ||
+      cudaHostAlloc(reinterpret_cast<void **>(&sp->h_lp_ids), sizeof(int) * (hb::kMaxTopLogprobs + 1),
                     cudaHostAllocDefault) != cudaSuccess)
     return bail(sampler_fail(HB_ERR_CUDA, "pinned host allocation failed"));
   if (cudaMemcpy(sp->d_leaves, pl.leaves.data(), sizeof(int2) * sp->n_leaves, cudaMemcpyHostToDevice) != cudaSuccess ||
@@ -1175,6 +1216,8 @@ int hb_sampler_create(int vocab, int device, hb_sampler **out) {
       (sp->n_levels && cudaMemcpy(sp->d_levels, pl.level_end.data(), sizeof(int) * sp->n_levels, cudaMemcpyHostToDevice) != cudaSuccess))
     return bail(sampler_fail(HB_ERR_CUDA, "sampler plan upload failed"));
   if (cudaFuncSetAttribute(reinterpret_cast<const void *>(&hb::sample_kernel),
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sizeof(hb::SampleSmem))) != cudaSuccess ||
+      cudaFuncSetAttribute(reinterpret_cast<const void *>(&hb::logprob_kernel),
                            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sizeof(hb::SampleSmem))) != cudaSuccess ||
       cudaStreamCreateWithFlags(&sp->own_stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(sampler_fail(HB_ERR_CUDA, "sampler set-up failed"));
@@ -1195,15 +1238,30 @@ int hb_sampler_select(hb_sampler *sp, const float *logits, int logits_on_device,
   return sampler_run(sp, sp->own_stream, dev, params, token_out);
 }
 
+int hb_sampler_logprobs(hb_sampler *sp, const float *logits, int logits_on_device, int token, int n_top,
+                        double *token_logprob, int32_t *top_ids, double *top_logprobs) {
+  if (!sp || !logits) return sampler_fail(HB_ERR_INVALID_ARG, "sampler or logits is NULL");
+  DeviceScope device_scope_(sp->device);
+  if (!device_scope_.ok) return sampler_fail(HB_ERR_CUDA, "cudaSetDevice(%d) failed", sp->device);
+  const float *dev = logits;
+  if (!logits_on_device) {
+    HB_SCUDA(cudaMemcpyAsync(sp->d_in, logits, sizeof(float) * sp->vocab, cudaMemcpyHostToDevice, sp->own_stream));
+    dev = sp->d_in;
+  }
+  return sampler_logprobs_run(sp, sp->own_stream, dev, token, n_top, token_logprob, top_ids, top_logprobs);
+}
+
 int hb_sampler_destroy(hb_sampler *sp) {
   if (!sp) return HB_OK;
   DeviceScope device_scope_(sp->device);
   if (sp->own_stream) cudaStreamSynchronize(sp->own_stream);
-  void *dev[] = {sp->d_in, sp->d_s, sp->d_e, sp->d_leaves, sp->d_nodes, sp->d_levels, sp->d_ints, sp->d_floats};
+  void *dev[] = {sp->d_in, sp->d_s, sp->d_e, sp->d_leaves, sp->d_nodes, sp->d_levels, sp->d_ints, sp->d_floats,
+                 sp->d_lp, sp->d_lp_ids};
   for (void *p : dev)
     if (p) cudaFree(p);
-  if (sp->h_ints) cudaFreeHost(sp->h_ints);
-  if (sp->h_floats) cudaFreeHost(sp->h_floats);
+  void *host[] = {sp->h_ints, sp->h_floats, sp->h_lp, sp->h_lp_ids};
+  for (void *p : host)
+    if (p) cudaFreeHost(p);
   if (sp->own_stream) cudaStreamDestroy(sp->own_stream);
   delete sp;
   return HB_OK;
@@ -1217,6 +1275,20 @@ int hb_sample(hb_engine *e, int row, const hb_sampling *params, int32_t *token_o
   if (!e->sampler && (rc = hb_sampler_create(e->desc.vocab, e->device, &e->sampler)))
     return fail(e, rc, "%s", g_lib_error.c_str());
   rc = sampler_run(e->sampler, e->stream, e->d_logits + static_cast<size_t>(row) * e->desc.vocab, params, token_out);
+  if (rc) return fail(e, rc, "%s", g_lib_error.c_str());
+  return HB_OK;
+}
+
+int hb_logprobs(hb_engine *e, int row, int token, int n_top, double *token_logprob, int32_t *top_ids,
+                double *top_logprobs) {
+  int rc = check_engine(e);
+  if (rc) return rc;
+  if (row < 0 || row >= kMaxBatch || row >= e->desc.max_batch)
+    return fail(e, HB_ERR_INVALID_ARG, "row %d outside the batch", row);
+  if (!e->sampler && (rc = hb_sampler_create(e->desc.vocab, e->device, &e->sampler)))
+    return fail(e, rc, "%s", g_lib_error.c_str());
+  rc = sampler_logprobs_run(e->sampler, e->stream, e->d_logits + static_cast<size_t>(row) * e->desc.vocab, token,
+                            n_top, token_logprob, top_ids, top_logprobs);
   if (rc) return fail(e, rc, "%s", g_lib_error.c_str());
   return HB_OK;
 }

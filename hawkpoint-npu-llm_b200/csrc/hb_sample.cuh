@@ -528,4 +528,89 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p)
   }
 }
 
+// Log-probabilities for an OpenAI ``logprobs`` entry: the reference's
+// log_softmax (npu_llm/runtime/stopping.py:101-109: float64 scores, the
+// finite maximum subtracted, log of the pairwise float64 sum of exp) at
+// `token`, and the n_top largest entries (np.argpartition + argsort,
+// descending; equal scores by index descending).  Reads the raw logits.
+// out_vals[0] = token's log-probability, out_vals[1 + i] / out_ids[i] the
+// i-th largest; out_ids[n_top] = 1 when there was no finite score.
+constexpr int kMaxTopLogprobs = 32;
+
+__global__ void __launch_bounds__(kSampThreads, 1) logprob_kernel(SampleParams p, int token, int n_top,
+                                                                  double *out_vals, int *out_ids) {
+  extern __shared__ __align__(16) uint8_t samp_smem_raw[];
+  SampleSmem &sm = *reinterpret_cast<SampleSmem *>(samp_smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int V = p.V;
+  float *s = p.s;
+  float peak = -INFINITY;
+  int finite = 0;
+  samp_map(p.logits, V, [&](int j, float v) {
+    s[j] = v;
+    if (isfinite(v)) {
+      peak = fmaxf(peak, v);
+      ++finite;
+    }
+  });
+  __syncthreads();
+  peak = samp_block_max(sm, peak);
+  finite = samp_block_sum(sm, finite);
+  if (finite == 0) {
+    if (tid == 0) out_ids[n_top] = 1;
+    return;
+  }
+  const double dpeak = static_cast<double>(peak);
+  const double total = tree_sum<double>(p, sm, [&](int j) {
+    const float v = s[j];
+    return isfinite(v) ? exp(__dsub_rn(static_cast<double>(v), dpeak)) : 0.0;
+  });
+  const double lse = log(total);
+  auto logprob = [&](float v) {
+    return isfinite(v) ? __dsub_rn(__dsub_rn(static_cast<double>(v), dpeak), lse) : -INFINITY;
+  };
+  // the n_top largest: every score >= the n_top-th largest, sorted on chip
+  uint32_t thr = 0u;
+  if (n_top > 0 && n_top < V) thr = samp_kth_largest(p, sm, n_top);
+  if (tid == 0) sm.misc[2] = 0;
+  __syncthreads();
+  if (n_top > 0) {
+    const int vpad = (V + kSampThreads - 1) / kSampThreads * kSampThreads;
+    for (int j = tid; j < vpad; j += kSampThreads) {
+      bool take = false;
+      uint32_t key = 0u;
+      if (j < V) {
+        key = samp_key(s[j]);
+        take = key >= thr;
+      }
+      const unsigned ballot = __ballot_sync(0xffffffffu, take);
+      int base = 0;
+      if (lane == 0 && ballot) base = atomicAdd(&sm.misc[2], __popc(ballot));
+      base = __shfl_sync(0xffffffffu, base, 0);
+      if (take) {
+        const int slot = base + __popc(ballot & ((1u << lane) - 1u));
+        if (slot < kTopPMax) sm.keys[slot] = (static_cast<unsigned long long>(key) << 32) | static_cast<uint32_t>(j);
+      }
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    const int cnt = min(sm.misc[2], kTopPMax);
+    // selection sort of the first n_top (n_top <= kMaxTopLogprobs)
+    for (int i = 0; i < n_top && i < cnt; ++i) {
+      int best = i;
+      for (int k = i + 1; k < cnt; ++k)
+        if (sm.keys[k] > sm.keys[best]) best = k;
+      const unsigned long long t = sm.keys[i];
+      sm.keys[i] = sm.keys[best];
+      sm.keys[best] = t;
+      const int idx = static_cast<int>(static_cast<uint32_t>(sm.keys[i]));
+      out_ids[i] = idx;
+      out_vals[1 + i] = logprob(s[idx]);
+    }
+    out_vals[0] = logprob(s[token]);
+    out_ids[n_top] = 0;
+  }
+}
+
 }  // namespace hb

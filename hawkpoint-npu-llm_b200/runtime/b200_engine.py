@@ -141,6 +141,13 @@ class B200DecoderEngine:
 
         return sample_engine_row(self._lib, self._live(), self.vocab, row, params, history, uniform)
 
+    def logprobs(self, token, n_top, row=0):
+        """(log-probability of ``token``, top ids, top log-probabilities) of
+        the logits the last ``step_device_logits`` left on the device."""
+        from runtime.device_sampler import engine_logprobs
+
+        return engine_logprobs(self._lib, self._live(), row, token, n_top)
+
     def device_logits(self, rows=1):
         """Host copy of the FP32 logits the last step left on the device."""
         h = self._live()

@@ -88,6 +88,14 @@ class DeviceSampler:
                                          ctypes.byref(token))
         return _result(rc, token)
 
+    def logprobs(self, logits, token, n_top):
+        """(log-probability of ``token``, top ids, top log-probabilities) of
+        the reference's float64 log_softmax of ``logits``."""
+        logits = np.ascontiguousarray(logits, np.float32)
+        if logits.shape != (self.vocab,):
+            raise ValueError(f"logits must have shape ({self.vocab},)")
+        return _logprobs_call(self._lib.hb_sampler_logprobs, (self._handle, logits.ctypes.data, 0), token, n_top)
+
     def close(self):
         if self._handle:
             self._lib.hb_sampler_destroy(self._handle)
@@ -104,6 +112,22 @@ class DeviceSampler:
             self.close()
         except Exception:
             pass
+
+
+def _logprobs_call(fn, lead, token, n_top, engine=None):
+    tok_lp = ctypes.c_double()
+    ids = np.zeros(max(1, int(n_top)), np.int32)
+    vals = np.zeros(max(1, int(n_top)), np.float64)
+    dp = ctypes.POINTER(ctypes.c_double)
+    rc = fn(*lead, int(token), int(n_top), ctypes.byref(tok_lp), ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+            vals.ctypes.data_as(dp))
+    hb_lib.check(rc, engine)
+    return float(tok_lp.value), ids[:n_top].tolist(), vals[:n_top].tolist()
+
+
+def engine_logprobs(lib, handle, row, token, n_top):
+    """Log-probabilities from row ``row`` of an engine's device logits."""
+    return _logprobs_call(lib.hb_logprobs, (handle, int(row)), token, n_top, handle)
 
 
 def sample_engine_row(lib, handle, vocab, row, params, history, uniform):

@@ -201,14 +201,18 @@ class NPUDecoder:
         self._record_phase("prefill", began)
         return [elapsed / (end - start)] * (end - start)
 
-    def _sample_step(self, token_id, position, sampler, history):
-        """One position with the next token selected on the GPU: the
-        reference ``Sampler.select`` (npu_llm/runtime/sampling.py:416-445) run
-        on logits that never leave the device, with the sampler's own
-        generator supplying the one ``random()`` its draw consumes.  When the
-        device reports a top-p nucleus too large to sort on chip, the
-        generator is rewound and the host sampler selects from a copy of the
-        same logits, so the random stream is identical either way."""
+    def _sample_step(self, token_id, position, sampler, history, top_logprobs=None):
+        """One position with the next token selected on the GPU: argmax for
+        greedy parameters, else the reference ``Sampler.select``
+        (npu_llm/runtime/sampling.py:416-445) run on logits that never leave
+        the device, with the sampler's own generator supplying the one
+        ``random()`` its draw consumes.  When the device reports a top-p
+        nucleus too large to sort on chip, the generator is rewound and the
+        host sampler selects from a copy of the same logits, so the random
+        stream is identical either way.  With ``top_logprobs`` the OpenAI
+        logprobs entry comes from the device too (float64 log_softmax, as
+        npu_llm/runtime/stopping.py:101-109).  Returns (token, seconds,
+        entry or None)."""
         from runtime.device_sampler import draws_uniform
 
         if not 0 <= position < self.context_length:
@@ -218,18 +222,31 @@ class NPUDecoder:
             raise RuntimeError("decoder is closed")
         start = time.perf_counter()
         engine = self._engine
-        engine.step_device_logits(token_id, position)
-        rng = sampler._rng
-        state = rng.bit_generator.state
-        u = rng.random() if draws_uniform(sampler.params, engine.vocab) else None
-        token = engine.sample(sampler.params, history, u)
-        if token is None:
-            rng.bit_generator.state = state
-            token = int(sampler.select(engine.device_logits(), history))
+        argmax = engine.step_device_logits(token_id, position)
+        host_logits = None
+        if sampler.greedy:
+            token = argmax
+        else:
+            rng = sampler._rng
+            state = rng.bit_generator.state
+            u = rng.random() if draws_uniform(sampler.params, engine.vocab) else None
+            token = engine.sample(sampler.params, history, u)
+            if token is None:
+                rng.bit_generator.state = state
+                host_logits = engine.device_logits()
+                token = int(sampler.select(host_logits, history))
+        entry = None
+        if top_logprobs is not None:
+            if host_logits is not None:
+                entry = self._logprob_entry(host_logits, token, top_logprobs)
+            else:
+                count = min(top_logprobs, engine.vocab)
+                lp, ids, lps = engine.logprobs(token, count)
+                entry = self._logprob_entry_from(token, lp, ids if top_logprobs else [], lps)
         self._record_phase("npu_engine", start)
         if len(self._cached_prefix) == position:
             self._cached_prefix.append(int(token_id))
-        return token, time.perf_counter() - start
+        return token, time.perf_counter() - start, entry
 
     def _decode_step(self, token_id, position, **kwargs):
         del self._cached_prefix[position:]
@@ -237,6 +254,20 @@ class NPUDecoder:
         if len(self._cached_prefix) == position:
             self._cached_prefix.append(int(token_id))
         return result
+
+    def _logprob_entry_from(self, token_id, logprob, top_ids, top_values):
+        """The same entry from log-probabilities computed on the device."""
+
+        def describe(index, value):
+            return {
+                "token": self.tokenizer.decode([int(index)]),
+                "logprob": float(value),
+                "bytes": list(self.tokenizer.token_bytes(int(index))),
+            }
+
+        entry = describe(token_id, logprob)
+        entry["top_logprobs"] = [describe(i, v) for i, v in zip(top_ids, top_values)]
+        return entry
 
     def _logprob_entry(self, logits, token_id, top_logprobs):
         """OpenAI ``logprobs`` entry from the raw distribution."""
@@ -325,17 +356,20 @@ class NPUDecoder:
 
         # greedy without logprobs keeps the on-device argmax path
         select = None if sampler.greedy and top_logprobs is None else choose
-        # a sampled request without logprobs selects on the device when the
-        # sampler exposes its generator (the reference Sampler does)
+        # selection and logprobs on the device: greedy with logprobs, or a
+        # sampled request whose sampler exposes its generator (the reference
+        # Sampler does)
         device_sampling = (
-            select is not None and top_logprobs is None and getattr(self, "_engine", None) is not None
-            and getattr(sampler, "_rng", None) is not None and hasattr(sampler, "params")
+            select is not None and getattr(self, "_engine", None) is not None
+            and (sampler.greedy or (getattr(sampler, "_rng", None) is not None and hasattr(sampler, "params")))
             and os.environ.get("HAWKPOINT_DEVICE_SAMPLING", "1") != "0"
         )
 
         def step(token_id, position, final=True):
             if final and device_sampling:
-                return self._sample_step(token_id, position, sampler, history)
+                token, elapsed, state["entry"] = self._sample_step(token_id, position, sampler, history,
+                                                                   top_logprobs)
+                return token, elapsed
             return self._decode_step(token_id, position, select=select if final else None,
                                      compute_logits=final)
 

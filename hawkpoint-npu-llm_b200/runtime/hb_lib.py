@@ -123,6 +123,9 @@ SIGNATURES = {
     "hb_sampler_destroy": (_I, [_P]),
     "hb_sample": (_I, [_P, _I, ctypes.POINTER(HbSampling), _I32P]),
     "hb_read_logits": (_I, [_P, _I, _FP]),
+    "hb_sampler_logprobs": (_I, [_P, _P, _I, _I, _I, ctypes.POINTER(ctypes.c_double), _I32P,
+                                 ctypes.POINTER(ctypes.c_double)]),
+    "hb_logprobs": (_I, [_P, _I, _I, _I, ctypes.POINTER(ctypes.c_double), _I32P, ctypes.POINTER(ctypes.c_double)]),
     "hb_library_error": (ctypes.c_char_p, []),
     "hb_device_sm_count": (_I, [_I]),
 }

@@ -241,10 +241,21 @@ int hb_sampler_create(int vocab, int device, hb_sampler **out);
 int hb_sampler_select(hb_sampler *sampler, const float *logits, int logits_on_device,
                       const hb_sampling *params, int32_t *token_out);
 int hb_sampler_destroy(hb_sampler *sampler);
+/* Log-probabilities of an OpenAI `logprobs` entry from the raw logits: the
+ * reference's float64 log_softmax (npu_llm/runtime/stopping.py:101-109) at
+ * `token`, and the n_top (<= 32) largest entries in descending order (equal
+ * scores by index descending) as npu_llm/runtime/generate.py builds them
+ * with np.argpartition + argsort.  Differences from NumPy: the float64 exp
+ * and log of CUDA against the host libm (an ulp). */
+int hb_sampler_logprobs(hb_sampler *sampler, const float *logits, int logits_on_device, int token,
+                        int n_top, double *token_logprob, int32_t *top_ids, double *top_logprobs);
 /* Select from row `row` of the logits the engine's last hb_step /
  * hb_step_batch left on the device (HB_STEP_DEVICE_LOGITS), on the
  * engine's stream. */
 int hb_sample(hb_engine *engine, int row, const hb_sampling *params, int32_t *token_out);
+/* hb_sampler_logprobs on row `row` of the engine's device logits. */
+int hb_logprobs(hb_engine *engine, int row, int token, int n_top, double *token_logprob,
+                int32_t *top_ids, double *top_logprobs);
 /* Copy rows [0, n_rows) of the FP32 logits the last step left on the device
  * to logits_out (host, n_rows x vocab) -- the host-selection fallback after
  * hb_sample returned HB_ERR_UNSUPPORTED, without recomputing the step. */

@@ -149,6 +149,29 @@ def draws_uniform(params, vocab):
     return not params.greedy_for(vocab) and params.temperature != 0.0
 
 
+# -- logprobs ---------------------------------------------------------------------
+def log_softmax(logits):
+    """float64 log-probabilities (npu_llm/runtime/stopping.py:101-109): the
+    finite maximum subtracted, non-finite scores at -inf, minus the log of
+    the pairwise float64 sum of exp."""
+    scores = np.asarray(logits, dtype=np.float64)
+    finite = np.isfinite(scores)
+    if not finite.any():
+        raise ValueError("logits contain no finite value")
+    shifted = np.where(finite, scores - scores[finite].max(), -np.inf)
+    return shifted - np.log(np.exp(shifted).sum())
+
+
+def top_logprobs(values, count):
+    """The ``count`` largest log-probabilities, largest first, as the
+    decoder's logprobs entry orders them (argpartition + argsort)."""
+    count = min(count, values.shape[0])
+    if count <= 0:
+        return np.zeros(0, np.int64)
+    best = np.argpartition(values, -count)[-count:]
+    return best[np.argsort(values[best])[::-1]]
+
+
 # -- NumPy's summation order -------------------------------------------------
 def pairwise_sum(values):
     """``values.sum()`` for a contiguous 1-D float32 / float64 array, in

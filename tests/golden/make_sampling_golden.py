@@ -6,7 +6,8 @@ Run in a container that has the reference checkout (read-only) at
 imports the reference's ``runtime/sampling.py`` (pure NumPy), runs
 ``Sampler(params).select`` twice per case with a seeded generator, and writes
 ``sampling.npz`` next to this script: the two tokens the reference chose per
-case.  The cases themselves (logits, history, bias) are rebuilt from seeds by
+case, and the reference ``log_softmax`` (runtime/stopping.py) of the first
+logits at the first token and its five largest entries.  The cases themselves (logits, history, bias) are rebuilt from seeds by
 ``cases()`` and ``build()`` below, which do not touch the reference.  Nothing
 at test time reads the reference; ``tests/test_sampling.py`` replays the
 cases through ``oracle.sampling.select_with_uniform`` with the seed's
@@ -49,11 +50,14 @@ SCALES = (0.05, 1.0, 4.0)    # flat (random-init-like), moderate, peaked logits
 VOCABS = (1024, 4096)
 
 
-def load_reference(root):
-    spec = importlib.util.spec_from_file_location("reference_sampling", Path(root) / "npu_llm/runtime/sampling.py")
+def load_reference(root, name="sampling"):
+    spec = importlib.util.spec_from_file_location(f"reference_{name}", Path(root) / f"npu_llm/runtime/{name}.py")
     module = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(module)
     return module
+
+
+LOGPROB_TOP = 5
 
 
 def cases():
@@ -89,7 +93,9 @@ def main():
     if not args.reference:
         raise SystemExit("pass --reference or set REFERENCE_ROOT")
     ref = load_reference(args.reference)
+    stopping = load_reference(args.reference, "stopping")
     rows = []
+    lp_token, lp_top_ids, lp_top_vals = [], [], []
     for vocab, scale, spec, seed in cases():
         logits, history, bias = build(vocab, scale, spec, seed)
         t, top_p, top_k, rep, pres, freq, _, _ = spec
@@ -98,7 +104,17 @@ def main():
                                     seed=seed)
         sampler = ref.Sampler(params, vocab_size=vocab)
         rows.append([sampler.select(logits[0], history), sampler.select(logits[1], history)])
-    np.savez_compressed(HERE / "sampling.npz", tokens=np.asarray(rows, np.int64))
+        # the reference log_softmax of the first logits: the chosen token and the top entries
+        values = stopping.log_softmax(logits[0])
+        best = np.argpartition(values, -LOGPROB_TOP)[-LOGPROB_TOP:]
+        best = best[np.argsort(values[best])[::-1]]
+        lp_token.append(values[rows[-1][0]])
+        lp_top_ids.append(best)
+        lp_top_vals.append(values[best])
+    np.savez_compressed(HERE / "sampling.npz", tokens=np.asarray(rows, np.int64),
+                        logprob_token=np.asarray(lp_token, np.float64),
+                        logprob_top_ids=np.asarray(lp_top_ids, np.int64),
+                        logprob_top_values=np.asarray(lp_top_vals, np.float64))
     print(f"wrote {len(rows)} cases to {HERE / 'sampling.npz'}")
 
 

@@ -66,6 +66,16 @@ def test_oracle_matches_reference_sampler():
         assert got == expect, (params, seed)
 
 
+def test_oracle_log_softmax_matches_reference():
+    data = np.load(GOLDEN / "sampling.npz")
+    for i, (logits, history, params, seed, expect) in enumerate(golden_cases()):
+        values = osamp.log_softmax(logits[0])
+        assert abs(values[expect[0]] - data["logprob_token"][i]) < 1e-12
+        top = osamp.top_logprobs(values, 5)
+        assert top.tolist() == data["logprob_top_ids"][i].tolist()
+        assert np.allclose(values[top], data["logprob_top_values"][i], rtol=0, atol=1e-12)
+
+
 def test_draw_consumes_one_uniform_like_generator_choice():
     rng = np.random.default_rng(5)
     for seed in range(50):
@@ -262,7 +272,8 @@ def test_drop_in_falls_back_to_the_host_with_the_same_draw():
     decoder.model = types.SimpleNamespace(metadata={"vocab_size": vocab})
     params = osamp.Params(temperature=0.8, top_p=0.9)
     sampler = OracleSampler(params, vocab, seed=17)
-    token, _ = decoder._sample_step(4, 0, sampler, [4])
+    token, _, entry = decoder._sample_step(4, 0, sampler, [4])
+    assert entry is None
     first_u = np.random.default_rng(17).random()
     assert calls[1] == ("sample", first_u)
     assert token == osamp.select_with_uniform(logits, [4], params, first_u)
@@ -294,7 +305,7 @@ def test_drop_in_device_sampling_matches_host_sampling():
             engine.step(tok, pos, logits=False)
         tok, pos = prompt[-1], len(prompt) - 1
         for _ in range(12):
-            a, _ = decoder._sample_step(tok, pos, dev_sampler, history)
+            a, _, _ = decoder._sample_step(tok, pos, dev_sampler, history)
             logits = engine.step(tok, pos, logits=True)
             b = host_sampler.select(logits, history)
             if a != b:
@@ -304,6 +315,96 @@ def test_drop_in_device_sampling_matches_host_sampling():
         else:
             return
         pytest.fail(f"device {a} != host {b} at position {pos}")
+    finally:
+        decoder.close()
+        engine.close()
+
+
+def _check_logprobs(got, logits, token, n_top):
+    values = osamp.log_softmax(logits)
+    tok_lp, ids, lps = got
+    assert abs(tok_lp - values[token]) < 1e-9
+    want = osamp.top_logprobs(values, n_top)
+    assert np.allclose(lps, values[want], rtol=0, atol=1e-9)
+    # the same set of entries; equal log-probabilities may come in any order
+    assert np.allclose(values[ids], values[want], rtol=0, atol=1e-12)
+    assert len(set(ids)) == len(ids)
+
+
+@pytest.mark.gpu
+def test_device_logprobs_match_reference_log_softmax():
+    from runtime.device_sampler import DeviceSampler
+
+    data = np.load(GOLDEN / "sampling.npz")
+    samplers = {}
+    try:
+        for i, (logits, history, params, seed, expect) in enumerate(golden_cases()):
+            vocab = logits[0].shape[0]
+            dev = samplers.setdefault(vocab, DeviceSampler(vocab))
+            tok_lp, ids, lps = dev.logprobs(logits[0], expect[0], 5)
+            assert abs(tok_lp - data["logprob_token"][i]) < 1e-9
+            assert ids == data["logprob_top_ids"][i].tolist()
+            assert np.allclose(lps, data["logprob_top_values"][i], rtol=0, atol=1e-9)
+        rng = np.random.default_rng(4)
+        with DeviceSampler(151936) as dev:
+            for scale in (0.05, 3.0):
+                for n_top in (0, 1, 20):
+                    logits = (rng.standard_normal(151936) * scale).astype(np.float32)
+                    logits[rng.integers(0, 151936, 10)] = -np.inf
+                    token = int(rng.integers(0, 151936))
+                    while not np.isfinite(logits[token]):
+                        token = int(rng.integers(0, 151936))
+                    _check_logprobs(dev.logprobs(logits, token, n_top), logits, token, n_top)
+    finally:
+        for dev in samplers.values():
+            dev.close()
+
+
+@pytest.mark.gpu
+def test_drop_in_device_logprobs_match_host_entries():
+    """Greedy and sampled requests with logprobs: the entries built from the
+    device's log-probabilities equal those the host builds from the logits."""
+    import types
+
+    from runtime import synthetic
+    from runtime.b200_engine import B200DecoderEngine
+    from runtime.generate import NPUDecoder
+
+    model = synthetic.build("tiny-qwen", seed=44)
+    vocab = model.shape.vocab
+    decoder = NPUDecoder(model)
+    engine = B200DecoderEngine(model, max_batch=1)
+
+    class Tok:
+        def decode(self, ids):
+            return "".join(f"<{t}>" for t in ids)
+
+        def token_bytes(self, t):
+            return self.decode([t]).encode()
+
+    decoder.tokenizer = Tok()
+    try:
+        prompt = synthetic.prompt_ids(vocab, 5, seed=9)
+        for params in (osamp.Params(), osamp.Params(temperature=0.9, top_k=100)):
+            decoder._engine.reset()
+            engine.reset()
+            dev_sampler, host_sampler = OracleSampler(params, vocab, 3), OracleSampler(params, vocab, 3)
+            history = list(prompt)
+            for pos, tok in enumerate(prompt[:-1]):
+                decoder.decode_token(tok, pos, compute_logits=False)
+                engine.step(tok, pos, logits=False)
+            tok, pos = prompt[-1], len(prompt) - 1
+            for _ in range(4):
+                a, _, entry = decoder._sample_step(tok, pos, dev_sampler, history, top_logprobs=3)
+                logits = engine.step(tok, pos, logits=True)
+                b = host_sampler.select(logits, history)
+                assert a == b
+                values = osamp.log_softmax(logits)
+                assert abs(entry["logprob"] - values[a]) < 1e-9
+                want = osamp.top_logprobs(values, 3)
+                assert [e["token"] for e in entry["top_logprobs"]] == [f"<{i}>" for i in want]
+                history.append(a)
+                tok, pos = a, pos + 1
     finally:
         decoder.close()
         engine.close()
