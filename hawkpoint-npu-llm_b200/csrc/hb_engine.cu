@@ -955,15 +955,19 @@ int hb_gemv_noalloc(const void *w_dev, const float *scales_dev, int weight_forma
 struct hb_sampler {
   int device = 0;
   int vocab = 0;
+  int rows = 1;              // rows selectable in one batch
   cudaStream_t own_stream = nullptr;
-  float *d_in = nullptr, *d_s = nullptr, *d_e = nullptr;
+  float *d_in = nullptr, *d_s = nullptr, *d_e = nullptr;  // d_s, d_e: [rows][vocab]
   int2 *d_leaves = nullptr, *d_nodes = nullptr;
   int *d_levels = nullptr;
   int n_leaves = 0, n_nodes = 0, n_levels = 0;
-  int *d_ints = nullptr;     // [2 out][kMaxHistory hist_tok][kMaxBias bias_tok]
-  float *d_floats = nullptr; // [kMaxHistory hist_cnt][kMaxBias bias_val]
-  int *h_ints = nullptr;     // pinned staging, same layout
+  // [2 rows: out][rows x kMaxHistory: history tokens][rows x kMaxBias: bias tokens]
+  int *d_ints = nullptr;
+  // [rows x kMaxHistory: history counts][rows x kMaxBias: bias values]
+  float *d_floats = nullptr;
+  int *h_ints = nullptr;     // pinned staging, same layouts
   float *h_floats = nullptr;
+  hb::SampleParams *d_params = nullptr, *h_params = nullptr;  // [rows]
   double *d_lp = nullptr, *h_lp = nullptr;  // [1 + kMaxTopLogprobs] log-probabilities
   int *d_lp_ids = nullptr, *h_lp_ids = nullptr;  // [kMaxTopLogprobs + 1]
 };
@@ -1048,12 +1052,13 @@ int sampler_alloc(T **p, size_t count) {
   return HB_OK;
 }
 
-// Select on `stream` from device logits.  The caller has made the sampler's
+// Validate one selection and stage its parameters for row `r` of the
+// sampler's scratch (P points at device memory; the host lists sit in the
+// pinned staging until sampler_upload).  The caller has made the sampler's
 // device current.
-int sampler_run(hb_sampler *sp, cudaStream_t stream, const float *logits_dev, const hb_sampling *q,
-                int32_t *token_out) {
+int sampler_prepare(hb_sampler *sp, int r, const float *logits_dev, const hb_sampling *q, hb::SampleParams &P) {
   const int V = sp->vocab;
-  if (!q || !token_out) return sampler_fail(HB_ERR_INVALID_ARG, "params or token_out is NULL");
+  if (!q) return sampler_fail(HB_ERR_INVALID_ARG, "params is NULL");
   auto finite = [](double v) { return v == v && v - v == 0.0; };
   if (!finite(q->temperature) || q->temperature < 0.f)
     return sampler_fail(HB_ERR_INVALID_ARG, "temperature must be finite and >= 0");
@@ -1079,11 +1084,11 @@ int sampler_run(hb_sampler *sp, cudaStream_t stream, const float *logits_dev, co
   const bool draws = !greedy && q->temperature != 0.f;
   if (draws && !(q->uniform >= 0.0 && q->uniform < 1.0))
     return sampler_fail(HB_ERR_INVALID_ARG, "uniform must be in [0, 1)");
-
-  hb::SampleParams P{};
+  const int R = sp->rows;
+  P = hb::SampleParams{};
   P.logits = logits_dev;
-  P.s = sp->d_s;
-  P.e = sp->d_e;
+  P.s = sp->d_s + static_cast<size_t>(r) * V;
+  P.e = sp->d_e + static_cast<size_t>(r) * V;
   P.V = V;
   P.temperature = greedy ? 0.f : q->temperature;
   P.top_p = q->top_p;
@@ -1095,9 +1100,9 @@ int sampler_run(hb_sampler *sp, cudaStream_t stream, const float *logits_dev, co
   // penalties apply only when one of them is not neutral (sampling.py:341-346)
   P.n_hist = (greedy || neutral) ? 0 : q->n_history;
   P.n_bias = greedy ? 0 : q->n_bias;
-  int *h_out = sp->h_ints;
-  int *h_htok = sp->h_ints + 2, *h_btok = sp->h_ints + 2 + kMaxHistory;
-  float *h_hcnt = sp->h_floats, *h_bval = sp->h_floats + kMaxHistory;
+  const size_t hist_off = static_cast<size_t>(r) * kMaxHistory, bias_off = static_cast<size_t>(r) * kMaxBias;
+  int *h_htok = sp->h_ints + 2 * R + hist_off, *h_btok = sp->h_ints + 2 * R + static_cast<size_t>(R) * kMaxHistory + bias_off;
+  float *h_hcnt = sp->h_floats + hist_off, *h_bval = sp->h_floats + static_cast<size_t>(R) * kMaxHistory + bias_off;
   for (int i = 0; i < P.n_hist; ++i) {
     h_htok[i] = q->history_tokens[i];
     h_hcnt[i] = q->history_counts[i];
@@ -1106,35 +1111,74 @@ int sampler_run(hb_sampler *sp, cudaStream_t stream, const float *logits_dev, co
     h_btok[i] = q->bias_tokens[i];
     h_bval[i] = q->bias_values[i];
   }
-  int *d_out = sp->d_ints;
-  P.hist_tok = sp->d_ints + 2;
-  P.bias_tok = sp->d_ints + 2 + kMaxHistory;
-  P.hist_cnt = sp->d_floats;
-  P.bias_val = sp->d_floats + kMaxHistory;
+  P.hist_tok = sp->d_ints + 2 * R + hist_off;
+  P.bias_tok = sp->d_ints + 2 * R + static_cast<size_t>(R) * kMaxHistory + bias_off;
+  P.hist_cnt = sp->d_floats + hist_off;
+  P.bias_val = sp->d_floats + static_cast<size_t>(R) * kMaxHistory + bias_off;
   P.leaves = sp->d_leaves;
   P.n_leaves = sp->n_leaves;
   P.nodes = sp->d_nodes;
   P.n_nodes = sp->n_nodes;
   P.level_end = sp->d_levels;
   P.n_levels = sp->n_levels;
-  P.out = d_out;
+  P.out = sp->d_ints + 2 * r;
+  return HB_OK;
+}
+
+// Copy a prepared row's lists from the staging to the device.
+int sampler_upload(hb_sampler *sp, cudaStream_t stream, const hb::SampleParams &P) {
+  const ptrdiff_t ti = P.hist_tok - sp->d_ints, bi = P.bias_tok - sp->d_ints;
+  const ptrdiff_t tf = P.hist_cnt - sp->d_floats, bf = P.bias_val - sp->d_floats;
   if (P.n_hist) {
-    HB_SCUDA(cudaMemcpyAsync(const_cast<int *>(P.hist_tok), h_htok, sizeof(int) * P.n_hist, cudaMemcpyHostToDevice, stream));
-    HB_SCUDA(cudaMemcpyAsync(const_cast<float *>(P.hist_cnt), h_hcnt, sizeof(float) * P.n_hist, cudaMemcpyHostToDevice, stream));
+    HB_SCUDA(cudaMemcpyAsync(sp->d_ints + ti, sp->h_ints + ti, sizeof(int) * P.n_hist, cudaMemcpyHostToDevice, stream));
+    HB_SCUDA(cudaMemcpyAsync(sp->d_floats + tf, sp->h_floats + tf, sizeof(float) * P.n_hist, cudaMemcpyHostToDevice, stream));
   }
   if (P.n_bias) {
-    HB_SCUDA(cudaMemcpyAsync(const_cast<int *>(P.bias_tok), h_btok, sizeof(int) * P.n_bias, cudaMemcpyHostToDevice, stream));
-    HB_SCUDA(cudaMemcpyAsync(const_cast<float *>(P.bias_val), h_bval, sizeof(float) * P.n_bias, cudaMemcpyHostToDevice, stream));
+    HB_SCUDA(cudaMemcpyAsync(sp->d_ints + bi, sp->h_ints + bi, sizeof(int) * P.n_bias, cudaMemcpyHostToDevice, stream));
+    HB_SCUDA(cudaMemcpyAsync(sp->d_floats + bf, sp->h_floats + bf, sizeof(float) * P.n_bias, cudaMemcpyHostToDevice, stream));
   }
+  return HB_OK;
+}
+
+// Select on `stream` from device logits.  The caller has made the sampler's
+// device current.
+int sampler_run(hb_sampler *sp, cudaStream_t stream, const float *logits_dev, const hb_sampling *q,
+                int32_t *token_out) {
+  if (!token_out) return sampler_fail(HB_ERR_INVALID_ARG, "token_out is NULL");
+  hb::SampleParams P;
+  int rc;
+  if ((rc = sampler_prepare(sp, 0, logits_dev, q, P)) || (rc = sampler_upload(sp, stream, P))) return rc;
   hb::sample_kernel<<<1, hb::kSampThreads, sizeof(hb::SampleSmem), stream>>>(P);
   HB_SCUDA(cudaGetLastError());
-  HB_SCUDA(cudaMemcpyAsync(h_out, d_out, sizeof(int) * 2, cudaMemcpyDeviceToHost, stream));
+  HB_SCUDA(cudaMemcpyAsync(sp->h_ints, sp->d_ints, sizeof(int) * 2, cudaMemcpyDeviceToHost, stream));
   HB_SCUDA(cudaStreamSynchronize(stream));
-  if (h_out[1] != 0) {
+  if (sp->h_ints[1] != 0) {
     *token_out = -1;
     return sampler_fail(HB_ERR_UNSUPPORTED, "top_p keeps more than %d candidates: select on the host", hb::kTopPMax);
   }
-  *token_out = h_out[0];
+  *token_out = sp->h_ints[0];
+  return HB_OK;
+}
+
+// Several selections in one launch: entry k from logits row rows[k] of
+// `logits_dev` ([rows][vocab]); tokens_out[k] = -1 where the top-p nucleus
+// is too large for the device.
+int sampler_run_batch(hb_sampler *sp, cudaStream_t stream, const float *logits_dev, int n, const int32_t *rows,
+                      const hb_sampling *q, int32_t *tokens_out, int max_row) {
+  if (!rows || !q || !tokens_out) return sampler_fail(HB_ERR_INVALID_ARG, "rows, params or tokens_out is NULL");
+  if (n < 1 || n > sp->rows) return sampler_fail(HB_ERR_INVALID_ARG, "%d selections outside [1, %d]", n, sp->rows);
+  for (int k = 0; k < n; ++k) {
+    if (rows[k] < 0 || rows[k] >= max_row) return sampler_fail(HB_ERR_INVALID_ARG, "row %d outside the batch", rows[k]);
+    int rc = sampler_prepare(sp, k, logits_dev + static_cast<size_t>(rows[k]) * sp->vocab, q + k, sp->h_params[k]);
+    if (!rc) rc = sampler_upload(sp, stream, sp->h_params[k]);
+    if (rc) return rc;
+  }
+  HB_SCUDA(cudaMemcpyAsync(sp->d_params, sp->h_params, sizeof(hb::SampleParams) * n, cudaMemcpyHostToDevice, stream));
+  hb::sample_batch_kernel<<<n, hb::kSampThreads, sizeof(hb::SampleSmem), stream>>>(sp->d_params);
+  HB_SCUDA(cudaGetLastError());
+  HB_SCUDA(cudaMemcpyAsync(sp->h_ints, sp->d_ints, sizeof(int) * 2 * n, cudaMemcpyDeviceToHost, stream));
+  HB_SCUDA(cudaStreamSynchronize(stream));
+  for (int k = 0; k < n; ++k) tokens_out[k] = sp->h_ints[2 * k + 1] != 0 ? -1 : sp->h_ints[2 * k];
   return HB_OK;
 }
 
@@ -1173,9 +1217,17 @@ int sampler_logprobs_run(hb_sampler *sp, cudaStream_t stream, const float *logit
 
 }  // namespace
 
+// A sampler with scratch for `rows` selections per launch (the engine's has
+// one per batch row).
+int sampler_create_rows(int vocab, int device, int rows, hb_sampler **out);
+
 extern "C" {
 
-int hb_sampler_create(int vocab, int device, hb_sampler **out) {
+int hb_sampler_create(int vocab, int device, hb_sampler **out) { return sampler_create_rows(vocab, device, 1, out); }
+
+}  // extern "C"
+
+int sampler_create_rows(int vocab, int device, int rows, hb_sampler **out) {
   if (!out) return sampler_fail(HB_ERR_INVALID_ARG, "out is NULL");
   *out = nullptr;
   if (vocab < 1 || vocab > hb::kSampMaxVocab)
@@ -1185,6 +1237,7 @@ int hb_sampler_create(int vocab, int device, hb_sampler **out) {
   hb_sampler *sp = new hb_sampler;
   sp->device = device;
   sp->vocab = vocab;
+  sp->rows = rows;
   auto bail = [&](int rc) {
     hb_sampler_destroy(sp);
     return rc;
@@ -1194,18 +1247,19 @@ int hb_sampler_create(int vocab, int device, hb_sampler **out) {
   sp->n_nodes = static_cast<int>(pl.nodes.size());
   sp->n_levels = static_cast<int>(pl.level_end.size());
   int rc;
-  if ((rc = sampler_alloc(&sp->d_in, vocab)) || (rc = sampler_alloc(&sp->d_s, vocab)) ||
-      (rc = sampler_alloc(&sp->d_e, vocab)) || (rc = sampler_alloc(&sp->d_leaves, sp->n_leaves)) ||
+  const size_t n_ints = static_cast<size_t>(rows) * (2 + kMaxHistory + kMaxBias);
+  const size_t n_floats = static_cast<size_t>(rows) * (kMaxHistory + kMaxBias);
+  if ((rc = sampler_alloc(&sp->d_in, vocab)) || (rc = sampler_alloc(&sp->d_s, static_cast<size_t>(rows) * vocab)) ||
+      (rc = sampler_alloc(&sp->d_e, static_cast<size_t>(rows) * vocab)) || (rc = sampler_alloc(&sp->d_leaves, sp->n_leaves)) ||
       (rc = sampler_alloc(&sp->d_nodes, sp->n_nodes)) || (rc = sampler_alloc(&sp->d_levels, sp->n_levels)) ||
-      (rc = sampler_alloc(&sp->d_ints, 2 + kMaxHistory + kMaxBias)) ||
-      (rc = sampler_alloc(&sp->d_floats, kMaxHistory + kMaxBias)) ||
+      (rc = sampler_alloc(&sp->d_ints, n_ints)) || (rc = sampler_alloc(&sp->d_floats, n_floats)) ||
+      (rc = sampler_alloc(&sp->d_params, rows)) ||
       (rc = sampler_alloc(&sp->d_lp, 1 + hb::kMaxTopLogprobs)) ||
       (rc = sampler_alloc(&sp->d_lp_ids, hb::kMaxTopLogprobs + 1)))
     return bail(rc);
-  if (cudaHostAlloc(reinterpret_cast<void **>(&sp->h_ints), sizeof(int) * (2 + kMaxHistory + kMaxBias),
-                    cudaHostAllocDefault) != cudaSuccess ||
-      cudaHostAlloc(reinterpret_cast<void **>(&sp->h_floats), sizeof(float) * (kMaxHistory + kMaxBias),
-                    cudaHostAllocDefault) != cudaSuccess ||
+  if (cudaHostAlloc(reinterpret_cast<void **>(&sp->h_ints), sizeof(int) * n_ints, cudaHostAllocDefault) != cudaSuccess ||
+      cudaHostAlloc(reinterpret_cast<void **>(&sp->h_floats), sizeof(float) * n_floats, cudaHostAllocDefault) != cudaSuccess ||
+      cudaHostAlloc(reinterpret_cast<void **>(&sp->h_params), sizeof(hb::SampleParams) * rows, cudaHostAllocDefault) != cudaSuccess ||
       cudaHostAlloc(reinterpret_cast<void **>(&sp->h_lp), sizeof(double) * (1 + hb::kMaxTopLogprobs),
                     cudaHostAllocDefault) != cudaSuccess ||
       cudaHostAlloc(reinterpret_cast<void **>(&sp->h_lp_ids), sizeof(int) * (hb::kMaxTopLogprobs + 1),
@@ -1217,6 +1271,8 @@ int hb_sampler_create(int vocab, int device, hb_sampler **out) {
     return bail(sampler_fail(HB_ERR_CUDA, "sampler plan upload failed"));
   if (cudaFuncSetAttribute(reinterpret_cast<const void *>(&hb::sample_kernel),
                            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sizeof(hb::SampleSmem))) != cudaSuccess ||
+      cudaFuncSetAttribute(reinterpret_cast<const void *>(&hb::sample_batch_kernel),
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sizeof(hb::SampleSmem))) != cudaSuccess ||
       cudaFuncSetAttribute(reinterpret_cast<const void *>(&hb::logprob_kernel),
                            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sizeof(hb::SampleSmem))) != cudaSuccess ||
       cudaStreamCreateWithFlags(&sp->own_stream, cudaStreamNonBlocking) != cudaSuccess)
@@ -1224,6 +1280,8 @@ int hb_sampler_create(int vocab, int device, hb_sampler **out) {
   *out = sp;
   return HB_OK;
 }
+
+extern "C" {
 
 int hb_sampler_select(hb_sampler *sp, const float *logits, int logits_on_device, const hb_sampling *params,
                       int32_t *token_out) {
@@ -1256,10 +1314,10 @@ int hb_sampler_destroy(hb_sampler *sp) {
   DeviceScope device_scope_(sp->device);
   if (sp->own_stream) cudaStreamSynchronize(sp->own_stream);
   void *dev[] = {sp->d_in, sp->d_s, sp->d_e, sp->d_leaves, sp->d_nodes, sp->d_levels, sp->d_ints, sp->d_floats,
-                 sp->d_lp, sp->d_lp_ids};
+                 sp->d_lp, sp->d_lp_ids, sp->d_params};
   for (void *p : dev)
     if (p) cudaFree(p);
-  void *host[] = {sp->h_ints, sp->h_floats, sp->h_lp, sp->h_lp_ids};
+  void *host[] = {sp->h_ints, sp->h_floats, sp->h_lp, sp->h_lp_ids, sp->h_params};
   for (void *p : host)
     if (p) cudaFreeHost(p);
   if (sp->own_stream) cudaStreamDestroy(sp->own_stream);
@@ -1272,9 +1330,19 @@ int hb_sample(hb_engine *e, int row, const hb_sampling *params, int32_t *token_o
   if (rc) return rc;
   if (row < 0 || row >= kMaxBatch || row >= e->desc.max_batch)
     return fail(e, HB_ERR_INVALID_ARG, "row %d outside the batch", row);
-  if (!e->sampler && (rc = hb_sampler_create(e->desc.vocab, e->device, &e->sampler)))
+  if (!e->sampler && (rc = sampler_create_rows(e->desc.vocab, e->device, kMaxBatch, &e->sampler)))
     return fail(e, rc, "%s", g_lib_error.c_str());
   rc = sampler_run(e->sampler, e->stream, e->d_logits + static_cast<size_t>(row) * e->desc.vocab, params, token_out);
+  if (rc) return fail(e, rc, "%s", g_lib_error.c_str());
+  return HB_OK;
+}
+
+int hb_sample_batch(hb_engine *e, int n, const int32_t *rows, const hb_sampling *params, int32_t *tokens_out) {
+  int rc = check_engine(e);
+  if (rc) return rc;
+  if (!e->sampler && (rc = sampler_create_rows(e->desc.vocab, e->device, kMaxBatch, &e->sampler)))
+    return fail(e, rc, "%s", g_lib_error.c_str());
+  rc = sampler_run_batch(e->sampler, e->stream, e->d_logits, n, rows, params, tokens_out, e->desc.max_batch);
   if (rc) return fail(e, rc, "%s", g_lib_error.c_str());
   return HB_OK;
 }
@@ -1285,7 +1353,7 @@ int hb_logprobs(hb_engine *e, int row, int token, int n_top, double *token_logpr
   if (rc) return rc;
   if (row < 0 || row >= kMaxBatch || row >= e->desc.max_batch)
     return fail(e, HB_ERR_INVALID_ARG, "row %d outside the batch", row);
-  if (!e->sampler && (rc = hb_sampler_create(e->desc.vocab, e->device, &e->sampler)))
+  if (!e->sampler && (rc = sampler_create_rows(e->desc.vocab, e->device, kMaxBatch, &e->sampler)))
     return fail(e, rc, "%s", g_lib_error.c_str());
   rc = sampler_logprobs_run(e->sampler, e->stream, e->d_logits + static_cast<size_t>(row) * e->desc.vocab, token,
                             n_top, token_logprob, top_ids, top_logprobs);

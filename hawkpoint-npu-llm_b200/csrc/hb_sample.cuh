@@ -285,9 +285,8 @@ __device__ uint32_t samp_kth_largest(const SampleParams &p, SampleSmem &sm, int 
   return prefix;
 }
 
-__global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p) {
-  extern __shared__ __align__(16) uint8_t samp_smem_raw[];
-  SampleSmem &sm = *reinterpret_cast<SampleSmem *>(samp_smem_raw);
+// One selection by the whole thread block (see the file comment).
+__device__ void sample_row(const SampleParams &p, SampleSmem &sm) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int V = p.V;
   float *s = p.s;
@@ -526,6 +525,19 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p)
     p.out[0] = first < V ? first : V - 1;
     p.out[1] = 0;
   }
+}
+
+__global__ void __launch_bounds__(kSampThreads, 1) sample_kernel(SampleParams p) {
+  extern __shared__ __align__(16) uint8_t samp_smem_raw[];
+  sample_row(p, *reinterpret_cast<SampleSmem *>(samp_smem_raw));
+}
+
+// Rows of a batch side by side: CTA b selects for ps[b] (its own logits row,
+// parameters, history, scratch and result words).
+__global__ void __launch_bounds__(kSampThreads, 1) sample_batch_kernel(const SampleParams *ps) {
+  extern __shared__ __align__(16) uint8_t samp_smem_raw[];
+  const SampleParams p = ps[blockIdx.x];
+  sample_row(p, *reinterpret_cast<SampleSmem *>(samp_smem_raw));
 }
 
 // Log-probabilities for an OpenAI ``logprobs`` entry: the reference's

@@ -186,7 +186,10 @@ class B200DecoderEngine:
             int(new_tokens), out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))))
         return [int(t) for t in out]
 
-    def step_batch(self, slots, tokens, positions, logits=False):
+    def step_batch(self, slots, tokens, positions, logits=False, device_logits=False):
+        """One position of each of several streams; (argmax per row, FP32
+        logits or None).  ``device_logits`` keeps the logits on the device
+        for ``sample_batch`` without copying them."""
         h = self._live()
         n = len(slots)
         s = np.ascontiguousarray(slots, np.int32)
@@ -197,10 +200,18 @@ class B200DecoderEngine:
         ip = ctypes.POINTER(ctypes.c_int32)
         self._check(self._lib.hb_step_batch(
             h, n, s.ctypes.data_as(ip), t.ctypes.data_as(ip), p.ctypes.data_as(ip),
-            hb_lib.HB_STEP_ARGMAX,
+            hb_lib.HB_STEP_DEVICE_LOGITS if device_logits else hb_lib.HB_STEP_ARGMAX,
             out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)) if logits else None,
             am.ctypes.data_as(ip)))
         return am, out
+
+    def sample_batch(self, rows, params, histories, uniforms):
+        """Device selections for several rows of the last ``step_batch(...,
+        device_logits=True)`` in one launch; a token per entry, None where the
+        top-p nucleus is too large (select those on the host)."""
+        from runtime.device_sampler import sample_engine_rows
+
+        return sample_engine_rows(self._lib, self._live(), self.vocab, rows, params, histories, uniforms)
 
     def reset(self, slot=None):
         """Forget every cached position (of one slot, or of all)."""

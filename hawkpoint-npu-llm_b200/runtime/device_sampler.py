@@ -137,3 +137,16 @@ def sample_engine_row(lib, handle, vocab, row, params, history, uniform):
     token = ctypes.c_int32()
     rc = lib.hb_sample(handle, int(row), ctypes.byref(args.struct), ctypes.byref(token))
     return _result(rc, token, handle)
+
+
+def sample_engine_rows(lib, handle, vocab, rows, params, histories, uniforms):
+    """Several selections from a batched step's device logits in one launch."""
+    n = len(rows)
+    args = [SamplingArgs(p, h, vocab, u) for p, h, u in zip(params, histories, uniforms)]
+    structs = (hb_lib.HbSampling * n)(*[a.struct for a in args])
+    rows_arr = np.ascontiguousarray(rows, np.int32)
+    out = np.empty(n, np.int32)
+    ip = ctypes.POINTER(ctypes.c_int32)
+    rc = lib.hb_sample_batch(handle, n, rows_arr.ctypes.data_as(ip), structs, out.ctypes.data_as(ip))
+    hb_lib.check(rc, handle)
+    return [None if t < 0 else int(t) for t in out]

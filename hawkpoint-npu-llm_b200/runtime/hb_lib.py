@@ -122,6 +122,7 @@ SIGNATURES = {
     "hb_sampler_select": (_I, [_P, _P, _I, ctypes.POINTER(HbSampling), _I32P]),
     "hb_sampler_destroy": (_I, [_P]),
     "hb_sample": (_I, [_P, _I, ctypes.POINTER(HbSampling), _I32P]),
+    "hb_sample_batch": (_I, [_P, _I, _I32P, ctypes.POINTER(HbSampling), _I32P]),
     "hb_read_logits": (_I, [_P, _I, _FP]),
     "hb_sampler_logprobs": (_I, [_P, _P, _I, _I, _I, ctypes.POINTER(ctypes.c_double), _I32P,
                                  ctypes.POINTER(ctypes.c_double)]),

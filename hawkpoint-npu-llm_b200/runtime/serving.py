@@ -1,5 +1,5 @@
-"""Multi-stream greedy serving on one GPU: continuous batching over the
-engine's batched decode step (``hb_step_batch``).
+"""Multi-stream serving on one GPU: continuous batching over the engine's
+batched decode step (``hb_step_batch``), greedy or sampled per request.
 
 The reference serves one request at a time behind a lock
 (npu_llm/api_server.py:646-678); its engine has no batched mode.  Here up to
@@ -8,6 +8,14 @@ launch is one stream at its own position -- a prompt token during sequential
 prefill (npu_llm/runtime/generate.py:1110-1126, logits unused), or its last
 generated token during decode.  A weight-streaming decode step costs about
 the same for 8 rows as for 1, so the aggregate rate scales with the batch.
+
+A request may carry a ``sampler`` with the reference ``Sampler`` surface
+(``params``, ``greedy``, its generator ``_rng``, ``select``;
+npu_llm/runtime/sampling.py:398-453).  The rows of a launch that sample
+select on the device in one further launch (``hb_sample_batch``), each
+request's own generator supplying its draw, so a seeded request yields the
+same tokens as alone; a row whose top-p nucleus is too large for the device
+is selected on the host from the same logits with its generator rewound.
 
 KV slots: ``max_batch`` slots for the running streams plus a small LRU pool
 that keeps shared prompt prefixes.  A request whose first ``prefix_tokens``
@@ -20,12 +28,15 @@ from collections import OrderedDict
 from dataclasses import dataclass, field
 import time
 
+import numpy as np
+
 
 @dataclass
 class Request:
     prompt: list
     new_tokens: int
     rid: int = 0
+    sampler: object = None   # None: greedy
     tokens: list = field(default_factory=list)
     admitted: float = 0.0
     first_token: float = 0.0
@@ -45,11 +56,13 @@ class _Stream:
 
 
 class MultiStreamServer:
-    """Runs a list of greedy requests to completion on one engine.
+    """Runs a list of requests to completion on one engine.
 
     ``engine`` needs ``step_batch(slots, tokens, positions) -> (argmax, _)``,
     ``copy_prefix(src, dst, n)``, ``max_slots`` and ``context``; it must have
-    at least ``max_batch + prefix_slots`` KV slots."""
+    at least ``max_batch + prefix_slots`` KV slots.  Sampled requests also
+    need ``step_batch(..., device_logits=True)``, ``sample_batch`` and
+    ``device_logits`` and the engine's ``vocab``."""
 
     def __init__(self, engine, max_batch=8, prefix_tokens=16, prefix_slots=4, clock=time.perf_counter):
         if max_batch < 1:
@@ -94,6 +107,30 @@ class MultiStreamServer:
         self.engine.copy_prefix(st.slot, pslot, self.prefix_tokens)
         self.prefixes[st.key] = pslot
 
+    def _sample_rows(self, active, rows):
+        """Tokens of the sampled rows of the last launch, on the device."""
+        from runtime.device_sampler import draws_uniform
+
+        vocab = self.engine.vocab
+        params, histories, uniforms, states = [], [], [], []
+        for i in rows:
+            req = active[i].req
+            rng = req.sampler._rng
+            states.append(rng.bit_generator.state)
+            params.append(req.sampler.params)
+            histories.append(list(req.prompt) + list(req.tokens))
+            uniforms.append(rng.random() if draws_uniform(req.sampler.params, vocab) else None)
+        tokens = self.engine.sample_batch(rows, params, histories, uniforms)
+        host = None
+        for k, i in enumerate(rows):
+            if tokens[k] is None:  # nucleus beyond the on-chip sort: same draw on the host
+                if host is None:
+                    host = np.asarray(self.engine.device_logits(rows=len(active))).reshape(len(active), -1)
+                req = active[i].req
+                req.sampler._rng.bit_generator.state = states[k]
+                tokens[k] = int(req.sampler.select(host[i], histories[k]))
+        return tokens
+
     def run(self, requests):
         context = self.engine.context
         for req in requests:
@@ -110,7 +147,16 @@ class MultiStreamServer:
             slots = [st.slot for st in active]
             tokens = [st.token for st in active]
             positions = [st.pos for st in active]
-            argmax, _ = self.engine.step_batch(slots, tokens, positions)
+            sampled = [i for i, st in enumerate(active)
+                       if st.pos >= len(st.req.prompt) - 1 and st.req.sampler is not None
+                       and not st.req.sampler.greedy]
+            if sampled:
+                argmax, _ = self.engine.step_batch(slots, tokens, positions, device_logits=True)
+                argmax = list(argmax)
+                for i, token in zip(sampled, self._sample_rows(active, sampled)):
+                    argmax[i] = token
+            else:
+                argmax, _ = self.engine.step_batch(slots, tokens, positions)
             self.launches += 1
             self.rows += len(active)
             now = self.clock()

@@ -253,6 +253,14 @@ int hb_sampler_logprobs(hb_sampler *sampler, const float *logits, int logits_on_
  * hb_step_batch left on the device (HB_STEP_DEVICE_LOGITS), on the
  * engine's stream. */
 int hb_sample(hb_engine *engine, int row, const hb_sampling *params, int32_t *token_out);
+/* Several selections in one launch (one thread block each), for a batched
+ * step (hb_step_batch with HB_STEP_DEVICE_LOGITS): entry k selects from
+ * logits row rows[k] with params[k].  tokens_out[k] = -1 marks an entry
+ * whose top-p nucleus is too large for the device (select it on the host
+ * from hb_read_logits).  n <= max_batch.  New in this build (the reference
+ * serves one request at a time). */
+int hb_sample_batch(hb_engine *engine, int n, const int32_t *rows, const hb_sampling *params,
+                    int32_t *tokens_out);
 /* hb_sampler_logprobs on row `row` of the engine's device logits. */
 int hb_logprobs(hb_engine *engine, int row, int token, int n_top, double *token_logprob,
                 int32_t *top_ids, double *top_logprobs);

@@ -19,20 +19,56 @@ class FakeEngine:
         self.batches = []
         self.copies = []
 
-    def step_batch(self, slots, tokens, positions):
+    def step_batch(self, slots, tokens, positions, device_logits=False):
         assert len(set(slots)) == len(slots), "two rows share a KV slot"
         self.batches.append(len(slots))
         out = []
+        self.logits = []
         for s, t, p in zip(slots, tokens, positions):
             self.cache[s][p] = t
             hist = self.cache[s][: p + 1]
             assert None not in hist, f"slot {s} position {p} reads an unwritten position"
             out.append(hash(tuple(hist)) % self.vocab)
+            self.logits.append(fake_logits(hist, self.vocab))
         return np.array(out), None
+
+    # the device sampler: the oracle; a top-p nucleus is "too large" here so
+    # the server's host fallback runs too
+    def sample_batch(self, rows, params, histories, uniforms):
+        from oracle.sampling import select_with_uniform
+
+        self.sampled = getattr(self, "sampled", 0) + len(rows)
+        return [None if p.top_p < 1.0 else select_with_uniform(self.logits[i], h, p, u)
+                for i, p, h, u in zip(rows, params, histories, uniforms)]
+
+    def device_logits(self, rows=1):
+        return np.stack(self.logits[:rows])
 
     def copy_prefix(self, src, dst, n):
         self.copies.append((src, dst, n))
         self.cache[dst][:n] = self.cache[src][:n]
+
+
+def fake_logits(hist, vocab):
+    return np.random.default_rng(hash(tuple(hist)) % (2 ** 32)).standard_normal(vocab).astype(np.float32)
+
+
+class OracleSampler:
+    """The reference ``Sampler`` surface over the oracle (seeded generator)."""
+
+    def __init__(self, params, vocab, seed):
+        self.params, self.vocab = params, vocab
+        self._rng = np.random.default_rng(seed)
+
+    @property
+    def greedy(self):
+        return self.params.greedy_for(self.vocab)
+
+    def select(self, logits, history):
+        from oracle import sampling as osamp
+
+        u = self._rng.random() if osamp.draws_uniform(self.params, self.vocab) else None
+        return osamp.select_with_uniform(logits, history, self.params, u)
 
 
 def reference_tokens(prompt, new_tokens, vocab=1000, context=64):
@@ -73,6 +109,38 @@ def test_continuous_batching_matches_single_streams():
     assert eng.copies[0][2] == 16
 
 
+def _sampled_requests(vocab, seed=0):
+    from oracle import sampling as osamp
+
+    reqs = config5_requests(n=24, seed=seed, vocab=vocab, new_tokens=8)
+    settings = [None, osamp.Params(temperature=0.9), osamp.Params(temperature=0.8, top_k=40, top_p=0.9),
+                osamp.Params(temperature=1.0, repetition_penalty=1.2, logit_bias={3: 2.0})]
+    for r in reqs:
+        params = settings[r.rid % len(settings)]
+        r.sampler = None if params is None else OracleSampler(params, vocab, 100 + r.rid)
+    return reqs
+
+
+def test_sampled_requests_in_continuous_batching():
+    """Sampled rows select per request, each with its own generator; the
+    tokens equal each request decoded alone with the host sampler, also
+    where the device reports a nucleus too large and the host selects."""
+    eng = FakeEngine(max_slots=12)
+    reqs = _sampled_requests(eng.vocab)
+    MultiStreamServer(eng, max_batch=8, prefix_slots=4).run(reqs)
+    assert eng.sampled > 0
+    alone = _sampled_requests(eng.vocab)
+    for r, a in zip(reqs, alone):
+        hist, want = list(a.prompt), []
+        while len(want) < a.new_tokens:
+            nxt = hash(tuple(hist)) % eng.vocab
+            if a.sampler is not None and not a.sampler.greedy:
+                nxt = a.sampler.select(fake_logits(hist, eng.vocab), list(a.prompt) + want)
+            want.append(int(nxt))
+            hist.append(int(nxt))
+        assert r.tokens == want, r.rid
+
+
 def test_context_limit_and_validation():
     eng = FakeEngine(max_slots=2, context=20)
     req = Request(prompt=list(range(18)), new_tokens=10)
@@ -108,5 +176,32 @@ def test_gpu_multistream_matches_generate():
             single = engine.generate(r.prompt, r.new_tokens, slot=11)
             assert r.tokens == single, f"request {r.rid}"
         assert any(r.reused_prefix for r in reqs)
+    finally:
+        engine.close()
+
+
+@pytest.mark.gpu
+def test_gpu_sampled_multistream_matches_each_request_alone():
+    """Sampled and greedy requests share launches; each request's tokens
+    equal the same request served alone (the batch kernel computes every row
+    the same way whatever the other rows are, and each generator supplies
+    its own draws)."""
+    from runtime import synthetic
+    from runtime.b200_engine import B200DecoderEngine
+
+    model = synthetic.build("tiny-qwen", seed=32)
+    vocab = model.shape.vocab
+    engine = B200DecoderEngine(model, max_slots=12, max_batch=8)
+    try:
+        reqs = _sampled_requests(vocab, seed=3)
+        for r in reqs:
+            r.prompt = [t % vocab for t in r.prompt]
+        MultiStreamServer(engine, max_batch=8, prefix_slots=4).run(reqs)
+        alone = _sampled_requests(vocab, seed=3)
+        for r, a in zip(reqs, alone):
+            a.prompt = [t % vocab for t in a.prompt]
+            engine.reset()
+            MultiStreamServer(engine, max_batch=8, prefix_slots=4).run([a])
+            assert r.tokens == a.tokens, r.rid
     finally:
         engine.close()
