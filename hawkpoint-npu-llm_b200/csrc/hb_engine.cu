@@ -970,12 +970,16 @@ struct hb_sampler {
   hb::SampleParams *d_params = nullptr, *h_params = nullptr;  // [rows]
   double *d_lp = nullptr, *h_lp = nullptr;  // [1 + kMaxTopLogprobs] log-probabilities
   int *d_lp_ids = nullptr, *h_lp_ids = nullptr;  // [kMaxTopLogprobs + 1]
+  // the grid-wide kernel for single selections over large vocabularies
+  int grid_ctas = 0;
+  hb::SampleGrid grid{};
 };
 
 namespace {
 
 constexpr int kMaxHistory = 8192;
 constexpr int kMaxBias = 1024;  // MAX_LOGIT_BIAS_ENTRIES of the reference
+constexpr int kGridMinVocab = 16384;  // below: one thread block selects
 
 // NumPy's pairwise reduction tree of n values (np.add.reduce on a contiguous
 // float array): leaves are runs of at most 128 values, a longer run splits
@@ -1148,7 +1152,13 @@ int sampler_run(hb_sampler *sp, cudaStream_t stream, const float *logits_dev, co
   hb::SampleParams P;
   int rc;
   if ((rc = sampler_prepare(sp, 0, logits_dev, q, P)) || (rc = sampler_upload(sp, stream, P))) return rc;
-  hb::sample_kernel<<<1, hb::kSampThreads, sizeof(hb::SampleSmem), stream>>>(P);
+  if (sp->grid_ctas > 0) {
+    void *args[] = {&P, &sp->grid};
+    HB_SCUDA(cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(&hb::sample_grid_kernel), dim3(sp->grid_ctas),
+                                         dim3(hb::kSampThreads), args, sizeof(hb::SampleSmem), stream));
+  } else {
+    hb::sample_kernel<<<1, hb::kSampThreads, sizeof(hb::SampleSmem), stream>>>(P);
+  }
   HB_SCUDA(cudaGetLastError());
   HB_SCUDA(cudaMemcpyAsync(sp->h_ints, sp->d_ints, sizeof(int) * 2, cudaMemcpyDeviceToHost, stream));
   HB_SCUDA(cudaStreamSynchronize(stream));
@@ -1275,8 +1285,27 @@ int sampler_create_rows(int vocab, int device, int rows, hb_sampler **out) {
                            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sizeof(hb::SampleSmem))) != cudaSuccess ||
       cudaFuncSetAttribute(reinterpret_cast<const void *>(&hb::logprob_kernel),
                            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sizeof(hb::SampleSmem))) != cudaSuccess ||
+      cudaFuncSetAttribute(reinterpret_cast<const void *>(&hb::sample_grid_kernel),
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sizeof(hb::SampleSmem))) != cudaSuccess ||
       cudaStreamCreateWithFlags(&sp->own_stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(sampler_fail(HB_ERR_CUDA, "sampler set-up failed"));
+  // single selections over a large vocabulary spread over every SM
+  int coop = 0, sms = 0, per_sm = 0;
+  if (vocab >= kGridMinVocab && cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device) == cudaSuccess &&
+      coop && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess &&
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, reinterpret_cast<const void *>(&hb::sample_grid_kernel),
+                                                    hb::kSampThreads, sizeof(hb::SampleSmem)) == cudaSuccess &&
+      per_sm >= 1) {
+    const int G = sms;
+    hb::SampleGrid &g = sp->grid;
+    if ((rc = sampler_alloc(&g.leaf32, sp->n_leaves)) || (rc = sampler_alloc(&g.leaf64, sp->n_leaves)) ||
+        (rc = sampler_alloc(&g.cta_f, G)) || (rc = sampler_alloc(&g.cta_i, G)) || (rc = sampler_alloc(&g.cta_d, G)) ||
+        (rc = sampler_alloc(&g.hist, 8 * 256)) || (rc = sampler_alloc(&g.cand, hb::kTopPMax)) ||
+        (rc = sampler_alloc(&g.ctr, 4)) || (rc = sampler_alloc(&g.fs, 4)) || (rc = sampler_alloc(&g.ds, 2)))
+      return bail(rc);
+    sp->grid_ctas = G;
+  }
+  cudaGetLastError();
   *out = sp;
   return HB_OK;
 }
@@ -1313,8 +1342,10 @@ int hb_sampler_destroy(hb_sampler *sp) {
   if (!sp) return HB_OK;
   DeviceScope device_scope_(sp->device);
   if (sp->own_stream) cudaStreamSynchronize(sp->own_stream);
+  const hb::SampleGrid &g = sp->grid;
   void *dev[] = {sp->d_in, sp->d_s, sp->d_e, sp->d_leaves, sp->d_nodes, sp->d_levels, sp->d_ints, sp->d_floats,
-                 sp->d_lp, sp->d_lp_ids, sp->d_params};
+                 sp->d_lp, sp->d_lp_ids, sp->d_params, g.leaf32, g.leaf64, g.cta_f, g.cta_i, g.cta_d, g.hist,
+                 g.cand, g.ctr, g.fs, g.ds};
   for (void *p : dev)
     if (p) cudaFree(p);
   void *host[] = {sp->h_ints, sp->h_floats, sp->h_lp, sp->h_lp_ids, sp->h_params};

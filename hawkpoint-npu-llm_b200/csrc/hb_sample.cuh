@@ -29,6 +29,7 @@
 // "unsupported" and the caller selects on the host instead.
 #pragma once
 
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include "hb_device.cuh"
@@ -113,17 +114,16 @@ __device__ __forceinline__ void samp_map(const float *src, int V, F &&body) {
 __device__ __forceinline__ float samp_add(float a, float b) { return __fadd_rn(a, b); }
 __device__ __forceinline__ double samp_add(double a, double b) { return __dadd_rn(a, b); }
 
-// Sum of elem(0..V-1) in NumPy's pairwise order.  All threads call it.
-// Leaves go to groups of eight lanes: lane j of a group keeps accumulator j
-// (elements j, j + 8, ... of the leaf, read coalesced across the group), the
-// eight are combined as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) with shuffles,
-// and the group's first lane adds the tail left to right.
+// Leaf sums of NumPy's pairwise tree: leaves first, first + stride, ... (in
+// blocks of 128 leaves) go to groups of eight lanes; lane j of a group keeps
+// accumulator j (elements j, j + 8, ... of the leaf, read coalesced across
+// the group), the eight are combined as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7))
+// with shuffles, and the group's first lane adds the tail left to right.
 template <class T, class F>
-__device__ T tree_sum(const SampleParams &p, SampleSmem &sm, F &&elem) {
-  T *vals = reinterpret_cast<T *>(sm.tree);
+__device__ void leaf_sums(const SampleParams &p, F &&elem, T *out, int first, int stride) {
   const int lane = threadIdx.x & 31, j = lane & 7;
   const int group = (threadIdx.x >> 3);  // 128 groups of 8 lanes
-  for (int base = 0; base < p.n_leaves; base += kSampThreads / 8) {
+  for (int base = first; base < p.n_leaves; base += stride) {
     const int l = base + group;
     int lo = 0, n = 0;
     if (l < p.n_leaves) {
@@ -156,10 +156,16 @@ __device__ T tree_sum(const SampleParams &p, SampleSmem &sm, F &&elem) {
         i = n - n % 8;
       }
       for (; i < n; ++i) res = samp_add(res, elem(lo + i));
-      vals[l] = res;
+      out[l] = res;
     }
   }
-  __syncthreads();
+}
+
+// Combine the leaf sums already in sm.tree one tree height per step; the
+// root.  All threads of the block call it.
+template <class T>
+__device__ T tree_combine(const SampleParams &p, SampleSmem &sm) {
+  T *vals = reinterpret_cast<T *>(sm.tree);
   int start = 0;
   for (int h = 0; h < p.n_levels; ++h) {
     const int end = p.level_end[h];
@@ -173,6 +179,14 @@ __device__ T tree_sum(const SampleParams &p, SampleSmem &sm, F &&elem) {
   const T r = vals[p.n_nodes > 0 ? p.n_leaves + p.n_nodes - 1 : 0];
   __syncthreads();
   return r;
+}
+
+// Sum of elem(0..V-1) in NumPy's pairwise order.  All threads call it.
+template <class T, class F>
+__device__ T tree_sum(const SampleParams &p, SampleSmem &sm, F &&elem) {
+  leaf_sums<T>(p, elem, reinterpret_cast<T *>(sm.tree), 0, kSampThreads / 8);
+  __syncthreads();
+  return tree_combine<T>(p, sm);
 }
 
 __device__ __forceinline__ float samp_block_max(SampleSmem &sm, float v) {
@@ -538,6 +552,435 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_batch_kernel(const Sam
   extern __shared__ __align__(16) uint8_t samp_smem_raw[];
   const SampleParams p = ps[blockIdx.x];
   sample_row(p, *reinterpret_cast<SampleSmem *>(samp_smem_raw));
+}
+
+// ---- the same selection spread over the grid (one row) --------------------
+// A cooperative launch of one CTA per SM: each CTA owns a contiguous slice
+// of the vocabulary for the element-wise work and the histograms, the leaf
+// sums of NumPy's tree are dealt round-robin, and the steps that need the
+// whole vector (tree roots, the top-p sort and running sum, the argmax and
+// the draw's crossing) meet at grid barriers.  Same arithmetic as
+// sample_row; only the draw's float64 running sums are grouped differently
+// (an ulp of a double).
+struct SampleGrid {
+  float *leaf32;             // [n_leaves]
+  double *leaf64;            // [n_leaves]
+  float *cta_f;              // [G]
+  int *cta_i;                // [G]
+  double *cta_d;             // [G]
+  unsigned *hist;            // [8][256], zeroed at the start of a launch
+  unsigned long long *cand;  // [kTopPMax] top-p candidates
+  int *ctr;                  // [0] candidates, [1] first crossing, [2] top-p keep, [3] cut key
+  float *fs;                 // [0] softmax total
+  double *ds;                // [0] float64 total
+};
+
+// Key of the k-th largest score over the grid (every CTA returns it).
+__device__ uint32_t grid_kth_largest(const SampleParams &p, SampleSmem &sm, unsigned *hist4, int k, int lo, int hi,
+                                     cooperative_groups::grid_group &grid) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t prefix = 0, mask = 0;
+  int kk = k;
+  const int span = hi - lo, pad = (span + kSampThreads - 1) / kSampThreads * kSampThreads;
+  for (int r = 0; r < 4; ++r) {
+    const int shift = 24 - 8 * r;
+    unsigned *gh = hist4 + 256 * r;
+    for (int i = threadIdx.x; i < kSampWarps * 256; i += kSampThreads) (&sm.hist[0][0])[i] = 0u;
+    __syncthreads();
+    for (int t = threadIdx.x; t < pad; t += kSampThreads) {
+      int bin = 256;
+      if (t < span) {
+        const uint32_t key = samp_key(p.s[lo + t]);
+        if ((key & mask) == prefix) bin = (key >> shift) & 255;
+      }
+      const unsigned peers = __match_any_sync(0xffffffffu, bin);
+      if (bin < 256 && lane == __ffs(peers) - 1) sm.hist[warp][bin] += __popc(peers);
+    }
+    __syncthreads();
+    if (threadIdx.x < 256) {
+      unsigned c = 0;
+      for (int w = 0; w < kSampWarps; ++w) c += sm.hist[w][threadIdx.x];
+      if (c) atomicAdd(&gh[threadIdx.x], c);
+    }
+    grid.sync();
+    if (threadIdx.x == 0) {
+      int acc = 0, b = 255;
+      for (; b > 0; --b) {
+        const int c = static_cast<int>(__ldcg(&gh[b]));
+        if (acc + c >= kk) break;
+        acc += c;
+      }
+      sm.misc[0] = b;
+      sm.misc[1] = kk - acc;
+    }
+    __syncthreads();
+    prefix |= static_cast<uint32_t>(sm.misc[0]) << shift;
+    mask |= 255u << shift;
+    kk = sm.misc[1];
+    __syncthreads();
+  }
+  return prefix;
+}
+
+// Block-wide inclusive scan of one double per thread; *total = block sum.
+__device__ __forceinline__ double samp_block_scan(SampleSmem &sm, double v, double *total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v = __dadd_rn(v, t);
+  }
+  if (lane == 31) sm.wscan[warp] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double acc = 0.0;
+    for (int w = 0; w < kSampWarps; ++w) {
+      const double t = sm.wscan[w];
+      sm.wscan[w] = acc;
+      acc = __dadd_rn(acc, t);
+    }
+    sm.dmisc[1] = acc;
+  }
+  __syncthreads();
+  const double r = __dadd_rn(v, sm.wscan[warp]);
+  *total = sm.dmisc[1];
+  __syncthreads();
+  return r;
+}
+
+// np.argmax order over this CTA's slice, merged over the grid by CTA 0
+// (after the caller's grid barrier) from cta_f / cta_i.
+__device__ void grid_argmax_partial(const SampleParams &p, SampleSmem &sm, const SampleGrid &g, int lo, int hi) {
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int j = lo + threadIdx.x; j < hi; j += kSampThreads) argmax_merge(bv, bi, p.s[j], j);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    argmax_merge(bv, bi, ov, oi);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sm.wf[threadIdx.x >> 5] = bv;
+    sm.wi[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v = sm.wf[0];
+    int i = sm.wi[0];
+    for (int w = 1; w < kSampWarps; ++w) argmax_merge(v, i, sm.wf[w], sm.wi[w]);
+    g.cta_f[blockIdx.x] = v;
+    g.cta_i[blockIdx.x] = i;
+  }
+  __syncthreads();
+}
+
+__device__ int grid_argmax_merge(const SampleGrid &g) {
+  float v = -INFINITY;
+  int i = 0x7fffffff;
+  for (int c = 0; c < static_cast<int>(gridDim.x); ++c) argmax_merge(v, i, __ldcg(&g.cta_f[c]), __ldcg(&g.cta_i[c]));
+  return i;
+}
+
+__global__ void __launch_bounds__(kSampThreads, 1) sample_grid_kernel(SampleParams p, SampleGrid g) {
+  extern __shared__ __align__(16) uint8_t samp_smem_raw[];
+  SampleSmem &sm = *reinterpret_cast<SampleSmem *>(samp_smem_raw);
+  cooperative_groups::grid_group grid = cooperative_groups::this_grid();
+  const int G = gridDim.x, b = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  const int V = p.V;
+  const int lo = static_cast<int>(static_cast<long long>(V) * b / G);
+  const int hi = static_cast<int>(static_cast<long long>(V) * (b + 1) / G);
+  float *s = p.s;
+  float *e = p.e;
+  if (b == 0) {  // read only after the first grid barrier
+    for (int i = tid; i < 8 * 256; i += kSampThreads) g.hist[i] = 0u;
+    if (tid == 0) {
+      g.ctr[0] = 0;
+      g.ctr[1] = 0x7fffffff;
+    }
+  }
+  // 1-2. this CTA's slice: copy, penalties, bias
+  for (int j = lo + tid; j < hi; j += kSampThreads) s[j] = p.logits[j];
+  __syncthreads();
+  for (int t = tid; t < p.n_hist; t += kSampThreads) {
+    const int tok = p.hist_tok[t];
+    if (tok < lo || tok >= hi) continue;
+    float v = s[tok];
+    if (p.rep != 1.0f) v = v > 0.f ? __fdiv_rn(v, p.rep) : __fmul_rn(v, p.rep);
+    v = __fsub_rn(v, __fmul_rn(p.freq, p.hist_cnt[t]));
+    v = __fsub_rn(v, p.pres);
+    s[tok] = v;
+  }
+  __syncthreads();
+  for (int t = tid; t < p.n_bias; t += kSampThreads) {
+    const int tok = p.bias_tok[t];
+    if (tok >= lo && tok < hi) s[tok] = __fadd_rn(s[tok], p.bias_val[t]);
+  }
+  __syncthreads();
+  if (p.temperature == 0.0f) {
+    grid_argmax_partial(p, sm, g, lo, hi);
+    grid.sync();
+    if (b == 0 && tid == 0) {
+      p.out[0] = grid_argmax_merge(g);
+      p.out[1] = 0;
+    }
+    return;
+  }
+  // 3. temperature
+  for (int j = lo + tid; j < hi; j += kSampThreads) s[j] = __fdiv_rn(s[j], p.temperature);
+  __syncthreads();
+  // 4. top-k
+  if (p.top_k > 0 && p.top_k < V) {
+    grid.sync();  // the zeroed histograms
+    const float thr = samp_unkey(grid_kth_largest(p, sm, g.hist, p.top_k, lo, hi, grid));
+    for (int j = lo + tid; j < hi; j += kSampThreads)
+      if (s[j] < thr) s[j] = -INFINITY;
+    __syncthreads();
+  }
+  // 5. top-p
+  if (p.top_p < 1.0f) {
+    int cand = 0;
+    float peak = -INFINITY;
+    for (int j = lo + tid; j < hi; j += kSampThreads) {
+      const float v = s[j];
+      if (isfinite(v)) {
+        ++cand;
+        peak = fmaxf(peak, v);
+      }
+    }
+    cand = samp_block_sum(sm, cand);
+    peak = samp_block_max(sm, peak);
+    if (tid == 0) {
+      g.cta_i[b] = cand;
+      g.cta_f[b] = peak;
+    }
+    grid.sync();
+    if (tid == 0) {
+      int c = 0;
+      float pk = -INFINITY;
+      for (int x = 0; x < G; ++x) {
+        c += __ldcg(&g.cta_i[x]);
+        pk = fmaxf(pk, __ldcg(&g.cta_f[x]));
+      }
+      sm.misc[4] = c;
+      sm.wf[0] = pk;
+    }
+    __syncthreads();
+    const int C = sm.misc[4];
+    peak = sm.wf[0];
+    __syncthreads();
+    uint32_t lo_key = 0u;
+    if (C > kTopPMax) lo_key = grid_kth_largest(p, sm, g.hist + 4 * 256, kTopPMax, lo, hi, grid);
+    const int span = hi - lo, pad = (span + kSampThreads - 1) / kSampThreads * kSampThreads;
+    for (int t = tid; t < pad; t += kSampThreads) {
+      bool take = false;
+      uint32_t key = 0u;
+      if (t < span) {
+        const float v = s[lo + t];
+        key = samp_key(v);
+        take = isfinite(v) && key >= lo_key;
+      }
+      const unsigned ballot = __ballot_sync(0xffffffffu, take);
+      int base = 0;
+      if (lane == 0 && ballot) base = atomicAdd(&g.ctr[0], __popc(ballot));
+      base = __shfl_sync(0xffffffffu, base, 0);
+      if (take) {
+        const int slot = base + __popc(ballot & ((1u << lane) - 1u));
+        if (slot < kTopPMax) g.cand[slot] = (static_cast<unsigned long long>(key) << 32) | static_cast<uint32_t>(lo + t);
+      }
+    }
+    if (C > kTopPMax) {
+      for (int j = lo + tid; j < hi; j += kSampThreads) {
+        const float v = s[j];
+        e[j] = isfinite(v) ? expf(__fsub_rn(v, peak)) : 0.f;
+      }
+    }
+    grid.sync();
+    if (C > kTopPMax) {
+      leaf_sums<float>(p, [&](int j) { return __ldcg(&e[j]); }, g.leaf32, b * (kSampThreads / 8), G * (kSampThreads / 8));
+      grid.sync();
+    }
+    if (b == 0) {
+      const int cnt = __ldcg(&g.ctr[0]);
+      if (cnt > kTopPMax) {
+        if (tid == 0) g.ctr[2] = -1;
+      } else {
+        int n2 = 1;
+        while (n2 < cnt) n2 <<= 1;
+        for (int i = tid; i < n2; i += kSampThreads) sm.keys[i] = i < cnt ? __ldcg(&g.cand[i]) : 0ull;
+        __syncthreads();
+        for (int k = 2; k <= n2; k <<= 1) {
+          for (int jj = k >> 1; jj > 0; jj >>= 1) {
+            for (int i = tid; i < n2; i += kSampThreads) {
+              const int ixj = i ^ jj;
+              if (ixj > i) {
+                const unsigned long long x = sm.keys[i], y = sm.keys[ixj];
+                const bool desc = (i & k) == 0;
+                if (desc ? (x < y) : (x > y)) {
+                  sm.keys[i] = y;
+                  sm.keys[ixj] = x;
+                }
+              }
+            }
+            __syncthreads();
+          }
+        }
+        for (int i = tid; i < cnt; i += kSampThreads)
+          sm.probs[i] = expf(__fsub_rn(samp_unkey(static_cast<uint32_t>(sm.keys[i] >> 32)), peak));
+        __syncthreads();
+        float total;
+        if (C <= kTopPMax) {
+          total = tree_sum<float>(p, sm, [&](int i) { return i < cnt ? sm.probs[i] : 0.f; });
+        } else {
+          float *vals = reinterpret_cast<float *>(sm.tree);
+          for (int l = tid; l < p.n_leaves; l += kSampThreads) vals[l] = __ldcg(&g.leaf32[l]);
+          __syncthreads();
+          total = tree_combine<float>(p, sm);
+        }
+        const bool degenerate = !(total > 0.f) || !isfinite(total);
+        for (int i = tid; i < cnt; i += kSampThreads) sm.probs[i] = __fdiv_rn(sm.probs[i], total);
+        __syncthreads();
+        if (tid == 0) {
+          int keep = -1;
+          if (degenerate) {
+            keep = 1;
+          } else {
+            float cum = 0.f;
+            for (int i = 0; i < cnt; ++i) {
+              const float pi = sm.probs[i];
+              cum = __fadd_rn(cum, pi);
+              if (i > 0 && !(__fsub_rn(cum, pi) < p.top_p)) {
+                keep = i;
+                break;
+              }
+            }
+            if (keep < 0 && C <= kTopPMax) keep = cnt;
+          }
+          sm.misc[3] = keep;
+          g.ctr[2] = keep;
+          if (keep > 0) g.ctr[3] = static_cast<int>(static_cast<uint32_t>(sm.keys[keep - 1] >> 32));
+        }
+        __syncthreads();
+        const int keep = sm.misc[3];
+        if (keep > 0) {
+          const uint32_t cut_key = static_cast<uint32_t>(sm.keys[keep - 1] >> 32);
+          for (int i = keep + tid; i < cnt; i += kSampThreads)  // ties with the cut beyond it
+            if (static_cast<uint32_t>(sm.keys[i] >> 32) == cut_key) s[static_cast<uint32_t>(sm.keys[i])] = -INFINITY;
+        }
+      }
+    }
+    grid.sync();
+    const int keep = __ldcg(&g.ctr[2]);
+    if (keep < 0) {  // the nucleus extends past the sorted candidates
+      if (b == 0 && tid == 0) {
+        p.out[0] = -1;
+        p.out[1] = 1;
+      }
+      return;
+    }
+    const float cut = samp_unkey(static_cast<uint32_t>(__ldcg(&g.ctr[3])));
+    for (int j = lo + tid; j < hi; j += kSampThreads)
+      if (s[j] < cut) s[j] = -INFINITY;
+    __syncthreads();
+  }
+  // 6. guarded softmax in index order, float64 renormalisation, the draw
+  float peak = -INFINITY;
+  for (int j = lo + tid; j < hi; j += kSampThreads)
+    if (isfinite(s[j])) peak = fmaxf(peak, s[j]);
+  peak = samp_block_max(sm, peak);
+  grid_argmax_partial(p, sm, g, lo, hi);  // for the degenerate case below
+  if (tid == 0) g.cta_d[b] = static_cast<double>(peak);
+  grid.sync();
+  if (tid == 0) {
+    double pk = -INFINITY;
+    for (int x = 0; x < G; ++x) pk = fmax(pk, __ldcg(&g.cta_d[x]));
+    sm.wf[0] = static_cast<float>(pk);
+  }
+  __syncthreads();
+  peak = sm.wf[0];
+  if (!isfinite(peak)) peak = 0.f;
+  __syncthreads();
+  for (int j = lo + tid; j < hi; j += kSampThreads) {
+    const float v = s[j];
+    e[j] = isfinite(v) ? expf(__fsub_rn(v, peak)) : 0.f;
+  }
+  grid.sync();
+  leaf_sums<float>(p, [&](int j) { return __ldcg(&e[j]); }, g.leaf32, b * (kSampThreads / 8), G * (kSampThreads / 8));
+  grid.sync();
+  if (b == 0) {
+    float *vals = reinterpret_cast<float *>(sm.tree);
+    for (int l = tid; l < p.n_leaves; l += kSampThreads) vals[l] = __ldcg(&g.leaf32[l]);
+    __syncthreads();
+    const float total = tree_combine<float>(p, sm);
+    if (tid == 0) g.fs[0] = total;
+  }
+  grid.sync();
+  const float total = __ldcg(&g.fs[0]);
+  if (!(total > 0.f) || !isfinite(total)) {  // every candidate underflowed
+    if (b == 0 && tid == 0) {
+      p.out[0] = grid_argmax_merge(g);
+      p.out[1] = 0;
+    }
+    return;
+  }
+  for (int j = lo + tid; j < hi; j += kSampThreads) e[j] = __fdiv_rn(e[j], total);
+  grid.sync();
+  leaf_sums<double>(p, [&](int j) { return static_cast<double>(__ldcg(&e[j])); }, g.leaf64, b * (kSampThreads / 8),
+                    G * (kSampThreads / 8));
+  grid.sync();
+  if (b == 0) {
+    double *vals = reinterpret_cast<double *>(sm.tree);
+    for (int l = tid; l < p.n_leaves; l += kSampThreads) vals[l] = __ldcg(&g.leaf64[l]);
+    __syncthreads();
+    const double s64 = tree_combine<double>(p, sm);
+    if (tid == 0) g.ds[0] = s64;
+  }
+  grid.sync();
+  const double inv = __ddiv_rn(1.0, __ldcg(&g.ds[0]));
+  // this CTA's float64 sum, in tiles of one value per thread
+  double mine = 0.0;
+  for (int base = lo; base < hi; base += kSampThreads) {
+    const int j = base + tid;
+    double tile;
+    samp_block_scan(sm, j < hi ? __dmul_rn(static_cast<double>(e[j]), inv) : 0.0, &tile);
+    mine = __dadd_rn(mine, tile);
+  }
+  if (tid == 0) g.cta_d[b] = mine;
+  grid.sync();
+  if (tid == 0) {
+    double before = 0.0, last = 0.0;
+    for (int x = 0; x < G; ++x) {
+      const double v = __ldcg(&g.cta_d[x]);
+      if (x < b) before = __dadd_rn(before, v);
+      last = __dadd_rn(last, v);
+    }
+    sm.dmisc[0] = before;
+    sm.dmisc[1] = __dmul_rn(p.u, last);
+  }
+  __syncthreads();
+  double run = sm.dmisc[0];
+  const double target = sm.dmisc[1];
+  __syncthreads();
+  if (__dadd_rn(run, mine) > target) {  // the crossing is in this slice (block-uniform)
+    for (int base = lo; base < hi; base += kSampThreads) {
+      const int j = base + tid;
+      double tile;
+      const double incl = samp_block_scan(sm, j < hi ? __dmul_rn(static_cast<double>(e[j]), inv) : 0.0, &tile);
+      const int hit = (j < hi && __dadd_rn(run, incl) > target) ? j : 0x7fffffff;
+      const int first = samp_block_min(sm, hit);
+      if (first != 0x7fffffff) {
+        if (tid == 0) atomicMin(&g.ctr[1], first);
+        break;
+      }
+      run = __dadd_rn(run, tile);
+    }
+  }
+  grid.sync();
+  if (b == 0 && tid == 0) {
+    const int first = __ldcg(&g.ctr[1]);
+    p.out[0] = first < V ? first : V - 1;
+    p.out[1] = 0;
+  }
 }
 
 // Log-probabilities for an OpenAI ``logprobs`` entry: the reference's
