@@ -408,3 +408,40 @@ def test_drop_in_device_logprobs_match_host_entries():
     finally:
         decoder.close()
         engine.close()
+
+
+@pytest.mark.gpu
+def test_batched_device_sampling_matches_single_rows_at_qwen_vocabulary():
+    """hb_sample_batch (one thread block per row) selects what the single
+    selection selects on the same logits (the grid-wide kernel at this
+    vocabulary), row by row, and reports a flat top-p nucleus as too large
+    (None) per row without disturbing the other rows."""
+    import dataclasses
+
+    from runtime import synthetic
+    from runtime.b200_engine import B200DecoderEngine
+    from runtime.device_sampler import DeviceSampler
+
+    shape = dataclasses.replace(synthetic.TINY_QWEN, vocab=151936)
+    model = synthetic.build(shape, seed=45)
+    engine = B200DecoderEngine(model, max_slots=4, max_batch=8)
+    try:
+        ids = synthetic.prompt_ids(shape.vocab, 4, seed=2)
+        engine.step_batch([0, 1, 2, 3], ids, [0, 0, 0, 0], device_logits=True)
+        logits = engine.device_logits(rows=4)
+        params = [osamp.Params(temperature=0.8), osamp.Params(temperature=1.0, top_k=50, top_p=0.9),
+                  osamp.Params(temperature=1.0, top_p=0.9),  # flat random-init logits: too large
+                  osamp.Params(temperature=0.7, repetition_penalty=1.3, logit_bias={11: 5.0})]
+        histories = [ids[:1], ids[:2], ids[:3], ids]
+        rng = np.random.default_rng(6)
+        uniforms = [rng.random() for _ in params]
+        got = engine.sample_batch([0, 1, 2, 3], params, histories, uniforms)
+        assert got[2] is None
+        with DeviceSampler(shape.vocab) as dev:
+            for r in (0, 1, 3):
+                single = dev.select(logits[r], histories[r], params[r], uniforms[r])
+                assert got[r] == single
+                want = osamp.select_with_uniform(logits[r], histories[r], params[r], uniforms[r])
+                assert got[r] == want or _near_tie(logits[r], histories[r], params[r], uniforms[r])
+    finally:
+        engine.close()
