@@ -1,4 +1,10 @@
-// hb_sample.cuh -- on-device token selection (one CTA of 1024 threads).
+// hb_sample.cuh -- on-device token selection and logprobs.
+//
+// Three launch shapes share one pipeline: sample_kernel (one CTA of 1024
+// threads), sample_batch_kernel (one such CTA per row of a batched step) and
+// sample_grid_kernel (one selection spread over every SM, cooperative
+// launch, for large vocabularies); logprob_kernel gives the log_softmax
+// entries of an OpenAI `logprobs` answer.
 //
 // The selection pipeline of the reference's Sampler.select
 // (npu_llm/runtime/sampling.py:416-445) on FP32 logits already in device

@@ -234,7 +234,8 @@ typedef struct {
 
 typedef struct hb_sampler hb_sampler;
 /* A standalone sampler for `vocab`-wide logits on `device` (owns its device
- * scratch and its stream). */
+ * scratch and its stream).  Vocabularies of 16,384 and more select with one
+ * thread block per SM (a cooperative launch), smaller ones with one. */
 int hb_sampler_create(int vocab, int device, hb_sampler **out);
 /* Select from `logits` (host memory, or device memory when
  * logits_on_device is nonzero). */
