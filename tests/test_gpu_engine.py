@@ -315,3 +315,30 @@ def test_full_size_batched_prefill_matches_sequential():
     assert got == ref
     n = len(ids) + 5
     assert np.array_equal(kv_b[:, :, :, :n].view(np.uint16), kv_s[:, :, :, :n].view(np.uint16))
+
+
+def test_full_context_matches_oracle(tiny):
+    """Every position of the 64-token context (the reference's maximum,
+    npu_llm/runtime/generate.py:43-44): teacher-forced logits against the
+    oracle up to position 63; a 63-position batched prefill gives the same KV
+    cache and last logits as one position per launch; a batch step at
+    position 63 matches the single-row step."""
+    model, engine = tiny
+    ctx = model.shape.context
+    ids = synthetic.prompt_ids(model.shape.vocab, ctx, seed=13)
+    oracle = OracleDecoder(model)
+    engine.reset(0)
+    for position, token in enumerate(ids):
+        got = engine.step(token, position, logits=True, slot=0)
+        assert_logits_close(got, oracle.step(token, position), f"position {position}")
+    engine.reset(1)
+    _, last = engine.prefill(ids, slot=1, logits=True)
+    single = engine.step(ids[-1], ctx - 1, logits=True, slot=0)
+    assert np.array_equal(last, single)
+    assert np.array_equal(engine.kv_cache(0), engine.kv_cache(1))
+    am, logits = engine.step_batch([0, 1], [ids[-1], ids[-1]], [ctx - 1, ctx - 1], logits=True)
+    assert np.array_equal(logits[0], logits[1])
+    assert_logits_close(logits[0], single, "batch row at position 63")
+    assert int(am[0]) == int(np.argmax(logits[0]))
+    with pytest.raises(ValueError):
+        engine.step(ids[0], ctx, slot=0)
