@@ -30,6 +30,15 @@
 // position (block cb of row s at s*128 + (cb ^ (s & 7))*16), so tensor-core
 // fragment loads (ldmatrix) of 8 consecutive positions are bank-conflict
 // free.
+//
+// Contexts longer than 64 positions (paged mode) keep the cache in pages of
+// 64 positions, each laid out as one 64-position slot above
+// ([L][KVH][K | V][64][128 B], same swizzle); a per-slot page table maps
+// position s to page table[slot][s / 64].  The attention phase then splits
+// each (row, q head) unit's positions over up to G / (rows * QH) CTAs: each
+// split publishes its partial (max, sum of exp, unnormalised P.V) to global
+// scratch, and the last split to arrive combines them and publishes the
+// head's outputs.
 #pragma once
 
 #include "hb_stream.cuh"
@@ -38,6 +47,10 @@ namespace hb {
 
 constexpr int kMaxBatch = 8;
 constexpr int kHeadDim = 64;
+constexpr int kPagePositions = 64;    // positions per KV page (paged mode)
+constexpr int kMaxPagedContext = 4096;
+constexpr int kSplitPositions = 128;  // positions per attention split, at least
+constexpr int kPartStride = 68;       // floats per split partial: P.V [64], max, sum
 constexpr int kMaxHPerThread = 8;  // hidden <= 8 * 224 = 1792 (two word pairs per thread)
 
 struct LayerPtrs {
@@ -82,6 +95,7 @@ struct DecParams {
   const __nv_bfloat16 *embed;
   const float *rope_cos, *rope_sin;  // [CTX][32]
   __nv_bfloat16 *kv;                 // [slots][L][KVH][K CTXx64 | V CTXx64], swizzled rows
+                                     // (paged: [pages][L][KVH][K 64x64 | V 64x64])
   uint64_t *ll;                      // LL words, see ll_* below
   float *logits;                     // [MB][V]
   float *part_val;                   // [G][kMaxBatch]
@@ -99,6 +113,11 @@ struct DecParams {
   uint64_t limit_ns;
   uint64_t stall_ns;
   unsigned long long *trace;         // optional [G][4L+2][4] phase timestamps
+  int paged;                         // CTX > 64: the cache is paged (the PG kernels)
+  int pages_per_slot, n_pages;
+  const int *page_table;             // paged: [slots][pages_per_slot] page ids
+  float *att_part;                   // paged: [G][kPartStride] split partials
+  int *att_cnt;                      // paged: [kMaxBatch * QH] split arrivals (reset by the last)
 };
 
 // LL buffer layout: per layer a block of kMaxBatch rows of each kind
@@ -123,7 +142,7 @@ __host__ __device__ inline size_t att_bytes(int /*QH*/, int /*ctx*/) {
 }
 
 __host__ __device__ inline SmemPlan smem_plan(int nslots, int mb, int xs_elems, int H, int QKV,
-                                              int QH, int KVH, int red_rows, int ctx) {
+                                              int QH, int KVH, int red_rows, int ctx, bool paged) {
   SmemPlan s;
   size_t o = 0;
   s.ring = o;
@@ -143,7 +162,11 @@ __host__ __device__ inline SmemPlan smem_plan(int nslots, int mb, int xs_elems, 
   // attention starts after the previous phase's epilogue read them
   const size_t red_bytes = align_up(static_cast<size_t>(kWarps) * mb * red_rows * 4, 128);
   const size_t att_b = align_up(att_bytes(QH, ctx), 128);
-  const size_t kv_b = align_up(static_cast<size_t>(2) * ctx * 128, 128);
+  // paged mode: K/V rows of this launch's positions [2][8][128 B], the
+  // per-warp P.V partials [kWarps][64] and the split's scores [ctx]
+  const size_t kv_b = paged
+                          ? align_up(static_cast<size_t>(2) * kMaxBatch * 128 + kWarps * 64 * 4 + 4 * ctx, 128)
+                          : align_up(static_cast<size_t>(2) * ctx * 128, 128);
   s.red = o;
   s.att = o;
   s.kv = o + att_b;  // K then V history of one (row, kv head): [2][ctx][128 B]
@@ -240,7 +263,7 @@ __device__ __forceinline__ bool ll_gather(const uint64_t *src, size_t row_words,
   return true;
 }
 
-template <int MB, bool W8>
+template <int MB, bool W8, bool PG>  // PG: paged KV cache (context > 64)
 struct DecoderCta {
   const DecParams &P;
   Ring ring;
@@ -257,7 +280,7 @@ struct DecoderCta {
   size_t lw;          // LL words per layer block
 
   __device__ DecoderCta(const DecParams &p, uint8_t *smem) : P(p) {
-    const SmemPlan sp = smem_plan(P.nslots, MB, P.xs_elems, P.H, P.QKV, P.QH, P.KVH, P.red_rows, P.CTX);
+    const SmemPlan sp = smem_plan(P.nslots, MB, P.xs_elems, P.H, P.QKV, P.QH, P.KVH, P.red_rows, P.CTX, PG);
     ring.slots = smem + sp.ring;
     ring.full = reinterpret_cast<uint64_t *>(smem + sp.full);
     ring.empty = reinterpret_cast<uint64_t *>(smem + sp.empty);
@@ -684,6 +707,258 @@ struct DecoderCta {
     ll_store(ll_att(layer, m) + h * 32 + lane, pack_bf16x2(o00 + o10, o01 + o11), epoch);
   }
 
+  // ---- paged attention (contexts longer than 64 positions) ---------------------
+  // Splits of each (row, q head) unit's positions: one per kSplitPositions
+  // positions of the longest row, at most as many as leave every split its
+  // own CTA.  The same value in every CTA (it depends only on the step).
+  __device__ int att_splits() const {
+    int n = 0;
+    for (int m = 0; m < mrows; ++m) n = max(n, s_pos[m] + 1);
+    const int want = (n + kSplitPositions - 1) / kSplitPositions;
+    const int cap = G / (mrows * P.QH);
+    return max(1, min(want, cap));
+  }
+
+  // Page holding position s of a slot; -1 (and the launch's error raised)
+  // when the table entry lies outside the pool -- the host maps every page
+  // a step reads or writes before the launch, so this guards only the
+  // bounds of the accesses below.
+  __device__ int kv_page(int slot, int s) const {
+    const int pg = __ldg(P.page_table + static_cast<size_t>(slot) * P.pages_per_slot + (s >> 6));
+    if (static_cast<unsigned>(pg) >= static_cast<unsigned>(P.n_pages)) {
+      raise_error(&P.result->ctrl, kErrBadPage, kWhereKvPage);
+      return -1;
+    }
+    return pg;
+  }
+
+  // The 64 K (kind 0) or V (kind 1) rows of one (layer, kv head) in page pg.
+  __device__ const uint8_t *page_rows(int pg, int layer, int kvh, int kind) const {
+    return reinterpret_cast<const uint8_t *>(P.kv) +
+           ((((static_cast<size_t>(pg) * P.L + layer) * P.KVH + kvh) * 2 + kind) << 13);
+  }
+
+  // One (row m, q head h, split sp of S) unit in paged mode: RoPE of q and
+  // of this launch's k rows (kept in shared memory, 128-byte rows in
+  // logical block order), the K/V append (split 0 of the group's first q
+  // head), then over the split's positions [lo, hi): scores q.k * 0.125,
+  // max, exp(score - max), their sum and the unnormalised P.V, all seven
+  // warps sharing the positions.  One split publishes o = P.V / sum; with
+  // several, each leaves (P.V, max, sum) in att_part and the last to arrive
+  // rescales them to the common max and publishes sum(w P.V) / sum(w sum).
+  __device__ void attention_paged(int layer, int m, int h, int j, int sp, int S, uint32_t *u96) {
+    const int p = s_pos[m], slot = s_slot[m];
+    const int f = run_start(m), p0 = s_pos[f];  // positions >= p0 are computed in this launch
+    const int n = p + 1;
+    int chunk = (n + S - 1) / S;
+    chunk = (chunk + 31) & ~31;
+    const int lo = min(n, sp * chunk), hi = min(n, lo + chunk);
+    float *qf = reinterpret_cast<float *>(u96 + 96);
+    float *rmax = qf + kHeadDim;  // [kWarps]
+    float *rsum = rmax + 8;       // [kWarps]
+    int *flag = reinterpret_cast<int *>(rsum + 8);
+    uint8_t *stk = kvs, *stv = kvs + kMaxBatch * 128;
+    float *pv = reinterpret_cast<float *>(kvs + 2 * kMaxBatch * 128);  // [kWarps][64]
+    float *sc = pv + kWarps * kHeadDim;                               // [hi - lo]
+    const int warp = tid >> 5, lane = tid & 31;
+    consumer_sync(kConsumerThreads);  // u96 complete
+    if (warp == 0) {
+      auto rope_pair = [&](const uint32_t *w32, int pr, int d, __nv_bfloat16 &rlo, __nv_bfloat16 &rhi) {
+        const uint32_t a = w32[d >> 1], b = w32[(d + 32) >> 1];
+        const float x0 = (d & 1) ? bf_hi(a) : bf_lo(a), x1 = (d & 1) ? bf_hi(b) : bf_lo(b);
+        const float c = P.rope_cos[pr * 32 + d], sn = P.rope_sin[pr * 32 + d];
+        rlo = f2bf(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+        rhi = f2bf(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
+      };
+      auto put_row = [&](int lr, __nv_bfloat16 klo, __nv_bfloat16 khi, uint32_t vword) {
+        reinterpret_cast<__nv_bfloat16 *>(stk + lr * 128)[lane] = klo;
+        reinterpret_cast<__nv_bfloat16 *>(stk + lr * 128)[lane + 32] = khi;
+        reinterpret_cast<uint32_t *>(stv + lr * 128)[lane] = vword;
+      };
+      __nv_bfloat16 rlo, rhi;
+      rope_pair(u96, p, lane, rlo, rhi);  // q
+      qf[lane] = bf2f(rlo);
+      qf[lane + 32] = bf2f(rhi);
+      rope_pair(u96 + 32, p, lane, rlo, rhi);  // k of row m
+      put_row(m - f, rlo, rhi, u96[64 + lane]);
+      for (int r = f; r < m; ++r) {  // batched prefill: the run's earlier rows
+        const uint32_t *w = u96 + kUnitWords + 64 * (r - f);
+        rope_pair(w, s_pos[r], lane, rlo, rhi);
+        put_row(r - f, rlo, rhi, w[32 + lane]);
+      }
+      __syncwarp();
+      if (sp == 0 && h % P.group == 0 && lane < 16) {
+        const int kind = lane >> 3, cb = lane & 7;
+        const int pg = kv_page(slot, p);
+        if (pg >= 0) {
+          const uint8_t *src = (kind ? stv : stk) + (m - f) * 128 + cb * 16;
+          uint8_t *dst = const_cast<uint8_t *>(page_rows(pg, layer, j, kind)) + kv_off(p & 63, cb);
+          *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
+        }
+      }
+    }
+    consumer_sync(kConsumerThreads);  // qf and the launch's rows visible
+    // scores: thread per position, two rows in flight (one in the 8-row
+    // kernels, whose GEMV leaves fewer registers)
+    constexpr int kRowsInFlight = MB == 1 ? 2 : 1;
+    float tmax = -INFINITY;
+    for (int s0 = lo + tid; s0 < hi; s0 += kRowsInFlight * kConsumerThreads) {
+      uint4 kw[kRowsInFlight][8];
+#pragma unroll
+      for (int e = 0; e < kRowsInFlight; ++e) {
+        const int s = s0 + e * kConsumerThreads;
+        if (s < hi && s < p0) {
+          const int pg = kv_page(slot, s);
+          const uint8_t *row = pg >= 0 ? page_rows(pg, layer, j, 0) + (s & 63) * 128 : nullptr;
+#pragma unroll
+          for (int cb = 0; cb < 8; ++cb)
+            kw[e][cb] = row ? __ldcg(reinterpret_cast<const uint4 *>(row + ((cb ^ (s & 7)) << 4)))
+                            : make_uint4(0u, 0u, 0u, 0u);
+        } else if (s < hi) {
+#pragma unroll
+          for (int cb = 0; cb < 8; ++cb) kw[e][cb] = reinterpret_cast<const uint4 *>(stk + (s - p0) * 128)[cb];
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < kRowsInFlight; ++e) {
+        const int s = s0 + e * kConsumerThreads;
+        if (s < hi) {
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int cb = 0; cb < 8; ++cb) {
+            const uint4 k = kw[e][cb];
+            const float *q = qf + 8 * cb;
+            float &a = acc[cb & 3];
+            a = fmaf(bf_lo(k.x), q[0], a);
+            a = fmaf(bf_hi(k.x), q[1], a);
+            a = fmaf(bf_lo(k.y), q[2], a);
+            a = fmaf(bf_hi(k.y), q[3], a);
+            a = fmaf(bf_lo(k.z), q[4], a);
+            a = fmaf(bf_hi(k.z), q[5], a);
+            a = fmaf(bf_lo(k.w), q[6], a);
+            a = fmaf(bf_hi(k.w), q[7], a);
+          }
+          const float score = ((acc[0] + acc[1]) + (acc[2] + acc[3])) * 0.125f;
+          sc[s - lo] = score;
+          tmax = fmaxf(tmax, score);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+    if (lane == 0) rmax[warp] = tmax;
+    consumer_sync(kConsumerThreads);
+    float mx = rmax[0];
+    for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, rmax[w]);
+    float tsum = 0.f;
+    for (int s = lo + tid; s < hi; s += kConsumerThreads) {
+      const float e = expf(__fsub_rn(sc[s - lo], mx));
+      sc[s - lo] = e;
+      tsum += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tsum += __shfl_xor_sync(0xffffffffu, tsum, o);
+    if (lane == 0) rsum[warp] = tsum;
+    consumer_sync(kConsumerThreads);  // sc (weights) and rsum visible
+    float sum = 0.f;
+    for (int w = 0; w < kWarps; ++w) sum += rsum[w];
+    // P.V: a quarter warp per position (lane: 8 dims of block cb), two
+    // positions per lane in flight
+    const int q4 = lane >> 3, cb = lane & 7;
+    float o8[8];
+#pragma unroll
+    for (int d = 0; d < 8; ++d) o8[d] = 0.f;
+    constexpr int kStride = kWarps * 4;
+    for (int s0 = lo + warp * 4 + q4; s0 < hi; s0 += 2 * kStride) {
+      uint4 vw[2];
+      float wt[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int s = s0 + e * kStride;
+        vw[e] = make_uint4(0u, 0u, 0u, 0u);
+        wt[e] = 0.f;
+        if (s < hi) {
+          wt[e] = sc[s - lo];
+          if (s < p0) {
+            const int pg = kv_page(slot, s);
+            if (pg >= 0)
+              vw[e] = __ldcg(reinterpret_cast<const uint4 *>(page_rows(pg, layer, j, 1) + (s & 63) * 128 +
+                                                             ((cb ^ (s & 7)) << 4)));
+          } else {
+            vw[e] = reinterpret_cast<const uint4 *>(stv + (s - p0) * 128)[cb];
+          }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        o8[0] = fmaf(wt[e], bf_lo(vw[e].x), o8[0]);
+        o8[1] = fmaf(wt[e], bf_hi(vw[e].x), o8[1]);
+        o8[2] = fmaf(wt[e], bf_lo(vw[e].y), o8[2]);
+        o8[3] = fmaf(wt[e], bf_hi(vw[e].y), o8[3]);
+        o8[4] = fmaf(wt[e], bf_lo(vw[e].z), o8[4]);
+        o8[5] = fmaf(wt[e], bf_hi(vw[e].z), o8[5]);
+        o8[6] = fmaf(wt[e], bf_lo(vw[e].w), o8[6]);
+        o8[7] = fmaf(wt[e], bf_hi(vw[e].w), o8[7]);
+      }
+    }
+#pragma unroll
+    for (int d = 0; d < 8; ++d) {
+      o8[d] += __shfl_xor_sync(0xffffffffu, o8[d], 8);
+      o8[d] += __shfl_xor_sync(0xffffffffu, o8[d], 16);
+    }
+    if (q4 == 0) {
+#pragma unroll
+      for (int d = 0; d < 8; ++d) pv[warp * kHeadDim + cb * 8 + d] = o8[d];
+    }
+    consumer_sync(kConsumerThreads);
+    uint64_t *out = ll_att(layer, m) + h * 32;
+    if (S == 1) {
+      if (tid < 32) {
+        float a = 0.f, b = 0.f;
+        for (int w = 0; w < kWarps; ++w) {
+          a += pv[w * kHeadDim + 2 * tid];
+          b += pv[w * kHeadDim + 2 * tid + 1];
+        }
+        ll_store(out + tid, pack_bf16x2(__fdiv_rn(a, sum), __fdiv_rn(b, sum)), epoch);
+      }
+      return;
+    }
+    float *part = P.att_part + static_cast<size_t>(cta) * kPartStride;
+    if (tid < kHeadDim) {
+      float a = 0.f;
+      for (int w = 0; w < kWarps; ++w) a += pv[w * kHeadDim + tid];
+      part[tid] = a;
+    } else if (tid == kHeadDim) {
+      part[kHeadDim] = mx;
+      part[kHeadDim + 1] = sum;
+    }
+    consumer_sync(kConsumerThreads);
+    int *cnt = P.att_cnt + m * P.QH + h;
+    if (tid == 0) {
+      __threadfence();
+      *flag = atomicAdd(cnt, 1) == S - 1 ? 1 : 0;
+    }
+    consumer_sync(kConsumerThreads);
+    if (*flag == 0) return;
+    // last split: every other split's partial is visible after the fence
+    if (tid == 0) atomicExch(cnt, 0);
+    __threadfence();
+    if (tid < 32) {
+      const float *base = P.att_part + static_cast<size_t>(cta - sp) * kPartStride;
+      float M = -INFINITY;
+      for (int q = 0; q < S; ++q) M = fmaxf(M, __ldcg(base + q * kPartStride + kHeadDim));
+      float den = 0.f, a = 0.f, b = 0.f;
+      for (int q = 0; q < S; ++q) {
+        const float *pq = base + q * kPartStride;
+        const float w = expf(__fsub_rn(__ldcg(pq + kHeadDim), M));
+        den = fmaf(w, __ldcg(pq + kHeadDim + 1), den);
+        a = fmaf(w, __ldcg(pq + 2 * tid), a);
+        b = fmaf(w, __ldcg(pq + 2 * tid + 1), b);
+      }
+      ll_store(out + tid, pack_bf16x2(__fdiv_rn(a, den), __fdiv_rn(b, den)), epoch);
+    }
+  }
+
   // One phase of a layer (kind = k & 3: 0 qkv, 1 attention + o_proj,
   // 2 gate_up + SwiGLU, 3 down).  A prologue leaves the GEMV's BF16 input in
   // xs, then the GEMV over this CTA's rows -- a single call site for every
@@ -701,7 +976,17 @@ struct DecoderCta {
     const float2 scale0 = load_pair(scale_p, r.g0 * 8, npairs);
     Gamma gamma;
     if (kind == 0 || kind == 2) gamma = load_gamma(kind == 0 ? lp.gamma_in : lp.gamma_post);
-    const int um = cta / P.QH, uh = cta - um * P.QH, uj = uh / P.group;  // attention unit
+    // attention unit of this CTA: (row um, q head uh, kv head uj), and in
+    // paged mode split us of S
+    int S = 1, us = 0, ucta = cta;
+    if constexpr (PG) {
+      if (kind == 1) {
+        S = att_splits();
+        ucta = cta / S;
+        us = cta - ucta * S;
+      }
+    }
+    const int um = ucta / P.QH, uh = ucta - um * P.QH, uj = uh / P.group;
     uint32_t *u96 = reinterpret_cast<uint32_t *>(att);
     // inputs: the previous phase's LL words (the embedding row for layer 0)
     bool ok = true;
@@ -719,7 +1004,9 @@ struct DecoderCta {
         ok = gather_to_hx(ll_hout(layer - 1, 0), P.H / 2, P.H);
       }
     } else if (kind == 1) {
-      if (has_unit()) {
+      if constexpr (PG) {
+        if (ucta < mrows * P.QH) ok = gather_unit(layer, um, uh, uj, u96);
+      } else if (has_unit()) {
         kv_prefetch_unit(layer, um, uj);  // overlaps the wait for q/k/v
         ok = gather_unit(layer, um, uh, uj, u96);
         if (!ok) cp_async_wait_all();
@@ -736,7 +1023,11 @@ struct DecoderCta {
     if (kind == 0 || kind == 2) {
       norm_rows(gamma);
     } else if (kind == 1) {
-      if (has_unit()) attention_unit(layer, um, uh, uj, u96);
+      if constexpr (PG) {
+        if (ucta < mrows * P.QH) attention_paged(layer, um, uh, uj, us, S, u96);
+      } else if (has_unit()) {
+        attention_unit(layer, um, uh, uj, u96);
+      }
       if (!gather_raw(ll_att(layer, 0), P.H / 2, P.H / 2, reinterpret_cast<uint32_t *>(xs), P.xs_elems / 2))
         return false;
       consumer_sync(kConsumerThreads);
@@ -955,10 +1246,10 @@ struct DecoderCta {
   }
 };
 
-template <int MB, bool W8>
+template <int MB, bool W8, bool PG>
 __global__ void __launch_bounds__(kThreads, 1) decoder_kernel(const __grid_constant__ DecParams P) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  DecoderCta<MB, W8> cx(P, smem);
+  DecoderCta<MB, W8, PG> cx(P, smem);
   if (threadIdx.x == 0) {
     for (int i = 0; i < P.nslots; ++i) {
       mbar_init(&cx.ring.full[i], 1);

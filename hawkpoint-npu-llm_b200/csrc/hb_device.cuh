@@ -29,6 +29,7 @@ enum : int {
   kErrNone = 0,
   kErrTimeout = 1,
   kErrBadToken = 2,  // a device-chained token id fell outside the vocabulary
+  kErrBadPage = 3,   // a KV page-table entry fell outside the page pool
 };
 
 enum : int {
@@ -38,6 +39,7 @@ enum : int {
   kWhereStall = 4,
   kWhereDrain = 5,
   kWhereToken = 6,
+  kWhereKvPage = 7,
 };
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {

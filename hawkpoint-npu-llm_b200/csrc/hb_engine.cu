@@ -63,6 +63,17 @@ struct hb_engine {
   float *d_rope_cos = nullptr, *d_rope_sin = nullptr;
   __nv_bfloat16 *d_kv = nullptr;
   size_t kv_slot_elems = 0;
+  // paged KV cache (context > 64): pages of 64 positions, a page table per
+  // slot (host copy authoritative, uploaded before a launch that follows a
+  // change), reference counts for pages shared by copy_prefix
+  bool paged = false;
+  int pages_per_slot = 0, n_pages = 0;
+  size_t page_bytes = 0;
+  std::vector<int> page_table, page_refs, free_pages;
+  bool table_dirty = false;
+  int *d_page_table = nullptr;
+  float *d_att_part = nullptr;
+  int *d_att_cnt = nullptr;
   uint64_t *d_ll = nullptr;
   size_t ll_words = 0;
   unsigned int *d_epoch = nullptr;
@@ -139,7 +150,7 @@ int validate_desc(const hb_model_desc *d) {
     return fail(nullptr, HB_ERR_INVALID_ARG, "abi_version %d != %d", d->abi_version, HB_ABI_VERSION);
   if (d->head_dim != hb::kHeadDim) return fail(nullptr, HB_ERR_UNSUPPORTED, "head_dim must be 64");
   if (d->hidden <= 0 || d->intermediate <= 0 || d->q_heads <= 0 || d->kv_heads <= 0 ||
-      d->layers <= 0 || d->vocab <= 0 || d->context <= 0 || d->context > 1024)
+      d->layers <= 0 || d->vocab <= 0 || d->context <= 0)
     return fail(nullptr, HB_ERR_INVALID_ARG, "invalid model dimensions");
   if (d->q_heads % d->kv_heads) return fail(nullptr, HB_ERR_INVALID_ARG, "q_heads %% kv_heads != 0");
   if (d->hidden != d->q_heads * d->head_dim)
@@ -155,9 +166,12 @@ int validate_desc(const hb_model_desc *d) {
   if (d->hidden > hb::kMaxHPerThread * hb::kConsumerThreads)
     return fail(nullptr, HB_ERR_UNSUPPORTED, "hidden > %d", hb::kMaxHPerThread * hb::kConsumerThreads);
   // attention: 8-position tiles of a 64-position context, split over at
-  // least two warps per kv head
-  if (d->kv_heads > 4 || d->context > 64)
-    return fail(nullptr, HB_ERR_UNSUPPORTED, "kv_heads <= 4 and context <= 64 required");
+  // least two warps per kv head; longer contexts use 64-position pages
+  if (d->kv_heads > 4) return fail(nullptr, HB_ERR_UNSUPPORTED, "kv_heads <= 4 required");
+  if (d->context > hb::kPagePositions &&
+      (d->context % hb::kPagePositions || d->context > hb::kMaxPagedContext))
+    return fail(nullptr, HB_ERR_UNSUPPORTED, "context must be <= 64, or a multiple of 64 up to %d",
+                hb::kMaxPagedContext);
   if (d->max_slots <= 0 || d->max_batch <= 0 || d->max_batch > kMaxBatch)
     return fail(nullptr, HB_ERR_INVALID_ARG, "max_slots > 0 and 1 <= max_batch <= 8 required");
   if (!d->layer_offsets || !d->rope_cos || !d->rope_sin)
@@ -187,14 +201,14 @@ int setup_variant(hb_engine *e, Variant &v, int mb, const void *fn, int smem_opt
   const hb_model_desc &d = e->desc;
   const int qkv = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
   const hb::SmemPlan base =
-      hb::smem_plan(0, mb, e->xs_elems, d.hidden, qkv, d.q_heads, d.kv_heads, e->red_rows, d.context);
+      hb::smem_plan(0, mb, e->xs_elems, d.hidden, qkv, d.q_heads, d.kv_heads, e->red_rows, d.context, e->paged);
   int nslots = static_cast<int>((static_cast<size_t>(smem_optin) - base.total - 16 * kMaxSlotsRing) /
                                 hb::kSlotBytes);
   if (nslots > kMaxSlotsRing) nslots = kMaxSlotsRing;
   if (nslots < kMinSlotsRing)
     return fail(e, HB_ERR_UNSUPPORTED, "model too large for the shared-memory plan (batch %d)", mb);
   const hb::SmemPlan sp =
-      hb::smem_plan(nslots, mb, e->xs_elems, d.hidden, qkv, d.q_heads, d.kv_heads, e->red_rows, d.context);
+      hb::smem_plan(nslots, mb, e->xs_elems, d.hidden, qkv, d.q_heads, d.kv_heads, e->red_rows, d.context, e->paged);
   HB_CUDA(e, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sp.total)));
   int blocks = 0;
   HB_CUDA(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, hb::kThreads, sp.total));
@@ -245,14 +259,27 @@ DecParams base_params(hb_engine *e, const Variant &v) {
   P.xs_elems = e->xs_elems;
   P.limit_ns = e->limit_ns;
   P.trace = e->trace_enabled ? e->d_trace : nullptr;
+  P.paged = e->paged ? 1 : 0;
+  P.pages_per_slot = e->pages_per_slot;
+  P.n_pages = e->n_pages;
+  P.page_table = e->d_page_table;
+  P.att_part = e->d_att_part;
+  P.att_cnt = e->d_att_cnt;
   return P;
 }
 
-const void *decoder_fn(int mb, bool w8) {
-  if (mb == 1) return w8 ? reinterpret_cast<const void *>(&hb::decoder_kernel<1, true>)
-                         : reinterpret_cast<const void *>(&hb::decoder_kernel<1, false>);
-  return w8 ? reinterpret_cast<const void *>(&hb::decoder_kernel<8, true>)
-            : reinterpret_cast<const void *>(&hb::decoder_kernel<8, false>);
+template <bool PG>
+const void *decoder_fn_t(int mb, bool w8) {
+  if (mb == 1) return w8 ? reinterpret_cast<const void *>(&hb::decoder_kernel<1, true, PG>)
+                         : reinterpret_cast<const void *>(&hb::decoder_kernel<1, false, PG>);
+  return w8 ? reinterpret_cast<const void *>(&hb::decoder_kernel<8, true, PG>)
+            : reinterpret_cast<const void *>(&hb::decoder_kernel<8, false, PG>);
+}
+
+// The kernels of a paged cache (context > 64) are separate instances, so
+// the attention of the 64-position kernels compiles as it would alone.
+const void *decoder_fn(int mb, bool w8, bool paged) {
+  return paged ? decoder_fn_t<true>(mb, w8) : decoder_fn_t<false>(mb, w8);
 }
 
 // Launch phases [pb, pe) for the rows in d_st.
@@ -294,9 +321,13 @@ int finish(hb_engine *e) {
     // words of the aborted launch may carry the current epoch: clear them all
     HB_CUDA(e, cudaMemsetAsync(e->d_ll, 0, e->ll_words * 8, e->stream));
     HB_CUDA(e, cudaMemsetAsync(e->d_result, 0, sizeof(hb::Result), e->stream));
+    if (e->d_att_cnt)
+      HB_CUDA(e, cudaMemsetAsync(e->d_att_cnt, 0, sizeof(int) * kMaxBatch * e->desc.q_heads, e->stream));
     HB_CUDA(e, cudaStreamSynchronize(e->stream));
     if (code == hb::kErrBadToken)
       return fail(e, HB_ERR_STATE, "device-chained token id outside the vocabulary; engine state reset");
+    if (code == hb::kErrBadPage)
+      return fail(e, HB_ERR_STATE, "KV page-table entry outside the page pool; engine state reset");
     static const char *names[] = {"?", "weight chunk", "ring slot", "grid barrier", "test stall flag", "drain"};
     return fail(e, HB_ERR_DEVICE_TIMEOUT, "device wait on %s timed out; engine state reset",
                 names[(where >= 0 && where <= 5) ? where : 0]);
@@ -320,6 +351,61 @@ int check_row(hb_engine *e, int slot, int token, int position) {
   return HB_OK;
 }
 
+// ---- paged KV cache -------------------------------------------------------------
+uint8_t *page_ptr(hb_engine *e, int pg) { return reinterpret_cast<uint8_t *>(e->d_kv) + e->page_bytes * pg; }
+
+// A page from the pool, zero-filled (a fresh slot reads zeros, as after a
+// reset), with one reference.
+int page_alloc(hb_engine *e, int *out) {
+  if (e->free_pages.empty()) return fail(e, HB_ERR_STATE, "KV page pool exhausted");
+  const int pg = e->free_pages.back();
+  e->free_pages.pop_back();
+  HB_CUDA(e, cudaMemsetAsync(page_ptr(e, pg), 0, e->page_bytes, e->stream));
+  e->page_refs[pg] = 1;
+  *out = pg;
+  return HB_OK;
+}
+
+void page_release(hb_engine *e, int pg) {
+  if (pg >= 0 && --e->page_refs[pg] == 0) e->free_pages.push_back(pg);
+}
+
+// Before a launch that reads positions [0, last] of a slot and writes
+// positions [first_write, last]: every page up to last mapped, and every
+// page written private (a page shared by copy_prefix is copied first).
+int pages_for_step(hb_engine *e, int slot, int first_write, int last) {
+  if (!e->paged) return HB_OK;
+  int *row = e->page_table.data() + static_cast<size_t>(slot) * e->pages_per_slot;
+  for (int i = 0; i <= last / hb::kPagePositions; ++i) {
+    const int pg = row[i];
+    if (pg < 0) {
+      int rc = page_alloc(e, &row[i]);
+      if (rc) return rc;
+      e->table_dirty = true;
+    } else if (i >= first_write / hb::kPagePositions && e->page_refs[pg] > 1) {
+      int fresh = -1;
+      int rc = page_alloc(e, &fresh);
+      if (rc) return rc;
+      HB_CUDA(e, cudaMemcpyAsync(page_ptr(e, fresh), page_ptr(e, pg), e->page_bytes, cudaMemcpyDeviceToDevice,
+                                 e->stream));
+      page_release(e, pg);
+      row[i] = fresh;
+      e->table_dirty = true;
+    }
+  }
+  return HB_OK;
+}
+
+// Uploads the page table after a change (from pageable memory: the copy
+// has taken the table's contents when the call returns).
+int upload_pages(hb_engine *e) {
+  if (!e->paged || !e->table_dirty) return HB_OK;
+  HB_CUDA(e, cudaMemcpyAsync(e->d_page_table, e->page_table.data(), sizeof(int) * e->page_table.size(),
+                             cudaMemcpyHostToDevice, e->stream));
+  e->table_dirty = false;
+  return HB_OK;
+}
+
 // Device-resident chained run: positions start..n_prompt-1 of ids (prefill;
 // the LM head only at the last), then n_new-1 further greedy steps.
 int run_chained(hb_engine *e, int slot, const int32_t *ids, int n_prompt, int start, int n_new,
@@ -334,6 +420,9 @@ int run_chained(hb_engine *e, int slot, const int32_t *ids, int n_prompt, int st
     if (rc) return rc;
   }
   for (int p = 0; p < d.context; ++p) e->h_prompt[p] = (p >= start && p < n_prompt) ? ids[p] : 0;
+  // the chained launches write positions start .. n_prompt + n_new - 2
+  int prc = pages_for_step(e, slot, start, n_prompt + n_new - 2);
+  if (prc || (prc = upload_pages(e))) return prc;
   const int body = 4 * d.layers;
   const int full = 4 * d.layers + 1;
   int upload = 0;
@@ -444,8 +533,11 @@ int hb_create(const hb_model_desc *desc, int device, hb_engine **out) {
   e->xs_elems = std::max(d.hidden, d.intermediate);  // GEMV inputs
   e->xs_elems = (e->xs_elems + 15) / 16 * 16;
   const bool w8 = d.weight_format == HB_WEIGHTS_W8;
-  if ((rc = setup_variant(e, e->var1, 1, decoder_fn(1, w8), prop.sharedMemPerBlockOptin))) return bail(rc);
-  if (d.max_batch > 1 && (rc = setup_variant(e, e->var8, 8, decoder_fn(8, w8), prop.sharedMemPerBlockOptin)))
+  const bool paged = d.context > hb::kPagePositions;
+  e->paged = paged;  // sizes the attention scratch of the shared-memory plan
+  if ((rc = setup_variant(e, e->var1, 1, decoder_fn(1, w8, paged), prop.sharedMemPerBlockOptin))) return bail(rc);
+  if (d.max_batch > 1 &&
+      (rc = setup_variant(e, e->var8, 8, decoder_fn(8, w8, paged), prop.sharedMemPerBlockOptin)))
     return bail(rc);
   if (cudaStreamCreateWithFlags(&e->own_stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(fail(nullptr, HB_ERR_CUDA, "stream creation failed"));
@@ -453,6 +545,20 @@ int hb_create(const hb_model_desc *desc, int device, hb_engine **out) {
 
   const int mb = d.max_batch > 1 ? kMaxBatch : 1;
   e->kv_slot_elems = static_cast<size_t>(d.layers) * d.kv_heads * 2 * d.context * hb::kHeadDim;
+  if (paged) {
+    // every slot can reach the full context with private pages
+    e->pages_per_slot = d.context / hb::kPagePositions;
+    e->n_pages = d.max_slots * e->pages_per_slot;
+    e->page_bytes = static_cast<size_t>(d.layers) * d.kv_heads * 2 * hb::kPagePositions * hb::kHeadDim * 2;
+    e->page_table.assign(static_cast<size_t>(d.max_slots) * e->pages_per_slot, -1);
+    e->page_refs.assign(e->n_pages, 0);
+    for (int pg = e->n_pages - 1; pg >= 0; --pg) e->free_pages.push_back(pg);
+    e->table_dirty = true;
+    if ((rc = dev_alloc(e, &e->d_page_table, e->page_table.size())) ||
+        (rc = dev_alloc(e, &e->d_att_part, static_cast<size_t>(e->G) * hb::kPartStride)) ||
+        (rc = dev_alloc(e, &e->d_att_cnt, static_cast<size_t>(kMaxBatch) * d.q_heads)))
+      return bail(rc);
+  }
   e->ll_words = hb::ll_layer_words(d.hidden, d.intermediate, qkv) * d.layers;
   const size_t half = static_cast<size_t>(d.head_dim / 2) * d.context;
   if ((rc = dev_alloc(e, &e->d_blob, d.blob_bytes)) || (rc = dev_alloc(e, &e->d_layers, d.layers)) ||
@@ -500,6 +606,9 @@ int hb_create(const hb_model_desc *desc, int device, hb_engine **out) {
   const unsigned int first_epoch = 1;
   if (cudaMemcpy(e->d_epoch, &first_epoch, sizeof(first_epoch), cudaMemcpyHostToDevice) != cudaSuccess)
     return bail(fail(nullptr, HB_ERR_CUDA, "epoch upload failed"));
+  if ((rc = upload_pages(e))) return bail(rc);
+  if (cudaStreamSynchronize(e->stream) != cudaSuccess)
+    return bail(fail(nullptr, HB_ERR_CUDA, "page table upload failed"));
   *out = e;
   return HB_OK;
 }
@@ -524,7 +633,7 @@ int hb_destroy(hb_engine *e) {
   for (auto ev : e->ev_b) cudaEventDestroy(ev);
   void *dev[] = {e->d_blob, e->d_layers, e->d_rope_cos, e->d_rope_sin, e->d_kv, e->d_ll, e->d_epoch,
                  e->d_logits, e->d_part_val, e->d_part_idx, e->d_result, e->d_st, e->d_prompt,
-                 e->d_gen, e->d_trace};
+                 e->d_gen, e->d_trace, e->d_page_table, e->d_att_part, e->d_att_cnt};
   for (void *p : dev)
     if (p) cudaFree(p);
   void *host[] = {e->h_st, e->h_result, e->h_prompt, e->h_gen};
@@ -542,6 +651,7 @@ int hb_step(hb_engine *e, int slot, int token_id, int position, int flags, float
   int rc = check_engine(e);
   if (rc) return rc;
   if ((rc = check_row(e, slot, token_id, position))) return rc;
+  if ((rc = pages_for_step(e, slot, position, position)) || (rc = upload_pages(e))) return rc;
   if (logits_out) flags |= HB_STEP_LOGITS;
   if (flags & (HB_STEP_LOGITS | HB_STEP_DEVICE_LOGITS)) flags |= HB_STEP_ARGMAX;
   const int device_logits = (logits_out || (flags & HB_STEP_DEVICE_LOGITS)) ? 1 : 0;
@@ -595,6 +705,9 @@ int hb_step_batch(hb_engine *e, int n, const int32_t *slots, const int32_t *toke
     for (int j = 0; j < i; ++j)
       if (slots[j] == slots[i]) return fail(e, HB_ERR_INVALID_ARG, "slot %d appears twice in one batch", slots[i]);
   }
+  for (int i = 0; i < n; ++i)
+    if ((rc = pages_for_step(e, slots[i], positions[i], positions[i]))) return rc;
+  if ((rc = upload_pages(e))) return rc;
   if (logits_out) flags |= HB_STEP_LOGITS;
   if (flags & (HB_STEP_LOGITS | HB_STEP_DEVICE_LOGITS)) flags |= HB_STEP_ARGMAX;
   const int device_logits = (logits_out || (flags & HB_STEP_DEVICE_LOGITS)) ? 1 : 0;
@@ -621,7 +734,19 @@ int hb_reset(hb_engine *e, int slot) {
   if (!e) return fail(nullptr, HB_ERR_INVALID_ARG, "engine is NULL");
   if (slot < 0 || slot >= e->desc.max_slots) return fail(e, HB_ERR_INVALID_ARG, "slot %d out of range", slot);
   HB_ON_DEVICE(e);
-  HB_CUDA(e, cudaMemsetAsync(e->d_kv + e->kv_slot_elems * slot, 0, e->kv_slot_elems * 2, e->stream));
+  if (e->paged) {
+    // the slot's pages go back to the pool; its next steps map zeroed pages
+    int *row = e->page_table.data() + static_cast<size_t>(slot) * e->pages_per_slot;
+    for (int i = 0; i < e->pages_per_slot; ++i) {
+      if (row[i] >= 0) e->table_dirty = true;
+      page_release(e, row[i]);
+      row[i] = -1;
+    }
+    int rc = upload_pages(e);
+    if (rc) return rc;
+  } else {
+    HB_CUDA(e, cudaMemsetAsync(e->d_kv + e->kv_slot_elems * slot, 0, e->kv_slot_elems * 2, e->stream));
+  }
   HB_CUDA(e, cudaStreamSynchronize(e->stream));
   return HB_OK;
 }
@@ -634,6 +759,36 @@ int hb_copy_prefix(hb_engine *e, int src, int dst, int n_positions) {
   if (n_positions < 0 || n_positions > d.context) return fail(e, HB_ERR_INVALID_ARG, "n_positions out of range");
   if (src == dst || n_positions == 0) return HB_OK;
   HB_ON_DEVICE(e);
+  if (e->paged) {
+    // whole pages below n_positions are shared (copied on their next
+    // write); the rows [0, n % 64) of a partial page are copied
+    int *srow = e->page_table.data() + static_cast<size_t>(src) * e->pages_per_slot;
+    int *drow = e->page_table.data() + static_cast<size_t>(dst) * e->pages_per_slot;
+    const int full = n_positions / hb::kPagePositions, rem = n_positions % hb::kPagePositions;
+    for (int i = 0; i < full; ++i) {
+      if (drow[i] == srow[i]) continue;
+      if (srow[i] >= 0) ++e->page_refs[srow[i]];
+      page_release(e, drow[i]);
+      drow[i] = srow[i];
+      e->table_dirty = true;
+    }
+    if (rem) {
+      int rc = pages_for_step(e, dst, full * hb::kPagePositions, full * hb::kPagePositions);
+      if (rc) return rc;
+      const size_t height = static_cast<size_t>(d.layers) * d.kv_heads * 2;
+      const size_t pitch = static_cast<size_t>(hb::kPagePositions) * 128;
+      uint8_t *to = page_ptr(e, drow[full]);
+      if (srow[full] >= 0)
+        HB_CUDA(e, cudaMemcpy2DAsync(to, pitch, page_ptr(e, srow[full]), pitch, static_cast<size_t>(rem) * 128,
+                                     height, cudaMemcpyDeviceToDevice, e->stream));
+      else
+        HB_CUDA(e, cudaMemset2DAsync(to, pitch, 0, static_cast<size_t>(rem) * 128, height, e->stream));
+    }
+    int rc = upload_pages(e);
+    if (rc) return rc;
+    HB_CUDA(e, cudaStreamSynchronize(e->stream));
+    return HB_OK;
+  }
   // every K and V block is [context][64] with 128-byte position rows: copy
   // the first n rows of each block
   const size_t pitch = static_cast<size_t>(d.context) * hb::kHeadDim * 2;
@@ -666,7 +821,23 @@ int hb_debug_dump(hb_engine *e, int what, void *out, size_t bytes) {
     if (slot < 0 || slot >= d.max_slots) return fail(e, HB_ERR_INVALID_ARG, "slot out of range");
     const size_t need = e->kv_slot_elems * 2;
     if (bytes < need) return fail(e, HB_ERR_INVALID_ARG, "need %zu bytes", need);
-    HB_CUDA(e, cudaMemcpyAsync(out, e->d_kv + e->kv_slot_elems * slot, need, cudaMemcpyDeviceToHost, e->stream));
+    if (e->paged) {
+      // gather the slot's pages into the [context][64] layout of each block
+      const size_t blocks = static_cast<size_t>(d.layers) * d.kv_heads * 2;
+      const size_t pitch = static_cast<size_t>(hb::kPagePositions) * 128, dpitch = static_cast<size_t>(d.context) * 128;
+      uint8_t *o = static_cast<uint8_t *>(out);
+      const int *row = e->page_table.data() + static_cast<size_t>(slot) * e->pages_per_slot;
+      for (int i = 0; i < e->pages_per_slot; ++i) {
+        if (row[i] >= 0) {
+          HB_CUDA(e, cudaMemcpy2DAsync(o + i * pitch, dpitch, page_ptr(e, row[i]), pitch, pitch, blocks,
+                                       cudaMemcpyDeviceToHost, e->stream));
+        } else {
+          for (size_t b = 0; b < blocks; ++b) std::memset(o + b * dpitch + i * pitch, 0, pitch);
+        }
+      }
+    } else {
+      HB_CUDA(e, cudaMemcpyAsync(out, e->d_kv + e->kv_slot_elems * slot, need, cudaMemcpyDeviceToHost, e->stream));
+    }
   } else if (what == 2) {
     // phase trace: [G][4L+2] globaltimer stamps of the last traced launch
     const size_t need = static_cast<size_t>(e->G) * (4 * d.layers + 2) * 8 * 8;

@@ -7,6 +7,12 @@ boundary: the embedding gather, the RoPE tables and the K/V append happen on
 the GPU, so ``step`` takes the token id instead of an embedding row; the LM
 head and the argmax run on the GPU for both model families; the KV cache has
 ``max_slots`` independent slots (streams).
+
+``context`` (default: the reference's 64 positions) may also be a multiple of
+64 up to 4096: the cache is then paged (64-position pages, a page table per
+slot; ``copy_prefix`` shares whole pages and copies a page only when a slot
+writes into a shared one) and the attention splits long histories over
+several SMs.  The reference has no counterpart: its cache is fixed at 64.
 """
 
 import ctypes
@@ -34,22 +40,30 @@ def rope_tables(theta, head_dim, context):
     return cos, sin
 
 
+MAX_CONTEXT = 4096  # longest paged context (64-position pages)
+
+
 class B200DecoderEngine:
     """All decoder layers + final norm + LM head + argmax of one position per
     call, on one GPU."""
 
-    def __init__(self, model, weights="bf16", device=0, max_slots=1, max_batch=1, blob=None):
+    def __init__(self, model, weights="bf16", device=0, max_slots=1, max_batch=1, blob=None, context=None):
         self._lib = hb_lib.load()
         self._handle = None
         meta = model.metadata
         self.shape = shape_from_metadata(meta)
         layout.check_dims(self.shape, weights)
-        if self.shape.context != 64:
-            raise ValueError("the engine keeps the reference's 64-token context")
+        if context is None:
+            if self.shape.context != 64:
+                raise ValueError("the engine keeps the reference's 64-token context")
+            context = 64
+        context = int(context)
+        if context != 64 and (context % 64 or not 64 < context <= MAX_CONTEXT):
+            raise ValueError(f"context must be 64 or a multiple of 64 up to {MAX_CONTEXT}")
         self.weights = weights
         self.layers = self.shape.layers
         self.vocab = self.shape.vocab
-        self.context = self.shape.context
+        self.context = context
         self.max_slots = int(max_slots)
         self.max_batch = int(max_batch)
         if blob is None:

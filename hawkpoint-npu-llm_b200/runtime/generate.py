@@ -53,7 +53,7 @@ except ImportError:
     SmolLMTokenizer = None
     from runtime.host_shims import StreamDetokenizer
 
-CONTEXT = 64
+CONTEXT = 64  # the reference's fixed cache (npu_llm/runtime/generate.py:43-44)
 
 
 def _load_tokenizer(model_dir, family):
@@ -73,8 +73,12 @@ class NPUDecoder:
     """Greedy / sampled generation over the B200 decoder engine."""
 
     def __init__(self, model_dir, context_length=64, npu_layers=None):
-        if context_length != CONTEXT:
-            raise ValueError("the decoder engine keeps a fixed 64-token cache")
+        # 64 is the reference's cache; a multiple of 64 up to 4096 selects
+        # the paged cache of the B200 engine (no reference counterpart)
+        from runtime.b200_engine import MAX_CONTEXT
+
+        if context_length != CONTEXT and (context_length % 64 or not CONTEXT < context_length <= MAX_CONTEXT):
+            raise ValueError(f"context_length must be 64 or a multiple of 64 up to {MAX_CONTEXT}")
         self._closed = False
         self._engine = None
         self.model = open_model(model_dir)
@@ -106,7 +110,8 @@ class NPUDecoder:
         from runtime.b200_engine import B200DecoderEngine
 
         # max_batch 8: prompts are prefilled up to 8 positions per launch
-        self._engine = B200DecoderEngine(self.model, weights=weights, device=device, max_batch=8)
+        self._engine = B200DecoderEngine(self.model, weights=weights, device=device, max_batch=8,
+                                         context=int(context_length))
         self.weights = weights
         self._qwen_embedding_cache = OrderedDict()  # kept for attribute compatibility
 
@@ -147,7 +152,7 @@ class NPUDecoder:
         ``(None, elapsed)``.
         """
         if not 0 <= position < self.context_length:
-            raise ValueError("position outside the 64-token context")
+            raise ValueError(f"position outside the {self.context_length}-token context")
         # This step overwrites the cache at `position`: later positions were
         # computed from another history and are no longer reusable.
         del self._cached_prefix[position:]
@@ -216,7 +221,7 @@ class NPUDecoder:
         from runtime.device_sampler import draws_uniform
 
         if not 0 <= position < self.context_length:
-            raise ValueError("position outside the 64-token context")
+            raise ValueError(f"position outside the {self.context_length}-token context")
         del self._cached_prefix[position:]
         if self._engine is None:
             raise RuntimeError("decoder is closed")
@@ -311,7 +316,7 @@ class NPUDecoder:
 
     def generate_messages(self, messages, max_new_tokens=16, sampling=None, *, stop=None, logprobs=None):
         """Chat completion over an OpenAI-style message list, windowed to the
-        64-token context at turn boundaries; yields ``(text, None[, entries])``
+        context at turn boundaries; yields ``(text, None[, entries])``
         chunks then ``("", stats[, []])``."""
         sampler, stop_matcher, top_logprobs = self._prepare(max_new_tokens, sampling, stop, logprobs)
         prompt_ids, truncation = self.tokenizer.encode_chat_window(
@@ -472,7 +477,7 @@ class NPUDecoder:
             raise ValueError(f"max_new_tokens must be between 1 and {self.context_length - 1}")
         prompt_ids = [int(t) for t in prompt_ids]
         if not prompt_ids or len(prompt_ids) + max_new_tokens > self.context_length:
-            raise ValueError("prompt + generated tokens must fit the 64-token context")
+            raise ValueError(f"prompt + generated tokens must fit the {self.context_length}-token context")
         reused = self._reusable_prefix(prompt_ids)
         start = time.perf_counter()
         ids = self._engine.generate(prompt_ids, max_new_tokens, start=reused)

@@ -85,3 +85,31 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(hb_lib, "LIB_PATH", tmp_path / "nope.so")
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         hb_lib.load()
+
+
+def test_context_rules_are_checked_on_the_host(lib):
+    """Contexts above 64 positions must be whole 64-position pages, at most
+    4096; the check runs before any device is touched."""
+    import numpy as np
+    from runtime import hb_lib, layout, synthetic
+    from runtime.b200_engine import B200DecoderEngine
+    shape = synthetic.TINY_QWEN
+    lay = layout.plan(shape)
+    table = lay.layer_table()
+    for context in (100, 8192, 4160):
+        cos = np.zeros((context, 32), np.float32)
+        desc = hb_lib.HbModelDesc(
+            abi_version=hb_lib.ABI_VERSION, family=1, hidden=shape.hidden, intermediate=shape.intermediate,
+            q_heads=shape.q_heads, kv_heads=shape.kv_heads, head_dim=64, layers=shape.layers, vocab=shape.vocab,
+            context=context, has_qkv_bias=1, weight_format=0, max_slots=1, max_batch=1, rms_eps=1e-6,
+            blob_bytes=lay.total, gamma_final=lay.gamma_final, w_lm=lay.w_lm, s_lm=0, embedding=lay.embedding)
+        desc.layer_offsets = table
+        desc.rope_cos = cos.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        desc.rope_sin = cos.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        handle = ctypes.c_void_p()
+        assert lib.hb_create(ctypes.byref(desc), 0, ctypes.byref(handle)) == hb_lib.HB_ERR_UNSUPPORTED
+        assert b"multiple of 64" in lib.hb_library_error()
+    model = synthetic.build("tiny-qwen", seed=1)
+    for context in (100, 32, 8192):
+        with pytest.raises(ValueError, match="multiple of 64"):
+            B200DecoderEngine(model, context=context)
