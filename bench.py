@@ -183,6 +183,43 @@ def prefill_launches(n_prompt, batch=8):
     return -(-(n_prompt - 1) // batch)
 
 
+def run_long_context(device, peak, context=4096, n_new=16):
+    """Greedy decode of the Qwen shape (BF16) with the paged cache of a
+    4096-position context, at several prompt depths: per depth the median
+    decode launch and its HBM bytes (the streamed weights plus the K/V
+    history every layer reads at the mean decode position)."""
+    import numpy as np
+    from runtime import layout, synthetic
+    from runtime.b200_engine import B200DecoderEngine
+
+    model = synthetic.build("qwen2.5-0.5b", seed=MODEL_SEED).materialize()
+    shape = model.shape
+    eng = B200DecoderEngine(model, device=device, max_batch=8, context=context)
+    rows = []
+    try:
+        ids_all = synthetic.prompt_ids(shape.vocab, context - 64, seed=MODEL_SEED + 3)
+        for depth in (256, 1024, 2048, context - 64):
+            ids = ids_all[:depth]
+            first = eng.generate(ids, n_new)
+            eng.profile(True)
+            eng.profile_read()
+            for _ in range(2):
+                assert eng.generate(ids, n_new) == first
+            n_pre = prefill_launches(depth)
+            ms = eng.profile_read().reshape(2, n_pre + n_new)
+            eng.profile(False)
+            dec = float(np.median(ms[:, n_pre + 1:]))
+            lay = layout.plan(shape, "bf16")
+            streamed = lay.total - shape.vocab * shape.hidden * 2
+            kv = shape.layers * shape.kv_heads * 2 * (depth + n_new // 2) * shape.head_dim * 2
+            rows.append({"depth": depth, "decode_launch_ms": dec, "decode_tokens_per_second": 1000.0 / dec,
+                         "kv_bytes_per_token": int(kv),
+                         "hbm_frac": (streamed + kv) / (dec / 1000.0) / 1e9 / peak})
+    finally:
+        eng.close()
+    return {"context": context, "new_tokens": n_new, "depths": rows}
+
+
 def run_other_configs(device, peak):
     """BASELINE configs 1, 2 and 4 on this GPU (single-GPU runs only): decode
     of the SmolLM2-135M shape (BF16) and of the Qwen shape in W8, and the
@@ -218,6 +255,7 @@ def run_other_configs(device, peak):
                     "ttft_ms": float(ms[:, :n_pre + 1].sum(axis=1).mean()),
                     "weight_bytes_per_token": int(streamed),
                     "hbm_frac": streamed / (dec / 1000.0) / 1e9 / peak}
+    out["long_context_qwen_bf16"] = run_long_context(device, peak)
     # config 2: y = W x (BF16 out) and the LM head with a fused argmax;
     # rotating weight copies keep every launch's weights out of L2
     lib = hb_lib.load()

@@ -426,13 +426,26 @@ int run_chained(hb_engine *e, int slot, const int32_t *ids, int n_prompt, int st
   const int body = 4 * d.layers;
   const int full = 4 * d.layers + 1;
   int upload = 0;
+  // the next pinned staging buffer; when all are taken, wait until the
+  // queued copies have read them (long prompts need more launches than the
+  // ring holds)
+  auto next_state = [&](hb::StepState **out) -> int {
+    if (upload == kStateRing) {
+      HB_CUDA(e, cudaStreamSynchronize(e->stream));
+      upload = 0;
+    }
+    *out = &e->h_st[upload++];
+    return HB_OK;
+  };
   int first = start;  // first position the chained (device-advanced) steps run
   if (d.max_batch > 1) {
     // batched prefill: up to kMaxBatch consecutive positions per launch, all
     // but the last prompt position (which the chained steps run with the head)
     for (int p0 = start; p0 < n_prompt - 1; p0 += kMaxBatch) {
       const int k = std::min(kMaxBatch, n_prompt - 1 - p0);
-      hb::StepState &sb = e->h_st[upload++];
+      hb::StepState *sbp = nullptr;
+      if ((prc = next_state(&sbp))) return prc;
+      hb::StepState &sb = *sbp;
       std::memset(&sb, 0, sizeof(sb));
       for (int i = 0; i < k; ++i) {
         sb.token[i] = ids[p0 + i];
@@ -446,7 +459,9 @@ int run_chained(hb_engine *e, int slot, const int32_t *ids, int n_prompt, int st
     }
     first = n_prompt - 1;
   }
-  hb::StepState &st = e->h_st[upload++];
+  hb::StepState *stp = nullptr;
+  if ((prc = next_state(&stp))) return prc;
+  hb::StepState &st = *stp;
   std::memset(&st, 0, sizeof(st));
   st.token[0] = ids[first];
   st.pos[0] = first;
