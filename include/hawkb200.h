@@ -68,6 +68,13 @@ typedef struct hb_layer_offsets {
   uint64_t w_down, s_down;
 } hb_layer_offsets;
 
+/* context: cache positions per slot.  <= 64 matches the reference's fixed
+ * cache (npu_llm/runtime/generate.py:43-44).  A multiple of 64 up to 4096
+ * (no reference counterpart) selects the paged cache: 64-position pages
+ * behind a per-slot page table, pages zero-filled when first mapped,
+ * hb_copy_prefix sharing whole pages that a slot copies only when it
+ * writes into one, and the attention of long histories split over several
+ * SMs.  Other values are HB_ERR_UNSUPPORTED. */
 typedef struct hb_model_desc {
   int32_t abi_version;      /* HB_ABI_VERSION */
   int32_t family;           /* HB_FAMILY_* */
@@ -136,13 +143,19 @@ int hb_step_batch(hb_engine *engine, int n, const int32_t *slots,
 
 /* KV-cache management.  hb_reset replaces QwenDecoderEngine.reset
  * (npu_llm/runtime/qwen_engine.py:65-66); hb_copy_prefix copies positions
- * [0, n_positions) of every layer from one slot to another (prefix sharing). */
+ * [0, n_positions) of every layer from one slot to another (prefix sharing).
+ * With a paged cache (context > 64) hb_reset returns the slot's pages to the
+ * pool, and hb_copy_prefix maps the source's whole pages below n_positions
+ * into the destination (a page is copied when either slot next writes into
+ * it) and copies the rows of a partial last page; the results are the same
+ * as copying. */
 int hb_reset(hb_engine *engine, int slot);
 int hb_copy_prefix(hb_engine *engine, int src_slot, int dst_slot, int n_positions);
 
 /* Diagnostics.  hb_debug_dump copies engine state for parity tests:
  * HB_DUMP_HIDDEN = BF16 residual stream [8 x hidden] after the last step;
- * HB_DUMP_KV = BF16 cache of one slot, per (layer, kv head) K then V, each
+ * HB_DUMP_KV = BF16 cache of one slot (paged: gathered from its pages, zeros
+ * where none is mapped), per (layer, kv head) K then V, each
  * [context][head_dim] with the eight 16-byte blocks of a position stored at
  * block ^ (position & 7) (slot taken from *(int*)out on entry); HB_DUMP_TRACE = uint64 [SMs][4*layers+2][8] device timestamps of
  * the last launch traced with hb_profile(engine, 2). */
