@@ -170,3 +170,31 @@ def test_full_size_split_attention_is_consistent():
         short.close()
     d = np.abs(a - b)
     assert d.max() <= ATOL_FULL and np.linalg.norm(a - b) / np.linalg.norm(b) <= RTOL_FULL
+
+
+def test_drop_in_decoder_with_a_longer_context():
+    """NPUDecoder(model, context_length=256): a 150-id prompt and 40 new
+    tokens through the drop-in give the engine's own greedy tokens, and the
+    repeated prompt reuses 149 cached positions."""
+    from runtime.generate import NPUDecoder
+    from test_decode_loop import FakeTokenizer, run
+
+    model = synthetic.build("tiny-qwen", seed=42)
+    prompt = synthetic.prompt_ids(model.shape.vocab, 150, seed=17)
+    decoder = NPUDecoder(model, context_length=256)
+    try:
+        assert decoder._engine.context == 256
+        decoder.tokenizer = FakeTokenizer(prompt)
+        decoder.tokenizer.eos_id = -1
+        _, stats = run(decoder, max_new_tokens=40)
+        _, again = run(decoder, max_new_tokens=40)
+    finally:
+        decoder.close()
+    engine = B200DecoderEngine(model, max_batch=8, context=256)
+    try:
+        ref = engine.generate(prompt, 40)
+    finally:
+        engine.close()
+    assert stats["generated_token_ids"] == ref
+    assert again["generated_token_ids"] == ref
+    assert again["cached_prompt_tokens"] == len(prompt) - 1
