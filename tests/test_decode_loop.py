@@ -176,6 +176,11 @@ def test_invalid_arguments():
         run(decoder, max_new_tokens=64)
     with pytest.raises(ValueError):
         NPUDecoder(object(), context_length=32)
+    # longer contexts: whole 64-position pages, at most 4096 (checked before
+    # any model or device is touched)
+    for context in (100, 4160, 8192):
+        with pytest.raises(ValueError, match="multiple of 64"):
+            NPUDecoder(object(), context_length=context)
 
 
 @pytest.mark.gpu
