@@ -109,6 +109,26 @@ def test_continuous_batching_matches_single_streams():
     assert eng.copies[0][2] == 16
 
 
+def test_continuous_batching_with_a_longer_context():
+    """Prompts of 60 to 300 positions plus 40 new tokens in a 512-position
+    context (the paged engine's range), a third of them opening with the
+    same 128 ids (two whole 64-position pages, which a paged engine shares
+    instead of copying): the same tokens as single streams, the prefix
+    computed once and reused."""
+    rng = np.random.default_rng(5)
+    shared = rng.integers(0, 1000, 128).tolist()
+    reqs = []
+    for i in range(24):
+        ids = rng.integers(0, 1000, int(rng.integers(60, 301))).tolist()
+        reqs.append(Request(prompt=shared + ids if i % 3 == 0 else ids, new_tokens=40, rid=i))
+    eng = FakeEngine(max_slots=12, context=512)
+    MultiStreamServer(eng, max_batch=8, prefix_tokens=128, prefix_slots=4).run(reqs)
+    for r in reqs:
+        assert r.tokens == reference_tokens(r.prompt, r.new_tokens, context=512), r.rid
+    reused = [r for r in reqs if r.reused_prefix]
+    assert len(reused) >= 3 and all(r.reused_prefix == 128 for r in reused)
+
+
 def _sampled_requests(vocab, seed=0):
     from oracle import sampling as osamp
 
