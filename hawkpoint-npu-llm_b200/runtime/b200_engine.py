@@ -8,8 +8,8 @@ the GPU, so ``step`` takes the token id instead of an embedding row; the LM
 head and the argmax run on the GPU for both model families; the KV cache has
 ``max_slots`` independent slots (streams).
 
-``context`` (default: the reference's 64 positions) may also be a multiple of
-64 up to 4096: the cache is then paged (64-position pages, a page table per
+``context`` (default: the model metadata's ``context_length``, 64 -- the
+reference's -- when it has none) may also be a multiple of 64 up to 4096: the cache is then paged (64-position pages, a page table per
 slot; ``copy_prefix`` shares whole pages and copies a page only when a slot
 writes into a shared one) and the attention splits long histories over
 several SMs.  The reference has no counterpart: its cache is fixed at 64.
@@ -53,13 +53,10 @@ class B200DecoderEngine:
         meta = model.metadata
         self.shape = shape_from_metadata(meta)
         layout.check_dims(self.shape, weights)
-        if context is None:
-            if self.shape.context != 64:
-                raise ValueError("the engine keeps the reference's 64-token context")
-            context = 64
-        context = int(context)
+        # the model metadata's context_length unless the caller names one
+        context = int(self.shape.context if context is None else context)
         if context != 64 and (context % 64 or not 64 < context <= MAX_CONTEXT):
-            raise ValueError(f"context must be 64 or a multiple of 64 up to {MAX_CONTEXT}")
+            raise ValueError(f"context {context}: must be 64 or a multiple of 64 up to {MAX_CONTEXT}")
         self.weights = weights
         self.layers = self.shape.layers
         self.vocab = self.shape.vocab
