@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Benchmark of the B200 decoder engine on BASELINE config 3 (the metric's config):
+"""Benchmark of the B200 decoder engine on the Qwen2.5-0.5B decode workload (config 3, the metric's):
 
     Qwen2.5-0.5B-shaped BF16 decoder, random-init N(0, 0.02) weights (seed 0),
     a 40-id seeded prompt windowed to the 32 positions that leave room for 32
@@ -115,22 +115,14 @@ def sum_over_ranks(value, world):
 
 
 def config5_requests(vocab, n=512, new_tokens=16, seed=MODEL_SEED + 5):
-    """8 x 64 independent requests, prompt lengths U[8, 48],
+    """Config 5: 8 x 64 independent requests, prompt lengths U[8, 48],
     every fourth request opening with one shared 16-token prefix, 16 greedy
     tokens each (seeded ids stand in for real prompts)."""
-    import numpy as np
+    from runtime import synthetic
     from runtime.serving import Request
 
-    rng = np.random.default_rng(seed)
-    shared = rng.integers(0, vocab, 16).tolist()
-    reqs = []
-    for i in range(n):
-        length = int(rng.integers(8, 49))
-        ids = rng.integers(0, vocab, length).tolist()
-        if i % 4 == 0:
-            ids = shared + ids[: max(1, length - 16)]
-        reqs.append(Request(prompt=ids, new_tokens=new_tokens, rid=i))
-    return reqs
+    return [Request(prompt=ids, new_tokens=new_tokens, rid=i)
+            for i, ids in enumerate(synthetic.ragged_prompts(vocab, n, seed))]
 
 
 def run_multistream(model, blob, device, rank, world):
@@ -221,7 +213,7 @@ def run_long_context(device, peak, context=4096, n_new=16):
 
 
 def run_other_configs(device, peak):
-    """BASELINE configs 1, 2 and 4 on this GPU (single-GPU runs only): decode
+    """Configs 1, 2 and 4 on this GPU (single-GPU runs only): decode
     of the SmolLM2-135M shape (BF16) and of the Qwen shape in W8, and the
     standalone GEMV shapes with HBM GB/s against the roofline."""
     import ctypes
@@ -246,6 +238,7 @@ def run_other_configs(device, peak):
             n_pre = prefill_launches(n_prompt)
             ms = eng.profile_read().reshape(3, n_pre + n_new)
             eng.profile(False)
+            parity = golden_parity(eng, name, weights)
         finally:
             eng.close()
         lay = layout.plan(model.shape, weights)
@@ -254,7 +247,7 @@ def run_other_configs(device, peak):
         out[key] = {"decode_tokens_per_second": 1000.0 / dec, "decode_launch_ms": dec,
                     "ttft_ms": float(ms[:, :n_pre + 1].sum(axis=1).mean()),
                     "weight_bytes_per_token": int(streamed),
-                    "hbm_frac": streamed / (dec / 1000.0) / 1e9 / peak}
+                    "hbm_frac": streamed / (dec / 1000.0) / 1e9 / peak, "parity": parity}
     out["long_context_qwen_bf16"] = run_long_context(device, peak)
     # config 2: y = W x (BF16 out) and the LM head with a fused argmax;
     # rotating weight copies keep every launch's weights out of L2
@@ -322,6 +315,33 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
+def golden_parity(engine, name, weights):
+    """Teacher-forced logits of `engine` at every position of the committed
+    reference request (tests/golden/request_<name>_<weights>.npz, written by
+    the reference CPU runtime): max |d| and ||d|| / ||ref|| over the
+    reference's top-32 entries and a strided sample, worst position; argmax
+    agreement count."""
+    import numpy as np
+
+    path = REPO / "tests" / "golden" / f"request_{name}_{weights}.npz"
+    if not path.exists():
+        return None
+    g = np.load(path)
+    stride = int(g["sample_stride"])
+    worst_abs, worst_rel, agree = 0.0, 0.0, 0
+    for p, t in enumerate(g["ids"]):
+        got = engine.step(int(t), p, logits=True)
+        sample = got[::stride]
+        ref = g["sample_logits"][p]
+        err = max(float(np.abs(got[g["top_ids"][p]] - g["top_logits"][p]).max()), float(np.abs(sample - ref).max()))
+        worst_abs = max(worst_abs, err)
+        worst_rel = max(worst_rel, float(np.linalg.norm(sample - ref) / np.linalg.norm(ref)))
+        agree += int(int(np.argmax(got)) == int(g["argmax"][p]))
+    engine.reset()
+    return {"positions": int(len(g["ids"])), "max_abs": worst_abs, "rel": worst_rel, "argmax_equal": agree,
+            "reference": str(g["source"]), "tolerance": {"max_abs": 0.1, "rel": 3e-2}}
+
+
 def profiled_traffic():
     """DRAM bytes per decode launch from the committed ncu summary, if any."""
     path = REPO / "profiles" / "decoder_kernel_qwen25_decode.md"
@@ -384,74 +404,111 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU oracle --
-def oracle_sample(model, prompt, prefill_positions, decode_steps):
-    """Decode tok/s of the CPU oracle over a bounded sample of the request:
-    the last `prefill_positions` prompt positions (logits at the last), then
-    `decode_steps` greedy steps.  Returns (tokens/s, seconds, sample text)."""
-    import numpy as np
-    from oracle.cpu_decoder import OracleDecoder, argmax_first
-
-    oracle = OracleDecoder(model)
-    start_pos = len(prompt) - prefill_positions
-    for p in range(start_pos):  # cache fill outside the sample (positions only)
+def cpu_host():
+    """What the CPU arm runs on: logical CPUs, model name, the BLAS library
+    NumPy calls and its thread pool size."""
+    info = {"nproc": os.cpu_count() or 1, "cpu_model": None, "blas": None, "blas_threads": None}
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                info["cpu_model"] = line.split(":", 1)[1].strip()
+                break
+    except OSError:
         pass
-    t0 = time.perf_counter()
-    token = None
-    for i, p in enumerate(range(start_pos, len(prompt))):
-        out = oracle.step(prompt[p], p, compute_logits=(p == len(prompt) - 1))
-        if out is not None:
-            token = argmax_first(out)
-    t_prefill = time.perf_counter() - t0
-    t1 = time.perf_counter()
-    pos = len(prompt)
-    for _ in range(decode_steps):
-        token = argmax_first(oracle.step(token, pos))
-        pos += 1
-    t_decode = time.perf_counter() - t1
-    sample = (f"{prefill_positions} prefill positions + {decode_steps} greedy decode steps of the "
-              f"config-3 request (positions {start_pos}..{pos - 1})")
-    return decode_steps / t_decode, t_prefill + t_decode, sample
-
-
-def threads_used():
     try:
         from threadpoolctl import threadpool_info
-        counts = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
-        if counts:
-            return max(counts)
+        for pool in threadpool_info():
+            if pool.get("user_api") == "blas":
+                info["blas"] = f"{pool.get('internal_api')} {pool.get('version')}"
+                info["blas_threads"] = pool.get("num_threads")
+                break
     except Exception:
         pass
-    return os.cpu_count() or 1
+    return info
+
+
+class OracleRequest:
+    """The config-3 request on the CPU oracle (the NumPy port of the
+    reference's BF16 CPU runtime): the prompt's positions fill the KV cache
+    once, untimed; each sample then times `decode_steps` greedy steps from
+    the first generated position (rewriting the same positions every time,
+    so each sample sees the same cache as the request)."""
+
+    def __init__(self, model, prompt):
+        from oracle.cpu_decoder import OracleDecoder, argmax_first
+
+        self.oracle = OracleDecoder(model)
+        self.argmax = argmax_first
+        self.prompt = list(prompt)
+        last = None
+        for p, t in enumerate(self.prompt):
+            last = self.oracle.step(t, p, compute_logits=(p == len(self.prompt) - 1))
+        self.first = self.argmax(last)
+
+    def sample(self, decode_steps):
+        """Decode tokens/s over `decode_steps` greedy steps, and the seconds."""
+        token, pos = self.first, len(self.prompt)
+        t0 = time.perf_counter()
+        for _ in range(decode_steps):
+            token = self.argmax(self.oracle.step(token, pos))
+            pos += 1
+        seconds = time.perf_counter() - t0
+        return decode_steps / seconds, seconds
+
+    def describe(self, decode_steps):
+        n = len(self.prompt)
+        return (f"{decode_steps} greedy decode steps of the config-3 request (positions {n}..{n + decode_steps - 1}) "
+                f"after an untimed fill of its {n} prompt positions")
+
+
+def pinned_blas(threads):
+    """Context manager pinning NumPy's BLAS pool to `threads` (torchrun sets
+    OMP_NUM_THREADS=1 for every rank; the CPU arm uses the whole host)."""
+    from threadpoolctl import threadpool_limits
+    return threadpool_limits(limits=threads, user_api="blas")
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    import numpy as np  # noqa: F401
     from runtime import synthetic
 
     model = synthetic.build("qwen2.5-0.5b", seed=MODEL_SEED).materialize()
     prompt = workload_prompt(model.shape.vocab)
-    for _ in range(args.warmup):
-        oracle_sample(model, prompt, 1, 2)
-    rates, secs = [], []
-    sample = ""
-    for _ in range(args.steps):
-        rate, sec, sample = oracle_sample(model, prompt, 2, 4)
-        rates.append(rate)
-        secs.append(sec)
+    decode_steps = 16
+    threads = os.cpu_count() or 1
+    with pinned_blas(threads):
+        req = OracleRequest(model, prompt)
+        for _ in range(args.warmup):
+            req.sample(2)
+        rates, secs = [], []
+        for _ in range(args.steps):
+            rate, sec = req.sample(decode_steps)
+            rates.append(rate)
+            secs.append(sec)
+        host = cpu_host()
     value = statistics.median(rates)
-    cores = threads_used()
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * statistics.median(secs),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "qwen2.5-0.5b-bf16 greedy decode (BASELINE config 3), CPU runtime",
-                   "prompt_positions": len(prompt), "new_tokens": NEW_TOKENS, "batch": 1},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "config": workload_config(len(prompt), world),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": host["blas_threads"] or threads,
+                         "kind": "port", "sample": req.describe(decode_steps),
+                         "nproc": host["nproc"], "cpu_model": host["cpu_model"], "blas": host["blas"],
+                         "weights": "BF16 weights converted to FP32 once at load (the reference converts "
+                                    "them on every projection, cpu_backend.py:64-69, which is slower)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def workload_config(n_prompt, world):
+    """The `config` object both arms print."""
+    return {"workload": "qwen2.5-0.5b-bf16 greedy decode (config 3)", "prompt_positions": n_prompt,
+            "new_tokens": NEW_TOKENS, "decode_steps": NEW_TOKENS - 1, "batch": 1,
+            "parallelism": f"replicas x{world}",
+            "l2": "weights 1 GB per token > 126 MB L2, no flush needed"}
 
 
 # ---------------------------------------------------------------- B200 arm --
@@ -524,6 +581,8 @@ def run_b200(args, rank, world, local):
     engine.generate(prompt, 1, start=n_prompt - 1)
     ttft_cached_ms = 1000 * (time.perf_counter() - t0)
 
+    parity = {"config3": golden_parity(engine, "qwen2.5-0.5b", "bf16")} if rank == 0 else None
+
     # e2e through the public decode_token API (host copies + sync per call)
     engine.close()
     decoder = NPUDecoder(model)
@@ -546,8 +605,15 @@ def run_b200(args, rank, world, local):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, _, sample = oracle_sample(model, prompt, 2, 8)
-        cpu = {"value": rate, "unit": "tokens/s", "cores": threads_used(), "kind": "port", "sample": sample}
+        threads = os.cpu_count() or 1
+        with pinned_blas(threads):
+            req = OracleRequest(model, prompt)
+            req.sample(2)
+            rate, _ = req.sample(16)
+            host = cpu_host()
+        cpu = {"value": rate, "unit": "tokens/s", "cores": host["blas_threads"] or threads, "kind": "port",
+               "sample": req.describe(16), "nproc": host["nproc"], "cpu_model": host["cpu_model"],
+               "blas": host["blas"]}
 
     if rank == 0:
         step_state_bytes = 32 * 4 - 16  # StepState: 3x8 ints + 4 ints
@@ -556,22 +622,22 @@ def run_b200(args, rank, world, local):
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "qwen2.5-0.5b-bf16 greedy decode (BASELINE config 3)",
-                       "prompt_positions": n_prompt, "new_tokens": NEW_TOKENS, "decode_steps": decode_steps,
-                       "batch": 1, "parallelism": f"replicas x{world}",
-                       "l2": "weights 1 GB per token > 126 MB L2, no flush needed"},
+            "config": workload_config(n_prompt, world),
             "ttft_ms": float(np.median(prefill_ms)),
             "ttft_cached_ms": ttft_cached_ms,
             "e2e_ttft_ms": 1000 * statistics.median(e2e_ttft),
             "decode_launch_ms": launch_ms,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": profiled_traffic(),
+                         "traffic_source": "ncu dram__bytes_read+write of one decode launch, "
+                                           "profiles/decoder_kernel_qwen25_decode.md (not measured in this run)",
                          "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg_bytes},
             "e2e": {"value": e2e_value, "unit": "tokens/s",
                     # decode_token runs one launch per position
                     "h2d_bytes_per_step": (n_prompt + NEW_TOKENS - 1) * step_state_bytes,
                     "d2h_bytes_per_step": (n_prompt + NEW_TOKENS - 1) * result_bytes},
             "gpu_launches": launches_per_step * args.steps,
+            "parity": parity,
             "multistream": multistream,
             "other_configs": others,
             "clocks": clocks.summary(),

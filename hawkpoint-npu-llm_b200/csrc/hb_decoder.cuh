@@ -250,13 +250,7 @@ __device__ __forceinline__ bool ll_gather(const uint64_t *src, size_t row_words,
       }
       if (pend) {
         if (start == 0) start = globaltimer_ns();
-        if ((++spins & 31u) == 0) {
-          if (ld_volatile_int(&ctrl->abort)) return false;
-          if (globaltimer_ns() - start > limit_ns) {
-            raise_error(ctrl, kErrTimeout, kWhereGrid);
-            return false;
-          }
-        }
+        if ((++spins & 31u) == 0 && wait_expired(ctrl, start, limit_ns, kWhereGrid)) return false;
       }
     }
   }
@@ -531,13 +525,7 @@ struct DecoderCta {
         return true;
       }
       if (start == 0) start = globaltimer_ns();
-      if ((spins & 31u) == 31u) {
-        if (ld_volatile_int(&P.result->ctrl.abort)) return false;
-        if (globaltimer_ns() - start > P.limit_ns) {
-          raise_error(&P.result->ctrl, kErrTimeout, kWhereGrid);
-          return false;
-        }
-      }
+      if ((spins & 31u) == 31u && wait_expired(&P.result->ctrl, start, P.limit_ns, kWhereGrid)) return false;
     }
   }
 
@@ -587,13 +575,7 @@ struct DecoderCta {
       }
       if (pend) {
         if (start == 0) start = globaltimer_ns();
-        if ((spins & 31u) == 31u) {
-          if (ld_volatile_int(&P.result->ctrl.abort)) return false;
-          if (globaltimer_ns() - start > P.limit_ns) {
-            raise_error(&P.result->ctrl, kErrTimeout, kWhereGrid);
-            return false;
-          }
-        }
+        if ((spins & 31u) == 31u && wait_expired(&P.result->ctrl, start, P.limit_ns, kWhereGrid)) return false;
       }
     }
     return true;
@@ -988,49 +970,48 @@ struct DecoderCta {
     }
     const int um = ucta / P.QH, uh = ucta - um * P.QH, uj = uh / P.group;
     uint32_t *u96 = reinterpret_cast<uint32_t *>(att);
-    // inputs: the previous phase's LL words (the embedding row for layer 0)
     bool ok = true;
-    if (kind == 0) {
-      if (layer == 0) {
-        // the embedding row (generate.py:758-768), same word-pair ownership
-        // as the gather (the norm reads these words next without a barrier)
-        for (int m = 0; m < mrows; ++m) {
-          const uint2 *e = reinterpret_cast<const uint2 *>(P.embed + static_cast<size_t>(s_tok[m]) * P.H);
-          for (int w = tid; w < P.H / 4; w += kConsumerThreads) {
-            reinterpret_cast<uint2 *>(hx + m * P.H)[w] = __ldg(e + w);
-          }
-        }
-      } else {
-        ok = gather_to_hx(ll_hout(layer - 1, 0), P.H / 2, P.H);
-      }
-    } else if (kind == 1) {
+    if (kind == 1) {
+      // this CTA's attention unit publishes its head's outputs first
       if constexpr (PG) {
         if (ucta < mrows * P.QH) ok = gather_unit(layer, um, uh, uj, u96);
+        if (!ok) return false;
+        if (ucta < mrows * P.QH) attention_paged(layer, um, uh, uj, us, S, u96);
       } else if (has_unit()) {
         kv_prefetch_unit(layer, um, uj);  // overlaps the wait for q/k/v
         ok = gather_unit(layer, um, uh, uj, u96);
-        if (!ok) cp_async_wait_all();
-      }
-    } else if (kind == 2) {
-      ok = gather_to_hx(ll_h1(layer, 0), P.H / 2, P.H);
-    } else {
-      ok = gather_raw(ll_act(layer, 0), P.I / 2, P.I / 2, reinterpret_cast<uint32_t *>(xs), P.xs_elems / 2);
-    }
-    if (!ok) return false;
-    // act is read across threads next (the attention unit synchronizes itself)
-    if (kind == 3) consumer_sync(kConsumerThreads);
-    mark(k, 1);
-    if (kind == 0 || kind == 2) {
-      norm_rows(gamma);
-    } else if (kind == 1) {
-      if constexpr (PG) {
-        if (ucta < mrows * P.QH) attention_paged(layer, um, uh, uj, us, S, u96);
-      } else if (has_unit()) {
+        if (!ok) {
+          cp_async_wait_all();
+          return false;
+        }
         attention_unit(layer, um, uh, uj, u96);
       }
-      if (!gather_raw(ll_att(layer, 0), P.H / 2, P.H / 2, reinterpret_cast<uint32_t *>(xs), P.xs_elems / 2))
-        return false;
-      consumer_sync(kConsumerThreads);
+    }
+    // the GEMV input: the previous phase's LL words, through one gather site
+    // for every kind (its code is fetched once per layer, not four times)
+    const bool to_hx = kind == 0 || kind == 2;
+    const uint64_t *gsrc = kind == 0 ? ll_hout(layer - 1, 0) : kind == 1 ? ll_att(layer, 0)
+                         : kind == 2 ? ll_h1(layer, 0) : ll_act(layer, 0);
+    const int gwords = kind == 3 ? P.I / 2 : P.H / 2;
+    if (kind == 0 && layer == 0) {
+      // the embedding row (generate.py:758-768), same word-pair ownership
+      // as the gather (the norm reads these words next without a barrier)
+      for (int m = 0; m < mrows; ++m) {
+        const uint2 *e = reinterpret_cast<const uint2 *>(P.embed + static_cast<size_t>(s_tok[m]) * P.H);
+        for (int w = tid; w < P.H / 4; w += kConsumerThreads) {
+          reinterpret_cast<uint2 *>(hx + m * P.H)[w] = __ldg(e + w);
+        }
+      }
+    } else {
+      ok = gather_raw(gsrc, gwords, gwords, reinterpret_cast<uint32_t *>(to_hx ? hx : xs),
+                      to_hx ? P.H / 2 : P.xs_elems / 2);
+    }
+    if (!ok) return false;
+    mark(k, 1);
+    if (to_hx) {
+      norm_rows(gamma);  // each thread starts on its own words; the norm synchronizes
+    } else {
+      consumer_sync(kConsumerThreads);  // xs is read across threads next
     }
     mark(k, 6);
     if (!consume_splitk<MB, W8>(ring, r, xs, P.xs_elems, mrows, red, P.red_rows, &P.result->ctrl, P.limit_ns))

@@ -54,11 +54,24 @@ __device__ __forceinline__ int ld_volatile_int(const int *p) {
   return v;
 }
 
-__device__ __forceinline__ void raise_error(Ctrl *ctrl, int code, int where) {
+__device__ __noinline__ void raise_error(Ctrl *ctrl, int code, int where) {
   if (atomicCAS(&ctrl->err, 0, code) == 0) {
     atomicExch(&ctrl->err_where, where);
   }
   atomicExch(&ctrl->abort, 1);
+}
+
+// The slow half of every bounded wait, kept out of line so that wait sites
+// compile to a load and a compare: true when the wait must give up because
+// another CTA raised the abort flag or because `limit_ns` passed since
+// `start` (then the timeout is recorded with `where`).
+__device__ __noinline__ bool wait_expired(Ctrl *ctrl, uint64_t start, uint64_t limit_ns, int where) {
+  if (ld_volatile_int(&ctrl->abort)) return true;
+  if (globaltimer_ns() - start > limit_ns) {
+    raise_error(ctrl, kErrTimeout, where);
+    return true;
+  }
+  return false;
 }
 
 // ---------------------------------------------------------------- mbarrier --
@@ -116,19 +129,21 @@ __device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t *bar, uint32_t pa
 }
 
 // Bounded wait for the phase with `parity` to complete.  Returns false on
-// timeout or when another CTA raised the abort flag.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, Ctrl *ctrl,
-                                          uint64_t limit_ns, int where) {
-  if (mbar_try_wait(bar, parity)) return true;
+// timeout or when another CTA raised the abort flag.  The first test is
+// inline; a phase still open goes to the out-of-line loop.
+__device__ __noinline__ bool mbar_wait_slow(uint64_t *bar, uint32_t parity, Ctrl *ctrl, uint64_t limit_ns,
+                                            int where) {
   const uint64_t start = globaltimer_ns();
   while (true) {
     if (mbar_try_wait_suspend(bar, parity, 20000u)) return true;
-    if (ld_volatile_int(&ctrl->abort)) return false;
-    if (globaltimer_ns() - start > limit_ns) {
-      raise_error(ctrl, kErrTimeout, where);
-      return false;
-    }
+    if (wait_expired(ctrl, start, limit_ns, where)) return false;
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, Ctrl *ctrl,
+                                          uint64_t limit_ns, int where) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, ctrl, limit_ns, where);
 }
 
 // 16-byte asynchronous copy global -> shared (L2 only, no L1 allocation),
@@ -202,13 +217,9 @@ __device__ __forceinline__ bool grid_barrier(Ctrl *ctrl, unsigned int target, in
       const uint64_t start = globaltimer_ns();
       uint32_t spins = 0;
       while (static_cast<int>(ld_acquire_u32(&ctrl->bar) - target) < 0) {
-        if ((++spins & 15u) == 0) {
-          if (ld_volatile_int(&ctrl->abort)) { ok = 0; break; }
-          if (globaltimer_ns() - start > limit_ns) {
-            raise_error(ctrl, kErrTimeout, kWhereGrid);
-            ok = 0;
-            break;
-          }
+        if ((++spins & 15u) == 0 && wait_expired(ctrl, start, limit_ns, kWhereGrid)) {
+          ok = 0;
+          break;
         }
       }
     }

@@ -344,131 +344,69 @@ class NPUDecoder:
         )
 
     def _generate_tokens_core(self, prompt_ids, truncation, max_new_tokens, sampler, stop_matcher, top_logprobs):
-        """Prefill (one step per prompt position, logits only at the last),
-        then decode until the token budget, EOS or a stop string -- the loop of
-        npu_llm/runtime/generate.py:1050-1200."""
-        history = list(prompt_ids)         # penalties see the prompt too
-        pending = []                       # (byte offset of the token's text, logprob entry)
-        state = {"entry": None}
-        produced = 0
-        emitted = 0
-
-        def choose(logits):
-            token = int(np.argmax(logits)) if sampler.greedy else sampler.select(logits, history)
-            if top_logprobs is not None:
-                state["entry"] = self._logprob_entry(logits, token, top_logprobs)
-            return token
-
-        # greedy without logprobs keeps the on-device argmax path
-        select = None if sampler.greedy and top_logprobs is None else choose
-        # selection and logprobs on the device: greedy with logprobs, or a
-        # sampled request whose sampler exposes its generator (the reference
-        # Sampler does)
-        device_sampling = (
-            select is not None and getattr(self, "_engine", None) is not None
-            and (sampler.greedy or (getattr(sampler, "_rng", None) is not None and hasattr(sampler, "params")))
-            and os.environ.get("HAWKPOINT_DEVICE_SAMPLING", "1") != "0"
-        )
-
-        def step(token_id, position, final=True):
-            if final and device_sampling:
-                token, elapsed, state["entry"] = self._sample_step(token_id, position, sampler, history,
-                                                                   top_logprobs)
-                return token, elapsed
-            return self._decode_step(token_id, position, select=select if final else None,
-                                     compute_logits=final)
-
-        def release(text, final=False):
-            nonlocal emitted
-            emitted += len(text.encode("utf-8"))
-            if final and stop_matcher.matched is None:
-                ready = len(pending)
-            else:
-                ready = 0
-                while ready < len(pending) and pending[ready][0] < emitted:
-                    ready += 1
-            out = [entry for _, entry in pending[:ready]]
-            del pending[:ready]
-            return out
-
-        def chunk(text, entries):
-            return (text, None) if top_logprobs is None else (text, None, entries)
-
+        """Serve one request from prepared prompt ids: ingest the uncached
+        prompt positions, then emit tokens until the budget, EOS or a stop
+        string.  Yields ``(text, None[, entries])`` chunks, then the
+        statistics (the chunk and statistics shapes of
+        npu_llm/runtime/generate.py:1050-1200)."""
+        picker = _TokenPicker(self, sampler, prompt_ids, top_logprobs)
+        writer = _ChunkWriter(self.tokenizer, stop_matcher, top_logprobs is not None)
         reused = self._reusable_prefix(prompt_ids)
-        timings = []
-        token = None
-        last = len(prompt_ids) - 1
-        if last > reused and getattr(self, "_engine", None) is not None:
-            # positions [reused, last) need no logits: batched prefill launches
-            timings.extend(self._prefill_positions(prompt_ids, reused, last))
-            first = last
-        else:
-            first = reused
-        for index in range(first, len(prompt_ids)):
-            token, elapsed = step(prompt_ids[index], index, final=index == last)
-            timings.append(elapsed)
-        prefill_steps = len(timings)
+        prompt_seconds = picker.ingest(prompt_ids, reused)
+        eos = self.tokenizer.eos_id
         position = len(prompt_ids)
-        detokenizer = StreamDetokenizer(self.tokenizer)
-        generated = []
+        token = picker.token
         finish_reason = "length"
-        text = ""
-        while len(generated) < max_new_tokens:
-            entry, state["entry"] = state["entry"], None
-            if token == self.tokenizer.eos_id:
-                finish_reason = "stop"
+        while token != eos:
+            chunk = writer.add(token, picker.take_entry())
+            if writer.stopped:
                 break
-            generated.append(token)
-            history.append(token)
-            if entry is not None:
-                pending.append((produced, entry))
-                produced += len(self.tokenizer.token_bytes(token))
-            text = stop_matcher.feed(detokenizer.push(token))
-            if stop_matcher.matched is not None:
-                finish_reason = "stop"
-                break
-            if text:
-                yield chunk(text, release(text))
-            if len(generated) >= max_new_tokens:
-                break  # never compute a discarded successor token
-            token, elapsed = step(token, position)
-            timings.append(elapsed)
+            if chunk is not None:
+                yield chunk
+            if len(writer.tokens) == max_new_tokens:
+                break  # the budget is spent: no step for a successor nobody reads
+            token = picker.advance(token, position)
             position += 1
-        if stop_matcher.matched is None:
-            text = stop_matcher.feed(detokenizer.flush())
-            if stop_matcher.matched is not None:
-                finish_reason = "stop"
-            text += stop_matcher.flush()
-        entries = release(text, final=True) if top_logprobs is not None else []
-        if text or entries:
-            yield chunk(text, entries)
-        prefill_seconds = sum(timings[:prefill_steps])
-        decode_seconds = sum(timings[prefill_steps:])
-        decode_steps = len(timings) - prefill_steps
+        if token == eos or writer.stopped:
+            finish_reason = "stop"
+        last, reached_stop = writer.finish()
+        if reached_stop:
+            finish_reason = "stop"
+        if last is not None:
+            yield last
+        stats = self._request_stats(prompt_ids, reused, truncation, writer, finish_reason, sampler,
+                                    prompt_seconds, picker.decode_seconds)
+        yield ("", stats) if top_logprobs is None else ("", stats, [])
+
+    def _request_stats(self, prompt_ids, reused, truncation, writer, finish_reason, sampler, prompt_seconds,
+                       decode_seconds):
+        """Statistics of one request under the reference's key names; the
+        time to first token is the sum of the prompt positions' step times."""
+        ingested = len(prompt_ids) - reused
+        steps = len(decode_seconds)
+        decoding = sum(decode_seconds)
+        ttft = sum(prompt_seconds)
         stats = {
             "prompt_tokens": len(prompt_ids),
             "cached_prompt_tokens": reused,
             "prompt_truncation": truncation,
-            "generated_tokens": len(generated),
-            "generated_token_ids": generated,
+            "generated_tokens": len(writer.tokens),
+            "generated_token_ids": list(writer.tokens),
             "npu_layers": self.npu_layers,
             "cpu_layers": self.layers - self.npu_layers,
             "finish_reason": finish_reason,
-            "stop_sequence": stop_matcher.matched,
-            "ttft_seconds": prefill_seconds,
-            "prefill_tokens_per_second": prefill_steps / max(1e-9, prefill_seconds),
-            "decode_steps": decode_steps,
-            "decode_seconds": decode_seconds,
-            "decode_tokens_per_second": decode_steps / max(1e-9, decode_seconds),
+            "stop_sequence": writer.stop.matched,
+            "ttft_seconds": ttft,
+            "prefill_tokens_per_second": ingested / max(1e-9, ttft),
+            "decode_steps": steps,
+            "decode_seconds": decoding,
+            "decode_tokens_per_second": steps / max(1e-9, decoding),
             "peak_ram_mib": resource.getrusage(resource.RUSAGE_SELF).ru_maxrss / 1024,
             "sampling": sampler.stats(),
         }
         if getattr(self, "_profile_enabled", False):
             stats["phase_ms"] = {name: round(s * 1000.0, 3) for name, s in self._phase_totals.items()}
-        if top_logprobs is None:
-            yield "", stats
-        else:
-            yield "", stats, []
+        return stats
 
     def generate_ids(self, prompt_ids, max_new_tokens):
         """Greedy generation from token ids with the whole loop on the device
@@ -496,3 +434,139 @@ class NPUDecoder:
         self._engine = None
         self._cached_prefix = []
         gc.collect()
+
+
+class _TokenPicker:
+    """Chooses the token that follows each computed position of one request.
+
+    Three routes, fixed per request: the engine's on-device argmax (greedy
+    without logprobs: no logits leave the GPU); selection on the device
+    through ``NPUDecoder._sample_step`` (sampled requests whose sampler
+    exposes its generator, and greedy requests with logprobs); or the
+    sampler's host ``select`` on logits copied back (any other sampler).
+    The sampler is consulted once per emitted token, never for prompt
+    positions whose successor is known, so its random stream advances as in
+    the reference loop.  ``history`` (prompt + generated ids) feeds the
+    repetition penalties."""
+
+    def __init__(self, decoder, sampler, prompt_ids, top_logprobs):
+        self.decoder = decoder
+        self.sampler = sampler
+        self.history = list(prompt_ids)
+        self.top_logprobs = top_logprobs
+        self.entry = None
+        self.token = None
+        self.decode_seconds = []
+        host_select = not (sampler.greedy and top_logprobs is None)
+        engine = getattr(decoder, "_engine", None)
+        on_device = (
+            host_select and engine is not None
+            and os.environ.get("HAWKPOINT_DEVICE_SAMPLING", "1") != "0"
+            and (sampler.greedy or (getattr(sampler, "_rng", None) is not None and hasattr(sampler, "params")))
+        )
+        self.route = "device" if on_device else ("host" if host_select else "argmax")
+
+    def _host_choice(self, logits):
+        if self.sampler.greedy:
+            token = int(np.argmax(logits))
+        else:
+            token = self.sampler.select(logits, self.history)
+        if self.top_logprobs is not None:
+            self.entry = self.decoder._logprob_entry(logits, token, self.top_logprobs)
+        return token
+
+    def _pick(self, token_id, position):
+        """Compute `position` and choose its successor: (token, seconds)."""
+        if self.route == "device":
+            token, seconds, self.entry = self.decoder._sample_step(
+                token_id, position, self.sampler, self.history, self.top_logprobs)
+            return token, seconds
+        select = self._host_choice if self.route == "host" else None
+        return self.decoder._decode_step(token_id, position, select=select)
+
+    def ingest(self, prompt_ids, reused):
+        """Compute prompt positions reused..end; only the last one selects a
+        token.  With an engine, the positions before it go through batched
+        prefill launches.  Returns the per-position seconds."""
+        last = len(prompt_ids) - 1
+        seconds = []
+        begin = reused
+        if last > begin and getattr(self.decoder, "_engine", None) is not None:
+            seconds += self.decoder._prefill_positions(prompt_ids, begin, last)
+            begin = last
+        for position in range(begin, last):
+            _, elapsed = self.decoder._decode_step(prompt_ids[position], position, compute_logits=False)
+            seconds.append(elapsed)
+        self.token, elapsed = self._pick(prompt_ids[last], last)
+        seconds.append(elapsed)
+        return seconds
+
+    def advance(self, token_id, position):
+        """Feed the emitted `token_id` at `position`; returns the next token."""
+        self.history.append(token_id)
+        self.token, elapsed = self._pick(token_id, position)
+        self.decode_seconds.append(elapsed)
+        return self.token
+
+    def take_entry(self):
+        entry, self.entry = self.entry, None
+        return entry
+
+
+class _ChunkWriter:
+    """Turns emitted token ids into the request's text chunks.
+
+    Text passes the stream detokenizer and the stop matcher (which holds
+    back anything that may begin a stop string).  With logprobs, each
+    token's entry is queued under the byte offset where its text starts and
+    leaves with the first chunk whose emitted text reaches past that
+    offset; on a normal end every queued entry leaves with the last chunk,
+    after a stop string only those whose text was emitted."""
+
+    def __init__(self, tokenizer, stop, logprobs):
+        self.tokenizer = tokenizer
+        self.stop = stop
+        self.logprobs = logprobs
+        self.detokenizer = StreamDetokenizer(tokenizer)
+        self.tokens = []
+        self.queue = []      # (byte offset of the token's text, entry), in order
+        self.produced = 0    # bytes of text the queued tokens produced
+        self.emitted = 0     # bytes of text handed out in chunks
+        self.pending_text = ""
+
+    @property
+    def stopped(self):
+        return self.stop.matched is not None
+
+    def _pack(self, text, flush_all):
+        if not self.logprobs:
+            return text, None
+        self.emitted += len(text.encode("utf-8"))
+        count = len(self.queue) if flush_all else sum(1 for offset, _ in self.queue if offset < self.emitted)
+        entries = [entry for _, entry in self.queue[:count]]
+        del self.queue[:count]
+        return text, None, entries
+
+    def add(self, token, entry):
+        """Record one emitted token; returns a chunk to yield, or None."""
+        self.tokens.append(token)
+        if entry is not None:
+            self.queue.append((self.produced, entry))
+            self.produced += len(self.tokenizer.token_bytes(token))
+        text = self.stop.feed(self.detokenizer.push(token))
+        if self.stopped:
+            self.pending_text = text  # what precedes the stop string goes out last
+            return None
+        return self._pack(text, False) if text else None
+
+    def finish(self):
+        """The final chunk (or None) and whether a stop string ended it."""
+        text = self.pending_text
+        hit_now = False
+        if not self.stopped:
+            text = self.stop.feed(self.detokenizer.flush())
+            hit_now = self.stopped
+            text += self.stop.flush()
+        chunk = self._pack(text, not self.stopped)
+        has_entries = self.logprobs and len(chunk) == 3 and chunk[2]
+        return (chunk if text or has_entries else None), hit_now

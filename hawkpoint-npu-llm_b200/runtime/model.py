@@ -49,29 +49,29 @@ def _file_sha256(path):
 
 def _inside(root, name):
     if not isinstance(name, str) or not name:
-        raise RuntimeError("model manifest contains an invalid file path")
+        raise RuntimeError("package manifest names a file with an empty or non-string path")
     p = Path(name)
     if p.is_absolute():
-        raise RuntimeError(f"absolute model path is not allowed: {name}")
+        raise RuntimeError(f"package files must use relative paths, got {name}")
     root = Path(root).resolve()
     full = (root / p).resolve()
     if root != full and root not in full.parents:
-        raise RuntimeError(f"model path escapes package root: {name}")
+        raise RuntimeError(f"package file {name} resolves outside the package directory")
     return full
 
 
 def _dims(shape, name):
     if not isinstance(shape, (list, tuple)) or not shape:
-        raise RuntimeError(f"tensor {name} has an invalid shape")
+        raise RuntimeError(f"{name}: shape must be a non-empty list of dimensions")
     count = 1
     for d in shape:
         if isinstance(d, bool) or not isinstance(d, int):
-            raise RuntimeError(f"tensor {name} has a non-integer shape")
+            raise RuntimeError(f"{name}: every dimension must be an integer")
         if d <= 0:
-            raise RuntimeError(f"tensor {name} has a non-positive shape")
+            raise RuntimeError(f"{name}: every dimension must be at least 1")
         count *= d
         if count > MAX_ELEMENTS:
-            raise RuntimeError(f"tensor {name} is too large")
+            raise RuntimeError(f"{name}: more than 2**31 elements")
     return tuple(shape), count
 
 
@@ -83,16 +83,16 @@ class PackageModel:
         try:
             meta = json.loads(_inside(self.root, "metadata.json").read_text())
         except (OSError, json.JSONDecodeError) as exc:
-            raise RuntimeError("model package has invalid metadata.json") from exc
+            raise RuntimeError("metadata.json is missing or is not valid JSON") from exc
         if not isinstance(meta, dict):
-            raise RuntimeError("model metadata must be a JSON object")
+            raise RuntimeError("metadata.json must hold a JSON object at the top level")
         if not isinstance(meta.get("tensors"), dict):
-            raise RuntimeError("model metadata has no tensor manifest")
+            raise RuntimeError("metadata.json lacks the 'tensors' table")
         digest = meta.get("metadata_sha256")
         if not isinstance(digest, str) or len(digest) != 64:
-            raise RuntimeError("model package has no metadata_sha256; reconvert the model")
+            raise RuntimeError("metadata.json carries no metadata_sha256 digest (written by an older converter?)")
         if _digest_metadata(meta) != digest:
-            raise RuntimeError("model metadata checksum mismatch")
+            raise RuntimeError("metadata checksum mismatch: metadata.json was edited after conversion")
         self.metadata = meta
         self.tensors = meta["tensors"]
         self._files = meta.get("files")
@@ -102,34 +102,34 @@ class PackageModel:
     def _verify(self):
         files = self._files
         if not isinstance(files, dict) or not files:
-            raise RuntimeError("model package has no integrity manifest; reconvert the model")
+            raise RuntimeError("metadata.json lists no files with sizes and digests; convert the model again")
         for name, entry in files.items():
             path = _inside(self.root, name)
             size = entry.get("size") if isinstance(entry, dict) else None
             sha = entry.get("sha256") if isinstance(entry, dict) else None
             if isinstance(size, bool) or not isinstance(size, int) or size < 0 \
                     or not isinstance(sha, str) or len(sha) != 64:
-                raise RuntimeError(f"invalid integrity entry: {name}")
+                raise RuntimeError(f"files[{name!r}] needs an integer size and a 64-digit sha256")
             if not path.is_file() or path.stat().st_size != size:
-                raise RuntimeError(f"model package file is missing or truncated: {name}")
+                raise RuntimeError(f"{name}: absent, or its size differs from the manifest")
             if _file_sha256(path) != sha:
-                raise RuntimeError(f"model package checksum mismatch: {name}")
+                raise RuntimeError(f"{name}: content checksum mismatch against the manifest")
         for tname, spec in self.tensors.items():
             if not isinstance(spec, dict):
-                raise RuntimeError(f"invalid tensor specification: {tname}")
+                raise RuntimeError(f"tensors[{tname!r}] must be a JSON object")
             for field in ("file", "weight", "scale", "bf16_file"):
                 fname = spec.get(field)
                 if fname is not None and fname not in files:
-                    raise RuntimeError(f"tensor file is missing from integrity manifest: {fname}")
+                    raise RuntimeError(f"{fname} is referenced by a tensor but not listed under files")
 
     def _map(self, fname, dtype, shape):
         path = _inside(self.root, fname)
         dtype = np.dtype(dtype)
         shape, count = _dims(list(shape), fname)
         if path.stat().st_size != count * dtype.itemsize:
-            raise RuntimeError(f"tensor file size mismatch for {fname}")
+            raise RuntimeError(f"{fname}: byte size does not match the tensor's shape and dtype")
         if isinstance(self._files, dict) and fname not in self._files:
-            raise RuntimeError(f"tensor file is missing from integrity manifest: {fname}")
+            raise RuntimeError(f"{fname} is referenced by a tensor but not listed under files")
         return np.memmap(path, mode="r", dtype=dtype, shape=shape)
 
     def raw(self, name):
@@ -137,20 +137,20 @@ class PackageModel:
         try:
             dtype = np.dtype(bfloat16) if spec["dtype"] == "bfloat16" else np.dtype(spec["dtype"])
         except (KeyError, TypeError) as exc:
-            raise RuntimeError(f"tensor {name} has an invalid dtype") from exc
+            raise RuntimeError(f"{name}: unknown or missing dtype") from exc
         return self._map(spec["file"], dtype, spec["shape"])
 
     def bf16_projection(self, name):
         spec = self.tensors[name]
         if "bf16_file" not in spec:
-            raise RuntimeError(f"{name} has no BF16 weights; reconvert the model")
+            raise RuntimeError(f"{name}: the package stores no BF16 copy of this projection")
         return self._map(spec["bf16_file"], bfloat16, spec["shape"])
 
     def quantized(self, name):
         spec = self.tensors[name]
         shape, _ = _dims(spec.get("shape"), name)
         if len(shape) != 2:
-            raise RuntimeError("quantized tensors must be rank two")
+            raise RuntimeError("an int8 projection must be a 2-D [rows, columns] matrix")
         return QuantizedView(
             self._map(spec["weight"], np.int8, shape), self._map(spec["scale"], np.float32, shape[:1])
         )

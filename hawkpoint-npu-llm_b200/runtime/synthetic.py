@@ -48,7 +48,9 @@ class ModelShape:
         return (self.q_heads + 2 * self.kv_heads) * self.head_dim
 
 
-# BASELINE configs[0] and configs[2] (SmolLM2-135M- and Qwen2.5-0.5B-shaped).
+# SmolLM2-135M and Qwen2.5-0.5B geometry: 30 layers of hidden 576 (9 q / 3 kv heads,
+# intermediate 1536, vocab 49152, theta 1e5, eps 1e-5); 24 layers of hidden 896
+# (14 q / 2 kv heads, intermediate 4864, vocab 151936, theta 1e6, eps 1e-6, qkv bias).
 SMOLLM2_135M = ModelShape("llama", 576, 1536, 9, 3, 64, 30, 49152, 1e5, 1e-5, False)
 QWEN25_05B = ModelShape("qwen2", 896, 4864, 14, 2, 64, 24, 151936, 1e6, 1e-6, True)
 # Small shapes with the same head geometry, for fast parity cases.
@@ -261,3 +263,19 @@ def prompt_ids(vocab, count, seed):
     """Seeded uniform token ids in [0, vocab), as the benchmark configs draw them."""
     rng = np.random.default_rng([seed, 0x9E3779B9])
     return [int(v) for v in rng.integers(0, vocab, size=count)]
+
+
+def ragged_prompts(vocab, count=512, seed=5, shared_len=16):
+    """The multi-stream serving workload's prompts: `count` independent
+    requests with lengths uniform in [8, 48], every fourth one opening with
+    one shared `shared_len`-token prefix (seeded ids stand in for text)."""
+    rng = np.random.default_rng(seed)
+    shared = rng.integers(0, vocab, shared_len).tolist()
+    prompts = []
+    for i in range(count):
+        length = int(rng.integers(8, 49))
+        ids = rng.integers(0, vocab, length).tolist()
+        if i % 4 == 0:
+            ids = shared + ids[: max(1, length - shared_len)]
+        prompts.append([int(t) for t in ids])
+    return prompts

@@ -21,6 +21,20 @@ Cases:
   and on BF16 projections of the seeded Qwen model.
 * ``attention.npz`` -- the reference ``_attention`` on the toy case of
   npu_llm/tests/test_cpu_backend.py:17-52 (seed 42).
+* ``request_<shape>_<weights>.npz`` -- the complete benchmarked requests:
+  the prompt, then greedy decoding with the token fed back, the way
+  ``NPUDecoder._generate_tokens_core`` drives the CPU stage
+  (npu_llm/runtime/generate.py:1110-1158); per position the argmax, top-2
+  margin, top-32 logits and a strided sample.  Qwen2.5-0.5B BF16: the
+  32-position window of the 40-id prompt + 32 tokens (64 positions);
+  SmolLM2-135M BF16: 35 + 16; Qwen2.5-0.5B W8: 32 + 32.  The reference has
+  no W8 CPU runtime, so the W8 request comes from this repository's W8
+  oracle (its projection arithmetic follows the reference W8 kernels; its
+  int8 bytes are pinned by ``quantize.npz``).
+* ``serving_qwen2.5-0.5b.npz`` -- four requests of the multi-stream serving
+  workload (two opening with its shared 16-token prefix), each with 16
+  greedy tokens from the reference CPU stage run alone, with per-token
+  top-2 margins.
 """
 
 import argparse
@@ -102,14 +116,111 @@ def decode_case(backend, name, seed, positions, full_logits, layers=None):
     return record
 
 
+class _ReferenceStep:
+    """One position of the reference CPU stage through every layer, as
+    ``decode_token`` runs it with ``npu_layers=0``."""
+
+    def __init__(self, backend, model):
+        self.backend = backend
+        self.stage = backend.CPUDecoderStage(model, 0, 64)
+        self.embedding = np.asarray(model.raw("token_embedding"), dtype=np.float32)
+        self.layers = model.metadata["layers"]
+
+    def __call__(self, token, position):
+        hidden = self.backend._bf16(self.embedding[token])
+        for layer in range(self.layers):
+            hidden = self.stage.layer(hidden, layer, position)
+        return np.asarray(self.stage.logits(hidden), dtype=np.float32)
+
+
+def greedy_request(step, prompt, new_tokens, context=64):
+    """Prompt positions, then greedy tokens fed back; every generated token
+    is also fed (its successor's logits are recorded) while the context
+    lasts.  Returns (fed ids, logits per position, generated tokens)."""
+    ids, rows, generated = [], [], []
+    token = None
+    for position in range(min(context, len(prompt) + new_tokens)):
+        token = prompt[position] if position < len(prompt) else generated[-1]
+        logits = step(int(token), position)
+        ids.append(int(token))
+        rows.append(logits)
+        if position >= len(prompt) - 1 and len(generated) < new_tokens:
+            generated.append(int(np.argmax(logits)))
+    return ids, np.stack(rows), generated
+
+
+def summarize_logits(logits, stride):
+    order = np.argsort(-logits, axis=1, kind="stable")
+    top = order[:, :32]
+    return {
+        "argmax": logits.argmax(axis=1).astype(np.int64),
+        "margin": np.take_along_axis(logits, order[:, :1], 1)[:, 0]
+        - np.take_along_axis(logits, order[:, 1:2], 1)[:, 0],
+        "top_ids": top.astype(np.int32),
+        "top_logits": np.take_along_axis(logits, top, 1),
+        "sample_stride": np.array(stride),
+        "sample_logits": logits[:, ::stride].astype(np.float32),
+        "norm": np.linalg.norm(logits, axis=1).astype(np.float32),
+    }
+
+
+def request_case(backend, name, weights, n_prompt, new_tokens, stride):
+    model = synthetic.build(name, seed=0).materialize()
+    prompt = synthetic.prompt_ids(model.shape.vocab, 40, 1)[:n_prompt]
+    if weights == "bf16":
+        step = _ReferenceStep(backend, model)
+    else:
+        sys.path.insert(0, str(REPO))
+        from oracle.cpu_decoder import OracleDecoder
+
+        oracle = OracleDecoder(model, weights="w8")
+        step = lambda token, position: oracle.step(token, position)  # noqa: E731
+    ids, logits, generated = greedy_request(step, prompt, new_tokens)
+    record = {"shape": np.array(name), "weights": np.array(weights), "seed": np.array(0),
+              "prompt": np.array(prompt, dtype=np.int64), "ids": np.array(ids, dtype=np.int64),
+              "generated": np.array(generated, dtype=np.int64),
+              "source": np.array("reference CPUDecoderStage" if weights == "bf16" else "repository W8 oracle")}
+    record.update(summarize_logits(logits, stride))
+    return record
+
+
+def serving_case(backend, picks=(0, 1, 2, 4), new_tokens=16):
+    model = synthetic.build("qwen2.5-0.5b", seed=0).materialize()
+    prompts = synthetic.ragged_prompts(model.shape.vocab)
+    out = {"picks": np.array(picks, dtype=np.int64)}
+    for i in picks:
+        step = _ReferenceStep(backend, model)  # a fresh cache per request
+        prompt = prompts[i]
+        ids, logits, generated = greedy_request(step, prompt, new_tokens, context=len(prompt) + new_tokens - 1)
+        summary = summarize_logits(logits[len(prompt) - 1:], 301)
+        out[f"prompt_{i}"] = np.array(prompt, dtype=np.int64)
+        out[f"generated_{i}"] = np.array(generated, dtype=np.int64)
+        out[f"margin_{i}"] = summary["margin"]
+    return out
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", default=os.environ.get("REFERENCE_ROOT"))
     parser.add_argument("--skip-full", action="store_true")
+    parser.add_argument("--only", choices=["all", "requests"], default="all",
+                        help="requests: write only the whole-request and serving fixtures")
     args = parser.parse_args()
     if not args.reference:
         raise SystemExit("pass --reference <reference checkout> or set REFERENCE_ROOT")
     backend, convert = load_reference(args.reference)
+    if args.only == "requests" or not args.skip_full:
+        for name, weights, n_prompt, new_tokens, stride in (("qwen2.5-0.5b", "bf16", 32, 32, 301),
+                                                            ("smollm2-135m", "bf16", 35, 16, 97),
+                                                            ("qwen2.5-0.5b", "w8", 32, 32, 301)):
+            record = request_case(backend, name, weights, n_prompt, new_tokens, stride)
+            np.savez_compressed(HERE / f"request_{name}_{weights}.npz", **record)
+            print(f"wrote request_{name}_{weights}.npz generated", record["generated"].tolist())
+        record = serving_case(backend)
+        np.savez_compressed(HERE / "serving_qwen2.5-0.5b.npz", **record)
+        print("wrote serving_qwen2.5-0.5b.npz")
+    if args.only == "requests":
+        return
 
     cases = [
         ("decode_tiny-qwen.npz", dict(name="tiny-qwen", seed=11, positions=20, full_logits=True)),

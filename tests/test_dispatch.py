@@ -13,7 +13,7 @@ from runtime import dispatch
 
 
 def workload(n=64, seed=3, shared_fraction=0.25, prefix=16):
-    """BASELINE config 5 in miniature: prompt lengths U[8, 48], a quarter of
+    """The multi-stream serving workload in miniature: prompt lengths U[8, 48], a quarter of
     the requests sharing one 16-token prefix."""
     rng = np.random.default_rng(seed)
     common = rng.integers(0, 151936, prefix).tolist()

@@ -249,7 +249,7 @@ def test_full_size_against_reference_golden(name, golden):
 
 
 def test_full_size_w8_against_w8_oracle():
-    """every projection and the LM head in int8 with FP32
+    """Qwen shape in W8: every projection and the LM head in int8 with FP32
     row scales, teacher-forced against the W8 oracle at full Qwen size."""
     model = synthetic.build("qwen2.5-0.5b", seed=0).materialize()
     engine = B200DecoderEngine(model, weights="w8")

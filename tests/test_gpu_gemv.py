@@ -1,4 +1,4 @@
-"""Standalone weight-streaming GEMV against a PyTorch FP32
+"""Standalone weight-streaming GEMV (the matrix_vector shapes of the GEMV microbenchmark) against a PyTorch FP32
 reference of the same op: ``bf16(W_f32 @ x_f32)`` (the BF16 projection of
 npu_llm/runtime/cpu_backend.py:64-69) and the W8 form
 ``bf16((q_f32 @ x_f32) * scale)`` (npu_llm/kernels/decoder_layer_bf16.cc:64-80).

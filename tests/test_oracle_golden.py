@@ -55,6 +55,38 @@ def test_oracle_matches_reference_full_size(name, golden):
         assert int(np.argmax(logits)) == int(g["argmax"][position]) or g["margin"][position] <= 0.05
 
 
+def test_oracle_matches_reference_whole_request(golden):
+    """The SmolLM2-135M request of the benchmark (35 prompt positions + 16
+    greedy tokens) through the oracle, against the reference CPU stage's
+    recording: logits at every position and the greedy tokens."""
+    g = golden("request_smollm2-135m_bf16.npz")
+    model = synthetic.build("smollm2-135m", seed=int(g["seed"])).materialize()
+    oracle = OracleDecoder(model)
+    stride = int(g["sample_stride"])
+    n_prompt = len(g["prompt"])
+    generated = []
+    for position, token in enumerate(g["ids"]):
+        logits = oracle.step(int(token), position)
+        np.testing.assert_allclose(logits[::stride], g["sample_logits"][position], rtol=0, atol=1e-4)
+        np.testing.assert_allclose(logits[g["top_ids"][position]], g["top_logits"][position], rtol=0, atol=1e-4)
+        if position >= n_prompt - 1 and len(generated) < len(g["generated"]):
+            generated.append(int(np.argmax(logits)))
+    assert generated == g["generated"].tolist()
+
+
+def test_request_fixtures_are_consistent(golden):
+    """Each whole-request fixture feeds its prompt, then its own greedy
+    tokens, and its top-1 entries are its argmax."""
+    for name in ("request_qwen2.5-0.5b_bf16", "request_smollm2-135m_bf16", "request_qwen2.5-0.5b_w8"):
+        g = golden(f"{name}.npz")
+        n = len(g["prompt"])
+        ids = g["ids"].tolist()
+        assert ids[:n] == g["prompt"].tolist()
+        assert ids[n:] == g["generated"].tolist()[: len(ids) - n]
+        assert np.array_equal(g["top_ids"][:, 0], g["argmax"])
+        assert np.all(g["margin"] >= 0)
+
+
 def test_quantiser_is_bit_exact_with_reference(golden):
     g = golden("quantize.npz")
     q, s = quantize_per_output_channel(g["matrix"])

@@ -1,4 +1,4 @@
-"""Multi-stream continuous batching (BASELINE config 5 on one GPU): the
+"""Multi-stream continuous batching (the 512-request ragged serving workload on one GPU): the
 scheduler on CPU against a fake causal engine, and on the GPU against
 single-stream generation through the same kernels."""
 
