@@ -581,57 +581,39 @@ struct DecoderCta {
     return true;
   }
 
-  // One unit: RoPE (rotate-half, unfused mul/add, BF16), K/V append, scores
-  // q.k * 0.125 over positions <= p, softmax (max-subtract, exp, divide),
-  // P.V in FP32; publishes bf16 outputs to ll_att(layer, m) + h * 32.
-  // Called by every consumer thread (one block barrier publishes the
-  // cp.async history); warp 0 does the work -- one head is a few thousand
-  // FMAs, so block barriers would cost more than the math.
-  __device__ void attention_unit(int layer, int m, int h, int j, uint32_t *u96) {
-    const int p = s_pos[m];
-    float *qf = reinterpret_cast<float *>(u96 + 96);
-    float *sc = qf + kHeadDim;
-    uint8_t *kb = kvs, *vb = kvs + static_cast<size_t>(P.CTX) * 128;
-    cp_async_wait_all();
-    consumer_sync(kConsumerThreads);  // every thread's history copies (and u96) are visible
-    if (tid >= 32) return;
-    const int lane = tid;
-    auto rope_pair = [&](const uint32_t *w32, int pr, int d, __nv_bfloat16 &lo, __nv_bfloat16 &hi) {
-      // elements d and d + 32 of the 64 held as BF16 pairs in w32[0..32)
-      const uint32_t a = w32[d >> 1], b = w32[(d + 32) >> 1];
-      const float x0 = (d & 1) ? bf_hi(a) : bf_lo(a), x1 = (d & 1) ? bf_hi(b) : bf_lo(b);
-      const float c = P.rope_cos[pr * 32 + d], sn = P.rope_sin[pr * 32 + d];
-      lo = f2bf(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
-      hi = f2bf(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
-    };
-    auto put_kv = [&](int pr, int d, __nv_bfloat16 klo, __nv_bfloat16 khi, uint32_t vword) {
-      *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(pr, d >> 3) + (d & 7) * 2) = klo;
-      *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(pr, 4 + (d >> 3)) + (d & 7) * 2) = khi;
-      *reinterpret_cast<uint32_t *>(vb + kv_off(pr, (2 * d) >> 3) + ((2 * d) & 7) * 2) = vword;
-    };
-    {
-      __nv_bfloat16 lo, hi;
-      rope_pair(u96, p, lane, lo, hi);  // q
-      qf[lane] = bf2f(lo);
-      qf[lane + 32] = bf2f(hi);
-      rope_pair(u96 + 32, p, lane, lo, hi);  // k
-      put_kv(p, lane, lo, hi, u96[64 + lane]);
-      // batched prefill: k and v of the earlier rows of the run
-      const int f = run_start(m);
-      for (int r = f; r < m; ++r) {
-        const uint32_t *w = u96 + kUnitWords + 64 * (r - f);
-        rope_pair(w, s_pos[r], lane, lo, hi);
-        put_kv(s_pos[r], lane, lo, hi, w[32 + lane]);
-      }
-    }
-    __syncwarp();
-    // the first q head of kv group j appends row p of K and V to the cache
-    if (h % P.group == 0 && lane < 16) {
-      const int kind = lane >> 3, cb = lane & 7;
-      const uint8_t *srow = (kind ? vb : kb) + kv_off(p, cb);
-      uint8_t *dst = reinterpret_cast<uint8_t *>(kv_block(s_slot[m], layer, j, kind)) + kv_off(p, cb);
-      *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(srow);
-    }
+  // Rotate-half RoPE of elements d and d + 32 of a 64-element head held as
+  // BF16 pairs in w32[0..32), at position pr (unfused mul / sub / add, as
+  // cpu_backend.py:78-93).
+  __device__ __forceinline__ void rope_pair(const uint32_t *w32, int pr, int d, __nv_bfloat16 &lo,
+                                            __nv_bfloat16 &hi) const {
+    rope_pair_cs(w32, d, P.rope_cos[pr * 32 + d], P.rope_sin[pr * 32 + d], lo, hi);
+  }
+  // The same with the position's cos / sin of dim d already loaded.
+  __device__ __forceinline__ static void rope_pair_cs(const uint32_t *w32, int d, float c, float sn,
+                                                      __nv_bfloat16 &lo, __nv_bfloat16 &hi) {
+    const uint32_t a = w32[d >> 1], b = w32[(d + 32) >> 1];
+    const float x0 = (d & 1) ? bf_hi(a) : bf_lo(a), x1 = (d & 1) ? bf_hi(b) : bf_lo(b);
+    lo = f2bf(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
+    hi = f2bf(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
+  }
+
+  // Lane d's part of position pr's K row (rotated dims d, d + 32) and V row
+  // (dims 2d, 2d + 1) in a swizzled K / V history block.
+  __device__ __forceinline__ static void put_kv(uint8_t *kb, uint8_t *vb, int pr, int d, __nv_bfloat16 klo,
+                                                __nv_bfloat16 khi, uint32_t vword) {
+    *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(pr, d >> 3) + (d & 7) * 2) = klo;
+    *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(pr, 4 + (d >> 3)) + (d & 7) * 2) = khi;
+    *reinterpret_cast<uint32_t *>(vb + kv_off(pr, (2 * d) >> 3) + ((2 * d) & 7) * 2) = vword;
+  }
+
+  // One warp: scores q.k * 0.125 over positions <= p of a K / V history in
+  // shared memory (qf: the rotated q in FP32, sc: 64 floats of scratch),
+  // softmax (max-subtract, exp, IEEE divide) and P.V in FP32; returns this
+  // lane's output dims 2 * lane, 2 * lane + 1 as a BF16 pair
+  // (cpu_backend.py:95-129).
+  __device__ __forceinline__ uint32_t attend(const float *qf, float *sc, const uint8_t *kb, const uint8_t *vb,
+                                             int p) const {
+    const int lane = tid & 31;
     // scores: lane takes positions lane and lane + 32
     float s2[2];  // (indexed by unrolled e only)
 #pragma unroll
@@ -686,7 +668,47 @@ struct DecoderCta {
       o00 = fmaf(w0, bf_lo(v0), o00);
       o01 = fmaf(w0, bf_hi(v0), o01);
     }
-    ll_store(ll_att(layer, m) + h * 32 + lane, pack_bf16x2(o00 + o10, o01 + o11), epoch);
+    return pack_bf16x2(o00 + o10, o01 + o11);
+  }
+
+  // One unit: RoPE (rotate-half, unfused mul/add, BF16), K/V append, then
+  // attend(); publishes the bf16 outputs to ll_att(layer, m) + h * 32.
+  // Called by every consumer thread (one block barrier publishes the
+  // cp.async history); warp 0 does the work -- one head is a few thousand
+  // FMAs, so block barriers would cost more than the math.
+  __device__ void attention_unit(int layer, int m, int h, int j, uint32_t *u96, float rc, float rs) {
+    const int p = s_pos[m];
+    float *qf = reinterpret_cast<float *>(u96 + 96);
+    float *sc = qf + kHeadDim;
+    uint8_t *kb = kvs, *vb = kvs + static_cast<size_t>(P.CTX) * 128;
+    cp_async_wait_all();
+    consumer_sync(kConsumerThreads);  // every thread's history copies (and u96) are visible
+    if (tid >= 32) return;
+    const int lane = tid;
+    {
+      __nv_bfloat16 lo, hi;
+      rope_pair_cs(u96, lane, rc, rs, lo, hi);  // q
+      qf[lane] = bf2f(lo);
+      qf[lane + 32] = bf2f(hi);
+      rope_pair_cs(u96 + 32, lane, rc, rs, lo, hi);  // k
+      put_kv(kb, vb, p, lane, lo, hi, u96[64 + lane]);
+      // batched prefill: k and v of the earlier rows of the run
+      const int f = run_start(m);
+      for (int r = f; r < m; ++r) {
+        const uint32_t *w = u96 + kUnitWords + 64 * (r - f);
+        rope_pair(w, s_pos[r], lane, lo, hi);
+        put_kv(kb, vb, s_pos[r], lane, lo, hi, w[32 + lane]);
+      }
+    }
+    __syncwarp();
+    // the first q head of kv group j appends row p of K and V to the cache
+    if (h % P.group == 0 && lane < 16) {
+      const int kind = lane >> 3, cb = lane & 7;
+      const uint8_t *srow = (kind ? vb : kb) + kv_off(p, cb);
+      uint8_t *dst = reinterpret_cast<uint8_t *>(kv_block(s_slot[m], layer, j, kind)) + kv_off(p, cb);
+      *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(srow);
+    }
+    ll_store(ll_att(layer, m) + h * 32 + lane, attend(qf, sc, kb, vb, p), epoch);
   }
 
   // ---- paged attention (contexts longer than 64 positions) ---------------------
@@ -978,13 +1000,17 @@ struct DecoderCta {
         if (!ok) return false;
         if (ucta < mrows * P.QH) attention_paged(layer, um, uh, uj, us, S, u96);
       } else if (has_unit()) {
-        kv_prefetch_unit(layer, um, uj);  // overlaps the wait for q/k/v
+        // this row's RoPE cos / sin (dim = lane) and the K/V history are
+        // fetched while the q/k/v words are awaited
+        const int lane = tid & 31;
+        const float rc = P.rope_cos[s_pos[um] * 32 + lane], rs = P.rope_sin[s_pos[um] * 32 + lane];
+        kv_prefetch_unit(layer, um, uj);
         ok = gather_unit(layer, um, uh, uj, u96);
         if (!ok) {
           cp_async_wait_all();
           return false;
         }
-        attention_unit(layer, um, uh, uj, u96);
+        attention_unit(layer, um, uh, uj, u96, rc, rs);
       }
     }
     // the GEMV input: the previous phase's LL words, through one gather site

@@ -156,6 +156,24 @@ __device__ __forceinline__ const uint8_t *slot_ptr(const Ring &ring, int slot) {
   return ring.slots + static_cast<size_t>(slot) * kSlotBytes;
 }
 
+// Lanes c < n each wait (bounded) for the full barrier of the chunk c slots
+// after p, so a warp waiting for several chunks pays about one wait.
+__device__ __forceinline__ bool ring_wait_lanes(Ring &ring, const RingPos &p, int n, Ctrl *ctrl,
+                                                uint64_t limit_ns) {
+  const int lane = threadIdx.x & 31;
+  bool ok = true;
+  if (lane < n) {
+    int s = p.slot + lane;
+    uint32_t par = p.parity;
+    while (s >= ring.nslots) {
+      s -= ring.nslots;
+      par ^= 1u;
+    }
+    ok = mbar_wait(&ring.full[s], par, ctrl, limit_ns, kWhereFull);
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ---- tensor-core dot products (BF16) -------------------------------------------
 // One row group (8 weight rows) is the B operand of mma.m16n8k16 (n = the 8
 // rows, k = 16 columns); the activations are the A operand with batch row m
@@ -278,17 +296,15 @@ __device__ __forceinline__ bool consume_splitk(Ring &ring, const MatRange &r, co
     RingPos pos{ring.slot, ring.parity};
 #pragma unroll
     for (int i = 0; i < kStepRows; ++i) d[i][0] = d[i][1] = d[i][2] = d[i][3] = 0.f;
-    // wait for the n (<= kStepRows) chunks from the cursor on
+    // wait for the n (<= kStepRows) chunks from the cursor on, one lane per
+    // chunk (the warp pays one wait latency, not n)
     auto wait_chunks = [&](int n) {
-      RingPos p = pos;
-      bool ok = true;
+      const bool ok = ring_wait_lanes(ring, pos, n, ctrl, limit_ns);
 #pragma unroll
       for (int c = 0; c < kStepRows; ++c) {
-        if (c < n) {
-          ok = ok && ring_wait(ring, p, ctrl, limit_ns);
-          unit[c] = smem_u32(slot_ptr(ring, p.slot)) + lane_off;
-          ring_advance(p, 1, ring.nslots);
-        }
+        int sl = pos.slot + c;
+        if (sl >= ring.nslots) sl -= ring.nslots;
+        unit[c] = smem_u32(slot_ptr(ring, sl)) + lane_off;
       }
       return ok;
     };
