@@ -19,8 +19,8 @@ REPO = PKG.parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libhawkb200.so"
-SOURCES = [CSRC / "hb_engine.cu"]
-HEADERS = sorted(CSRC.glob("*.cuh")) + [REPO / "include" / "hawkb200.h"]
+SOURCES = [CSRC / "hb_engine.cu", CSRC / "hb_batch.cu"]
+HEADERS = sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + [REPO / "include" / "hawkb200.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

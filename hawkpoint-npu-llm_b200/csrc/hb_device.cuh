@@ -54,7 +54,7 @@ __device__ __forceinline__ int ld_volatile_int(const int *p) {
   return v;
 }
 
-__device__ __noinline__ void raise_error(Ctrl *ctrl, int code, int where) {
+static __device__ __noinline__ void raise_error(Ctrl *ctrl, int code, int where) {
   if (atomicCAS(&ctrl->err, 0, code) == 0) {
     atomicExch(&ctrl->err_where, where);
   }
@@ -65,7 +65,7 @@ __device__ __noinline__ void raise_error(Ctrl *ctrl, int code, int where) {
 // compile to a load and a compare: true when the wait must give up because
 // another CTA raised the abort flag or because `limit_ns` passed since
 // `start` (then the timeout is recorded with `where`).
-__device__ __noinline__ bool wait_expired(Ctrl *ctrl, uint64_t start, uint64_t limit_ns, int where) {
+static __device__ __noinline__ bool wait_expired(Ctrl *ctrl, uint64_t start, uint64_t limit_ns, int where) {
   if (ld_volatile_int(&ctrl->abort)) return true;
   if (globaltimer_ns() - start > limit_ns) {
     raise_error(ctrl, kErrTimeout, where);
@@ -131,7 +131,7 @@ __device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t *bar, uint32_t pa
 // Bounded wait for the phase with `parity` to complete.  Returns false on
 // timeout or when another CTA raised the abort flag.  The first test is
 // inline; a phase still open goes to the out-of-line loop.
-__device__ __noinline__ bool mbar_wait_slow(uint64_t *bar, uint32_t parity, Ctrl *ctrl, uint64_t limit_ns,
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t *bar, uint32_t parity, Ctrl *ctrl, uint64_t limit_ns,
                                             int where) {
   const uint64_t start = globaltimer_ns();
   while (true) {

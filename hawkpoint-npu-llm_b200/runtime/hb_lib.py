@@ -127,6 +127,9 @@ SIGNATURES = {
     "hb_sampler_logprobs": (_I, [_P, _P, _I, _I, _I, ctypes.POINTER(ctypes.c_double), _I32P,
                                  ctypes.POINTER(ctypes.c_double)]),
     "hb_logprobs": (_I, [_P, _I, _I, _I, ctypes.POINTER(ctypes.c_double), _I32P, ctypes.POINTER(ctypes.c_double)]),
+    "hb_tc_gemm_scratch_bytes": (ctypes.c_size_t, [_I, _I, _I]),
+    "hb_tc_gemm": (_I, [_P, _I, _I, _P, _I, _FP, _P, ctypes.c_size_t, _P]),
+    "hb_tc_gemm_status": (_I, [_P, _P]),
     "hb_library_error": (ctypes.c_char_p, []),
     "hb_device_sm_count": (_I, [_I]),
 }

@@ -283,6 +283,26 @@ int hb_logprobs(hb_engine *engine, int row, int token, int n_top, double *token_
  * hb_sample returned HB_ERR_UNSUPPORTED, without recomputing the step. */
 int hb_read_logits(hb_engine *engine, int n_rows, float *logits_out);
 
+/* ---- tensor-core GEMM for batched rows (new in this build) ------------------
+ * y[n][r] = sum_k W[r][k] * X[n][k] on the 5th-generation tensor cores
+ * (tcgen05.mma, BF16 inputs, FP32 accumulate in tensor memory): the dense
+ * contraction that batched prefill and multi-stream decode reduce to.  The
+ * reference runs these projections one position at a time
+ * (npu_llm/runtime/generate.py:1110-1126, one engine dispatch per position;
+ * npu_llm/designs/qwen_engine.py:158-212 inside the dispatch).
+ * w_dev: BF16 rows x k in the packed row-group layout (runtime/layout.py
+ * pack_matrix_bytes); x_dev: BF16 n x k activations in the same layout, n
+ * rounded up to a multiple of 8 rows; y_dev: FP32 [n][rows].  rows a
+ * multiple of 8, k of 64, 1 <= n <= 256, operands 16-byte aligned.  The
+ * caller owns scratch_dev (hb_tc_gemm_scratch_bytes); each call clears its
+ * control block and counters, so calls on one scratch must not overlap.
+ * Asynchronous on `stream`; hb_tc_gemm_status() waits for the stream and
+ * reports a device-side wait that gave up. */
+size_t hb_tc_gemm_scratch_bytes(int rows, int k, int n);
+int hb_tc_gemm(const void *w_dev, int rows, int k, const void *x_dev, int n, float *y_dev, void *scratch_dev,
+               size_t scratch_bytes, void *stream);
+int hb_tc_gemm_status(const void *scratch_dev, void *stream);
+
 /* Library-level error text (for calls that have no engine, e.g. hb_gemv). */
 const char *hb_library_error(void);
 
