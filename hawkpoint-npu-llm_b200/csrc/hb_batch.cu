@@ -50,8 +50,204 @@ size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 }  // namespace
 
+// Device buffers of the batched path, sized for kMaxRows rows and
+// allocated on an engine's first batched step.
+constexpr int kMaxRows = 128;
+
+struct hb_batch {
+  int *d_meta = nullptr;            // slot [kMaxRows] | pos | tok
+  int *d_argmax = nullptr;          // [kMaxRows]
+  __nv_bfloat16 *h = nullptr, *h1 = nullptr, *qkv = nullptr;  // row-major [kMaxRows][*]
+  uint8_t *xn = nullptr, *att = nullptr, *act = nullptr;      // packed GEMM inputs
+  uint8_t *scratch = nullptr;       // Ctrl | slice counters | split-K partials
+  size_t ws_floats = 0;
+  int max_tiles = 0;
+  float *part_val = nullptr;
+  int *part_idx = nullptr;
+  int lm_tiles = 0;
+  float *logits = nullptr;          // [kMaxRows][vocab], allocated when first asked for
+  int *h_meta = nullptr;            // pinned staging
+  int *h_argmax = nullptr;
+  hb::Ctrl *h_ctrl = nullptr;
+  int sms = 0;
+  size_t attr_smem[5] = {0, 0, 0, 0, 0};  // shared memory each GEMM variant is opted into on this device
+};
+
+namespace {
+
+hb::Ctrl *batch_ctrl(hb_batch *b) { return reinterpret_cast<hb::Ctrl *>(b->scratch); }
+unsigned int *batch_cnt(hb_batch *b) { return reinterpret_cast<unsigned int *>(b->scratch + kCtrlBytes); }
+float *batch_ws(hb_batch *b) {
+  return reinterpret_cast<float *>(b->scratch + kCtrlBytes + align256(sizeof(unsigned int) * b->max_tiles));
+}
+
+int batch_setup(hb_engine *e) {
+  if (e->batch) return HB_OK;
+  const hb_model_desc &d = e->desc;
+  auto *b = new hb_batch();
+  e->batch = b;
+  cudaDeviceGetAttribute(&b->sms, cudaDevAttrMultiProcessorCount, e->device);
+  const int H = d.hidden, I = d.intermediate, QKV = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
+  const int shapes[5][2] = {{QKV, H}, {H, H}, {2 * I, H}, {H, I}, {d.vocab, H}};
+  for (const auto &sh : shapes) {
+    const GemmShape g = gemm_shape(sh[0], sh[1], kMaxRows, b->sms);
+    b->ws_floats = std::max(b->ws_floats, g.ws_floats);
+    b->max_tiles = std::max(b->max_tiles, g.tiles);
+  }
+  b->lm_tiles = (d.vocab + hb::tc::kTileRows - 1) / hb::tc::kTileRows;
+  const size_t scratch = kCtrlBytes + align256(sizeof(unsigned int) * b->max_tiles) + b->ws_floats * sizeof(float);
+  int rc;
+  if ((rc = dev_alloc(e, &b->d_meta, 3 * kMaxRows)) || (rc = dev_alloc(e, &b->d_argmax, kMaxRows)) ||
+      (rc = dev_alloc(e, &b->h, static_cast<size_t>(kMaxRows) * H)) ||
+      (rc = dev_alloc(e, &b->h1, static_cast<size_t>(kMaxRows) * H)) ||
+      (rc = dev_alloc(e, &b->qkv, static_cast<size_t>(kMaxRows) * QKV)) ||
+      (rc = dev_alloc(e, &b->xn, static_cast<size_t>(kMaxRows) * H * 2)) ||
+      (rc = dev_alloc(e, &b->att, static_cast<size_t>(kMaxRows) * H * 2)) ||
+      (rc = dev_alloc(e, &b->act, static_cast<size_t>(kMaxRows) * I * 2)) ||
+      (rc = dev_alloc(e, &b->scratch, scratch)) ||
+      (rc = dev_alloc(e, &b->part_val, static_cast<size_t>(b->lm_tiles) * kMaxRows)) ||
+      (rc = dev_alloc(e, &b->part_idx, static_cast<size_t>(b->lm_tiles) * kMaxRows)))
+    return rc;
+  HB_CUDA(e, cudaMallocHost(reinterpret_cast<void **>(&b->h_meta), sizeof(int) * 3 * kMaxRows));
+  HB_CUDA(e, cudaMallocHost(reinterpret_cast<void **>(&b->h_argmax), sizeof(int) * kMaxRows));
+  HB_CUDA(e, cudaMallocHost(reinterpret_cast<void **>(&b->h_ctrl), sizeof(hb::Ctrl)));
+  return HB_OK;
+}
+
+// One tensor-core GEMM of the step: W (packed, rows x K) times the packed
+// rows `x`, epilogue EPI.
+template <int EPI>
+int gemm(hb_engine *e, const uint8_t *w, int rows, int K, const uint8_t *x, int n, hb::tc::GemmParams P) {
+  hb_batch *b = e->batch;
+  const GemmShape g = gemm_shape(rows, K, n, b->sms);
+  P.w = w;
+  P.x = x;
+  P.rows = rows;
+  P.K = K;
+  P.N = n;
+  P.npad = g.npad;
+  P.tiles = g.tiles;
+  P.ksplit = g.ksplit;
+  P.kst = g.kst;
+  P.stages = g.stages;
+  P.ws = g.ksplit > 1 ? batch_ws(b) : nullptr;
+  P.cnt = batch_cnt(b);
+  P.ctrl = batch_ctrl(b);
+  P.limit_ns = e->limit_ns;
+  const size_t smem = hb::tc::gemm_smem_bytes(g.stages, g.npad);
+  if (b->attr_smem[EPI] < smem) {
+    // opt in once per engine (the attribute is per device) for the largest
+    // shared-memory size the ring sizing can ask for
+    const size_t want = std::max(smem, static_cast<size_t>(200 * 1024));
+    HB_CUDA(e, cudaFuncSetAttribute(hb::tc::gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(want)));
+    b->attr_smem[EPI] = want;
+  }
+  hb::tc::gemm_kernel<EPI><<<g.tiles * g.ksplit, hb::tc::kThreads, smem, e->stream>>>(P);
+  HB_CUDA(e, cudaGetLastError());
+  return HB_OK;
+}
+
+// The whole model over n rows: row i is token tok[i] at position pos[i] of
+// KV slot slot[i] (the host has checked them).  Leaves each row's argmax
+// in b->h_argmax (and FP32 logits when want_logits).
+int batch_forward(hb_engine *e, int n, bool want_logits) {
+  hb_batch *b = e->batch;
+  const hb_model_desc &d = e->desc;
+  const int H = d.hidden, I = d.intermediate, QKV = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
+  const int group = d.q_heads / d.kv_heads;
+  cudaStream_t st = e->stream;
+  HB_CUDA(e, cudaMemsetAsync(b->scratch, 0, kCtrlBytes, st));
+  HB_CUDA(e, cudaMemcpyAsync(b->d_meta, b->h_meta, sizeof(int) * 3 * kMaxRows, cudaMemcpyHostToDevice, st));
+  hb::tc::Rows R{b->d_meta, b->d_meta + kMaxRows, b->d_meta + 2 * kMaxRows};
+  const auto *embed = reinterpret_cast<const __nv_bfloat16 *>(e->d_blob + d.embedding);
+  hb::tc::embed_kernel<<<n, 128, 0, st>>>(embed, R.tok, H, b->h);
+  hb::tc::KvArgs A{};
+  A.qkv = b->qkv;
+  A.QKV = QKV;
+  A.QH = d.q_heads;
+  A.KVH = d.kv_heads;
+  A.group = group;
+  A.H = H;
+  A.cos = e->d_rope_cos;
+  A.sin = e->d_rope_sin;
+  A.kv = e->d_kv;
+  A.L = d.layers;
+  A.ctx = d.context;
+  const size_t att_smem = static_cast<size_t>(2) * d.context * 128 + static_cast<size_t>(group) * 512;
+  int rc;
+  for (int l = 0; l < d.layers; ++l) {
+    const hb::LayerPtrs &lp = e->layer_ptrs[l];
+    hb::tc::norm_pack_kernel<<<n, 128, 0, st>>>(b->h, lp.gamma_in, d.rms_eps, H, b->xn);
+    hb::tc::GemmParams P{};
+    P.bias = d.has_qkv_bias ? lp.bias : nullptr;
+    P.out = b->qkv;
+    if ((rc = gemm<hb::tc::kEpiBias>(e, lp.w_qkv, QKV, H, b->xn, n, P))) return rc;
+    A.layer = l;
+    hb::tc::kv_append_kernel<<<dim3(n, d.kv_heads), 32, 0, st>>>(A, R);
+    hb::tc::attention_kernel<<<dim3(n, d.kv_heads), 32 * group, att_smem, st>>>(A, R, b->att);
+    P = hb::tc::GemmParams{};
+    P.resid = b->h;
+    P.out = b->h1;
+    if ((rc = gemm<hb::tc::kEpiResid>(e, lp.w_o, H, H, b->att, n, P))) return rc;
+    hb::tc::norm_pack_kernel<<<n, 128, 0, st>>>(b->h1, lp.gamma_post, d.rms_eps, H, b->xn);
+    P = hb::tc::GemmParams{};
+    P.out = reinterpret_cast<__nv_bfloat16 *>(b->act);
+    if ((rc = gemm<hb::tc::kEpiSwiglu>(e, lp.w_gu, 2 * I, H, b->xn, n, P))) return rc;
+    P = hb::tc::GemmParams{};
+    P.resid = b->h1;
+    P.out = b->h;
+    if ((rc = gemm<hb::tc::kEpiResid>(e, lp.w_down, H, I, b->act, n, P))) return rc;
+  }
+  hb::tc::norm_pack_kernel<<<n, 128, 0, st>>>(b->h, reinterpret_cast<const float *>(e->d_blob + d.gamma_final),
+                                               d.rms_eps, H, b->xn);
+  hb::tc::GemmParams P{};
+  P.y = want_logits ? b->logits : nullptr;
+  P.part_val = b->part_val;
+  P.part_idx = b->part_idx;
+  P.pstride = kMaxRows;
+  if ((rc = gemm<hb::tc::kEpiLogits>(e, e->d_blob + d.w_lm, d.vocab, H, b->xn, n, P))) return rc;
+  hb::tc::argmax_reduce_kernel<<<n, 256, 0, st>>>(b->part_val, b->part_idx, b->lm_tiles, kMaxRows, b->d_argmax);
+  HB_CUDA(e, cudaGetLastError());
+  HB_CUDA(e, cudaMemcpyAsync(b->h_argmax, b->d_argmax, sizeof(int) * n, cudaMemcpyDeviceToHost, st));
+  HB_CUDA(e, cudaMemcpyAsync(b->h_ctrl, b->scratch, sizeof(hb::Ctrl), cudaMemcpyDeviceToHost, st));
+  HB_CUDA(e, cudaStreamSynchronize(st));
+  if (b->h_ctrl->err == hb::kErrTimeout)
+    return fail(e, HB_ERR_DEVICE_TIMEOUT, "batched step: a device wait gave up (where %d)", b->h_ctrl->err_where);
+  if (b->h_ctrl->err) return fail(e, HB_ERR_STATE, "batched step: device error %d", b->h_ctrl->err);
+  return HB_OK;
+}
+
+// Checks shared by the batched entry points; makes the engine's device current.
+int batch_check(hb_engine *e, int n) {
+  if (!e) return fail(nullptr, HB_ERR_INVALID_ARG, "engine is NULL");
+  if (!e->loaded) return fail(e, HB_ERR_STATE, "weights not loaded");
+  if (e->desc.weight_format != HB_WEIGHTS_BF16)
+    return fail(e, HB_ERR_UNSUPPORTED, "the batched tensor-core step needs BF16 weights");
+  if (e->paged) return fail(e, HB_ERR_UNSUPPORTED, "the batched tensor-core step needs the 64-position cache");
+  if (n < 1 || n > kMaxRows) return fail(e, HB_ERR_INVALID_ARG, "n must be in [1, %d]", kMaxRows);
+  const hb_model_desc &d = e->desc;
+  if (d.hidden % hb::tc::kStageK || d.intermediate % hb::tc::kStageK)
+    return fail(e, HB_ERR_UNSUPPORTED, "hidden and intermediate must be multiples of 64");
+  return HB_OK;
+}
+
+}  // namespace
+
 namespace hbi {
-void batch_release(hb_engine *) {}
+void batch_release(hb_engine *e) {
+  hb_batch *b = e->batch;
+  if (!b) return;
+  void *dev[] = {b->d_meta, b->d_argmax, b->h, b->h1, b->qkv, b->xn, b->att, b->act, b->scratch,
+                 b->part_val, b->part_idx, b->logits};
+  for (void *p : dev)
+    if (p) cudaFree(p);
+  void *host[] = {b->h_meta, b->h_argmax, b->h_ctrl};
+  for (void *p : host)
+    if (p) cudaFreeHost(p);
+  delete b;
+  e->batch = nullptr;
+}
 }  // namespace hbi
 
 extern "C" {
@@ -107,11 +303,74 @@ int hb_tc_gemm(const void *w_dev, int rows, int k, const void *x_dev, int n, flo
                      : nullptr;
   P.limit_ns = kDefaultLimitNs;
   const size_t smem = hb::tc::gemm_smem_bytes(g.stages, g.npad);
-  HB_CUDA(nullptr, cudaFuncSetAttribute(hb::tc::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(smem)));
-  hb::tc::gemm_kernel<<<g.tiles * g.ksplit, hb::tc::kThreads, smem, st>>>(P);
+  HB_CUDA(nullptr, cudaFuncSetAttribute(hb::tc::gemm_kernel<hb::tc::kEpiF32>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  hb::tc::gemm_kernel<hb::tc::kEpiF32><<<g.tiles * g.ksplit, hb::tc::kThreads, smem, st>>>(P);
   HB_CUDA(nullptr, cudaGetLastError());
   return HB_OK;
+}
+
+int hb_step_rows(hb_engine *e, int n, const int32_t *slots, const int32_t *token_ids, const int32_t *positions,
+                 int32_t *argmax_out, float *logits_out) {
+  int rc = batch_check(e, n);
+  if (rc) return rc;
+  DeviceScope device_scope_(e->device);
+  if (!device_scope_.ok) return fail(e, HB_ERR_CUDA, "cudaSetDevice(%d) failed", e->device);
+  if (!slots || !token_ids || !positions) return fail(e, HB_ERR_INVALID_ARG, "rows are NULL");
+  const hb_model_desc &d = e->desc;
+  for (int i = 0; i < n; ++i) {
+    if (slots[i] < 0 || slots[i] >= d.max_slots)
+      return fail(e, HB_ERR_INVALID_ARG, "row %d: slot %d outside [0, %d)", i, slots[i], d.max_slots);
+    if (token_ids[i] < 0 || token_ids[i] >= d.vocab)
+      return fail(e, HB_ERR_INVALID_ARG, "row %d: token id %d outside the vocabulary", i, token_ids[i]);
+    if (positions[i] < 0 || positions[i] >= d.context)
+      return fail(e, HB_ERR_INVALID_ARG, "row %d: position outside the %d-token context", i, d.context);
+    for (int k = 0; k < i; ++k)
+      if (slots[k] == slots[i] && positions[k] == positions[i])
+        return fail(e, HB_ERR_INVALID_ARG, "rows %d and %d write the same slot position", k, i);
+  }
+  if ((rc = batch_setup(e))) return rc;
+  hb_batch *b = e->batch;
+  if (logits_out && !b->logits && (rc = dev_alloc(e, &b->logits, static_cast<size_t>(kMaxRows) * d.vocab)))
+    return rc;
+  for (int i = 0; i < n; ++i) {
+    b->h_meta[i] = slots[i];
+    b->h_meta[kMaxRows + i] = positions[i];
+    b->h_meta[2 * kMaxRows + i] = token_ids[i];
+  }
+  if ((rc = batch_forward(e, n, logits_out != nullptr))) return rc;
+  if (argmax_out)
+    for (int i = 0; i < n; ++i) argmax_out[i] = b->h_argmax[i];
+  if (logits_out)
+    HB_CUDA(e, cudaMemcpy(logits_out, b->logits, sizeof(float) * n * d.vocab, cudaMemcpyDeviceToHost));
+  return HB_OK;
+}
+
+int hb_prefill_tc(hb_engine *e, int slot, const int32_t *ids, int n, int start_pos, float *last_logits,
+                  int32_t *argmax_out) {
+  if (!ids || n < 1) return fail(e, HB_ERR_INVALID_ARG, "ids must hold at least one token");
+  std::vector<int32_t> slots(kMaxRows, slot), pos(kMaxRows);
+  int rc = HB_OK;
+  for (int done = 0; done < n && rc == HB_OK;) {
+    const int m = std::min(kMaxRows, n - done);
+    for (int i = 0; i < m; ++i) pos[i] = start_pos + done + i;
+    const bool last = done + m == n;
+    std::vector<int32_t> am(m);
+    std::vector<float> lg;
+    float *lp = nullptr;
+    if (last && last_logits) {
+      lg.resize(static_cast<size_t>(m) * e->desc.vocab);
+      lp = lg.data();
+    }
+    rc = hb_step_rows(e, m, slots.data(), ids + done, pos.data(), am.data(), lp);
+    if (rc == HB_OK && last) {
+      if (argmax_out) *argmax_out = am[m - 1];
+      if (last_logits)
+        std::memcpy(last_logits, lg.data() + static_cast<size_t>(m - 1) * e->desc.vocab, sizeof(float) * e->desc.vocab);
+    }
+    done += m;
+  }
+  return rc;
 }
 
 int hb_tc_gemm_status(const void *scratch_dev, void *stream) {

@@ -22,7 +22,7 @@
 // drains what it issued, frees TMEM and returns.
 #pragma once
 
-#include "hb_device.cuh"
+#include "hb_attn.cuh"
 
 namespace hb {
 namespace tc {
@@ -33,6 +33,7 @@ constexpr int kStageK = 64;                    // K elements per stage (8 chunk 
 constexpr uint32_t kGroupStageBytes = 1024;    // one row group's 8 chunk columns
 constexpr uint32_t kAStageBytes = 16 * kGroupStageBytes;
 constexpr int kMaxN = 256;
+constexpr int kHeadDimTc = 64;
 
 // ---- tcgen05 PTX --------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols) {
@@ -105,7 +106,13 @@ struct GemmParams {
   int npad;           // N rounded up to 16 (the MMA's N)
   int tiles, ksplit, kst;     // kst: K stages (K / 64) in all; slice s takes [s kst / ksplit, (s + 1) kst / ksplit)
   int stages;
-  float *y;           // [N][rows] FP32 out
+  float *y;           // kEpiF32: [N][rows] FP32 out; kEpiLogits: optional FP32 logits [N][rows]
+  const float *bias;  // kEpiBias: [rows] FP32 (nullptr: none)
+  const __nv_bfloat16 *resid;  // kEpiResid: [N][rows] BF16
+  __nv_bfloat16 *out;  // kEpiBias / kEpiResid: [N][rows] BF16; kEpiSwiglu: packed [N][rows / 2]
+  float *part_val;    // kEpiLogits: [tiles][pstride] per-tile maxima
+  int *part_idx;
+  int pstride;
   float *ws;          // [tiles][ksplit][npad][128] FP32 partials (ksplit > 1)
   unsigned int *cnt;  // [tiles] slice arrivals (reset by the last)
   Ctrl *ctrl;
@@ -116,6 +123,15 @@ __host__ __device__ inline size_t gemm_smem_bytes(int stages, int npad) {
   return static_cast<size_t>(stages) * (kAStageBytes + static_cast<size_t>(npad) * 128) + 16 * stages + 64;
 }
 
+// What a GEMM does with y[n][r] (cpu_backend.py rounding points):
+enum : int {
+  kEpiF32 = 0,     // y -> FP32 [N][rows]
+  kEpiBias = 1,    // bf16(bf16(y) + bias[r]) -> BF16 [N][rows]          (qkv, :134-143)
+  kEpiResid = 2,   // bf16(bf16(y) + resid[n][r]) -> BF16 [N][rows]      (o / down, :145-151, :166-171)
+  kEpiSwiglu = 3,  // rows are gate / up row-group pairs: bf16(silu(bf16 g) * bf16 u) -> packed act (:154-165)
+  kEpiLogits = 4,  // FP32 logits (optional) and each row's maximum over the tile (np.argmax order)
+};
+
 // Bounded wait that does not raise on abort (cleanup paths).
 __device__ __forceinline__ void mbar_wait_quiet(uint64_t *bar, uint32_t parity, uint64_t limit_ns) {
   const uint64_t start = globaltimer_ns();
@@ -124,6 +140,7 @@ __device__ __forceinline__ void mbar_wait_quiet(uint64_t *bar, uint32_t parity, 
   }
 }
 
+template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ GemmParams P) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int S = P.stages;
@@ -208,21 +225,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   const bool ok = __syncthreads_and(mbar_wait(done, 0, P.ctrl, P.limit_ns, kWhereFull) &&
                                     ld_volatile_int(&P.ctrl->abort) == 0) != 0;
   tc_fence_after();
-  const int row = g0 * 8 + warp * 32 + lane;  // this thread's weight row
+  const int r_t = warp * 32 + lane;  // this thread's row within the tile (its TMEM lane)
   const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  // the ring is idle now (every copy landed, every MMA done): its space
+  // stages the tile's FP32 results [npad][128]
+  float *stage = reinterpret_cast<float *>(smem);
+  float *part = P.ksplit > 1 ? P.ws + (static_cast<size_t>(tile) * P.ksplit + split) * P.npad * kTileRows : nullptr;
   if (ok) {
-    float *part = P.ksplit > 1 ? P.ws + (static_cast<size_t>(tile) * P.ksplit + split) * P.npad * kTileRows : nullptr;
     for (int c0 = 0; c0 < P.npad; c0 += 16) {
       uint32_t v[16];
       tmem_ld16(taddr + c0, v);
       tmem_ld_wait();
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const int n = c0 + j;
         if (part != nullptr) {
-          part[static_cast<size_t>(n) * kTileRows + warp * 32 + lane] = __uint_as_float(v[j]);
-        } else if (n < P.N && row < P.rows) {
-          P.y[static_cast<size_t>(n) * P.rows + row] = __uint_as_float(v[j]);
+          part[static_cast<size_t>(c0 + j) * kTileRows + r_t] = __uint_as_float(v[j]);
+        } else {
+          stage[(c0 + j) * kTileRows + r_t] = __uint_as_float(v[j]);
         }
       }
     }
@@ -230,24 +249,222 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, ncols);
-  if (!ok || P.ksplit == 1) return;
-  // split-K: the last slice to arrive sums the slices in order
-  if (threadIdx.x == 0) {
+  if (!ok) return;
+  if (P.ksplit > 1) {
+    // the last slice to arrive sums the slices in order
+    if (threadIdx.x == 0) {
+      __threadfence();
+      *s_flag = atomicAdd(&P.cnt[tile], 1u) == static_cast<unsigned>(P.ksplit - 1) ? 1 : 0;
+    }
+    __syncthreads();
+    if (*s_flag == 0) return;
     __threadfence();
-    *s_flag = atomicAdd(&P.cnt[tile], 1u) == static_cast<unsigned>(P.ksplit - 1) ? 1 : 0;
-  }
-  __syncthreads();
-  if (*s_flag == 0) return;
-  __threadfence();
-  if (threadIdx.x == 0) P.cnt[tile] = 0u;
-  const float *base = P.ws + static_cast<size_t>(tile) * P.ksplit * P.npad * kTileRows;
-  if (row < P.rows) {
+    if (threadIdx.x == 0) P.cnt[tile] = 0u;
+    const float *base = P.ws + static_cast<size_t>(tile) * P.ksplit * P.npad * kTileRows;
     for (int n = 0; n < P.N; ++n) {
       float acc = 0.f;
-      for (int s2 = 0; s2 < P.ksplit; ++s2)
-        acc += __ldcg(base + (static_cast<size_t>(s2) * P.npad + n) * kTileRows + warp * 32 + lane);
-      P.y[static_cast<size_t>(n) * P.rows + row] = acc;
+      for (int s2 = 0; s2 < P.ksplit; ++s2) acc += __ldcg(base + (static_cast<size_t>(s2) * P.npad + n) * kTileRows + r_t);
+      stage[n * kTileRows + r_t] = acc;
     }
+  }
+  __syncthreads();
+  const int row0 = g0 * 8;
+  if constexpr (EPI == kEpiF32 || EPI == kEpiBias || EPI == kEpiResid) {
+    for (int idx = threadIdx.x; idx < P.N * kTileRows; idx += kThreads) {
+      const int n = idx >> 7, row = row0 + (idx & 127);
+      if (row >= P.rows) continue;
+      const float v = stage[idx];
+      const size_t o = static_cast<size_t>(n) * P.rows + row;
+      if constexpr (EPI == kEpiF32) {
+        P.y[o] = v;
+      } else if constexpr (EPI == kEpiBias) {
+        float yv = rbf(v);
+        if (P.bias != nullptr) yv = __fadd_rn(yv, P.bias[row]);
+        P.out[o] = f2bf(yv);
+      } else {
+        P.out[o] = f2bf(__fadd_rn(rbf(v), bf2f(P.resid[o])));
+      }
+    }
+  } else if constexpr (EPI == kEpiSwiglu) {
+    // pair q of the tile: gate rows q*16 + rr, up rows q*16 + 8 + rr, act
+    // column (row0 / 16 + q) * 8 + rr; 8 outputs = one 16-byte chunk
+    const int inter = P.rows / 2, kc = inter / 8;
+    for (int idx = threadIdx.x; idx < P.N * 8; idx += kThreads) {
+      const int n = idx >> 3, q = idx & 7;
+      if (row0 + q * 16 >= P.rows) continue;
+      uint32_t w4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float a[2];
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int rr = 2 * e + h2;
+          const float g = rbf(stage[n * kTileRows + q * 16 + rr]);
+          const float u = rbf(stage[n * kTileRows + q * 16 + 8 + rr]);
+          const float ex = expf(-fminf(fmaxf(g, -80.f), 80.f));
+          a[h2] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, ex)), u);
+        }
+        w4[e] = pack_bf16x2(a[0], a[1]);
+      }
+      uint8_t *dst = reinterpret_cast<uint8_t *>(P.out) +
+                     (static_cast<size_t>(n >> 3) * kc + (row0 / 16 + q)) * 128 + (n & 7) * 16;
+      *reinterpret_cast<uint4 *>(dst) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    }
+  } else if constexpr (EPI == kEpiLogits) {
+    for (int n = warp; n < P.N; n += kThreads / 32) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int r = lane; r < kTileRows; r += 32) {
+        const int row = row0 + r;
+        if (row >= P.rows) break;
+        const float v = stage[n * kTileRows + r];
+        if (P.y != nullptr) P.y[static_cast<size_t>(n) * P.rows + row] = v;
+        if (argmax_better(v, row, bv, bi)) {
+          bv = v;
+          bi = row;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        argmax_merge(bv, bi, ov, oi);
+      }
+      if (lane == 0) {
+        P.part_val[static_cast<size_t>(tile) * P.pstride + n] = bv;
+        P.part_idx[static_cast<size_t>(tile) * P.pstride + n] = bi;
+      }
+    }
+  }
+}
+
+// ---- per-row kernels of the batched step ---------------------------------------
+// Row metadata of a batched step (device arrays of n entries).
+struct Rows {
+  const int *slot, *pos, *tok;
+};
+
+// h[n][:] = the embedding row of token tok[n] (generate.py:758-768).
+__global__ void embed_kernel(const __nv_bfloat16 *embed, const int *tok, int H, __nv_bfloat16 *h) {
+  const int n = blockIdx.x;
+  const uint4 *src = reinterpret_cast<const uint4 *>(embed + static_cast<size_t>(tok[n]) * H);
+  uint4 *dst = reinterpret_cast<uint4 *>(h + static_cast<size_t>(n) * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = __ldg(src + i);
+}
+
+// out (packed row-group layout) = bf16((x * inv_rms) * gamma) of row n of x
+// (cpu_backend.py:71-76), one CTA of 128 threads per row.
+__global__ void norm_pack_kernel(const __nv_bfloat16 *x, const float *gamma, float eps, int H, uint8_t *out) {
+  __shared__ float part[4];
+  const int n = blockIdx.x, tid = threadIdx.x;
+  const uint32_t *row = reinterpret_cast<const uint32_t *>(x + static_cast<size_t>(n) * H);
+  float ss = 0.f;
+  for (int i = tid; i < H / 2; i += blockDim.x) {
+    const uint32_t w = row[i];
+    ss = fmaf(bf_lo(w), bf_lo(w), ss);
+    ss = fmaf(bf_hi(w), bf_hi(w), ss);
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) part[tid >> 5] = ss;
+  __syncthreads();
+  const float total = (part[0] + part[1]) + (part[2] + part[3]);
+  const float mean = __fdiv_rn(total, static_cast<float>(H));
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  const int kc = H / 8;
+  for (int c = tid; c < kc; c += blockDim.x) {
+    const uint4 w = reinterpret_cast<const uint4 *>(row)[c];
+    const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float a = __fmul_rn(__fmul_rn(bf_lo(in[e]), inv), gamma[8 * c + 2 * e]);
+      const float b = __fmul_rn(__fmul_rn(bf_hi(in[e]), inv), gamma[8 * c + 2 * e + 1]);
+      o[e] = pack_bf16x2(a, b);
+    }
+    *reinterpret_cast<uint4 *>(out + (static_cast<size_t>(n >> 3) * kc + c) * 128 + (n & 7) * 16) =
+        make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+struct KvArgs {
+  const __nv_bfloat16 *qkv;  // [N][QKV] BF16 (biased q / k / v)
+  int QKV, QH, KVH, group, H;
+  const float *cos, *sin;    // [ctx][32]
+  __nv_bfloat16 *kv;         // [slots][L][KVH][K | V][ctx][64], swizzled rows
+  int L, layer, ctx;
+};
+
+__device__ __forceinline__ uint8_t *kv_rows(const KvArgs &A, int slot, int j, int kind) {
+  return reinterpret_cast<uint8_t *>(A.kv) +
+         ((((static_cast<size_t>(slot) * A.L + A.layer) * A.KVH + j) * 2 + kind) * A.ctx * kHeadDimTc) * 2;
+}
+
+// Rotates each row's k and appends its K and V rows to its slot's cache at
+// its position (grid: rows x kv heads, one warp), before any row attends:
+// rows of one sequence in the same step see each other's keys.
+__global__ void kv_append_kernel(const __grid_constant__ KvArgs A, Rows R) {
+  const int n = blockIdx.x, j = blockIdx.y, lane = threadIdx.x;
+  const int p = R.pos[n], slot = R.slot[n];
+  const uint32_t *row = reinterpret_cast<const uint32_t *>(A.qkv + static_cast<size_t>(n) * A.QKV);
+  __nv_bfloat16 lo, hi;
+  rope_pair_cs(row + (A.QH + j) * 32, lane, A.cos[p * 32 + lane], A.sin[p * 32 + lane], lo, hi);
+  put_kv(kv_rows(A, slot, j, 0), kv_rows(A, slot, j, 1), p, lane, lo, hi, row[(A.QH + A.KVH + j) * 32 + lane]);
+}
+
+// Attention of every (row, q head): a CTA per (row, kv head) copies that kv
+// head's K / V rows 0..pos into shared memory; warp w attends q head
+// j * group + w with attend_warp() and writes its 64 outputs into the
+// o-projection's packed input.
+__global__ void attention_kernel(const __grid_constant__ KvArgs A, Rows R, uint8_t *att) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  const int n = blockIdx.x, j = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int p = R.pos[n], slot = R.slot[n];
+  uint8_t *kb = sm, *vb = sm + static_cast<size_t>(A.ctx) * 128;
+  float *qf = reinterpret_cast<float *>(sm + static_cast<size_t>(2) * A.ctx * 128) + warp * 128;
+  const int pieces = (p + 1) * 8;  // 16-byte pieces of positions 0..p
+  const uint8_t *ks = kv_rows(A, slot, j, 0), *vs = kv_rows(A, slot, j, 1);
+  for (int i = threadIdx.x; i < 2 * pieces; i += blockDim.x) {
+    const int kind = i >= pieces ? 1 : 0, off = (i - kind * pieces) * 16;
+    cp_async16((kind ? vb : kb) + off, (kind ? vs : ks) + off);
+  }
+  cp_async_commit();
+  const int h = j * A.group + warp;
+  const uint32_t *row = reinterpret_cast<const uint32_t *>(A.qkv + static_cast<size_t>(n) * A.QKV);
+  __nv_bfloat16 lo, hi;
+  rope_pair_cs(row + h * 32, lane, A.cos[p * 32 + lane], A.sin[p * 32 + lane], lo, hi);
+  qf[lane] = bf2f(lo);
+  qf[lane + 32] = bf2f(hi);
+  cp_async_wait_all();
+  __syncthreads();
+  const uint32_t o = attend_warp(qf, qf + 64, kb, vb, p);
+  const int c = h * 64 + 2 * lane;  // output column of this lane's pair
+  *reinterpret_cast<uint32_t *>(att + (static_cast<size_t>(n >> 3) * (A.H / 8) + (c >> 3)) * 128 + (n & 7) * 16 +
+                                (c & 7) * 2) = o;
+}
+
+// out[n] = argmax over the LM head's tiles of row n (np.argmax order).
+__global__ void argmax_reduce_kernel(const float *pv, const int *pi, int tiles, int pstride, int *out) {
+  __shared__ float sv[8];
+  __shared__ int si[8];
+  const int n = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int t = threadIdx.x; t < tiles; t += blockDim.x)
+    argmax_merge(bv, bi, pv[static_cast<size_t>(t) * pstride + n], pi[static_cast<size_t>(t) * pstride + n]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    argmax_merge(bv, bi, ov, oi);
+  }
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x / 32); ++w) argmax_merge(bv, bi, sv[w], si[w]);
+    out[n] = bi;
   }
 }
 

@@ -216,6 +216,41 @@ class B200DecoderEngine:
             am.ctypes.data_as(ip)))
         return am, out
 
+    # -- batched tensor-core path (hb_step_rows / hb_prefill_tc) ----------------
+    MAX_ROWS = 128
+
+    def step_rows(self, slots, tokens, positions, logits=False):
+        """Up to 128 rows through the whole model on the tensor cores (row i:
+        tokens[i] at positions[i] of KV slot slots[i]); rows may be several
+        consecutive positions of one sequence.  Returns (argmax per row, FP32
+        logits [rows, vocab] or None).  BF16 weights, 64-position cache."""
+        h = self._live()
+        n = len(slots)
+        s = np.ascontiguousarray(slots, np.int32)
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(positions, np.int32)
+        if not (s.size == t.size == p.size == n):
+            raise ValueError("slots, tokens and positions must have the same length")
+        out = np.empty((n, self.vocab), np.float32) if logits else None
+        am = np.empty(n, np.int32)
+        ip = ctypes.POINTER(ctypes.c_int32)
+        self._check(self._lib.hb_step_rows(
+            h, n, s.ctypes.data_as(ip), t.ctypes.data_as(ip), p.ctypes.data_as(ip), am.ctypes.data_as(ip),
+            out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)) if logits else None))
+        return am, out
+
+    def prefill_tc(self, ids, start=0, slot=0, logits=False):
+        """Prefill of ``ids`` at positions start.. in one batched
+        tensor-core pass; (argmax of the last position, its logits or None)."""
+        h = self._live()
+        ids = np.ascontiguousarray(ids, np.int32)
+        out = np.empty(self.vocab, np.float32) if logits else None
+        self._check(self._lib.hb_prefill_tc(
+            h, slot, ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), ids.size, int(start),
+            out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)) if logits else None,
+            ctypes.byref(self._argmax)))
+        return int(self._argmax.value), out
+
     def sample_batch(self, rows, params, histories, uniforms):
         """Device selections for several rows of the last ``step_batch(...,
         device_logits=True)`` in one launch; a token per entry, None where the

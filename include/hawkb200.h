@@ -303,6 +303,32 @@ int hb_tc_gemm(const void *w_dev, int rows, int k, const void *x_dev, int n, flo
                size_t scratch_bytes, void *stream);
 int hb_tc_gemm_status(const void *scratch_dev, void *stream);
 
+/* ---- batched step on the tensor cores (new in this build) -------------------
+ * n rows (1 <= n <= 128) through every layer, the final norm and the LM
+ * head in one call: row i feeds token_ids[i] at positions[i] of KV slot
+ * slots[i] and returns its argmax in argmax_out[i] (and, when logits_out is
+ * not NULL, its FP32 logits in logits_out[i * vocab ...]).  Rows may mix
+ * sequences (multi-stream decode) and may hold consecutive positions of one
+ * sequence (chunked prefill): every row's K/V is appended before any row
+ * attends, so a row sees the rows of its sequence at earlier positions.  No
+ * two rows may write the same (slot, position).  Per layer: RMSNorm, qkv
+ * (tcgen05 GEMM + bias), RoPE and K/V append, attention, o (GEMM +
+ * residual), RMSNorm, gate/up (GEMM + SwiGLU), down (GEMM + residual), with
+ * the reference's BF16 rounding points (npu_llm/runtime/cpu_backend.py:131-181);
+ * FP32 sums run in a different order than the persistent kernel's, so
+ * results agree with hb_step to the documented tolerance, not bit for bit.
+ * BF16 weights and the 64-position cache only (HB_ERR_UNSUPPORTED otherwise).
+ * Replaces the reference's one dispatch per position
+ * (npu_llm/runtime/generate.py:1110-1126) and its single-lock serving
+ * (npu_llm/api_server.py:646-678) for the rows it batches. */
+int hb_step_rows(hb_engine *engine, int n, const int32_t *slots, const int32_t *token_ids,
+                 const int32_t *positions, int32_t *argmax_out, float *logits_out);
+/* Prefill of positions start_pos .. start_pos + n - 1 of one slot through
+ * hb_step_rows (128 rows per launch sequence); the last position's argmax and,
+ * when last_logits is not NULL, its FP32 logits. */
+int hb_prefill_tc(hb_engine *engine, int slot, const int32_t *ids, int n, int start_pos, float *last_logits,
+                  int32_t *argmax_out);
+
 /* Library-level error text (for calls that have no engine, e.g. hb_gemv). */
 const char *hb_library_error(void);
 
