@@ -7,6 +7,8 @@
 // sequence of kernels per layer around tcgen05 GEMMs (hb_tc.cuh): the
 // weights stream once per step for up to 128 rows, accumulate in TMEM, and
 // the epilogues apply the reference's BF16 rounding points.
+#include <unordered_map>
+
 #include "hb_engine_impl.h"
 #include "hb_tc.cuh"
 
@@ -14,11 +16,13 @@ using namespace hbi;
 
 namespace {
 
-// K slices per tile so that tiles x slices roughly fills the GPU, each slice
-// at least two K stages when the matrix has them.
-int choose_ksplit(int tiles, int kst, int sms) {
-  int ks = (sms + tiles - 1) / tiles;
+// K slices per tile so that tiles x slices fills at most one wave, each slice
+// at least two K stages, and the FP32 partials (slices x npad x 4 bytes per
+// weight row) at most half the weight bytes (K x 2 per row).
+int choose_ksplit(int tiles, int kst, int sms, int npad) {
+  int ks = sms / tiles;  // one wave: a second partial wave doubles the time
   ks = std::min(ks, kst >= 2 ? kst / 2 : 1);
+  ks = std::min(ks, 16 * kst / npad);
   return std::max(ks, 1);
 }
 
@@ -37,8 +41,8 @@ GemmShape gemm_shape(int rows, int k, int n, int sms) {
   GemmShape g{};
   g.tiles = (rows + hb::tc::kTileRows - 1) / hb::tc::kTileRows;
   g.kst = k / hb::tc::kStageK;
-  g.ksplit = choose_ksplit(g.tiles, g.kst, sms);
   g.npad = hb::tc::pad_n(n);
+  g.ksplit = choose_ksplit(g.tiles, g.kst, sms, g.npad);
   g.stages = choose_stages(g.npad);
   g.ws_floats = g.ksplit > 1 ? static_cast<size_t>(g.tiles) * g.ksplit * g.npad * hb::tc::kTileRows : 0;
   return g;
@@ -48,6 +52,55 @@ constexpr size_t kCtrlBytes = 256;
 
 size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled from the driver the runtime loaded (no link to
+// libcuda); NULL when the driver has none.
+EncodeTiled encode_tiled() {
+  static const EncodeTiled fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    cudaGetLastError();
+    return reinterpret_cast<EncodeTiled>(p);
+  }();
+  return fn;
+}
+
+// The GEMM's 3-D view of a packed matrix of `groups` row groups x K columns:
+// 32-bit words {256 (a row group's 1 KB per 64-column stage), K / 64 stages,
+// row groups}, box {256, 1, box_groups}; boxes past the last row group read
+// zeros.  base is 16-byte aligned, K a multiple of 64.
+bool packed_map(CUtensorMap *m, const void *base, int K, int groups, int box_groups) {
+  const EncodeTiled fn = encode_tiled();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {256, static_cast<cuuint64_t>(K / hb::tc::kStageK), static_cast<cuuint64_t>(groups)};
+  const cuuint64_t strides[2] = {hb::tc::kGroupStageBytes, static_cast<cuuint64_t>(K) * 16};
+  const cuuint32_t box[3] = {256, 1, static_cast<cuuint32_t>(box_groups)};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void *>(base), dims, strides, box, estride,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Fills P's shape fields and tensor maps for W (rows x K) times n rows of x.
+bool gemm_params(hb::tc::GemmParams &P, const GemmShape &g, const void *w, int rows, int K, const void *x, int n) {
+  P.rows = rows;
+  P.K = K;
+  P.N = n;
+  P.npad = g.npad;
+  P.tiles = g.tiles;
+  P.ksplit = g.ksplit;
+  P.kst = g.kst;
+  P.stages = g.stages;
+  return packed_map(&P.map_w, w, K, (rows + 7) / 8, hb::tc::kTileRows / 8) &&
+         packed_map(&P.map_x, x, K, (n + 7) / 8, g.npad / 8);
+}
+
 }  // namespace
 
 // Device buffers of the batched path, sized for kMaxRows rows and
@@ -55,7 +108,7 @@ size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 constexpr int kMaxRows = 128;
 
 struct hb_batch {
-  int *d_meta = nullptr;            // slot [kMaxRows] | pos | tok
+  int *d_meta = nullptr;            // slot [kMaxRows] | pos | tok | output rows
   int *d_argmax = nullptr;          // [kMaxRows]
   __nv_bfloat16 *h = nullptr, *h1 = nullptr, *qkv = nullptr;  // row-major [kMaxRows][*]
   uint8_t *xn = nullptr, *att = nullptr, *act = nullptr;      // packed GEMM inputs
@@ -70,13 +123,17 @@ struct hb_batch {
   int *h_argmax = nullptr;
   hb::Ctrl *h_ctrl = nullptr;
   int sms = 0;
-  size_t attr_smem[5] = {0, 0, 0, 0, 0};  // shared memory each GEMM variant is opted into on this device
+  // the step's launch sequence, captured once per (rows, output rows,
+  // logits wanted); at most kMaxGraphs kept (all dropped when full)
+  std::unordered_map<uint32_t, cudaGraphExec_t> graphs;
 };
+
+constexpr size_t kMaxGraphs = 512;
+constexpr int kMetaWords = 4 * kMaxRows;
 
 namespace {
 
 hb::Ctrl *batch_ctrl(hb_batch *b) { return reinterpret_cast<hb::Ctrl *>(b->scratch); }
-unsigned int *batch_cnt(hb_batch *b) { return reinterpret_cast<unsigned int *>(b->scratch + kCtrlBytes); }
 float *batch_ws(hb_batch *b) {
   return reinterpret_cast<float *>(b->scratch + kCtrlBytes + align256(sizeof(unsigned int) * b->max_tiles));
 }
@@ -90,14 +147,16 @@ int batch_setup(hb_engine *e) {
   const int H = d.hidden, I = d.intermediate, QKV = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
   const int shapes[5][2] = {{QKV, H}, {H, H}, {2 * I, H}, {H, I}, {d.vocab, H}};
   for (const auto &sh : shapes) {
-    const GemmShape g = gemm_shape(sh[0], sh[1], kMaxRows, b->sms);
-    b->ws_floats = std::max(b->ws_floats, g.ws_floats);
-    b->max_tiles = std::max(b->max_tiles, g.tiles);
+    for (int n = 16; n <= kMaxRows; n += 16) {
+      const GemmShape g = gemm_shape(sh[0], sh[1], n, b->sms);
+      b->ws_floats = std::max(b->ws_floats, g.ws_floats);
+      b->max_tiles = std::max(b->max_tiles, g.tiles);
+    }
   }
   b->lm_tiles = (d.vocab + hb::tc::kTileRows - 1) / hb::tc::kTileRows;
   const size_t scratch = kCtrlBytes + align256(sizeof(unsigned int) * b->max_tiles) + b->ws_floats * sizeof(float);
   int rc;
-  if ((rc = dev_alloc(e, &b->d_meta, 3 * kMaxRows)) || (rc = dev_alloc(e, &b->d_argmax, kMaxRows)) ||
+  if ((rc = dev_alloc(e, &b->d_meta, kMetaWords)) || (rc = dev_alloc(e, &b->d_argmax, kMaxRows)) ||
       (rc = dev_alloc(e, &b->h, static_cast<size_t>(kMaxRows) * H)) ||
       (rc = dev_alloc(e, &b->h1, static_cast<size_t>(kMaxRows) * H)) ||
       (rc = dev_alloc(e, &b->qkv, static_cast<size_t>(kMaxRows) * QKV)) ||
@@ -108,9 +167,21 @@ int batch_setup(hb_engine *e) {
       (rc = dev_alloc(e, &b->part_val, static_cast<size_t>(b->lm_tiles) * kMaxRows)) ||
       (rc = dev_alloc(e, &b->part_idx, static_cast<size_t>(b->lm_tiles) * kMaxRows)))
     return rc;
-  HB_CUDA(e, cudaMallocHost(reinterpret_cast<void **>(&b->h_meta), sizeof(int) * 3 * kMaxRows));
+  HB_CUDA(e, cudaMallocHost(reinterpret_cast<void **>(&b->h_meta), sizeof(int) * kMetaWords));
   HB_CUDA(e, cudaMallocHost(reinterpret_cast<void **>(&b->h_argmax), sizeof(int) * kMaxRows));
   HB_CUDA(e, cudaMallocHost(reinterpret_cast<void **>(&b->h_ctrl), sizeof(hb::Ctrl)));
+  // opt every GEMM variant into the most shared memory any row count needs
+  // (outside any stream capture)
+  size_t smem = 0;
+  for (int n = 16; n <= kMaxRows; n += 16)
+    smem = std::max(smem, hb::tc::gemm_smem_bytes(choose_stages(n), n));
+  const void *fns[5] = {reinterpret_cast<const void *>(hb::tc::gemm_kernel<0>),
+                        reinterpret_cast<const void *>(hb::tc::gemm_kernel<1>),
+                        reinterpret_cast<const void *>(hb::tc::gemm_kernel<2>),
+                        reinterpret_cast<const void *>(hb::tc::gemm_kernel<3>),
+                        reinterpret_cast<const void *>(hb::tc::gemm_kernel<4>)};
+  for (const void *fn : fns)
+    HB_CUDA(e, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   return HB_OK;
 }
 
@@ -120,45 +191,32 @@ template <int EPI>
 int gemm(hb_engine *e, const uint8_t *w, int rows, int K, const uint8_t *x, int n, hb::tc::GemmParams P) {
   hb_batch *b = e->batch;
   const GemmShape g = gemm_shape(rows, K, n, b->sms);
-  P.w = w;
-  P.x = x;
-  P.rows = rows;
-  P.K = K;
-  P.N = n;
-  P.npad = g.npad;
-  P.tiles = g.tiles;
-  P.ksplit = g.ksplit;
-  P.kst = g.kst;
-  P.stages = g.stages;
+  if (!gemm_params(P, g, w, rows, K, x, n)) return fail(e, HB_ERR_CUDA, "batched step: tensor map encoding failed");
   P.ws = g.ksplit > 1 ? batch_ws(b) : nullptr;
-  P.cnt = batch_cnt(b);
   P.ctrl = batch_ctrl(b);
   P.limit_ns = e->limit_ns;
   const size_t smem = hb::tc::gemm_smem_bytes(g.stages, g.npad);
-  if (b->attr_smem[EPI] < smem) {
-    // opt in once per engine (the attribute is per device) for the largest
-    // shared-memory size the ring sizing can ask for
-    const size_t want = std::max(smem, static_cast<size_t>(200 * 1024));
-    HB_CUDA(e, cudaFuncSetAttribute(hb::tc::gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(want)));
-    b->attr_smem[EPI] = want;
-  }
   hb::tc::gemm_kernel<EPI><<<g.tiles * g.ksplit, hb::tc::kThreads, smem, e->stream>>>(P);
+  if (g.ksplit > 1)
+    hb::tc::reduce_kernel<EPI><<<dim3(g.tiles, n), hb::tc::kThreads, 0, e->stream>>>(P);
   HB_CUDA(e, cudaGetLastError());
   return HB_OK;
 }
 
-// The whole model over n rows: row i is token tok[i] at position pos[i] of
-// KV slot slot[i] (the host has checked them).  Leaves each row's argmax
-// in b->h_argmax (and FP32 logits when want_logits).
-int batch_forward(hb_engine *e, int n, bool want_logits) {
+// Enqueues the whole model over n rows on the engine's stream: row i is
+// token tok[i] at position pos[i] of KV slot slot[i] (uploaded from the
+// pinned h_meta; the host has checked them).  The final norm and LM head run
+// over the n_out rows listed in h_meta's output-row region only (a prefill
+// chunk needs one), leaving their argmax in the pinned h_argmax and the
+// control block in h_ctrl.
+int batch_record(hb_engine *e, int n, int n_out, bool want_logits) {
   hb_batch *b = e->batch;
   const hb_model_desc &d = e->desc;
   const int H = d.hidden, I = d.intermediate, QKV = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
   const int group = d.q_heads / d.kv_heads;
   cudaStream_t st = e->stream;
   HB_CUDA(e, cudaMemsetAsync(b->scratch, 0, kCtrlBytes, st));
-  HB_CUDA(e, cudaMemcpyAsync(b->d_meta, b->h_meta, sizeof(int) * 3 * kMaxRows, cudaMemcpyHostToDevice, st));
+  HB_CUDA(e, cudaMemcpyAsync(b->d_meta, b->h_meta, sizeof(int) * kMetaWords, cudaMemcpyHostToDevice, st));
   hb::tc::Rows R{b->d_meta, b->d_meta + kMaxRows, b->d_meta + 2 * kMaxRows};
   const auto *embed = reinterpret_cast<const __nv_bfloat16 *>(e->d_blob + d.embedding);
   hb::tc::embed_kernel<<<n, 128, 0, st>>>(embed, R.tok, H, b->h);
@@ -178,7 +236,7 @@ int batch_forward(hb_engine *e, int n, bool want_logits) {
   int rc;
   for (int l = 0; l < d.layers; ++l) {
     const hb::LayerPtrs &lp = e->layer_ptrs[l];
-    hb::tc::norm_pack_kernel<<<n, 128, 0, st>>>(b->h, lp.gamma_in, d.rms_eps, H, b->xn);
+    hb::tc::norm_pack_kernel<<<n, 128, 0, st>>>(b->h, nullptr, lp.gamma_in, d.rms_eps, H, b->xn);
     hb::tc::GemmParams P{};
     P.bias = d.has_qkv_bias ? lp.bias : nullptr;
     P.out = b->qkv;
@@ -190,7 +248,7 @@ int batch_forward(hb_engine *e, int n, bool want_logits) {
     P.resid = b->h;
     P.out = b->h1;
     if ((rc = gemm<hb::tc::kEpiResid>(e, lp.w_o, H, H, b->att, n, P))) return rc;
-    hb::tc::norm_pack_kernel<<<n, 128, 0, st>>>(b->h1, lp.gamma_post, d.rms_eps, H, b->xn);
+    hb::tc::norm_pack_kernel<<<n, 128, 0, st>>>(b->h1, nullptr, lp.gamma_post, d.rms_eps, H, b->xn);
     P = hb::tc::GemmParams{};
     P.out = reinterpret_cast<__nv_bfloat16 *>(b->act);
     if ((rc = gemm<hb::tc::kEpiSwiglu>(e, lp.w_gu, 2 * I, H, b->xn, n, P))) return rc;
@@ -199,18 +257,54 @@ int batch_forward(hb_engine *e, int n, bool want_logits) {
     P.out = b->h;
     if ((rc = gemm<hb::tc::kEpiResid>(e, lp.w_down, H, I, b->act, n, P))) return rc;
   }
-  hb::tc::norm_pack_kernel<<<n, 128, 0, st>>>(b->h, reinterpret_cast<const float *>(e->d_blob + d.gamma_final),
-                                               d.rms_eps, H, b->xn);
+  hb::tc::norm_pack_kernel<<<n_out, 128, 0, st>>>(b->h, b->d_meta + 3 * kMaxRows,
+                                                   reinterpret_cast<const float *>(e->d_blob + d.gamma_final),
+                                                   d.rms_eps, H, b->xn);
   hb::tc::GemmParams P{};
   P.y = want_logits ? b->logits : nullptr;
   P.part_val = b->part_val;
   P.part_idx = b->part_idx;
   P.pstride = kMaxRows;
-  if ((rc = gemm<hb::tc::kEpiLogits>(e, e->d_blob + d.w_lm, d.vocab, H, b->xn, n, P))) return rc;
-  hb::tc::argmax_reduce_kernel<<<n, 256, 0, st>>>(b->part_val, b->part_idx, b->lm_tiles, kMaxRows, b->d_argmax);
+  if ((rc = gemm<hb::tc::kEpiLogits>(e, e->d_blob + d.w_lm, d.vocab, H, b->xn, n_out, P))) return rc;
+  hb::tc::argmax_reduce_kernel<<<n_out, 256, 0, st>>>(b->part_val, b->part_idx, b->lm_tiles, kMaxRows,
+                                                      b->d_argmax);
   HB_CUDA(e, cudaGetLastError());
-  HB_CUDA(e, cudaMemcpyAsync(b->h_argmax, b->d_argmax, sizeof(int) * n, cudaMemcpyDeviceToHost, st));
+  HB_CUDA(e, cudaMemcpyAsync(b->h_argmax, b->d_argmax, sizeof(int) * n_out, cudaMemcpyDeviceToHost, st));
   HB_CUDA(e, cudaMemcpyAsync(b->h_ctrl, b->scratch, sizeof(hb::Ctrl), cudaMemcpyDeviceToHost, st));
+  return HB_OK;
+}
+
+void drop_graphs(hb_batch *b) {
+  for (auto &kv : b->graphs) cudaGraphExecDestroy(kv.second);
+  b->graphs.clear();
+}
+
+// One batched step: replays the captured launch sequence for (n, n_out,
+// logits) -- capturing it on first use -- then waits and checks the control
+// block.  A stream that cannot be captured runs the sequence directly.
+int batch_forward(hb_engine *e, int n, int n_out, bool want_logits) {
+  hb_batch *b = e->batch;
+  cudaStream_t st = e->stream;
+  const uint32_t key = static_cast<uint32_t>(n) | static_cast<uint32_t>(n_out) << 8 | (want_logits ? 1u << 16 : 0u);
+  if (!b->graphs.count(key) && b->graphs.size() >= kMaxGraphs) drop_graphs(b);
+  cudaGraphExec_t &exec = b->graphs[key];
+  int rc = HB_OK;
+  if (!exec && st != nullptr && cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+    rc = batch_record(e, n, n_out, want_logits);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t end = cudaStreamEndCapture(st, &graph);
+    if (rc == HB_OK && end == cudaSuccess && graph != nullptr &&
+        cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess)
+      exec = nullptr;
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    if (rc) return rc;
+    if (end != cudaSuccess || !exec) return fail(e, HB_ERR_CUDA, "batched step: graph capture failed");
+  } else if (!exec) {
+    cudaGetLastError();
+    if ((rc = batch_record(e, n, n_out, want_logits))) return rc;
+  }
+  if (exec) HB_CUDA(e, cudaGraphLaunch(exec, st));
   HB_CUDA(e, cudaStreamSynchronize(st));
   if (b->h_ctrl->err == hb::kErrTimeout)
     return fail(e, HB_ERR_DEVICE_TIMEOUT, "batched step: a device wait gave up (where %d)", b->h_ctrl->err_where);
@@ -245,6 +339,7 @@ void batch_release(hb_engine *e) {
   void *host[] = {b->h_meta, b->h_argmax, b->h_ctrl};
   for (void *p : host)
     if (p) cudaFreeHost(p);
+  drop_graphs(b);
   delete b;
   e->batch = nullptr;
 }
@@ -286,19 +381,10 @@ int hb_tc_gemm(const void *w_dev, int rows, int k, const void *x_dev, int n, flo
   // control block and slice counters start at zero on every call
   HB_CUDA(nullptr, cudaMemsetAsync(scr, 0, kCtrlBytes + align256(sizeof(unsigned int) * g.tiles), st));
   hb::tc::GemmParams P{};
-  P.w = static_cast<const uint8_t *>(w_dev);
-  P.x = static_cast<const uint8_t *>(x_dev);
-  P.rows = rows;
-  P.K = k;
-  P.N = n;
-  P.npad = g.npad;
-  P.tiles = g.tiles;
-  P.ksplit = g.ksplit;
-  P.kst = g.kst;
-  P.stages = g.stages;
+  if (!gemm_params(P, g, w_dev, rows, k, x_dev, n))
+    return fail(nullptr, HB_ERR_CUDA, "hb_tc_gemm: tensor map encoding failed");
   P.y = y_dev;
   P.ctrl = reinterpret_cast<hb::Ctrl *>(scr);
-  P.cnt = reinterpret_cast<unsigned int *>(scr + kCtrlBytes);
   P.ws = g.ws_floats ? reinterpret_cast<float *>(scr + kCtrlBytes + align256(sizeof(unsigned int) * g.tiles))
                      : nullptr;
   P.limit_ns = kDefaultLimitNs;
@@ -306,17 +392,21 @@ int hb_tc_gemm(const void *w_dev, int rows, int k, const void *x_dev, int n, flo
   HB_CUDA(nullptr, cudaFuncSetAttribute(hb::tc::gemm_kernel<hb::tc::kEpiF32>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   hb::tc::gemm_kernel<hb::tc::kEpiF32><<<g.tiles * g.ksplit, hb::tc::kThreads, smem, st>>>(P);
+  if (g.ksplit > 1)
+    hb::tc::reduce_kernel<hb::tc::kEpiF32><<<dim3(g.tiles, n), hb::tc::kThreads, 0, st>>>(P);
   HB_CUDA(nullptr, cudaGetLastError());
   return HB_OK;
 }
 
 int hb_step_rows(hb_engine *e, int n, const int32_t *slots, const int32_t *token_ids, const int32_t *positions,
-                 int32_t *argmax_out, float *logits_out) {
+                 int n_out, const int32_t *out_rows, int32_t *argmax_out, float *logits_out) {
   int rc = batch_check(e, n);
   if (rc) return rc;
   DeviceScope device_scope_(e->device);
   if (!device_scope_.ok) return fail(e, HB_ERR_CUDA, "cudaSetDevice(%d) failed", e->device);
   if (!slots || !token_ids || !positions) return fail(e, HB_ERR_INVALID_ARG, "rows are NULL");
+  if (out_rows ? (n_out < 1 || n_out > n) : n_out != n)
+    return fail(e, HB_ERR_INVALID_ARG, "n_out must be in [1, n] with out_rows, n without");
   const hb_model_desc &d = e->desc;
   for (int i = 0; i < n; ++i) {
     if (slots[i] < 0 || slots[i] >= d.max_slots)
@@ -329,6 +419,9 @@ int hb_step_rows(hb_engine *e, int n, const int32_t *slots, const int32_t *token
       if (slots[k] == slots[i] && positions[k] == positions[i])
         return fail(e, HB_ERR_INVALID_ARG, "rows %d and %d write the same slot position", k, i);
   }
+  for (int i = 0; out_rows && i < n_out; ++i)
+    if (out_rows[i] < 0 || out_rows[i] >= n)
+      return fail(e, HB_ERR_INVALID_ARG, "output row %d: %d outside [0, %d)", i, out_rows[i], n);
   if ((rc = batch_setup(e))) return rc;
   hb_batch *b = e->batch;
   if (logits_out && !b->logits && (rc = dev_alloc(e, &b->logits, static_cast<size_t>(kMaxRows) * d.vocab)))
@@ -338,11 +431,12 @@ int hb_step_rows(hb_engine *e, int n, const int32_t *slots, const int32_t *token
     b->h_meta[kMaxRows + i] = positions[i];
     b->h_meta[2 * kMaxRows + i] = token_ids[i];
   }
-  if ((rc = batch_forward(e, n, logits_out != nullptr))) return rc;
+  for (int i = 0; i < n_out; ++i) b->h_meta[3 * kMaxRows + i] = out_rows ? out_rows[i] : i;
+  if ((rc = batch_forward(e, n, n_out, logits_out != nullptr))) return rc;
   if (argmax_out)
-    for (int i = 0; i < n; ++i) argmax_out[i] = b->h_argmax[i];
+    for (int i = 0; i < n_out; ++i) argmax_out[i] = b->h_argmax[i];
   if (logits_out)
-    HB_CUDA(e, cudaMemcpy(logits_out, b->logits, sizeof(float) * n * d.vocab, cudaMemcpyDeviceToHost));
+    HB_CUDA(e, cudaMemcpy(logits_out, b->logits, sizeof(float) * n_out * d.vocab, cudaMemcpyDeviceToHost));
   return HB_OK;
 }
 
@@ -355,19 +449,11 @@ int hb_prefill_tc(hb_engine *e, int slot, const int32_t *ids, int n, int start_p
     const int m = std::min(kMaxRows, n - done);
     for (int i = 0; i < m; ++i) pos[i] = start_pos + done + i;
     const bool last = done + m == n;
-    std::vector<int32_t> am(m);
-    std::vector<float> lg;
-    float *lp = nullptr;
-    if (last && last_logits) {
-      lg.resize(static_cast<size_t>(m) * e->desc.vocab);
-      lp = lg.data();
-    }
-    rc = hb_step_rows(e, m, slots.data(), ids + done, pos.data(), am.data(), lp);
-    if (rc == HB_OK && last) {
-      if (argmax_out) *argmax_out = am[m - 1];
-      if (last_logits)
-        std::memcpy(last_logits, lg.data() + static_cast<size_t>(m - 1) * e->desc.vocab, sizeof(float) * e->desc.vocab);
-    }
+    const int32_t out_row = m - 1;  // only the chunk's last position reaches the LM head
+    int32_t am = 0;
+    rc = hb_step_rows(e, m, slots.data(), ids + done, pos.data(), 1, &out_row, &am,
+                      last ? last_logits : nullptr);
+    if (rc == HB_OK && last && argmax_out) *argmax_out = am;
     done += m;
   }
   return rc;

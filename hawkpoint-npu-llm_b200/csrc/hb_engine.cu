@@ -815,9 +815,11 @@ int hb_gemv(const void *w_dev, const float *scales_dev, int weight_format, int r
   const int red_rows = per_warp ? 1 : rg_per_cta * 8;
   const int mb = batch > 1 ? 8 : 1;
   const size_t fixed = hb::gemv_smem_bytes(0, mb, k, red_rows);
+  // (checked before subtracting: the sizes are unsigned)
+  if (fixed + 16 * kMaxSlotsRing + static_cast<size_t>(kMinSlotsRing) * hb::kSlotBytes > static_cast<size_t>(optin))
+    return fail(nullptr, HB_ERR_UNSUPPORTED, "hb_gemv: shape too large for shared memory");
   int nslots = static_cast<int>((static_cast<size_t>(optin) - fixed - 16 * kMaxSlotsRing) / hb::kSlotBytes);
   nslots = std::min(nslots, kMaxSlotsRing);
-  if (nslots < kMinSlotsRing) return fail(nullptr, HB_ERR_UNSUPPORTED, "hb_gemv: shape too large for shared memory");
   const size_t smem = hb::gemv_smem_bytes(nslots, mb, k, red_rows);
   const void *fn;
   if (mb == 1) fn = w8 ? reinterpret_cast<const void *>(&hb::gemv_kernel<1, true>) : reinterpret_cast<const void *>(&hb::gemv_kernel<1, false>);
@@ -873,7 +875,12 @@ int hb_gemv(const void *w_dev, const float *scales_dev, int weight_format, int r
 //   process exits;
 // * the first call on a device looks up the array's device address
 //   (cudaGetSymbolAddress, with that device current) and caches it, so that
-//   first call should come before any stream capture;
+//   first call should come before any stream capture; the cached address
+//   belongs to the device's primary context, so a process that calls
+//   cudaDeviceReset after using this entry point must not call it again;
+// * a device-side wait that gives up (HB_ERR_DEVICE_TIMEOUT on other entry
+//   points) is reported in-band: the argmax of every batch row reads -1
+//   (the control block lives in the array, which the caller cannot read);
 // * all calls on a device share that one array, so calls whose kernels could
 //   run at the same time on the GPU (different streams, no ordering between
 //   them) race on it and may return wrong argmax results; order such calls
@@ -890,7 +897,6 @@ constexpr int kNoAllocBatch = hb::kMaxBatchGemv;      // 8 batch rows
 constexpr size_t kNoAllocScratchBytes =
     sizeof(hb::Ctrl) + 2 * sizeof(float) * kNoAllocCtas * kNoAllocBatch;  // 65,568 bytes
 constexpr int kMaxDevices = 64;
-constexpr uint64_t kLimitNs = 2000000000ull;
 
 // The scratch itself.  In host code this name is only a stand-in for the
 // device symbol, never a device address: the device address comes from
@@ -949,6 +955,7 @@ int hb_gemv_noalloc(const void *w_dev, const float *scales_dev, int weight_forma
     return noalloc_fail(HB_ERR_CUDA, "device query failed");
   const int n_rg = rows / 8;
   const int G = sms < n_rg ? sms : n_rg;
+  // one CTA per SM at most: this only guards a future grid with more CTAs
   if (G > kNoAllocCtas)
     return noalloc_fail(HB_ERR_UNSUPPORTED, "more CTAs than the built-in scratch has partial slots");
 
@@ -965,9 +972,11 @@ int hb_gemv_noalloc(const void *w_dev, const float *scales_dev, int weight_forma
   const int red_rows = per_warp ? 1 : rg_per_cta * 8;
   const int mb = batch > 1 ? 8 : 1;
   const size_t fixed = hb::gemv_smem_bytes(0, mb, k, red_rows);
+  // (checked before subtracting: the sizes are unsigned)
+  if (fixed + 16 * 16 + 4 * static_cast<size_t>(hb::kSlotBytes) > static_cast<size_t>(optin))
+    return noalloc_fail(HB_ERR_UNSUPPORTED, "shape too large for shared memory");
   int nslots = static_cast<int>((static_cast<size_t>(optin) - fixed - 16 * 16) / hb::kSlotBytes);
   if (nslots > 16) nslots = 16;
-  if (nslots < 4) return noalloc_fail(HB_ERR_UNSUPPORTED, "shape too large for shared memory");
   const size_t smem = hb::gemv_smem_bytes(nslots, mb, k, red_rows);
   const void *fn;
   if (mb == 1)
@@ -1002,7 +1011,7 @@ int hb_gemv_noalloc(const void *w_dev, const float *scales_dev, int weight_forma
   P.nslots = nslots;
   P.red_rows = red_rows;
   P.per_warp = per_warp;
-  P.limit_ns = kLimitNs;
+  P.limit_ns = kDefaultLimitNs;
   void *args[] = {&P};
   err = cudaLaunchKernel(fn, dim3(G), dim3(hb::kThreads), args, smem, s);
   if (err != cudaSuccess) return noalloc_fail(HB_ERR_CUDA, cudaGetErrorString(err));

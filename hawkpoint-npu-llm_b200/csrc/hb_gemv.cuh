@@ -170,6 +170,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   consumer_sync(kConsumerThreads);
   if (*s_last && warp == 0) {
     __threadfence();
+    if (ld_volatile_int(&ctrl->abort) != 0) {
+      // some CTA gave up a wait: its partial is not a result, so no row's
+      // argmax is one either
+      if (lane < mrows) P.argmax_out[lane] = -1;
+      if (lane == 0) {
+        atomicExch(&ctrl->done, 0u);
+        __threadfence();
+      }
+      return;
+    }
     for (int m = 0; m < mrows; ++m) {
       float v = -INFINITY;
       int i = 0x7fffffff;

@@ -4,23 +4,31 @@
 // to 256 activation rows X [N x K], both BF16 in the packed row-group layout
 // of runtime/layout.py: 8 rows x 16 bytes per core matrix, row group g at
 // g * K * 16 bytes and chunk column j (8 K elements) at + j * 128.  That is
-// the canonical no-swizzle K-major layout of a UMMA shared-memory operand,
-// so one 1 KB bulk copy (cp.async.bulk, no tensor map, no multicast) moves
-// 8 chunk columns of one row group straight into place.
+// the canonical no-swizzle K-major layout of a UMMA shared-memory operand:
+// one stage (64 K elements) of a row group is 1 KB, contiguous, and a stage
+// of several row groups lands in shared memory already in MMA order.  Each
+// operand is addressed through a 3-D tensor map over that layout (1 KB
+// stage piece x K stage x row group), so one TMA load (no multicast) fetches
+// a whole stage of a tile: per-copy cost, not bytes, limits an SM that
+// streams 1 KB pieces one bulk copy each (about 25 GB/s per SM against
+// about 80 GB/s for one load per stage, measured on B200).  Row groups past
+// the end of W or of the batch read as zeros.
 //
 // One CTA = one 128-row tile of W x one K slice (split-K when there are
 // fewer tiles than SMs).  Warp 0 lane 0 streams the tile's A (16 row groups)
-// and the B operand (N / 8 row groups) through an S-stage shared-memory ring,
-// 64 K elements per stage; warp 1 lane 0 issues tcgen05.mma (M = 128, N =
+// and the B operand (npad / 8 row groups) through an S-stage shared-memory
+// ring, 64 K elements per stage; warp 1 lane 0 issues tcgen05.mma (M = 128, N =
 // the padded batch, K = 16, BF16 -> FP32) into a TMEM accumulator and
 // commits each stage back to the producer; all four warps then read the
 // accumulator (warp w holds TMEM lanes 32w .. 32w + 31, one weight row per
 // thread) and either finish the tile (one K slice) or leave an FP32 partial
-// for the last slice to arrive, which sums the slices in slice order -- the
-// result does not depend on which CTA finishes last.  Every wait is bounded
+// that reduce_kernel sums in slice order (the result does not depend on the
+// order the slices finish in).  Every wait is bounded
 // (hb_device.cuh); on a timeout the kernel records it, still commits and
 // drains what it issued, frees TMEM and returns.
 #pragma once
+
+#include <cuda.h>
 
 #include "hb_attn.cuh"
 
@@ -77,6 +85,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// One box of a 3-D tensor map (coordinates x, y, z) into shared memory,
+// completion on `bar`.  No multicast.
+__device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *map, int x, int y, int z,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(smem_u32(smem_dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Shared-memory operand descriptor, no swizzle, K-major: core matrices of
 // 8 rows x 16 bytes; `lbo` = byte step between core matrices along K,
 // `sbo` = byte step between 8-row groups (M / N); descriptor version 1.
@@ -100,8 +118,10 @@ __host__ __device__ inline uint32_t tmem_cols(int npad) {
 }
 
 struct GemmParams {
-  const uint8_t *w;   // packed weights, rows x K
-  const uint8_t *x;   // packed activations, N (rounded up to 8) x K
+  // packed weights (rows x K) and activations (N x K) as 3-D maps of 32-bit
+  // words: {256 (one 1 KB stage piece), K / 64 stages, row groups}, boxes
+  // {256, 1, 16} and {256, 1, npad / 8}
+  CUtensorMap map_w, map_x;
   int rows, K, N;
   int npad;           // N rounded up to 16 (the MMA's N)
   int tiles, ksplit, kst;     // kst: K stages (K / 64) in all; slice s takes [s kst / ksplit, (s + 1) kst / ksplit)
@@ -114,7 +134,6 @@ struct GemmParams {
   int *part_idx;
   int pstride;
   float *ws;          // [tiles][ksplit][npad][128] FP32 partials (ksplit > 1)
-  unsigned int *cnt;  // [tiles] slice arrivals (reset by the last)
   Ctrl *ctrl;
   uint64_t limit_ns;
 };
@@ -140,6 +159,81 @@ __device__ __forceinline__ void mbar_wait_quiet(uint64_t *bar, uint32_t parity, 
   }
 }
 
+// The epilogue of columns [n0, n1) of a tile from its FP32 results in
+// shared memory (stage[(n - n0) * 128 + row in tile]); 128 threads.
+template <int EPI>
+__device__ __forceinline__ void finish_tile(const GemmParams &P, const float *stage, int tile, int n0, int n1) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = tile * kTileRows;
+  if constexpr (EPI == kEpiF32 || EPI == kEpiBias || EPI == kEpiResid) {
+    for (int idx = threadIdx.x; idx < (n1 - n0) * kTileRows; idx += kThreads) {
+      const int n = n0 + (idx >> 7), row = row0 + (idx & 127);
+      if (row >= P.rows) continue;
+      const float v = stage[idx];
+      const size_t o = static_cast<size_t>(n) * P.rows + row;
+      if constexpr (EPI == kEpiF32) {
+        P.y[o] = v;
+      } else if constexpr (EPI == kEpiBias) {
+        float yv = rbf(v);
+        if (P.bias != nullptr) yv = __fadd_rn(yv, P.bias[row]);
+        P.out[o] = f2bf(yv);
+      } else {
+        P.out[o] = f2bf(__fadd_rn(rbf(v), bf2f(P.resid[o])));
+      }
+    }
+  } else if constexpr (EPI == kEpiSwiglu) {
+    // pair q of the tile: gate rows q*16 + rr, up rows q*16 + 8 + rr, act
+    // column (row0 / 16 + q) * 8 + rr; 8 outputs = one 16-byte chunk
+    const int inter = P.rows / 2, kc = inter / 8;
+    for (int idx = threadIdx.x; idx < (n1 - n0) * 8; idx += kThreads) {
+      const int n = n0 + (idx >> 3), q = idx & 7;
+      if (row0 + q * 16 >= P.rows) continue;
+      uint32_t w4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float a[2];
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int rr = 2 * e + h2;
+          const float g = rbf(stage[(n - n0) * kTileRows + q * 16 + rr]);
+          const float u = rbf(stage[(n - n0) * kTileRows + q * 16 + 8 + rr]);
+          const float ex = expf(-fminf(fmaxf(g, -80.f), 80.f));
+          a[h2] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, ex)), u);
+        }
+        w4[e] = pack_bf16x2(a[0], a[1]);
+      }
+      uint8_t *dst = reinterpret_cast<uint8_t *>(P.out) +
+                     (static_cast<size_t>(n >> 3) * kc + (row0 / 16 + q)) * 128 + (n & 7) * 16;
+      *reinterpret_cast<uint4 *>(dst) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    }
+  } else if constexpr (EPI == kEpiLogits) {
+    for (int n = n0 + warp; n < n1; n += kThreads / 32) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int r = lane; r < kTileRows; r += 32) {
+        const int row = row0 + r;
+        if (row >= P.rows) break;
+        const float v = stage[(n - n0) * kTileRows + r];
+        if (P.y != nullptr) P.y[static_cast<size_t>(n) * P.rows + row] = v;
+        if (argmax_better(v, row, bv, bi)) {
+          bv = v;
+          bi = row;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        argmax_merge(bv, bi, ov, oi);
+      }
+      if (lane == 0) {
+        P.part_val[static_cast<size_t>(tile) * P.pstride + n] = bv;
+        P.part_idx[static_cast<size_t>(tile) * P.pstride + n] = bi;
+      }
+    }
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ GemmParams P) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -150,7 +244,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   uint64_t *empty = full + S;
   uint64_t *done = empty + S;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
-  int *s_flag = reinterpret_cast<int *>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x / P.ksplit, split = blockIdx.x - tile * P.ksplit;
   const uint32_t ncols = tmem_cols(P.npad);
@@ -172,33 +265,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  const int groups_w = (P.rows + 7) / 8;
-  const int groups_x = (P.N + 7) / 8;
-  const int g0 = tile * 16;
-  const int ga = min(16, groups_w - g0);  // row groups of this tile that exist
-  const size_t rg_bytes = static_cast<size_t>(P.K) * 16;
   const int k0 = split * P.kst / P.ksplit;
   const int nk = (split + 1) * P.kst / P.ksplit - k0;  // K stages of this slice (>= 1)
 
   if (warp == 0 && lane == 0) {
-    // producer
-    const uint32_t bytes = static_cast<uint32_t>(ga + groups_x) * kGroupStageBytes;
+    // producer: a stage is one box of W's tile and one of the batch (full
+    // boxes: row groups past either end arrive as zeros and still count)
+    const uint32_t bytes = kAStageBytes + static_cast<uint32_t>(P.npad) * 128;
     int issued = 0;
     for (int i = 0; i < nk; ++i) {
       const int s = i % S;
       const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
       if (i >= S && !mbar_wait(&empty[s], ph ^ 1u, P.ctrl, P.limit_ns, kWhereEmpty)) break;
       mbar_arrive_expect_tx(&full[s], bytes);
-      const size_t koff = static_cast<size_t>(k0 + i) * kGroupStageBytes;
-      for (int g = 0; g < ga; ++g)
-        bulk_g2s(sa + static_cast<size_t>(s) * kAStageBytes + g * kGroupStageBytes,
-                 P.w + static_cast<size_t>(g0 + g) * rg_bytes + koff, kGroupStageBytes, &full[s]);
-      for (int b = 0; b < groups_x; ++b)
-        bulk_g2s(sb + static_cast<size_t>(s) * P.npad * 128 + b * kGroupStageBytes,
-                 P.x + static_cast<size_t>(b) * rg_bytes + koff, kGroupStageBytes, &full[s]);
+      tma_load_3d(sa + static_cast<size_t>(s) * kAStageBytes, &P.map_w, 0, k0 + i, tile * 16, &full[s]);
+      tma_load_3d(sb + static_cast<size_t>(s) * P.npad * 128, &P.map_x, 0, k0 + i, 0, &full[s]);
       ++issued;
     }
-    // every copy this thread issued has landed before the CTA can exit
+    // every load issued has landed before the CTA can exit
     for (int i = max(0, issued - S); i < issued; ++i)
       mbar_wait_quiet(&full[i % S], static_cast<uint32_t>(i / S) & 1u, P.limit_ns);
   } else if (warp == 1 && lane == 0) {
@@ -227,8 +311,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   tc_fence_after();
   const int r_t = warp * 32 + lane;  // this thread's row within the tile (its TMEM lane)
   const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  // the ring is idle now (every copy landed, every MMA done): its space
-  // stages the tile's FP32 results [npad][128]
+  // one slice: the ring is idle now (every copy landed, every MMA done) and
+  // its space stages the tile's FP32 results [npad][128]; several slices:
+  // each leaves its partial for reduce_kernel
   float *stage = reinterpret_cast<float *>(smem);
   float *part = P.ksplit > 1 ? P.ws + (static_cast<size_t>(tile) * P.ksplit + split) * P.npad * kTileRows : nullptr;
   if (ok) {
@@ -249,93 +334,41 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, ncols);
-  if (!ok) return;
-  if (P.ksplit > 1) {
-    // the last slice to arrive sums the slices in order
-    if (threadIdx.x == 0) {
-      __threadfence();
-      *s_flag = atomicAdd(&P.cnt[tile], 1u) == static_cast<unsigned>(P.ksplit - 1) ? 1 : 0;
-    }
-    __syncthreads();
-    if (*s_flag == 0) return;
-    __threadfence();
-    if (threadIdx.x == 0) P.cnt[tile] = 0u;
-    const float *base = P.ws + static_cast<size_t>(tile) * P.ksplit * P.npad * kTileRows;
-    for (int n = 0; n < P.N; ++n) {
-      float acc = 0.f;
-      for (int s2 = 0; s2 < P.ksplit; ++s2) acc += __ldcg(base + (static_cast<size_t>(s2) * P.npad + n) * kTileRows + r_t);
-      stage[n * kTileRows + r_t] = acc;
-    }
+  if (!ok || P.ksplit > 1) return;
+  finish_tile<EPI>(P, stage, tile, 0, P.N);
+}
+
+// Sums the K slices of column by of tile bx in slice order and applies the
+// epilogue (grid: tiles x N, 128 threads, a weight row per thread) -- a
+// tile's partials are spread over many CTAs, each with all its loads in
+// flight at once.
+template <int EPI>
+__global__ void __launch_bounds__(kThreads) reduce_kernel(const __grid_constant__ GemmParams P) {
+  __shared__ float stage[kTileRows];
+  const int tile = blockIdx.x, n = blockIdx.y;
+  const int r = threadIdx.x;
+  const size_t sstride = static_cast<size_t>(P.npad) * kTileRows;
+  const float *col = P.ws + static_cast<size_t>(tile) * P.ksplit * sstride + static_cast<size_t>(n) * kTileRows + r;
+  float acc = 0.f;
+  int s2 = 0;
+  for (; s2 + 16 <= P.ksplit; s2 += 16) {
+    float v[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) v[u] = __ldcg(col + (s2 + u) * sstride);
+#pragma unroll
+    for (int u = 0; u < 16; ++u) acc += v[u];
   }
+  if (s2 < P.ksplit) {
+    float v[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) v[u] = s2 + u < P.ksplit ? __ldcg(col + (s2 + u) * sstride) : 0.f;
+#pragma unroll
+    for (int u = 0; u < 16; ++u)
+      if (s2 + u < P.ksplit) acc += v[u];
+  }
+  stage[r] = acc;
   __syncthreads();
-  const int row0 = g0 * 8;
-  if constexpr (EPI == kEpiF32 || EPI == kEpiBias || EPI == kEpiResid) {
-    for (int idx = threadIdx.x; idx < P.N * kTileRows; idx += kThreads) {
-      const int n = idx >> 7, row = row0 + (idx & 127);
-      if (row >= P.rows) continue;
-      const float v = stage[idx];
-      const size_t o = static_cast<size_t>(n) * P.rows + row;
-      if constexpr (EPI == kEpiF32) {
-        P.y[o] = v;
-      } else if constexpr (EPI == kEpiBias) {
-        float yv = rbf(v);
-        if (P.bias != nullptr) yv = __fadd_rn(yv, P.bias[row]);
-        P.out[o] = f2bf(yv);
-      } else {
-        P.out[o] = f2bf(__fadd_rn(rbf(v), bf2f(P.resid[o])));
-      }
-    }
-  } else if constexpr (EPI == kEpiSwiglu) {
-    // pair q of the tile: gate rows q*16 + rr, up rows q*16 + 8 + rr, act
-    // column (row0 / 16 + q) * 8 + rr; 8 outputs = one 16-byte chunk
-    const int inter = P.rows / 2, kc = inter / 8;
-    for (int idx = threadIdx.x; idx < P.N * 8; idx += kThreads) {
-      const int n = idx >> 3, q = idx & 7;
-      if (row0 + q * 16 >= P.rows) continue;
-      uint32_t w4[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float a[2];
-#pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          const int rr = 2 * e + h2;
-          const float g = rbf(stage[n * kTileRows + q * 16 + rr]);
-          const float u = rbf(stage[n * kTileRows + q * 16 + 8 + rr]);
-          const float ex = expf(-fminf(fmaxf(g, -80.f), 80.f));
-          a[h2] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, ex)), u);
-        }
-        w4[e] = pack_bf16x2(a[0], a[1]);
-      }
-      uint8_t *dst = reinterpret_cast<uint8_t *>(P.out) +
-                     (static_cast<size_t>(n >> 3) * kc + (row0 / 16 + q)) * 128 + (n & 7) * 16;
-      *reinterpret_cast<uint4 *>(dst) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-    }
-  } else if constexpr (EPI == kEpiLogits) {
-    for (int n = warp; n < P.N; n += kThreads / 32) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-      for (int r = lane; r < kTileRows; r += 32) {
-        const int row = row0 + r;
-        if (row >= P.rows) break;
-        const float v = stage[n * kTileRows + r];
-        if (P.y != nullptr) P.y[static_cast<size_t>(n) * P.rows + row] = v;
-        if (argmax_better(v, row, bv, bi)) {
-          bv = v;
-          bi = row;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        argmax_merge(bv, bi, ov, oi);
-      }
-      if (lane == 0) {
-        P.part_val[static_cast<size_t>(tile) * P.pstride + n] = bv;
-        P.part_idx[static_cast<size_t>(tile) * P.pstride + n] = bi;
-      }
-    }
-  }
+  finish_tile<EPI>(P, stage, tile, n, n + 1);
 }
 
 // ---- per-row kernels of the batched step ---------------------------------------
@@ -352,12 +385,15 @@ __global__ void embed_kernel(const __nv_bfloat16 *embed, const int *tok, int H, 
   for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = __ldg(src + i);
 }
 
-// out (packed row-group layout) = bf16((x * inv_rms) * gamma) of row n of x
-// (cpu_backend.py:71-76), one CTA of 128 threads per row.
-__global__ void norm_pack_kernel(const __nv_bfloat16 *x, const float *gamma, float eps, int H, uint8_t *out) {
+// Row n of out (packed row-group layout) = bf16((x * inv_rms) * gamma) of
+// row rows[n] of x, or of row n when rows is NULL (cpu_backend.py:71-76);
+// one CTA of 128 threads per row.
+__global__ void norm_pack_kernel(const __nv_bfloat16 *x, const int *rows, const float *gamma, float eps, int H,
+                                 uint8_t *out) {
   __shared__ float part[4];
   const int n = blockIdx.x, tid = threadIdx.x;
-  const uint32_t *row = reinterpret_cast<const uint32_t *>(x + static_cast<size_t>(n) * H);
+  const int src = rows ? rows[n] : n;
+  const uint32_t *row = reinterpret_cast<const uint32_t *>(x + static_cast<size_t>(src) * H);
   float ss = 0.f;
   for (int i = tid; i < H / 2; i += blockDim.x) {
     const uint32_t w = row[i];

@@ -219,11 +219,13 @@ class B200DecoderEngine:
     # -- batched tensor-core path (hb_step_rows / hb_prefill_tc) ----------------
     MAX_ROWS = 128
 
-    def step_rows(self, slots, tokens, positions, logits=False):
+    def step_rows(self, slots, tokens, positions, logits=False, out_rows=None):
         """Up to 128 rows through the whole model on the tensor cores (row i:
         tokens[i] at positions[i] of KV slot slots[i]); rows may be several
-        consecutive positions of one sequence.  Returns (argmax per row, FP32
-        logits [rows, vocab] or None).  BF16 weights, 64-position cache."""
+        consecutive positions of one sequence.  The LM head runs over
+        ``out_rows`` (indices into the rows; default every row).  Returns
+        (argmax per output row, FP32 logits [outputs, vocab] or None).  BF16
+        weights, 64-position cache."""
         h = self._live()
         n = len(slots)
         s = np.ascontiguousarray(slots, np.int32)
@@ -231,11 +233,14 @@ class B200DecoderEngine:
         p = np.ascontiguousarray(positions, np.int32)
         if not (s.size == t.size == p.size == n):
             raise ValueError("slots, tokens and positions must have the same length")
-        out = np.empty((n, self.vocab), np.float32) if logits else None
-        am = np.empty(n, np.int32)
+        sel = None if out_rows is None else np.ascontiguousarray(out_rows, np.int32)
+        n_out = n if sel is None else sel.size
+        out = np.empty((n_out, self.vocab), np.float32) if logits else None
+        am = np.empty(n_out, np.int32)
         ip = ctypes.POINTER(ctypes.c_int32)
         self._check(self._lib.hb_step_rows(
-            h, n, s.ctypes.data_as(ip), t.ctypes.data_as(ip), p.ctypes.data_as(ip), am.ctypes.data_as(ip),
+            h, n, s.ctypes.data_as(ip), t.ctypes.data_as(ip), p.ctypes.data_as(ip), n_out,
+            None if sel is None else sel.ctypes.data_as(ip), am.ctypes.data_as(ip),
             out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)) if logits else None))
         return am, out
 

@@ -19,6 +19,9 @@ HB_ERR_DEVICE_TIMEOUT = -3
 HB_ERR_UNSUPPORTED = -4
 HB_ERR_STATE = -5
 
+HB_WEIGHTS_BF16 = 0
+HB_WEIGHTS_W8 = 1
+
 HB_STEP_ARGMAX = 1
 HB_STEP_LOGITS = 2
 HB_STEP_DEVICE_LOGITS = 4
@@ -130,7 +133,7 @@ SIGNATURES = {
     "hb_tc_gemm_scratch_bytes": (ctypes.c_size_t, [_I, _I, _I]),
     "hb_tc_gemm": (_I, [_P, _I, _I, _P, _I, _FP, _P, ctypes.c_size_t, _P]),
     "hb_tc_gemm_status": (_I, [_P, _P]),
-    "hb_step_rows": (_I, [_P, _I, _I32P, _I32P, _I32P, _I32P, _FP]),
+    "hb_step_rows": (_I, [_P, _I, _I32P, _I32P, _I32P, _I, _I32P, _I32P, _FP]),
     "hb_prefill_tc": (_I, [_P, _I, _I32P, _I, _I, _FP, _I32P]),
     "hb_library_error": (ctypes.c_char_p, []),
     "hb_device_sm_count": (_I, [_I]),

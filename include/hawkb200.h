@@ -190,7 +190,9 @@ int hb_test_stall_next(hb_engine *engine, uint64_t limit_ns);
  * HB_GEMV_ARGMAX also writes argmax_dev[b] (first index of the maximum, as
  * np.argmax).  W is packed row-group major (runtime/layout.py); rows % 8 == 0,
  * k % 32 == 0; batch is 1..8.  All pointers are device pointers; scratch_dev
- * must hold hb_gemv_scratch_bytes(rows, batch) bytes.  Runs on `stream`. */
+ * must hold hb_gemv_scratch_bytes(rows, batch) bytes.  Runs on `stream`.
+ * If a bounded device wait gives up, every argmax_dev[b] reads -1 and the
+ * control block at the start of scratch_dev records the timeout. */
 enum { HB_GEMV_OUT_BF16 = 0, HB_GEMV_OUT_F32 = 1, HB_GEMV_OUT_NONE = 2 };
 enum { HB_GEMV_ARGMAX = 4 };
 size_t hb_gemv_scratch_bytes(int rows, int batch);
@@ -208,10 +210,12 @@ int hb_gemv(const void *w_dev, const float *scales_dev, int weight_format,
  * __device__ array inside the library (room for batch <= 8 and up to 1024
  * CTAs; larger requests return HB_ERR_UNSUPPORTED), held by every GPU that
  * loads the library until the process exits.  The first call on a device
- * looks the array's address up (make it before any stream capture).  All
- * calls on a device share the array: calls that may overlap on the GPU
- * (unordered streams) race.  Allocates nothing; errors in
- * hb_library_error(). */
+ * looks the array's address up (make it before any stream capture) and
+ * keeps it for the primary context, so do not call it again after a
+ * cudaDeviceReset.  All calls on a device share the array: calls that may
+ * overlap on the GPU (unordered streams) race.  A device wait that gives up
+ * shows as argmax_dev[b] == -1 for every row (the control block is inside
+ * the library).  Allocates nothing; errors in hb_library_error(). */
 int hb_gemv_noalloc(const void *w_dev, const float *scales_dev, int weight_format,
                     int rows, int k, const void *x_dev, int batch, void *y_dev,
                     int flags, int32_t *argmax_dev, void *stream);
@@ -306,8 +310,11 @@ int hb_tc_gemm_status(const void *scratch_dev, void *stream);
 /* ---- batched step on the tensor cores (new in this build) -------------------
  * n rows (1 <= n <= 128) through every layer, the final norm and the LM
  * head in one call: row i feeds token_ids[i] at positions[i] of KV slot
- * slots[i] and returns its argmax in argmax_out[i] (and, when logits_out is
- * not NULL, its FP32 logits in logits_out[i * vocab ...]).  Rows may mix
+ * slots[i].  The final norm and LM head run over the output rows only: with
+ * out_rows NULL (n_out == n) every row, else the n_out rows out_rows[0..)
+ * (e.g. the last position of each sequence in a chunked-prefill step).
+ * Output j's argmax goes to argmax_out[j] and, when logits_out is not NULL,
+ * its FP32 logits to logits_out[j * vocab ...].  Rows may mix
  * sequences (multi-stream decode) and may hold consecutive positions of one
  * sequence (chunked prefill): every row's K/V is appended before any row
  * attends, so a row sees the rows of its sequence at earlier positions.  No
@@ -322,10 +329,12 @@ int hb_tc_gemm_status(const void *scratch_dev, void *stream);
  * (npu_llm/runtime/generate.py:1110-1126) and its single-lock serving
  * (npu_llm/api_server.py:646-678) for the rows it batches. */
 int hb_step_rows(hb_engine *engine, int n, const int32_t *slots, const int32_t *token_ids,
-                 const int32_t *positions, int32_t *argmax_out, float *logits_out);
+                 const int32_t *positions, int n_out, const int32_t *out_rows, int32_t *argmax_out,
+                 float *logits_out);
 /* Prefill of positions start_pos .. start_pos + n - 1 of one slot through
- * hb_step_rows (128 rows per launch sequence); the last position's argmax and,
- * when last_logits is not NULL, its FP32 logits. */
+ * hb_step_rows (128 rows per launch sequence, the LM head on each chunk's
+ * last row only); the last position's argmax and, when last_logits is not
+ * NULL, its FP32 logits. */
 int hb_prefill_tc(hb_engine *engine, int slot, const int32_t *ids, int n, int start_pos, float *last_logits,
                   int32_t *argmax_out);
 

@@ -101,6 +101,31 @@ def test_chunked_prefill_rows_with_decode_rows(tiny):
     assert_logits_close(logits[5], ref_b[12], "decode row")
 
 
+def test_output_rows_select_the_lm_head_rows(tiny):
+    """A chunk of five positions of one sequence plus a decode row of
+    another, the LM head on the last row of each only: those two outputs
+    equal the same rows of an all-rows step (tolerance: the LM head's K split
+    follows the output count)."""
+    model, engine = tiny
+    engine.reset()
+    a = synthetic.prompt_ids(model.shape.vocab, 9, seed=17)
+    b = synthetic.prompt_ids(model.shape.vocab, 6, seed=18)
+    engine.prefill(b[:5], slot=3)
+    slots = [2] * 8 + [3]
+    tokens = a[:8] + [b[5]]
+    positions = list(range(8)) + [5]
+    am_all, all_rows = engine.step_rows(slots, tokens, positions, logits=True)
+    am_sel, sel = engine.step_rows(slots, tokens, positions, logits=True, out_rows=[7, 8])
+    assert sel.shape == (2, model.shape.vocab)
+    for j, r in enumerate([7, 8]):
+        assert_logits_close(sel[j], all_rows[r], f"output row {r}")
+        assert int(am_sel[j]) == int(np.argmax(sel[j]))
+    am_only, none = engine.step_rows(slots, tokens, positions, out_rows=[8])
+    assert none is None and am_only.shape == (1,)
+    with pytest.raises(ValueError):
+        engine.step_rows(slots, tokens, positions, out_rows=[9])
+
+
 def test_step_rows_rejects_bad_rows(tiny):
     model, engine = tiny
     with pytest.raises(ValueError):

@@ -6,7 +6,10 @@ buffer from the caller), twice in a row, and compared with it: the two run the
 same kernel, so outputs and argmax must agree within the GEMV tests' tolerance
 (they are in fact expected to be identical).  The second call checks that the
 state a call leaves in the shared array does not leak into the next one.
-This file is named to be collected last.
+The outputs are also checked against an FP32 reference of the same product,
+for BF16 and W8 weights, with FP32 / argmax-only outputs, and for calls of
+different grid sizes queued back to back on one stream (they reuse the same
+partial slots).  This file is named to be collected last.
 """
 
 import ctypes
@@ -71,3 +74,79 @@ def test_noalloc_rejects_oversized_requests():
                              hb_lib.HB_GEMV_OUT_NONE | hb_lib.HB_GEMV_ARGMAX, ctypes.c_void_p(256), None)
     assert rc == hb_lib.HB_ERR_UNSUPPORTED
     assert b"scratch" in lib.hb_library_error()
+
+
+def _fp32_reference(w, x, scales=None):
+    ref = x.astype(np.float32) @ w.astype(np.float32).T
+    return ref * scales[None, :] if scales is not None else ref
+
+
+def test_noalloc_w8_and_argmax_only_against_fp32():
+    """W8 weights (int8 + FP32 row scales) with FP32 output, and the same
+    product with argmax only (HB_GEMV_OUT_NONE): both against FP32 numpy."""
+    import torch
+    from runtime.quantize import quantize_per_output_channel
+
+    lib = hb_lib.load()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rows, k, batch = 4864, 896, 3
+    rng = np.random.default_rng(11)
+    wf = rng.standard_normal((rows, k), dtype=np.float32) * 0.02
+    q, scales = quantize_per_output_channel(wf)
+    x = rng.standard_normal((batch, k), dtype=np.float32).astype(bfloat16)
+    dev = torch.device("cuda:0")
+    wd = torch.from_numpy(layout.pack_matrix_bytes(np.ascontiguousarray(q))).to(dev)
+    sd = torch.from_numpy(np.ascontiguousarray(scales, np.float32)).to(dev)
+    xd = torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).to(dev)
+    ref = _fp32_reference(q, x, scales)
+    y, am = _outputs(rows, batch)
+    fp = ctypes.cast(sd.data_ptr(), ctypes.POINTER(ctypes.c_float))
+    hb_lib.check(lib.hb_gemv_noalloc(wd.data_ptr(), fp, hb_lib.HB_WEIGHTS_W8, rows, k, xd.data_ptr(), batch,
+                                     y.data_ptr(), hb_lib.HB_GEMV_OUT_F32 | hb_lib.HB_GEMV_ARGMAX, am.data_ptr(),
+                                     stream))
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    assert np.all(np.abs(got - ref) <= 1e-4 * np.abs(ref) + 1e-5), np.abs(got - ref).max()
+    assert np.array_equal(am.cpu().numpy(), got.argmax(axis=1).astype(np.int32))
+    _, am2 = _outputs(rows, batch)
+    hb_lib.check(lib.hb_gemv_noalloc(wd.data_ptr(), fp, hb_lib.HB_WEIGHTS_W8, rows, k, xd.data_ptr(), batch, None,
+                                     hb_lib.HB_GEMV_OUT_NONE | hb_lib.HB_GEMV_ARGMAX, am2.data_ptr(), stream))
+    torch.cuda.synchronize()
+    assert np.array_equal(am2.cpu().numpy(), am.cpu().numpy())
+
+
+def test_noalloc_back_to_back_grid_sizes_on_one_stream():
+    """A 151,936-row call (one CTA per SM) and an 896-row call (112 CTAs)
+    queued on one stream without a synchronisation between them: each
+    equals hb_gemv on its own scratch and the FP32 reference."""
+    import torch
+
+    lib = hb_lib.load()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    flags = hb_lib.HB_GEMV_OUT_F32 | hb_lib.HB_GEMV_ARGMAX
+    cases = []
+    for rows, k, batch in ((151936, 896, 2), (896, 896, 2)):
+        rng = np.random.default_rng([rows, 3])
+        w = rng.standard_normal((rows, k), dtype=np.float32).astype(bfloat16)
+        x = rng.standard_normal((batch, k), dtype=np.float32).astype(bfloat16)
+        dev = torch.device("cuda:0")
+        wd = torch.from_numpy(layout.pack_matrix_bytes(w)).to(dev)
+        xd = torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).to(dev)
+        y, am = _outputs(rows, batch)
+        cases.append((rows, k, batch, w, x, wd, xd, y, am))
+    for rows, k, batch, w, x, wd, xd, y, am in cases:
+        hb_lib.check(lib.hb_gemv_noalloc(wd.data_ptr(), None, 0, rows, k, xd.data_ptr(), batch, y.data_ptr(), flags,
+                                         am.data_ptr(), stream))
+    torch.cuda.synchronize()
+    for rows, k, batch, w, x, wd, xd, y, am in cases:
+        ref = _fp32_reference(w, x)
+        got = y.cpu().numpy()
+        assert np.all(np.abs(got - ref) <= 1e-4 * np.abs(ref) + 1e-4 * np.sqrt(k)), (rows, np.abs(got - ref).max())
+        y2, am2 = _outputs(rows, batch)
+        nscratch = lib.hb_gemv_scratch_bytes(rows, batch)
+        scratch = torch.zeros(nscratch, dtype=torch.uint8, device="cuda:0")
+        hb_lib.check(lib.hb_gemv(wd.data_ptr(), None, 0, rows, k, xd.data_ptr(), batch, y2.data_ptr(), flags,
+                                 am2.data_ptr(), scratch.data_ptr(), nscratch, stream))
+        torch.cuda.synchronize()
+        assert np.array_equal(y2.cpu().numpy(), got)
+        assert np.array_equal(am2.cpu().numpy(), am.cpu().numpy())
