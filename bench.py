@@ -114,6 +114,18 @@ def sum_over_ranks(value, world):
     return float(t.item())
 
 
+def gather_over_ranks(value, world):
+    """Every rank's value, in rank order."""
+    if world == 1:
+        return [value]
+    import torch
+    import torch.distributed as dist
+    dev = torch.device("cuda", LOCAL_DEVICE[0]) if dist.get_backend() == "nccl" else "cpu"
+    out = [torch.zeros(1, dtype=torch.float64, device=dev) for _ in range(world)]
+    dist.all_gather(out, torch.tensor([value], dtype=torch.float64, device=dev))
+    return [float(t.item()) for t in out]
+
+
 def config5_requests(vocab, n=512, new_tokens=16, seed=MODEL_SEED + 5):
     """Config 5: 8 x 64 independent requests, prompt lengths U[8, 48],
     every fourth request opening with one shared 16-token prefix, 16 greedy
@@ -125,44 +137,66 @@ def config5_requests(vocab, n=512, new_tokens=16, seed=MODEL_SEED + 5):
             for i, ids in enumerate(synthetic.ragged_prompts(vocab, n, seed))]
 
 
-def run_multistream(model, blob, device, rank, world):
-    """Config 5 on this rank's shard: continuous batching of 8 streams per
-    launch, shared prefixes reused from the KV prefix pool."""
+MULTISTREAM_MODES = {
+    # the batched tensor-core step: 64 streams, prompts in chunks of 32
+    # positions, up to 128 rows a step
+    "rows": {"max_slots": 68, "server": {"max_batch": 64, "prefill_chunk": 32, "max_rows": 128}},
+    # the persistent decoder kernel: 8 streams a launch, one position each
+    "persistent": {"max_slots": 12, "server": {"max_batch": 8}},
+}
+
+
+def run_multistream(model, blob, device, rank, world, mode="rows"):
+    """Config 5 on this rank's shard (requests split over ranks, no
+    collective on the token path): continuous batching, shared prefixes
+    reused from the KV prefix pool.  A first run of the same requests
+    captures every launch sequence the timed run replays."""
     import numpy as np
     import torch
     from runtime import dispatch
     from runtime.b200_engine import B200DecoderEngine
     from runtime.serving import MultiStreamServer, Request
 
+    spec = MULTISTREAM_MODES[mode]
     everything = config5_requests(model.shape.vocab)
     mine = dispatch.shard([r.prompt for r in everything], rank, world, 16)
-    engine = B200DecoderEngine(model, device=device, blob=blob, max_slots=12, max_batch=8)
+    engine = B200DecoderEngine(model, device=device, blob=blob, max_slots=spec["max_slots"], max_batch=8)
+    stream = torch.cuda.Stream(device=device)
+    engine.set_stream(stream.cuda_stream)
+
+    def requests():
+        return [Request(prompt=everything[i].prompt, new_tokens=everything[i].new_tokens, rid=i) for i in mine]
+
     try:
-        warm = [Request(prompt=everything[i].prompt, new_tokens=4) for i in mine[:8]]
-        MultiStreamServer(engine).run(warm)
-        reqs = [Request(prompt=everything[i].prompt, new_tokens=everything[i].new_tokens, rid=i) for i in mine]
-        server = MultiStreamServer(engine)
+        MultiStreamServer(engine, **spec["server"]).run(requests())
+        reqs = requests()
+        server = MultiStreamServer(engine, **spec["server"])
         torch.cuda.synchronize()
         barrier(world)
-        engine.profile(True)
-        engine.profile_read()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0 = time.perf_counter()
+        ev0.record(stream)
         server.run(reqs)
+        ev1.record(stream)
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
-        device_s = float(engine.profile_read().sum()) / 1000.0
-        engine.profile(False)
+        device_s = ev0.elapsed_time(ev1) / 1000.0
     finally:
         engine.close()
     tokens = sum(len(r.tokens) for r in reqs)
     all_tokens = sum_over_ranks(float(tokens), world)
-    t_max = max_over_ranks(wall, world)
+    walls = gather_over_ranks(wall, world)
+    launches = gather_over_ranks(float(server.launches), world)
     d_max = max_over_ranks(device_s, world)
+    t_max = max(walls)
     return {
         "workload": "config 5: 512 requests, prompts U[8,48], 25% share a 16-token prefix, 16 greedy tokens",
-        "requests": len(everything), "requests_this_rank": len(reqs), "batch": 8,
+        "mode": mode, "server": spec["server"],
+        "requests": len(everything), "requests_this_rank": len(reqs),
         "value": all_tokens / t_max, "unit": "tokens/s", "device_value": all_tokens / d_max,
         "p50_ttft_ms": 1000 * float(np.median([r.ttft for r in reqs])),
+        "wall_s_per_rank": walls, "launches_per_rank": [int(v) for v in launches],
+        "slowest_rank": int(np.argmax(walls)),
         "launches_rank0": server.launches, "rows_rank0": server.rows,
         "prefix_reuses_rank0": sum(1 for r in reqs if r.reused_prefix),
     }
@@ -581,6 +615,21 @@ def run_b200(args, rank, world, local):
     engine.generate(prompt, 1, start=n_prompt - 1)
     ttft_cached_ms = 1000 * (time.perf_counter() - t0)
 
+    # TTFT through the batched tensor-core prefill: the 32 prompt positions
+    # in one launch sequence, the LM head on the last one (device events on
+    # the engine's stream; host row upload and argmax read-back included)
+    for _ in range(3):
+        tc_first, _ = engine.prefill_tc(prompt)
+    ttft_tc = []
+    for _ in range(max(5, args.steps)):
+        ev0.record(stream)
+        tc_first, _ = engine.prefill_tc(prompt)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        ttft_tc.append(ev0.elapsed_time(ev1))
+    ttft_tc_ms = float(np.median(ttft_tc))
+    tc_first = {"token": int(tc_first), "equals_persistent": int(tc_first) == ref_tokens[0]}
+
     parity = {"config3": golden_parity(engine, "qwen2.5-0.5b", "bf16")} if rank == 0 else None
 
     # e2e through the public decode_token API (host copies + sync per call)
@@ -600,7 +649,10 @@ def run_b200(args, rank, world, local):
     e2e_value = decode_steps * args.steps * world / e2e_t
     decoder.close()
 
-    multistream = None if args.no_extras else run_multistream(model, blob, device, rank, world)
+    multistream = multistream_persistent = None
+    if not args.no_extras:
+        multistream = run_multistream(model, blob, device, rank, world, "rows")
+        multistream_persistent = run_multistream(model, blob, device, rank, world, "persistent")
     others = run_other_configs(device, measured_peak()[0]) if world == 1 and not args.no_extras else None
 
     cpu = None
@@ -639,6 +691,9 @@ def run_b200(args, rank, world, local):
             "gpu_launches": launches_per_step * args.steps,
             "parity": parity,
             "multistream": multistream,
+            "multistream_persistent": multistream_persistent,
+            "ttft_tc_ms": ttft_tc_ms,
+            "ttft_tc_first_token": tc_first,
             "other_configs": others,
             "clocks": clocks.summary(),
         }

@@ -19,24 +19,40 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // an ldmatrix reads fall in distinct banks.
 __device__ __forceinline__ int kv_off(int s, int cb) { return s * 128 + ((cb ^ (s & 7)) << 4); }
 
-// Rotate-half RoPE of elements d and d + 32 of a 64-element head held as
-// BF16 pairs in w32[0..32), with the position's cos / sin of dim d (unfused
-// mul / sub / add, as cpu_backend.py:78-93).
-__device__ __forceinline__ void rope_pair_cs(const uint32_t *w32, int d, float c, float sn, __nv_bfloat16 &lo,
-                                             __nv_bfloat16 &hi) {
-  const uint32_t a = w32[d >> 1], b = w32[(d + 32) >> 1];
-  const float x0 = (d & 1) ? bf_hi(a) : bf_lo(a), x1 = (d & 1) ? bf_hi(b) : bf_lo(b);
+// Rotate-half RoPE of the BF16 values x0 (dim d) and x1 (dim d + 32) of a
+// head with the position's cos / sin of dim d (unfused mul / sub / add, as
+// cpu_backend.py:78-93).
+__device__ __forceinline__ void rope_vals(float x0, float x1, float c, float sn, __nv_bfloat16 &lo,
+                                          __nv_bfloat16 &hi) {
   lo = f2bf(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)));
   hi = f2bf(__fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn)));
 }
 
-// Lane d's part of position pr's K row (rotated dims d, d + 32) and V row
-// (dims 2d, 2d + 1) in a swizzled K / V history block.
-__device__ __forceinline__ void put_kv(uint8_t *kb, uint8_t *vb, int pr, int d, __nv_bfloat16 klo,
-                                       __nv_bfloat16 khi, uint32_t vword) {
+// rope_vals of elements d and d + 32 of a 64-element head held as BF16
+// pairs in w32[0..32).
+__device__ __forceinline__ void rope_pair_cs(const uint32_t *w32, int d, float c, float sn, __nv_bfloat16 &lo,
+                                             __nv_bfloat16 &hi) {
+  const uint32_t a = w32[d >> 1], b = w32[(d + 32) >> 1];
+  rope_vals((d & 1) ? bf_hi(a) : bf_lo(a), (d & 1) ? bf_hi(b) : bf_lo(b), c, sn, lo, hi);
+}
+
+// Lane d's part of position pr's K row (rotated dims d, d + 32) in a
+// swizzled K history block.
+__device__ __forceinline__ void put_k(uint8_t *kb, int pr, int d, __nv_bfloat16 klo, __nv_bfloat16 khi) {
   *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(pr, d >> 3) + (d & 7) * 2) = klo;
   *reinterpret_cast<__nv_bfloat16 *>(kb + kv_off(pr, 4 + (d >> 3)) + (d & 7) * 2) = khi;
+}
+
+// Lane d's part of position pr's V row (dims 2d, 2d + 1) in a swizzled V
+// history block.
+__device__ __forceinline__ void put_v(uint8_t *vb, int pr, int d, uint32_t vword) {
   *reinterpret_cast<uint32_t *>(vb + kv_off(pr, (2 * d) >> 3) + ((2 * d) & 7) * 2) = vword;
+}
+
+__device__ __forceinline__ void put_kv(uint8_t *kb, uint8_t *vb, int pr, int d, __nv_bfloat16 klo,
+                                       __nv_bfloat16 khi, uint32_t vword) {
+  put_k(kb, pr, d, klo, khi);
+  put_v(vb, pr, d, vword);
 }
 
 // One warp: scores q.k * 0.125 over positions <= p of a K / V history in

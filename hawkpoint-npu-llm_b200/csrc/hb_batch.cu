@@ -16,25 +16,27 @@ using namespace hbi;
 
 namespace {
 
-// K slices per tile so that tiles x slices fills at most one wave, each slice
-// at least two K stages, and the FP32 partials (slices x npad x 4 bytes per
-// weight row) at most half the weight bytes (K x 2 per row).
-int choose_ksplit(int tiles, int kst, int sms, int npad) {
-  int ks = sms / tiles;  // one wave: a second partial wave doubles the time
+// K slices per tile (one cluster) so that tiles x slices fills at most one
+// wave (a second, partial wave doubles the time), each slice at least two K
+// stages, at most a portable cluster's 8 CTAs.
+int choose_ksplit(int tiles, int kst, int sms) {
+  int ks = sms / tiles;
   ks = std::min(ks, kst >= 2 ? kst / 2 : 1);
-  ks = std::min(ks, 16 * kst / npad);
+  ks = std::min(ks, hb::tc::kMaxSlices);
   return std::max(ks, 1);
 }
 
-int choose_stages(int npad) {
+// Ring stages: at most 6, no more than a slice has K stages, within about
+// 200 KB of shared memory.
+int choose_stages(int npad, int ksplit, int kst) {
   const size_t per = hb::tc::kAStageBytes + static_cast<size_t>(npad) * 128;
-  const int s = static_cast<int>((200u * 1024u - 64u) / (per + 16));
-  return std::max(2, std::min(6, s));
+  const size_t budget = 200u * 1024u - 64u;
+  const int s = static_cast<int>(budget / (per + 16));
+  return std::max(1, std::min({6, s, (kst + ksplit - 1) / ksplit}));
 }
 
 struct GemmShape {
   int tiles, ksplit, kst, npad, stages;
-  size_t ws_floats;
 };
 
 GemmShape gemm_shape(int rows, int k, int n, int sms) {
@@ -42,15 +44,12 @@ GemmShape gemm_shape(int rows, int k, int n, int sms) {
   g.tiles = (rows + hb::tc::kTileRows - 1) / hb::tc::kTileRows;
   g.kst = k / hb::tc::kStageK;
   g.npad = hb::tc::pad_n(n);
-  g.ksplit = choose_ksplit(g.tiles, g.kst, sms, g.npad);
-  g.stages = choose_stages(g.npad);
-  g.ws_floats = g.ksplit > 1 ? static_cast<size_t>(g.tiles) * g.ksplit * g.npad * hb::tc::kTileRows : 0;
+  g.ksplit = choose_ksplit(g.tiles, g.kst, sms);
+  g.stages = choose_stages(g.npad, g.ksplit, g.kst);
   return g;
 }
 
 constexpr size_t kCtrlBytes = 256;
-
-size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -87,6 +86,37 @@ bool packed_map(CUtensorMap *m, const void *base, int K, int groups, int box_gro
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// A launch of `kernel` that may start before the previous kernel on the
+// stream completes (programmatic dependent launch: the kernel waits for it
+// with griddepcontrol.wait before reading its results), the K slices of a
+// GEMM tile one cluster of `cluster` CTAs.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_early(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, int cluster,
+                         Args &&...args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = cluster > 1 ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// One GEMM launch: tiles x ksplit CTAs, the K slices of a tile one cluster.
+template <int EPI>
+cudaError_t launch_gemm(const GemmShape &g, const hb::tc::GemmParams &P, cudaStream_t st) {
+  return launch_early(hb::tc::gemm_kernel<EPI>, dim3(g.tiles * g.ksplit), dim3(hb::tc::kThreads),
+                      hb::tc::gemm_smem_bytes(g.stages, g.npad, g.ksplit), st, g.ksplit, P);
+}
+
 // Fills P's shape fields and tensor maps for W (rows x K) times n rows of x.
 bool gemm_params(hb::tc::GemmParams &P, const GemmShape &g, const void *w, int rows, int K, const void *x, int n) {
   P.rows = rows;
@@ -112,9 +142,7 @@ struct hb_batch {
   int *d_argmax = nullptr;          // [kMaxRows]
   __nv_bfloat16 *h = nullptr, *h1 = nullptr, *qkv = nullptr;  // row-major [kMaxRows][*]
   uint8_t *xn = nullptr, *att = nullptr, *act = nullptr;      // packed GEMM inputs
-  uint8_t *scratch = nullptr;       // Ctrl | slice counters | split-K partials
-  size_t ws_floats = 0;
-  int max_tiles = 0;
+  uint8_t *scratch = nullptr;       // Ctrl (cleared every step)
   float *part_val = nullptr;
   int *part_idx = nullptr;
   int lm_tiles = 0;
@@ -134,9 +162,6 @@ constexpr int kMetaWords = 4 * kMaxRows;
 namespace {
 
 hb::Ctrl *batch_ctrl(hb_batch *b) { return reinterpret_cast<hb::Ctrl *>(b->scratch); }
-float *batch_ws(hb_batch *b) {
-  return reinterpret_cast<float *>(b->scratch + kCtrlBytes + align256(sizeof(unsigned int) * b->max_tiles));
-}
 
 int batch_setup(hb_engine *e) {
   if (e->batch) return HB_OK;
@@ -145,16 +170,8 @@ int batch_setup(hb_engine *e) {
   e->batch = b;
   cudaDeviceGetAttribute(&b->sms, cudaDevAttrMultiProcessorCount, e->device);
   const int H = d.hidden, I = d.intermediate, QKV = (d.q_heads + 2 * d.kv_heads) * d.head_dim;
-  const int shapes[5][2] = {{QKV, H}, {H, H}, {2 * I, H}, {H, I}, {d.vocab, H}};
-  for (const auto &sh : shapes) {
-    for (int n = 16; n <= kMaxRows; n += 16) {
-      const GemmShape g = gemm_shape(sh[0], sh[1], n, b->sms);
-      b->ws_floats = std::max(b->ws_floats, g.ws_floats);
-      b->max_tiles = std::max(b->max_tiles, g.tiles);
-    }
-  }
   b->lm_tiles = (d.vocab + hb::tc::kTileRows - 1) / hb::tc::kTileRows;
-  const size_t scratch = kCtrlBytes + align256(sizeof(unsigned int) * b->max_tiles) + b->ws_floats * sizeof(float);
+  const size_t scratch = kCtrlBytes;
   int rc;
   if ((rc = dev_alloc(e, &b->d_meta, kMetaWords)) || (rc = dev_alloc(e, &b->d_argmax, kMaxRows)) ||
       (rc = dev_alloc(e, &b->h, static_cast<size_t>(kMaxRows) * H)) ||
@@ -173,8 +190,12 @@ int batch_setup(hb_engine *e) {
   // opt every GEMM variant into the most shared memory any row count needs
   // (outside any stream capture)
   size_t smem = 0;
-  for (int n = 16; n <= kMaxRows; n += 16)
-    smem = std::max(smem, hb::tc::gemm_smem_bytes(choose_stages(n), n));
+  const int shapes[5][2] = {{QKV, H}, {H, H}, {2 * I, H}, {H, I}, {d.vocab, H}};
+  for (const auto &sh : shapes)
+    for (int n = 16; n <= kMaxRows; n += 16) {
+      const GemmShape g = gemm_shape(sh[0], sh[1], n, b->sms);
+      smem = std::max(smem, hb::tc::gemm_smem_bytes(g.stages, g.npad, g.ksplit));
+    }
   const void *fns[5] = {reinterpret_cast<const void *>(hb::tc::gemm_kernel<0>),
                         reinterpret_cast<const void *>(hb::tc::gemm_kernel<1>),
                         reinterpret_cast<const void *>(hb::tc::gemm_kernel<2>),
@@ -192,14 +213,9 @@ int gemm(hb_engine *e, const uint8_t *w, int rows, int K, const uint8_t *x, int 
   hb_batch *b = e->batch;
   const GemmShape g = gemm_shape(rows, K, n, b->sms);
   if (!gemm_params(P, g, w, rows, K, x, n)) return fail(e, HB_ERR_CUDA, "batched step: tensor map encoding failed");
-  P.ws = g.ksplit > 1 ? batch_ws(b) : nullptr;
   P.ctrl = batch_ctrl(b);
   P.limit_ns = e->limit_ns;
-  const size_t smem = hb::tc::gemm_smem_bytes(g.stages, g.npad);
-  hb::tc::gemm_kernel<EPI><<<g.tiles * g.ksplit, hb::tc::kThreads, smem, e->stream>>>(P);
-  if (g.ksplit > 1)
-    hb::tc::reduce_kernel<EPI><<<dim3(g.tiles, n), hb::tc::kThreads, 0, e->stream>>>(P);
-  HB_CUDA(e, cudaGetLastError());
+  HB_CUDA(e, launch_gemm<EPI>(g, P, e->stream));
   return HB_OK;
 }
 
@@ -219,7 +235,8 @@ int batch_record(hb_engine *e, int n, int n_out, bool want_logits) {
   HB_CUDA(e, cudaMemcpyAsync(b->d_meta, b->h_meta, sizeof(int) * kMetaWords, cudaMemcpyHostToDevice, st));
   hb::tc::Rows R{b->d_meta, b->d_meta + kMaxRows, b->d_meta + 2 * kMaxRows};
   const auto *embed = reinterpret_cast<const __nv_bfloat16 *>(e->d_blob + d.embedding);
-  hb::tc::embed_kernel<<<n, 128, 0, st>>>(embed, R.tok, H, b->h);
+  hb::tc::embed_norm_kernel<<<(n + 3) / 4, hb::tc::kThreads, 0, st>>>(embed, R.tok, n, e->layer_ptrs[0].gamma_in,
+                                                                     d.rms_eps, H, b->h, b->xn);
   hb::tc::KvArgs A{};
   A.qkv = b->qkv;
   A.QKV = QKV;
@@ -233,22 +250,29 @@ int batch_record(hb_engine *e, int n, int n_out, bool want_logits) {
   A.L = d.layers;
   A.ctx = d.context;
   const size_t att_smem = static_cast<size_t>(2) * d.context * 128 + static_cast<size_t>(group) * 512;
+  // per layer: qkv (+ RoPE and K / V append), attention, o (+ residual),
+  // norm, gate / up (+ SwiGLU), down (+ residual), the next layer's norm --
+  // each launched early, its weights prefetched while its predecessor ends
+  const dim3 norm_grid((n + 3) / 4);
   int rc;
   for (int l = 0; l < d.layers; ++l) {
     const hb::LayerPtrs &lp = e->layer_ptrs[l];
-    hb::tc::norm_pack_kernel<<<n, 128, 0, st>>>(b->h, nullptr, lp.gamma_in, d.rms_eps, H, b->xn);
     hb::tc::GemmParams P{};
     P.bias = d.has_qkv_bias ? lp.bias : nullptr;
     P.out = b->qkv;
-    if ((rc = gemm<hb::tc::kEpiBias>(e, lp.w_qkv, QKV, H, b->xn, n, P))) return rc;
     A.layer = l;
-    hb::tc::kv_append_kernel<<<dim3(n, d.kv_heads), 32, 0, st>>>(A, R);
-    hb::tc::attention_kernel<<<dim3(n, d.kv_heads), 32 * group, att_smem, st>>>(A, R, b->att);
+    P.kv = A;
+    P.R = R;
+    if ((rc = gemm<hb::tc::kEpiQkv>(e, lp.w_qkv, QKV, H, b->xn, n, P))) return rc;
+    HB_CUDA(e, launch_early(hb::tc::attention_kernel, dim3(n, d.kv_heads), dim3(32 * group), att_smem, st, 1, A, R,
+                            b->att));
     P = hb::tc::GemmParams{};
     P.resid = b->h;
     P.out = b->h1;
     if ((rc = gemm<hb::tc::kEpiResid>(e, lp.w_o, H, H, b->att, n, P))) return rc;
-    hb::tc::norm_pack_kernel<<<n, 128, 0, st>>>(b->h1, nullptr, lp.gamma_post, d.rms_eps, H, b->xn);
+    HB_CUDA(e, launch_early(hb::tc::norm_pack_kernel, norm_grid, dim3(hb::tc::kThreads), 0, st, 1,
+                            static_cast<const __nv_bfloat16 *>(b->h1), static_cast<const int *>(nullptr), n,
+                            lp.gamma_post, d.rms_eps, H, b->xn));
     P = hb::tc::GemmParams{};
     P.out = reinterpret_cast<__nv_bfloat16 *>(b->act);
     if ((rc = gemm<hb::tc::kEpiSwiglu>(e, lp.w_gu, 2 * I, H, b->xn, n, P))) return rc;
@@ -256,18 +280,23 @@ int batch_record(hb_engine *e, int n, int n_out, bool want_logits) {
     P.resid = b->h1;
     P.out = b->h;
     if ((rc = gemm<hb::tc::kEpiResid>(e, lp.w_down, H, I, b->act, n, P))) return rc;
+    if (l + 1 < d.layers)
+      HB_CUDA(e, launch_early(hb::tc::norm_pack_kernel, norm_grid, dim3(hb::tc::kThreads), 0, st, 1,
+                              static_cast<const __nv_bfloat16 *>(b->h), static_cast<const int *>(nullptr), n,
+                              e->layer_ptrs[l + 1].gamma_in, d.rms_eps, H, b->xn));
   }
-  hb::tc::norm_pack_kernel<<<n_out, 128, 0, st>>>(b->h, b->d_meta + 3 * kMaxRows,
-                                                   reinterpret_cast<const float *>(e->d_blob + d.gamma_final),
-                                                   d.rms_eps, H, b->xn);
+  HB_CUDA(e, launch_early(hb::tc::norm_pack_kernel, dim3((n_out + 3) / 4), dim3(hb::tc::kThreads), 0, st, 1,
+                          static_cast<const __nv_bfloat16 *>(b->h), static_cast<const int *>(b->d_meta + 3 * kMaxRows),
+                          n_out, reinterpret_cast<const float *>(e->d_blob + d.gamma_final), d.rms_eps, H, b->xn));
   hb::tc::GemmParams P{};
   P.y = want_logits ? b->logits : nullptr;
   P.part_val = b->part_val;
   P.part_idx = b->part_idx;
   P.pstride = kMaxRows;
   if ((rc = gemm<hb::tc::kEpiLogits>(e, e->d_blob + d.w_lm, d.vocab, H, b->xn, n_out, P))) return rc;
-  hb::tc::argmax_reduce_kernel<<<n_out, 256, 0, st>>>(b->part_val, b->part_idx, b->lm_tiles, kMaxRows,
-                                                      b->d_argmax);
+  HB_CUDA(e, launch_early(hb::tc::argmax_reduce_kernel, dim3(n_out), dim3(256), 0, st, 1,
+                          static_cast<const float *>(b->part_val), static_cast<const int *>(b->part_idx), b->lm_tiles,
+                          kMaxRows, b->d_argmax));
   HB_CUDA(e, cudaGetLastError());
   HB_CUDA(e, cudaMemcpyAsync(b->h_argmax, b->d_argmax, sizeof(int) * n_out, cudaMemcpyDeviceToHost, st));
   HB_CUDA(e, cudaMemcpyAsync(b->h_ctrl, b->scratch, sizeof(hb::Ctrl), cudaMemcpyDeviceToHost, st));
@@ -323,6 +352,8 @@ int batch_check(hb_engine *e, int n) {
   const hb_model_desc &d = e->desc;
   if (d.hidden % hb::tc::kStageK || d.intermediate % hb::tc::kStageK)
     return fail(e, HB_ERR_UNSUPPORTED, "hidden and intermediate must be multiples of 64");
+  if (d.head_dim != hb::tc::kHeadDimTc)
+    return fail(e, HB_ERR_UNSUPPORTED, "the batched step needs 64-dimension heads");
   return HB_OK;
 }
 
@@ -349,12 +380,7 @@ extern "C" {
 
 size_t hb_tc_gemm_scratch_bytes(int rows, int k, int n) {
   if (rows <= 0 || k <= 0 || n <= 0) return 0;
-  int sms = 148;
-  int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  cudaGetLastError();
-  const GemmShape g = gemm_shape(rows, k, n, sms);
-  return kCtrlBytes + align256(sizeof(unsigned int) * g.tiles) + g.ws_floats * sizeof(float);
+  return kCtrlBytes;  // the control block (partial sums stay on chip)
 }
 
 int hb_tc_gemm(const void *w_dev, int rows, int k, const void *x_dev, int n, float *y_dev, void *scratch_dev,
@@ -373,28 +399,21 @@ int hb_tc_gemm(const void *w_dev, int rows, int k, const void *x_dev, int n, flo
   HB_CUDA(nullptr, cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
   if (major != 10) return fail(nullptr, HB_ERR_UNSUPPORTED, "hb_tc_gemm: needs an sm_100 GPU");
   const GemmShape g = gemm_shape(rows, k, n, sms);
-  const size_t need = kCtrlBytes + align256(sizeof(unsigned int) * g.tiles) + g.ws_floats * sizeof(float);
-  if (scratch_bytes < need)
-    return fail(nullptr, HB_ERR_INVALID_ARG, "hb_tc_gemm: scratch needs %zu bytes", need);
+  if (scratch_bytes < kCtrlBytes)
+    return fail(nullptr, HB_ERR_INVALID_ARG, "hb_tc_gemm: scratch needs %zu bytes", kCtrlBytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t *scr = static_cast<uint8_t *>(scratch_dev);
-  // control block and slice counters start at zero on every call
-  HB_CUDA(nullptr, cudaMemsetAsync(scr, 0, kCtrlBytes + align256(sizeof(unsigned int) * g.tiles), st));
+  HB_CUDA(nullptr, cudaMemsetAsync(scr, 0, kCtrlBytes, st));  // the control block starts clear on every call
   hb::tc::GemmParams P{};
   if (!gemm_params(P, g, w_dev, rows, k, x_dev, n))
     return fail(nullptr, HB_ERR_CUDA, "hb_tc_gemm: tensor map encoding failed");
   P.y = y_dev;
   P.ctrl = reinterpret_cast<hb::Ctrl *>(scr);
-  P.ws = g.ws_floats ? reinterpret_cast<float *>(scr + kCtrlBytes + align256(sizeof(unsigned int) * g.tiles))
-                     : nullptr;
   P.limit_ns = kDefaultLimitNs;
-  const size_t smem = hb::tc::gemm_smem_bytes(g.stages, g.npad);
+  const size_t smem = hb::tc::gemm_smem_bytes(g.stages, g.npad, g.ksplit);
   HB_CUDA(nullptr, cudaFuncSetAttribute(hb::tc::gemm_kernel<hb::tc::kEpiF32>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-  hb::tc::gemm_kernel<hb::tc::kEpiF32><<<g.tiles * g.ksplit, hb::tc::kThreads, smem, st>>>(P);
-  if (g.ksplit > 1)
-    hb::tc::reduce_kernel<hb::tc::kEpiF32><<<dim3(g.tiles, n), hb::tc::kThreads, 0, st>>>(P);
-  HB_CUDA(nullptr, cudaGetLastError());
+  HB_CUDA(nullptr, launch_gemm<hb::tc::kEpiF32>(g, P, st));
   return HB_OK;
 }
 

@@ -21,11 +21,13 @@
 // the padded batch, K = 16, BF16 -> FP32) into a TMEM accumulator and
 // commits each stage back to the producer; all four warps then read the
 // accumulator (warp w holds TMEM lanes 32w .. 32w + 31, one weight row per
-// thread) and either finish the tile (one K slice) or leave an FP32 partial
-// that reduce_kernel sums in slice order (the result does not depend on the
-// order the slices finish in).  Every wait is bounded
-// (hb_device.cuh); on a timeout the kernel records it, still commits and
-// drains what it issued, frees TMEM and returns.
+// thread) into shared memory.  One K slice finishes the tile there; the K
+// slices of a tile run as one thread-block cluster and sum their partials
+// through distributed shared memory in slice order, each slice finishing a
+// share of the columns (the result does not depend on the order the slices
+// finish in).  Every mbarrier wait is bounded (hb_device.cuh); on a timeout
+// the kernel records it, still commits and drains what it issued, frees
+// TMEM, passes the cluster barriers (which every CTA reaches) and returns.
 #pragma once
 
 #include <cuda.h>
@@ -117,6 +119,24 @@ __host__ __device__ inline uint32_t tmem_cols(int npad) {
   return c;
 }
 
+// Row metadata of a batched step (device arrays of n entries).
+struct Rows {
+  const int *slot, *pos, *tok;
+};
+
+struct KvArgs {
+  const __nv_bfloat16 *qkv;  // [N][QKV] BF16 (biased q / k / v)
+  int QKV, QH, KVH, group, H;
+  const float *cos, *sin;    // [ctx][32]
+  __nv_bfloat16 *kv;         // [slots][L][KVH][K | V][ctx][64], swizzled rows
+  int L, layer, ctx;
+};
+
+__device__ __forceinline__ uint8_t *kv_rows(const KvArgs &A, int slot, int j, int kind) {
+  return reinterpret_cast<uint8_t *>(A.kv) +
+         ((((static_cast<size_t>(slot) * A.L + A.layer) * A.KVH + j) * 2 + kind) * A.ctx * kHeadDimTc) * 2;
+}
+
 struct GemmParams {
   // packed weights (rows x K) and activations (N x K) as 3-D maps of 32-bit
   // words: {256 (one 1 KB stage piece), K / 64 stages, row groups}, boxes
@@ -127,25 +147,67 @@ struct GemmParams {
   int tiles, ksplit, kst;     // kst: K stages (K / 64) in all; slice s takes [s kst / ksplit, (s + 1) kst / ksplit)
   int stages;
   float *y;           // kEpiF32: [N][rows] FP32 out; kEpiLogits: optional FP32 logits [N][rows]
-  const float *bias;  // kEpiBias: [rows] FP32 (nullptr: none)
+  const float *bias;  // kEpiQkv: [rows] FP32 (nullptr: none)
   const __nv_bfloat16 *resid;  // kEpiResid: [N][rows] BF16
-  __nv_bfloat16 *out;  // kEpiBias / kEpiResid: [N][rows] BF16; kEpiSwiglu: packed [N][rows / 2]
+  __nv_bfloat16 *out;  // kEpiQkv (q rows) / kEpiResid: [N][rows] BF16; kEpiSwiglu: packed [N][rows / 2]
+  KvArgs kv;           // kEpiQkv: the K / V cache the k and v rows go to
+  Rows R;              // kEpiQkv: each column's slot and position
   float *part_val;    // kEpiLogits: [tiles][pstride] per-tile maxima
   int *part_idx;
   int pstride;
-  float *ws;          // [tiles][ksplit][npad][128] FP32 partials (ksplit > 1)
   Ctrl *ctrl;
   uint64_t limit_ns;
 };
 
-__host__ __device__ inline size_t gemm_smem_bytes(int stages, int npad) {
-  return static_cast<size_t>(stages) * (kAStageBytes + static_cast<size_t>(npad) * 128) + 16 * stages + 64;
+// Shared memory of a GEMM CTA: the operand ring, reused after the last MMA
+// for the epilogue -- the tile's FP32 results (this slice's partial)
+// [npad][128] and, with K slices, the slice's summed share of columns --
+// then the barriers.
+__host__ __device__ inline int gemm_share(int npad, int ksplit) { return (npad + ksplit - 1) / ksplit; }
+__host__ __device__ inline size_t gemm_epi_bytes(int npad, int ksplit) {
+  return (static_cast<size_t>(npad) + (ksplit > 1 ? gemm_share(npad, ksplit) : 0)) * kTileRows * 4;
 }
+__host__ __device__ inline size_t gemm_data_bytes(int stages, int npad, int ksplit) {
+  const size_t ring = static_cast<size_t>(stages) * (kAStageBytes + static_cast<size_t>(npad) * 128);
+  const size_t epi = gemm_epi_bytes(npad, ksplit);
+  return ((ring > epi ? ring : epi) + 1023) / 1024 * 1024;
+}
+__host__ __device__ inline size_t gemm_smem_bytes(int stages, int npad, int ksplit) {
+  return gemm_data_bytes(stages, npad, ksplit) + 16 * stages + 64;
+}
+
+// ---- programmatic dependent launch ----------------------------------------------
+// Lets the next kernel of the stream be scheduled now (its CTAs start on free
+// SMs and may prefetch weights); no-op without the launch attribute.
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Waits until the kernels this one depends on have completed and their
+// writes are visible; no-op without the launch attribute.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ---- thread-block cluster (the K slices of one tile) ---------------------------
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// The address of the same shared-memory variable in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+constexpr int kMaxSlices = 8;  // portable cluster size
 
 // What a GEMM does with y[n][r] (cpu_backend.py rounding points):
 enum : int {
   kEpiF32 = 0,     // y -> FP32 [N][rows]
-  kEpiBias = 1,    // bf16(bf16(y) + bias[r]) -> BF16 [N][rows]          (qkv, :134-143)
+  kEpiQkv = 1,     // bf16(bf16(y) + bias[r]): q rows -> BF16 [N][rows]; k rows rotated and v rows
+                   // appended to the K / V cache at the column's slot / position (qkv, :78-93, :134-143)
   kEpiResid = 2,   // bf16(bf16(y) + resid[n][r]) -> BF16 [N][rows]      (o / down, :145-151, :166-171)
   kEpiSwiglu = 3,  // rows are gate / up row-group pairs: bf16(silu(bf16 g) * bf16 u) -> packed act (:154-165)
   kEpiLogits = 4,  // FP32 logits (optional) and each row's maximum over the tile (np.argmax order)
@@ -159,13 +221,104 @@ __device__ __forceinline__ void mbar_wait_quiet(uint64_t *bar, uint32_t parity, 
   }
 }
 
+// Row n of `out` (packed row-group layout) = bf16((x * inv_rms) * gamma) of
+// the BF16 row x (cpu_backend.py:71-76); one warp, lane l taking 16-byte
+// chunks l, l + 32, ... (held in registers for rows of up to 1024 values).
+// Reads through L2, so rows that other CTAs of the same kernel wrote are
+// seen.
+__device__ __forceinline__ float sum_squares8(const uint4 &w, float ss) {
+  const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    ss = fmaf(bf_lo(in[e]), bf_lo(in[e]), ss);
+    ss = fmaf(bf_hi(in[e]), bf_hi(in[e]), ss);
+  }
+  return ss;
+}
+
+// Chunk c (8 values, gamma g) of a normalised row into the packed layout.
+__device__ __forceinline__ void put_norm8(const uint4 &w, const float (&g)[8], float inv, int c, int kc, uint8_t *out,
+                                          int n) {
+  const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float a = __fmul_rn(__fmul_rn(bf_lo(in[e]), inv), g[2 * e]);
+    const float b = __fmul_rn(__fmul_rn(bf_hi(in[e]), inv), g[2 * e + 1]);
+    o[e] = pack_bf16x2(a, b);
+  }
+  *reinterpret_cast<uint4 *>(out + (static_cast<size_t>(n >> 3) * kc + c) * 128 + (n & 7) * 16) =
+      make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__device__ __forceinline__ void load_gamma8(const float *gamma, int c, float (&g)[8]) {
+  const float4 g0 = __ldg(reinterpret_cast<const float4 *>(gamma) + 2 * c);
+  const float4 g1 = __ldg(reinterpret_cast<const float4 *>(gamma) + 2 * c + 1);
+  g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w;
+  g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
+}
+
+// Rows n[i] of `out` (packed row-group layout) = bf16((x * inv_rms) * gamma)
+// of the BF16 rows x[i] (cpu_backend.py:71-76) for the R rows with n[i] >= 0;
+// one warp, lane l taking 16-byte chunks l, l + 32, ... of every row.  Every
+// load (both rows, gamma) is issued before the first store, and rows of up
+// to 1024 values stay in registers.  Reads through L2, so rows that other
+// CTAs of the same kernel wrote are seen.
+template <int R>
+__device__ __forceinline__ void norm_pack_rows(const __nv_bfloat16 *const (&x)[R], const int (&n)[R],
+                                               const float *gamma, float eps, int H, uint8_t *out) {
+  constexpr int kHeld = 4;
+  const int lane = threadIdx.x & 31, kc = H / 8;
+  uint4 held[R][kHeld];
+  float g[kHeld][8];
+#pragma unroll
+  for (int i = 0; i < kHeld; ++i) {
+    const int c = lane + 32 * i;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      held[r][i] = n[r] >= 0 && c < kc ? __ldcg(reinterpret_cast<const uint4 *>(x[r]) + c) : make_uint4(0, 0, 0, 0);
+    if (c < kc) load_gamma8(gamma, c, g[i]);
+  }
+  float inv[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kHeld; ++i)
+      if (lane + 32 * i < kc) ss = sum_squares8(held[r][i], ss);
+    if (n[r] >= 0)
+      for (int c = lane + 32 * kHeld; c < kc; c += 32) ss = sum_squares8(__ldcg(reinterpret_cast<const uint4 *>(x[r]) + c), ss);
+    const float total = warp_sum(ss);
+    inv[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(H)), eps)));
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if (n[r] < 0) continue;
+#pragma unroll
+    for (int i = 0; i < kHeld; ++i)
+      if (lane + 32 * i < kc) put_norm8(held[r][i], g[i], inv[r], lane + 32 * i, kc, out, n[r]);
+    for (int c = lane + 32 * kHeld; c < kc; c += 32) {
+      float gg[8];
+      load_gamma8(gamma, c, gg);
+      put_norm8(__ldcg(reinterpret_cast<const uint4 *>(x[r]) + c), gg, inv[r], c, kc, out, n[r]);
+    }
+  }
+}
+
+__device__ __forceinline__ void norm_pack_row(const __nv_bfloat16 *x, const float *gamma, float eps, int H,
+                                              uint8_t *out, int n) {
+  const __nv_bfloat16 *const xs[1] = {x};
+  const int ns[1] = {n};
+  norm_pack_rows<1>(xs, ns, gamma, eps, H, out);
+}
+
 // The epilogue of columns [n0, n1) of a tile from its FP32 results in
 // shared memory (stage[(n - n0) * 128 + row in tile]); 128 threads.
 template <int EPI>
-__device__ __forceinline__ void finish_tile(const GemmParams &P, const float *stage, int tile, int n0, int n1) {
+__device__ __forceinline__ void finish_tile(const GemmParams &P, float *stage, int tile, int n0, int n1) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = tile * kTileRows;
-  if constexpr (EPI == kEpiF32 || EPI == kEpiBias || EPI == kEpiResid) {
+  if constexpr (EPI == kEpiF32 || EPI == kEpiResid) {
     for (int idx = threadIdx.x; idx < (n1 - n0) * kTileRows; idx += kThreads) {
       const int n = n0 + (idx >> 7), row = row0 + (idx & 127);
       if (row >= P.rows) continue;
@@ -173,12 +326,43 @@ __device__ __forceinline__ void finish_tile(const GemmParams &P, const float *st
       const size_t o = static_cast<size_t>(n) * P.rows + row;
       if constexpr (EPI == kEpiF32) {
         P.y[o] = v;
-      } else if constexpr (EPI == kEpiBias) {
-        float yv = rbf(v);
-        if (P.bias != nullptr) yv = __fadd_rn(yv, P.bias[row]);
-        P.out[o] = f2bf(yv);
       } else {
         P.out[o] = f2bf(__fadd_rn(rbf(v), bf2f(P.resid[o])));
+      }
+    }
+  } else if constexpr (EPI == kEpiQkv) {
+    // BF16 biased values back into the stage; q rows to out
+    const int qrows = P.kv.QH * kHeadDimTc;
+    for (int idx = threadIdx.x; idx < (n1 - n0) * kTileRows; idx += kThreads) {
+      const int n = n0 + (idx >> 7), row = row0 + (idx & 127);
+      if (row >= P.rows) continue;
+      float yv = rbf(stage[idx]);
+      if (P.bias != nullptr) yv = __fadd_rn(yv, P.bias[row]);
+      const __nv_bfloat16 b = f2bf(yv);
+      stage[idx] = bf2f(b);
+      if (row < qrows) P.out[static_cast<size_t>(n) * P.rows + row] = b;
+    }
+    // the tile's two heads per column: a k head is rotated at the column's
+    // position and stored as K, a v head stored as V (one warp per head)
+    if (row0 + kTileRows <= P.kv.QH * kHeadDimTc) return;  // q rows only
+    __shared__ int s_pos[kMaxN], s_slot[kMaxN];
+    for (int c = threadIdx.x; c < n1 - n0; c += kThreads) {
+      s_pos[c] = P.R.pos[n0 + c];
+      s_slot[c] = P.R.slot[n0 + c];
+    }
+    __syncthreads();
+    for (int u = warp; u < (n1 - n0) * 2; u += kThreads / 32) {
+      const int n = n0 + (u >> 1), hh = u & 1;
+      const int head = row0 / kHeadDimTc + hh;
+      if (head < P.kv.QH || head * kHeadDimTc >= P.rows) continue;
+      const float *v = stage + (n - n0) * kTileRows + hh * kHeadDimTc;
+      const int p = s_pos[n - n0], slot = s_slot[n - n0];
+      if (head < P.kv.QH + P.kv.KVH) {
+        __nv_bfloat16 lo, hi;
+        rope_vals(v[lane], v[lane + 32], P.kv.cos[p * 32 + lane], P.kv.sin[p * 32 + lane], lo, hi);
+        put_k(kv_rows(P.kv, slot, head - P.kv.QH, 0), p, lane, lo, hi);
+      } else {
+        put_v(kv_rows(P.kv, slot, head - P.kv.QH - P.kv.KVH, 1), p, lane, pack_bf16x2(v[2 * lane], v[2 * lane + 1]));
       }
     }
   } else if constexpr (EPI == kEpiSwiglu) {
@@ -240,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   const int S = P.stages;
   uint8_t *sa = smem;                                                   // [S][16 KB]
   uint8_t *sb = smem + static_cast<size_t>(S) * kAStageBytes;           // [S][npad * 128]
-  uint64_t *full = reinterpret_cast<uint64_t *>(sb + static_cast<size_t>(S) * P.npad * 128);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + gemm_data_bytes(S, P.npad, P.ksplit));
   uint64_t *empty = full + S;
   uint64_t *done = empty + S;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
@@ -264,19 +448,30 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_launch();
 
   const int k0 = split * P.kst / P.ksplit;
   const int nk = (split + 1) * P.kst / P.ksplit - k0;  // K stages of this slice (>= 1)
 
   if (warp == 0 && lane == 0) {
     // producer: a stage is one box of W's tile and one of the batch (full
-    // boxes: row groups past either end arrive as zeros and still count)
+    // boxes: row groups past either end arrive as zeros and still count).
+    // The first stages' weights do not depend on earlier kernels: they are
+    // requested before the wait for those kernels, the batch after it.
     const uint32_t bytes = kAStageBytes + static_cast<uint32_t>(P.npad) * 128;
-    int issued = 0;
-    for (int i = 0; i < nk; ++i) {
+    const int early = min(S, nk);
+    for (int i = 0; i < early; ++i) {
+      mbar_arrive_expect_tx(&full[i], bytes);
+      tma_load_3d(sa + static_cast<size_t>(i) * kAStageBytes, &P.map_w, 0, k0 + i, tile * 16, &full[i]);
+    }
+    grid_dep_wait();
+    for (int i = 0; i < early; ++i)
+      tma_load_3d(sb + static_cast<size_t>(i) * P.npad * 128, &P.map_x, 0, k0 + i, 0, &full[i]);
+    int issued = early;
+    for (int i = early; i < nk; ++i) {
       const int s = i % S;
       const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
-      if (i >= S && !mbar_wait(&empty[s], ph ^ 1u, P.ctrl, P.limit_ns, kWhereEmpty)) break;
+      if (!mbar_wait(&empty[s], ph ^ 1u, P.ctrl, P.limit_ns, kWhereEmpty)) break;
       mbar_arrive_expect_tx(&full[s], bytes);
       tma_load_3d(sa + static_cast<size_t>(s) * kAStageBytes, &P.map_w, 0, k0 + i, tile * 16, &full[s]);
       tma_load_3d(sb + static_cast<size_t>(s) * P.npad * 128, &P.map_x, 0, k0 + i, 0, &full[s]);
@@ -285,24 +480,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     // every load issued has landed before the CTA can exit
     for (int i = max(0, issued - S); i < issued; ++i)
       mbar_wait_quiet(&full[i % S], static_cast<uint32_t>(i / S) & 1u, P.limit_ns);
-  } else if (warp == 1 && lane == 0) {
-    // MMA issuer
-    const uint32_t idesc = idesc_bf16(P.npad);
-    for (int i = 0; i < nk; ++i) {
-      const int s = i % S;
-      const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
-      if (!mbar_wait(&full[s], ph, P.ctrl, P.limit_ns, kWhereFull)) break;
-      tc_fence_after();
-      const uint32_t a = smem_u32(sa + static_cast<size_t>(s) * kAStageBytes);
-      const uint32_t b = smem_u32(sb + static_cast<size_t>(s) * P.npad * 128);
+  } else {
+    grid_dep_wait();  // the epilogue reads what earlier kernels wrote
+    if (warp == 1 && lane == 0) {
+      // MMA issuer
+      const uint32_t idesc = idesc_bf16(P.npad);
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % S;
+        const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
+        if (!mbar_wait(&full[s], ph, P.ctrl, P.limit_ns, kWhereFull)) break;
+        tc_fence_after();
+        const uint32_t a = smem_u32(sa + static_cast<size_t>(s) * kAStageBytes);
+        const uint32_t b = smem_u32(sb + static_cast<size_t>(s) * P.npad * 128);
 #pragma unroll
-      for (int kk = 0; kk < kStageK / 16; ++kk) {
-        umma_bf16(tmem, smem_desc(a + kk * 256, 128, kGroupStageBytes), smem_desc(b + kk * 256, 128, kGroupStageBytes),
-                  idesc, (i | kk) != 0 ? 1u : 0u);
+        for (int kk = 0; kk < kStageK / 16; ++kk) {
+          umma_bf16(tmem, smem_desc(a + kk * 256, 128, kGroupStageBytes),
+                    smem_desc(b + kk * 256, 128, kGroupStageBytes), idesc, (i | kk) != 0 ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);  // the slot is free once these MMAs have read it
       }
-      umma_commit(&empty[s]);  // the slot is free once these MMAs have read it
+      umma_commit(done);  // also on an early exit: nothing in flight when TMEM is freed
     }
-    umma_commit(done);  // also on an early exit: nothing in flight when TMEM is freed
   }
   __syncwarp();
   // epilogue: wait for the accumulator (or, after an abort, for the MMAs in flight)
@@ -311,140 +509,102 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   tc_fence_after();
   const int r_t = warp * 32 + lane;  // this thread's row within the tile (its TMEM lane)
   const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  // one slice: the ring is idle now (every copy landed, every MMA done) and
-  // its space stages the tile's FP32 results [npad][128]; several slices:
-  // each leaves its partial for reduce_kernel
+  // the ring is idle now (every copy landed, every MMA done): its space
+  // stages the tile's FP32 results (this slice's partial) [npad][128]
   float *stage = reinterpret_cast<float *>(smem);
-  float *part = P.ksplit > 1 ? P.ws + (static_cast<size_t>(tile) * P.ksplit + split) * P.npad * kTileRows : nullptr;
   if (ok) {
     for (int c0 = 0; c0 < P.npad; c0 += 16) {
       uint32_t v[16];
       tmem_ld16(taddr + c0, v);
       tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        if (part != nullptr) {
-          part[static_cast<size_t>(c0 + j) * kTileRows + r_t] = __uint_as_float(v[j]);
-        } else {
-          stage[(c0 + j) * kTileRows + r_t] = __uint_as_float(v[j]);
-        }
-      }
+      for (int j = 0; j < 16; ++j) stage[(c0 + j) * kTileRows + r_t] = __uint_as_float(v[j]);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, ncols);
-  if (!ok || P.ksplit > 1) return;
-  finish_tile<EPI>(P, stage, tile, 0, P.N);
-}
-
-// Sums the K slices of column by of tile bx in slice order and applies the
-// epilogue (grid: tiles x N, 128 threads, a weight row per thread) -- a
-// tile's partials are spread over many CTAs, each with all its loads in
-// flight at once.
-template <int EPI>
-__global__ void __launch_bounds__(kThreads) reduce_kernel(const __grid_constant__ GemmParams P) {
-  __shared__ float stage[kTileRows];
-  const int tile = blockIdx.x, n = blockIdx.y;
-  const int r = threadIdx.x;
-  const size_t sstride = static_cast<size_t>(P.npad) * kTileRows;
-  const float *col = P.ws + static_cast<size_t>(tile) * P.ksplit * sstride + static_cast<size_t>(n) * kTileRows + r;
-  float acc = 0.f;
-  int s2 = 0;
-  for (; s2 + 16 <= P.ksplit; s2 += 16) {
-    float v[16];
-#pragma unroll
-    for (int u = 0; u < 16; ++u) v[u] = __ldcg(col + (s2 + u) * sstride);
-#pragma unroll
-    for (int u = 0; u < 16; ++u) acc += v[u];
+  if (P.ksplit == 1) {
+    if (ok) finish_tile<EPI>(P, stage, tile, 0, P.N);
+    return;
   }
-  if (s2 < P.ksplit) {
-    float v[16];
+  // K slices: the tile's slices are one cluster (rank = slice).  Once every
+  // partial is staged, slice s sums columns [s N / ksplit, (s + 1) N /
+  // ksplit) -- a contiguous block of each slice's partial, read as 16-byte
+  // vectors through distributed shared memory, every load in flight at once
+  // -- in slice order (the result does not depend on which slice finishes
+  // first) and finishes them.  Every CTA reaches both cluster barriers, on
+  // an abort too, and none exits while a peer may still read its partial.
+  cluster_arrive();
+  cluster_wait();
+  const int n0 = split * P.N / P.ksplit, n1 = (split + 1) * P.N / P.ksplit;
+  float *red = stage + static_cast<size_t>(P.npad) * kTileRows;
+  if (ok) {
+    const uint32_t base = smem_u32(stage) + static_cast<uint32_t>(n0 * kTileRows * 4);
+    const int vecs = (n1 - n0) * (kTileRows / 4);  // float4s in the block
+    constexpr int kPer = 4;                          // float4s per thread per pass
+    for (int v0 = 0; v0 < vecs; v0 += kPer * kThreads) {
+      float4 acc[kPer];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) v[u] = s2 + u < P.ksplit ? __ldcg(col + (s2 + u) * sstride) : 0.f;
+      for (int u = 0; u < kPer; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int u = 0; u < 16; ++u)
-      if (s2 + u < P.ksplit) acc += v[u];
+      for (int sl = 0; sl < kMaxSlices; ++sl) {
+        if (sl >= P.ksplit) break;
+        const uint32_t peer = cluster_addr(base, static_cast<uint32_t>(sl));
+        float4 v[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+          const int idx = v0 + u * kThreads + threadIdx.x;
+          v[u] = idx < vecs ? ld_cluster_f32x4(peer + static_cast<uint32_t>(idx) * 16u) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+          acc[u].x += v[u].x;
+          acc[u].y += v[u].y;
+          acc[u].z += v[u].z;
+          acc[u].w += v[u].w;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        const int idx = v0 + u * kThreads + threadIdx.x;
+        if (idx < vecs) reinterpret_cast<float4 *>(red)[idx] = acc[u];
+      }
+    }
   }
-  stage[r] = acc;
+  cluster_arrive();
   __syncthreads();
-  finish_tile<EPI>(P, stage, tile, n, n + 1);
+  if (ok) finish_tile<EPI>(P, red, tile, n0, n1);
+  cluster_wait();
 }
 
 // ---- per-row kernels of the batched step ---------------------------------------
-// Row metadata of a batched step (device arrays of n entries).
-struct Rows {
-  const int *slot, *pos, *tok;
-};
-
-// h[n][:] = the embedding row of token tok[n] (generate.py:758-768).
-__global__ void embed_kernel(const __nv_bfloat16 *embed, const int *tok, int H, __nv_bfloat16 *h) {
-  const int n = blockIdx.x;
-  const uint4 *src = reinterpret_cast<const uint4 *>(embed + static_cast<size_t>(tok[n]) * H);
-  uint4 *dst = reinterpret_cast<uint4 *>(h + static_cast<size_t>(n) * H);
-  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = __ldg(src + i);
-}
-
 // Row n of out (packed row-group layout) = bf16((x * inv_rms) * gamma) of
-// row rows[n] of x, or of row n when rows is NULL (cpu_backend.py:71-76);
-// one CTA of 128 threads per row.
-__global__ void norm_pack_kernel(const __nv_bfloat16 *x, const int *rows, const float *gamma, float eps, int H,
-                                 uint8_t *out) {
-  __shared__ float part[4];
-  const int n = blockIdx.x, tid = threadIdx.x;
-  const int src = rows ? rows[n] : n;
-  const uint32_t *row = reinterpret_cast<const uint32_t *>(x + static_cast<size_t>(src) * H);
-  float ss = 0.f;
-  for (int i = tid; i < H / 2; i += blockDim.x) {
-    const uint32_t w = row[i];
-    ss = fmaf(bf_lo(w), bf_lo(w), ss);
-    ss = fmaf(bf_hi(w), bf_hi(w), ss);
-  }
-  ss = warp_sum(ss);
-  if ((tid & 31) == 0) part[tid >> 5] = ss;
-  __syncthreads();
-  const float total = (part[0] + part[1]) + (part[2] + part[3]);
-  const float mean = __fdiv_rn(total, static_cast<float>(H));
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-  const int kc = H / 8;
-  for (int c = tid; c < kc; c += blockDim.x) {
-    const uint4 w = reinterpret_cast<const uint4 *>(row)[c];
-    const uint32_t in[4] = {w.x, w.y, w.z, w.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float a = __fmul_rn(__fmul_rn(bf_lo(in[e]), inv), gamma[8 * c + 2 * e]);
-      const float b = __fmul_rn(__fmul_rn(bf_hi(in[e]), inv), gamma[8 * c + 2 * e + 1]);
-      o[e] = pack_bf16x2(a, b);
-    }
-    *reinterpret_cast<uint4 *>(out + (static_cast<size_t>(n >> 3) * kc + c) * 128 + (n & 7) * 16) =
-        make_uint4(o[0], o[1], o[2], o[3]);
-  }
+// row rows[n] of x, or of row n when rows is NULL, for the n < count rows;
+// a warp per row, 4 rows per CTA.
+__global__ void __launch_bounds__(kThreads) norm_pack_kernel(const __nv_bfloat16 *x, const int *rows, int count,
+                                                             const float *gamma, float eps, int H, uint8_t *out) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const int n = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+  if (n >= count) return;
+  norm_pack_row(x + static_cast<size_t>(rows ? rows[n] : n) * H, gamma, eps, H, out, n);
 }
 
-struct KvArgs {
-  const __nv_bfloat16 *qkv;  // [N][QKV] BF16 (biased q / k / v)
-  int QKV, QH, KVH, group, H;
-  const float *cos, *sin;    // [ctx][32]
-  __nv_bfloat16 *kv;         // [slots][L][KVH][K | V][ctx][64], swizzled rows
-  int L, layer, ctx;
-};
-
-__device__ __forceinline__ uint8_t *kv_rows(const KvArgs &A, int slot, int j, int kind) {
-  return reinterpret_cast<uint8_t *>(A.kv) +
-         ((((static_cast<size_t>(slot) * A.L + A.layer) * A.KVH + j) * 2 + kind) * A.ctx * kHeadDimTc) * 2;
-}
-
-// Rotates each row's k and appends its K and V rows to its slot's cache at
-// its position (grid: rows x kv heads, one warp), before any row attends:
-// rows of one sequence in the same step see each other's keys.
-__global__ void kv_append_kernel(const __grid_constant__ KvArgs A, Rows R) {
-  const int n = blockIdx.x, j = blockIdx.y, lane = threadIdx.x;
-  const int p = R.pos[n], slot = R.slot[n];
-  const uint32_t *row = reinterpret_cast<const uint32_t *>(A.qkv + static_cast<size_t>(n) * A.QKV);
-  __nv_bfloat16 lo, hi;
-  rope_pair_cs(row + (A.QH + j) * 32, lane, A.cos[p * 32 + lane], A.sin[p * 32 + lane], lo, hi);
-  put_kv(kv_rows(A, slot, j, 0), kv_rows(A, slot, j, 1), p, lane, lo, hi, row[(A.QH + A.KVH + j) * 32 + lane]);
+// For the n < count rows: h[n][:] = the embedding row of token tok[n]
+// (generate.py:758-768) and row n of out = its RMS norm with the first
+// layer's gamma; a warp per row, 4 rows per CTA.
+__global__ void __launch_bounds__(kThreads) embed_norm_kernel(const __nv_bfloat16 *embed, const int *tok, int count,
+                                                              const float *gamma, float eps, int H,
+                                                              __nv_bfloat16 *h, uint8_t *out) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const int n = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (n >= count) return;
+  const __nv_bfloat16 *src = embed + static_cast<size_t>(tok[n]) * H;
+  uint4 *dst = reinterpret_cast<uint4 *>(h + static_cast<size_t>(n) * H);
+  for (int i = lane; i < H / 8; i += 32) dst[i] = __ldg(reinterpret_cast<const uint4 *>(src) + i);
+  norm_pack_row(src, gamma, eps, H, out, n);
 }
 
 // Attention of every (row, q head): a CTA per (row, kv head) copies that kv
@@ -453,6 +613,8 @@ __global__ void kv_append_kernel(const __grid_constant__ KvArgs A, Rows R) {
 // o-projection's packed input.
 __global__ void attention_kernel(const __grid_constant__ KvArgs A, Rows R, uint8_t *att) {
   extern __shared__ __align__(128) uint8_t sm[];
+  grid_dep_launch();
+  grid_dep_wait();
   const int n = blockIdx.x, j = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int p = R.pos[n], slot = R.slot[n];
   uint8_t *kb = sm, *vb = sm + static_cast<size_t>(A.ctx) * 128;
@@ -482,6 +644,8 @@ __global__ void attention_kernel(const __grid_constant__ KvArgs A, Rows R, uint8
 __global__ void argmax_reduce_kernel(const float *pv, const int *pi, int tiles, int pstride, int *out) {
   __shared__ float sv[8];
   __shared__ int si[8];
+  grid_dep_launch();
+  grid_dep_wait();
   const int n = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float bv = -INFINITY;
   int bi = 0x7fffffff;

@@ -256,6 +256,19 @@ class B200DecoderEngine:
             ctypes.byref(self._argmax)))
         return int(self._argmax.value), out
 
+    def generate_rows(self, ids, n_new, slot=0):
+        """Greedy decode through the batched tensor-core step alone: the
+        prompt in one prefill pass, then one row per step.  Stops early when
+        the cache is full."""
+        first, _ = self.prefill_tc(ids, slot=slot)
+        out = [int(first)]
+        pos = len(ids)
+        while len(out) < n_new and pos < self.context:
+            am, _ = self.step_rows([slot], [out[-1]], [pos])
+            out.append(int(am[0]))
+            pos += 1
+        return out
+
     def sample_batch(self, rows, params, histories, uniforms):
         """Device selections for several rows of the last ``step_batch(...,
         device_logits=True)`` in one launch; a token per entry, None where the

@@ -17,6 +17,15 @@ request's own generator supplying its draw, so a seeded request yields the
 same tokens as alone; a row whose top-p nucleus is too large for the device
 is selected on the host from the same logits with its generator rewound.
 
+With ``prefill_chunk`` set the server drives the engine's batched
+tensor-core step instead (``step_rows``, up to ``max_rows`` rows a step):
+each decoding stream is one row and each prefilling stream up to
+``prefill_chunk`` consecutive prompt positions (chunked prefill), so a
+prompt takes a few steps rather than one per position, and the LM head runs
+only for the rows whose next token is wanted (the last prompt position and
+decode rows).  Sampled rows take their logits to the host and select with
+the request's own sampler.
+
 KV slots: ``max_batch`` slots for the running streams plus a small LRU pool
 that keeps shared prompt prefixes.  A request whose first ``prefix_tokens``
 ids match a kept prefix starts after it (the cached positions are copied into
@@ -64,15 +73,20 @@ class MultiStreamServer:
     need ``step_batch(..., device_logits=True)``, ``sample_batch`` and
     ``device_logits`` and the engine's ``vocab``."""
 
-    def __init__(self, engine, max_batch=8, prefix_tokens=16, prefix_slots=4, clock=time.perf_counter):
+    def __init__(self, engine, max_batch=8, prefix_tokens=16, prefix_slots=4, clock=time.perf_counter,
+                 prefill_chunk=0, max_rows=128):
         if max_batch < 1:
             raise ValueError("max_batch must be >= 1")
         if engine.max_slots < max_batch + prefix_slots:
             raise ValueError(f"engine has {engine.max_slots} KV slots, needs {max_batch + prefix_slots}")
+        if prefill_chunk and not 1 <= max_batch <= max_rows:
+            raise ValueError("with prefill_chunk, max_batch must be in [1, max_rows]")
         self.engine = engine
         self.max_batch = max_batch
         self.prefix_tokens = prefix_tokens
         self.clock = clock
+        self.prefill_chunk = int(prefill_chunk)
+        self.max_rows = int(max_rows)
         self.stream_slots = list(range(max_batch))
         self.prefix_pool = list(range(max_batch, max_batch + prefix_slots))
         self.prefixes = OrderedDict()   # prefix ids -> slot holding their positions
@@ -144,6 +158,9 @@ class MultiStreamServer:
         while queue or active:
             while queue and free and len(active) < self.max_batch:
                 active.append(self._admit(queue.pop(), free))
+            if self.prefill_chunk:
+                active = self._step_rows(active, free, context)
+                continue
             slots = [st.slot for st in active]
             tokens = [st.token for st in active]
             positions = [st.pos for st in active]
@@ -181,3 +198,61 @@ class MultiStreamServer:
                     still.append(st)
             active = still
         return requests
+
+    def _step_rows(self, active, free, context):
+        """One batched tensor-core step: a row per decoding stream, then up
+        to ``prefill_chunk`` prompt positions per prefilling stream while the
+        row budget lasts.  Returns the streams still running."""
+        budget = self.max_rows
+        plan = []  # (stream, first position, rows)
+        for st in active:
+            if st.pos >= len(st.req.prompt) - 1:
+                plan.append((st, st.pos, 1))
+                budget -= 1
+        for st in active:
+            last_prompt = len(st.req.prompt) - 1
+            if st.pos < last_prompt and budget > 0:
+                take = min(self.prefill_chunk, last_prompt + 1 - st.pos, budget)
+                plan.append((st, st.pos, take))
+                budget -= take
+        slots, tokens, positions, out_rows, wanted = [], [], [], [], []
+        for st, p0, take in plan:
+            prompt = st.req.prompt
+            for k in range(take):
+                p = p0 + k
+                slots.append(st.slot)
+                positions.append(p)
+                tokens.append(int(prompt[p]) if p < len(prompt) else st.token)
+            if p0 + take - 1 >= len(prompt) - 1:  # this row's next token is wanted
+                out_rows.append(len(slots) - 1)
+                wanted.append(st)
+        sampled = [j for j, st in enumerate(wanted) if st.req.sampler is not None and not st.req.sampler.greedy]
+        rows = out_rows or [len(slots) - 1]
+        argmax, logits = self.engine.step_rows(slots, tokens, positions, logits=bool(sampled), out_rows=rows)
+        picks = [int(t) for t in argmax[: len(wanted)]]
+        for j in sampled:
+            req = wanted[j].req
+            picks[j] = int(req.sampler.select(np.asarray(logits[j]), list(req.prompt) + list(req.tokens)))
+        self.launches += 1
+        self.rows += len(slots)
+        now = self.clock()
+        nxt = dict(zip((id(st) for st in wanted), picks))
+        done = set()
+        for st, p0, take in plan:
+            req = st.req
+            before = st.pos
+            st.pos = p0 + take
+            if id(st) in nxt:
+                req.tokens.append(nxt[id(st)])
+                if len(req.tokens) == 1:
+                    req.first_token = now
+                st.token = nxt[id(st)]
+            else:
+                st.token = int(req.prompt[st.pos])
+            if before < self.prefix_tokens <= st.pos:
+                self._keep_prefix(st)
+            if len(req.tokens) >= req.new_tokens or st.pos >= context:
+                req.finished = now
+                free.append(st.slot)
+                done.add(id(st))
+        return [st for st in active if id(st) not in done]

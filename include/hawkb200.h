@@ -298,8 +298,9 @@ int hb_read_logits(hb_engine *engine, int n_rows, float *logits_out);
  * pack_matrix_bytes); x_dev: BF16 n x k activations in the same layout, n
  * rounded up to a multiple of 8 rows; y_dev: FP32 [n][rows].  rows a
  * multiple of 8, k of 64, 1 <= n <= 256, operands 16-byte aligned.  The
- * caller owns scratch_dev (hb_tc_gemm_scratch_bytes); each call clears its
- * control block and counters, so calls on one scratch must not overlap.
+ * caller owns scratch_dev (hb_tc_gemm_scratch_bytes: the control block;
+ * split-K partial sums stay in the cluster's shared memory); each call
+ * clears it, so calls on one scratch must not overlap.
  * Asynchronous on `stream`; hb_tc_gemm_status() waits for the stream and
  * reports a device-side wait that gave up. */
 size_t hb_tc_gemm_scratch_bytes(int rows, int k, int n);

@@ -62,8 +62,9 @@ def test_tc_gemm_matches_float64(rows, k, n):
 
 
 def test_tc_gemm_is_deterministic():
-    """Split-K partials are summed in slice order by whichever slice
-    arrives last: repeated calls give identical bits."""
+    """Split-K partials are summed in slice order across the tile's
+    cluster, whichever slice finishes first: repeated calls give identical
+    bits."""
     rng = np.random.default_rng(5)
     w = rng.standard_normal((896, 4864), dtype=np.float32).astype(bfloat16)
     x = rng.standard_normal((48, 4864), dtype=np.float32).astype(bfloat16)

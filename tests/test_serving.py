@@ -41,6 +41,23 @@ class FakeEngine:
         return [None if p.top_p < 1.0 else select_with_uniform(self.logits[i], h, p, u)
                 for i, p, h, u in zip(rows, params, histories, uniforms)]
 
+    def step_rows(self, slots, tokens, positions, logits=False, out_rows=None):
+        """The batched step: every row's position is cached before any row
+        reads (rows of one slot see each other); outputs for out_rows."""
+        assert len(slots) <= 128
+        assert len(set(zip(slots, positions))) == len(slots), "two rows write one slot position"
+        self.row_steps = getattr(self, "row_steps", []) + [len(slots)]
+        for s, t, p in zip(slots, tokens, positions):
+            self.cache[s][p] = t
+        rows = range(len(slots)) if out_rows is None else out_rows
+        out, lg = [], []
+        for i in rows:
+            hist = self.cache[slots[i]][: positions[i] + 1]
+            assert None not in hist, f"row {i} reads an unwritten position"
+            out.append(hash(tuple(hist)) % self.vocab)
+            lg.append(fake_logits(hist, self.vocab))
+        return np.array(out), (np.stack(lg) if logits else None)
+
     def device_logits(self, rows=1):
         return np.stack(self.logits[:rows])
 
@@ -161,6 +178,49 @@ def test_sampled_requests_in_continuous_batching():
         assert r.tokens == want, r.rid
 
 
+def test_chunked_prefill_rows_match_single_streams():
+    """Rows mode (the batched tensor-core step): prompts advance up to 8
+    positions a step, decode streams one; the same tokens as single streams,
+    far fewer steps than one position per launch, prefixes reused, the row
+    budget respected."""
+    eng = FakeEngine(max_slots=36)
+    reqs = config5_requests()
+    server = MultiStreamServer(eng, max_batch=32, prefix_slots=4, prefill_chunk=8, max_rows=48)
+    server.run(reqs)
+    for r in reqs:
+        assert r.tokens == reference_tokens(r.prompt, r.new_tokens), r.rid
+    assert max(eng.row_steps) <= 48 and max(eng.row_steps) > 32
+    per_position = MultiStreamServer(FakeEngine(max_slots=36), max_batch=32, prefix_slots=4)
+    per_position.run(config5_requests())
+    assert server.launches < per_position.launches
+    # the 8 sharing requests among the first 32 admitted compute the prefix
+    # themselves; the 8 admitted later reuse it
+    reused = [r for r in reqs if r.reused_prefix]
+    assert len(reused) >= 6 and all(r.reused_prefix == 16 for r in reused)
+
+
+def test_chunked_prefill_rows_with_sampling_and_context_limit():
+    eng = FakeEngine(max_slots=12)
+    reqs = _sampled_requests(eng.vocab)
+    MultiStreamServer(eng, max_batch=8, prefix_slots=4, prefill_chunk=5, max_rows=16).run(reqs)
+    alone = _sampled_requests(eng.vocab)
+    for r, a in zip(reqs, alone):
+        hist, want = list(a.prompt), []
+        while len(want) < a.new_tokens:
+            nxt = hash(tuple(hist)) % eng.vocab
+            if a.sampler is not None and not a.sampler.greedy:
+                nxt = a.sampler.select(fake_logits(hist, eng.vocab), list(a.prompt) + want)
+            want.append(int(nxt))
+            hist.append(int(nxt))
+        assert r.tokens == want, r.rid
+    eng = FakeEngine(max_slots=2, context=20)
+    req = Request(prompt=list(range(18)), new_tokens=10)
+    MultiStreamServer(eng, max_batch=1, prefix_slots=1, prefill_chunk=4).run([req])
+    assert req.tokens == reference_tokens(req.prompt, 10, context=20)[:3]
+    with pytest.raises(ValueError):
+        MultiStreamServer(FakeEngine(max_slots=200), max_batch=130, prefix_slots=4, prefill_chunk=4)
+
+
 def test_context_limit_and_validation():
     eng = FakeEngine(max_slots=2, context=20)
     req = Request(prompt=list(range(18)), new_tokens=10)
@@ -223,5 +283,35 @@ def test_gpu_sampled_multistream_matches_each_request_alone():
             engine.reset()
             MultiStreamServer(engine, max_batch=8, prefix_slots=4).run([a])
             assert r.tokens == a.tokens, r.rid
+    finally:
+        engine.close()
+
+
+@pytest.mark.gpu
+def test_gpu_chunked_rows_match_batched_single_streams():
+    """Rows mode on the tensor-core step: 40 ragged requests, 32 streams,
+    8-position prefill chunks.  A row's arithmetic does not depend on the
+    other rows of its step, so every request's tokens equal the same
+    request generated alone through the batched step."""
+    from runtime import synthetic
+    from runtime.b200_engine import B200DecoderEngine
+
+    model = synthetic.build("tiny-qwen", seed=31)
+    engine = B200DecoderEngine(model, max_slots=40, max_batch=8)
+    try:
+        rng = np.random.default_rng(9)
+        shared = rng.integers(0, model.shape.vocab, 16).tolist()
+        reqs = []
+        for i in range(40):
+            ids = rng.integers(0, model.shape.vocab, int(rng.integers(8, 40))).tolist()
+            if i % 4 == 0:
+                ids = shared + ids[:8]
+            reqs.append(Request(prompt=ids, new_tokens=6, rid=i))
+        server = MultiStreamServer(engine, max_batch=32, prefix_slots=4, prefill_chunk=8, max_rows=64)
+        server.run(reqs)
+        assert server.rows > 2 * server.launches
+        for r in reqs:
+            assert r.tokens == engine.generate_rows(r.prompt, r.new_tokens, slot=39), f"request {r.rid}"
+        assert any(r.reused_prefix for r in reqs)
     finally:
         engine.close()
