@@ -35,6 +35,13 @@ int choose_stages(int npad, int ksplit, int kst) {
   return std::max(1, std::min({6, s, (kst + ksplit - 1) / ksplit}));
 }
 
+// Ring stages of the persistent LM head: at most 6 within about 200 KB.
+int head_stages(int npad) {
+  const size_t per = hb::tc::kAStageBytes + static_cast<size_t>(npad) * 128;
+  const size_t fixed = hb::tc::head_smem_bytes(0, npad);
+  return std::max(2, std::min(6, static_cast<int>((200u * 1024u - fixed) / per)));
+}
+
 struct GemmShape {
   int tiles, ksplit, kst, npad, stages;
 };
@@ -203,6 +210,10 @@ int batch_setup(hb_engine *e) {
                         reinterpret_cast<const void *>(hb::tc::gemm_kernel<4>)};
   for (const void *fn : fns)
     HB_CUDA(e, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  size_t head_smem = 0;
+  for (int n = 16; n <= kMaxRows; n += 16) head_smem = std::max(head_smem, hb::tc::head_smem_bytes(head_stages(n), n));
+  HB_CUDA(e, cudaFuncSetAttribute(hb::tc::lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(head_smem)));
   return HB_OK;
 }
 
@@ -216,6 +227,24 @@ int gemm(hb_engine *e, const uint8_t *w, int rows, int K, const uint8_t *x, int 
   P.ctrl = batch_ctrl(b);
   P.limit_ns = e->limit_ns;
   HB_CUDA(e, launch_gemm<EPI>(g, P, e->stream));
+  return HB_OK;
+}
+
+// The LM head over every vocabulary tile (persistent lm_head_kernel, one CTA
+// per SM at most): FP32 logits when P.y is set, per-tile column maxima.
+int lm_head(hb_engine *e, const uint8_t *w, int rows, int K, const uint8_t *x, int n, hb::tc::GemmParams P) {
+  hb_batch *b = e->batch;
+  GemmShape g{};
+  g.tiles = (rows + hb::tc::kTileRows - 1) / hb::tc::kTileRows;
+  g.kst = K / hb::tc::kStageK;
+  g.npad = hb::tc::pad_n(n);
+  g.ksplit = 1;
+  g.stages = head_stages(g.npad);
+  if (!gemm_params(P, g, w, rows, K, x, n)) return fail(e, HB_ERR_CUDA, "batched step: tensor map encoding failed");
+  P.ctrl = batch_ctrl(b);
+  P.limit_ns = e->limit_ns;
+  HB_CUDA(e, launch_early(hb::tc::lm_head_kernel, dim3(std::min(g.tiles, b->sms)), dim3(hb::tc::kHeadThreads),
+                          hb::tc::head_smem_bytes(g.stages, g.npad), e->stream, 1, P));
   return HB_OK;
 }
 
@@ -293,7 +322,7 @@ int batch_record(hb_engine *e, int n, int n_out, bool want_logits) {
   P.part_val = b->part_val;
   P.part_idx = b->part_idx;
   P.pstride = kMaxRows;
-  if ((rc = gemm<hb::tc::kEpiLogits>(e, e->d_blob + d.w_lm, d.vocab, H, b->xn, n_out, P))) return rc;
+  if ((rc = lm_head(e, e->d_blob + d.w_lm, d.vocab, H, b->xn, n_out, P))) return rc;
   HB_CUDA(e, launch_early(hb::tc::argmax_reduce_kernel, dim3(n_out), dim3(256), 0, st, 1,
                           static_cast<const float *>(b->part_val), static_cast<const int *>(b->part_idx), b->lm_tiles,
                           kMaxRows, b->d_argmax));

@@ -578,6 +578,201 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   cluster_wait();
 }
 
+// ---- persistent LM head -----------------------------------------------------------
+// logits[n][r] = sum_k W[r][k] X[n][k] over the whole vocabulary with each
+// tile's per-column maximum (np.argmax order) for argmax_reduce_kernel.
+// One CTA per SM walks tiles blockIdx.x, blockIdx.x + gridDim.x, ...: warp 0
+// lane 0 streams every (tile, K stage) of the CTA through one ring without
+// a break between tiles, warp 1 lane 0 accumulates tile t into TMEM buffer
+// t & 1, and warps 2..5 (TMEM lane quarters 2, 3, 0, 1) read a finished
+// buffer -- the optional FP32 logits, then the tile transposed through
+// shared memory and one thread per column scanning its 128 rows -- while
+// the next tile's MMAs run.  (A shuffle reduction per column, unrolled over
+// the columns, is tens of KB of code that misses the instruction cache on
+// every pass; the scan loop is a few instructions.)
+constexpr int kHeadThreads = 192;
+constexpr int kHeadEpiWarps = 4;
+
+__host__ __device__ inline size_t head_ring_bytes(int stages, int npad) {
+  return static_cast<size_t>(stages) * (kAStageBytes + static_cast<size_t>(npad) * 128);
+}
+constexpr int kHeadStride = kTileRows + 1;  // transposed tile row pitch (floats): conflict-free
+// ring | full[S] empty[S] acc_full[2] acc_empty[2] done | tmem slot | tile [npad][129] FP32
+__host__ __device__ inline size_t head_smem_bytes(int stages, int npad) {
+  return head_ring_bytes(stages, npad) + 8 * (2 * static_cast<size_t>(stages) + 5) + 16 +
+         static_cast<size_t>(npad) * kHeadStride * 4;
+}
+
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+// Named barrier over `threads` threads that also ANDs `pred` across them.
+__device__ __forceinline__ bool named_and(int id, int threads, bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, r;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred r, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, r;\n\t}"
+      : "=r"(out)
+      : "r"(pred ? 1u : 0u), "r"(id), "r"(threads)
+      : "memory");
+  return out != 0;
+}
+
+__global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const __grid_constant__ GemmParams P) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int S = P.stages;
+  uint8_t *sa = smem;
+  uint8_t *sb = smem + static_cast<size_t>(S) * kAStageBytes;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + head_ring_bytes(S, P.npad));
+  uint64_t *empty = full + S;
+  uint64_t *acc_full = empty + S;    // [2] an accumulator buffer holds a finished tile
+  uint64_t *acc_empty = acc_full + 2;  // [2] the epilogue has read it
+  uint64_t *done = acc_empty + 2;      // every MMA of this CTA has completed
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+  float *tpose = reinterpret_cast<float *>(tmem_slot + 4);  // [npad][kHeadStride]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t ncols = tmem_cols(2 * P.npad);
+  const int mine = (P.tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                   static_cast<int>(gridDim.x);  // tiles of this CTA
+  const int total = mine * P.kst;                // (tile, K stage) steps
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kHeadEpiWarps);
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, ncols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  grid_dep_launch();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // producer; the first stages' weights are requested before the wait
+      // for the previous kernel, the batch rows after it
+      const uint32_t bytes = kAStageBytes + static_cast<uint32_t>(P.npad) * 128;
+      const int early = min(S, total);
+      for (int it = 0; it < early; ++it) {
+        const int tile = static_cast<int>(blockIdx.x) + (it / P.kst) * static_cast<int>(gridDim.x);
+        mbar_arrive_expect_tx(&full[it], bytes);
+        tma_load_3d(sa + static_cast<size_t>(it) * kAStageBytes, &P.map_w, 0, it % P.kst, tile * 16, &full[it]);
+      }
+      grid_dep_wait();
+      for (int it = 0; it < early; ++it)
+        tma_load_3d(sb + static_cast<size_t>(it) * P.npad * 128, &P.map_x, 0, it % P.kst, 0, &full[it]);
+      int issued = early;
+      for (int it = early; it < total; ++it) {
+        const int s = it % S;
+        const uint32_t ph = static_cast<uint32_t>(it / S) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, P.ctrl, P.limit_ns, kWhereEmpty)) break;
+        const int tile = static_cast<int>(blockIdx.x) + (it / P.kst) * static_cast<int>(gridDim.x);
+        mbar_arrive_expect_tx(&full[s], bytes);
+        tma_load_3d(sa + static_cast<size_t>(s) * kAStageBytes, &P.map_w, 0, it % P.kst, tile * 16, &full[s]);
+        tma_load_3d(sb + static_cast<size_t>(s) * P.npad * 128, &P.map_x, 0, it % P.kst, 0, &full[s]);
+        ++issued;
+      }
+      for (int it = max(0, issued - S); it < issued; ++it)
+        mbar_wait_quiet(&full[it % S], static_cast<uint32_t>(it / S) & 1u, P.limit_ns);
+    }
+  } else if (warp == 1) {
+    grid_dep_wait();
+    if (lane == 0) {
+      // MMA issuer: tile t into TMEM columns [(t & 1) npad, + npad)
+      const uint32_t idesc = idesc_bf16(P.npad);
+      bool go = true;
+      for (int t = 0; t < mine && go; ++t) {
+        const int buf = t & 1;
+        if (t >= 2 && !mbar_wait(&acc_empty[buf], static_cast<uint32_t>((t >> 1) - 1) & 1u, P.ctrl, P.limit_ns,
+                                 kWhereEmpty))
+          break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * P.npad);
+        for (int k = 0; k < P.kst; ++k) {
+          const int it = t * P.kst + k;
+          const int s = it % S;
+          if (!mbar_wait(&full[s], static_cast<uint32_t>(it / S) & 1u, P.ctrl, P.limit_ns, kWhereFull)) {
+            go = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(sa + static_cast<size_t>(s) * kAStageBytes);
+          const uint32_t b = smem_u32(sb + static_cast<size_t>(s) * P.npad * 128);
+#pragma unroll
+          for (int kk = 0; kk < kStageK / 16; ++kk)
+            umma_bf16(d, smem_desc(a + kk * 256, 128, kGroupStageBytes), smem_desc(b + kk * 256, 128, kGroupStageBytes),
+                      idesc, (k | kk) != 0 ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (go) umma_commit(&acc_full[buf]);
+      }
+      umma_commit(done);  // also on an early exit: nothing in flight when TMEM is freed
+    }
+  } else {
+
+    // epilogue warps 2..5: warp w reads TMEM lanes 32 (w % 4) .. + 31
+    grid_dep_wait();
+    const int q = warp & 3;
+    for (int t = 0; t < mine; ++t) {
+      const int buf = t & 1;
+      // the four warps agree before any of them waits at a named barrier
+      if (!named_and(1, kHeadEpiWarps * 32,
+                     mbar_wait(&acc_full[buf], static_cast<uint32_t>(t >> 1) & 1u, P.ctrl, P.limit_ns, kWhereFull)))
+        break;
+      tc_fence_after();
+      const int tile = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
+      const int row = tile * kTileRows + q * 32 + lane;
+      const bool valid = row < P.rows;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * P.npad);
+      for (int c0 = 0; c0 < P.N; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(taddr + c0, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float val = __uint_as_float(v[j]);
+          if (valid && c0 + j < P.N && P.y != nullptr) P.y[static_cast<size_t>(c0 + j) * P.rows + row] = val;
+          tpose[(c0 + j) * kHeadStride + q * 32 + lane] = val;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_count(&acc_empty[buf], 1);  // the buffer may take the next tile
+      named_sync(1, kHeadEpiWarps * 32);
+      const int live = min(kTileRows, P.rows - tile * kTileRows);  // rows of this tile inside W
+      for (int n = (warp - 2) * 32 + lane; n < P.N; n += kHeadEpiWarps * 32) {
+        const float *col = tpose + n * kHeadStride;
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll 4
+        for (int r = 0; r < live; ++r) argmax_merge(bv, bi, col[r], tile * kTileRows + r);
+        P.part_val[static_cast<size_t>(tile) * P.pstride + n] = bv;
+        P.part_idx[static_cast<size_t>(tile) * P.pstride + n] = bi;
+      }
+      named_sync(1, kHeadEpiWarps * 32);  // the transposed tile may be overwritten
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    mbar_wait_quiet(done, 0, P.limit_ns);
+    tc_fence_after();
+    tmem_dealloc(tmem, ncols);
+  }
+}
+
 // ---- per-row kernels of the batched step ---------------------------------------
 // Row n of out (packed row-group layout) = bf16((x * inv_rms) * gamma) of
 // row rows[n] of x, or of row n when rows is NULL, for the n < count rows;
