@@ -64,6 +64,9 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-extras", action="store_true",
                    help="skip the config 1/2/4/5 measurements (profiling runs of config 3 only)")
+    p.add_argument("--profile-rows", type=int, default=0, metavar="N",
+                   help="profiling entry: run the N-row batched tensor-core step --warmup + --steps times "
+                        "and print its mean time (no metric line)")
     return p.parse_args()
 
 
@@ -724,8 +727,35 @@ def run_decode_token_request(decoder, prompt):
     return generated, ttft, decode
 
 
+def run_profile_rows(args, n):
+    """The batched tensor-core step on its own, for ncu captures: n rows
+    (stream i in KV slot i at position 40, the Qwen2.5-0.5B shape, BF16)."""
+    import torch
+    from runtime import synthetic
+    from runtime.b200_engine import B200DecoderEngine
+
+    model = synthetic.build("qwen2.5-0.5b", seed=MODEL_SEED).materialize()
+    engine = B200DecoderEngine(model, max_slots=max(n, 8) + 4, max_batch=8)
+    try:
+        tokens = synthetic.prompt_ids(model.shape.vocab, n, seed=MODEL_SEED + 9)
+        rows = (list(range(n)), tokens, [40] * n)
+        for _ in range(args.warmup):
+            engine.step_rows(*rows)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            engine.step_rows(*rows)
+        ms = 1000 * (time.perf_counter() - t0) / max(1, args.steps)
+        print(f"profile-rows {n}: {ms:.3f} ms per step (host wall, {args.steps} steps)", flush=True)
+    finally:
+        engine.close()
+
+
 def main():
     args = parse()
+    if args.profile_rows:
+        run_profile_rows(args, args.profile_rows)
+        return
     rank, world, local = dist_setup(args.gpus)
     try:
         if args.impl == "reference":

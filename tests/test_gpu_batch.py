@@ -59,6 +59,22 @@ def test_prefill_tc_matches_oracle_and_sequential_cache(tiny):
     cache_close(engine.kv_cache(1)[:, :, :, :n], engine.kv_cache(0)[:, :, :, :n], "prefill cache")
 
 
+def test_prefill_tc_in_one_pass_equals_row_by_row(tiny):
+    """A row's arithmetic does not depend on the other rows of its step:
+    prefilling 20 positions in one batched pass leaves the same K/V bits and
+    the same last-position logits as 20 one-row batched steps."""
+    model, engine = tiny
+    engine.reset()
+    ids = synthetic.prompt_ids(model.shape.vocab, 20, seed=11)
+    first, one_pass = engine.prefill_tc(ids, slot=2, logits=True)
+    for p, t in enumerate(ids):
+        am, last = engine.step_rows([3], [t], [p], logits=p == len(ids) - 1)
+    assert np.array_equal(one_pass, last[0])
+    assert first == int(am[0])
+    n = len(ids)
+    assert np.array_equal(engine.kv_cache(2)[:, :, :, :n], engine.kv_cache(3)[:, :, :, :n])
+
+
 def test_step_rows_across_streams_matches_single_rows(tiny):
     """Six sequences at different depths in one step: each row equals that
     sequence's own single-row step (tolerance), its cache row too."""
