@@ -67,6 +67,8 @@ def parse():
     p.add_argument("--profile-rows", type=int, default=0, metavar="N",
                    help="profiling entry: run the N-row batched tensor-core step --warmup + --steps times "
                         "and print its mean time (no metric line)")
+    p.add_argument("--profile-gemv", action="store_true",
+                   help="profiling entry: config 2 (standalone GEMV shapes) only, one JSON line per shape")
     return p.parse_args()
 
 
@@ -253,11 +255,9 @@ def run_other_configs(device, peak):
     """Configs 1, 2 and 4 on this GPU (single-GPU runs only): decode
     of the SmolLM2-135M shape (BF16) and of the Qwen shape in W8, and the
     standalone GEMV shapes with HBM GB/s against the roofline."""
-    import ctypes
     import numpy as np
     import torch
-    from ml_dtypes import bfloat16
-    from runtime import hb_lib, layout, synthetic
+    from runtime import layout, synthetic
     from runtime.b200_engine import B200DecoderEngine
 
     out = {}
@@ -288,12 +288,30 @@ def run_other_configs(device, peak):
     out["long_context_qwen_bf16"] = run_long_context(device, peak)
     # config 2: y = W x (BF16 out) and the LM head with a fused argmax;
     # rotating weight copies keep every launch's weights out of L2
-    lib = hb_lib.load()
     dev = torch.device("cuda", device)
     stream = torch.cuda.Stream(device=dev)
     rng = np.random.default_rng(MODEL_SEED + 2)
+    out["config2_gemv"] = measure_gemv(dev, stream, rng, peak)
+    return out
+
+
+CONFIG2_SHAPES = ((896, 896), (4864, 896), (896, 4864), (576, 1536), (151936, 896))
+
+
+def measure_gemv(dev, stream, rng, peak, n=40):
+    """Config 2: hb_gemv on each shape at batch 1 and 8 (the LM head with the
+    fused argmax and no logits), W and x ~ N(0, 1) in BF16; 5 warm-up and n
+    timed back-to-back launches on `stream`, rotating over copies of W that
+    together exceed L2 (256 MB) so every launch reads HBM."""
+    import ctypes
+    import numpy as np
+    import torch
+    from ml_dtypes import bfloat16
+    from runtime import hb_lib, layout
+
+    lib = hb_lib.load()
     gemv = []
-    for rows, k in ((896, 896), (4864, 896), (896, 4864), (576, 1536), (151936, 896)):
+    for rows, k in CONFIG2_SHAPES:
         w = rng.standard_normal((rows, k), dtype=np.float32).astype(bfloat16)
         packed = torch.from_numpy(layout.pack_matrix_bytes(w)).to(dev)
         copies = [packed] + [packed.clone() for _ in range(max(0, -(-256 * 2**20 // packed.numel()) - 1))]
@@ -314,7 +332,6 @@ def run_other_configs(device, peak):
                 for i in range(5):
                     launch(i)
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                n = 40
                 e0.record(stream)
                 for i in range(n):
                     launch(i)
@@ -325,8 +342,8 @@ def run_other_configs(device, peak):
             gemv.append({"rows": rows, "k": k, "batch": batch, "argmax": head, "us": us,
                          "gbs": nbytes / (us * 1e-6) / 1e9, "hbm_frac": nbytes / (us * 1e-6) / 1e9 / peak})
         del copies, packed
-    out["config2_gemv"] = gemv
-    return out
+    return gemv
+
 
 
 def barrier(world):
@@ -751,8 +768,23 @@ def run_profile_rows(args, n):
         engine.close()
 
 
+def run_profile_gemv():
+    """Config 2 on its own (the standalone GEMV shapes), for ncu launch lists
+    beside the CUDA-event times it prints."""
+    import numpy as np
+    import torch
+
+    dev = torch.device("cuda", 0)
+    for r in measure_gemv(dev, torch.cuda.Stream(device=dev), np.random.default_rng(MODEL_SEED + 2),
+                          measured_peak()[0]):
+        print(json.dumps(r), flush=True)
+
+
 def main():
     args = parse()
+    if args.profile_gemv:
+        run_profile_gemv()
+        return
     if args.profile_rows:
         run_profile_rows(args, args.profile_rows)
         return

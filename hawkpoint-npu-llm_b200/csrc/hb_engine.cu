@@ -775,6 +775,86 @@ int hb_test_stall_next(hb_engine *e, uint64_t limit_ns) {
 }
 
 // ------------------------------------------------------------------ GEMV --
+}  // extern "C"
+
+namespace {
+
+// Per device: the SM count and opt-in shared memory, queried once, and the
+// dynamic shared memory each GEMV kernel variant has been opted into, so a
+// call sets the attribute only when it needs more than any call before (the
+// attribute call and the queries cost more than a small GEMV's kernel).
+struct GemvDevice {
+  bool known = false;
+  int sms = 0, optin = 0;
+  int smem[4] = {0, 0, 0, 0};  // by variant: (batch 8) * 2 + W8
+};
+constexpr int kGemvDevices = 64;
+std::mutex g_gemv_mutex;
+GemvDevice g_gemv_device[kGemvDevices];
+
+int gemv_device(int *dev, int *sms, int *optin) {
+  if (cudaGetDevice(dev) != cudaSuccess || *dev < 0 || *dev >= kGemvDevices)
+    return fail(nullptr, HB_ERR_CUDA, "hb_gemv: no usable current CUDA device");
+  std::lock_guard<std::mutex> lock(g_gemv_mutex);
+  GemvDevice &g = g_gemv_device[*dev];
+  if (!g.known) {
+    if (cudaDeviceGetAttribute(&g.sms, cudaDevAttrMultiProcessorCount, *dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&g.optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, *dev) != cudaSuccess)
+      return fail(nullptr, HB_ERR_CUDA, "hb_gemv: device query failed");
+    g.known = true;
+  }
+  *sms = g.sms;
+  *optin = g.optin;
+  return HB_OK;
+}
+
+// Opts variant `v` (kernel fn) into `smem` bytes unless it already is;
+// forget=true drops the record first (a launch that failed after a device
+// reset lost the attribute).
+int gemv_opt_in(int dev, int v, const void *fn, size_t smem, bool forget) {
+  std::lock_guard<std::mutex> lock(g_gemv_mutex);
+  int &have = g_gemv_device[dev].smem[v];
+  if (forget) have = 0;
+  if (have >= static_cast<int>(smem)) return HB_OK;
+  const cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (err != cudaSuccess) return fail(nullptr, HB_ERR_CUDA, "hb_gemv: %s", cudaGetErrorString(err));
+  have = static_cast<int>(smem);
+  return HB_OK;
+}
+
+// The GEMV kernel of (batch rows mb, W8) and its variant index.
+const void *gemv_fn(int mb, bool w8, int *v) {
+  *v = (mb > 1 ? 2 : 0) + (w8 ? 1 : 0);
+  if (mb == 1)
+    return w8 ? reinterpret_cast<const void *>(&hb::gemv_kernel<1, true>)
+              : reinterpret_cast<const void *>(&hb::gemv_kernel<1, false>);
+  return w8 ? reinterpret_cast<const void *>(&hb::gemv_kernel<8, true>)
+            : reinterpret_cast<const void *>(&hb::gemv_kernel<8, false>);
+}
+
+// Launches a GEMV, retrying once with the attribute set again if the launch
+// fails (the device was reset since the attribute was recorded).
+int gemv_launch(int dev, int mb, bool w8, int grid, size_t smem, hb::GemvParams &P, cudaStream_t stream,
+                const char *who) {
+  int v = 0;
+  const void *fn = gemv_fn(mb, w8, &v);
+  int rc = gemv_opt_in(dev, v, fn, smem, false);
+  if (rc) return rc;
+  void *args[] = {&P};
+  cudaError_t err = cudaLaunchKernel(fn, dim3(grid), dim3(hb::kThreads), args, smem, stream);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    if ((rc = gemv_opt_in(dev, v, fn, smem, true))) return rc;
+    err = cudaLaunchKernel(fn, dim3(grid), dim3(hb::kThreads), args, smem, stream);
+  }
+  if (err != cudaSuccess) return fail(nullptr, HB_ERR_CUDA, "%s launch: %s", who, cudaGetErrorString(err));
+  return HB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 size_t hb_gemv_scratch_bytes(int rows, int batch) {
   (void)rows;
   (void)batch;
@@ -798,11 +878,9 @@ int hb_gemv(const void *w_dev, const float *scales_dev, int weight_format, int r
   const auto check = [](uintptr_t p) { return p % 16 == 0; };
   if (!check(reinterpret_cast<uintptr_t>(w_dev)) || !check(reinterpret_cast<uintptr_t>(x_dev)))
     return fail(nullptr, HB_ERR_INVALID_ARG, "hb_gemv: W and x must be 16-byte aligned");
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return fail(nullptr, HB_ERR_CUDA, "no CUDA device");
-  int sms = 0, optin = 0;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  int dev = 0, sms = 0, optin = 0;
+  int rc = gemv_device(&dev, &sms, &optin);
+  if (rc) return rc;
   const bool w8 = weight_format == HB_WEIGHTS_W8;
   const int esize = w8 ? 1 : 2;
   const int kc = k * esize / 16;
@@ -821,11 +899,6 @@ int hb_gemv(const void *w_dev, const float *scales_dev, int weight_format, int r
   int nslots = static_cast<int>((static_cast<size_t>(optin) - fixed - 16 * kMaxSlotsRing) / hb::kSlotBytes);
   nslots = std::min(nslots, kMaxSlotsRing);
   const size_t smem = hb::gemv_smem_bytes(nslots, mb, k, red_rows);
-  const void *fn;
-  if (mb == 1) fn = w8 ? reinterpret_cast<const void *>(&hb::gemv_kernel<1, true>) : reinterpret_cast<const void *>(&hb::gemv_kernel<1, false>);
-  else fn = w8 ? reinterpret_cast<const void *>(&hb::gemv_kernel<8, true>) : reinterpret_cast<const void *>(&hb::gemv_kernel<8, false>);
-  cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (err != cudaSuccess) return fail(nullptr, HB_ERR_CUDA, "hb_gemv: %s", cudaGetErrorString(err));
   hb::GemvParams P{};
   P.w = static_cast<const uint8_t *>(w_dev);
   P.scales = scales_dev;
@@ -845,10 +918,7 @@ int hb_gemv(const void *w_dev, const float *scales_dev, int weight_format, int r
   P.red_rows = red_rows;
   P.per_warp = per_warp;
   P.limit_ns = kDefaultLimitNs;
-  void *args[] = {&P};
-  err = cudaLaunchKernel(fn, dim3(G), dim3(hb::kThreads), args, smem, static_cast<cudaStream_t>(stream));
-  if (err != cudaSuccess) return fail(nullptr, HB_ERR_CUDA, "hb_gemv launch: %s", cudaGetErrorString(err));
-  return HB_OK;
+  return gemv_launch(dev, mb, w8, G, smem, P, static_cast<cudaStream_t>(stream), "hb_gemv");
 }
 
 }  // extern "C"
@@ -946,13 +1016,9 @@ int hb_gemv_noalloc(const void *w_dev, const float *scales_dev, int weight_forma
   if (reinterpret_cast<uintptr_t>(w_dev) % 16 || reinterpret_cast<uintptr_t>(x_dev) % 16)
     return noalloc_fail(HB_ERR_INVALID_ARG, "W and x must be 16-byte aligned");
 
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+  int dev = 0, sms = 0, optin = 0;
+  if (gemv_device(&dev, &sms, &optin) != HB_OK || dev >= kMaxDevices)
     return noalloc_fail(HB_ERR_CUDA, "no usable current CUDA device");
-  int sms = 0, optin = 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
-    return noalloc_fail(HB_ERR_CUDA, "device query failed");
   const int n_rg = rows / 8;
   const int G = sms < n_rg ? sms : n_rg;
   // one CTA per SM at most: this only guards a future grid with more CTAs
@@ -978,19 +1044,10 @@ int hb_gemv_noalloc(const void *w_dev, const float *scales_dev, int weight_forma
   int nslots = static_cast<int>((static_cast<size_t>(optin) - fixed - 16 * 16) / hb::kSlotBytes);
   if (nslots > 16) nslots = 16;
   const size_t smem = hb::gemv_smem_bytes(nslots, mb, k, red_rows);
-  const void *fn;
-  if (mb == 1)
-    fn = w8 ? reinterpret_cast<const void *>(&hb::gemv_kernel<1, true>)
-            : reinterpret_cast<const void *>(&hb::gemv_kernel<1, false>);
-  else
-    fn = w8 ? reinterpret_cast<const void *>(&hb::gemv_kernel<8, true>)
-            : reinterpret_cast<const void *>(&hb::gemv_kernel<8, false>);
-  cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (err != cudaSuccess) return noalloc_fail(HB_ERR_CUDA, cudaGetErrorString(err));
 
   // the control block must start at zero (done counter, error flags)
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  err = cudaMemsetAsync(scratch, 0, sizeof(hb::Ctrl), s);
+  cudaError_t err = cudaMemsetAsync(scratch, 0, sizeof(hb::Ctrl), s);
   if (err != cudaSuccess) return noalloc_fail(HB_ERR_CUDA, cudaGetErrorString(err));
 
   hb::GemvParams P{};
@@ -1012,10 +1069,7 @@ int hb_gemv_noalloc(const void *w_dev, const float *scales_dev, int weight_forma
   P.red_rows = red_rows;
   P.per_warp = per_warp;
   P.limit_ns = kDefaultLimitNs;
-  void *args[] = {&P};
-  err = cudaLaunchKernel(fn, dim3(G), dim3(hb::kThreads), args, smem, s);
-  if (err != cudaSuccess) return noalloc_fail(HB_ERR_CUDA, cudaGetErrorString(err));
-  return HB_OK;
+  return gemv_launch(dev, mb, w8, G, smem, P, s, "hb_gemv_noalloc");
 }
 
 }  // extern "C"
