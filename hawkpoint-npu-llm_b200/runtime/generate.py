@@ -69,6 +69,44 @@ def _load_tokenizer(model_dir, family):
     return SmolLMTokenizer(model_dir, default_system=system)
 
 
+def prepare_request(vocab, context, max_new_tokens, sampling, stop, logprobs):
+    """(sampler, stop matcher, top logprobs) of one request, with the
+    reference's argument checks (npu_llm/runtime/generate.py:1022-1035)."""
+    if not 0 < max_new_tokens < context:
+        raise ValueError(f"max_new_tokens must be between 1 and {context - 1}")
+    if sampling is None:
+        params = GREEDY
+    elif isinstance(sampling, SamplingParams):
+        params = sampling
+    else:
+        params = SamplingParams.from_dict(sampling)
+    stop_matcher = StopMatcher(normalize_stop(stop))
+    top_logprobs = normalize_logprobs(logprobs)
+    return Sampler(params, vocab_size=vocab), stop_matcher, top_logprobs
+
+
+def logprob_entry(tokenizer, logits, token_id, top_logprobs):
+    """OpenAI ``logprobs`` entry of `token_id` from the raw distribution."""
+    values = log_softmax(logits)
+
+    def describe(index):
+        return {
+            "token": tokenizer.decode([int(index)]),
+            "logprob": float(values[index]),
+            "bytes": list(tokenizer.token_bytes(int(index))),
+        }
+
+    entry = describe(token_id)
+    top = []
+    if top_logprobs:
+        count = min(top_logprobs, values.shape[0])
+        best = np.argpartition(values, -count)[-count:]
+        best = best[np.argsort(values[best])[::-1]]
+        top = [describe(i) for i in best]
+    entry["top_logprobs"] = top
+    return entry
+
+
 class NPUDecoder:
     """Greedy / sampled generation over the B200 decoder engine."""
 
@@ -275,44 +313,17 @@ class NPUDecoder:
         return entry
 
     def _logprob_entry(self, logits, token_id, top_logprobs):
-        """OpenAI ``logprobs`` entry from the raw distribution."""
-        values = log_softmax(logits)
-
-        def describe(index):
-            return {
-                "token": self.tokenizer.decode([int(index)]),
-                "logprob": float(values[index]),
-                "bytes": list(self.tokenizer.token_bytes(int(index))),
-            }
-
-        entry = describe(token_id)
-        top = []
-        if top_logprobs:
-            count = min(top_logprobs, values.shape[0])
-            best = np.argpartition(values, -count)[-count:]
-            best = best[np.argsort(values[best])[::-1]]
-            top = [describe(i) for i in best]
-        entry["top_logprobs"] = top
-        return entry
+        return logprob_entry(self.tokenizer, logits, token_id, top_logprobs)
 
     # -- generation ------------------------------------------------------------------
     def _prepare(self, max_new_tokens, sampling, stop, logprobs):
-        if not 0 < max_new_tokens < self.context_length:
-            raise ValueError(f"max_new_tokens must be between 1 and {self.context_length - 1}")
-        if sampling is None:
-            params = GREEDY
-        elif isinstance(sampling, SamplingParams):
-            params = sampling
-        else:
-            params = SamplingParams.from_dict(sampling)
-        stop_matcher = StopMatcher(normalize_stop(stop))
-        top_logprobs = normalize_logprobs(logprobs)
-        sampler = Sampler(params, vocab_size=self.model.metadata["vocab_size"])
+        prepared = prepare_request(self.model.metadata["vocab_size"], self.context_length, max_new_tokens,
+                                   sampling, stop, logprobs)
         if getattr(self, "_profile_enabled", False):
             self._phase_totals = {}
         if self.tokenizer is None:
             raise RuntimeError("the model package has no tokenizer; use decode_token with token ids")
-        return sampler, stop_matcher, top_logprobs
+        return prepared
 
     def generate_messages(self, messages, max_new_tokens=16, sampling=None, *, stop=None, logprobs=None):
         """Chat completion over an OpenAI-style message list, windowed to the

@@ -33,7 +33,7 @@ its slot with ``hb_copy_prefix``), the same reuse rule as the reference's
 prefix cache (``min(shared, len - 1)`` positions, generate.py:952-973).
 """
 
-from collections import OrderedDict
+from collections import OrderedDict, deque
 from dataclasses import dataclass, field
 import time
 
@@ -51,6 +51,10 @@ class Request:
     first_token: float = 0.0
     finished: float = 0.0
     reused_prefix: int = 0
+    eos: int = None            # a generated eos ends the request (the token is kept)
+    cancelled: bool = False    # set by the caller: the stream ends at the next step
+    want_logits: bool = False  # rows mode: hand each generated token's FP32 logits to the listener
+    listener: object = None    # listener(req, token, logits_or_None) per token; listener(req, None, None) at the end
 
     @property
     def ttft(self):
@@ -88,6 +92,9 @@ class MultiStreamServer:
         self.prefill_chunk = int(prefill_chunk)
         self.max_rows = int(max_rows)
         self.stream_slots = list(range(max_batch))
+        self._pending = deque()                    # submitted, not admitted
+        self._free = list(reversed(self.stream_slots))
+        self._active = []
         self.prefix_pool = list(range(max_batch, max_batch + prefix_slots))
         self.prefixes = OrderedDict()   # prefix ids -> slot holding their positions
         self.launches = 0
@@ -145,59 +152,98 @@ class MultiStreamServer:
                 tokens[k] = int(req.sampler.select(host[i], histories[k]))
         return tokens
 
-    def run(self, requests):
+    # -- incremental use: submit requests as they arrive, step while busy ------
+    def submit(self, req):
+        """Queue a request (checked now; admitted in arrival order)."""
         context = self.engine.context
-        for req in requests:
-            if not 1 <= len(req.prompt) < context:
-                raise ValueError(f"prompt of {len(req.prompt)} ids does not fit a {context}-token context")
-            if req.new_tokens < 1:
-                raise ValueError("new_tokens must be >= 1")
-        queue = list(reversed(requests))
-        free = list(reversed(self.stream_slots))
-        active = []
-        while queue or active:
-            while queue and free and len(active) < self.max_batch:
-                active.append(self._admit(queue.pop(), free))
-            if self.prefill_chunk:
-                active = self._step_rows(active, free, context)
-                continue
-            slots = [st.slot for st in active]
-            tokens = [st.token for st in active]
-            positions = [st.pos for st in active]
-            sampled = [i for i, st in enumerate(active)
-                       if st.pos >= len(st.req.prompt) - 1 and st.req.sampler is not None
-                       and not st.req.sampler.greedy]
-            if sampled:
-                argmax, _ = self.engine.step_batch(slots, tokens, positions, device_logits=True)
-                argmax = list(argmax)
-                for i, token in zip(sampled, self._sample_rows(active, sampled)):
-                    argmax[i] = token
+        if not 1 <= len(req.prompt) < context:
+            raise ValueError(f"prompt of {len(req.prompt)} ids does not fit a {context}-token context")
+        if req.new_tokens < 1:
+            raise ValueError("new_tokens must be >= 1")
+        self._pending.append(req)
+
+    @property
+    def busy(self):
+        return bool(self._pending or self._active)
+
+    def step(self):
+        """Admit what fits, drop cancelled streams, run one launch."""
+        while self._pending and self._free and len(self._active) < self.max_batch:
+            self._active.append(self._admit(self._pending.popleft(), self._free))
+        still = []
+        for st in self._active:
+            if st.req.cancelled:
+                self._finish(st, self.clock(), self._free)
             else:
-                argmax, _ = self.engine.step_batch(slots, tokens, positions)
-            self.launches += 1
-            self.rows += len(active)
-            now = self.clock()
-            still = []
-            for st, nxt in zip(active, argmax):
-                req = st.req
-                last_prompt = len(req.prompt) - 1
-                if st.pos < last_prompt:
-                    st.token = int(req.prompt[st.pos + 1])        # sequential prefill
-                else:
-                    req.tokens.append(int(nxt))
-                    if len(req.tokens) == 1:
-                        req.first_token = now
-                    st.token = int(nxt)
-                st.pos += 1
-                if st.pos == self.prefix_tokens:
-                    self._keep_prefix(st)
-                if len(req.tokens) >= req.new_tokens or st.pos >= context:
-                    req.finished = now
-                    free.append(st.slot)
-                else:
-                    still.append(st)
-            active = still
+                still.append(st)
+        self._active = still
+        if not self._active:
+            return
+        if self.prefill_chunk:
+            self._active = self._step_rows(self._active, self._free, self.engine.context)
+        else:
+            self._active = self._step_positions(self._active, self._free, self.engine.context)
+
+    def run(self, requests):
+        """Every request to completion; returns them."""
+        for req in requests:
+            self.submit(req)
+        while self.busy:
+            self.step()
         return requests
+
+    def _finish(self, st, now, free):
+        st.req.finished = now
+        free.append(st.slot)
+        if st.req.listener is not None:
+            st.req.listener(st.req, None, None)
+
+    def _emit(self, st, token, now, logits=None):
+        """Record a generated token; True when the stream is done."""
+        req = st.req
+        req.tokens.append(int(token))
+        if len(req.tokens) == 1:
+            req.first_token = now
+        st.token = int(token)
+        if req.listener is not None:
+            req.listener(req, int(token), logits)
+        return len(req.tokens) >= req.new_tokens or (req.eos is not None and int(token) == req.eos)
+
+    def _step_positions(self, active, free, context):
+        """One launch of the persistent kernel: a row per stream, its next
+        prompt position or its last token.  Returns the streams still running."""
+        slots = [st.slot for st in active]
+        tokens = [st.token for st in active]
+        positions = [st.pos for st in active]
+        sampled = [i for i, st in enumerate(active)
+                   if st.pos >= len(st.req.prompt) - 1 and st.req.sampler is not None
+                   and not st.req.sampler.greedy]
+        if sampled:
+            argmax, _ = self.engine.step_batch(slots, tokens, positions, device_logits=True)
+            argmax = list(argmax)
+            for i, token in zip(sampled, self._sample_rows(active, sampled)):
+                argmax[i] = token
+        else:
+            argmax, _ = self.engine.step_batch(slots, tokens, positions)
+        self.launches += 1
+        self.rows += len(active)
+        now = self.clock()
+        still = []
+        for st, nxt in zip(active, argmax):
+            req = st.req
+            done = False
+            if st.pos < len(req.prompt) - 1:
+                st.token = int(req.prompt[st.pos + 1])        # sequential prefill
+            else:
+                done = self._emit(st, nxt, now)
+            st.pos += 1
+            if st.pos == self.prefix_tokens:
+                self._keep_prefix(st)
+            if done or st.pos >= context:
+                self._finish(st, now, free)
+            else:
+                still.append(st)
+        return still
 
     def _step_rows(self, active, free, context):
         """One batched tensor-core step: a row per decoding stream, then up
@@ -227,8 +273,9 @@ class MultiStreamServer:
                 out_rows.append(len(slots) - 1)
                 wanted.append(st)
         sampled = [j for j, st in enumerate(wanted) if st.req.sampler is not None and not st.req.sampler.greedy]
+        need_logits = bool(sampled) or any(st.req.want_logits for st in wanted)
         rows = out_rows or [len(slots) - 1]
-        argmax, logits = self.engine.step_rows(slots, tokens, positions, logits=bool(sampled), out_rows=rows)
+        argmax, logits = self.engine.step_rows(slots, tokens, positions, logits=need_logits, out_rows=rows)
         picks = [int(t) for t in argmax[: len(wanted)]]
         for j in sampled:
             req = wanted[j].req
@@ -236,23 +283,21 @@ class MultiStreamServer:
         self.launches += 1
         self.rows += len(slots)
         now = self.clock()
-        nxt = dict(zip((id(st) for st in wanted), picks))
+        nxt = {id(st): (picks[j], logits[j] if need_logits and st.req.want_logits else None)
+               for j, st in enumerate(wanted)}
         done = set()
         for st, p0, take in plan:
             req = st.req
             before = st.pos
             st.pos = p0 + take
+            ended = False
             if id(st) in nxt:
-                req.tokens.append(nxt[id(st)])
-                if len(req.tokens) == 1:
-                    req.first_token = now
-                st.token = nxt[id(st)]
+                ended = self._emit(st, nxt[id(st)][0], now, nxt[id(st)][1])
             else:
                 st.token = int(req.prompt[st.pos])
             if before < self.prefix_tokens <= st.pos:
                 self._keep_prefix(st)
-            if len(req.tokens) >= req.new_tokens or st.pos >= context:
-                req.finished = now
-                free.append(st.slot)
+            if ended or st.pos >= context:
+                self._finish(st, now, free)
                 done.add(id(st))
         return [st for st in active if id(st) not in done]
