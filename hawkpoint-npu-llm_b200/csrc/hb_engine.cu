@@ -5,6 +5,8 @@
 // cooperatively (all CTAs co-resident, one per SM, so the grid barriers always
 // complete), reads back one small result block per call and turns device-side
 // wait timeouts into HB_ERR_DEVICE_TIMEOUT.
+#include <atomic>
+
 #include "hb_engine_impl.h"
 #include "hb_gemv.cuh"
 #include "hb_sample.cuh"
@@ -791,6 +793,8 @@ struct GemvDevice {
 constexpr int kGemvDevices = 64;
 std::mutex g_gemv_mutex;
 GemvDevice g_gemv_device[kGemvDevices];
+// test hook (hb_test_gemv_stall_next): consumed by the next GEMV launch
+std::atomic<uint64_t> g_gemv_stall_ns{0};
 
 int gemv_device(int *dev, int *sms, int *optin) {
   if (cudaGetDevice(dev) != cudaSuccess || *dev < 0 || *dev >= kGemvDevices)
@@ -838,6 +842,7 @@ int gemv_launch(int dev, int mb, bool w8, int grid, size_t smem, hb::GemvParams 
                 const char *who) {
   int v = 0;
   const void *fn = gemv_fn(mb, w8, &v);
+  P.stall_ns = g_gemv_stall_ns.exchange(0);
   int rc = gemv_opt_in(dev, v, fn, smem, false);
   if (rc) return rc;
   void *args[] = {&P};
@@ -854,6 +859,12 @@ int gemv_launch(int dev, int mb, bool w8, int grid, size_t smem, hb::GemvParams 
 }  // namespace
 
 extern "C" {
+
+int hb_test_gemv_stall_next(uint64_t limit_ns) {
+  if (limit_ns == 0 || limit_ns > 10000000000ull) return fail(nullptr, HB_ERR_INVALID_ARG, "limit must be in (0, 10 s]");
+  g_gemv_stall_ns.store(limit_ns);
+  return HB_OK;
+}
 
 size_t hb_gemv_scratch_bytes(int rows, int batch) {
   (void)rows;

@@ -33,6 +33,7 @@ struct GemvParams {
   int red_rows;
   int per_warp;
   uint64_t limit_ns;
+  uint64_t stall_ns;        // test hook: CTA 0 first waits this long on a flag nothing sets
 };
 
 __host__ __device__ inline size_t gemv_smem_bytes(int nslots, int mb, int K, int red_rows) {
@@ -89,6 +90,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     return;
   }
 
+  if (P.stall_ns != 0 && cta == 0 && tid == 0) stall_on_unset_flag(ctrl, P.stall_ns);
   const int mrows = min(P.batch, MB);
   const int n8 = P.K / 8;
   for (int idx = tid; idx < mrows * n8; idx += kConsumerThreads) {

@@ -118,6 +118,7 @@ SIGNATURES = {
     "hb_profile_read": (_I, [_P, _FP, _FP, _I, ctypes.POINTER(_I)]),
     "hb_set_stream": (_I, [_P, _P]),
     "hb_test_stall_next": (_I, [_P, ctypes.c_uint64]),
+    "hb_test_gemv_stall_next": (_I, [ctypes.c_uint64]),
     "hb_gemv_scratch_bytes": (ctypes.c_size_t, [_I, _I]),
     "hb_gemv": (_I, [_P, _P, _I, _I, _I, _P, _I, _P, _I, _P, _P, ctypes.c_size_t, _P]),
     "hb_gemv_noalloc": (_I, [_P, _P, _I, _I, _I, _P, _I, _P, _I, _P, _P]),

@@ -180,6 +180,12 @@ int hb_set_stream(hb_engine *engine, void *stream);
  * that nothing sets, with the given limit (ns), so the bounded wait runs out
  * and the call returns HB_ERR_DEVICE_TIMEOUT.  No GPU fault is involved. */
 int hb_test_stall_next(hb_engine *engine, uint64_t limit_ns);
+/* The same for the next hb_gemv / hb_gemv_noalloc launch in the process: its
+ * first CTA waits on a flag nothing sets until the limit passes, the launch
+ * aborts, and the fused argmax of every batch row reads -1 (how both entry
+ * points report a device wait that gave up; hb_gemv's scratch also holds the
+ * timeout in its control block). */
+int hb_test_gemv_stall_next(uint64_t limit_ns);
 
 /* Standalone weight-streaming GEMV (the microbenchmark of the reference's
  * q_gemv4 / q_gemv_slice, npu_llm/kernels/qwen_engine_common.h:89-110, and

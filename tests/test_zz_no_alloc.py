@@ -9,7 +9,8 @@ state a call leaves in the shared array does not leak into the next one.
 The outputs are also checked against an FP32 reference of the same product,
 for BF16 and W8 weights, with FP32 / argmax-only outputs, and for calls of
 different grid sizes queued back to back on one stream (they reuse the same
-partial slots).  This file is named to be collected last.
+partial slots), and a launch whose device wait runs out (test hook) reports
+-1 in-band.  This file is named to be collected last.
 """
 
 import ctypes
@@ -150,3 +151,29 @@ def test_noalloc_back_to_back_grid_sizes_on_one_stream():
         torch.cuda.synchronize()
         assert np.array_equal(y2.cpu().numpy(), got)
         assert np.array_equal(am2.cpu().numpy(), am.cpu().numpy())
+
+
+def test_noalloc_reports_a_device_wait_that_gave_up():
+    """The first CTA of the next launch waits on a flag nothing sets
+    (hb_test_gemv_stall_next, a 1 ms limit): the launch aborts and every
+    batch row's argmax reads -1, the in-band timeout report of the
+    allocation-free entry point; the next call is correct again.  No GPU
+    fault is involved."""
+    import torch
+
+    lib = hb_lib.load()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rows, k, batch = 151936, 896, 2
+    wd, xd = _case(rows, k, batch, 21)
+    _, am = _outputs(rows, batch)
+    am.fill_(7)
+    hb_lib.check(lib.hb_test_gemv_stall_next(1_000_000))
+    hb_lib.check(lib.hb_gemv_noalloc(wd.data_ptr(), None, hb_lib.HB_WEIGHTS_BF16, rows, k, xd.data_ptr(), batch, None,
+                                     hb_lib.HB_GEMV_OUT_NONE | hb_lib.HB_GEMV_ARGMAX, am.data_ptr(), stream))
+    torch.cuda.synchronize()
+    assert am.cpu().numpy().tolist() == [-1] * batch
+    _, again = _outputs(rows, batch)
+    hb_lib.check(lib.hb_gemv_noalloc(wd.data_ptr(), None, hb_lib.HB_WEIGHTS_BF16, rows, k, xd.data_ptr(), batch, None,
+                                     hb_lib.HB_GEMV_OUT_NONE | hb_lib.HB_GEMV_ARGMAX, again.data_ptr(), stream))
+    torch.cuda.synchronize()
+    assert all(0 <= t < rows for t in again.cpu().numpy().tolist())
