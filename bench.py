@@ -147,9 +147,9 @@ def config5_requests(vocab, n=512, new_tokens=16, seed=MODEL_SEED + 5):
 
 
 MULTISTREAM_MODES = {
-    # the batched tensor-core step: 64 streams, prompts in chunks of 32
-    # positions, up to 128 rows a step
-    "rows": {"max_slots": 68, "server": {"max_batch": 64, "prefill_chunk": 32, "max_rows": 128}},
+    # the batched tensor-core step: 128 streams, prompts in chunks of 32
+    # positions, up to 256 rows a step
+    "rows": {"max_slots": 132, "server": {"max_batch": 128, "prefill_chunk": 32, "max_rows": 256}},
     # the persistent decoder kernel: 8 streams a launch, one position each
     "persistent": {"max_slots": 12, "server": {"max_batch": 8}},
 }

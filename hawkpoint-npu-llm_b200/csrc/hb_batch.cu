@@ -142,7 +142,10 @@ bool gemm_params(hb::tc::GemmParams &P, const GemmShape &g, const void *w, int r
 
 // Device buffers of the batched path, sized for kMaxRows rows and
 // allocated on an engine's first batched step.
-constexpr int kMaxRows = 128;
+constexpr int kMaxRows = 256;
+// the persistent LM head takes up to 128 output rows a launch (its
+// transposed tile, 129 floats per row, must fit beside its ring)
+constexpr int kHeadRows = 128;
 
 struct hb_batch {
   int *d_meta = nullptr;            // slot [kMaxRows] | pos | tok | output rows
@@ -211,7 +214,7 @@ int batch_setup(hb_engine *e) {
   for (const void *fn : fns)
     HB_CUDA(e, cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   size_t head_smem = 0;
-  for (int n = 16; n <= kMaxRows; n += 16) head_smem = std::max(head_smem, hb::tc::head_smem_bytes(head_stages(n), n));
+  for (int n = 16; n <= kHeadRows; n += 16) head_smem = std::max(head_smem, hb::tc::head_smem_bytes(head_stages(n), n));
   HB_CUDA(e, cudaFuncSetAttribute(hb::tc::lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(head_smem)));
   return HB_OK;
@@ -317,12 +320,17 @@ int batch_record(hb_engine *e, int n, int n_out, bool want_logits) {
   HB_CUDA(e, launch_early(hb::tc::norm_pack_kernel, dim3((n_out + 3) / 4), dim3(hb::tc::kThreads), 0, st, 1,
                           static_cast<const __nv_bfloat16 *>(b->h), static_cast<const int *>(b->d_meta + 3 * kMaxRows),
                           n_out, reinterpret_cast<const float *>(e->d_blob + d.gamma_final), d.rms_eps, H, b->xn));
-  hb::tc::GemmParams P{};
-  P.y = want_logits ? b->logits : nullptr;
-  P.part_val = b->part_val;
-  P.part_idx = b->part_idx;
-  P.pstride = kMaxRows;
-  if ((rc = lm_head(e, e->d_blob + d.w_lm, d.vocab, H, b->xn, n_out, P))) return rc;
+  // the LM head in launches of up to 128 output rows (packed rows c0.. start
+  // at row group c0 / 8 of xn)
+  for (int c0 = 0; c0 < n_out; c0 += kHeadRows) {
+    hb::tc::GemmParams P{};
+    P.y = want_logits ? b->logits + static_cast<size_t>(c0) * d.vocab : nullptr;
+    P.part_val = b->part_val + c0;
+    P.part_idx = b->part_idx + c0;
+    P.pstride = kMaxRows;
+    const uint8_t *x = b->xn + static_cast<size_t>(c0 / 8) * H * 16;
+    if ((rc = lm_head(e, e->d_blob + d.w_lm, d.vocab, H, x, std::min(kHeadRows, n_out - c0), P))) return rc;
+  }
   HB_CUDA(e, launch_early(hb::tc::argmax_reduce_kernel, dim3(n_out), dim3(256), 0, st, 1,
                           static_cast<const float *>(b->part_val), static_cast<const int *>(b->part_idx), b->lm_tiles,
                           kMaxRows, b->d_argmax));
@@ -343,7 +351,7 @@ void drop_graphs(hb_batch *b) {
 int batch_forward(hb_engine *e, int n, int n_out, bool want_logits) {
   hb_batch *b = e->batch;
   cudaStream_t st = e->stream;
-  const uint32_t key = static_cast<uint32_t>(n) | static_cast<uint32_t>(n_out) << 8 | (want_logits ? 1u << 16 : 0u);
+  const uint32_t key = static_cast<uint32_t>(n) | static_cast<uint32_t>(n_out) << 9 | (want_logits ? 1u << 18 : 0u);
   if (!b->graphs.count(key) && b->graphs.size() >= kMaxGraphs) drop_graphs(b);
   cudaGraphExec_t &exec = b->graphs[key];
   int rc = HB_OK;

@@ -217,10 +217,10 @@ class B200DecoderEngine:
         return am, out
 
     # -- batched tensor-core path (hb_step_rows / hb_prefill_tc) ----------------
-    MAX_ROWS = 128
+    MAX_ROWS = 256
 
     def step_rows(self, slots, tokens, positions, logits=False, out_rows=None):
-        """Up to 128 rows through the whole model on the tensor cores (row i:
+        """Up to 256 rows through the whole model on the tensor cores (row i:
         tokens[i] at positions[i] of KV slot slots[i]); rows may be several
         consecutive positions of one sequence.  The LM head runs over
         ``out_rows`` (indices into the rows; default every row).  Returns

@@ -315,7 +315,7 @@ int hb_tc_gemm(const void *w_dev, int rows, int k, const void *x_dev, int n, flo
 int hb_tc_gemm_status(const void *scratch_dev, void *stream);
 
 /* ---- batched step on the tensor cores (new in this build) -------------------
- * n rows (1 <= n <= 128) through every layer, the final norm and the LM
+ * n rows (1 <= n <= 256) through every layer, the final norm and the LM
  * head in one call: row i feeds token_ids[i] at positions[i] of KV slot
  * slots[i].  The final norm and LM head run over the output rows only: with
  * out_rows NULL (n_out == n) every row, else the n_out rows out_rows[0..)
@@ -339,7 +339,7 @@ int hb_step_rows(hb_engine *engine, int n, const int32_t *slots, const int32_t *
                  const int32_t *positions, int n_out, const int32_t *out_rows, int32_t *argmax_out,
                  float *logits_out);
 /* Prefill of positions start_pos .. start_pos + n - 1 of one slot through
- * hb_step_rows (128 rows per launch sequence, the LM head on each chunk's
+ * hb_step_rows (256 rows per launch sequence, the LM head on each chunk's
  * last row only); the last position's argmax and, when last_logits is not
  * NULL, its FP32 logits. */
 int hb_prefill_tc(hb_engine *engine, int slot, const int32_t *ids, int n, int start_pos, float *last_logits,

@@ -75,6 +75,26 @@ def test_prefill_tc_in_one_pass_equals_row_by_row(tiny):
     assert np.array_equal(engine.kv_cache(2)[:, :, :, :n], engine.kv_cache(3)[:, :, :, :n])
 
 
+def test_step_above_128_rows_equals_each_sequence_alone(tiny):
+    """156 rows in one step (13 prompt positions of each of 12 slots), the
+    LM head on each slot's last row: every slot's logits equal the same
+    positions prefilled alone (rows are independent of their step)."""
+    model, engine = tiny
+    engine.reset()
+    prompts = [synthetic.prompt_ids(model.shape.vocab, 13, seed=70 + k) for k in range(12)]
+    slots = [k for k in range(12) for _ in range(13)]
+    tokens = [t for p in prompts for t in p]
+    positions = list(range(13)) * 12
+    out_rows = [13 * k + 12 for k in range(12)]
+    am, logits = engine.step_rows(slots, tokens, positions, logits=True, out_rows=out_rows)
+    assert logits.shape == (12, model.shape.vocab)
+    for k, p in enumerate(prompts):
+        engine.reset(k)
+        first, alone = engine.prefill_tc(p, slot=k, logits=True)
+        assert np.array_equal(logits[k], alone), k
+        assert int(am[k]) == first
+
+
 def test_step_rows_across_streams_matches_single_rows(tiny):
     """Six sequences at different depths in one step: each row equals that
     sequence's own single-row step (tolerance), its cache row too."""
@@ -147,7 +167,7 @@ def test_step_rows_rejects_bad_rows(tiny):
     with pytest.raises(ValueError):
         engine.step_rows([0, 0], [1, 2], [3, 3])           # same slot position twice
     with pytest.raises(ValueError):
-        engine.step_rows([0] * 129, [1] * 129, list(range(129)))
+        engine.step_rows(list(range(257)), [1] * 257, [0] * 257)
     with pytest.raises(ValueError):
         engine.step_rows([0], [model.shape.vocab], [0])     # token outside the vocabulary
 
