@@ -603,6 +603,16 @@ __host__ __device__ inline size_t head_smem_bytes(int stages, int npad) {
          static_cast<size_t>(npad) * kHeadStride * 4;
 }
 
+// One row of a column scan whose rows arrive in index order: a larger value
+// wins, a tie keeps the earlier row, a NaN beats every number and the first
+// NaN stays (np.argmax order).
+__device__ __forceinline__ void scan_take(float v, int i, float &bv, int &bi) {
+  if (v > bv || (v != v && bv == bv)) {
+    bv = v;
+    bi = i;
+  }
+}
+
 __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -726,6 +736,8 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const __grid_c
     // epilogue warps 2..5: warp w reads TMEM lanes 32 (w % 4) .. + 31
     grid_dep_wait();
     const int q = warp & 3;
+    int parts = 32;  // threads per column in the scan: 128 / (N rounded up to a power of two), at most 32
+    while (parts > 1 && (128 / parts) < P.N) parts >>= 1;
     for (int t = 0; t < mine; ++t) {
       const int buf = t & 1;
       // the four warps agree before any of them waits at a named barrier
@@ -752,13 +764,41 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const __grid_c
       __syncwarp();
       if (lane == 0) mbar_arrive_count(&acc_empty[buf], 1);  // the buffer may take the next tile
       named_sync(1, kHeadEpiWarps * 32);
+      // the column maxima: a column's 128 rows split over `parts` threads
+      // of one warp, each walking rows part, part + parts, ... in four
+      // interleaved chains, then a butterfly over the column's threads
       const int live = min(kTileRows, P.rows - tile * kTileRows);  // rows of this tile inside W
-      for (int n = (warp - 2) * 32 + lane; n < P.N; n += kHeadEpiWarps * 32) {
+      const int et = (warp - 2) * 32 + lane;  // epilogue thread
+      const int n = et / parts, part = et - n * parts;
+      const int row0 = tile * kTileRows;
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      if (n < P.N) {
         const float *col = tpose + n * kHeadStride;
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-#pragma unroll 4
-        for (int r = 0; r < live; ++r) argmax_merge(bv, bi, col[r], tile * kTileRows + r);
+        float cv[4];
+        int ci[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // each chain starts at its first row: a tie keeps the earlier row
+          const int r = part + c * parts;
+          cv[c] = r < live ? col[r] : -INFINITY;
+          ci[c] = r < live ? row0 + r : 0x7fffffff;
+        }
+        for (int r = part + 4 * parts; r < live; r += 4 * parts) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int rr = r + c * parts;
+            if (rr < live) scan_take(col[rr], row0 + rr, cv[c], ci[c]);
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) argmax_merge(bv, bi, cv[c], ci[c]);
+      }
+      for (int o = parts / 2; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        argmax_merge(bv, bi, ov, oi);
+      }
+      if (n < P.N && part == 0) {
         P.part_val[static_cast<size_t>(tile) * P.pstride + n] = bv;
         P.part_idx[static_cast<size_t>(tile) * P.pstride + n] = bi;
       }
