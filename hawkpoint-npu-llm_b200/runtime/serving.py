@@ -301,3 +301,40 @@ class MultiStreamServer:
                 self._finish(st, now, free)
                 done.add(id(st))
         return [st for st in active if id(st) not in done]
+
+
+def run_lanes(servers, requests, new_tokens=16, prefix_tokens=16):
+    """Serves ``requests`` on several servers at once, each server's engine
+    on its own CUDA stream and each server driven by its own host thread
+    (the engine calls release the interpreter lock), so the servers'
+    launch sequences overlap on one GPU: a batched step is a chain of
+    dependent kernels that leaves most SMs idle between them, and a second
+    or third chain fills them.  Requests are assigned to lanes as requests
+    are assigned to GPUs (runtime/dispatch.py: requests sharing a prompt
+    prefix go to the same lane, where its prefix pool keeps it).  Returns
+    the requests; re-raises the first lane's error."""
+    import threading
+
+    from runtime import dispatch
+
+    lanes = len(servers)
+    prompts = [r.prompt for r in requests]
+    groups = [[requests[i] for i in dispatch.shard(prompts, k, lanes, new_tokens, prefix_tokens)]
+              for k in range(lanes)]
+    errors = [None] * lanes
+
+    def serve(k):
+        try:
+            servers[k].run(groups[k])
+        except BaseException as exc:  # reported after every lane stopped
+            errors[k] = exc
+
+    threads = [threading.Thread(target=serve, args=(k,), name=f"hawkpoint-lane-{k}") for k in range(lanes)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    for exc in errors:
+        if exc is not None:
+            raise exc
+    return requests

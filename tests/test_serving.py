@@ -5,7 +5,7 @@ single-stream generation through the same kernels."""
 import numpy as np
 import pytest
 
-from runtime.serving import MultiStreamServer, Request
+from runtime.serving import MultiStreamServer, Request, run_lanes
 
 
 class FakeEngine:
@@ -231,6 +231,84 @@ def test_context_limit_and_validation():
         MultiStreamServer(eng, max_batch=1, prefix_slots=1).run([Request(prompt=list(range(20)), new_tokens=1)])
     with pytest.raises(ValueError):
         MultiStreamServer(FakeEngine(max_slots=4), max_batch=8, prefix_slots=0)
+
+
+def test_lanes_serve_every_request_once_with_prefixes_kept_together():
+    """Three lanes (servers on their own engines, one host thread each): the
+    same tokens as single streams, every request served by exactly one
+    lane.  The shared-prefix group (a quarter of the load, more than a
+    lane's fair share) is cut into one piece per lane, and each lane
+    computes the prefix once and reuses it for its piece."""
+    engines = [FakeEngine(max_slots=12) for _ in range(3)]
+    servers = [MultiStreamServer(e, max_batch=8, prefix_slots=4, prefill_chunk=8, max_rows=48) for e in engines]
+    reqs = config5_requests(n=96)
+    run_lanes(servers, reqs)
+    for r in reqs:
+        assert r.tokens == reference_tokens(r.prompt, r.new_tokens), r.rid
+    rows = [sum(getattr(e, "row_steps", [])) for e in engines]
+    assert all(n > 0 for n in rows)
+    assert sum(s.rows for s in servers) == sum(rows)
+    for e in engines:
+        assert e.copies and all(n == 16 for _, _, n in e.copies)
+    assert sum(1 for r in reqs if r.reused_prefix) >= 6
+
+
+def test_a_failing_lane_raises_after_the_others_finish():
+    class Broken(FakeEngine):
+        def step_rows(self, *args, **kwargs):
+            raise RuntimeError("lane fault (planted)")
+
+    good = FakeEngine(max_slots=36)
+    servers = [MultiStreamServer(good, max_batch=32, prefix_slots=4, prefill_chunk=8, max_rows=48),
+               MultiStreamServer(Broken(max_slots=36), max_batch=32, prefix_slots=4, prefill_chunk=8, max_rows=48)]
+    reqs = config5_requests(n=48)
+    with pytest.raises(RuntimeError, match="planted"):
+        run_lanes(servers, reqs)
+    served = [r for r in reqs if r.tokens and len(r.tokens) == r.new_tokens]
+    assert served and all(r.tokens == reference_tokens(r.prompt, r.new_tokens) for r in served)
+
+
+@pytest.mark.gpu
+def test_gpu_lanes_match_one_lane():
+    """Two lanes, each an engine on its own CUDA stream driven by its own
+    thread, their steps overlapping on the GPU: every request's tokens
+    equal the single-lane run's (a row's arithmetic does not depend on the
+    other rows of its step, nor on the other lane's kernels)."""
+    import torch
+
+    from runtime import layout, synthetic
+    from runtime.b200_engine import B200DecoderEngine
+
+    model = synthetic.build("tiny-qwen", seed=33).materialize()
+    blob = layout.pack(model, "bf16")
+    engines, streams = [], []
+    try:
+        for _ in range(3):
+            engines.append(B200DecoderEngine(model, blob=blob, max_slots=36, max_batch=8))
+            streams.append(torch.cuda.Stream())
+            engines[-1].set_stream(streams[-1].cuda_stream)
+
+        def make():
+            rng = np.random.default_rng(12)
+            shared = rng.integers(0, model.shape.vocab, 16).tolist()
+            reqs = []
+            for i in range(60):
+                ids = rng.integers(0, model.shape.vocab, int(rng.integers(8, 40))).tolist()
+                reqs.append(Request(prompt=shared + ids[:8] if i % 4 == 0 else ids, new_tokens=6, rid=i))
+            return reqs
+
+        one = make()
+        MultiStreamServer(engines[0], max_batch=32, prefix_slots=4, prefill_chunk=8, max_rows=64).run(one)
+        two = make()
+        servers = [MultiStreamServer(e, max_batch=32, prefix_slots=4, prefill_chunk=8, max_rows=64)
+                   for e in engines[1:]]
+        run_lanes(servers, two)
+        assert all(s.rows > 0 for s in servers)
+        for a, b in zip(one, two):
+            assert a.tokens == b.tokens, a.rid
+    finally:
+        for e in engines:
+            e.close()
 
 
 @pytest.mark.gpu
