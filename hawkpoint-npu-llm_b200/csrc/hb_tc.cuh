@@ -318,29 +318,47 @@ template <int EPI>
 __device__ __forceinline__ void finish_tile(const GemmParams &P, float *stage, int tile, int n0, int n1) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = tile * kTileRows;
+  // with 128 threads stepping by 128, a thread's row within the tile is
+  // fixed: threadIdx.x; its columns are n0 + k
+  const int row = row0 + threadIdx.x;
+  const bool row_ok = row < P.rows;
   if constexpr (EPI == kEpiF32 || EPI == kEpiResid) {
-    for (int idx = threadIdx.x; idx < (n1 - n0) * kTileRows; idx += kThreads) {
-      const int n = n0 + (idx >> 7), row = row0 + (idx & 127);
-      if (row >= P.rows) continue;
-      const float v = stage[idx];
-      const size_t o = static_cast<size_t>(n) * P.rows + row;
-      if constexpr (EPI == kEpiF32) {
-        P.y[o] = v;
-      } else {
-        P.out[o] = f2bf(__fadd_rn(rbf(v), bf2f(P.resid[o])));
+    if (!row_ok) return;
+    // the residual reads of kBatch columns are all in flight before the
+    // first store (one memory round per kBatch columns, not per column)
+    constexpr int kBatch = 8;
+    for (int c0 = n0; c0 < n1; c0 += kBatch) {
+      float r[kBatch];
+      if constexpr (EPI == kEpiResid) {
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+          r[u] = c0 + u < n1 ? bf2f(P.resid[static_cast<size_t>(c0 + u) * P.rows + row]) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        if (c0 + u >= n1) break;
+        const float v = stage[(c0 + u - n0) * kTileRows + threadIdx.x];
+        const size_t o = static_cast<size_t>(c0 + u) * P.rows + row;
+        if constexpr (EPI == kEpiF32) {
+          P.y[o] = v;
+        } else {
+          P.out[o] = f2bf(__fadd_rn(rbf(v), r[u]));
+        }
       }
     }
   } else if constexpr (EPI == kEpiQkv) {
     // BF16 biased values back into the stage; q rows to out
     const int qrows = P.kv.QH * kHeadDimTc;
-    for (int idx = threadIdx.x; idx < (n1 - n0) * kTileRows; idx += kThreads) {
-      const int n = n0 + (idx >> 7), row = row0 + (idx & 127);
-      if (row >= P.rows) continue;
-      float yv = rbf(stage[idx]);
-      if (P.bias != nullptr) yv = __fadd_rn(yv, P.bias[row]);
-      const __nv_bfloat16 b = f2bf(yv);
-      stage[idx] = bf2f(b);
-      if (row < qrows) P.out[static_cast<size_t>(n) * P.rows + row] = b;
+    if (row_ok) {
+      const float bias = P.bias != nullptr ? P.bias[row] : 0.f;
+      for (int n = n0; n < n1; ++n) {
+        const int idx = (n - n0) * kTileRows + threadIdx.x;
+        float yv = rbf(stage[idx]);
+        if (P.bias != nullptr) yv = __fadd_rn(yv, bias);
+        const __nv_bfloat16 b = f2bf(yv);
+        stage[idx] = bf2f(b);
+        if (row < qrows) P.out[static_cast<size_t>(n) * P.rows + row] = b;
+      }
     }
     // the tile's two heads per column: a k head is rotated at the column's
     // position and stored as K, a v head stored as V (one warp per head)
@@ -351,18 +369,39 @@ __device__ __forceinline__ void finish_tile(const GemmParams &P, float *stage, i
       s_slot[c] = P.R.slot[n0 + c];
     }
     __syncthreads();
-    for (int u = warp; u < (n1 - n0) * 2; u += kThreads / 32) {
-      const int n = n0 + (u >> 1), hh = u & 1;
-      const int head = row0 / kHeadDimTc + hh;
-      if (head < P.kv.QH || head * kHeadDimTc >= P.rows) continue;
-      const float *v = stage + (n - n0) * kTileRows + hh * kHeadDimTc;
-      const int p = s_pos[n - n0], slot = s_slot[n - n0];
-      if (head < P.kv.QH + P.kv.KVH) {
-        __nv_bfloat16 lo, hi;
-        rope_vals(v[lane], v[lane + 32], P.kv.cos[p * 32 + lane], P.kv.sin[p * 32 + lane], lo, hi);
-        put_k(kv_rows(P.kv, slot, head - P.kv.QH, 0), p, lane, lo, hi);
-      } else {
-        put_v(kv_rows(P.kv, slot, head - P.kv.QH - P.kv.KVH, 1), p, lane, pack_bf16x2(v[2 * lane], v[2 * lane + 1]));
+    // kBatch units per warp per pass, their RoPE table reads in flight together
+    constexpr int kBatch = 4, kWarps = kThreads / 32;
+    const int units = (n1 - n0) * 2;
+    for (int u0 = warp; u0 < units; u0 += kBatch * kWarps) {
+      float cs[kBatch], sn[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int u = u0 + j * kWarps;
+        const int head = row0 / kHeadDimTc + (u & 1);
+        cs[j] = sn[j] = 0.f;
+        if (u < units && head >= P.kv.QH && head < P.kv.QH + P.kv.KVH) {
+          const int p = s_pos[u >> 1];
+          cs[j] = P.kv.cos[p * 32 + lane];
+          sn[j] = P.kv.sin[p * 32 + lane];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int u = u0 + j * kWarps;
+        if (u >= units) break;
+        const int n = n0 + (u >> 1), hh = u & 1;
+        const int head = row0 / kHeadDimTc + hh;
+        if (head < P.kv.QH || head * kHeadDimTc >= P.rows) continue;
+        const float *v = stage + (n - n0) * kTileRows + hh * kHeadDimTc;
+        const int p = s_pos[n - n0], slot = s_slot[n - n0];
+        if (head < P.kv.QH + P.kv.KVH) {
+          __nv_bfloat16 lo, hi;
+          rope_vals(v[lane], v[lane + 32], cs[j], sn[j], lo, hi);
+          put_k(kv_rows(P.kv, slot, head - P.kv.QH, 0), p, lane, lo, hi);
+        } else {
+          put_v(kv_rows(P.kv, slot, head - P.kv.QH - P.kv.KVH, 1), p, lane,
+                pack_bf16x2(v[2 * lane], v[2 * lane + 1]));
+        }
       }
     }
   } else if constexpr (EPI == kEpiSwiglu) {
