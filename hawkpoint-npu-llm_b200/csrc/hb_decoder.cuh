@@ -204,8 +204,9 @@ __device__ __forceinline__ void ll_load2(const uint64_t *p, uint64_t &a, uint64_
 // per pair (words even and < 65536, row_words even, src 16-byte aligned): pair p of every
 // row goes to thread p % kConsumerThreads, so a thread owns the same words
 // (2p, 2p + 1) of each row.  All rows are polled together, up to U pairs per
-// thread in flight: 4 for one row (8 words, as many as the decode kernel's
-// register budget affords without slowing its GEMV loops), 8 for 8 rows,
+// thread in flight: 6 for one row (the 4,864-value activation gather in one
+// round instead of two: 0.492 against 0.496 ms a decode step; 8 pushed the
+// kernel to 254 registers and slowed its GEMV loops), 8 for 8 rows,
 // where the deeper queue halves the rounds of the 8 x 4864 activation gather
 // (6 in the int8-weight 8-row kernel, which has fewer registers to spare).
 template <int U, class Sink>
@@ -466,7 +467,7 @@ struct DecoderCta {
   // Raw payloads of the LL words (BF16 pairs) into dst[m * dst_words + i].
   __device__ bool gather_raw(const uint64_t *src, size_t row_words, int words, uint32_t *dst,
                                           size_t dst_words) {
-    return ll_gather<(MB > 1 ? (W8 ? 6 : 8) : 4)>(src, row_words, words, mrows, epoch, &P.result->ctrl, P.limit_ns,
+    return ll_gather<(MB > 1 ? (W8 ? 6 : 8) : 6)>(src, row_words, words, mrows, epoch, &P.result->ctrl, P.limit_ns,
                      [&](int m, int i, uint32_t d) { dst[m * dst_words + i] = d; });
   }
 

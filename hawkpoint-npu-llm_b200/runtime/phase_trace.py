@@ -58,6 +58,32 @@ def summarize(stamps, layers):
     return out, span
 
 
+def critical_path(stamps, layers):
+    """Per phase kind, medians over layers 1.. (us) measured from the moment
+    the previous phase's last CTA stored its outputs: its inputs gathered by
+    the median and by the last CTA, then the median CTA's norm (or, for
+    attn, the barrier after the gather), GEMV and epilogue, and the critical
+    span to this phase's last store."""
+    out = {}
+    for kind, name in KINDS:
+        vals = []
+        for layer in range(1, layers):
+            k = 4 * layer + kind
+            pub = stamps[:, k - 1, 3].max()
+            g, n6, c2, s3 = (stamps[:, k, i] for i in (1, 6, 2, 3))
+            vals.append((np.median(g - pub), g.max() - pub, np.median(n6 - g), np.median(c2 - n6),
+                         np.median(s3 - c2), s3.max() - pub))
+        out[name] = tuple(float(v) / 1e3 for v in np.median(np.array(vals, dtype=np.float64), axis=0))
+    k = 4 * layers
+    pub = stamps[:, k - 1, 3].max()
+    out["head"] = (float(np.median(stamps[:, k, 1] - pub)) / 1e3, float(stamps[:, k, 1].max() - pub) / 1e3,
+                   float(np.median(stamps[:, k, 6] - stamps[:, k, 1])) / 1e3,
+                   float(np.median(stamps[:, k, 2] - stamps[:, k, 6])) / 1e3,
+                   float(np.median(stamps[:, k, 3] - stamps[:, k, 2])) / 1e3,
+                   float(stamps[:, k, 3].max() - pub) / 1e3)
+    return out
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     parser.add_argument("--model", default="qwen2.5-0.5b", choices=sorted(synthetic.SHAPES))
@@ -65,6 +91,8 @@ def main():
     parser.add_argument("--context", type=int, default=4096)
     parser.add_argument("--depths", type=int, nargs="+", default=[256, 4032])
     parser.add_argument("--device", type=int, default=0)
+    parser.add_argument("--critical-path", action="store_true",
+                        help="also print each phase's chain from the previous phase's last store")
     args = parser.parse_args()
     model = synthetic.build(args.model, seed=0).materialize()
     engine = B200DecoderEngine(model, weights=args.weights, device=args.device, max_batch=8, context=args.context)
@@ -77,6 +105,12 @@ def main():
             for name, (wait, prologue, gemv, phase) in rows.items():
                 print(f"  {name:8s} wait {wait:6.2f}  prologue {prologue:6.2f}  gemv+epilogue {gemv:6.2f}  "
                       f"phase {phase:6.2f} us (median over layers)")
+            if args.critical_path:
+                stamps = trace_step(engine, ids, depth)
+                print("  critical path from the previous phase's last store (us; median over layers 1..):")
+                print("  phase     inputs(median CTA)  inputs(last CTA)  norm/sync  gemv  epilogue  last store")
+                for name, v in critical_path(stamps, model.shape.layers).items():
+                    print(f"  {name:8s} " + "  ".join(f"{x:8.2f}" for x in v))
     finally:
         engine.close()
 
