@@ -312,10 +312,18 @@ __device__ __forceinline__ void norm_pack_row(const __nv_bfloat16 *x, const floa
   norm_pack_rows<1>(xs, ns, gamma, eps, H, out);
 }
 
+// Residual columns a kEpiResid CTA stages in shared memory while its MMAs
+// run (the first kResPre of the columns it finishes; the rest are read in
+// the epilogue).
+constexpr int kResPre = 40;
+
 // The epilogue of columns [n0, n1) of a tile from its FP32 results in
-// shared memory (stage[(n - n0) * 128 + row in tile]); 128 threads.
+// shared memory (stage[(n - n0) * 128 + row in tile]); 128 threads.  sres:
+// kEpiResid's staged residual, column n0 + c at sres[c * 128 + row in tile]
+// for c < kResPre.
 template <int EPI>
-__device__ __forceinline__ void finish_tile(const GemmParams &P, float *stage, int tile, int n0, int n1) {
+__device__ __forceinline__ void finish_tile(const GemmParams &P, float *stage, int tile, int n0, int n1,
+                                            const __nv_bfloat16 *sres) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = tile * kTileRows;
   // with 128 threads stepping by 128, a thread's row within the tile is
@@ -331,8 +339,12 @@ __device__ __forceinline__ void finish_tile(const GemmParams &P, float *stage, i
       float r[kBatch];
       if constexpr (EPI == kEpiResid) {
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u)
-          r[u] = c0 + u < n1 ? bf2f(P.resid[static_cast<size_t>(c0 + u) * P.rows + row]) : 0.f;
+        for (int u = 0; u < kBatch; ++u) {
+          const int c = c0 + u - n0;
+          r[u] = c0 + u >= n1     ? 0.f
+                 : c < kResPre ? bf2f(sres[c * kTileRows + threadIdx.x])
+                               : bf2f(P.resid[static_cast<size_t>(c0 + u) * P.rows + row]);
+        }
       }
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
@@ -460,6 +472,10 @@ __device__ __forceinline__ void finish_tile(const GemmParams &P, float *stage, i
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ GemmParams P) {
   extern __shared__ __align__(1024) uint8_t smem[];
+  // kEpiResid: the residual of the columns this CTA finishes, bulk-copied
+  // while the MMAs run
+  __shared__ __align__(128) __nv_bfloat16 s_res[EPI == kEpiResid ? kResPre * kTileRows : 8];
+  __shared__ __align__(8) uint64_t s_resbar;
   const int S = P.stages;
   uint8_t *sa = smem;                                                   // [S][16 KB]
   uint8_t *sb = smem + static_cast<size_t>(S) * kAStageBytes;           // [S][npad * 128]
@@ -477,6 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       mbar_init(&empty[i], 1);
     }
     mbar_init(done, 1);
+    if (EPI == kEpiResid) mbar_init(&s_resbar, 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -491,6 +508,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 
   const int k0 = split * P.kst / P.ksplit;
   const int nk = (split + 1) * P.kst / P.ksplit - k0;  // K stages of this slice (>= 1)
+  // the columns this CTA finishes: a share of them with K slices, else all
+  const int n0 = P.ksplit > 1 ? split * P.N / P.ksplit : 0;
+  const int n1 = P.ksplit > 1 ? (split + 1) * P.N / P.ksplit : P.N;
+  const int res_cols = EPI == kEpiResid ? min(n1 - n0, kResPre) : 0;
+  const int res_rows = min(kTileRows, P.rows - tile * kTileRows);
 
   if (warp == 0 && lane == 0) {
     // producer: a stage is one box of W's tile and one of the batch (full
@@ -521,6 +543,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       mbar_wait_quiet(&full[i % S], static_cast<uint32_t>(i / S) & 1u, P.limit_ns);
   } else {
     grid_dep_wait();  // the epilogue reads what earlier kernels wrote
+    if (EPI == kEpiResid && warp == 2 && lane == 0 && res_cols > 0) {
+      // the staged residual: one 16-byte-aligned run of the tile's rows per
+      // column (rows a multiple of 8)
+      const uint32_t bytes = static_cast<uint32_t>(res_rows) * 2;
+      mbar_arrive_expect_tx(&s_resbar, bytes * static_cast<uint32_t>(res_cols));
+      for (int c = 0; c < res_cols; ++c)
+        bulk_g2s(s_res + c * kTileRows, P.resid + static_cast<size_t>(n0 + c) * P.rows + tile * kTileRows, bytes,
+                 &s_resbar);
+    }
     if (warp == 1 && lane == 0) {
       // MMA issuer
       const uint32_t idesc = idesc_bf16(P.npad);
@@ -542,9 +573,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
   }
   __syncwarp();
-  // epilogue: wait for the accumulator (or, after an abort, for the MMAs in flight)
+  // epilogue: wait for the accumulator (or, after an abort, for the MMAs in
+  // flight) and the staged residual
   const bool ok = __syncthreads_and(mbar_wait(done, 0, P.ctrl, P.limit_ns, kWhereFull) &&
+                                    (res_cols == 0 || mbar_wait(&s_resbar, 0, P.ctrl, P.limit_ns, kWhereFull)) &&
                                     ld_volatile_int(&P.ctrl->abort) == 0) != 0;
+  // no staged copy is in flight when the CTA exits (after an abort too)
+  if (res_cols > 0 && warp == 2 && lane == 0) mbar_wait_quiet(&s_resbar, 0, P.limit_ns);
   tc_fence_after();
   const int r_t = warp * 32 + lane;  // this thread's row within the tile (its TMEM lane)
   const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
@@ -564,7 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, ncols);
   if (P.ksplit == 1) {
-    if (ok) finish_tile<EPI>(P, stage, tile, 0, P.N);
+    if (ok) finish_tile<EPI>(P, stage, tile, 0, P.N, s_res);
     return;
   }
   // K slices: the tile's slices are one cluster (rank = slice).  Once every
@@ -576,7 +611,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   // an abort too, and none exits while a peer may still read its partial.
   cluster_arrive();
   cluster_wait();
-  const int n0 = split * P.N / P.ksplit, n1 = (split + 1) * P.N / P.ksplit;
   float *red = stage + static_cast<size_t>(P.npad) * kTileRows;
   if (ok) {
     const uint32_t base = smem_u32(stage) + static_cast<uint32_t>(n0 * kTileRows * 4);
@@ -613,7 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   }
   cluster_arrive();
   __syncthreads();
-  if (ok) finish_tile<EPI>(P, red, tile, n0, n1);
+  if (ok) finish_tile<EPI>(P, red, tile, n0, n1, s_res);
   cluster_wait();
 }
 
@@ -888,9 +922,13 @@ __global__ void __launch_bounds__(kThreads) embed_norm_kernel(const __nv_bfloat1
 __global__ void attention_kernel(const __grid_constant__ KvArgs A, Rows R, uint8_t *att) {
   extern __shared__ __align__(128) uint8_t sm[];
   grid_dep_launch();
-  grid_dep_wait();
   const int n = blockIdx.x, j = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the rows' metadata (uploaded before the step's first kernel) and the
+  // RoPE tables do not depend on the kernels before this one: read before
+  // the wait
   const int p = R.pos[n], slot = R.slot[n];
+  const float rc = A.cos[p * 32 + lane], rs = A.sin[p * 32 + lane];
+  grid_dep_wait();
   uint8_t *kb = sm, *vb = sm + static_cast<size_t>(A.ctx) * 128;
   float *qf = reinterpret_cast<float *>(sm + static_cast<size_t>(2) * A.ctx * 128) + warp * 128;
   const int pieces = (p + 1) * 8;  // 16-byte pieces of positions 0..p
@@ -903,7 +941,7 @@ __global__ void attention_kernel(const __grid_constant__ KvArgs A, Rows R, uint8
   const int h = j * A.group + warp;
   const uint32_t *row = reinterpret_cast<const uint32_t *>(A.qkv + static_cast<size_t>(n) * A.QKV);
   __nv_bfloat16 lo, hi;
-  rope_pair_cs(row + h * 32, lane, A.cos[p * 32 + lane], A.sin[p * 32 + lane], lo, hi);
+  rope_pair_cs(row + h * 32, lane, rc, rs, lo, hi);
   qf[lane] = bf2f(lo);
   qf[lane + 32] = bf2f(hi);
   cp_async_wait_all();
