@@ -317,13 +317,22 @@ __device__ __forceinline__ void norm_pack_row(const __nv_bfloat16 *x, const floa
 // the epilogue).
 constexpr int kResPre = 40;
 
+// Epilogue inputs a GEMM CTA stages in shared memory before its epilogue,
+// for the columns n0 + c it finishes:
+// kEpiResid: res[c * 128 + row in tile], the residual (c < kResPre);
+// kEpiQkv (tiles with k / v rows): pos[c], slot[c] (every c), and cs[c * 64 +
+// d] = cos, cs[c * 64 + 32 + d] = sin of the column's position (c < kResPre).
+struct EpiSmem {
+  const __nv_bfloat16 *res;
+  const int *pos, *slot;
+  const float *cs;
+};
+
 // The epilogue of columns [n0, n1) of a tile from its FP32 results in
-// shared memory (stage[(n - n0) * 128 + row in tile]); 128 threads.  sres:
-// kEpiResid's staged residual, column n0 + c at sres[c * 128 + row in tile]
-// for c < kResPre.
+// shared memory (stage[(n - n0) * 128 + row in tile]); 128 threads.
 template <int EPI>
 __device__ __forceinline__ void finish_tile(const GemmParams &P, float *stage, int tile, int n0, int n1,
-                                            const __nv_bfloat16 *sres) {
+                                            const EpiSmem &E) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = tile * kTileRows;
   // with 128 threads stepping by 128, a thread's row within the tile is
@@ -342,7 +351,7 @@ __device__ __forceinline__ void finish_tile(const GemmParams &P, float *stage, i
         for (int u = 0; u < kBatch; ++u) {
           const int c = c0 + u - n0;
           r[u] = c0 + u >= n1     ? 0.f
-                 : c < kResPre ? bf2f(sres[c * kTileRows + threadIdx.x])
+                 : c < kResPre ? bf2f(E.res[c * kTileRows + threadIdx.x])
                                : bf2f(P.resid[static_cast<size_t>(c0 + u) * P.rows + row]);
         }
       }
@@ -375,12 +384,7 @@ __device__ __forceinline__ void finish_tile(const GemmParams &P, float *stage, i
     // the tile's two heads per column: a k head is rotated at the column's
     // position and stored as K, a v head stored as V (one warp per head)
     if (row0 + kTileRows <= P.kv.QH * kHeadDimTc) return;  // q rows only
-    __shared__ int s_pos[kMaxN], s_slot[kMaxN];
-    for (int c = threadIdx.x; c < n1 - n0; c += kThreads) {
-      s_pos[c] = P.R.pos[n0 + c];
-      s_slot[c] = P.R.slot[n0 + c];
-    }
-    __syncthreads();
+    __syncthreads();  // the stage is read across threads next
     // kBatch units per warp per pass, their RoPE table reads in flight together
     constexpr int kBatch = 4, kWarps = kThreads / 32;
     const int units = (n1 - n0) * 2;
@@ -392,9 +396,15 @@ __device__ __forceinline__ void finish_tile(const GemmParams &P, float *stage, i
         const int head = row0 / kHeadDimTc + (u & 1);
         cs[j] = sn[j] = 0.f;
         if (u < units && head >= P.kv.QH && head < P.kv.QH + P.kv.KVH) {
-          const int p = s_pos[u >> 1];
-          cs[j] = P.kv.cos[p * 32 + lane];
-          sn[j] = P.kv.sin[p * 32 + lane];
+          const int c = u >> 1;
+          if (c < kResPre) {
+            cs[j] = E.cs[c * 64 + lane];
+            sn[j] = E.cs[c * 64 + 32 + lane];
+          } else {
+            const int p = E.pos[c];
+            cs[j] = P.kv.cos[p * 32 + lane];
+            sn[j] = P.kv.sin[p * 32 + lane];
+          }
         }
       }
 #pragma unroll
@@ -405,7 +415,7 @@ __device__ __forceinline__ void finish_tile(const GemmParams &P, float *stage, i
         const int head = row0 / kHeadDimTc + hh;
         if (head < P.kv.QH || head * kHeadDimTc >= P.rows) continue;
         const float *v = stage + (n - n0) * kTileRows + hh * kHeadDimTc;
-        const int p = s_pos[n - n0], slot = s_slot[n - n0];
+        const int p = E.pos[n - n0], slot = E.slot[n - n0];
         if (head < P.kv.QH + P.kv.KVH) {
           __nv_bfloat16 lo, hi;
           rope_vals(v[lane], v[lane + 32], cs[j], sn[j], lo, hi);
@@ -476,6 +486,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   // while the MMAs run
   __shared__ __align__(128) __nv_bfloat16 s_res[EPI == kEpiResid ? kResPre * kTileRows : 8];
   __shared__ __align__(8) uint64_t s_resbar;
+  // kEpiQkv: the columns' rows metadata and RoPE values, read before the
+  // dependency wait (host-uploaded rows, constant tables)
+  __shared__ int s_pos[EPI == kEpiQkv ? kMaxN : 1], s_slot[EPI == kEpiQkv ? kMaxN : 1];
+  __shared__ float s_cs[EPI == kEpiQkv ? kResPre * 64 : 1];
   const int S = P.stages;
   uint8_t *sa = smem;                                                   // [S][16 KB]
   uint8_t *sb = smem + static_cast<size_t>(S) * kAStageBytes;           // [S][npad * 128]
@@ -542,6 +556,39 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     for (int i = max(0, issued - S); i < issued; ++i)
       mbar_wait_quiet(&full[i % S], static_cast<uint32_t>(i / S) & 1u, P.limit_ns);
   } else {
+    if constexpr (EPI == kEpiQkv) {
+      // warps 2 and 3 of a tile with k / v rows: each column's position and
+      // slot, then (lanes = dimensions) its RoPE cos / sin
+      if (warp >= 2 && (tile + 1) * kTileRows > P.kv.QH * kHeadDimTc) {
+        for (int c = threadIdx.x - 64; c < n1 - n0; c += 64) {
+          s_pos[c] = P.R.pos[n0 + c];
+          s_slot[c] = P.R.slot[n0 + c];
+        }
+        // warp 2 takes the even columns < kResPre, warp 3 the odd ones: lane k
+        // fetches the position of the warp's column k, then every lane loads
+        // its dimension of all the warp's columns, all loads in flight
+        constexpr int kPer = kResPre / 2;
+        const int cols = min(n1 - n0, kResPre);
+        const int cl = warp - 2 + 2 * lane;
+        const int pl = lane < kPer && cl < cols ? P.R.pos[n0 + cl] : 0;
+        float cv[kPer], sv[kPer];
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+          const int p = __shfl_sync(0xffffffffu, pl, k);
+          const bool in = warp - 2 + 2 * k < cols;
+          cv[k] = in ? P.kv.cos[p * 32 + lane] : 0.f;
+          sv[k] = in ? P.kv.sin[p * 32 + lane] : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+          const int c = warp - 2 + 2 * k;
+          if (c < cols) {
+            s_cs[c * 64 + lane] = cv[k];
+            s_cs[c * 64 + 32 + lane] = sv[k];
+          }
+        }
+      }
+    }
     grid_dep_wait();  // the epilogue reads what earlier kernels wrote
     if (EPI == kEpiResid && warp == 2 && lane == 0 && res_cols > 0) {
       // the staged residual: one 16-byte-aligned run of the tile's rows per
@@ -599,7 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, ncols);
   if (P.ksplit == 1) {
-    if (ok) finish_tile<EPI>(P, stage, tile, 0, P.N, s_res);
+    if (ok) finish_tile<EPI>(P, stage, tile, 0, P.N, EpiSmem{s_res, s_pos, s_slot, s_cs});
     return;
   }
   // K slices: the tile's slices are one cluster (rank = slice).  Once every
@@ -647,7 +694,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   }
   cluster_arrive();
   __syncthreads();
-  if (ok) finish_tile<EPI>(P, red, tile, n0, n1, s_res);
+  if (ok) finish_tile<EPI>(P, red, tile, n0, n1, EpiSmem{s_res, s_pos, s_slot, s_cs});
   cluster_wait();
 }
 
@@ -928,13 +975,28 @@ __global__ void attention_kernel(const __grid_constant__ KvArgs A, Rows R, uint8
   // the wait
   const int p = R.pos[n], slot = R.slot[n];
   const float rc = A.cos[p * 32 + lane], rs = A.sin[p * 32 + lane];
-  grid_dep_wait();
+  // K / V rows of the slot's positions before its first row in this step
+  // were written by earlier steps: they are fetched before the wait, the
+  // rest (this step's qkv kernel writes them) after it
+  __shared__ int s_first;
+  if (threadIdx.x == 0) s_first = p;
+  __syncthreads();
+  for (int i = threadIdx.x; i < static_cast<int>(gridDim.x); i += blockDim.x)
+    if (R.slot[i] == slot) atomicMin(&s_first, R.pos[i]);
+  __syncthreads();
   uint8_t *kb = sm, *vb = sm + static_cast<size_t>(A.ctx) * 128;
   float *qf = reinterpret_cast<float *>(sm + static_cast<size_t>(2) * A.ctx * 128) + warp * 128;
   const int pieces = (p + 1) * 8;  // 16-byte pieces of positions 0..p
+  const int early = s_first * 8;   // pieces of positions < s_first (<= p)
   const uint8_t *ks = kv_rows(A, slot, j, 0), *vs = kv_rows(A, slot, j, 1);
-  for (int i = threadIdx.x; i < 2 * pieces; i += blockDim.x) {
-    const int kind = i >= pieces ? 1 : 0, off = (i - kind * pieces) * 16;
+  for (int i = threadIdx.x; i < 2 * early; i += blockDim.x) {
+    const int kind = i >= early ? 1 : 0, off = (i - kind * early) * 16;
+    cp_async16((kind ? vb : kb) + off, (kind ? vs : ks) + off);
+  }
+  grid_dep_wait();
+  const int late = pieces - early;
+  for (int i = threadIdx.x; i < 2 * late; i += blockDim.x) {
+    const int kind = i >= late ? 1 : 0, off = (early + i - kind * late) * 16;
     cp_async16((kind ? vb : kb) + off, (kind ? vs : ks) + off);
   }
   cp_async_commit();
