@@ -317,6 +317,20 @@ struct DecoderCta {
   }
 
   // ---- work split -------------------------------------------------------------
+  // Gate/up pair blocks [gu_lo(n, c), gu_lo(n, c + 1)) of CTA c: n / G each,
+  // and the n % G left over go to CTAs that own no down-projection row group
+  // (down gives CTA c split_lo(H/8, G, c + 1) - split_lo(H/8, G, c) groups,
+  // 0 or 1), so no CTA streams both an extra gate/up block and a down row
+  // group in one layer: the largest per-layer weight share a CTA's ring must
+  // hold drops from qkv + o + 5 gate/up blocks + down to 4 blocks + down.
+  // When the leftover exceeds those CTAs, the plain balanced split.
+  __device__ int gu_lo(int n, int c) const {
+    const int hg = P.H / 8, base = n / G, rem = n - base * G;
+    if (hg > G || rem > G - hg) return split_lo(n, G, c);
+    const int nodown = c - split_lo(hg, G, c);  // CTAs before c without a down group
+    return base * c + min(rem, nodown);
+  }
+
   __device__ MatRange phase_range(int k) const {
     if (k >= 4 * P.L) {
       const int n = P.V / 8;
@@ -334,7 +348,7 @@ struct DecoderCta {
       }
       case 2: {
         const int n = P.I / 8;  // gate/up pair blocks
-        return MatRange{lp.w_gu, 2 * split_lo(n, G, cta), 2 * split_lo(n, G, cta + 1), P.kc_h};
+        return MatRange{lp.w_gu, 2 * gu_lo(n, cta), 2 * gu_lo(n, cta + 1), P.kc_h};
       }
       default: {
         const int n = P.H / 8;
